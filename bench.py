@@ -1,0 +1,499 @@
+"""Benchmark of the quantized-inference hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kq|reference] [--config 1]
+
+Workload (default): BASELINE configuration 1, the q8_0 x q8_1 W8A8 GEMM
+M=512, N=11008, K=4096 with fp32 activations quantised on the fly. One step
+is one call of the operator (activation quantisation + GEMM) on one batch of
+synthetic, seeded input already resident in HBM. Other --config values
+(0: q4_0 GEMV, 2: q4_0 sweep point, 3: ragged q8_0-KV flash decode) are for
+DESIGN.md tables, not the headline line.
+
+Timing: W untimed warm-up steps, then K steps bracketed by a barrier and
+torch.cuda.synchronize(), timed with CUDA events on the launching stream,
+max over ranks. Consecutive steps rotate through input sets whose combined
+size exceeds 2x the L2 cache, so every step reads its operands from HBM.
+
+Multi-GPU (torchrun, one rank per GPU): weak scaling. Every rank runs the same
+per-GPU workload on its own shard of output columns (the N-sharded GEMM); the
+shards are independent, so the timed step has no collective.
+
+--impl reference times the reference's own CPU implementation of the same
+operator (kernelevalplus-main/include/gemm_reference.h gemm_w8a8_reference,
+built into oracle/_ref/libkqref.so) on the host cores, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "k-search_b200"))
+sys.path.insert(0, REPO)
+
+import numpy as np  # noqa: E402
+
+CONFIGS = {
+    0: dict(kind="gemm", wtype="q4_0", M=1, N=4096, K=4096, act="sum_dq",
+            workload="configs[0]: q4_0 x q8_1 GEMV M=1 N=4096 K=4096"),
+    1: dict(kind="gemm", wtype="q8_0", M=512, N=11008, K=4096, act="sum_dq",
+            workload="configs[1]: q8_0 W8A8 GEMM M=512 N=11008 K=4096"),
+    2: dict(kind="gemm", wtype="q4_0", M=1, N=14336, K=4096, act="sum_dq",
+            workload="configs[2]: q4_0 x q8_1 M=1 N=14336 K=4096"),
+    3: dict(kind="fa", B=32, Hq=32, Hkv=8, D=128, Lmin=64, Lmax=8192,
+            workload="configs[3]: ragged GQA flash decode, q8_0 KV, B=32 Hq=32 Hkv=8 D=128 L~U[64,8192]"),
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="kq", choices=["kq", "reference"])
+    ap.add_argument("--config", type=int, default=1)
+    ap.add_argument("--M", type=int, default=None, help="override M for gemm configs")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+
+def load_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sms, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sms.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        med = float(np.median(sms)) if sms else None
+        return {"sm_mhz": med, "sm_max_mhz": mx, "samples": len(sms), "reasons": sorted(reasons)}
+
+
+def dist_setup(gpus: int):
+    import torch
+    import torch.distributed as dist
+
+    if gpus > 1 or int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        rank, world = dist.get_rank(), dist.get_world_size()
+        local = int(os.environ.get("LOCAL_RANK", rank))
+    else:
+        rank, world, local = 0, 1, 0
+    torch.cuda.set_device(local)
+    return rank, world, local
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (reference C++ routines or the oracle port)
+# ---------------------------------------------------------------------------
+
+def cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+_CPU_INPUTS = {}
+
+
+def cpu_gemm_baseline(cfg: dict, seconds: float = 12.0) -> dict:
+    """Time the reference's C++ CPU GEMM (gemm_w8a8_reference / gemm_w4a8_reference)
+    on all host threads over a bounded sample of rows of the same workload."""
+    from oracle import native, quant as Q
+
+    M, N, K, wt = cfg["M"], cfg["N"], cfg["K"], cfg["wtype"]
+    threads = cpu_threads()
+    key = (wt, M, N, K)
+    if key not in _CPU_INPUTS:
+        rng = np.random.default_rng(0)
+        _CPU_INPUTS[key] = (Q.make_blocks(wt, rng, N, K), rng.standard_normal((M, K)).astype(np.float32))
+    w, x = _CPU_INPUTS[key]
+    if native.available() and wt in ("q4_0", "q8_0"):
+        kind = "reference"
+        run = lambda rows: native.gemm(wt, w, native.quantize_q8_1(x[:rows], threads), rows, N, K, threads)  # noqa: E731
+    else:
+        kind = "port"
+        run = lambda rows: Q.gemm_f32act(wt, w, x[:rows], rows, N, K, Q.SUM_DQ)  # noqa: E731
+    rows = 1
+    t0 = time.perf_counter()
+    run(rows)
+    dt = time.perf_counter() - t0
+    # grow the sample while it stays inside the time budget
+    while rows < M and dt * 2 < seconds:
+        rows = min(M, rows * 2)
+        t0 = time.perf_counter()
+        run(rows)
+        dt = time.perf_counter() - t0
+    ops = 2.0 * rows * N * K
+    return {"value": ops / dt / 1e12, "unit": "TOPS", "cores": threads, "kind": kind,
+            "sample": f"{rows} of {M} activation rows x N={N} x K={K} ({wt}), q8_1 quantise + GEMM, {dt:.2f} s"}
+
+
+def cpu_fa_baseline(cfg: dict, seconds: float = 10.0) -> dict:
+    from oracle import quant as Q
+    rng = np.random.default_rng(0)
+    B, Hq, Hkv, D = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["D"]
+    lens = rng.integers(cfg["Lmin"], cfg["Lmax"] + 1, size=B)
+    done, t_all, nseq = 0, 0.0, 0
+    while t_all < seconds and nseq < B:
+        L = int(lens[nseq])
+        q = rng.standard_normal((1, Hq, D)).astype(np.float16)
+        k = Q.quantize_q8_0(rng.standard_normal((L * Hkv, D)).astype(np.float32))
+        v = Q.quantize_q8_0(rng.standard_normal((L * Hkv, D)).astype(np.float32))
+        cu = np.array([0, L], dtype=np.int32)
+        t0 = time.perf_counter()
+        Q.flash_decode_ragged(q, k, v, cu, Hq, Hkv, D, 1.0 / np.sqrt(D))
+        t_all += time.perf_counter() - t0
+        nseq += 1
+    return {"value": nseq / t_all, "unit": "tok/s", "cores": cpu_threads(), "kind": "port",
+            "sample": f"{nseq} of {B} sequences decoded one by one with the numpy oracle, {t_all:.2f} s"}
+
+
+# ---------------------------------------------------------------------------
+# GPU arms
+# ---------------------------------------------------------------------------
+
+def bench_gemm(args, cfg, rank, world):
+    import torch
+    import kq
+    from kq import _lib
+
+    M = args.M or cfg["M"]
+    N, K, wt = cfg["N"], cfg["K"], cfg["wtype"]
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device="cpu").manual_seed(1234 + rank)
+    nb = K // 32
+    bb = kq.BLOCK_BYTES[wt]
+    # synthetic weights drawn directly as blocks (configs[0]/[1] distributions)
+    from kq import synth
+    rng = np.random.default_rng(1234 + rank)
+    w_host = synth.blocks(wt, rng, N, K)
+    step_bytes = N * nb * bb + M * K * 4 + M * N * 4
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    nsets = max(2, int(np.ceil(2.5 * l2 / step_bytes)))
+    ws = [torch.from_numpy(w_host).to(dev) for _ in range(nsets)]
+    xs = [torch.randn((M, K), generator=g, dtype=torch.float32).to(dev) for _ in range(nsets)]
+    outs = [torch.empty((M, N), dtype=torch.float32, device=dev) for _ in range(nsets)]
+    L = kq.lib()
+    wtc = kq.WTYPES[wt]
+    act_mode = kq.ACT_MODES[cfg["act"]]
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step(i):
+        j = i % nsets
+        _lib.check(L.kq_gemm_f32act(wtc, ws[j].data_ptr(), xs[j].data_ptr(), outs[j].data_ptr(), M, N, K, act_mode, sp),
+                   "kq_gemm_f32act")
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop() if clocks else None
+    ms = max_over_ranks(ms, world)
+    ops = 2.0 * M * N * K
+    value = world * ops * args.steps / (ms * 1e-3) / 1e12
+
+    # ---- dominant kernel alone (the GEMM on pre-staged activations) ----
+    qs = [torch.empty((M, K), dtype=torch.int8, device=dev) for _ in range(nsets)]
+    dss = [torch.empty((M, nb, 2), dtype=torch.float32, device=dev) for _ in range(nsets)]
+    for j in range(nsets):  # stage once with the library's own quantiser (not timed)
+        a8 = kq.quantize_q8_1(xs[j], "sum_dq")
+        dss[j].copy_(torch.stack([a8[:, :, 0:2].contiguous().view(torch.float16).float().squeeze(-1),
+                                  a8[:, :, 2:4].contiguous().view(torch.float16).float().squeeze(-1)], dim=-1))
+        qs[j].copy_(a8[:, :, 4:].contiguous().view(torch.int8).reshape(M, K))
+
+    def kstep(i):
+        j = i % nsets
+        _lib.check(L.kq_mul_mat_q8x(wtc, ws[j].data_ptr(), qs[j].data_ptr(), dss[j].data_ptr(), outs[j].data_ptr(),
+                                    M, N, K, sp), "kq_mul_mat_q8x")
+
+    for i in range(3):
+        kstep(i)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(args.steps):
+        kstep(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    kms = e0.elapsed_time(e1) / args.steps
+    kms = max_over_ranks(kms, world)
+
+    # ---- end to end through the public API with host buffers ----
+    xh = [torch.randn((M, K), generator=g, dtype=torch.float32).pin_memory() for _ in range(2)]
+    oh = [torch.empty((M, N), dtype=torch.float32).pin_memory() for _ in range(2)]
+    xd = torch.empty((M, K), dtype=torch.float32, device=dev)
+
+    def estep(i):
+        j = i % nsets
+        xd.copy_(xh[i % 2], non_blocking=True)
+        kq.gemm_f32act(ws[j], xd, M, N, K, wt, cfg["act"], out=outs[j])
+        oh[i % 2].copy_(outs[j], non_blocking=True)
+
+    for i in range(3):
+        estep(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    e0.record(stream)
+    for i in range(args.steps):
+        estep(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ems = max_over_ranks(e0.elapsed_time(e1), world)
+    e2e = {"value": world * ops * args.steps / (ems * 1e-3) / 1e12, "unit": "TOPS",
+           "h2d_bytes_per_step": M * K * 4, "d2h_bytes_per_step": M * N * 4}
+
+    hbm, bf16, src = load_peaks()
+    kernel_bytes = N * nb * bb + M * K + M * nb * 8 + M * N * 4
+    if M <= 8:
+        achieved = kernel_bytes / (kms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(achieved / hbm, 4), "traffic": None,
+                "kernel": "gemv_kernel", "peak_source": f"{src} hbm_gbs (copy)"}
+    else:
+        achieved = ops / (kms * 1e-3) / 1e12
+        peak = 2.0 * bf16
+        roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4), "traffic": None,
+                "kernel": "quantised GEMM (M > 8)",
+                "peak_source": f"int8 dense = 2 x {src} bf16_tflops (cuBLAS bf16 burst)"}
+    launches_per_step = 2
+    line = {
+        "metric": "W8A8 GEMM TOPS (q8_0 x q8_1)" if wt == "q8_0" else "W4A8 GEMM TOPS (q4_0 x q8_1)",
+        "value": round(value, 3), "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded; weights drawn directly as q-blocks)",
+        "config": {"workload": cfg["workload"], "M": M, "N": N, "K": K, "wtype": wt, "act_quant": cfg["act"],
+                   "l2": f"{nsets} rotating input sets ({nsets * step_bytes / 1e6:.0f} MB > 2x L2)",
+                   "parallelism": f"N-sharded weak scaling x{world} (independent column shards)"},
+        "roofline": roof,
+        "e2e": e2e,
+        "gpu_launches": launches_per_step * args.steps,
+        "kernel_ms": round(kms, 5),
+    }
+    if clk is not None:
+        line["clocks"] = clk
+    return line
+
+
+def bench_fa(args, cfg, rank, world):
+    import torch
+    import kq
+
+    B, Hq, Hkv, D = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["D"]
+    dev = torch.device("cuda", torch.cuda.current_device())
+    rng = np.random.default_rng(99 + rank)
+    lens = rng.integers(cfg["Lmin"], cfg["Lmax"] + 1, size=B).astype(np.int32)
+    cu = np.zeros(B + 1, dtype=np.int32)
+    cu[1:] = np.cumsum(lens)
+    T = int(cu[-1])
+    kv_bytes = T * Hkv * (D // 32) * 34
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    nsets = max(2, int(np.ceil(2.5 * l2 / (2 * kv_bytes))))
+    g = torch.Generator(device="cpu").manual_seed(5 + rank)
+    gd = torch.Generator(device=dev).manual_seed(7 + rank)
+    # K and V drawn fp32 N(0,1) and quantised to q8_0 along head_dim on the GPU
+    ks = [kq.quantize_rows(torch.randn((T * Hkv, D), generator=gd, device=dev), "q8_0") for _ in range(nsets)]
+    vs = [kq.quantize_rows(torch.randn((T * Hkv, D), generator=gd, device=dev), "q8_0") for _ in range(nsets)]
+    q = torch.randn((B, Hq, D), generator=g).half().to(dev)
+    cud = torch.from_numpy(cu).to(dev)
+    out = torch.empty_like(q)
+    maxlen = int(lens.max())
+
+    def step(i):
+        j = i % nsets
+        kq.flash_decode_ragged(q, ks[j], vs[j], cud, Hkv, maxlen, out=out)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    barrier(world)
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    clk = clocks.stop() if clocks else None
+    value = world * B * args.steps / (ms * 1e-3)
+    per = ms / args.steps
+    hbm, _, src = load_peaks()
+    algo = 2 * kv_bytes + B * Hq * D * 2 * 2
+    achieved = algo / (per * 1e-3) / 1e9
+    line = {
+        "metric": "q8_0-KV flash-decode tok/s", "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp32", "data": "synthetic (seeded)",
+        "config": {"workload": cfg["workload"], "sum_L": T, "l2": f"{nsets} rotating KV caches"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": None, "kernel": "fa decode (partial+combine)",
+                     "peak_source": f"{src} hbm_gbs"},
+        "gpu_launches": 2 * args.steps,
+    }
+    if clk is not None:
+        line["clocks"] = clk
+    return line
+
+
+def reference_arm(args, cfg):
+    """The reference's CPU implementation of the same operator, all host threads.
+    Each step is a bounded sample of the workload (a slice of activation rows)
+    so that the whole --warmup W --steps K run ends within a few minutes."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    budget = min(2.0, 120.0 / max(1, args.warmup + args.steps))
+    if cfg["kind"] == "fa":
+        vals, cb = [], None
+        for i in range(args.warmup + args.steps):
+            cb = cpu_fa_baseline(cfg, seconds=budget)
+            if i >= args.warmup:
+                vals.append(cb["value"])
+        unit, metric = "tok/s", "q8_0-KV flash-decode tok/s"
+    else:
+        vals, cb = [], None
+        for i in range(args.warmup + args.steps):
+            cb = cpu_gemm_baseline(cfg, seconds=budget)
+            if i >= args.warmup:
+                vals.append(cb["value"])
+        unit = "TOPS"
+        metric = "W8A8 GEMM TOPS (q8_0 x q8_1)" if cfg["wtype"] == "q8_0" else "W4A8 GEMM TOPS (q4_0 x q8_1)"
+    value = float(np.median(vals)) if vals else cb["value"]
+    cb = dict(cb)
+    cb["value"] = value
+    return {
+        "impl": "reference", "metric": metric, "value": round(value, 6), "unit": unit, "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded)",
+        "config": {"workload": cfg["workload"]},
+        "cpu_baseline": cb,
+        "e2e": {"value": round(value, 6), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse()
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        line = reference_arm(args, cfg)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    import torch
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (the kernels have no CPU path)")
+    rank, world, _ = dist_setup(args.gpus)
+    if cfg["kind"] == "fa":
+        line = bench_fa(args, cfg, rank, world)
+        cpu = (lambda: cpu_fa_baseline(cfg)) if (rank == 0 and world == 1) else None
+    else:
+        line = bench_gemm(args, cfg, rank, world)
+        cpu = (lambda: cpu_gemm_baseline(cfg)) if (rank == 0 and world == 1) else None
+    if cpu is not None and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

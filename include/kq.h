@@ -1,0 +1,161 @@
+/*
+ * kq.h - C ABI of libkq.so, the B200 (sm_100a) kernels for the GGML
+ * block-quantized inference path that KernelEvalPlus (inside qhy991/K-Search)
+ * defines.
+ *
+ * Plain pointers and sizes only. All pointers are DEVICE pointers unless a
+ * comment says otherwise; buffers belong to the caller. Streams are passed as
+ * an opaque cudaStream_t (NULL = legacy default stream).
+ *
+ * Two families of entry points:
+ *
+ *  1. The KernelEvalPlus operator ABI, signature for signature. The harness
+ *     binds the first `extern "C" void` of an attempt's kernel.cu
+ *     (kernelevalplus-main/llm_kernel_test/op_test_handler.py:305-349 for
+ *     quant_gemm, llm_kernel_test/unified_test_runner.py:295-324 for
+ *     flash_attention). These return void, run on the legacy default stream
+ *     (as the harness's candidate kernels do) and record failures for
+ *     kq_last_error(); the harness-side shim (k-search_b200/harness/) turns a
+ *     failure into a C++ exception.
+ *
+ *  2. Status-returning entry points with an explicit stream (kq_status_t,
+ *     KQ_OK == 0). These are what the Python package and the benchmarks call.
+ *
+ * Block layouts are the reference's (kernelevalplus-main/include/quant_types.h:
+ * 59-152): q4_0 = fp16 d | 16 B nibbles (18 B), q4_1 = fp16 d | fp16 m |
+ * 16 B (20 B), q8_0 = fp16 d | 32 x int8 (34 B), q8_1 = fp16 d | fp16 s |
+ * 32 x int8 (36 B); a weight matrix [N, K] is N rows of K/32 blocks.
+ */
+#ifndef KQ_H
+#define KQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int kq_status_t;
+#define KQ_OK 0
+#define KQ_ERR_INVALID 1     /* bad argument: shape, type, null pointer, alignment */
+#define KQ_ERR_UNSUPPORTED 2 /* valid input this build does not handle */
+#define KQ_ERR_CUDA 3        /* CUDA runtime error (launch, memory) */
+#define KQ_ERR_NOMEM 4       /* library workspace could not be allocated */
+#define KQ_ERR_TIMEOUT 5     /* a bounded device-side wait gave up */
+#define KQ_ERR_DEVICE 6      /* a device-side check recorded an error */
+
+/* weight block types */
+#define KQ_Q4_0 0
+#define KQ_Q4_1 1
+#define KQ_Q8_0 2
+
+/* On-the-fly activation quantisation modes. The int8 codes are the same in
+ * all three (q = round_half_even(x / d), d = amax/127, d = 1 when amax == 0;
+ * llm_kernel_test/reference/quantize.py:181-191); they differ in the block
+ * scale d and sum s used by the fp32 epilogue:
+ *   KQ_ACT_SUM_X  fp16 d, fp16 s = sum(x)        (quantize.py:193-209, q8_1 bytes)
+ *   KQ_ACT_SUM_DQ fp16 d, fp16 s = fp16(d)*sum(q) (benchmark configurations)
+ *   KQ_ACT_F32    fp32 d, fp32 s = sum(x)         (per-definition W4A32C8 reference,
+ *                 core/operators/quant_gemm/variants/deepseek_v2/w4a32c8_q4_0_fp32_int8/reference.py:50-90) */
+#define KQ_ACT_SUM_X 0
+#define KQ_ACT_SUM_DQ 1
+#define KQ_ACT_F32 2
+
+typedef void* kq_stream_t; /* cudaStream_t */
+
+/* ---- library ------------------------------------------------------------ */
+
+/* ABI version (bumped on any signature change). */
+int kq_abi_version(void);
+/* Message of the last failure on the calling host thread ("" if none). */
+const char* kq_last_error(void);
+/* Bytes per block of a weight type (18, 20, 34), 0 for an unknown type. */
+size_t kq_block_bytes(int wtype);
+/* Reads and clears the device error word of the current device (synchronises
+ * the given stream). *code receives the first recorded device error (0 = none). */
+kq_status_t kq_device_error(int* code, kq_stream_t stream);
+
+/* ---- 1. KernelEvalPlus operator ABI (void, legacy default stream) -------- */
+
+/* quant_gemm, fp32 activations quantised on the fly (W4A32C8 / W8A32C8):
+ * output[M, N] = activation[M, K] x dequant(weight[N, K/32 blocks])^T with the
+ * llama.cpp per-block formula. Activation mode KQ_ACT_F32.
+ * Replaces the attempt entry bound by op_test_handler.py:315-320
+ * (`extern "C" void <entry>(const uint8_t*, const float*, float*, int, int, int)`)
+ * for definitions with weight dtype block_q4_0 / block_q4_1 / block_q8_0 and
+ * activation dtype float32 (e.g. definitions/quant_gemm/.../w4a32c8_q4_0_fp32_int8_*.json). */
+void kq_w4a32c8_q4_0_fp32_int8(const uint8_t* weight, const float* activation, float* output, int M, int N, int K);
+void kq_w4a32c8_q4_1_fp32_int8(const uint8_t* weight, const float* activation, float* output, int M, int N, int K);
+void kq_w8a32c8_q8_0_fp32_int8(const uint8_t* weight, const float* activation, float* output, int M, int N, int K);
+
+/* quant_gemm with pre-quantised q8_1 activations (activation dtype block_q8_1;
+ * op_test_handler.py:311-313 switches the activation pointer to uint8_t).
+ * Replaces the same attempt entry for W4A8 definitions. */
+void kq_w4a8_q4_0_q8_1(const uint8_t* weight, const uint8_t* activation, float* output, int M, int N, int K);
+
+/* flash_attention decode with a q8_0 KV cache: query fp32 [B, H, D];
+ * key_cache / value_cache = q8_0 blocks of the [S, H, D] cache (row (s, h) is
+ * D/32 blocks, op_test_handler.py:489-508); all B queries attend to the same
+ * cache; scale 1/sqrt(D); output fp32 [B, H, D].
+ * Replaces `extern "C" void flash_attn_kernel(...)` bound by
+ * unified_test_runner.py:298-303. */
+void kq_flash_attn_q8_0(const float* query, const void* key_cache, const void* value_cache, float* output,
+                        int batch_size, int seq_len, int num_heads, int head_dim);
+
+/* ---- 2. Status-returning entry points ------------------------------------ */
+
+/* fp32 x[M, K] -> q8_1 blocks y[M, K/32] (36 B each), sum_mode KQ_ACT_SUM_X
+ * or KQ_ACT_SUM_DQ. Bit-exact with quantize_to_q8_1 (quantize.py:165-214) for
+ * KQ_ACT_SUM_X, including the fp32 summation order of s.
+ * GPU form of quantize_q8_1_kernel (include/quantize.h:302-340). */
+kq_status_t kq_quantize_q8_1(const float* x, void* y, int64_t M, int64_t K, int sum_mode, kq_stream_t stream);
+
+/* fp32 rows x[rows, K] -> q4_0 / q4_1 / q8_0 blocks y (weights, KV caches).
+ * Bit-exact with quantize_to_q4_0 / _q4_1 / _q8_0 (quantize.py:12-162); GPU
+ * form of quantize_q4_0_kernel / quantize_q8_0_kernel (include/quantize.h:221-294). */
+kq_status_t kq_quantize_rows(int wtype, const float* x, void* y, int64_t rows, int64_t K, kq_stream_t stream);
+
+/* Weights x pre-quantised q8_1 activations a[M, K/32] -> fp32 out[M, N]
+ * (reference_q4_0_q8_1_gemm gemm_ref.py:100-153, reference_q4_1_q8_1_gemm
+ * gemm_ref.py:274-331, vec_dot_q8_0_q8_1 gemm_reference.h:311-336). */
+kq_status_t kq_mul_mat_q(int wtype, const void* w, const void* a_q8_1, float* out, int M, int N, int K,
+                         kq_stream_t stream);
+
+/* Weights x fp32 activations quantised on the fly (the harness operator).
+ * act_mode is one of KQ_ACT_*; the status form of the void entries above. */
+kq_status_t kq_gemm_f32act(int wtype, const void* w, const float* x, float* out, int M, int N, int K,
+                           int act_mode, kq_stream_t stream);
+
+/* Weights x activations already in the kernels' staging layout: int8 codes
+ * a_qs[M, K] (row stride K bytes, 16-byte aligned) and one (d, s) fp32 pair
+ * per 32-block a_ds[M, K/32, 2]. For callers that quantise inside their own
+ * producer kernel; the same per-block formulas as kq_mul_mat_q. */
+kq_status_t kq_mul_mat_q8x(int wtype, const void* w, const int8_t* a_qs, const float* a_ds, float* out, int M, int N,
+                           int K, kq_stream_t stream);
+
+/* Debug / parity: int32 sumi[m, n, b] = sum_i q_w[n, b, i] * q_a[m, b, i] with
+ * q_w the stored code (0..15 for q4_0/q4_1, int8 for q8_0), as the reference
+ * forms it (gemm_ref.py:146, gemm_reference.h:200-211). */
+kq_status_t kq_block_sums_i32(int wtype, const void* w, const void* a_q8_1, int32_t* sumi, int M, int N, int K,
+                              kq_stream_t stream);
+
+/* Flash-attention decode, harness semantics (see kq_flash_attn_q8_0). */
+kq_status_t kq_fa_decode_q8_0_mha(const float* q, const void* k, const void* v, float* out, int B, int S, int H,
+                                  int D, kq_stream_t stream);
+
+/* Ragged GQA flash-decode over a q8_0 KV cache (benchmark configuration 3).
+ * q fp16 [B, Hq, D]; k, v = q8_0 blocks of [T, Hkv, D] with T = cu_seqlens[B];
+ * sequence b owns cache rows cu_seqlens[b] .. cu_seqlens[b+1]-1 (int32, device);
+ * query head h reads KV head h / (Hq / Hkv); fp32 softmax and accumulation;
+ * out fp16 [B, Hq, D]. max_seqlen bounds the per-sequence length (used to
+ * size the split-KV grid). An empty sequence yields zeros. */
+kq_status_t kq_fa_decode_q8_0_ragged(const void* q_f16, const void* k, const void* v, const int32_t* cu_seqlens,
+                                     int B, int Hq, int Hkv, int D, int max_seqlen, float scale, void* out_f16,
+                                     kq_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KQ_H */

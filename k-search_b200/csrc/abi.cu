@@ -1,0 +1,273 @@
+// libkq C ABI: argument checks, dispatch, per-device workspace, error state.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "kq_internal.h"
+
+namespace kq {
+
+namespace {
+thread_local std::string g_last_error;
+
+constexpr int kMaxDevices = 64;
+struct DeviceState {
+  void* ws[WS_NSLOTS] = {};
+  size_t ws_size[WS_NSLOTS] = {};
+  int* err_word = nullptr;
+  int sms = 0;
+};
+DeviceState g_dev[kMaxDevices];
+std::mutex g_mu;
+}  // namespace
+
+kq_status_t fail(kq_status_t st, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return st;
+}
+
+kq_status_t check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return KQ_OK;
+  return fail(KQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+kq_status_t check_launch(const char* what) { return check_cuda(cudaGetLastError(), what); }
+
+int current_device() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d;
+}
+
+int sm_count() {
+  const int d = current_device();
+  if (d < 0 || d >= kMaxDevices) return 148;
+  if (g_dev[d].sms == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
+    g_dev[d].sms = n > 0 ? n : 148;
+  }
+  return g_dev[d].sms;
+}
+
+void* workspace(WsSlot slot, size_t bytes) {
+  const int d = current_device();
+  if (d < 0 || d >= kMaxDevices) {
+    fail(KQ_ERR_INVALID, "device ordinal %d out of range", d);
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceState& st = g_dev[d];
+  if (bytes == 0) bytes = 256;
+  if (st.ws_size[slot] >= bytes) return st.ws[slot];
+  size_t grow = bytes + bytes / 4;
+  grow = (grow + (1u << 20) - 1) & ~(size_t)((1u << 20) - 1);
+  if (st.ws[slot]) {
+    cudaFree(st.ws[slot]);  // implicitly synchronises the device
+    st.ws[slot] = nullptr;
+    st.ws_size[slot] = 0;
+  }
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, grow);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    fail(KQ_ERR_NOMEM, "workspace allocation of %zu bytes failed: %s", grow, cudaGetErrorString(e));
+    return nullptr;
+  }
+  st.ws[slot] = p;
+  st.ws_size[slot] = grow;
+  return p;
+}
+
+int* device_error_word() {
+  const int d = current_device();
+  if (d < 0 || d >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceState& st = g_dev[d];
+  if (!st.err_word) {
+    if (cudaMalloc(&st.err_word, sizeof(int)) != cudaSuccess) {
+      cudaGetLastError();
+      st.err_word = nullptr;
+      return nullptr;
+    }
+    cudaMemset(st.err_word, 0, sizeof(int));
+  }
+  return st.err_word;
+}
+
+namespace {
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+kq_status_t check_gemm_args(int wtype, const void* w, const void* a, const float* out, int M, int N, int K) {
+  if (block_bytes(wtype) == 0) return fail(KQ_ERR_INVALID, "unknown weight type %d", wtype);
+  if (M < 0 || N < 0 || K < 0) return fail(KQ_ERR_INVALID, "negative dimension (M=%d N=%d K=%d)", M, N, K);
+  if (K % 32 != 0) return fail(KQ_ERR_INVALID, "K=%d is not a multiple of 32", K);
+  if ((long long)M * N > 0 && K > 0 && (!w || !a || !out)) return fail(KQ_ERR_INVALID, "null pointer");
+  return KQ_OK;
+}
+
+// Quantised activations are staged; choose the GEMM kernel for the shape.
+kq_status_t dispatch_gemm(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, cudaStream_t s,
+                          bool pdl) {
+  if (gemv_supported(wtype, M, N, K) && aligned(w, 16)) return launch_gemv(wtype, w, act, out, M, N, K, pdl, s);
+  return launch_gemm_simt(wtype, w, act, out, M, N, K, s);
+}
+
+kq_status_t zero_output(float* out, int M, int N, cudaStream_t s) {
+  if ((long long)M * N == 0) return KQ_OK;
+  return check_cuda(cudaMemsetAsync(out, 0, sizeof(float) * (size_t)M * N, s), "zero output");
+}
+
+}  // namespace
+}  // namespace kq
+
+using namespace kq;
+
+extern "C" {
+
+int kq_abi_version(void) { return 1; }
+
+const char* kq_last_error(void) { return g_last_error.c_str(); }
+
+size_t kq_block_bytes(int wtype) { return (size_t)block_bytes(wtype); }
+
+kq_status_t kq_device_error(int* code, kq_stream_t stream) {
+  if (!code) return fail(KQ_ERR_INVALID, "null code pointer");
+  int* w = device_error_word();
+  if (!w) return fail(KQ_ERR_NOMEM, "device error word unavailable");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int v = 0;
+  kq_status_t st = check_cuda(cudaMemcpyAsync(&v, w, sizeof(int), cudaMemcpyDeviceToHost, s), "read error word");
+  if (st) return st;
+  st = check_cuda(cudaStreamSynchronize(s), "sync");
+  if (st) return st;
+  *code = v;
+  if (v) return check_cuda(cudaMemsetAsync(w, 0, sizeof(int), s), "clear error word");
+  return KQ_OK;
+}
+
+kq_status_t kq_quantize_q8_1(const float* x, void* y, int64_t M, int64_t K, int sum_mode, kq_stream_t stream) {
+  if (M < 0 || K < 0 || K % 32 != 0) return fail(KQ_ERR_INVALID, "quantize_q8_1: bad shape M=%lld K=%lld", (long long)M, (long long)K);
+  if (M * K == 0) return KQ_OK;
+  if (!x || !y) return fail(KQ_ERR_INVALID, "quantize_q8_1: null pointer");
+  if (!aligned(x, 16) || !aligned(y, 4)) return fail(KQ_ERR_INVALID, "quantize_q8_1: x must be 16-byte and y 4-byte aligned");
+  return launch_quantize_q8_1_bytes(x, y, M, K, sum_mode, static_cast<cudaStream_t>(stream));
+}
+
+kq_status_t kq_quantize_rows(int wtype, const float* x, void* y, int64_t rows, int64_t K, kq_stream_t stream) {
+  if (block_bytes(wtype) == 0) return fail(KQ_ERR_INVALID, "unknown weight type %d", wtype);
+  if (rows < 0 || K < 0 || K % 32 != 0) return fail(KQ_ERR_INVALID, "quantize_rows: bad shape rows=%lld K=%lld", (long long)rows, (long long)K);
+  if (rows * K == 0) return KQ_OK;
+  if (!x || !y || !aligned(y, 2)) return fail(KQ_ERR_INVALID, "quantize_rows: null or misaligned pointer");
+  return launch_quantize_rows(wtype, x, y, rows, K, static_cast<cudaStream_t>(stream));
+}
+
+kq_status_t kq_mul_mat_q(int wtype, const void* w, const void* a_q8_1, float* out, int M, int N, int K,
+                         kq_stream_t stream) {
+  kq_status_t st = check_gemm_args(wtype, w, a_q8_1, out, M, N, K);
+  if (st) return st;
+  if ((long long)M * N == 0) return KQ_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (K == 0) return zero_output(out, M, N, s);
+  if (!aligned(a_q8_1, 4)) return fail(KQ_ERR_INVALID, "q8_1 activations must be 4-byte aligned");
+  void* ws = workspace(WS_ACT, act8_bytes(M, K));
+  if (!ws) return KQ_ERR_NOMEM;
+  Act8 act = act8_view(ws, M, K);
+  st = launch_q8_1_to_act(a_q8_1, act, M, K, s);
+  if (st) return st;
+  return dispatch_gemm(wtype, w, act, out, M, N, K, s, true);
+}
+
+kq_status_t kq_gemm_f32act(int wtype, const void* w, const float* x, float* out, int M, int N, int K, int act_mode,
+                           kq_stream_t stream) {
+  kq_status_t st = check_gemm_args(wtype, w, x, out, M, N, K);
+  if (st) return st;
+  if (act_mode < KQ_ACT_SUM_X || act_mode > KQ_ACT_F32) return fail(KQ_ERR_INVALID, "unknown activation mode %d", act_mode);
+  if ((long long)M * N == 0) return KQ_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (K == 0) return zero_output(out, M, N, s);
+  if (!aligned(x, 16)) return fail(KQ_ERR_INVALID, "activations must be 16-byte aligned");
+  void* ws = workspace(WS_ACT, act8_bytes(M, K));
+  if (!ws) return KQ_ERR_NOMEM;
+  Act8 act = act8_view(ws, M, K);
+  st = launch_quantize_act(x, act, M, K, act_mode, s);
+  if (st) return st;
+  return dispatch_gemm(wtype, w, act, out, M, N, K, s, true);
+}
+
+kq_status_t kq_mul_mat_q8x(int wtype, const void* w, const int8_t* a_qs, const float* a_ds, float* out, int M, int N,
+                           int K, kq_stream_t stream) {
+  kq_status_t st = check_gemm_args(wtype, w, a_qs, out, M, N, K);
+  if (st) return st;
+  if ((long long)M * N == 0) return KQ_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (K == 0) return zero_output(out, M, N, s);
+  if (!a_ds || !aligned(a_qs, 16) || !aligned(a_ds, 8))
+    return fail(KQ_ERR_INVALID, "staged activations: codes must be 16-byte and scales 8-byte aligned");
+  Act8 act{const_cast<int8_t*>(a_qs), reinterpret_cast<float2*>(const_cast<float*>(a_ds))};
+  return dispatch_gemm(wtype, w, act, out, M, N, K, s, false);
+}
+
+kq_status_t kq_block_sums_i32(int wtype, const void* w, const void* a_q8_1, int32_t* sumi, int M, int N, int K,
+                              kq_stream_t stream) {
+  if (block_bytes(wtype) == 0) return fail(KQ_ERR_INVALID, "unknown weight type %d", wtype);
+  if (M < 0 || N < 0 || K < 0 || K % 32) return fail(KQ_ERR_INVALID, "block_sums: bad shape");
+  if ((long long)M * N * K == 0) return KQ_OK;
+  if (!w || !a_q8_1 || !sumi) return fail(KQ_ERR_INVALID, "block_sums: null pointer");
+  return launch_block_sums(wtype, w, a_q8_1, sumi, M, N, K, static_cast<cudaStream_t>(stream));
+}
+
+kq_status_t kq_fa_decode_q8_0_mha(const float* q, const void* k, const void* v, float* out, int B, int S, int H,
+                                  int D, kq_stream_t stream) {
+  if (B < 0 || S < 0 || H < 0 || D <= 0 || D % 32 || D > 256)
+    return fail(KQ_ERR_INVALID, "fa_mha: bad shape B=%d S=%d H=%d D=%d (D must be a multiple of 32, <= 256)", B, S, H, D);
+  if ((long long)B * H == 0) return KQ_OK;
+  if (!q || !out || (S > 0 && (!k || !v))) return fail(KQ_ERR_INVALID, "fa_mha: null pointer");
+  if (!aligned(k, 2) || !aligned(v, 2)) return fail(KQ_ERR_INVALID, "fa_mha: caches must be 2-byte aligned");
+  return launch_fa_mha(q, k, v, out, B, S, H, D, static_cast<cudaStream_t>(stream));
+}
+
+kq_status_t kq_fa_decode_q8_0_ragged(const void* q_f16, const void* k, const void* v, const int32_t* cu_seqlens,
+                                     int B, int Hq, int Hkv, int D, int max_seqlen, float scale, void* out_f16,
+                                     kq_stream_t stream) {
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || D <= 0 || D % 32 || D > 256 || max_seqlen < 0)
+    return fail(KQ_ERR_INVALID, "fa_ragged: bad shape B=%d Hq=%d Hkv=%d D=%d", B, Hq, Hkv, D);
+  if (B == 0) return KQ_OK;
+  if (!q_f16 || !out_f16 || !cu_seqlens || !k || !v) return fail(KQ_ERR_INVALID, "fa_ragged: null pointer");
+  if (!aligned(k, 2) || !aligned(v, 2)) return fail(KQ_ERR_INVALID, "fa_ragged: caches must be 2-byte aligned");
+  return launch_fa_ragged(q_f16, k, v, cu_seqlens, B, Hq, Hkv, D, max_seqlen, scale, out_f16,
+                          static_cast<cudaStream_t>(stream));
+}
+
+// ---- KernelEvalPlus operator ABI --------------------------------------------
+
+void kq_w4a32c8_q4_0_fp32_int8(const uint8_t* weight, const float* activation, float* output, int M, int N, int K) {
+  kq_gemm_f32act(KQ_Q4_0, weight, activation, output, M, N, K, KQ_ACT_F32, nullptr);
+}
+
+void kq_w4a32c8_q4_1_fp32_int8(const uint8_t* weight, const float* activation, float* output, int M, int N, int K) {
+  kq_gemm_f32act(KQ_Q4_1, weight, activation, output, M, N, K, KQ_ACT_F32, nullptr);
+}
+
+void kq_w8a32c8_q8_0_fp32_int8(const uint8_t* weight, const float* activation, float* output, int M, int N, int K) {
+  kq_gemm_f32act(KQ_Q8_0, weight, activation, output, M, N, K, KQ_ACT_F32, nullptr);
+}
+
+void kq_w4a8_q4_0_q8_1(const uint8_t* weight, const uint8_t* activation, float* output, int M, int N, int K) {
+  kq_mul_mat_q(KQ_Q4_0, weight, activation, output, M, N, K, nullptr);
+}
+
+void kq_flash_attn_q8_0(const float* query, const void* key_cache, const void* value_cache, float* output,
+                        int batch_size, int seq_len, int num_heads, int head_dim) {
+  kq_fa_decode_q8_0_mha(query, key_cache, value_cache, output, batch_size, seq_len, num_heads, head_dim, nullptr);
+}
+
+}  // extern "C"

@@ -1,0 +1,76 @@
+// Internal host-side declarations shared by the libkq translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "kq.h"
+
+namespace kq {
+
+// ---- errors ---------------------------------------------------------------
+// Records `msg` as the calling thread's last error and returns `st`.
+kq_status_t fail(kq_status_t st, const char* fmt, ...);
+// Turns a pending launch / runtime error into KQ_ERR_CUDA.
+kq_status_t check_cuda(cudaError_t e, const char* what);
+kq_status_t check_launch(const char* what);
+
+// ---- device properties ----------------------------------------------------
+int current_device();
+int sm_count();
+
+// ---- workspace ------------------------------------------------------------
+// Per-device cached scratch, one buffer per slot, grown on demand (never
+// shrunk). The buffer is ordered on `stream`: growing it synchronises the
+// device before the old buffer is freed. Returns nullptr (and records the
+// error) on allocation failure.
+enum WsSlot { WS_ACT = 0, WS_FA = 1, WS_MOE = 2, WS_MOE2 = 3, WS_NSLOTS = 8 };
+void* workspace(WsSlot slot, size_t bytes);
+// Device error word of the current device (zeroed at allocation).
+int* device_error_word();
+
+// ---- activation staging ---------------------------------------------------
+// Quantised activations as the kernels consume them: int8 codes row-major
+// [M, K] (row stride K bytes) and one float2 (d, s) per 32-block [M, K/32].
+struct Act8 {
+  int8_t* qs;
+  float2* ds;
+};
+inline size_t act8_bytes(int M, int K) {
+  const size_t q = ((size_t)M * K + 255) & ~(size_t)255;
+  return q + (size_t)M * (K / 32) * sizeof(float2);
+}
+inline Act8 act8_view(void* base, int M, int K) {
+  const size_t q = ((size_t)M * K + 255) & ~(size_t)255;
+  return Act8{static_cast<int8_t*>(base), reinterpret_cast<float2*>(static_cast<char*>(base) + q)};
+}
+
+inline int block_bytes(int wtype) {
+  return wtype == KQ_Q4_0 ? 18 : wtype == KQ_Q4_1 ? 20 : wtype == KQ_Q8_0 ? 34 : 0;
+}
+
+// ---- kernel launchers (one per translation unit family) -------------------
+// quantize.cu
+kq_status_t launch_quantize_act(const float* x, Act8 act, int M, int K, int mode, cudaStream_t s);
+kq_status_t launch_quantize_q8_1_bytes(const float* x, void* y, int64_t M, int64_t K, int mode, cudaStream_t s);
+kq_status_t launch_quantize_rows(int wtype, const float* x, void* y, int64_t rows, int64_t K, cudaStream_t s);
+kq_status_t launch_q8_1_to_act(const void* a_q8_1, Act8 act, int M, int K, cudaStream_t s);
+// gemv.cu (M <= 8, K % 256 == 0); `pdl` = launched as a programmatic
+// dependent of the preceding kernel on `s` (the activation producer).
+bool gemv_supported(int wtype, int M, int N, int K);
+kq_status_t launch_gemv(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, bool pdl,
+                        cudaStream_t s);
+// gemm_simt.cu (any shape; the generic path)
+kq_status_t launch_gemm_simt(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, cudaStream_t s);
+kq_status_t launch_block_sums(int wtype, const void* w, const void* a_q8_1, int32_t* sumi, int M, int N, int K,
+                              cudaStream_t s);
+// fa_decode.cu
+kq_status_t launch_fa_mha(const float* q, const void* k, const void* v, float* out, int B, int S, int H, int D,
+                          cudaStream_t s);
+kq_status_t launch_fa_ragged(const void* q, const void* k, const void* v, const int32_t* cu, int B, int Hq, int Hkv,
+                             int D, int max_seqlen, float scale, void* out, cudaStream_t s);
+
+}  // namespace kq

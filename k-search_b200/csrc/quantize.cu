@@ -1,0 +1,264 @@
+// Activation quantisation: fp32 rows -> q8_1 (reference byte layout) or the
+// kernels' staging layout (int8 codes [M, K] + float2 (d, s) per block).
+//
+// Semantics follow llm_kernel_test/reference/quantize.py:165-214 exactly:
+//   amax = max |x|, d = amax / 127 (IEEE fp32 division), d = 1 if amax == 0,
+//   q = round_half_even(x / d) clamped to [-128, 127],
+//   s = fp32 sum of the 32 values in numpy's pairwise order (8 strided
+//       partial sums r[j] = x[j] + x[j+8] + x[j+16] + x[j+24], then
+//       ((r0+r1)+(r2+r3)) + ((r4+r5)+(r6+r7)), then added to +0.0).
+// The reference's GPU kernel (include/quantize.h:302-340) uses one thread per
+// block, x * (1/d) and a serial sum; this one uses 8 lanes per block with
+// 16-byte loads and reproduces the Python oracle bit for bit instead.
+#include <algorithm>
+
+#include "kq_internal.h"
+#include "kq_device.cuh"
+
+namespace kq {
+namespace {
+
+struct BlockQ {
+  uint32_t qs;  // this lane's 4 codes, packed little endian
+  float d;      // fp32 scale (unrounded)
+  float s;      // fp32 sum per mode (unrounded)
+};
+
+// 8 lanes (an aligned octet of the warp) quantise one 32-value block; lane
+// `sub` holds values 4*sub .. 4*sub+3. All 32 lanes must call this.
+template <int MODE>
+__device__ __forceinline__ BlockQ quantize_octet(float4 v, int lane) {
+  const unsigned full = 0xffffffffu;
+  const int sub = lane & 7;
+  const int base = lane & ~7;
+
+  float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+  amax = fmaxf(amax, __shfl_xor_sync(full, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(full, amax, 2));
+  amax = fmaxf(amax, __shfl_xor_sync(full, amax, 4));
+  const float d = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+
+  int q0 = max(-128, min(127, __float2int_rn(__fdiv_rn(v.x, d))));
+  int q1 = max(-128, min(127, __float2int_rn(__fdiv_rn(v.y, d))));
+  int q2 = max(-128, min(127, __float2int_rn(__fdiv_rn(v.z, d))));
+  int q3 = max(-128, min(127, __float2int_rn(__fdiv_rn(v.w, d))));
+  BlockQ r;
+  r.qs = (uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8) | ((uint32_t)(q2 & 0xff) << 16) |
+         ((uint32_t)(q3 & 0xff) << 24);
+  r.d = d;
+
+  if (MODE == KQ_ACT_SUM_DQ) {
+    int sq = q0 + q1 + q2 + q3;
+    sq += __shfl_xor_sync(full, sq, 1);
+    sq += __shfl_xor_sync(full, sq, 2);
+    sq += __shfl_xor_sync(full, sq, 4);
+    const float dh = __half2float(__float2half_rn(d));
+    r.s = __fmul_rn(dh, (float)sq);
+  } else {
+    // numpy pairwise order. Value j of the block is lane j/4, component j%4.
+    // Lanes sub=0 and sub=1 build r[4*sub + c] = x[4sub+c] + x[4sub+c+8]
+    // + x[4sub+c+16] + x[4sub+c+24] (lanes sub, sub+2, sub+4, sub+6).
+    const int a = sub & 1;
+    float t0 = v.x, t1 = v.y, t2 = v.z, t3 = v.w;
+#pragma unroll
+    for (int k = 1; k < 4; ++k) {
+      const int src = base + a + 2 * k;
+      t0 = __fadd_rn(t0, __shfl_sync(full, v.x, src));
+      t1 = __fadd_rn(t1, __shfl_sync(full, v.y, src));
+      t2 = __fadd_rn(t2, __shfl_sync(full, v.z, src));
+      t3 = __fadd_rn(t3, __shfl_sync(full, v.w, src));
+    }
+    const float p = __fadd_rn(__fadd_rn(t0, t1), __fadd_rn(t2, t3));
+    const float other = __shfl_xor_sync(full, p, 1);
+    // lane sub=0 holds the left half of the final addition, sub=1 the right.
+    const float res = (a == 0) ? __fadd_rn(p, other) : __fadd_rn(other, p);
+    r.s = __fadd_rn(res, 0.0f);
+    r.s = __shfl_sync(full, r.s, base);
+  }
+  return r;
+}
+
+// One warp quantises 4 consecutive blocks per step (grid-stride).
+template <int MODE, bool BYTES>
+__global__ void __launch_bounds__(256) quantize_kernel(const float* __restrict__ x, int8_t* __restrict__ qs,
+                                                       float2* __restrict__ ds, uint8_t* __restrict__ q81,
+                                                       long long total_blocks) {
+  const int lane = threadIdx.x & 31;
+  const int grp = lane >> 3;
+  const int sub = lane & 7;
+  const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long b0 = ((long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 4; b0 < total_blocks;
+       b0 += nwarps * 4) {
+    const long long blk = b0 + grp;
+    const bool valid = blk < total_blocks;
+    const long long src = valid ? blk : b0;  // keep all lanes in the shuffles
+    const float4 v = __ldg(reinterpret_cast<const float4*>(x + src * 32) + sub);
+    const BlockQ r = quantize_octet<MODE>(v, lane);
+    if (!valid) continue;
+    if (BYTES) {
+      uint8_t* dst = q81 + blk * 36;
+      reinterpret_cast<uint32_t*>(dst + 4)[sub] = r.qs;
+      if (sub == 0) {
+        const uint32_t ds16 = float_to_half_bits(r.d) | (float_to_half_bits(r.s) << 16);
+        *reinterpret_cast<uint32_t*>(dst) = ds16;
+      }
+    } else {
+      reinterpret_cast<uint32_t*>(qs + blk * 32)[sub] = r.qs;
+      if (sub == 0) {
+        float2 o;
+        if (MODE == KQ_ACT_F32) {
+          o = make_float2(r.d, r.s);
+        } else {
+          o = make_float2(__half2float(__float2half_rn(r.d)), __half2float(__float2half_rn(r.s)));
+        }
+        ds[blk] = o;
+      }
+    }
+  }
+  // Let a programmatic dependent (the GEMV) start its weight prefetch; it
+  // reads these results only after griddepcontrol.wait.
+  pdl_launch_dependents();
+}
+
+// q8_1 bytes [blocks, 36] -> staging layout. One thread per block.
+__global__ void __launch_bounds__(256) q8_1_to_act_kernel(const uint8_t* __restrict__ a, int8_t* __restrict__ qs,
+                                                          float2* __restrict__ ds, long long total_blocks) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < total_blocks) {
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(a + i * 36);
+    const uint32_t h = src[0];
+    uint4 lo = make_uint4(src[1], src[2], src[3], src[4]);
+    uint4 hi = make_uint4(src[5], src[6], src[7], src[8]);
+    uint4* dst = reinterpret_cast<uint4*>(qs + i * 32);
+    dst[0] = lo;
+    dst[1] = hi;
+    ds[i] = make_float2(half_bits_to_float(h), half_bits_to_float(h >> 16));
+  }
+  pdl_launch_dependents();
+}
+
+// Weight / KV-cache quantisers, one warp per 32-value block, lane = element.
+// Bit-exact with quantize.py:12-162 (division and round-half-even, not the
+// reciprocal-multiply of include/quantize.h:221-294).
+template <int WT>
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restrict__ x, uint8_t* __restrict__ y,
+                                                            long long total_blocks) {
+  const unsigned full = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long blk = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); blk < total_blocks;
+       blk += nwarps) {
+    const float v = x[blk * 32 + lane];
+    if (WT == KQ_Q8_0) {
+      float amax = fabsf(v);
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(full, amax, o));
+      const float d = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+      const int q = max(-128, min(127, __float2int_rn(__fdiv_rn(v, d))));
+      uint8_t* b = y + blk * 34;
+      b[2 + lane] = (uint8_t)(q & 0xff);
+      if (lane == 0) *reinterpret_cast<uint16_t*>(b) = (uint16_t)float_to_half_bits(d);
+    } else {
+      float lo = v, hi = v;
+      if (WT == KQ_Q4_0) {
+        lo = fabsf(v);
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) lo = fmaxf(lo, __shfl_xor_sync(full, lo, o));
+      } else {
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+          lo = fminf(lo, __shfl_xor_sync(full, lo, o));
+          hi = fmaxf(hi, __shfl_xor_sync(full, hi, o));
+        }
+      }
+      float d;
+      int q;
+      if (WT == KQ_Q4_0) {
+        d = lo > 0.0f ? __fdiv_rn(lo, 7.0f) : 1.0f;  // lo holds amax here
+        q = max(0, min(15, __float2int_rn(__fadd_rn(__fdiv_rn(v, d), 8.0f))));
+      } else {
+        d = hi > lo ? __fdiv_rn(__fsub_rn(hi, lo), 15.0f) : 1.0f;
+        q = max(0, min(15, __float2int_rn(__fdiv_rn(__fsub_rn(v, lo), d))));
+      }
+      const int qhi = __shfl_down_sync(full, q, 16);
+      const int hdr = (WT == KQ_Q4_0) ? 2 : 4;
+      uint8_t* b = y + blk * (WT == KQ_Q4_0 ? 18 : 20);
+      if (lane < 16) b[hdr + lane] = (uint8_t)((q & 0x0F) | ((qhi & 0x0F) << 4));
+      if (lane == 0) {
+        reinterpret_cast<uint16_t*>(b)[0] = (uint16_t)float_to_half_bits(d);
+        if (WT == KQ_Q4_1) reinterpret_cast<uint16_t*>(b)[1] = (uint16_t)float_to_half_bits(lo);
+      }
+    }
+  }
+}
+
+int grid_for(long long total_blocks) {
+  const long long warps = (total_blocks + 3) / 4;
+  const long long ctas = (warps + 7) / 8;
+  const long long cap = (long long)sm_count() * 8;
+  return (int)std::max(1LL, std::min(ctas, cap));
+}
+
+}  // namespace
+
+kq_status_t launch_quantize_act(const float* x, Act8 act, int M, int K, int mode, cudaStream_t s) {
+  const long long nb = (long long)M * (K / 32);
+  if (nb == 0) return KQ_OK;
+  const int grid = grid_for(nb);
+  switch (mode) {
+    case KQ_ACT_SUM_X:
+      quantize_kernel<KQ_ACT_SUM_X, false><<<grid, 256, 0, s>>>(x, act.qs, act.ds, nullptr, nb);
+      break;
+    case KQ_ACT_SUM_DQ:
+      quantize_kernel<KQ_ACT_SUM_DQ, false><<<grid, 256, 0, s>>>(x, act.qs, act.ds, nullptr, nb);
+      break;
+    case KQ_ACT_F32:
+      quantize_kernel<KQ_ACT_F32, false><<<grid, 256, 0, s>>>(x, act.qs, act.ds, nullptr, nb);
+      break;
+    default:
+      return fail(KQ_ERR_INVALID, "unknown activation mode %d", mode);
+  }
+  return check_launch("quantize_act");
+}
+
+kq_status_t launch_quantize_q8_1_bytes(const float* x, void* y, int64_t M, int64_t K, int mode, cudaStream_t s) {
+  const long long nb = (long long)M * (K / 32);
+  if (nb == 0) return KQ_OK;
+  const int grid = grid_for(nb);
+  uint8_t* out = static_cast<uint8_t*>(y);
+  switch (mode) {
+    case KQ_ACT_SUM_X:
+      quantize_kernel<KQ_ACT_SUM_X, true><<<grid, 256, 0, s>>>(x, nullptr, nullptr, out, nb);
+      break;
+    case KQ_ACT_SUM_DQ:
+      quantize_kernel<KQ_ACT_SUM_DQ, true><<<grid, 256, 0, s>>>(x, nullptr, nullptr, out, nb);
+      break;
+    default:
+      return fail(KQ_ERR_INVALID, "q8_1 bytes hold fp16 d and s: sum_mode must be KQ_ACT_SUM_X or KQ_ACT_SUM_DQ");
+  }
+  return check_launch("quantize_q8_1");
+}
+
+kq_status_t launch_quantize_rows(int wtype, const float* x, void* y, int64_t rows, int64_t K, cudaStream_t s) {
+  const long long nb = (long long)rows * (K / 32);
+  if (nb == 0) return KQ_OK;
+  const int grid = (int)std::min<long long>((nb + 7) / 8, (long long)sm_count() * 16);
+  uint8_t* out = static_cast<uint8_t*>(y);
+  switch (wtype) {
+    case KQ_Q4_0: quantize_rows_kernel<KQ_Q4_0><<<grid, 256, 0, s>>>(x, out, nb); break;
+    case KQ_Q4_1: quantize_rows_kernel<KQ_Q4_1><<<grid, 256, 0, s>>>(x, out, nb); break;
+    case KQ_Q8_0: quantize_rows_kernel<KQ_Q8_0><<<grid, 256, 0, s>>>(x, out, nb); break;
+    default: return fail(KQ_ERR_INVALID, "unknown weight type %d", wtype);
+  }
+  return check_launch("quantize_rows");
+}
+
+kq_status_t launch_q8_1_to_act(const void* a_q8_1, Act8 act, int M, int K, cudaStream_t s) {
+  const long long nb = (long long)M * (K / 32);
+  if (nb == 0) return KQ_OK;
+  const int grid = (int)((nb + 255) / 256);
+  q8_1_to_act_kernel<<<grid, 256, 0, s>>>(static_cast<const uint8_t*>(a_q8_1), act.qs, act.ds, nb);
+  return check_launch("q8_1_to_act");
+}
+
+}  // namespace kq

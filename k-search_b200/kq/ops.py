@@ -1,0 +1,176 @@
+"""PyTorch-facing operators over libkq (device tensors in, device tensors out).
+
+Every function runs on the current CUDA stream of its input's device and
+raises ``KQError`` on a non-zero status. Tensors must be contiguous CUDA
+tensors; nothing here falls back to a CPU path.
+
+Byte layouts are the reference's (kernelevalplus-main/include/quant_types.h):
+weights are uint8 tensors holding N rows of K/32 blocks (any shape whose
+element count is N * K/32 * block_bytes), q8_1 activations likewise.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from ._lib import check, lib
+
+WTYPES = {"q4_0": 0, "q4_1": 1, "q8_0": 2}
+BLOCK_BYTES = {"q4_0": 18, "q4_1": 20, "q8_0": 34, "q8_1": 36}
+# Activation-quantisation modes (include/kq.h KQ_ACT_*).
+ACT_MODES = {"sum_x": 0, "sum_dq": 1, "f32": 2}
+
+
+def _wtype(wtype) -> int:
+    if isinstance(wtype, int):
+        return wtype
+    w = str(wtype).replace("block_", "")
+    if w not in WTYPES:
+        raise ValueError(f"unsupported weight type {wtype!r}")
+    return WTYPES[w]
+
+
+def _act_mode(mode) -> int:
+    return mode if isinstance(mode, int) else ACT_MODES[mode]
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _cuda(t: torch.Tensor, name: str, dtype=None, numel=None) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if dtype is not None and t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    if numel is not None and t.numel() != numel:
+        raise ValueError(f"{name} has {t.numel()} elements, expected {numel}")
+    return t
+
+
+def quantize_q8_1(x: torch.Tensor, sum_mode: str = "sum_x") -> torch.Tensor:
+    """fp32 [M, K] -> q8_1 bytes uint8 [M, K/32, 36] (quantize.py:165-214)."""
+    _cuda(x, "x", torch.float32)
+    M, K = x.shape
+    y = torch.empty((M, K // 32, 36), dtype=torch.uint8, device=x.device)
+    check(lib().kq_quantize_q8_1(x.data_ptr(), y.data_ptr(), M, K, _act_mode(sum_mode), _stream(x)),
+          "kq_quantize_q8_1")
+    return y
+
+
+def quantize_rows(x: torch.Tensor, wtype="q8_0") -> torch.Tensor:
+    """fp32 [rows, K] -> q4_0 / q4_1 / q8_0 bytes uint8 [rows, K/32, block_bytes]
+    (quantize.py:12-162: weights and KV caches)."""
+    _cuda(x, "x", torch.float32)
+    wt = _wtype(wtype)
+    rows, K = x.shape
+    y = torch.empty((rows, K // 32, lib().kq_block_bytes(wt)), dtype=torch.uint8, device=x.device)
+    check(lib().kq_quantize_rows(wt, x.data_ptr(), y.data_ptr(), rows, K, _stream(x)), "kq_quantize_rows")
+    return y
+
+
+def mul_mat_q(weight: torch.Tensor, a_q8_1: torch.Tensor, M: int, N: int, K: int, wtype="q4_0",
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """Weights x pre-quantised q8_1 activations -> fp32 [M, N]."""
+    wt = _wtype(wtype)
+    nb = K // 32
+    _cuda(weight, "weight", torch.uint8, N * nb * lib().kq_block_bytes(wt))
+    _cuda(a_q8_1, "a_q8_1", torch.uint8, M * nb * 36)
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=weight.device)
+    check(lib().kq_mul_mat_q(wt, weight.data_ptr(), a_q8_1.data_ptr(), out.data_ptr(), M, N, K, _stream(weight)),
+          "kq_mul_mat_q")
+    return out
+
+
+def gemm_f32act(weight: torch.Tensor, activation: torch.Tensor, M: int, N: int, K: int, wtype="q4_0",
+                act_mode="f32", out: torch.Tensor | None = None) -> torch.Tensor:
+    """Weights x fp32 activations quantised on the fly -> fp32 [M, N]
+    (the harness quant_gemm operator; act_mode 'f32' is its semantics)."""
+    wt = _wtype(wtype)
+    nb = K // 32
+    _cuda(weight, "weight", torch.uint8, N * nb * lib().kq_block_bytes(wt))
+    _cuda(activation, "activation", torch.float32, M * K)
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=weight.device)
+    check(lib().kq_gemm_f32act(wt, weight.data_ptr(), activation.data_ptr(), out.data_ptr(), M, N, K,
+                               _act_mode(act_mode), _stream(weight)), "kq_gemm_f32act")
+    return out
+
+
+def mul_mat_q8x(weight: torch.Tensor, a_qs: torch.Tensor, a_ds: torch.Tensor, M: int, N: int, K: int, wtype="q4_0",
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """Weights x staged activations (int8 codes [M, K], fp32 (d, s) [M, K/32, 2]) -> fp32 [M, N]."""
+    wt = _wtype(wtype)
+    nb = K // 32
+    _cuda(weight, "weight", torch.uint8, N * nb * lib().kq_block_bytes(wt))
+    _cuda(a_qs, "a_qs", torch.int8, M * K)
+    _cuda(a_ds, "a_ds", torch.float32, M * nb * 2)
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=weight.device)
+    check(lib().kq_mul_mat_q8x(wt, weight.data_ptr(), a_qs.data_ptr(), a_ds.data_ptr(), out.data_ptr(), M, N, K,
+                               _stream(weight)), "kq_mul_mat_q8x")
+    return out
+
+
+def block_sums_i32(weight: torch.Tensor, a_q8_1: torch.Tensor, M: int, N: int, K: int, wtype="q4_0") -> torch.Tensor:
+    """int32 sumi [M, N, K/32] (the bit-exact parity quantity)."""
+    wt = _wtype(wtype)
+    nb = K // 32
+    _cuda(weight, "weight", torch.uint8, N * nb * lib().kq_block_bytes(wt))
+    _cuda(a_q8_1, "a_q8_1", torch.uint8, M * nb * 36)
+    out = torch.empty((M, N, nb), dtype=torch.int32, device=weight.device)
+    check(lib().kq_block_sums_i32(wt, weight.data_ptr(), a_q8_1.data_ptr(), out.data_ptr(), M, N, K, _stream(weight)),
+          "kq_block_sums_i32")
+    return out
+
+
+def flash_attn_q8_0(query: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor, batch_size: int,
+                    seq_len: int, num_heads: int, head_dim: int) -> torch.Tensor:
+    """Harness flash_attention with q8_0 caches -> fp32 [B, H, D]."""
+    _cuda(query, "query", torch.float32, batch_size * num_heads * head_dim)
+    nbytes = seq_len * num_heads * (head_dim // 32) * 34
+    _cuda(key_cache, "key_cache", None, None)
+    _cuda(value_cache, "value_cache", None, None)
+    if key_cache.numel() * key_cache.element_size() != nbytes or value_cache.numel() * value_cache.element_size() != nbytes:
+        raise ValueError("q8_0 cache size does not match seq_len * num_heads * head_dim/32 * 34 bytes")
+    out = torch.empty((batch_size, num_heads, head_dim), dtype=torch.float32, device=query.device)
+    check(lib().kq_fa_decode_q8_0_mha(query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), out.data_ptr(),
+                                      batch_size, seq_len, num_heads, head_dim, _stream(query)),
+          "kq_fa_decode_q8_0_mha")
+    return out
+
+
+def flash_decode_ragged(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: torch.Tensor, num_kv_heads: int,
+                        max_seqlen: int | None = None, scale: float | None = None,
+                        out: torch.Tensor | None = None) -> torch.Tensor:
+    """Ragged GQA decode: q fp16 [B, Hq, D]; k, v q8_0 bytes of [T, Hkv, D];
+    cu_seqlens int32 [B+1] (device). Returns fp16 [B, Hq, D]."""
+    _cuda(q, "q", torch.float16)
+    B, Hq, D = q.shape
+    _cuda(cu_seqlens, "cu_seqlens", torch.int32, B + 1)
+    _cuda(k, "k")
+    _cuda(v, "v")
+    if max_seqlen is None:
+        max_seqlen = int((cu_seqlens[1:] - cu_seqlens[:-1]).max().item()) if B else 0
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty_like(q)
+    check(lib().kq_fa_decode_q8_0_ragged(q.data_ptr(), k.data_ptr(), v.data_ptr(), cu_seqlens.data_ptr(), B, Hq,
+                                         num_kv_heads, D, int(max_seqlen), float(scale), out.data_ptr(), _stream(q)),
+          "kq_fa_decode_q8_0_ragged")
+    return out
+
+
+def device_error(stream: torch.cuda.Stream | None = None) -> int:
+    """Read and clear the device error word (0 = no device-side error)."""
+    import ctypes
+
+    s = (stream or torch.cuda.current_stream()).cuda_stream
+    code = ctypes.c_int(0)
+    check(lib().kq_device_error(ctypes.byref(code), s), "kq_device_error")
+    return code.value

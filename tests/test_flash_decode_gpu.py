@@ -1,0 +1,100 @@
+"""GPU parity of flash-attention decode over a q8_0 KV cache.
+
+Bar: rel-L2 <= 1e-3 and per element |out - ref| <= 1e-2 |ref| + 1e-3 rms(ref)
+against the fp64 oracle on the same q8_0 bytes; fp16 outputs are compared
+after the oracle's fp64 result (the fp16 rounding of the output is inside
+the bar). Plus the harness's NMSE <= 0.05 gate against unquantised K/V.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import quant as Q
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def test_golden_fixture(cuda):
+    import kq
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "flash_attn.npz"))
+    B, S, H, D = (int(g[k]) for k in "BSHD")
+    got = kq.flash_attn_q8_0(_t(g["q"], cuda), _t(g["k_q8_0"], cuda), _t(g["v_q8_0"], cuda), B, S, H, D).cpu().numpy()
+    ok, msg = Q.check_close(got, g["ref_on_q8_0"])
+    assert ok, msg
+    assert Q.nmse(got, g["ref_on_fp32"]) < 0.05
+
+
+@pytest.mark.parametrize("B,S,H,D", [(1, 512, 32, 128), (8, 1000, 4, 128), (3, 4096, 2, 64), (2, 1, 3, 32),
+                                     (16, 300, 2, 256)])
+def test_mha_parity(cuda, B, S, H, D):
+    import kq
+    rng = np.random.default_rng(B * S + H)
+    q = rng.standard_normal((B, H, D)).astype(np.float32)
+    kf = rng.standard_normal((S * H, D)).astype(np.float32)
+    vf = rng.standard_normal((S * H, D)).astype(np.float32)
+    k, v = Q.quantize_q8_0(kf), Q.quantize_q8_0(vf)
+    got = kq.flash_attn_q8_0(_t(q, cuda), _t(k, cuda), _t(v, cuda), B, S, H, D).cpu().numpy()
+    ok, msg = Q.check_close(got, Q.flash_decode_mha(q, k, v, S, H, D))
+    assert ok, msg
+
+
+def test_harness_void_entry(cuda):
+    import kq
+    rng = np.random.default_rng(5)
+    B, S, H, D = 2, 512, 32, 128
+    q = rng.standard_normal((B, H, D)).astype(np.float32)
+    kf = rng.standard_normal((S, H, D)).astype(np.float32)
+    vf = rng.standard_normal((S, H, D)).astype(np.float32)
+    k, v = Q.quantize_q8_0(kf.reshape(-1, D)), Q.quantize_q8_0(vf.reshape(-1, D))
+    out = torch.empty((B, H, D), dtype=torch.float32, device=cuda)
+    qd, kd, vd = _t(q, cuda), _t(k, cuda), _t(v, cuda)
+    torch.cuda.synchronize()
+    kq.lib().kq_flash_attn_q8_0(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), out.data_ptr(), B, S, H, D)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    ok, msg = Q.check_close(got, Q.flash_decode_mha(q, k, v, S, H, D))
+    assert ok, msg
+    # harness gate: attention on the unquantised caches
+    ref = np.einsum("bhs,shd->bhd", _softmax(np.einsum("bhd,shd->bhs", q, kf) / np.sqrt(D)), vf)
+    assert Q.nmse(got, ref) < 0.05
+
+
+def _softmax(x):
+    x = x - x.max(-1, keepdims=True)
+    e = np.exp(x)
+    return e / e.sum(-1, keepdims=True)
+
+
+def _ragged_case(rng, lens, Hq, Hkv, D):
+    B = len(lens)
+    cu = np.zeros(B + 1, dtype=np.int32)
+    cu[1:] = np.cumsum(lens)
+    T = int(cu[-1])
+    q = rng.standard_normal((B, Hq, D)).astype(np.float16)
+    k = Q.quantize_q8_0(rng.standard_normal((max(T, 1) * Hkv, D)).astype(np.float32))
+    v = Q.quantize_q8_0(rng.standard_normal((max(T, 1) * Hkv, D)).astype(np.float32))
+    return q, k, v, cu
+
+
+@pytest.mark.parametrize("lens,Hq,Hkv,D", [
+    ([64, 8192, 1000, 3], 32, 8, 128),
+    ([1, 2, 300, 257], 8, 8, 64),
+    ([500, 0, 77], 16, 2, 128),        # an empty sequence
+    ([4096] * 4, 32, 4, 128),
+])
+def test_ragged_parity(cuda, lens, Hq, Hkv, D):
+    import kq
+    rng = np.random.default_rng(sum(lens) + Hq)
+    q, k, v, cu = _ragged_case(rng, lens, Hq, Hkv, D)
+    scale = 1.0 / np.sqrt(D)
+    got = kq.flash_decode_ragged(_t(q, cuda), _t(k, cuda), _t(v, cuda), _t(cu, cuda), Hkv, scale=scale)
+    got = got.float().cpu().numpy()
+    ref = Q.flash_decode_ragged(q, k, v, cu, Hq, Hkv, D, scale)
+    ok, msg = Q.check_close(got, ref)
+    assert ok, msg

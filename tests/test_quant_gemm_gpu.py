@@ -1,0 +1,207 @@
+"""GPU parity of the quantised GEMV/GEMM path against the oracle.
+
+Bars: int32 block sums and q8_1 bytes bit-exact; fp32 outputs rel-L2 <= 1e-3
+and per element |out - ref| <= 1e-2 |ref| + 1e-3 rms(ref) (oracle.quant.check_close),
+plus the harness's own NMSE <= 0.05 gate against the fp32 dequant matmul.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import quant as Q
+
+pytestmark = pytest.mark.gpu
+MODES = {"sum_x": Q.SUM_X, "sum_dq": Q.SUM_DQ, "f32": Q.ACT_F32}
+
+
+def _t(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _x(rng, M, K):
+    return rng.standard_normal((M, K)).astype(np.float32)
+
+
+def test_quantize_q8_1_bit_exact(cuda):
+    import kq
+    rng = np.random.default_rng(10)
+    x = _x(rng, 33, 4096)
+    x[1] = 0.0
+    x[2, :64] = -0.0
+    x[3] *= np.float32(1e-6)
+    x[4] *= np.float32(1e4)
+    x[5, :32] = np.float32(0.5) * (np.arange(32) % 5 - 2)   # exact .5 ties
+    x[6, :32] = np.float32(1.0) * (np.arange(32) - 16)
+    for mode in ("sum_x", "sum_dq"):
+        got = kq.quantize_q8_1(_t(x, cuda), mode).cpu().numpy()
+        ref = Q.quantize_q8_1(x, MODES[mode])
+        assert np.array_equal(got, ref), (mode, np.argwhere(got != ref)[:5])
+
+
+def test_quantize_q8_1_golden(cuda):
+    import kq
+    g = np.load(__import__("os").path.join(__import__("os").path.dirname(__file__), "golden", "quantize.npz"))
+    got = kq.quantize_q8_1(_t(g["x"], cuda)).cpu().numpy().reshape(-1)
+    assert np.array_equal(got, g["q8_1"])
+
+
+@pytest.mark.parametrize("wtype", ["q4_0", "q4_1", "q8_0"])
+@pytest.mark.parametrize("M,N,K", [(1, 96, 256), (3, 200, 512), (8, 64, 4096), (5, 130, 96), (40, 72, 320)])
+def test_block_sums_bit_exact(cuda, wtype, M, N, K):
+    import kq
+    rng = np.random.default_rng(M * 1000 + N + K)
+    w = Q.make_blocks(wtype, rng, N, K)
+    a = Q.quantize_q8_1(_x(rng, M, K))
+    got = kq.block_sums_i32(_t(w, cuda), _t(a, cuda), M, N, K, wtype).cpu().numpy()
+    assert np.array_equal(got, Q.block_sums_i32(wtype, w, a, M, N, K))
+
+
+SHAPES = [
+    (1, 4096, 4096),    # configuration 0 (GEMV)
+    (1, 257, 512),      # ragged row split
+    (2, 1000, 1024),
+    (3, 333, 768),
+    (4, 512, 4352),     # K slices with a partial tail (nb = 136)
+    (5, 96, 256),
+    (8, 1024, 2048),
+    (8, 77, 14336),     # long rows
+    (1, 64, 96),        # K % 256 != 0 -> generic path
+    (16, 256, 512),
+    (64, 320, 1024),
+]
+
+
+@pytest.mark.parametrize("wtype", ["q4_0", "q4_1", "q8_0"])
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_gemm_f32act_parity(cuda, wtype, M, N, K):
+    import kq
+    rng = np.random.default_rng(7 * M + N + 3 * K)
+    w = Q.make_blocks(wtype, rng, N, K)
+    x = _x(rng, M, K)
+    wd, xd = _t(w, cuda), _t(x, cuda)
+    for mode in ("f32", "sum_x", "sum_dq"):
+        got = kq.gemm_f32act(wd, xd, M, N, K, wtype, mode).cpu().numpy()
+        ref = Q.gemm_f32act(wtype, w, x, M, N, K, MODES[mode])
+        ok, msg = Q.check_close(got, ref)
+        assert ok, f"{mode}: {msg}"
+
+
+@pytest.mark.parametrize("wtype", ["q4_0", "q4_1", "q8_0"])
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (4, 300, 1024), (8, 128, 256), (12, 64, 512)])
+def test_mul_mat_q_parity(cuda, wtype, M, N, K):
+    import kq
+    rng = np.random.default_rng(M + N + K)
+    w = Q.make_blocks(wtype, rng, N, K)
+    a = Q.quantize_q8_1(_x(rng, M, K))
+    got = kq.mul_mat_q(_t(w, cuda), _t(a, cuda), M, N, K, wtype).cpu().numpy()
+    ok, msg = Q.check_close(got, Q.gemm_q8_1(wtype, w, a, M, N, K))
+    assert ok, msg
+
+
+def test_golden_reference_outputs(cuda):
+    """The fixtures hold the reference's own gemm_ref.py outputs."""
+    import kq
+    import os
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "gemm.npz"))
+    M, N, K = int(g["M"]), int(g["N"]), int(g["K"])
+    for wtype, key in (("q4_0", "ref_q4_0_q8_1"), ("q4_1", "ref_q4_1_q8_1")):
+        got = kq.mul_mat_q(_t(g["w_" + wtype], cuda), _t(g["a_q8_1"], cuda), M, N, K, wtype).cpu().numpy()
+        ok, msg = Q.check_close(got, g[key])
+        assert ok, msg
+    for wtype in ("q4_0", "q4_1", "q8_0"):
+        got = kq.gemm_f32act(_t(g["w_" + wtype], cuda), _t(g["act"], cuda), M, N, K, wtype).cpu().numpy()
+        assert Q.nmse(got, g[f"ref_{wtype}_fp32"]) < 0.05
+    v = np.load(os.path.join(os.path.dirname(__file__), "golden", "variants.npz"))
+    M, N, K = int(v["M"]), int(v["N"]), int(v["K"])
+    got = kq.gemm_f32act(_t(v["w_q4_0"], cuda), _t(v["act"], cuda), M, N, K, "q4_0", "f32").cpu().numpy()
+    ok, msg = Q.check_close(got, v["ref_w4a32c8"])
+    assert ok, msg
+    got = kq.gemm_f32act(_t(v["w_q8_0"], cuda), _t(v["act"], cuda), M, N, K, "q8_0", "f32").cpu().numpy()
+    ok, msg = Q.check_close(got, v["ref_w8a8c8"])
+    assert ok, msg
+
+
+@pytest.mark.parametrize("wtype", ["q4_0", "q4_1", "q8_0"])
+@pytest.mark.parametrize("M", [1, 8, 512])
+def test_harness_configs(cuda, wtype, M):
+    """The harness's own test configurations (op_test_handler.py:449-458: M in
+    {1, 8, 512}) on weights quantised from N(0,1) as the harness makes them,
+    against the fp32 dequant-matmul gate (NMSE <= 0.05) and the oracle."""
+    import kq
+    N, K = 512, 4096
+    rng = np.random.default_rng(M)
+    wf = rng.standard_normal((N, K)).astype(np.float32)
+    w = Q.quantize_weights(wtype, wf)
+    x = _x(rng, M, K)
+    got = kq.gemm_f32act(_t(w, cuda), _t(x, cuda), M, N, K, wtype).cpu().numpy()
+    assert not np.isnan(got).any() and not np.isinf(got).any()
+    assert Q.nmse(got, Q.gemm_dequant_f32(wtype, w, x, M, N, K)) < 0.05
+    ok, msg = Q.check_close(got, Q.gemm_f32act(wtype, w, x, M, N, K, Q.ACT_F32))
+    assert ok, msg
+
+
+def test_void_harness_entry_points(cuda):
+    """The signature-for-signature KernelEvalPlus entries (legacy stream)."""
+    import kq
+    L = kq.lib()
+    rng = np.random.default_rng(11)
+    M, N, K = 3, 256, 1024
+    x = _x(rng, M, K)
+    for wtype, fn in (("q4_0", L.kq_w4a32c8_q4_0_fp32_int8), ("q4_1", L.kq_w4a32c8_q4_1_fp32_int8),
+                      ("q8_0", L.kq_w8a32c8_q8_0_fp32_int8)):
+        w = Q.make_blocks(wtype, rng, N, K)
+        wd, xd = _t(w, cuda), _t(x, cuda)
+        out = torch.empty((M, N), dtype=torch.float32, device=cuda)
+        torch.cuda.synchronize()
+        fn(wd.data_ptr(), xd.data_ptr(), out.data_ptr(), M, N, K)
+        torch.cuda.synchronize()
+        ok, msg = Q.check_close(out.cpu().numpy(), Q.gemm_f32act(wtype, w, x, M, N, K, Q.ACT_F32))
+        assert ok, f"{wtype}: {msg}"
+    w = Q.make_q4_0_blocks(rng, N, K)
+    a = Q.quantize_q8_1(x)
+    out = torch.empty((M, N), dtype=torch.float32, device=cuda)
+    torch.cuda.synchronize()
+    L.kq_w4a8_q4_0_q8_1(_t(w, cuda).data_ptr(), _t(a, cuda).data_ptr(), out.data_ptr(), M, N, K)
+    torch.cuda.synchronize()
+    ok, msg = Q.check_close(out.cpu().numpy(), Q.gemm_q8_1("q4_0", w, a, M, N, K))
+    assert ok, msg
+
+
+def test_errors_raise(cuda):
+    import kq
+    w = torch.zeros(18 * 4, dtype=torch.uint8, device=cuda)
+    x = torch.zeros((1, 100), dtype=torch.float32, device=cuda)
+    with pytest.raises((kq.KQError, ValueError)):
+        kq.gemm_f32act(w, x, 1, 1, 100, "q4_0")
+    with pytest.raises(ValueError):
+        kq.gemm_f32act(w.cpu(), x, 1, 1, 128, "q4_0")
+    assert kq.device_error() == 0
+
+
+def test_stream_and_repeat_determinism(cuda):
+    """Same inputs on a side stream give the identical bits (no atomics)."""
+    import kq
+    rng = np.random.default_rng(12)
+    M, N, K = 4, 2048, 4096
+    w, x = _t(Q.make_q4_0_blocks(rng, N, K), cuda), _t(_x(rng, M, K), cuda)
+    a = kq.gemm_f32act(w, x, M, N, K)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        b = kq.gemm_f32act(w, x, M, N, K)
+    s.synchronize()
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("wtype", ["q4_0", "q4_1", "q8_0"])
+def test_quantize_rows_bit_exact(cuda, wtype):
+    import kq
+    rng = np.random.default_rng(21)
+    w = rng.standard_normal((37, 512)).astype(np.float32)
+    w[1] = 0.0
+    w[2, 32:64] = 3.0          # constant block (q4_1: max == min)
+    w[3] *= np.float32(1e-5)
+    got = kq.quantize_rows(_t(w, cuda), wtype).cpu().numpy()
+    assert np.array_equal(got, Q.quantize_weights(wtype, w))
+    g = np.load(__import__("os").path.join(__import__("os").path.dirname(__file__), "golden", "quantize.npz"))
+    got = kq.quantize_rows(_t(g["w"], cuda), wtype).cpu().numpy().reshape(-1)
+    assert np.array_equal(got, g[wtype])
