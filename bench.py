@@ -158,6 +158,44 @@ def barrier(world: int):
         dist.barrier()
 
 
+def graph_time_ms(step, steps: int, warmup: int, world: int, clocks=None) -> tuple[float, dict | None]:
+    """Capture `steps` calls of step(i) in one CUDA graph, replay it once
+    untimed, then time one replay with CUDA events on the capturing stream.
+    Launch overhead of the Python / ctypes layer is outside the timed region;
+    the kernels run back to back as they would in a captured serving step."""
+    import torch
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for i in range(warmup):
+            step(i)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(steps):
+            step(i)
+    g.replay()
+    torch.cuda.synchronize()
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop() if clocks else None
+    del g
+    return max_over_ranks(ms, world), clk
+
+
 # ---------------------------------------------------------------------------
 # CPU baseline (reference C++ routines or the oracle port)
 # ---------------------------------------------------------------------------
@@ -253,33 +291,14 @@ def bench_gemm(args, cfg, rank, world):
     L = kq.lib()
     wtc = kq.WTYPES[wt]
     act_mode = kq.ACT_MODES[cfg["act"]]
-    stream = torch.cuda.current_stream()
-    sp = stream.cuda_stream
-
     def step(i):
         j = i % nsets
+        sp = torch.cuda.current_stream().cuda_stream
         _lib.check(L.kq_gemm_f32act(wtc, ws[j].data_ptr(), xs[j].data_ptr(), outs[j].data_ptr(), M, N, K, act_mode, sp),
                    "kq_gemm_f32act")
 
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize()
     clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
-    if clocks:
-        clocks.start()
-        time.sleep(0.3)
-    barrier(world)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(args.steps):
-        step(i)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    barrier(world)
-    ms = e0.elapsed_time(e1)
-    clk = clocks.stop() if clocks else None
-    ms = max_over_ranks(ms, world)
+    ms, clk = graph_time_ms(step, args.steps, args.warmup, world, clocks)
     ops = 2.0 * M * N * K
     value = world * ops * args.steps / (ms * 1e-3) / 1e12
 
@@ -294,19 +313,14 @@ def bench_gemm(args, cfg, rank, world):
 
     def kstep(i):
         j = i % nsets
+        sp = torch.cuda.current_stream().cuda_stream
         _lib.check(L.kq_mul_mat_q8x(wtc, ws[j].data_ptr(), qs[j].data_ptr(), dss[j].data_ptr(), outs[j].data_ptr(),
                                     M, N, K, sp), "kq_mul_mat_q8x")
 
-    for i in range(3):
-        kstep(i)
-    torch.cuda.synchronize()
-    e0.record(stream)
-    for i in range(args.steps):
-        kstep(i)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    kms = e0.elapsed_time(e1) / args.steps
-    kms = max_over_ranks(kms, world)
+    kms, _ = graph_time_ms(kstep, args.steps, 3, world)
+    kms /= args.steps
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
     # ---- end to end through the public API with host buffers ----
     xh = [torch.randn((M, K), generator=g, dtype=torch.float32).pin_memory() for _ in range(2)]
@@ -394,23 +408,8 @@ def bench_fa(args, cfg, rank, world):
         j = i % nsets
         kq.flash_decode_ragged(q, ks[j], vs[j], cud, Hkv, maxlen, out=out)
 
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize()
     clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
-    if clocks:
-        clocks.start()
-        time.sleep(0.3)
-    barrier(world)
-    stream = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(args.steps):
-        step(i)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms = max_over_ranks(e0.elapsed_time(e1), world)
-    clk = clocks.stop() if clocks else None
+    ms, clk = graph_time_ms(step, args.steps, args.warmup, world, clocks)
     value = world * B * args.steps / (ms * 1e-3)
     per = ms / args.steps
     hbm, _, src = load_peaks()

@@ -118,6 +118,7 @@ kq_status_t check_gemm_args(int wtype, const void* w, const void* a, const float
 kq_status_t dispatch_gemm(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, cudaStream_t s,
                           bool pdl) {
   if (gemv_supported(wtype, M, N, K) && aligned(w, 16)) return launch_gemv(wtype, w, act, out, M, N, K, pdl, s);
+  if (gemm_tc_supported(wtype, M, N, K, w, act)) return launch_gemm_tc(wtype, w, act, out, M, N, K, pdl, s);
   return launch_gemm_simt(wtype, w, act, out, M, N, K, s);
 }
 

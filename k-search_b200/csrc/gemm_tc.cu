@@ -1,0 +1,512 @@
+// Tensor-core quantised GEMM for M > 8 activation rows (llama.cpp's
+// mul_mat_q family) on sm_100a: tcgen05.mma.kind::i8 with TMEM accumulators.
+//
+//   out[m, n] = sum_b scale(m, n, b) * sumi[m, n, b]
+//   sumi[m, n, b] = sum_{i<32} q_a[m, 32b+i] * q_w[n, b, i]      (exact int32)
+//   q8_0: scale term d_w * d_a * sumi                   (gemm_reference.h:311-336)
+//   q4_0: d_w * (d_a * sumi - 8 s_a)   (codes 0..15)    (gemm_ref.py:100-153)
+//   q4_1: d_w * d_a * sumi + m_w * s_a                  (gemm_ref.py:274-331)
+//
+// Every 32-wide K block has its own scales, so each block's product is a
+// separate MMA (K = 32, one instruction) into a fresh TMEM buffer; the fp32
+// accumulation across blocks happens in the epilogue warps' registers.
+//
+// CTA = 14 warps, one CTA per SM, persistent over 128 x 128 output tiles
+// (tokens x weight rows), tokens fastest so co-running CTAs share weights in L2:
+//   warp 0      TMA producer: activation codes (int8 [M, K], 128B-swizzled
+//               boxes of 128 rows x 128 B = 4 blocks), activation (d, s)
+//               pairs, and raw weight rows (the unchanged AoS q-blocks,
+//               128 rows x 8 blocks per box). No multicast anywhere.
+//   warp 1      TMEM allocator + single-thread MMA issuer.
+//   warps 2-5   converters: one weight row per thread, raw AoS blocks ->
+//               int8 codes in the UMMA K-major SWIZZLE_128B layout + fp32
+//               scale rows, then fence.proxy.async and release the stage.
+//   warps 6-13  epilogue: two warpgroups (64 columns each) read the int32
+//               block result from TMEM (tcgen05.ld 32x32b), apply the block's
+//               scales and accumulate in fp32 registers; 4 TMEM buffers of
+//               128 columns let the MMA run ahead of the epilogue.
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "kq_internal.h"
+#include "kq_device.cuh"
+
+namespace kq {
+namespace {
+
+constexpr int TM = 128;        // tokens per tile (TMEM lanes)
+constexpr int TN = 128;        // weight rows per tile (TMEM columns per buffer)
+constexpr int KSUB = 4;        // blocks per activation / converted-weight stage (128 B of K)
+constexpr int KRAW = 8;        // blocks per raw weight stage (16-byte aligned for all block sizes)
+constexpr int SA = 3;          // activation stages
+constexpr int SWS = 3;         // converted weight stages
+constexpr int SRAW = 2;        // raw weight stages
+constexpr int NBUF = 4;        // TMEM buffers
+constexpr int kWarpTma = 0, kWarpMma = 1, kWarpConv = 2, kConvWarps = 4, kWarpEpi = 6, kEpiWarps = 8;
+constexpr int kWarps = kWarpEpi + kEpiWarps;
+constexpr int kThreads = kWarps * 32;
+constexpr int kTmemCols = NBUF * TN;  // 512
+
+template <int WT>
+struct TcTraits {
+  static constexpr int BB = WT == KQ_Q4_0 ? 18 : WT == KQ_Q4_1 ? 20 : 34;
+  static constexpr bool kHasMin = WT == KQ_Q4_1;
+  static constexpr bool kSignedW = WT == KQ_Q8_0;
+  static constexpr int RAW_ROW = KRAW * BB;                 // bytes per raw row per stage
+  static constexpr int RAW_STAGE = TN * RAW_ROW;
+  static constexpr int ACT_TILE = TM * 128;                 // 16 KB, 1024-aligned
+  static constexpr int W_TILE = TN * 128;                   // 16 KB
+  static constexpr int ASC_STAGE = TM * KSUB * 8;           // (d, s) per row and block
+  static constexpr int WSC_STAGE = KSUB * TN * 4 * (kHasMin ? 2 : 1);
+  // byte offsets in dynamic shared memory (base aligned to 1024)
+  static constexpr int OFF_ACT = 0;
+  static constexpr int OFF_W = OFF_ACT + SA * ACT_TILE;
+  static constexpr int OFF_RAW = OFF_W + SWS * W_TILE;
+  static constexpr int OFF_ASC = OFF_RAW + SRAW * RAW_STAGE;
+  static constexpr int OFF_WSC = OFF_ASC + SA * ASC_STAGE;
+  static constexpr int OFF_BAR = (OFF_WSC + SWS * WSC_STAGE + 15) / 16 * 16;
+  static constexpr int NBARS = 2 * SA + 2 * SWS + 2 * SRAW + 2 * NBUF;
+  static constexpr int OFF_TMEM = OFF_BAR + NBARS * 8;
+  static constexpr int SMEM = OFF_TMEM + 16 + 1024;  // + alignment slack
+  static_assert(RAW_ROW % 16 == 0, "raw rows must stay 16-byte aligned");
+  static_assert(SMEM <= 232448, "shared memory budget");
+};
+
+// ---- tcgen05 / TMA primitives ---------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// UMMA shared-memory descriptor: K-major, SWIZZLE_128B, 8-row groups 1024 B
+// apart (SBO), version 1 (sm_100).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;                 // LBO (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;       // SBO
+  d |= (uint64_t)1 << 46;                 // version
+  d |= (uint64_t)2 << 61;                 // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::i8: D s32, A = activations (signed),
+// B = weights (signed for q8_0, unsigned codes 0..15 for q4_x), both K-major.
+__host__ __device__ constexpr uint32_t idesc_i8(bool b_signed) {
+  return (2u << 4)                        // D format S32
+         | (1u << 7)                      // A signed 8-bit
+         | ((b_signed ? 1u : 0u) << 10)   // B signed / unsigned 8-bit
+         | ((uint32_t)(TN >> 3) << 17)    // N
+         | ((uint32_t)(TM >> 4) << 24);   // M
+}
+
+// byte offset of (row r, 16-byte chunk c) in a 128B-swizzled K-major tile
+__device__ __forceinline__ int sw128_off(int r, int c) { return (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4); }
+
+struct TcParams {
+  int M, N, K, nb;
+  int num_m_tiles, num_tiles;
+  float* out;
+  int* err;
+};
+
+template <int WT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_act, const __grid_constant__ CUtensorMap map_asc,
+                   const __grid_constant__ CUtensorMap map_raw, TcParams p) {
+  using T = TcTraits<WT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + T::OFF_BAR);
+  uint64_t* act_full = bars;
+  uint64_t* act_empty = act_full + SA;
+  uint64_t* w_full = act_empty + SA;
+  uint64_t* w_empty = w_full + SWS;
+  uint64_t* raw_full = w_empty + SWS;
+  uint64_t* raw_empty = raw_full + SRAW;
+  uint64_t* tm_full = raw_empty + SRAW;
+  uint64_t* tm_empty = tm_full + NBUF;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + T::OFF_TMEM);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkb8 = p.nb / KRAW;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < SA; ++i) {
+      mbar_init(&act_full[i], 1);
+      mbar_init(&act_empty[i], 1 + kEpiWarps);  // MMA commit + epilogue warps (they read the scales)
+    }
+    for (int i = 0; i < SWS; ++i) {
+      mbar_init(&w_full[i], kConvWarps);
+      mbar_init(&w_empty[i], 1 + kEpiWarps);
+    }
+    for (int i = 0; i < SRAW; ++i) {
+      mbar_init(&raw_full[i], 1);
+      mbar_init(&raw_empty[i], kConvWarps);
+    }
+    for (int i = 0; i < NBUF; ++i) {
+      mbar_init(&tm_full[i], 1);
+      mbar_init(&tm_empty[i], kEpiWarps);
+    }
+    fence_mbar_init();
+  }
+  if (warp == kWarpMma) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  bool dead = false;
+  if (warp == kWarpTma) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tmap(&map_act);
+      prefetch_tmap(&map_asc);
+      prefetch_tmap(&map_raw);
+      int ia = 0, ir = 0;
+      bool waited_pdl = false;
+      for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+        const int m0 = (t % p.num_m_tiles) * TM, n0 = (t / p.num_m_tiles) * TN;
+        for (int k8 = 0; k8 < nkb8; ++k8, ++ir) {
+          const int rs = ir % SRAW;
+          if (ir >= SRAW) mbar_wait_or_poison(&raw_empty[rs], ((ir / SRAW) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+          mbar_arrive_expect_tx(&raw_full[rs], T::RAW_STAGE);
+          tma_load_2d(smem + T::OFF_RAW + rs * T::RAW_STAGE, &map_raw, k8 * (T::RAW_ROW / 2), n0, &raw_full[rs]);
+          if (!waited_pdl) {  // activations are produced by the preceding kernel
+            pdl_wait();
+            waited_pdl = true;
+          }
+          for (int sub = 0; sub < KRAW / KSUB; ++sub, ++ia) {
+            const int as = ia % SA;
+            if (ia >= SA) mbar_wait_or_poison(&act_empty[as], ((ia / SA) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+            const int kb = k8 * KRAW + sub * KSUB;  // first block of this stage
+            mbar_arrive_expect_tx(&act_full[as], T::ACT_TILE + T::ASC_STAGE);
+            tma_load_2d(smem + T::OFF_ACT + as * T::ACT_TILE, &map_act, kb * 32, m0, &act_full[as]);
+            tma_load_2d(smem + T::OFF_ASC + as * T::ASC_STAGE, &map_asc, kb * 2, m0, &act_full[as]);
+          }
+        }
+      }
+    }
+  } else if (warp == kWarpMma) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_i8(T::kSignedW);
+      const uint32_t act_base = smem_u32(smem + T::OFF_ACT);
+      const uint32_t w_base = smem_u32(smem + T::OFF_W);
+      int ia = 0, iw = 0, ib = 0;
+      for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+        for (int s = 0; s < p.nb / KSUB; ++s, ++ia, ++iw) {
+          const int as = ia % SA, ws = iw % SWS;
+          mbar_wait_or_poison(&act_full[as], (ia / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+          mbar_wait_or_poison(&w_full[ws], (iw / SWS) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+          tc_fence_after();
+          const uint64_t adesc = sw128_desc(act_base + as * T::ACT_TILE);
+          const uint64_t bdesc = sw128_desc(w_base + ws * T::W_TILE);
+#pragma unroll
+          for (int j = 0; j < KSUB; ++j, ++ib) {
+            const int buf = ib % NBUF;
+            if (ib >= NBUF) mbar_wait_or_poison(&tm_empty[buf], ((ib / NBUF) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+            tc_fence_after();
+            // K block j of the stage: +32 bytes inside the 128-byte swizzle atom
+            mma_i8(tmem_base + buf * TN, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), idesc, 0u);
+            mma_commit(&tm_full[buf]);
+          }
+          mma_commit(&act_empty[as]);
+          mma_commit(&w_empty[ws]);
+        }
+      }
+    }
+  } else if (warp < kWarpEpi) {
+    // ------------------------------------------------------------ converters
+    const int r = (warp - kWarpConv) * 32 + lane;  // weight row in the tile
+    int ir = 0, iw = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+      for (int k8 = 0; k8 < nkb8; ++k8, ++ir) {
+        const int rs = ir % SRAW;
+        mbar_wait_or_poison(&raw_full[rs], (ir / SRAW) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+        const uint8_t* raw = smem + T::OFF_RAW + rs * T::RAW_STAGE + r * T::RAW_ROW;
+#pragma unroll
+        for (int sub = 0; sub < KRAW / KSUB; ++sub, ++iw) {
+          // this row's 4 raw blocks of the sub-stage, into registers
+          constexpr int HB = KSUB * T::BB;  // 72 / 80 / 136 bytes, 8-byte aligned
+          uint32_t w[HB / 4 + 1];
+          const uint8_t* src = raw + sub * HB;
+          if constexpr (HB % 16 == 0) {
+#pragma unroll
+            for (int i = 0; i < HB / 16; ++i) {
+              const uint4 v = reinterpret_cast<const uint4*>(src)[i];
+              w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < HB / 8; ++i) {
+              const uint2 v = reinterpret_cast<const uint2*>(src)[i];
+              w[2 * i] = v.x; w[2 * i + 1] = v.y;
+            }
+          }
+          w[HB / 4] = 0;
+          if (sub == KRAW / KSUB - 1) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&raw_empty[rs]);  // raw bytes of this stage are all in registers
+          }
+          const int ws = iw % SWS;
+          if (iw >= SWS) mbar_wait_or_poison(&w_empty[ws], ((iw / SWS) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+          uint8_t* wt = smem + T::OFF_W + ws * T::W_TILE;
+          float* wsc = reinterpret_cast<float*>(smem + T::OFF_WSC + ws * T::WSC_STAGE);
+#pragma unroll
+          for (int j = 0; j < KSUB; ++j) {
+            const int o = j * T::BB;  // byte offset of the block in w[] (compile time after unrolling)
+            auto u32 = [&](int off) -> uint32_t {
+              return (off & 3) ? __funnelshift_r(w[off >> 2], w[(off >> 2) + 1], 16) : w[off >> 2];
+            };
+            auto u16 = [&](int off) -> uint32_t { return (off & 3) ? (w[off >> 2] >> 16) : (w[off >> 2] & 0xFFFFu); };
+            uint4 c0, c1;
+            float mn = 0.0f;
+            const float d = half_bits_to_float(u16(o));
+            if constexpr (WT == KQ_Q8_0) {
+              c0 = make_uint4(u32(o + 2), u32(o + 6), u32(o + 10), u32(o + 14));
+              c1 = make_uint4(u32(o + 18), u32(o + 22), u32(o + 26), u32(o + 30));
+            } else {
+              const int q = o + (WT == KQ_Q4_0 ? 2 : 4);
+              if constexpr (WT == KQ_Q4_1) mn = half_bits_to_float(u16(o + 2));
+              const uint32_t a0 = u32(q), a1 = u32(q + 4), a2 = u32(q + 8), a3 = u32(q + 12);
+              c0 = make_uint4(a0 & 0x0F0F0F0Fu, a1 & 0x0F0F0F0Fu, a2 & 0x0F0F0F0Fu, a3 & 0x0F0F0F0Fu);
+              c1 = make_uint4((a0 >> 4) & 0x0F0F0F0Fu, (a1 >> 4) & 0x0F0F0F0Fu, (a2 >> 4) & 0x0F0F0F0Fu,
+                              (a3 >> 4) & 0x0F0F0F0Fu);
+            }
+            *reinterpret_cast<uint4*>(wt + sw128_off(r, 2 * j)) = c0;
+            *reinterpret_cast<uint4*>(wt + sw128_off(r, 2 * j + 1)) = c1;
+            wsc[j * TN + r] = d;
+            if constexpr (T::kHasMin) wsc[KSUB * TN + j * TN + r] = mn;
+          }
+          fence_proxy_async_smem();  // generic-proxy writes -> tensor-core reads
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&w_full[ws]);
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - kWarpEpi;
+    const int quarter = warp & 3;           // TMEM lane quarter this warp may access
+    const int half = ew >> 2;               // column half
+    const int row = quarter * 32 + lane;    // token row in the tile
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    int ia = 0, iw = 0, ib = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+      const int m0 = (t % p.num_m_tiles) * TM, n0 = (t / p.num_m_tiles) * TN;
+      float acc[64];
+#pragma unroll
+      for (int c = 0; c < 64; ++c) acc[c] = 0.0f;
+      for (int s = 0; s < p.nb / KSUB; ++s, ++ia, ++iw) {
+        const int as = ia % SA, ws = iw % SWS;
+        mbar_wait_or_poison(&act_full[as], (ia / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+        mbar_wait_or_poison(&w_full[ws], (iw / SWS) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+        const float2* asc = reinterpret_cast<const float2*>(smem + T::OFF_ASC + as * T::ASC_STAGE) + row * KSUB;
+        const float* wsc = reinterpret_cast<const float*>(smem + T::OFF_WSC + ws * T::WSC_STAGE);
+#pragma unroll 1
+        for (int j = 0; j < KSUB; ++j, ++ib) {
+          const int buf = ib % NBUF;
+          mbar_wait_or_poison(&tm_full[buf], (ib / NBUF) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+          tc_fence_after();
+          const uint32_t taddr = tmem_base + lane_addr + buf * TN + half * 64;
+          const float2 ds = asc[j];
+          const float* dw = wsc + j * TN + half * 64;
+          const float* mw = wsc + KSUB * TN + j * TN + half * 64;
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            uint32_t v[32];
+            tmem_ld32(taddr + 32 * h2, v);
+            tmem_ld_wait();
+            if (h2 == 1) {  // both halves are in registers: hand the buffer back to the MMA warp
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&tm_empty[buf]);
+            }
+#pragma unroll
+            for (int c4 = 0; c4 < 8; ++c4) {
+              const float4 w4 = reinterpret_cast<const float4*>(dw + 32 * h2)[c4];
+              const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+              float mv[4] = {0.f, 0.f, 0.f, 0.f};
+              if constexpr (WT == KQ_Q4_1) {
+                const float4 m4 = reinterpret_cast<const float4*>(mw + 32 * h2)[c4];
+                mv[0] = m4.x; mv[1] = m4.y; mv[2] = m4.z; mv[3] = m4.w;
+              }
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int c = 32 * h2 + 4 * c4 + e;
+                const float f = (float)(int)v[4 * c4 + e];
+                if constexpr (WT == KQ_Q8_0) {
+                  acc[c] = fmaf(wv[e] * ds.x, f, acc[c]);
+                } else if constexpr (WT == KQ_Q4_0) {
+                  acc[c] = fmaf(wv[e], fmaf(ds.x, f, -8.0f * ds.y), acc[c]);
+                } else {
+                  acc[c] = fmaf(wv[e] * ds.x, f, fmaf(mv[e], ds.y, acc[c]));
+                }
+              }
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&act_empty[as]);
+          mbar_arrive(&w_empty[ws]);
+        }
+      }
+      // ---- store this tile's rows ----
+      const int m = m0 + row;
+      const int nb0 = n0 + half * 64;
+      if (m < p.M) {
+        float* o = p.out + (size_t)m * p.N + nb0;
+        if (nb0 + 64 <= p.N && (p.N & 3) == 0) {
+#pragma unroll
+          for (int c = 0; c < 64; c += 4)
+            *reinterpret_cast<float4*>(o + c) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (nb0 + c < p.N) o[c] = acc[c];
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---- host side -----------------------------------------------------------------
+bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t dim0, uint64_t dim1,
+                uint64_t stride1_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle swz) {
+  cuuint64_t dims[2] = {dim0, dim1};
+  cuuint64_t strides[1] = {stride1_bytes};
+  cuuint32_t box[2] = {box0, box1};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = cuTensorMapEncodeTiled(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                                      CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int WT>
+kq_status_t launch_tc(const void* w, Act8 act, float* out, int M, int N, int K, bool pdl, cudaStream_t s) {
+  using T = TcTraits<WT>;
+  const int nb = K / 32;
+  CUtensorMap m_act, m_asc, m_raw;
+  if (!encode_map(&m_act, CU_TENSOR_MAP_DATA_TYPE_UINT8, act.qs, (uint64_t)K, (uint64_t)M, (uint64_t)K, 128, TM,
+                  CU_TENSOR_MAP_SWIZZLE_128B))
+    return fail(KQ_ERR_CUDA, "tensor map (activation codes) rejected");
+  if (!encode_map(&m_asc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, act.ds, (uint64_t)nb * 2, (uint64_t)M, (uint64_t)nb * 8,
+                  KSUB * 2, TM, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return fail(KQ_ERR_CUDA, "tensor map (activation scales) rejected");
+  const uint64_t rowbytes = (uint64_t)nb * T::BB;
+  if (!encode_map(&m_raw, CU_TENSOR_MAP_DATA_TYPE_UINT16, w, rowbytes / 2, (uint64_t)N, rowbytes, T::RAW_ROW / 2, TN,
+                  CU_TENSOR_MAP_SWIZZLE_NONE))
+    return fail(KQ_ERR_CUDA, "tensor map (weights) rejected");
+
+  auto kern = gemm_tc_kernel<WT>;
+  static unsigned attr_done = 0;
+  const int dev = current_device();
+  if (!(attr_done & (1u << (dev & 31)))) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::SMEM);
+    if (e != cudaSuccess) return check_cuda(e, "gemm_tc smem attribute");
+    attr_done |= 1u << (dev & 31);
+  }
+  TcParams p;
+  p.M = M; p.N = N; p.K = K; p.nb = nb;
+  p.num_m_tiles = (M + TM - 1) / TM;
+  p.num_tiles = p.num_m_tiles * ((N + TN - 1) / TN);
+  p.out = out;
+  p.err = device_error_word();
+  const int grid = std::max(1, std::min(sm_count(), p.num_tiles));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = T::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, m_act, m_asc, m_raw, p);
+  if (e != cudaSuccess) return check_cuda(e, "gemm_tc launch");
+  return check_launch("gemm_tc");
+}
+
+}  // namespace
+
+bool gemm_tc_supported(int wtype, int M, int N, int K, const void* w, Act8 act) {
+  (void)wtype;
+  const int nb = K / 32;
+  return M > 8 && N >= 1 && K >= 256 && nb % KRAW == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0 &&
+         (reinterpret_cast<uintptr_t>(act.qs) & 15) == 0 && (reinterpret_cast<uintptr_t>(act.ds) & 15) == 0;
+}
+
+kq_status_t launch_gemm_tc(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, bool pdl,
+                           cudaStream_t s) {
+  switch (wtype) {
+    case KQ_Q4_0: return launch_tc<KQ_Q4_0>(w, act, out, M, N, K, pdl, s);
+    case KQ_Q4_1: return launch_tc<KQ_Q4_1>(w, act, out, M, N, K, pdl, s);
+    case KQ_Q8_0: return launch_tc<KQ_Q8_0>(w, act, out, M, N, K, pdl, s);
+    default: return fail(KQ_ERR_INVALID, "unknown weight type %d", wtype);
+  }
+}
+
+}  // namespace kq

@@ -66,8 +66,12 @@ SHAPES = [
     (8, 1024, 2048),
     (8, 77, 14336),     # long rows
     (1, 64, 96),        # K % 256 != 0 -> generic path
-    (16, 256, 512),
+    (16, 256, 512),     # tensor-core path from here on (M > 8, K % 256 == 0)
     (64, 320, 1024),
+    (9, 128, 256),
+    (33, 130, 2048),    # partial weight tile
+    (129, 200, 512),    # partial token tile
+    (256, 384, 4096),
 ]
 
 
@@ -160,8 +164,9 @@ def test_void_harness_entry_points(cuda):
     w = Q.make_q4_0_blocks(rng, N, K)
     a = Q.quantize_q8_1(x)
     out = torch.empty((M, N), dtype=torch.float32, device=cuda)
+    wd, ad = _t(w, cuda), _t(a, cuda)   # keep the device buffers alive across the raw call
     torch.cuda.synchronize()
-    L.kq_w4a8_q4_0_q8_1(_t(w, cuda).data_ptr(), _t(a, cuda).data_ptr(), out.data_ptr(), M, N, K)
+    L.kq_w4a8_q4_0_q8_1(wd.data_ptr(), ad.data_ptr(), out.data_ptr(), M, N, K)
     torch.cuda.synchronize()
     ok, msg = Q.check_close(out.cpu().numpy(), Q.gemm_q8_1("q4_0", w, a, M, N, K))
     assert ok, msg
@@ -205,3 +210,23 @@ def test_quantize_rows_bit_exact(cuda, wtype):
     g = np.load(__import__("os").path.join(__import__("os").path.dirname(__file__), "golden", "quantize.npz"))
     got = kq.quantize_rows(_t(g["w"], cuda), wtype).cpu().numpy().reshape(-1)
     assert np.array_equal(got, g[wtype])
+
+
+@pytest.mark.parametrize("wtype", ["q4_0", "q8_0"])
+def test_full_size_config_sampled_rows(cuda, wtype):
+    """BASELINE configuration 1 shape (M=512, N=11008, K=4096): rows of the
+    output are independent, so the oracle checks a sample of token rows that
+    covers every 128-row tile boundary; the whole output is checked for
+    finiteness and against the harness's NMSE gate on the same rows."""
+    import kq
+    M, N, K = 512, 11008, 4096
+    rng = np.random.default_rng(2026)
+    w = Q.make_blocks(wtype, rng, N, K)
+    x = _x(rng, M, K)
+    got = kq.gemm_f32act(_t(w, cuda), _t(x, cuda), M, N, K, wtype, "sum_dq").cpu().numpy()
+    assert np.isfinite(got).all()
+    rows = np.array([0, 1, 126, 127, 128, 255, 256, 383, 384, 510, 511])
+    ref = Q.gemm_f32act(wtype, w, x[rows], len(rows), N, K, Q.SUM_DQ)
+    ok, msg = Q.check_close(got[rows], ref)
+    assert ok, msg
+    assert Q.nmse(got[rows], Q.gemm_dequant_f32(wtype, w, x[rows], len(rows), N, K)) < 0.05
