@@ -11,17 +11,17 @@
 // separate MMA (K = 32, one instruction) into a fresh TMEM buffer; the fp32
 // accumulation across blocks happens in the epilogue warps' registers.
 //
-// CTA = 14 warps, one CTA per SM, persistent over 128 x 128 output tiles
+// CTA = 12 warps, one CTA per SM, persistent over 128 x 128 output tiles
 // (tokens x weight rows), tokens fastest so co-running CTAs share weights in L2:
 //   warp 0      TMA producer: activation codes (int8 [M, K], 128B-swizzled
 //               boxes of 128 rows x 128 B = 4 blocks), activation (d, s)
 //               pairs, and raw weight rows (the unchanged AoS q-blocks,
 //               128 rows x 8 blocks per box). No multicast anywhere.
 //   warp 1      TMEM allocator + single-thread MMA issuer.
-//   warps 2-5   converters: one weight row per thread, raw AoS blocks ->
+//   warps 2-3   converters: two weight rows per thread, raw AoS blocks ->
 //               int8 codes in the UMMA K-major SWIZZLE_128B layout + fp32
 //               scale rows, then fence.proxy.async and release the stage.
-//   warps 6-13  epilogue: two warpgroups (64 columns each) read the int32
+//   warps 4-11  epilogue: two warpgroups (64 columns each) read the int32
 //               block result from TMEM (tcgen05.ld 32x32b), apply the block's
 //               scales and accumulate in fp32 registers; 4 TMEM buffers of
 //               128 columns let the MMA run ahead of the epilogue.
@@ -44,7 +44,7 @@ constexpr int SA = 3;          // activation stages
 constexpr int SWS = 3;         // converted weight stages
 constexpr int SRAW = 2;        // raw weight stages
 constexpr int NBUF = 4;        // TMEM buffers
-constexpr int kWarpTma = 0, kWarpMma = 1, kWarpConv = 2, kConvWarps = 4, kWarpEpi = 6, kEpiWarps = 8;
+constexpr int kWarpTma = 0, kWarpMma = 1, kWarpConv = 2, kConvWarps = 2, kWarpEpi = 4, kEpiWarps = 8;
 constexpr int kWarps = kWarpEpi + kEpiWarps;
 constexpr int kThreads = kWarps * 32;
 constexpr int kTmemCols = NBUF * TN;  // 512
@@ -127,6 +127,56 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
 }
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Writes the same 32-bit value to 32 consecutive columns of this thread's lane.
+__device__ __forceinline__ void tmem_st32_const(uint32_t taddr, uint32_t v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
+      "%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
+      "r"(v)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Packed fp32 pairs (one instruction, two lanes of math each).
+__device__ __forceinline__ uint64_t pk2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ uint64_t pk2u(uint32_t lo, uint32_t hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 upk2(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// The MMA accumulates each block's int32 sum onto TMEM words pre-set to
+// kBias = bits of 12582912.0f (1.5 * 2^23). For |sumi| < 2^22 the int32 sum
+// (kBias + sumi) is the fp32 bit pattern of 12582912 + sumi exactly, so the
+// epilogue needs no int->float conversion: d * sumi = fma(f, d, -12582912 d),
+// exact before the final rounding when 12582912 d is exact (d with <= 22
+// significant bits; fp16 scales always are, fp32 scales are rounded to 22
+// bits, a relative change below 2^-22).
+constexpr uint32_t kBias = 0x4B400000u;
+constexpr float kBiasF = 12582912.0f;
+__device__ __forceinline__ float round22(float d) {
+  return __uint_as_float((__float_as_uint(d) + 2u) & ~3u);
+}
 
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -257,10 +307,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < KSUB; ++j, ++ib) {
             const int buf = ib % NBUF;
-            if (ib >= NBUF) mbar_wait_or_poison(&tm_empty[buf], ((ib / NBUF) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+            mbar_wait_or_poison(&tm_empty[buf], (ib / NBUF) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
             tc_fence_after();
-            // K block j of the stage: +32 bytes inside the 128-byte swizzle atom
-            mma_i8(tmem_base + buf * TN, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), idesc, 0u);
+            // K block j of the stage: +32 bytes inside the 128-byte swizzle atom;
+            // accumulate onto the bias words the epilogue left in the buffer.
+            mma_i8(tmem_base + buf * TN, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), idesc, 1u);
             mma_commit(&tm_full[buf]);
           }
           mma_commit(&act_empty[as]);
@@ -270,15 +321,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < kWarpEpi) {
     // ------------------------------------------------------------ converters
-    const int r = (warp - kWarpConv) * 32 + lane;  // weight row in the tile
+    const int r0 = (warp - kWarpConv) * 32 + lane;  // weight rows r0 and r0 + 64 of the tile
     int ir = 0, iw = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
       for (int k8 = 0; k8 < nkb8; ++k8, ++ir) {
         const int rs = ir % SRAW;
         mbar_wait_or_poison(&raw_full[rs], (ir / SRAW) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-        const uint8_t* raw = smem + T::OFF_RAW + rs * T::RAW_STAGE + r * T::RAW_ROW;
 #pragma unroll
         for (int sub = 0; sub < KRAW / KSUB; ++sub, ++iw) {
+          const int ws = iw % SWS;
+          if (iw >= SWS) mbar_wait_or_poison(&w_empty[ws], ((iw / SWS) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+          uint8_t* wt = smem + T::OFF_W + ws * T::W_TILE;
+          float* wsc = reinterpret_cast<float*>(smem + T::OFF_WSC + ws * T::WSC_STAGE);
+#pragma unroll 1
+          for (int rr = 0; rr < TN / (kConvWarps * 32); ++rr) {
+          const int r = r0 + rr * kConvWarps * 32;
+          const uint8_t* raw = smem + T::OFF_RAW + rs * T::RAW_STAGE + r * T::RAW_ROW;
           // this row's 4 raw blocks of the sub-stage, into registers
           constexpr int HB = KSUB * T::BB;  // 72 / 80 / 136 bytes, 8-byte aligned
           uint32_t w[HB / 4 + 1];
@@ -297,14 +355,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           w[HB / 4] = 0;
-          if (sub == KRAW / KSUB - 1) {
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&raw_empty[rs]);  // raw bytes of this stage are all in registers
-          }
-          const int ws = iw % SWS;
-          if (iw >= SWS) mbar_wait_or_poison(&w_empty[ws], ((iw / SWS) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
-          uint8_t* wt = smem + T::OFF_W + ws * T::W_TILE;
-          float* wsc = reinterpret_cast<float*>(smem + T::OFF_WSC + ws * T::WSC_STAGE);
 #pragma unroll
           for (int j = 0; j < KSUB; ++j) {
             const int o = j * T::BB;  // byte offset of the block in w[] (compile time after unrolling)
@@ -331,10 +381,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             wsc[j * TN + r] = d;
             if constexpr (T::kHasMin) wsc[KSUB * TN + j * TN + r] = mn;
           }
+          }  // rows
           fence_proxy_async_smem();  // generic-proxy writes -> tensor-core reads
           __syncwarp();
           if (lane == 0) mbar_arrive(&w_full[ws]);
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[rs]);  // every sub-stage of the raw stage is converted
       }
     }
   } else {
@@ -344,12 +397,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = ew >> 2;               // column half
     const int row = quarter * 32 + lane;    // token row in the tile
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    // initial bias fill of every buffer's (lanes, columns) owned by this warp
+#pragma unroll 1
+    for (int b = 0; b < NBUF; ++b) {
+      const uint32_t ta = tmem_base + lane_addr + b * TN + half * 64;
+      tmem_st32_const(ta, kBias);
+      tmem_st32_const(ta + 32, kBias);
+    }
+    tmem_st_wait();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      for (int b = 0; b < NBUF; ++b) mbar_arrive(&tm_empty[b]);
+    }
     int ia = 0, iw = 0, ib = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
       const int m0 = (t % p.num_m_tiles) * TM, n0 = (t / p.num_m_tiles) * TN;
-      float acc[64];
+      uint64_t acc[32];  // 64 fp32 accumulators as packed pairs
 #pragma unroll
-      for (int c = 0; c < 64; ++c) acc[c] = 0.0f;
+      for (int c = 0; c < 32; ++c) acc[c] = 0ull;
       for (int s = 0; s < p.nb / KSUB; ++s, ++ia, ++iw) {
         const int as = ia % SA, ws = iw % SWS;
         mbar_wait_or_poison(&act_full[as], (ia / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
@@ -363,38 +429,38 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t taddr = tmem_base + lane_addr + buf * TN + half * 64;
           const float2 ds = asc[j];
-          const float* dw = wsc + j * TN + half * 64;
-          const float* mw = wsc + KSUB * TN + j * TN + half * 64;
+          const float d = round22(ds.x);
+          const uint64_t D2 = pk2(d, d);
+          const uint64_t NC2 = pk2(-kBiasF * d, -kBiasF * d);
+          const uint64_t MS2 = pk2(-8.0f * ds.y, -8.0f * ds.y);
+          const uint64_t S2 = pk2(ds.y, ds.y);
+          const uint64_t* dw = reinterpret_cast<const uint64_t*>(wsc + j * TN + half * 64);
+          const uint64_t* mw = reinterpret_cast<const uint64_t*>(wsc + KSUB * TN + j * TN + half * 64);
 #pragma unroll
           for (int h2 = 0; h2 < 2; ++h2) {
             uint32_t v[32];
             tmem_ld32(taddr + 32 * h2, v);
             tmem_ld_wait();
-            if (h2 == 1) {  // both halves are in registers: hand the buffer back to the MMA warp
+            // put the bias back for the buffer's next block
+            tmem_st32_const(taddr + 32 * h2, kBias);
+            if (h2 == 1) {
+              tmem_st_wait();
               tc_fence_before();
               __syncwarp();
               if (lane == 0) mbar_arrive(&tm_empty[buf]);
             }
 #pragma unroll
-            for (int c4 = 0; c4 < 8; ++c4) {
-              const float4 w4 = reinterpret_cast<const float4*>(dw + 32 * h2)[c4];
-              const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
-              float mv[4] = {0.f, 0.f, 0.f, 0.f};
-              if constexpr (WT == KQ_Q4_1) {
-                const float4 m4 = reinterpret_cast<const float4*>(mw + 32 * h2)[c4];
-                mv[0] = m4.x; mv[1] = m4.y; mv[2] = m4.z; mv[3] = m4.w;
-              }
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int c = 32 * h2 + 4 * c4 + e;
-                const float f = (float)(int)v[4 * c4 + e];
-                if constexpr (WT == KQ_Q8_0) {
-                  acc[c] = fmaf(wv[e] * ds.x, f, acc[c]);
-                } else if constexpr (WT == KQ_Q4_0) {
-                  acc[c] = fmaf(wv[e], fmaf(ds.x, f, -8.0f * ds.y), acc[c]);
-                } else {
-                  acc[c] = fmaf(wv[e] * ds.x, f, fmaf(mv[e], ds.y, acc[c]));
-                }
+            for (int c2 = 0; c2 < 16; ++c2) {
+              const int a = 16 * h2 + c2;  // packed accumulator index
+              const uint64_t f2 = pk2u(v[2 * c2], v[2 * c2 + 1]);
+              const uint64_t p2 = fma2(f2, D2, NC2);  // d_a * sumi, two columns
+              const uint64_t w2 = dw[a];
+              if constexpr (WT == KQ_Q8_0) {
+                acc[a] = fma2(p2, w2, acc[a]);
+              } else if constexpr (WT == KQ_Q4_0) {
+                acc[a] = fma2(add2(p2, MS2), w2, acc[a]);  // d_w * (d_a sumi - 8 s_a)
+              } else {
+                acc[a] = fma2(mw[a], S2, fma2(p2, w2, acc[a]));  // d_w d_a sumi + m_w s_a
               }
             }
           }
@@ -412,12 +478,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         float* o = p.out + (size_t)m * p.N + nb0;
         if (nb0 + 64 <= p.N && (p.N & 3) == 0) {
 #pragma unroll
-          for (int c = 0; c < 64; c += 4)
-            *reinterpret_cast<float4*>(o + c) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
+          for (int c = 0; c < 32; c += 2) {
+            const float2 a0 = upk2(acc[c]), a1 = upk2(acc[c + 1]);
+            *reinterpret_cast<float4*>(o + 2 * c) = make_float4(a0.x, a0.y, a1.x, a1.y);
+          }
         } else {
 #pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if (nb0 + c < p.N) o[c] = acc[c];
+          for (int c = 0; c < 32; ++c) {
+            const float2 a0 = upk2(acc[c]);
+            if (nb0 + 2 * c < p.N) o[2 * c] = a0.x;
+            if (nb0 + 2 * c + 1 < p.N) o[2 * c + 1] = a0.y;
+          }
         }
       }
     }

@@ -235,7 +235,12 @@ __global__ void __launch_bounds__(32 * (kConsumerWarps + 1), 1)
           mbar_arrive_expect_tx(&full[slot], pitch * rows);
           uint8_t* dst = smem + slot * C::SB;
           const uint8_t* src = w + (size_t)n0 * rowbytes + (size_t)it * C::KS * BB;
-          for (int r = 0; r < rows; ++r) bulk_g2s_hint(dst + r * pitch, src + r * rowbytes, pitch, &full[slot], pol);
+          if (nits == 1) {
+            // whole rows: the stage is one contiguous byte range
+            bulk_g2s_hint(dst, src, pitch * rows, &full[slot], pol);
+          } else {
+            for (int r = 0; r < rows; ++r) bulk_g2s_hint(dst + r * pitch, src + r * rowbytes, pitch, &full[slot], pol);
+          }
         }
       }
       // Drain: every filled slot must be released by the consumers (who
