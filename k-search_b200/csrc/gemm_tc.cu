@@ -11,7 +11,7 @@
 // separate MMA (K = 32, one instruction) into a fresh TMEM buffer; the fp32
 // accumulation across blocks happens in the epilogue warps' registers.
 //
-// CTA = 12 warps, one CTA per SM, persistent over 128 x 128 output tiles
+// CTA = 20 warps, one CTA per SM, persistent over 128 x 128 output tiles
 // (tokens x weight rows), tokens fastest so co-running CTAs share weights in L2:
 //   warp 0      TMA producer: activation codes (int8 [M, K], 128B-swizzled
 //               boxes of 128 rows x 128 B = 4 blocks), activation (d, s)
@@ -21,7 +21,7 @@
 //   warps 2-3   converters: two weight rows per thread, raw AoS blocks ->
 //               int8 codes in the UMMA K-major SWIZZLE_128B layout + fp32
 //               scale rows, then fence.proxy.async and release the stage.
-//   warps 4-11  epilogue: two warpgroups (64 columns each) read the int32
+//   warps 4-19  epilogue: four warpgroups (32 columns each) read the int32
 //               block result from TMEM (tcgen05.ld 32x32b), apply the block's
 //               scales and accumulate in fp32 registers; 4 TMEM buffers of
 //               128 columns let the MMA run ahead of the epilogue.
@@ -44,7 +44,8 @@ constexpr int SA = 3;          // activation stages
 constexpr int SWS = 3;         // converted weight stages
 constexpr int SRAW = 2;        // raw weight stages
 constexpr int NBUF = 4;        // TMEM buffers
-constexpr int kWarpTma = 0, kWarpMma = 1, kWarpConv = 2, kConvWarps = 2, kWarpEpi = 4, kEpiWarps = 8;
+constexpr int kWarpTma = 0, kWarpMma = 1, kWarpConv = 2, kConvWarps = 2, kWarpEpi = 4, kEpiWarps = 16;
+constexpr int kEpiCols = TN / (kEpiWarps / 4);  // columns per epilogue thread (32)
 constexpr int kWarps = kWarpEpi + kEpiWarps;
 constexpr int kThreads = kWarps * 32;
 constexpr int kTmemCols = NBUF * TN;  // 512
@@ -394,16 +395,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int ew = warp - kWarpEpi;
     const int quarter = warp & 3;           // TMEM lane quarter this warp may access
-    const int half = ew >> 2;               // column half
+    const int cg = ew >> 2;                 // column group
     const int row = quarter * 32 + lane;    // token row in the tile
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
     // initial bias fill of every buffer's (lanes, columns) owned by this warp
 #pragma unroll 1
-    for (int b = 0; b < NBUF; ++b) {
-      const uint32_t ta = tmem_base + lane_addr + b * TN + half * 64;
-      tmem_st32_const(ta, kBias);
-      tmem_st32_const(ta + 32, kBias);
-    }
+    for (int b = 0; b < NBUF; ++b) tmem_st32_const(tmem_base + lane_addr + b * TN + cg * kEpiCols, kBias);
     tmem_st_wait();
     tc_fence_before();
     __syncwarp();
@@ -413,9 +410,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     int ia = 0, iw = 0, ib = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
       const int m0 = (t % p.num_m_tiles) * TM, n0 = (t / p.num_m_tiles) * TN;
-      uint64_t acc[32];  // 64 fp32 accumulators as packed pairs
+      uint64_t acc[kEpiCols / 2];  // fp32 accumulators as packed pairs
 #pragma unroll
-      for (int c = 0; c < 32; ++c) acc[c] = 0ull;
+      for (int c = 0; c < kEpiCols / 2; ++c) acc[c] = 0ull;
       for (int s = 0; s < p.nb / KSUB; ++s, ++ia, ++iw) {
         const int as = ia % SA, ws = iw % SWS;
         mbar_wait_or_poison(&act_full[as], (ia / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
@@ -425,43 +422,41 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
         for (int j = 0; j < KSUB; ++j, ++ib) {
           const int buf = ib % NBUF;
-          mbar_wait_or_poison(&tm_full[buf], (ib / NBUF) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-          tc_fence_after();
-          const uint32_t taddr = tmem_base + lane_addr + buf * TN + half * 64;
-          const float2 ds = asc[j];
-          const float d = round22(ds.x);
+          const float2 dsj = asc[j];
+          const float d = round22(dsj.x);
           const uint64_t D2 = pk2(d, d);
           const uint64_t NC2 = pk2(-kBiasF * d, -kBiasF * d);
-          const uint64_t MS2 = pk2(-8.0f * ds.y, -8.0f * ds.y);
-          const uint64_t S2 = pk2(ds.y, ds.y);
-          const uint64_t* dw = reinterpret_cast<const uint64_t*>(wsc + j * TN + half * 64);
-          const uint64_t* mw = reinterpret_cast<const uint64_t*>(wsc + KSUB * TN + j * TN + half * 64);
+          const uint64_t MS2 = pk2(-8.0f * dsj.y, -8.0f * dsj.y);
+          const uint64_t S2 = pk2(dsj.y, dsj.y);
+          const uint4* dw = reinterpret_cast<const uint4*>(wsc + j * TN + cg * kEpiCols);
+          const uint4* mw = reinterpret_cast<const uint4*>(wsc + KSUB * TN + j * TN + cg * kEpiCols);
+          mbar_wait_or_poison(&tm_full[buf], (ib / NBUF) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+          tc_fence_after();
+          const uint32_t taddr = tmem_base + lane_addr + buf * TN + cg * kEpiCols;
+          uint32_t v[32];
+          tmem_ld32(taddr, v);
+          tmem_ld_wait();
+          tmem_st32_const(taddr, kBias);  // the bias for the buffer's next block
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tm_empty[buf]);
 #pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {
-            uint32_t v[32];
-            tmem_ld32(taddr + 32 * h2, v);
-            tmem_ld_wait();
-            // put the bias back for the buffer's next block
-            tmem_st32_const(taddr + 32 * h2, kBias);
-            if (h2 == 1) {
-              tmem_st_wait();
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&tm_empty[buf]);
-            }
-#pragma unroll
-            for (int c2 = 0; c2 < 16; ++c2) {
-              const int a = 16 * h2 + c2;  // packed accumulator index
-              const uint64_t f2 = pk2u(v[2 * c2], v[2 * c2 + 1]);
-              const uint64_t p2 = fma2(f2, D2, NC2);  // d_a * sumi, two columns
-              const uint64_t w2 = dw[a];
-              if constexpr (WT == KQ_Q8_0) {
-                acc[a] = fma2(p2, w2, acc[a]);
-              } else if constexpr (WT == KQ_Q4_0) {
-                acc[a] = fma2(add2(p2, MS2), w2, acc[a]);  // d_w * (d_a sumi - 8 s_a)
-              } else {
-                acc[a] = fma2(mw[a], S2, fma2(p2, w2, acc[a]));  // d_w d_a sumi + m_w s_a
-              }
+          for (int q = 0; q < kEpiCols / 4; ++q) {
+            const uint4 w4 = dw[q];  // scales of 4 columns (broadcast read)
+            const uint64_t wa = pk2u(w4.x, w4.y), wb = pk2u(w4.z, w4.w);
+            const uint64_t fa = pk2u(v[4 * q], v[4 * q + 1]), fb = pk2u(v[4 * q + 2], v[4 * q + 3]);
+            const uint64_t pa = fma2(fa, D2, NC2), pb = fma2(fb, D2, NC2);  // d_a * sumi
+            if constexpr (WT == KQ_Q8_0) {
+              acc[2 * q] = fma2(pa, wa, acc[2 * q]);
+              acc[2 * q + 1] = fma2(pb, wb, acc[2 * q + 1]);
+            } else if constexpr (WT == KQ_Q4_0) {
+              acc[2 * q] = fma2(add2(pa, MS2), wa, acc[2 * q]);  // d_w * (d_a sumi - 8 s_a)
+              acc[2 * q + 1] = fma2(add2(pb, MS2), wb, acc[2 * q + 1]);
+            } else {
+              const uint4 m4 = mw[q];
+              acc[2 * q] = fma2(pk2u(m4.x, m4.y), S2, fma2(pa, wa, acc[2 * q]));  // d_w d_a sumi + m_w s_a
+              acc[2 * q + 1] = fma2(pk2u(m4.z, m4.w), S2, fma2(pb, wb, acc[2 * q + 1]));
             }
           }
         }
@@ -473,21 +468,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // ---- store this tile's rows ----
       const int m = m0 + row;
-      const int nb0 = n0 + half * 64;
+      const int nc0 = n0 + cg * kEpiCols;
       if (m < p.M) {
-        float* o = p.out + (size_t)m * p.N + nb0;
-        if (nb0 + 64 <= p.N && (p.N & 3) == 0) {
+        float* o = p.out + (size_t)m * p.N + nc0;
+        if (nc0 + kEpiCols <= p.N && (p.N & 3) == 0) {
 #pragma unroll
-          for (int c = 0; c < 32; c += 2) {
+          for (int c = 0; c < kEpiCols / 2; c += 2) {
             const float2 a0 = upk2(acc[c]), a1 = upk2(acc[c + 1]);
             *reinterpret_cast<float4*>(o + 2 * c) = make_float4(a0.x, a0.y, a1.x, a1.y);
           }
         } else {
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
+          for (int c = 0; c < kEpiCols / 2; ++c) {
             const float2 a0 = upk2(acc[c]);
-            if (nb0 + 2 * c < p.N) o[2 * c] = a0.x;
-            if (nb0 + 2 * c + 1 < p.N) o[2 * c + 1] = a0.y;
+            if (nc0 + 2 * c < p.N) o[2 * c] = a0.x;
+            if (nc0 + 2 * c + 1 < p.N) o[2 * c + 1] = a0.y;
           }
         }
       }
