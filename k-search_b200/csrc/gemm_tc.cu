@@ -11,20 +11,21 @@
 // separate MMA (K = 32, one instruction) into a fresh TMEM buffer; the fp32
 // accumulation across blocks happens in the epilogue warps' registers.
 //
-// CTA = 20 warps, one CTA per SM, persistent over 128 x 128 output tiles
+// CTA = 10 warps, one CTA per SM, persistent over 128 x 128 output tiles
 // (tokens x weight rows), tokens fastest so co-running CTAs share weights in L2:
 //   warp 0      TMA producer: activation codes (int8 [M, K], 128B-swizzled
 //               boxes of 128 rows x 128 B = 4 blocks), activation (d, s)
 //               pairs, and raw weight rows (the unchanged AoS q-blocks,
 //               128 rows x 8 blocks per box). No multicast anywhere.
 //   warp 1      TMEM allocator + single-thread MMA issuer.
-//   warps 2-3   converters: two weight rows per thread, raw AoS blocks ->
-//               int8 codes in the UMMA K-major SWIZZLE_128B layout + fp32
-//               scale rows, then fence.proxy.async and release the stage.
-//   warps 4-19  epilogue: four warpgroups (32 columns each) read the int32
-//               block result from TMEM (tcgen05.ld 32x32b), apply the block's
-//               scales and accumulate in fp32 registers; 4 TMEM buffers of
-//               128 columns let the MMA run ahead of the epilogue.
+//   warps 2-9   workers. For K stage s they first convert the raw weight
+//               blocks of stage s+1 (two blocks of one row per thread) into
+//               int8 codes in the UMMA K-major SWIZZLE_128B layout plus fp32
+//               scale rows (then fence.proxy.async and release it to the MMA),
+//               then run the epilogue of stage s: read each block's int32
+//               result from TMEM (tcgen05.ld 32x32b, 64 columns per thread),
+//               apply the block's scales and accumulate in fp32 registers.
+//               4 TMEM buffers of 128 columns let the MMA run ahead.
 #include <cuda.h>
 
 #include <algorithm>
@@ -44,9 +45,9 @@ constexpr int SA = 3;          // activation stages
 constexpr int SWS = 3;         // converted weight stages
 constexpr int SRAW = 2;        // raw weight stages
 constexpr int NBUF = 4;        // TMEM buffers
-constexpr int kWarpTma = 0, kWarpMma = 1, kWarpConv = 2, kConvWarps = 2, kWarpEpi = 4, kEpiWarps = 16;
-constexpr int kEpiCols = TN / (kEpiWarps / 4);  // columns per epilogue thread (32)
-constexpr int kWarps = kWarpEpi + kEpiWarps;
+constexpr int kWarpTma = 0, kWarpMma = 1, kWarpWork = 2, kWorkWarps = 8;
+constexpr int kEpiCols = TN / (kWorkWarps / 4);  // columns per worker thread in the epilogue (64)
+constexpr int kWarps = kWarpWork + kWorkWarps;
 constexpr int kThreads = kWarps * 32;
 constexpr int kTmemCols = NBUF * TN;  // 512
 
@@ -123,6 +124,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
         "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
         "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
         "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+      "[%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
       : "r"(taddr)
       : "memory");
 }
@@ -237,19 +248,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < SA; ++i) {
       mbar_init(&act_full[i], 1);
-      mbar_init(&act_empty[i], 1 + kEpiWarps);  // MMA commit + epilogue warps (they read the scales)
+      mbar_init(&act_empty[i], 1 + kWorkWarps);  // MMA commit + workers (they read the scales)
     }
     for (int i = 0; i < SWS; ++i) {
-      mbar_init(&w_full[i], kConvWarps);
-      mbar_init(&w_empty[i], 1 + kEpiWarps);
+      mbar_init(&w_full[i], kWorkWarps);
+      mbar_init(&w_empty[i], 1 + kWorkWarps);
     }
     for (int i = 0; i < SRAW; ++i) {
       mbar_init(&raw_full[i], 1);
-      mbar_init(&raw_empty[i], kConvWarps);
+      mbar_init(&raw_empty[i], kWorkWarps);
     }
     for (int i = 0; i < NBUF; ++i) {
       mbar_init(&tm_full[i], 1);
-      mbar_init(&tm_empty[i], kEpiWarps);
+      mbar_init(&tm_empty[i], kWorkWarps);
     }
     fence_mbar_init();
   }
@@ -320,169 +331,175 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp < kWarpEpi) {
-    // ------------------------------------------------------------ converters
-    const int r0 = (warp - kWarpConv) * 32 + lane;  // weight rows r0 and r0 + 64 of the tile
-    int ir = 0, iw = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
-      for (int k8 = 0; k8 < nkb8; ++k8, ++ir) {
-        const int rs = ir % SRAW;
-        mbar_wait_or_poison(&raw_full[rs], (ir / SRAW) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-#pragma unroll
-        for (int sub = 0; sub < KRAW / KSUB; ++sub, ++iw) {
-          const int ws = iw % SWS;
-          if (iw >= SWS) mbar_wait_or_poison(&w_empty[ws], ((iw / SWS) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
-          uint8_t* wt = smem + T::OFF_W + ws * T::W_TILE;
-          float* wsc = reinterpret_cast<float*>(smem + T::OFF_WSC + ws * T::WSC_STAGE);
-#pragma unroll 1
-          for (int rr = 0; rr < TN / (kConvWarps * 32); ++rr) {
-          const int r = r0 + rr * kConvWarps * 32;
-          const uint8_t* raw = smem + T::OFF_RAW + rs * T::RAW_STAGE + r * T::RAW_ROW;
-          // this row's 4 raw blocks of the sub-stage, into registers
-          constexpr int HB = KSUB * T::BB;  // 72 / 80 / 136 bytes, 8-byte aligned
-          uint32_t w[HB / 4 + 1];
-          const uint8_t* src = raw + sub * HB;
-          if constexpr (HB % 16 == 0) {
-#pragma unroll
-            for (int i = 0; i < HB / 16; ++i) {
-              const uint4 v = reinterpret_cast<const uint4*>(src)[i];
-              w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < HB / 8; ++i) {
-              const uint2 v = reinterpret_cast<const uint2*>(src)[i];
-              w[2 * i] = v.x; w[2 * i + 1] = v.y;
-            }
-          }
-          w[HB / 4] = 0;
-#pragma unroll
-          for (int j = 0; j < KSUB; ++j) {
-            const int o = j * T::BB;  // byte offset of the block in w[] (compile time after unrolling)
-            auto u32 = [&](int off) -> uint32_t {
-              return (off & 3) ? __funnelshift_r(w[off >> 2], w[(off >> 2) + 1], 16) : w[off >> 2];
-            };
-            auto u16 = [&](int off) -> uint32_t { return (off & 3) ? (w[off >> 2] >> 16) : (w[off >> 2] & 0xFFFFu); };
-            uint4 c0, c1;
-            float mn = 0.0f;
-            const float d = half_bits_to_float(u16(o));
-            if constexpr (WT == KQ_Q8_0) {
-              c0 = make_uint4(u32(o + 2), u32(o + 6), u32(o + 10), u32(o + 14));
-              c1 = make_uint4(u32(o + 18), u32(o + 22), u32(o + 26), u32(o + 30));
-            } else {
-              const int q = o + (WT == KQ_Q4_0 ? 2 : 4);
-              if constexpr (WT == KQ_Q4_1) mn = half_bits_to_float(u16(o + 2));
-              const uint32_t a0 = u32(q), a1 = u32(q + 4), a2 = u32(q + 8), a3 = u32(q + 12);
-              c0 = make_uint4(a0 & 0x0F0F0F0Fu, a1 & 0x0F0F0F0Fu, a2 & 0x0F0F0F0Fu, a3 & 0x0F0F0F0Fu);
-              c1 = make_uint4((a0 >> 4) & 0x0F0F0F0Fu, (a1 >> 4) & 0x0F0F0F0Fu, (a2 >> 4) & 0x0F0F0F0Fu,
-                              (a3 >> 4) & 0x0F0F0F0Fu);
-            }
-            *reinterpret_cast<uint4*>(wt + sw128_off(r, 2 * j)) = c0;
-            *reinterpret_cast<uint4*>(wt + sw128_off(r, 2 * j + 1)) = c1;
-            wsc[j * TN + r] = d;
-            if constexpr (T::kHasMin) wsc[KSUB * TN + j * TN + r] = mn;
-          }
-          }  // rows
-          fence_proxy_async_smem();  // generic-proxy writes -> tensor-core reads
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&w_full[ws]);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&raw_empty[rs]);  // every sub-stage of the raw stage is converted
-      }
-    }
   } else {
-    // ------------------------------------------------------------ epilogue
-    const int ew = warp - kWarpEpi;
+    // ------------------------------------------------------------ workers
+    const int wi = warp - kWarpWork;        // 0..7
     const int quarter = warp & 3;           // TMEM lane quarter this warp may access
-    const int cg = ew >> 2;                 // column group
-    const int row = quarter * 32 + lane;    // token row in the tile
+    const int cg = wi >> 2;                 // column half of the epilogue
+    const int row = quarter * 32 + lane;    // token row in the tile (epilogue)
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    const int crow = (wi * 32 + lane) >> 1; // weight row converted by this thread
+    const int chalf = lane & 1;             // which two blocks of the 4-block stage
+    // byte offsets of this row's 16-byte chunks 4*chalf .. 4*chalf+3 in a 128B-swizzled tile
+    int coff[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) coff[c] = sw128_off(crow, 4 * chalf + c);
+    const int spt = p.nb / KSUB;            // K stages per tile (even: nb % 8 == 0)
+    const int my_tiles = (p.num_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int total = my_tiles * spt;
+
+    // Convert global stage gs: blocks 2*chalf, 2*chalf+1 of row crow.
+    auto convert = [&](int gs) {
+      const int irr = gs >> 1, sub = gs & 1;
+      const int rs = irr % SRAW;
+      mbar_wait_or_poison(&raw_full[rs], (irr / SRAW) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+      constexpr int HB = 2 * T::BB;  // 36 / 40 / 68 bytes, 4-byte aligned
+      const uint32_t* src = reinterpret_cast<const uint32_t*>(smem + T::OFF_RAW + rs * T::RAW_STAGE +
+                                                              crow * T::RAW_ROW + (sub * KSUB + 2 * chalf) * T::BB);
+      uint32_t w[HB / 4 + 1];
+#pragma unroll
+      for (int i = 0; i < HB / 4; ++i) w[i] = src[i];
+      w[HB / 4] = 0;
+      const int ws = gs % SWS;
+      if (gs >= SWS) mbar_wait_or_poison(&w_empty[ws], ((gs / SWS) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+      uint8_t* wt = smem + T::OFF_W + ws * T::W_TILE;
+      float* wsc = reinterpret_cast<float*>(smem + T::OFF_WSC + ws * T::WSC_STAGE);
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const int o = jj * T::BB;  // compile-time after unrolling
+        auto u32 = [&](int off) -> uint32_t {
+          return (off & 3) ? __funnelshift_r(w[off >> 2], w[(off >> 2) + 1], 16) : w[off >> 2];
+        };
+        auto u16 = [&](int off) -> uint32_t { return (off & 3) ? (w[off >> 2] >> 16) : (w[off >> 2] & 0xFFFFu); };
+        uint4 c0, c1;
+        float mn = 0.0f;
+        const float d = half_bits_to_float(u16(o));
+        if constexpr (WT == KQ_Q8_0) {
+          c0 = make_uint4(u32(o + 2), u32(o + 6), u32(o + 10), u32(o + 14));
+          c1 = make_uint4(u32(o + 18), u32(o + 22), u32(o + 26), u32(o + 30));
+        } else {
+          const int q = o + (WT == KQ_Q4_0 ? 2 : 4);
+          if constexpr (WT == KQ_Q4_1) mn = half_bits_to_float(u16(o + 2));
+          const uint32_t a0 = u32(q), a1 = u32(q + 4), a2 = u32(q + 8), a3 = u32(q + 12);
+          c0 = make_uint4(a0 & 0x0F0F0F0Fu, a1 & 0x0F0F0F0Fu, a2 & 0x0F0F0F0Fu, a3 & 0x0F0F0F0Fu);
+          c1 = make_uint4((a0 >> 4) & 0x0F0F0F0Fu, (a1 >> 4) & 0x0F0F0F0Fu, (a2 >> 4) & 0x0F0F0F0Fu,
+                          (a3 >> 4) & 0x0F0F0F0Fu);
+        }
+        *reinterpret_cast<uint4*>(wt + coff[2 * jj]) = c0;
+        *reinterpret_cast<uint4*>(wt + coff[2 * jj + 1]) = c1;
+        const int j = 2 * chalf + jj;
+        wsc[j * TN + crow] = d;
+        if constexpr (T::kHasMin) wsc[KSUB * TN + j * TN + crow] = mn;
+      }
+      fence_proxy_async_smem();  // generic-proxy writes -> tensor-core reads
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&w_full[ws]);
+        if (sub == 1) mbar_arrive(&raw_empty[rs]);  // both halves of the raw stage are converted
+      }
+    };
+
     // initial bias fill of every buffer's (lanes, columns) owned by this warp
-#pragma unroll 1
-    for (int b = 0; b < NBUF; ++b) tmem_st32_const(tmem_base + lane_addr + b * TN + cg * kEpiCols, kBias);
+    for (int b = 0; b < NBUF; ++b)
+      for (int c32 = 0; c32 < kEpiCols / 32; ++c32)
+        tmem_st32_const(tmem_base + lane_addr + b * TN + cg * kEpiCols + 32 * c32, kBias);
     tmem_st_wait();
     tc_fence_before();
     __syncwarp();
     if (lane == 0) {
       for (int b = 0; b < NBUF; ++b) mbar_arrive(&tm_empty[b]);
     }
-    int ia = 0, iw = 0, ib = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
-      const int m0 = (t % p.num_m_tiles) * TM, n0 = (t / p.num_m_tiles) * TN;
-      uint64_t acc[kEpiCols / 2];  // fp32 accumulators as packed pairs
+
+    if (total > 0) convert(0);
+    uint64_t acc[kEpiCols / 2];  // fp32 accumulators as packed pairs
+    int ib = 0;
+    for (int es = 0; es < total; ++es) {
+      if (es + 1 < total) convert(es + 1);
+      const int s = es % spt;
+      const int t = (int)blockIdx.x + (es / spt) * (int)gridDim.x;
+      if (s == 0) {
 #pragma unroll
-      for (int c = 0; c < kEpiCols / 2; ++c) acc[c] = 0ull;
-      for (int s = 0; s < p.nb / KSUB; ++s, ++ia, ++iw) {
-        const int as = ia % SA, ws = iw % SWS;
-        mbar_wait_or_poison(&act_full[as], (ia / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-        mbar_wait_or_poison(&w_full[ws], (iw / SWS) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-        const float2* asc = reinterpret_cast<const float2*>(smem + T::OFF_ASC + as * T::ASC_STAGE) + row * KSUB;
-        const float* wsc = reinterpret_cast<const float*>(smem + T::OFF_WSC + ws * T::WSC_STAGE);
+        for (int c = 0; c < kEpiCols / 2; ++c) acc[c] = 0ull;
+      }
+      const int as = es % SA, ws = es % SWS;
+      mbar_wait_or_poison(&act_full[as], (es / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+      mbar_wait_or_poison(&w_full[ws], (es / SWS) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+      const float2* asc = reinterpret_cast<const float2*>(smem + T::OFF_ASC + as * T::ASC_STAGE) + row * KSUB;
+      const float* wsc = reinterpret_cast<const float*>(smem + T::OFF_WSC + ws * T::WSC_STAGE);
 #pragma unroll 1
-        for (int j = 0; j < KSUB; ++j, ++ib) {
-          const int buf = ib % NBUF;
-          const float2 dsj = asc[j];
-          const float d = round22(dsj.x);
-          const uint64_t D2 = pk2(d, d);
-          const uint64_t NC2 = pk2(-kBiasF * d, -kBiasF * d);
-          const uint64_t MS2 = pk2(-8.0f * dsj.y, -8.0f * dsj.y);
-          const uint64_t S2 = pk2(dsj.y, dsj.y);
-          const uint4* dw = reinterpret_cast<const uint4*>(wsc + j * TN + cg * kEpiCols);
-          const uint4* mw = reinterpret_cast<const uint4*>(wsc + KSUB * TN + j * TN + cg * kEpiCols);
-          mbar_wait_or_poison(&tm_full[buf], (ib / NBUF) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-          tc_fence_after();
-          const uint32_t taddr = tmem_base + lane_addr + buf * TN + cg * kEpiCols;
-          uint32_t v[32];
-          tmem_ld32(taddr, v);
-          tmem_ld_wait();
-          tmem_st32_const(taddr, kBias);  // the bias for the buffer's next block
-          tmem_st_wait();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tm_empty[buf]);
+      for (int j = 0; j < KSUB; ++j, ++ib) {
+        const int buf = ib % NBUF;
+        const float2 dsj = asc[j];
+        const float d = round22(dsj.x);
+        const uint64_t D2 = pk2(d, d);
+        const uint64_t NC2 = pk2(-kBiasF * d, -kBiasF * d);
+        const uint64_t MS2 = pk2(-8.0f * dsj.y, -8.0f * dsj.y);
+        const uint64_t S2 = pk2(dsj.y, dsj.y);
+        const uint4* dw = reinterpret_cast<const uint4*>(wsc + j * TN + cg * kEpiCols);
+        const uint4* mw = reinterpret_cast<const uint4*>(wsc + KSUB * TN + j * TN + cg * kEpiCols);
+        mbar_wait_or_poison(&tm_full[buf], (ib / NBUF) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + lane_addr + buf * TN + cg * kEpiCols;
 #pragma unroll
-          for (int q = 0; q < kEpiCols / 4; ++q) {
-            const uint4 w4 = dw[q];  // scales of 4 columns (broadcast read)
+        for (int ch = 0; ch < kEpiCols / 16; ++ch) {
+          uint32_t v[16];
+          tmem_ld16(taddr + 16 * ch, v);
+          tmem_ld_wait();
+          if (ch == kEpiCols / 16 - 1) {
+            // every column of this thread is in registers: restore the bias and hand the buffer back
+#pragma unroll
+            for (int c32 = 0; c32 < kEpiCols / 32; ++c32) tmem_st32_const(taddr + 32 * c32, kBias);
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tm_empty[buf]);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int a = 8 * ch + 2 * q;  // packed accumulator index
+            const uint4 w4 = dw[4 * ch + q];  // scales of 4 columns (broadcast read)
             const uint64_t wa = pk2u(w4.x, w4.y), wb = pk2u(w4.z, w4.w);
             const uint64_t fa = pk2u(v[4 * q], v[4 * q + 1]), fb = pk2u(v[4 * q + 2], v[4 * q + 3]);
             const uint64_t pa = fma2(fa, D2, NC2), pb = fma2(fb, D2, NC2);  // d_a * sumi
             if constexpr (WT == KQ_Q8_0) {
-              acc[2 * q] = fma2(pa, wa, acc[2 * q]);
-              acc[2 * q + 1] = fma2(pb, wb, acc[2 * q + 1]);
+              acc[a] = fma2(pa, wa, acc[a]);
+              acc[a + 1] = fma2(pb, wb, acc[a + 1]);
             } else if constexpr (WT == KQ_Q4_0) {
-              acc[2 * q] = fma2(add2(pa, MS2), wa, acc[2 * q]);  // d_w * (d_a sumi - 8 s_a)
-              acc[2 * q + 1] = fma2(add2(pb, MS2), wb, acc[2 * q + 1]);
+              acc[a] = fma2(add2(pa, MS2), wa, acc[a]);  // d_w * (d_a sumi - 8 s_a)
+              acc[a + 1] = fma2(add2(pb, MS2), wb, acc[a + 1]);
             } else {
-              const uint4 m4 = mw[q];
-              acc[2 * q] = fma2(pk2u(m4.x, m4.y), S2, fma2(pa, wa, acc[2 * q]));  // d_w d_a sumi + m_w s_a
-              acc[2 * q + 1] = fma2(pk2u(m4.z, m4.w), S2, fma2(pb, wb, acc[2 * q + 1]));
+              const uint4 m4 = mw[4 * ch + q];
+              acc[a] = fma2(pk2u(m4.x, m4.y), S2, fma2(pa, wa, acc[a]));  // d_w d_a sumi + m_w s_a
+              acc[a + 1] = fma2(pk2u(m4.z, m4.w), S2, fma2(pb, wb, acc[a + 1]));
             }
           }
         }
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&act_empty[as]);
-          mbar_arrive(&w_empty[ws]);
-        }
       }
-      // ---- store this tile's rows ----
-      const int m = m0 + row;
-      const int nc0 = n0 + cg * kEpiCols;
-      if (m < p.M) {
-        float* o = p.out + (size_t)m * p.N + nc0;
-        if (nc0 + kEpiCols <= p.N && (p.N & 3) == 0) {
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&act_empty[as]);
+        mbar_arrive(&w_empty[ws]);
+      }
+      if (s == spt - 1) {
+        // ---- store this tile's rows ----
+        const int m0 = (t % p.num_m_tiles) * TM, n0 = (t / p.num_m_tiles) * TN;
+        const int m = m0 + row;
+        const int nc0 = n0 + cg * kEpiCols;
+        if (m < p.M) {
+          float* o = p.out + (size_t)m * p.N + nc0;
+          if (nc0 + kEpiCols <= p.N && (p.N & 3) == 0) {
 #pragma unroll
-          for (int c = 0; c < kEpiCols / 2; c += 2) {
-            const float2 a0 = upk2(acc[c]), a1 = upk2(acc[c + 1]);
-            *reinterpret_cast<float4*>(o + 2 * c) = make_float4(a0.x, a0.y, a1.x, a1.y);
-          }
-        } else {
+            for (int c = 0; c < kEpiCols / 2; c += 2) {
+              const float2 a0 = upk2(acc[c]), a1 = upk2(acc[c + 1]);
+              *reinterpret_cast<float4*>(o + 2 * c) = make_float4(a0.x, a0.y, a1.x, a1.y);
+            }
+          } else {
 #pragma unroll
-          for (int c = 0; c < kEpiCols / 2; ++c) {
-            const float2 a0 = upk2(acc[c]);
-            if (nc0 + 2 * c < p.N) o[2 * c] = a0.x;
-            if (nc0 + 2 * c + 1 < p.N) o[2 * c + 1] = a0.y;
+            for (int c = 0; c < kEpiCols / 2; ++c) {
+              const float2 a0 = upk2(acc[c]);
+              if (nc0 + 2 * c < p.N) o[2 * c] = a0.x;
+              if (nc0 + 2 * c + 1 < p.N) o[2 * c + 1] = a0.y;
+            }
           }
         }
       }
