@@ -177,13 +177,12 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
   return d;
 }
 
-// The MMA accumulates each block's int32 sum onto TMEM words pre-set to
-// kBias = bits of 12582912.0f (1.5 * 2^23). For |sumi| < 2^22 the int32 sum
-// (kBias + sumi) is the fp32 bit pattern of 12582912 + sumi exactly, so the
-// epilogue needs no int->float conversion: d * sumi = fma(f, d, -12582912 d),
-// exact before the final rounding when 12582912 d is exact (d with <= 22
-// significant bits; fp16 scales always are, fp32 scales are rounded to 22
-// bits, a relative change below 2^-22).
+// Integer -> float without a conversion instruction: for |sumi| < 2^22 the
+// int32 (kBias + sumi), kBias = bits of 12582912.0f (1.5 * 2^23), is the fp32
+// bit pattern of 12582912 + sumi exactly (one integer add on the ALU pipe).
+// Then d * sumi = fma(f, d, -12582912 d), exact before the final rounding
+// when 12582912 d is exact (d with <= 22 significant bits; fp16 scales always
+// are, fp32 scales are rounded to 22 bits, a relative change below 2^-22).
 constexpr uint32_t kBias = 0x4B400000u;
 constexpr float kBiasF = 12582912.0f;
 __device__ __forceinline__ float round22(float d) {
@@ -321,9 +320,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int buf = ib % NBUF;
             mbar_wait_or_poison(&tm_empty[buf], (ib / NBUF) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
             tc_fence_after();
-            // K block j of the stage: +32 bytes inside the 128-byte swizzle atom;
-            // accumulate onto the bias words the epilogue left in the buffer.
-            mma_i8(tmem_base + buf * TN, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), idesc, 1u);
+            // K block j of the stage: +32 bytes inside the 128-byte swizzle atom
+            mma_i8(tmem_base + buf * TN, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), idesc, 0u);
             mma_commit(&tm_full[buf]);
           }
           mma_commit(&act_empty[as]);
@@ -399,13 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     };
 
-    // initial bias fill of every buffer's (lanes, columns) owned by this warp
-    for (int b = 0; b < NBUF; ++b)
-      for (int c32 = 0; c32 < kEpiCols / 32; ++c32)
-        tmem_st32_const(tmem_base + lane_addr + b * TN + cg * kEpiCols + 32 * c32, kBias);
-    tmem_st_wait();
-    tc_fence_before();
-    __syncwarp();
+    // every TMEM buffer starts free
     if (lane == 0) {
       for (int b = 0; b < NBUF; ++b) mbar_arrive(&tm_empty[b]);
     }
@@ -440,38 +432,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait_or_poison(&tm_full[buf], (ib / NBUF) & 1, p.err, DEV_TIMEOUT_FULL, dead);
         tc_fence_after();
         const uint32_t taddr = tmem_base + lane_addr + buf * TN + cg * kEpiCols;
+        // all of this thread's columns in one round trip, then hand the buffer back
+        uint32_t v[kEpiCols];
 #pragma unroll
-        for (int ch = 0; ch < kEpiCols / 16; ++ch) {
-          uint32_t v[16];
-          tmem_ld16(taddr + 16 * ch, v);
-          tmem_ld_wait();
-          if (ch == kEpiCols / 16 - 1) {
-            // every column of this thread is in registers: restore the bias and hand the buffer back
+        for (int ch = 0; ch < kEpiCols / 16; ++ch)
+          tmem_ld16(taddr + 16 * ch, *reinterpret_cast<uint32_t(*)[16]>(&v[16 * ch]));
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tm_empty[buf]);
 #pragma unroll
-            for (int c32 = 0; c32 < kEpiCols / 32; ++c32) tmem_st32_const(taddr + 32 * c32, kBias);
-            tmem_st_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tm_empty[buf]);
-          }
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int a = 8 * ch + 2 * q;  // packed accumulator index
-            const uint4 w4 = dw[4 * ch + q];  // scales of 4 columns (broadcast read)
-            const uint64_t wa = pk2u(w4.x, w4.y), wb = pk2u(w4.z, w4.w);
-            const uint64_t fa = pk2u(v[4 * q], v[4 * q + 1]), fb = pk2u(v[4 * q + 2], v[4 * q + 3]);
-            const uint64_t pa = fma2(fa, D2, NC2), pb = fma2(fb, D2, NC2);  // d_a * sumi
-            if constexpr (WT == KQ_Q8_0) {
-              acc[a] = fma2(pa, wa, acc[a]);
-              acc[a + 1] = fma2(pb, wb, acc[a + 1]);
-            } else if constexpr (WT == KQ_Q4_0) {
-              acc[a] = fma2(add2(pa, MS2), wa, acc[a]);  // d_w * (d_a sumi - 8 s_a)
-              acc[a + 1] = fma2(add2(pb, MS2), wb, acc[a + 1]);
-            } else {
-              const uint4 m4 = mw[4 * ch + q];
-              acc[a] = fma2(pk2u(m4.x, m4.y), S2, fma2(pa, wa, acc[a]));  // d_w d_a sumi + m_w s_a
-              acc[a + 1] = fma2(pk2u(m4.z, m4.w), S2, fma2(pb, wb, acc[a + 1]));
-            }
+        for (int q = 0; q < kEpiCols / 4; ++q) {
+          const int a = 2 * q;  // packed accumulator index
+          const uint4 w4 = dw[q];  // scales of 4 columns (broadcast read)
+          const uint64_t wa = pk2u(w4.x, w4.y), wb = pk2u(w4.z, w4.w);
+          const uint64_t fa = pk2u(v[4 * q] + kBias, v[4 * q + 1] + kBias);
+          const uint64_t fb = pk2u(v[4 * q + 2] + kBias, v[4 * q + 3] + kBias);
+          const uint64_t pa = fma2(fa, D2, NC2), pb = fma2(fb, D2, NC2);  // d_a * sumi
+          if constexpr (WT == KQ_Q8_0) {
+            acc[a] = fma2(pa, wa, acc[a]);
+            acc[a + 1] = fma2(pb, wb, acc[a + 1]);
+          } else if constexpr (WT == KQ_Q4_0) {
+            acc[a] = fma2(add2(pa, MS2), wa, acc[a]);  // d_w * (d_a sumi - 8 s_a)
+            acc[a + 1] = fma2(add2(pb, MS2), wb, acc[a + 1]);
+          } else {
+            const uint4 m4 = mw[q];
+            acc[a] = fma2(pk2u(m4.x, m4.y), S2, fma2(pa, wa, acc[a]));  // d_w d_a sumi + m_w s_a
+            acc[a + 1] = fma2(pk2u(m4.z, m4.w), S2, fma2(pb, wb, acc[a + 1]));
           }
         }
       }
