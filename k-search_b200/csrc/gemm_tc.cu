@@ -11,14 +11,17 @@
 // separate MMA (K = 32, one instruction) into a fresh TMEM buffer; the fp32
 // accumulation across blocks happens in the epilogue warps' registers.
 //
-// CTA = 10 warps, one CTA per SM, persistent over 128 x 128 output tiles
+// CTA = 11 warps, one CTA per SM, persistent over 128 x 128 output tiles
 // (tokens x weight rows), tokens fastest so co-running CTAs share weights in L2:
 //   warp 0      TMA producer: activation codes (int8 [M, K], 128B-swizzled
 //               boxes of 128 rows x 128 B = 4 blocks), activation (d, s)
 //               pairs, and raw weight rows (the unchanged AoS q-blocks,
 //               128 rows x 8 blocks per box). No multicast anywhere.
-//   warp 1      TMEM allocator + single-thread MMA issuer.
-//   warps 2-9   workers. For K stage s they first convert the raw weight
+//   warps 1-2   MMA issuers (one thread each): warp 1+i issues K blocks
+//               i, i+2 of every stage into TMEM buffers i, i+2, so two
+//               issue/commit latency chains run side by side; warp 1 also
+//               owns the TMEM allocation.
+//   warps 3-10  workers. For K stage s they first convert the raw weight
 //               blocks of stage s+1 (two blocks of one row per thread) into
 //               int8 codes in the UMMA K-major SWIZZLE_128B layout plus fp32
 //               scale rows (then fence.proxy.async and release it to the MMA),
@@ -45,11 +48,12 @@ constexpr int SA = 3;          // activation stages
 constexpr int SWS = 3;         // converted weight stages
 constexpr int SRAW = 2;        // raw weight stages
 constexpr int NBUF = 4;        // TMEM buffers
-constexpr int kWarpTma = 0, kWarpMma = 1, kWarpWork = 2, kWorkWarps = 8;
-constexpr int kEpiCols = TN / (kWorkWarps / 4);  // columns per worker thread in the epilogue (64)
+constexpr int kWarpTma = 0, kWarpMma = 1, kMmaWarps = 2, kWarpWork = kWarpMma + kMmaWarps, kWorkWarps = 8;
+constexpr int kEpiCols = TN / (kWorkWarps / 4);  // columns per worker thread in the epilogue (32)
 constexpr int kWarps = kWarpWork + kWorkWarps;
 constexpr int kThreads = kWarps * 32;
 constexpr int kTmemCols = NBUF * TN;  // 512
+static_assert(NBUF == KSUB && NBUF % kMmaWarps == 0, "one TMEM buffer per K block of a stage, split over the issuers");
 
 template <int WT>
 struct TcTraits {
@@ -177,11 +181,12 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
   return d;
 }
 
-// Integer -> float without a conversion instruction: for |sumi| < 2^22 the
-// int32 (kBias + sumi), kBias = bits of 12582912.0f (1.5 * 2^23), is the fp32
-// bit pattern of 12582912 + sumi exactly (one integer add on the ALU pipe).
-// Then d * sumi = fma(f, d, -12582912 d), exact before the final rounding
-// when 12582912 d is exact (d with <= 22 significant bits; fp16 scales always
+// Integer -> float without a conversion instruction: every TMEM accumulator
+// word is preset to kBias = bits of 12582912.0f (1.5 * 2^23) and the MMA
+// accumulates the block's int32 sum onto it; for |sumi| < 2^22 the result
+// (kBias + sumi) is the fp32 bit pattern of 12582912 + sumi exactly. Then
+// d * sumi = fma(f, d, -12582912 d), exact before the final rounding when
+// 12582912 d is exact (d with <= 22 significant bits; fp16 scales always
 // are, fp32 scales are rounded to 22 bits, a relative change below 2^-22).
 constexpr uint32_t kBias = 0x4B400000u;
 constexpr float kBiasF = 12582912.0f;
@@ -247,11 +252,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < SA; ++i) {
       mbar_init(&act_full[i], 1);
-      mbar_init(&act_empty[i], 1 + kWorkWarps);  // MMA commit + workers (they read the scales)
+      mbar_init(&act_empty[i], kMmaWarps + kWorkWarps);  // MMA commits + workers (they read the scales)
     }
     for (int i = 0; i < SWS; ++i) {
       mbar_init(&w_full[i], kWorkWarps);
-      mbar_init(&w_empty[i], 1 + kWorkWarps);
+      mbar_init(&w_empty[i], kMmaWarps + kWorkWarps);
     }
     for (int i = 0; i < SRAW; ++i) {
       mbar_init(&raw_full[i], 1);
@@ -300,29 +305,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == kWarpMma) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp < kWarpWork) {
+    // ------------------------------------------------------------ MMA issuers
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_i8(T::kSignedW);
+      const int i0 = warp - kWarpMma;  // this thread issues K blocks i0, i0 + kMmaWarps, ... of every stage
       const uint32_t act_base = smem_u32(smem + T::OFF_ACT);
       const uint32_t w_base = smem_u32(smem + T::OFF_W);
-      int ia = 0, iw = 0, ib = 0;
+      int ia = 0;
       for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
-        for (int s = 0; s < p.nb / KSUB; ++s, ++ia, ++iw) {
-          const int as = ia % SA, ws = iw % SWS;
+        for (int s = 0; s < p.nb / KSUB; ++s, ++ia) {
+          const int as = ia % SA, ws = ia % SWS;
           mbar_wait_or_poison(&act_full[as], (ia / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-          mbar_wait_or_poison(&w_full[ws], (iw / SWS) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-          tc_fence_after();
+          mbar_wait_or_poison(&w_full[ws], (ia / SWS) & 1, p.err, DEV_TIMEOUT_FULL, dead);
           const uint64_t adesc = sw128_desc(act_base + as * T::ACT_TILE);
           const uint64_t bdesc = sw128_desc(w_base + ws * T::W_TILE);
 #pragma unroll
-          for (int j = 0; j < KSUB; ++j, ++ib) {
-            const int buf = ib % NBUF;
-            mbar_wait_or_poison(&tm_empty[buf], (ib / NBUF) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+          for (int j = i0; j < KSUB; j += kMmaWarps) {
+            mbar_wait_or_poison(&tm_empty[j], ia & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
             tc_fence_after();
-            // K block j of the stage: +32 bytes inside the 128-byte swizzle atom
-            mma_i8(tmem_base + buf * TN, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), idesc, 0u);
-            mma_commit(&tm_full[buf]);
+            // K block j of the stage: +32 bytes inside the 128-byte swizzle atom;
+            // accumulate onto the bias words the workers left in the buffer.
+            mma_i8(tmem_base + j * TN, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), idesc, 1u);
+            mma_commit(&tm_full[j]);
           }
           mma_commit(&act_empty[as]);
           mma_commit(&w_empty[ws]);
@@ -337,11 +342,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = quarter * 32 + lane;    // token row in the tile (epilogue)
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
     const int crow = (wi * 32 + lane) >> 1; // weight row converted by this thread
-    const int chalf = lane & 1;             // which two blocks of the 4-block stage
-    // byte offsets of this row's 16-byte chunks 4*chalf .. 4*chalf+3 in a 128B-swizzled tile
-    int coff[4];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) coff[c] = sw128_off(crow, 4 * chalf + c);
+    const int chalf = lane & 1;             // blocks 2*chalf, 2*chalf+1 of the 4-block stage
+    const int coff0 = sw128_off(crow, 4 * chalf), coff1 = sw128_off(crow, 4 * chalf + 1);
+    const int coff2 = sw128_off(crow, 4 * chalf + 2), coff3 = sw128_off(crow, 4 * chalf + 3);
     const int spt = p.nb / KSUB;            // K stages per tile (even: nb % 8 == 0)
     const int my_tiles = (p.num_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
     const int total = my_tiles * spt;
@@ -383,8 +386,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           c1 = make_uint4((a0 >> 4) & 0x0F0F0F0Fu, (a1 >> 4) & 0x0F0F0F0Fu, (a2 >> 4) & 0x0F0F0F0Fu,
                           (a3 >> 4) & 0x0F0F0F0Fu);
         }
-        *reinterpret_cast<uint4*>(wt + coff[2 * jj]) = c0;
-        *reinterpret_cast<uint4*>(wt + coff[2 * jj + 1]) = c1;
+        *reinterpret_cast<uint4*>(wt + (jj == 0 ? coff0 : coff2)) = c0;
+        *reinterpret_cast<uint4*>(wt + (jj == 0 ? coff1 : coff3)) = c1;
         const int j = 2 * chalf + jj;
         wsc[j * TN + crow] = d;
         if constexpr (T::kHasMin) wsc[KSUB * TN + j * TN + crow] = mn;
@@ -397,13 +400,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     };
 
-    // every TMEM buffer starts free
+    // every TMEM buffer starts free, preset to the bias
+    for (int b = 0; b < NBUF; ++b)
+      for (int c32 = 0; c32 < kEpiCols / 32; ++c32)
+        tmem_st32_const(tmem_base + lane_addr + b * TN + cg * kEpiCols + 32 * c32, kBias);
+    tmem_st_wait();
+    tc_fence_before();
+    __syncwarp();
     if (lane == 0) {
       for (int b = 0; b < NBUF; ++b) mbar_arrive(&tm_empty[b]);
     }
 
     if (total > 0) convert(0);
-    uint64_t acc[kEpiCols / 2];  // fp32 accumulators as packed pairs
+    float acc[kEpiCols];  // fp32 accumulators
     int ib = 0;
     for (int es = 0; es < total; ++es) {
       if (es + 1 < total) convert(es + 1);
@@ -411,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int t = (int)blockIdx.x + (es / spt) * (int)gridDim.x;
       if (s == 0) {
 #pragma unroll
-        for (int c = 0; c < kEpiCols / 2; ++c) acc[c] = 0ull;
+        for (int c = 0; c < kEpiCols; ++c) acc[c] = 0.0f;
       }
       const int as = es % SA, ws = es % SWS;
       mbar_wait_or_poison(&act_full[as], (es / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
@@ -423,44 +432,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int buf = ib % NBUF;
         const float2 dsj = asc[j];
         const float d = round22(dsj.x);
-        const uint64_t D2 = pk2(d, d);
-        const uint64_t NC2 = pk2(-kBiasF * d, -kBiasF * d);
-        const uint64_t MS2 = pk2(-8.0f * dsj.y, -8.0f * dsj.y);
-        const uint64_t S2 = pk2(dsj.y, dsj.y);
-        const uint4* dw = reinterpret_cast<const uint4*>(wsc + j * TN + cg * kEpiCols);
-        const uint4* mw = reinterpret_cast<const uint4*>(wsc + KSUB * TN + j * TN + cg * kEpiCols);
+        const float ncs = -kBiasF * d;
+        const float ms8 = -8.0f * dsj.y;
+        const float sy = dsj.y;
+        const float* dw = wsc + j * TN + cg * kEpiCols;
+        const float* mw = wsc + KSUB * TN + j * TN + cg * kEpiCols;
         mbar_wait_or_poison(&tm_full[buf], (ib / NBUF) & 1, p.err, DEV_TIMEOUT_FULL, dead);
         tc_fence_after();
         const uint32_t taddr = tmem_base + lane_addr + buf * TN + cg * kEpiCols;
-        // all of this thread's columns in one round trip, then hand the buffer back
-        uint32_t v[kEpiCols];
+        // 16 columns per TMEM round trip; re-arm the bias (asynchronously) and
+        // hand the buffer back after the math
 #pragma unroll
-        for (int ch = 0; ch < kEpiCols / 16; ++ch)
-          tmem_ld16(taddr + 16 * ch, *reinterpret_cast<uint32_t(*)[16]>(&v[16 * ch]));
-        tmem_ld_wait();
+        for (int h = 0; h < kEpiCols / 16; ++h) {
+          uint32_t v[16];
+          tmem_ld16(taddr + 16 * h, v);
+          tmem_ld_wait();
+          if (h == kEpiCols / 16 - 1) {
+#pragma unroll
+            for (int c32 = 0; c32 < kEpiCols / 32; ++c32) tmem_st32_const(taddr + 32 * c32, kBias);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 w4 = reinterpret_cast<const float4*>(dw + 16 * h)[q];  // scales of 4 columns (broadcast)
+            const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+            float mv[4] = {0.f, 0.f, 0.f, 0.f};
+            if constexpr (WT == KQ_Q4_1) {
+              const float4 m4 = reinterpret_cast<const float4*>(mw + 16 * h)[q];
+              mv[0] = m4.x; mv[1] = m4.y; mv[2] = m4.z; mv[3] = m4.w;
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int c = 16 * h + 4 * q + e;
+              const float pr = fmaf(__uint_as_float(v[4 * q + e]), d, ncs);  // d_a * sumi
+              if constexpr (WT == KQ_Q8_0) {
+                acc[c] = fmaf(pr, wv[e], acc[c]);
+              } else if constexpr (WT == KQ_Q4_0) {
+                acc[c] = fmaf(pr + ms8, wv[e], acc[c]);  // d_w * (d_a sumi - 8 s_a)
+              } else {
+                acc[c] = fmaf(mv[e], sy, fmaf(pr, wv[e], acc[c]));  // d_w d_a sumi + m_w s_a
+              }
+            }
+          }
+        }
+        tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tm_empty[buf]);
-#pragma unroll
-        for (int q = 0; q < kEpiCols / 4; ++q) {
-          const int a = 2 * q;  // packed accumulator index
-          const uint4 w4 = dw[q];  // scales of 4 columns (broadcast read)
-          const uint64_t wa = pk2u(w4.x, w4.y), wb = pk2u(w4.z, w4.w);
-          const uint64_t fa = pk2u(v[4 * q] + kBias, v[4 * q + 1] + kBias);
-          const uint64_t fb = pk2u(v[4 * q + 2] + kBias, v[4 * q + 3] + kBias);
-          const uint64_t pa = fma2(fa, D2, NC2), pb = fma2(fb, D2, NC2);  // d_a * sumi
-          if constexpr (WT == KQ_Q8_0) {
-            acc[a] = fma2(pa, wa, acc[a]);
-            acc[a + 1] = fma2(pb, wb, acc[a + 1]);
-          } else if constexpr (WT == KQ_Q4_0) {
-            acc[a] = fma2(add2(pa, MS2), wa, acc[a]);  // d_w * (d_a sumi - 8 s_a)
-            acc[a + 1] = fma2(add2(pb, MS2), wb, acc[a + 1]);
-          } else {
-            const uint4 m4 = mw[q];
-            acc[a] = fma2(pk2u(m4.x, m4.y), S2, fma2(pa, wa, acc[a]));  // d_w d_a sumi + m_w s_a
-            acc[a + 1] = fma2(pk2u(m4.z, m4.w), S2, fma2(pb, wb, acc[a + 1]));
-          }
-        }
       }
       __syncwarp();
       if (lane == 0) {
@@ -476,17 +493,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           float* o = p.out + (size_t)m * p.N + nc0;
           if (nc0 + kEpiCols <= p.N && (p.N & 3) == 0) {
 #pragma unroll
-            for (int c = 0; c < kEpiCols / 2; c += 2) {
-              const float2 a0 = upk2(acc[c]), a1 = upk2(acc[c + 1]);
-              *reinterpret_cast<float4*>(o + 2 * c) = make_float4(a0.x, a0.y, a1.x, a1.y);
-            }
+            for (int c = 0; c < kEpiCols; c += 4)
+              *reinterpret_cast<float4*>(o + c) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
           } else {
 #pragma unroll
-            for (int c = 0; c < kEpiCols / 2; ++c) {
-              const float2 a0 = upk2(acc[c]);
-              if (nc0 + 2 * c < p.N) o[2 * c] = a0.x;
-              if (nc0 + 2 * c + 1 < p.N) o[2 * c + 1] = a0.y;
-            }
+            for (int c = 0; c < kEpiCols; ++c)
+              if (nc0 + c < p.N) o[c] = acc[c];
           }
         }
       }
