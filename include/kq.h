@@ -145,14 +145,15 @@ kq_status_t kq_fa_decode_q8_0_mha(const float* q, const void* k, const void* v, 
                                   int D, kq_stream_t stream);
 
 /* Ragged GQA flash-decode over a q8_0 KV cache (benchmark configuration 3).
- * q fp16 [B, Hq, D]; k, v = q8_0 blocks of [T, Hkv, D] with T = cu_seqlens[B];
- * sequence b owns cache rows cu_seqlens[b] .. cu_seqlens[b+1]-1 (int32, device);
- * query head h reads KV head h / (Hq / Hkv); fp32 softmax and accumulation;
- * out fp16 [B, Hq, D]. max_seqlen bounds the per-sequence length (used to
- * size the split-KV grid). An empty sequence yields zeros. */
+ * q fp16 [B, Hq, D]; k, v = q8_0 blocks of [total_rows, Hkv, D] (total_rows =
+ * token rows allocated in the cache, >= cu_seqlens[B]); sequence b owns cache
+ * rows cu_seqlens[b] .. cu_seqlens[b+1]-1 (int32, device); query head h reads
+ * KV head h / (Hq / Hkv); fp32 softmax and accumulation; out fp16 [B, Hq, D].
+ * max_seqlen bounds the per-sequence length (it sizes the split-KV grid).
+ * An empty sequence yields zeros. */
 kq_status_t kq_fa_decode_q8_0_ragged(const void* q_f16, const void* k, const void* v, const int32_t* cu_seqlens,
-                                     int B, int Hq, int Hkv, int D, int max_seqlen, float scale, void* out_f16,
-                                     kq_stream_t stream);
+                                     int B, int Hq, int Hkv, int D, int max_seqlen, int total_rows, float scale,
+                                     void* out_f16, kq_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -102,6 +102,21 @@ int* device_error_word() {
   return st.err_word;
 }
 
+void* tensor_map_encoder() {
+  static void* fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = f;
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
 namespace {
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -237,14 +252,14 @@ kq_status_t kq_fa_decode_q8_0_mha(const float* q, const void* k, const void* v, 
 }
 
 kq_status_t kq_fa_decode_q8_0_ragged(const void* q_f16, const void* k, const void* v, const int32_t* cu_seqlens,
-                                     int B, int Hq, int Hkv, int D, int max_seqlen, float scale, void* out_f16,
-                                     kq_stream_t stream) {
-  if (B < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || D <= 0 || D % 32 || D > 256 || max_seqlen < 0)
+                                     int B, int Hq, int Hkv, int D, int max_seqlen, int total_rows, float scale,
+                                     void* out_f16, kq_stream_t stream) {
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || D <= 0 || D % 32 || D > 256 || max_seqlen < 0 || total_rows < 0)
     return fail(KQ_ERR_INVALID, "fa_ragged: bad shape B=%d Hq=%d Hkv=%d D=%d", B, Hq, Hkv, D);
   if (B == 0) return KQ_OK;
   if (!q_f16 || !out_f16 || !cu_seqlens || !k || !v) return fail(KQ_ERR_INVALID, "fa_ragged: null pointer");
   if (!aligned(k, 2) || !aligned(v, 2)) return fail(KQ_ERR_INVALID, "fa_ragged: caches must be 2-byte aligned");
-  return launch_fa_ragged(q_f16, k, v, cu_seqlens, B, Hq, Hkv, D, max_seqlen, scale, out_f16,
+  return launch_fa_ragged(q_f16, k, v, cu_seqlens, B, Hq, Hkv, D, max_seqlen, total_rows, scale, out_f16,
                           static_cast<cudaStream_t>(stream));
 }
 

@@ -7,12 +7,24 @@
 // x = q * d. The ragged GQA form (one KV stream per (sequence, KV head),
 // shared by Hq/Hkv query heads) follows the same arithmetic.
 //
-// Structure: pass 1 gives every (KV stream, token chunk, query group) to one
+// Fast path (head_dim 128, KV heads in groups of 8, <= 4 queries per KV
+// head): one CTA per (sequence or query group, token chunk, group of 8 KV
+// heads). A producer warp streams 32-token tiles of K and V for the 8 heads
+// (1088 contiguous bytes per token row: the cache's own layout) with 2D TMA
+// boxes into a double-buffered ring; each of 8 compute warps owns one KV head
+// and its queries, lanes own 4 head dims. Scores are partial dot products
+// reduced with a transpose-halving warp reduction (8 tokens x 4 queries per
+// step); q8_0 bytes become fp32 exactly through a sign-extending byte permute
+// and the 1.5 * 2^23 bias (x = fma(f, d, -12582912 d)), no conversion op.
+//
+// Generic path: pass 1 gives every (KV stream, token chunk, query group) to one
 // CTA, one warp per query; each warp keeps an online-softmax state (running
 // max in the log2 domain, running sum, fp32 accumulator) and writes it as a
 // partial. Pass 2 merges the partials of each query. Lanes own head-dim
 // elements {32 j + lane}, so every q8_0 block row is read as 32 consecutive
 // bytes by the warp.
+#include <cuda.h>
+
 #include <algorithm>
 #include <cmath>
 
@@ -21,6 +33,19 @@
 
 namespace kq {
 namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+CUresult encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, cuuint32_t rank, void* base, const cuuint64_t* dims,
+                      const cuuint64_t* strides, const cuuint32_t* box, const cuuint32_t* estr,
+                      CUtensorMapInterleave il, CUtensorMapSwizzle sw, CUtensorMapL2promotion l2,
+                      CUtensorMapFloatOOBfill oob) {
+  auto fn = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
+  if (!fn) return CUDA_ERROR_NOT_SUPPORTED;
+  return fn(map, dt, rank, base, dims, strides, box, estr, il, sw, l2, oob);
+}
 
 constexpr int kQPerCta = 4;  // queries (warps) per CTA
 constexpr int kMaxDJ = 8;    // head_dim <= 256
@@ -151,6 +176,288 @@ __global__ void __launch_bounds__(128) fa_combine_kernel(FaParams p, int Q) {
     if (j < dj) store_o(o, (size_t)j * 32 + lane, acc[j] * inv);
 }
 
+// ---------------------------------------------------------------------------
+// Fast path
+// ---------------------------------------------------------------------------
+constexpr int kHpc = 8;        // KV heads per CTA (one compute warp each)
+constexpr int kG = 4;          // queries per KV head per CTA
+constexpr int kSt = 32;        // tokens per TMA tile
+constexpr int kStages = 2;
+constexpr int kRowBytes = kHpc * 136;  // one token row of 8 heads x (4 q8_0 blocks of 34 B)
+constexpr int kTile = kSt * kRowBytes;
+constexpr int kFastThreads = (kHpc + 1) * 32;
+constexpr size_t kFastSmem = 2 * kStages * kTile + kHpc * kG * 128 * 4 + kHpc * kSt * kG * 4 + 4 * kStages * 8 + 128;
+
+struct FastParams {
+  const void* q;
+  const int32_t* cu;  // ragged only
+  float* pm;
+  float* pl;
+  float* pacc;
+  int B, H, Hkv, S, NC, chunk;
+  int n_hg;           // KV head groups (Hkv / 8)
+  float qscale;
+};
+
+__device__ __forceinline__ void tma_load_2d_u64(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Transpose-halving warp reduction of 32 per-lane values: lane l ends with the
+// sum over lanes of value index l.
+__device__ __forceinline__ float warp_reduce32_transpose(float (&v)[32], int lane) {
+#pragma unroll
+  for (int mask = 16, half = 16; mask >= 1; mask >>= 1, half >>= 1) {
+    const bool upper = (lane & mask) != 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if (i < half) {
+        const float send = upper ? v[i] : v[i + half];
+        const float keep = upper ? v[i + half] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, mask);
+      }
+    }
+  }
+  return v[0];
+}
+
+// 4 signed bytes of w -> fp32 values d * byte (exact before the final rounding).
+__device__ __forceinline__ void dequant4(uint32_t w, float d, float (&o)[4]) {
+  const float nc = -12582912.0f * d;  // exact: fp16 d times 1.5 * 2^23
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int k = (int)__byte_perm(w, 0u, (unsigned)(i | ((8 | i) << 4) | ((8 | i) << 8) | ((8 | i) << 12)));
+    o[i] = fmaf(__int_as_float(k + 0x4B400000), d, nc);
+  }
+}
+
+// Read the 4 code bytes (head dims 4l..4l+3) and the block scale of one token
+// row for KV head `w`; rows are 4-byte aligned, blocks 2-byte aligned.
+__device__ __forceinline__ uint32_t row_codes(const uint8_t* row, int w, int lane, float& d) {
+  const int blk = lane >> 3;
+  const uint8_t* b = row + w * 136 + blk * 34;
+  d = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(b)));
+  const uintptr_t a = reinterpret_cast<uintptr_t>(b + 2 + 4 * (lane & 7));
+  const uint32_t* p = reinterpret_cast<const uint32_t*>(a & ~(uintptr_t)3);
+  return __funnelshift_r(p[0], p[1], (a & 2) ? 16u : 0u);
+}
+
+template <typename QT, bool RAGGED>
+__global__ void __launch_bounds__(kFastThreads, 1)
+    fa_fast_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, FastParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~(uintptr_t)127);
+  uint8_t* ktile = smem;
+  uint8_t* vtile = smem + kStages * kTile;
+  float* qs = reinterpret_cast<float*>(smem + 2 * kStages * kTile);      // [8][4][128]
+  float* ps = qs + kHpc * kG * 128;                                       // [8][32 tokens][4]
+  uint64_t* full = reinterpret_cast<uint64_t*>(ps + kHpc * kSt * kG);
+  uint64_t* empty = full + kStages;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x;
+  const int item = blockIdx.y;
+  const int hg = item % p.n_hg;
+  const int grp = item / p.n_hg;  // RAGGED: sequence b; else query group
+  int L, row0, nq;
+  if (RAGGED) {
+    row0 = p.cu[grp];
+    L = p.cu[grp + 1] - row0;
+    nq = p.H / p.Hkv;
+  } else {
+    row0 = 0;
+    L = p.S;
+    nq = min(kG, p.B - grp * kG);
+  }
+  const int t0 = c * p.chunk, t1 = min(L, t0 + p.chunk);
+  const int nsub = t1 > t0 ? (t1 - t0 + kSt - 1) / kSt : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kHpc);
+    }
+    fence_mbar_init();
+  }
+  // queries of this CTA into shared memory, pre-scaled by scale * log2(e)
+  for (int i = threadIdx.x; i < kHpc * kG * 128; i += blockDim.x) {
+    const int w = i / (kG * 128), j = (i / 128) % kG, dim = i % 128;
+    const int hk = hg * kHpc + w;
+    float v = 0.0f;
+    if (j < nq) {
+      size_t qi;
+      if (RAGGED) qi = ((size_t)grp * p.H + (size_t)hk * (p.H / p.Hkv) + j) * 128 + dim;
+      else qi = ((size_t)(grp * kG + j) * p.H + hk) * 128 + dim;
+      v = load_q(static_cast<const QT*>(p.q), qi) * p.qscale;
+    }
+    qs[i] = v;
+  }
+  __syncthreads();
+
+  bool dead = false;
+  if (warp == kHpc) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      for (int i = 0; i < nsub; ++i) {
+        const int s = i % kStages;
+        if (i >= kStages) mbar_wait_or_poison(&empty[s], ((i / kStages) - 1) & 1, nullptr, 0, dead);
+        mbar_arrive_expect_tx(&full[s], 2 * kTile);
+        const int y = row0 + t0 + i * kSt;
+        tma_load_2d_u64(ktile + s * kTile, &kmap, hg * (kRowBytes / 8), y, &full[s]);
+        tma_load_2d_u64(vtile + s * kTile, &vmap, hg * (kRowBytes / 8), y, &full[s]);
+      }
+      // drain: every issued tile must be consumed before the CTA exits
+      for (int i = max(0, nsub - kStages); i < nsub; ++i)
+        mbar_wait_or_poison(&empty[i % kStages], (i / kStages) & 1, nullptr, 0, dead);
+    }
+    return;
+  }
+
+  // ---------------- compute warp: KV head hg*8 + warp ----------------
+  const int w = warp;
+  float qv[kG][4];
+#pragma unroll
+  for (int j = 0; j < kG; ++j) {
+    const float4 t = reinterpret_cast<const float4*>(qs + (w * kG + j) * 128)[lane];
+    qv[j][0] = t.x; qv[j][1] = t.y; qv[j][2] = t.z; qv[j][3] = t.w;
+  }
+  float acc[kG][4];
+#pragma unroll
+  for (int j = 0; j < kG; ++j)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[j][i] = 0.0f;
+  float m_run = -INFINITY, l_run = 0.0f;  // for query (lane & 3)
+  float* pw = ps + w * kSt * kG;
+
+  for (int it = 0; it < nsub; ++it) {
+    const int s = it % kStages;
+    mbar_wait_or_poison(&full[s], (it / kStages) & 1, nullptr, 0, dead);
+    const uint8_t* kt = ktile + s * kTile;
+    const uint8_t* vt = vtile + s * kTile;
+    const int tb = t0 + it * kSt;  // first token of the tile
+
+    // ---- scores: 4 groups of 8 tokens x 4 queries ----
+    float sc[4];
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+      float part[32];
+#pragma unroll
+      for (int tt = 0; tt < 8; ++tt) {
+        float d;
+        const uint32_t cw = row_codes(kt + (8 * g + tt) * kRowBytes, w, lane, d);
+        float kf[4];
+        dequant4(cw, d, kf);
+#pragma unroll
+        for (int j = 0; j < kG; ++j)
+          part[tt * kG + j] = fmaf(qv[j][0], kf[0], fmaf(qv[j][1], kf[1], fmaf(qv[j][2], kf[2], qv[j][3] * kf[3])));
+      }
+      const float sv = warp_reduce32_transpose(part, lane);  // token 8g + lane/4, query lane%4
+      const int tok = tb + 8 * g + (lane >> 2);
+      sc[g] = (tok < t1 && (lane & 3) < nq) ? sv : -INFINITY;
+    }
+    // ---- online softmax for query (lane & 3) ----
+    float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    const float m_new = fmaxf(m_run, mx);
+    float pr[4], ls = 0.0f;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      pr[g] = (m_new == -INFINITY) ? 0.0f : exp2f(sc[g] - m_new);
+      ls += pr[g];
+    }
+    ls += __shfl_xor_sync(0xffffffffu, ls, 4);
+    ls += __shfl_xor_sync(0xffffffffu, ls, 8);
+    ls += __shfl_xor_sync(0xffffffffu, ls, 16);
+    const float corr = (m_run == -INFINITY) ? 0.0f : exp2f(m_run - m_new);
+    l_run = fmaf(l_run, corr, ls);
+    m_run = m_new;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) pw[(8 * g + (lane >> 2)) * kG + (lane & 3)] = pr[g];
+    __syncwarp();
+    // ---- rescale and accumulate P . V ----
+#pragma unroll
+    for (int j = 0; j < kG; ++j) {
+      const float cj = __shfl_sync(0xffffffffu, corr, j);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[j][i] *= cj;
+    }
+#pragma unroll 4
+    for (int tt = 0; tt < kSt; ++tt) {
+      float d;
+      const uint32_t cw = row_codes(vt + tt * kRowBytes, w, lane, d);
+      float vf[4];
+      dequant4(cw, d, vf);
+      const float4 pj = reinterpret_cast<const float4*>(pw)[tt];
+      const float pv[4] = {pj.x, pj.y, pj.z, pj.w};
+#pragma unroll
+      for (int j = 0; j < kG; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[j][i] = fmaf(pv[j], vf[i], acc[j][i]);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+
+  // ---- partial state of each query of this warp ----
+  const int hk = hg * kHpc + w;
+#pragma unroll
+  for (int j = 0; j < kG; ++j) {
+    if (j >= nq) break;
+    size_t qg;
+    if (RAGGED) qg = (size_t)grp * p.H + (size_t)hk * (p.H / p.Hkv) + j;
+    else qg = (size_t)(grp * kG + j) * p.H + hk;
+    const size_t pi = qg * p.NC + c;
+    const float mj = __shfl_sync(0xffffffffu, m_run, j);
+    const float lj = __shfl_sync(0xffffffffu, l_run, j);
+    if (lane == 0) {
+      p.pm[pi] = mj;
+      p.pl[pi] = lj;
+    }
+    reinterpret_cast<float4*>(p.pacc + pi * 128)[lane] = make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
+  }
+}
+
+bool encode_kv_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t heads) {
+  // [rows][heads * 136 bytes] as uint64 elements; boxes of 32 rows x 8 heads
+  cuuint64_t dims[2] = {heads * 17, rows};
+  cuuint64_t strides[1] = {heads * 136};
+  cuuint32_t box[2] = {kRowBytes / 8, kSt};
+  cuuint32_t estr[2] = {1, 1};
+  return encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(base), dims, strides, box,
+                                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename QT, bool RAGGED>
+kq_status_t launch_fast(const FastParams& p, const void* k, const void* v, uint64_t rows, int heads, int items,
+                        cudaStream_t s) {
+  CUtensorMap km, vm;
+  if (!encode_kv_map(&km, k, rows, heads) || !encode_kv_map(&vm, v, rows, heads))
+    return fail(KQ_ERR_CUDA, "fa: KV tensor map rejected");
+  auto kern = fa_fast_kernel<QT, RAGGED>;
+  static unsigned attr_done = 0;
+  const int dev = current_device();
+  if (!(attr_done & (1u << (dev & 31)))) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFastSmem);
+    if (e != cudaSuccess) return check_cuda(e, "fa smem attribute");
+    attr_done |= 1u << (dev & 31);
+  }
+  dim3 grid(p.NC, items);
+  kern<<<grid, kFastThreads, kFastSmem, s>>>(km, vm, p);
+  return check_launch("fa_fast");
+}
+
+bool fast_ok(const void* k, const void* v, int D, int Hkv, int g) {
+  return D == 128 && Hkv % kHpc == 0 && g <= kG && (reinterpret_cast<uintptr_t>(k) & 15) == 0 &&
+         (reinterpret_cast<uintptr_t>(v) & 15) == 0;
+}
+
 // Choose the number of chunks so the partial buffers stay within `budget`.
 int choose_chunks(long long Q, int D, int max_len, size_t budget, int* chunk) {
   int nc = std::max(1, (max_len + 255) / 256);
@@ -181,6 +488,16 @@ kq_status_t launch_fa_mha(const float* q, const void* k, const void* v, float* o
   p.pm = ws; p.pl = ws + Q * NC; p.pacc = ws + 2 * Q * NC; p.out = out;
   p.B = B; p.H = H; p.Hkv = H; p.D = D; p.S = S; p.NC = NC; p.chunk = chunk;
   p.qscale = (float)(1.0 / std::sqrt((double)D) * 1.4426950408889634);
+  if (fast_ok(k, v, D, H, 1) && S > 0) {
+    FastParams f{q, nullptr, p.pm, p.pl, p.pacc, B, H, H, S, NC, chunk, H / kHpc, p.qscale};
+    const long long items = (long long)((B + kG - 1) / kG) * (H / kHpc);
+    if (items <= 65535) {
+      kq_status_t st = launch_fast<float, false>(f, k, v, (uint64_t)S, H, (int)items, s);
+      if (st) return st;
+      fa_combine_kernel<float><<<(unsigned)((Q + 3) / 4), 128, 0, s>>>(p, (int)Q);
+      return check_launch("fa_combine(mha)");
+    }
+  }
   dim3 grid(NC, H, (B + kQPerCta - 1) / kQPerCta);
   if (grid.z > 65535 || grid.y > 65535) return fail(KQ_ERR_UNSUPPORTED, "fa_mha: grid too large");
   fa_partial_kernel<float, false><<<grid, 32 * kQPerCta, 0, s>>>(p);
@@ -191,7 +508,7 @@ kq_status_t launch_fa_mha(const float* q, const void* k, const void* v, float* o
 }
 
 kq_status_t launch_fa_ragged(const void* q, const void* k, const void* v, const int32_t* cu, int B, int Hq, int Hkv,
-                             int D, int max_seqlen, float scale, void* out, cudaStream_t s) {
+                             int D, int max_seqlen, int total_rows, float scale, void* out, cudaStream_t s) {
   const long long Q = (long long)B * Hq;
   if (Q == 0) return KQ_OK;
   int chunk = 0;
@@ -205,6 +522,14 @@ kq_status_t launch_fa_ragged(const void* q, const void* k, const void* v, const 
   p.B = B; p.H = Hq; p.Hkv = Hkv; p.D = D; p.S = max_seqlen; p.NC = NC; p.chunk = chunk;
   p.qscale = (float)((double)scale * 1.4426950408889634);
   const int g = Hq / Hkv;
+  if (fast_ok(k, v, D, Hkv, g) && total_rows > 0 && (long long)B * (Hkv / kHpc) <= 65535) {
+    // total_rows bounds the TMA map: no tile reads past the cache allocation
+    FastParams f{q, cu, p.pm, p.pl, p.pacc, B, Hq, Hkv, max_seqlen, NC, chunk, Hkv / kHpc, p.qscale};
+    kq_status_t st = launch_fast<__half, true>(f, k, v, (uint64_t)total_rows, Hkv, B * (Hkv / kHpc), s);
+    if (st) return st;
+    fa_combine_kernel<__half><<<(unsigned)((Q + 3) / 4), 128, 0, s>>>(p, (int)Q);
+    return check_launch("fa_combine(ragged)");
+  }
   dim3 grid(NC, (unsigned)((long long)B * Hkv), (g + kQPerCta - 1) / kQPerCta);
   if (grid.y > 65535) return fail(KQ_ERR_UNSUPPORTED, "fa_ragged: B*Hkv too large");
   fa_partial_kernel<__half, true><<<grid, 32 * kQPerCta, 0, s>>>(p);

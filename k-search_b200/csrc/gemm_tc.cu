@@ -40,6 +40,19 @@
 namespace kq {
 namespace {
 
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+CUresult encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, cuuint32_t rank, void* base, const cuuint64_t* dims,
+                      const cuuint64_t* strides, const cuuint32_t* box, const cuuint32_t* estr,
+                      CUtensorMapInterleave il, CUtensorMapSwizzle sw, CUtensorMapL2promotion l2,
+                      CUtensorMapFloatOOBfill oob) {
+  auto fn = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
+  if (!fn) return CUDA_ERROR_NOT_SUPPORTED;
+  return fn(map, dt, rank, base, dims, strides, box, estr, il, sw, l2, oob);
+}
+
 constexpr int TM = 128;        // tokens per tile (TMEM lanes)
 constexpr int TN = 128;        // weight rows per tile (TMEM columns per buffer)
 constexpr int KSUB = 4;        // blocks per activation / converted-weight stage (128 B of K)
@@ -520,7 +533,7 @@ bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint
   cuuint64_t strides[1] = {stride1_bytes};
   cuuint32_t box[2] = {box0, box1};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = cuTensorMapEncodeTiled(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+  CUresult r = encode_tiled(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
                                       CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;

@@ -22,6 +22,12 @@ kq_status_t check_launch(const char* what);
 int current_device();
 int sm_count();
 
+// ---- driver entry points ----------------------------------------------------
+// cuTensorMapEncodeTiled resolved through the runtime (no link-time libcuda
+// dependency, so the library loads on hosts without a driver). Returns
+// nullptr if unavailable.
+void* tensor_map_encoder();
+
 // ---- workspace ------------------------------------------------------------
 // Per-device cached scratch, one buffer per slot, grown on demand (never
 // shrunk). The buffer is ordered on `stream`: growing it synchronises the
@@ -75,6 +81,6 @@ kq_status_t launch_block_sums(int wtype, const void* w, const void* a_q8_1, int3
 kq_status_t launch_fa_mha(const float* q, const void* k, const void* v, float* out, int B, int S, int H, int D,
                           cudaStream_t s);
 kq_status_t launch_fa_ragged(const void* q, const void* k, const void* v, const int32_t* cu, int B, int Hq, int Hkv,
-                             int D, int max_seqlen, float scale, void* out, cudaStream_t s);
+                             int D, int max_seqlen, int total_rows, float scale, void* out, cudaStream_t s);
 
 }  // namespace kq

@@ -37,7 +37,7 @@ SIGNATURES = {
     "kq_mul_mat_q8x": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "kq_block_sums_i32": (_i, [_i, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "kq_fa_decode_q8_0_mha": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
-    "kq_fa_decode_q8_0_ragged": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _vp]),
+    "kq_fa_decode_q8_0_ragged": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp, _vp]),
 }
 
 _lib: ctypes.CDLL | None = None

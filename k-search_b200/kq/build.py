@@ -70,7 +70,7 @@ def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | N
                 if rc != 0:
                     raise RuntimeError(f"nvcc failed on {os.path.basename(src)}")
     if jobs or not os.path.exists(LIB) or os.path.getmtime(LIB) < _newest(objs):
-        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcuda"]
+        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             sys.stderr.write(r.stdout + r.stderr)

@@ -147,13 +147,18 @@ def flash_attn_q8_0(query: torch.Tensor, key_cache: torch.Tensor, value_cache: t
 def flash_decode_ragged(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: torch.Tensor, num_kv_heads: int,
                         max_seqlen: int | None = None, scale: float | None = None,
                         out: torch.Tensor | None = None) -> torch.Tensor:
-    """Ragged GQA decode: q fp16 [B, Hq, D]; k, v q8_0 bytes of [T, Hkv, D];
-    cu_seqlens int32 [B+1] (device). Returns fp16 [B, Hq, D]."""
+    """Ragged GQA decode: q fp16 [B, Hq, D]; k, v q8_0 bytes of [T, Hkv, D]
+    (T cache rows); cu_seqlens int32 [B+1] (device). Returns fp16 [B, Hq, D]."""
     _cuda(q, "q", torch.float16)
     B, Hq, D = q.shape
     _cuda(cu_seqlens, "cu_seqlens", torch.int32, B + 1)
     _cuda(k, "k")
     _cuda(v, "v")
+    row_bytes = num_kv_heads * (D // 32) * 34
+    nbytes = k.numel() * k.element_size()
+    if nbytes % row_bytes or v.numel() * v.element_size() != nbytes:
+        raise ValueError("k/v must hold whole cache rows of num_kv_heads * D/32 q8_0 blocks")
+    total_rows = nbytes // row_bytes
     if max_seqlen is None:
         max_seqlen = int((cu_seqlens[1:] - cu_seqlens[:-1]).max().item()) if B else 0
     if scale is None:
@@ -161,7 +166,8 @@ def flash_decode_ragged(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_se
     if out is None:
         out = torch.empty_like(q)
     check(lib().kq_fa_decode_q8_0_ragged(q.data_ptr(), k.data_ptr(), v.data_ptr(), cu_seqlens.data_ptr(), B, Hq,
-                                         num_kv_heads, D, int(max_seqlen), float(scale), out.data_ptr(), _stream(q)),
+                                         num_kv_heads, D, int(max_seqlen), int(total_rows), float(scale),
+                                         out.data_ptr(), _stream(q)),
           "kq_fa_decode_q8_0_ragged")
     return out
 

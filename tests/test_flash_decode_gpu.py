@@ -31,7 +31,10 @@ def test_golden_fixture(cuda):
 
 
 @pytest.mark.parametrize("B,S,H,D", [(1, 512, 32, 128), (8, 1000, 4, 128), (3, 4096, 2, 64), (2, 1, 3, 32),
-                                     (16, 300, 2, 256)])
+                                     (16, 300, 2, 256),
+                                     # TMA fast path (D = 128, heads in groups of 8): partial tiles,
+                                     # partial query groups, one-token cache
+                                     (5, 77, 8, 128), (12, 1000, 16, 128), (3, 1, 8, 128), (4, 33, 32, 128)])
 def test_mha_parity(cuda, B, S, H, D):
     import kq
     rng = np.random.default_rng(B * S + H)
@@ -87,6 +90,11 @@ def _ragged_case(rng, lens, Hq, Hkv, D):
     ([1, 2, 300, 257], 8, 8, 64),
     ([500, 0, 77], 16, 2, 128),        # an empty sequence
     ([4096] * 4, 32, 4, 128),
+    # TMA fast path (Hkv = 8, D = 128): g = 4, 2, 1; empty and one-token sequences
+    ([100, 33, 1, 0, 257], 32, 8, 128),
+    ([7, 4097, 64], 16, 8, 128),
+    ([31, 32, 33], 8, 8, 128),
+    ([2000, 5], 32, 16, 128),
 ])
 def test_ragged_parity(cuda, lens, Hq, Hkv, D):
     import kq
