@@ -14,7 +14,7 @@
 // boxes into a double-buffered ring; each of 8 compute warps owns one KV head
 // and its queries, lanes own 4 head dims. Scores are partial dot products
 // reduced with a transpose-halving warp reduction (8 tokens x 4 queries per
-// step); q8_0 bytes become fp32 exactly through a sign-extending byte permute
+// step); q8_0 bytes become fp32 exactly through a signed bit-field extract
 // and the 1.5 * 2^23 bias (x = fma(f, d, -12582912 d)), no conversion op.
 //
 // Generic path: pass 1 gives every (KV stream, token chunk, query group) to one
@@ -225,14 +225,18 @@ __device__ __forceinline__ float warp_reduce32_transpose(float (&v)[32], int lan
   return v[0];
 }
 
+// Signed byte i of w as int32 (bit-field extract with sign extension).
+__device__ __forceinline__ int sbyte(uint32_t w, int i) {
+  int r;
+  asm("bfe.s32 %0, %1, %2, 8;" : "=r"(r) : "r"(w), "r"(8 * i));
+  return r;
+}
+
 // 4 signed bytes of w -> fp32 values d * byte (exact before the final rounding).
 __device__ __forceinline__ void dequant4(uint32_t w, float d, float (&o)[4]) {
   const float nc = -12582912.0f * d;  // exact: fp16 d times 1.5 * 2^23
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int k = (int)__byte_perm(w, 0u, (unsigned)(i | ((8 | i) << 4) | ((8 | i) << 8) | ((8 | i) << 12)));
-    o[i] = fmaf(__int_as_float(k + 0x4B400000), d, nc);
-  }
+  for (int i = 0; i < 4; ++i) o[i] = fmaf(__int_as_float(sbyte(w, i) + 0x4B400000), d, nc);
 }
 
 // Read the 4 code bytes (head dims 4l..4l+3) and the block scale of one token
