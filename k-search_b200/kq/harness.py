@@ -1,0 +1,56 @@
+"""Mirror of the KernelEvalPlus operator interface for this path.
+
+``quant_gemm_forward`` and ``flash_attention_forward`` have the signatures of
+the ``module.forward`` the harness calls
+(kernelevalplus-main/llm_kernel_test/op_test_handler.py:251-256 and :565-579);
+``quant_gemm_test_configs`` / ``*_performance`` restate the harness's test
+configurations and FLOP accounting (op_test_handler.py:258-266, :449-458,
+:581-596) so runs here report the same numbers the harness would.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import ops
+
+# definition dtype -> weight type; activation dtype "float32" = on-the-fly q8_1
+_WEIGHT = {"block_q4_0": "q4_0", "q4_0": "q4_0", "block_q4_1": "q4_1", "q4_1": "q4_1",
+           "block_q8_0": "q8_0", "q8_0": "q8_0"}
+
+
+def quant_gemm_forward(weight: torch.Tensor, activation: torch.Tensor, M: int, N: int, K: int,
+                       weight_dtype: str = "block_q4_0", activation_dtype: str = "float32") -> torch.Tensor:
+    """forward(weight, activation, M, N, K) -> fp32 [M, N] (op_test_handler.py:251-256).
+    fp32 activations use the per-definition W4A32C8 semantics (fp32 block
+    scale and sum); ``block_q8_1`` activations are pre-quantised bytes."""
+    wt = _WEIGHT[weight_dtype]
+    if activation_dtype in ("float32", "fp32"):
+        return ops.gemm_f32act(weight, activation, M, N, K, wt, "f32")
+    if activation_dtype in ("q8_1", "block_q8_1"):
+        return ops.mul_mat_q(weight, activation, M, N, K, wt)
+    raise ValueError(f"unsupported activation dtype {activation_dtype!r}")
+
+
+def flash_attention_forward(query: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
+                            batch_size: int, seq_len: int, num_heads: int, head_dim: int) -> torch.Tensor:
+    """forward(q, k, v, B, S, H, D) -> fp32 [B, H, D] for q8_0 caches (op_test_handler.py:565-579)."""
+    return ops.flash_attn_q8_0(query, key_cache, value_cache, batch_size, seq_len, num_heads, head_dim)
+
+
+def quant_gemm_test_configs(N: int, K: int) -> list[dict]:
+    """The harness's fixed configurations (op_test_handler.py:449-458)."""
+    return [{"M": 1, "N": N, "K": K, "name": "single_token"},
+            {"M": 8, "N": N, "K": K, "name": "small_batch"},
+            {"M": 512, "N": N, "K": K, "name": "large_batch"}]
+
+
+def quant_gemm_performance(latency_ms: float, M: int, N: int, K: int) -> dict:
+    """TFLOPS as the harness reports them: 2 M N K / latency (op_test_handler.py:258-266)."""
+    flops = 2 * M * N * K / (latency_ms / 1000)
+    return {"tflops": round(flops / 1e12, 3), "gflops": round(flops / 1e9, 1)}
+
+
+def flash_attention_performance(latency_ms: float, batch_size: int, seq_len: int, num_heads: int,
+                                head_dim: int) -> dict:
+    """4 B H S D / latency (op_test_handler.py:581-596)."""
+    return {"tflops": round(4 * batch_size * num_heads * seq_len * head_dim / (latency_ms / 1000) / 1e12, 3)}

@@ -230,3 +230,21 @@ def test_full_size_config_sampled_rows(cuda, wtype):
     ok, msg = Q.check_close(got[rows], ref)
     assert ok, msg
     assert Q.nmse(got[rows], Q.gemm_dequant_f32(wtype, w, x[rows], len(rows), N, K)) < 0.05
+
+
+def test_harness_mirror(cuda):
+    """kq.harness.quant_gemm_forward has the harness module.forward signature."""
+    import kq
+    rng = np.random.default_rng(31)
+    M, N, K = 8, 256, 1024
+    w = Q.make_q4_1_blocks(rng, N, K)
+    x = _x(rng, M, K)
+    got = kq.harness.quant_gemm_forward(_t(w, cuda).reshape(-1), _t(x, cuda), M, N, K, "block_q4_1", "float32")
+    ok, msg = Q.check_close(got.cpu().numpy(), Q.gemm_f32act("q4_1", w, x, M, N, K, Q.ACT_F32))
+    assert ok, msg
+    a = Q.quantize_q8_1(x)
+    got = kq.harness.quant_gemm_forward(_t(Q.make_q4_0_blocks(rng, N, K), cuda), _t(a, cuda), M, N, K,
+                                        "block_q4_0", "block_q8_1")
+    assert got.shape == (M, N)
+    perf = kq.harness.quant_gemm_performance(0.01, M, N, K)
+    assert perf["tflops"] == round(2 * M * N * K / 1e-5 / 1e12, 3)
