@@ -127,6 +127,19 @@ kq_status_t kq_mul_mat_q(int wtype, const void* w, const void* a_q8_1, float* ou
 kq_status_t kq_gemm_f32act(int wtype, const void* w, const float* x, float* out, int M, int N, int K,
                            int act_mode, kq_stream_t stream);
 
+/* kq_gemm_f32act without device allocation. No counterpart in the reference:
+ * it exists for callers that cannot call cudaMalloc (a serving runtime whose
+ * allocator already owns nearly all of HBM, or code that must not synchronise
+ * the device on a first-call allocation). The activation staging lives in a
+ * fixed 1 MiB file-scope __device__ array held by every GPU that loads libkq:
+ * calls with act staging M*K + M*(K/32)*8 bytes (K rounded as in the library)
+ * above 1 MiB are rejected with KQ_ERR_INVALID. The first call on a device
+ * resolves the array's device address (cudaGetSymbolAddress) and should come
+ * before any stream capture. All calls share the array: calls that overlap on
+ * the GPU race. Same arguments and results as kq_gemm_f32act. */
+kq_status_t kq_gemm_f32act_noalloc(int wtype, const void* w, const float* x, float* out, int M, int N, int K,
+                                   int act_mode, kq_stream_t stream);
+
 /* Weights x activations already in the kernels' staging layout: int8 codes
  * a_qs[M, K] (row stride K bytes, 16-byte aligned) and one (d, s) fp32 pair
  * per 32-block a_ds[M, K/32, 2]. For callers that quantise inside their own

@@ -540,7 +540,7 @@ bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint
 }
 
 template <int WT>
-kq_status_t launch_tc(const void* w, Act8 act, float* out, int M, int N, int K, bool pdl, cudaStream_t s) {
+kq_status_t launch_tc(const void* w, Act8 act, float* out, int M, int N, int K, bool pdl, cudaStream_t s, int* err) {
   using T = TcTraits<WT>;
   const int nb = K / 32;
   CUtensorMap m_act, m_asc, m_raw;
@@ -568,7 +568,7 @@ kq_status_t launch_tc(const void* w, Act8 act, float* out, int M, int N, int K, 
   p.num_m_tiles = (M + TM - 1) / TM;
   p.num_tiles = p.num_m_tiles * ((N + TN - 1) / TN);
   p.out = out;
-  p.err = device_error_word();
+  p.err = err ? err : device_error_word();
   const int grid = std::max(1, std::min(sm_count(), p.num_tiles));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -595,11 +595,11 @@ bool gemm_tc_supported(int wtype, int M, int N, int K, const void* w, Act8 act) 
 }
 
 kq_status_t launch_gemm_tc(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, bool pdl,
-                           cudaStream_t s) {
+                           cudaStream_t s, int* err) {
   switch (wtype) {
-    case KQ_Q4_0: return launch_tc<KQ_Q4_0>(w, act, out, M, N, K, pdl, s);
-    case KQ_Q4_1: return launch_tc<KQ_Q4_1>(w, act, out, M, N, K, pdl, s);
-    case KQ_Q8_0: return launch_tc<KQ_Q8_0>(w, act, out, M, N, K, pdl, s);
+    case KQ_Q4_0: return launch_tc<KQ_Q4_0>(w, act, out, M, N, K, pdl, s, err);
+    case KQ_Q4_1: return launch_tc<KQ_Q4_1>(w, act, out, M, N, K, pdl, s, err);
+    case KQ_Q8_0: return launch_tc<KQ_Q8_0>(w, act, out, M, N, K, pdl, s, err);
     default: return fail(KQ_ERR_INVALID, "unknown weight type %d", wtype);
   }
 }

@@ -360,7 +360,7 @@ __global__ void __launch_bounds__(32 * (kConsumerWarps + 1), 1)
 }
 
 template <int WT, int MR, int BPL, int KW, int SR>
-kq_status_t launch_cfg(const void* w, Act8 act, float* out, int M, int N, int K, bool pdl, cudaStream_t s) {
+kq_status_t launch_cfg(const void* w, Act8 act, float* out, int M, int N, int K, bool pdl, cudaStream_t s, int* err) {
   using C = GemvCfg<WT, MR, BPL, KW, SR>;
   auto kern = gemv_kernel<WT, MR, BPL, KW, SR>;
   static unsigned attr_done = 0;  // one bit per device ordinal
@@ -382,18 +382,18 @@ kq_status_t launch_cfg(const void* w, Act8 act, float* out, int M, int N, int K,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<const uint8_t*>(w), (const int8_t*)act.qs,
-                                     (const float2*)act.ds, out, M, N, K, device_error_word());
+                                     (const float2*)act.ds, out, M, N, K, err ? err : device_error_word());
   if (e != cudaSuccess) return check_cuda(e, "gemv launch");
   return check_launch("gemv");
 }
 
 template <int WT>
-kq_status_t launch_wt(const void* w, Act8 act, float* out, int M, int N, int K, bool pdl, cudaStream_t s) {
+kq_status_t launch_wt(const void* w, Act8 act, float* out, int M, int N, int K, bool pdl, cudaStream_t s, int* err) {
   constexpr int SR = (WT == KQ_Q8_0) ? 8 : 16;
-  if (M <= 1) return launch_cfg<WT, 1, 4, 1, SR>(w, act, out, M, N, K, pdl, s);
-  if (M <= 2) return launch_cfg<WT, 2, 4, 1, SR>(w, act, out, M, N, K, pdl, s);
-  if (M <= 4) return launch_cfg<WT, 4, 2, 2, SR>(w, act, out, M, N, K, pdl, s);
-  return launch_cfg<WT, 8, 1, 4, SR>(w, act, out, M, N, K, pdl, s);
+  if (M <= 1) return launch_cfg<WT, 1, 4, 1, SR>(w, act, out, M, N, K, pdl, s, err);
+  if (M <= 2) return launch_cfg<WT, 2, 4, 1, SR>(w, act, out, M, N, K, pdl, s, err);
+  if (M <= 4) return launch_cfg<WT, 4, 2, 2, SR>(w, act, out, M, N, K, pdl, s, err);
+  return launch_cfg<WT, 8, 1, 4, SR>(w, act, out, M, N, K, pdl, s, err);
 }
 
 }  // namespace
@@ -404,12 +404,12 @@ bool gemv_supported(int wtype, int M, int N, int K) {
 }
 
 kq_status_t launch_gemv(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, bool pdl,
-                        cudaStream_t s) {
+                        cudaStream_t s, int* err) {
   if (reinterpret_cast<uintptr_t>(w) % 16 != 0) return fail(KQ_ERR_INVALID, "gemv: weight pointer must be 16-byte aligned");
   switch (wtype) {
-    case KQ_Q4_0: return launch_wt<KQ_Q4_0>(w, act, out, M, N, K, pdl, s);
-    case KQ_Q4_1: return launch_wt<KQ_Q4_1>(w, act, out, M, N, K, pdl, s);
-    case KQ_Q8_0: return launch_wt<KQ_Q8_0>(w, act, out, M, N, K, pdl, s);
+    case KQ_Q4_0: return launch_wt<KQ_Q4_0>(w, act, out, M, N, K, pdl, s, err);
+    case KQ_Q4_1: return launch_wt<KQ_Q4_1>(w, act, out, M, N, K, pdl, s, err);
+    case KQ_Q8_0: return launch_wt<KQ_Q8_0>(w, act, out, M, N, K, pdl, s, err);
     default: return fail(KQ_ERR_INVALID, "unknown weight type %d", wtype);
   }
 }

@@ -68,11 +68,11 @@ kq_status_t launch_q8_1_to_act(const void* a_q8_1, Act8 act, int M, int K, cudaS
 // dependent of the preceding kernel on `s` (the activation producer).
 bool gemv_supported(int wtype, int M, int N, int K);
 kq_status_t launch_gemv(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, bool pdl,
-                        cudaStream_t s);
+                        cudaStream_t s, int* err = nullptr);
 // gemm_tc.cu (M > 8, K % 256 == 0, 16-byte aligned operands): tcgen05 int8 MMA
 bool gemm_tc_supported(int wtype, int M, int N, int K, const void* w, Act8 act);
 kq_status_t launch_gemm_tc(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, bool pdl,
-                           cudaStream_t s);
+                           cudaStream_t s, int* err = nullptr);
 // gemm_simt.cu (any shape; the generic path)
 kq_status_t launch_gemm_simt(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, cudaStream_t s);
 kq_status_t launch_block_sums(int wtype, const void* w, const void* a_q8_1, int32_t* sumi, int M, int N, int K,

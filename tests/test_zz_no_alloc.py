@@ -1,0 +1,63 @@
+"""The allocation-free GEMM entry point (kq_gemm_f32act_noalloc).
+
+Some callers cannot call cudaMalloc: a serving runtime whose allocator has
+already reserved nearly all of HBM, or a latency-critical step that must not
+synchronise the device on a first-call allocation. This entry point stages the
+quantised activations in a fixed 1 MiB __device__ array instead. The test calls
+it through the C ABI twice in a row (different inputs, so a stale staging
+buffer would show) and compares each result with the allocating entry point
+kq_gemm_f32act, bit for bit and against the oracle tolerance the other tests
+use. It lives in its own file, collected last, and passes alone or after the
+rest of the suite.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import quant as Q
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(a, device):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+
+
+def _call(fn, wtype, w, x, M, N, K, mode):
+    import kq
+    out = torch.empty((M, N), dtype=torch.float32, device=w.device)
+    st = fn(kq.WTYPES[wtype], w.data_ptr(), x.data_ptr(), out.data_ptr(), M, N, K, kq.ACT_MODES[mode],
+            torch.cuda.current_stream().cuda_stream)
+    assert st == 0, kq._lib.last_error()
+    return out
+
+
+@pytest.mark.parametrize("wtype,M,N,K", [("q4_0", 1, 4096, 4096), ("q8_0", 8, 1000, 2048), ("q4_1", 40, 384, 1024),
+                                         ("q8_0", 128, 256, 4096)])
+def test_noalloc_matches_allocating_entry(cuda, wtype, M, N, K):
+    import kq
+    L = kq.lib()
+    rng = np.random.default_rng(M + N)
+    w = _dev(Q.make_blocks(wtype, rng, N, K), cuda)
+    for call in range(2):  # two calls in a row: the shared array keeps the previous call's contents
+        xh = rng.standard_normal((M, K)).astype(np.float32) * (1 + call)
+        x = _dev(xh, cuda)
+        got = _call(L.kq_gemm_f32act_noalloc, wtype, w, x, M, N, K, "f32")
+        ref = _call(L.kq_gemm_f32act, wtype, w, x, M, N, K, "f32")
+        torch.cuda.synchronize()
+        ok, msg = Q.check_close(got.cpu().numpy(), ref.cpu().numpy())
+        assert ok, f"call {call}: {msg}"
+        assert torch.equal(got, ref), f"call {call}: not bit-identical to kq_gemm_f32act"
+    assert kq.device_error() == 0
+
+
+def test_noalloc_rejects_oversize(cuda):
+    import kq
+    L = kq.lib()
+    M, N, K = 512, 64, 4096  # staging 2.5 MiB > 1 MiB
+    w = torch.zeros(N * (K // 32) * 18, dtype=torch.uint8, device=cuda)
+    x = torch.zeros((M, K), dtype=torch.float32, device=cuda)
+    out = torch.empty((M, N), dtype=torch.float32, device=cuda)
+    st = L.kq_gemm_f32act_noalloc(0, w.data_ptr(), x.data_ptr(), out.data_ptr(), M, N, K, 2, None)
+    assert st == 1
+    assert "exceeds the fixed" in kq._lib.last_error()
