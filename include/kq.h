@@ -147,6 +147,20 @@ kq_status_t kq_gemm_f32act_noalloc(int wtype, const void* w, const float* x, flo
 kq_status_t kq_mul_mat_q8x(int wtype, const void* w, const int8_t* a_qs, const float* a_ds, float* out, int M, int N,
                            int K, kq_stream_t stream);
 
+/* Grouped q4_0 MoE expert FFN (benchmark configuration 4). x fp32 [T, H];
+ * router_logits fp32 [T, E]; per expert, contiguous q4_0 weights: w_gate and
+ * w_up [E][I rows][H/32 blocks], w_down [E][H rows][I/32 blocks]. Routing:
+ * softmax over E, top-k (ties -> lower expert index), weights renormalised
+ * over the k chosen. Per expert: h = silu(x Wg^T) * (x Wu^T), y = h Wd^T, with
+ * activations quantised (act_mode) before each GEMM; out fp32 [T, H] =
+ * sum_k w[t,k] y_k[t]. No grouped MoE operator exists in the reference; each
+ * expert GEMM is the W4A32C8 operator
+ * (definitions/quant_gemm/mixtral8x7b/w4a32c8_q4_0_fp32_int8_mixtral8x7b_moe_up_n14336_k4096.json).
+ * Reads the per-expert token counts back to the host once per call. */
+kq_status_t kq_moe_q4_0(const float* x, const float* router_logits, const void* w_gate, const void* w_up,
+                       const void* w_down, int E, int topk, int T, int H, int I, int act_mode, float* out,
+                       kq_stream_t stream);
+
 /* Debug / parity: int32 sumi[m, n, b] = sum_i q_w[n, b, i] * q_a[m, b, i] with
  * q_w the stored code (0..15 for q4_0/q4_1, int8 for q8_0), as the reference
  * forms it (gemm_ref.py:146, gemm_reference.h:200-211). */

@@ -137,6 +137,14 @@ kq_status_t dispatch_gemm(int wtype, const void* w, Act8 act, float* out, int M,
   return launch_gemm_simt(wtype, w, act, out, M, N, K, s);
 }
 
+}  // namespace
+
+kq_status_t gemm_any(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, cudaStream_t s) {
+  return dispatch_gemm(wtype, w, act, out, M, N, K, s, false);
+}
+
+namespace {
+
 kq_status_t zero_output(float* out, int M, int N, cudaStream_t s) {
   if ((long long)M * N == 0) return KQ_OK;
   return check_cuda(cudaMemsetAsync(out, 0, sizeof(float) * (size_t)M * N, s), "zero output");
@@ -230,6 +238,18 @@ kq_status_t kq_mul_mat_q8x(int wtype, const void* w, const int8_t* a_qs, const f
     return fail(KQ_ERR_INVALID, "staged activations: codes must be 16-byte and scales 8-byte aligned");
   Act8 act{const_cast<int8_t*>(a_qs), reinterpret_cast<float2*>(const_cast<float*>(a_ds))};
   return dispatch_gemm(wtype, w, act, out, M, N, K, s, false);
+}
+
+kq_status_t kq_moe_q4_0(const float* x, const float* router_logits, const void* w_gate, const void* w_up,
+                       const void* w_down, int E, int topk, int T, int H, int I, int act_mode, float* out,
+                       kq_stream_t stream) {
+  if (T < 0 || H <= 0 || I <= 0 || H % 32 || I % 32) return fail(KQ_ERR_INVALID, "moe: bad shape T=%d H=%d I=%d", T, H, I);
+  if (act_mode < KQ_ACT_SUM_X || act_mode > KQ_ACT_F32) return fail(KQ_ERR_INVALID, "unknown activation mode %d", act_mode);
+  if (T == 0) return KQ_OK;
+  if (!x || !router_logits || !w_gate || !w_up || !w_down || !out) return fail(KQ_ERR_INVALID, "moe: null pointer");
+  if (!aligned(x, 16) || !aligned(out, 16)) return fail(KQ_ERR_INVALID, "moe: x and out must be 16-byte aligned");
+  return launch_moe_q4_0(x, router_logits, w_gate, w_up, w_down, E, topk, T, H, I, act_mode, out,
+                         static_cast<cudaStream_t>(stream));
 }
 
 kq_status_t kq_block_sums_i32(int wtype, const void* w, const void* a_q8_1, int32_t* sumi, int M, int N, int K,

@@ -64,6 +64,12 @@ kq_status_t launch_quantize_act(const float* x, Act8 act, int M, int K, int mode
 kq_status_t launch_quantize_q8_1_bytes(const float* x, void* y, int64_t M, int64_t K, int mode, cudaStream_t s);
 kq_status_t launch_quantize_rows(int wtype, const float* x, void* y, int64_t rows, int64_t K, cudaStream_t s);
 kq_status_t launch_q8_1_to_act(const void* a_q8_1, Act8 act, int M, int K, cudaStream_t s);
+// staging row r <- quantise(x row rowmap[r] / div)
+kq_status_t launch_quantize_act_gather(const float* x, const int* rowmap, int div, Act8 act, int M, int K, int mode,
+                                       cudaStream_t s);
+// staging <- quantise(silu(gate) * up), gate/up fp32 [M, K]
+kq_status_t launch_silu_mul_quantize(const float* gate, const float* up, Act8 act, int M, int K, int mode,
+                                     cudaStream_t s);
 // gemv.cu (M <= 8, K % 256 == 0); `pdl` = launched as a programmatic
 // dependent of the preceding kernel on `s` (the activation producer).
 bool gemv_supported(int wtype, int M, int N, int K);
@@ -75,6 +81,13 @@ kq_status_t launch_gemm_tc(int wtype, const void* w, Act8 act, float* out, int M
                            cudaStream_t s, int* err = nullptr);
 // gemm_simt.cu (any shape; the generic path)
 kq_status_t launch_gemm_simt(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, cudaStream_t s);
+// any shape: GEMV (M <= 8), tcgen05 GEMM, else the generic kernel (no PDL)
+kq_status_t gemm_any(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, cudaStream_t s);
+// moe.cu
+size_t moe_workspace_bytes(int T, int E, int topk, int H, int I);
+kq_status_t launch_moe_q4_0(const float* x, const float* logits, const void* w_gate, const void* w_up,
+                            const void* w_down, int E, int topk, int T, int H, int I, int act_mode, float* out,
+                            cudaStream_t s);
 kq_status_t launch_block_sums(int wtype, const void* w, const void* a_q8_1, int32_t* sumi, int M, int N, int K,
                               cudaStream_t s);
 // fa_decode.cu

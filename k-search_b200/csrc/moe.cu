@@ -1,0 +1,227 @@
+// Grouped q4_0 MoE expert FFN (benchmark configuration 4):
+//
+//   route:   p = softmax(logits[t, :]), top-k experts (ties -> lower index),
+//            weights renormalised over the k chosen
+//   per expert e and its routed tokens X_e:
+//            h = silu(X_e W_gate[e]^T) * (X_e W_up[e]^T)      (activations q8_1-quantised)
+//            y = h W_down[e]^T                               (h q8_1-quantised)
+//   combine: out[t] = sum_k w[t, k] * y[pair(t, k)]          (fixed slot order)
+//
+// The reference has no grouped MoE operator; each expert GEMM is the
+// per-definition W4A32C8 operator (e.g. definitions/quant_gemm/mixtral8x7b/
+// w4a32c8_q4_0_fp32_int8_mixtral8x7b_moe_up_n14336_k4096.json), and SiLU
+// follows kernels/activation/silu.cuh:97 (silu(g) * u).
+//
+// Pipeline (all on one stream): route_kernel -> expert_rank_kernel (a stable
+// counting sort of (token, slot) pairs by expert) -> gather_quantize (routed
+// rows of x into the GEMM staging layout, expert-contiguous) -> per-expert
+// gate / up GEMMs (tcgen05 / GEMV / generic by size, on row ranges of the
+// shared staging) -> silu_mul_quantize (h straight into staging) -> per-expert
+// down GEMMs -> combine_kernel. Expert row counts come back to the host once
+// per call to size the per-expert launches.
+#include <algorithm>
+#include <cmath>
+
+#include "kq_internal.h"
+#include "kq_device.cuh"
+
+namespace kq {
+namespace {
+
+constexpr int kMaxExperts = 64;
+constexpr int kMaxTopk = 8;
+
+// One thread per token: softmax over E logits, top-k, renormalised weights.
+__global__ void route_kernel(const float* __restrict__ logits, int T, int E, int topk, int* __restrict__ idx,
+                             float* __restrict__ wts, int* __restrict__ counts) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  const float* l = logits + (size_t)t * E;
+  float mx = -INFINITY;
+  for (int e = 0; e < E; ++e) mx = fmaxf(mx, l[e]);
+  float den = 0.0f;
+  for (int e = 0; e < E; ++e) den += expf(l[e] - mx);
+  int chosen[kMaxTopk];
+  float pw[kMaxTopk];
+  float tot = 0.0f;
+  for (int k = 0; k < topk; ++k) {
+    int best = -1;
+    float bv = -INFINITY;
+    for (int e = 0; e < E; ++e) {
+      bool used = false;
+      for (int q = 0; q < k; ++q) used |= (chosen[q] == e);
+      if (!used && (best < 0 || l[e] > bv)) {
+        best = e;
+        bv = l[e];
+      }
+    }
+    chosen[k] = best;
+    pw[k] = expf(bv - mx) / den;
+    tot += pw[k];
+  }
+  for (int k = 0; k < topk; ++k) {
+    idx[(size_t)t * topk + k] = chosen[k];
+    wts[(size_t)t * topk + k] = pw[k] / tot;
+    atomicAdd(&counts[chosen[k]], 1);
+  }
+}
+
+// Block e lists the pairs routed to expert e in (token, slot) order: a stable
+// counting sort. row_of_pair[t * topk + k] = row of that pair in the grouped
+// layout; pair_of_row[row] = t * topk + k.
+__global__ void __launch_bounds__(1024) expert_rank_kernel(const int* __restrict__ idx, const int* __restrict__ counts,
+                                                           int P, int E, int* __restrict__ row_of_pair,
+                                                           int* __restrict__ pair_of_row) {
+  const int e = blockIdx.x;
+  __shared__ int base;
+  __shared__ int warp_tot[32];
+  if (threadIdx.x == 0) {
+    int b = 0;
+    for (int q = 0; q < e; ++q) b += counts[q];
+    base = b;
+  }
+  __syncthreads();
+  int running = base;
+  for (int c0 = 0; c0 < P; c0 += blockDim.x) {
+    const int i = c0 + threadIdx.x;
+    const int flag = (i < P && idx[i] == e) ? 1 : 0;
+    // block-wide exclusive scan of flags
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    int v = flag;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += n;
+    }
+    if (lane == 31) warp_tot[wid] = v;
+    __syncthreads();
+    if (wid == 0) {
+      int w = (lane < (int)(blockDim.x >> 5)) ? warp_tot[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += n;
+      }
+      warp_tot[lane] = w;  // inclusive prefix over warps
+    }
+    __syncthreads();
+    const int before = (wid > 0 ? warp_tot[wid - 1] : 0) + v - flag;
+    if (flag) {
+      const int row = running + before;
+      row_of_pair[i] = row;
+      pair_of_row[row] = i;
+    }
+    const int chunk_total = warp_tot[(blockDim.x >> 5) - 1];
+    __syncthreads();
+    running += chunk_total;
+  }
+}
+
+// y[t] = sum_k w[t,k] * Y[row_of_pair[t*topk+k]]   (fp32, fixed slot order)
+__global__ void combine_kernel(const float* __restrict__ Y, const int* __restrict__ row_of_pair,
+                               const float* __restrict__ wts, int T, int topk, int H, float* __restrict__ out) {
+  const int t = blockIdx.x;
+  for (int h = threadIdx.x * 4; h < H; h += blockDim.x * 4) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < topk; ++k) {
+      const float w = wts[(size_t)t * topk + k];
+      const float4 y = *reinterpret_cast<const float4*>(Y + (size_t)row_of_pair[(size_t)t * topk + k] * H + h);
+      acc.x = fmaf(w, y.x, acc.x);
+      acc.y = fmaf(w, y.y, acc.y);
+      acc.z = fmaf(w, y.z, acc.z);
+      acc.w = fmaf(w, y.w, acc.w);
+    }
+    *reinterpret_cast<float4*>(out + (size_t)t * H + h) = acc;
+  }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+size_t moe_workspace_bytes(int T, int E, int topk, int H, int I) {
+  const size_t P = (size_t)T * topk;
+  size_t b = 0;
+  auto add = [&](size_t n) { b += (n + 255) & ~(size_t)255; };
+  add(E * sizeof(int));                 // counts
+  add(P * sizeof(int));                 // idx
+  add(P * sizeof(float));               // wts
+  add(P * sizeof(int));                 // row_of_pair
+  add(P * sizeof(int));                 // pair_of_row
+  add(act8_bytes((int)P, H));           // staged x rows
+  add(P * (size_t)I * sizeof(float));   // gate
+  add(P * (size_t)I * sizeof(float));   // up
+  add(act8_bytes((int)P, I));           // staged h
+  add(P * (size_t)H * sizeof(float));   // y
+  return b;
+}
+
+kq_status_t launch_moe_q4_0(const float* x, const float* logits, const void* w_gate, const void* w_up,
+                            const void* w_down, int E, int topk, int T, int H, int I, int act_mode, float* out,
+                            cudaStream_t s) {
+  if (E < 1 || E > kMaxExperts || topk < 1 || topk > kMaxTopk || topk > E)
+    return fail(KQ_ERR_INVALID, "moe: unsupported E=%d topk=%d", E, topk);
+  if (H % 32 || I % 32 || H % 4) return fail(KQ_ERR_INVALID, "moe: H and I must be multiples of 32");
+  const int P = T * topk;
+  uint8_t* ws = static_cast<uint8_t*>(workspace(WS_MOE, moe_workspace_bytes(T, E, topk, H, I)));
+  if (!ws) return KQ_ERR_NOMEM;
+  size_t off = 0;
+  auto take = [&](size_t n) {
+    uint8_t* p = ws + off;
+    off += (n + 255) & ~(size_t)255;
+    return p;
+  };
+  int* counts = reinterpret_cast<int*>(take(E * sizeof(int)));
+  int* idx = reinterpret_cast<int*>(take((size_t)P * sizeof(int)));
+  float* wts = reinterpret_cast<float*>(take((size_t)P * sizeof(float)));
+  int* row_of_pair = reinterpret_cast<int*>(take((size_t)P * sizeof(int)));
+  int* pair_of_row = reinterpret_cast<int*>(take((size_t)P * sizeof(int)));
+  Act8 ax = act8_view(take(act8_bytes(P, H)), P, H);
+  float* G = reinterpret_cast<float*>(take((size_t)P * I * sizeof(float)));
+  float* U = reinterpret_cast<float*>(take((size_t)P * I * sizeof(float)));
+  Act8 ah = act8_view(take(act8_bytes(P, I)), P, I);
+  float* Y = reinterpret_cast<float*>(take((size_t)P * H * sizeof(float)));
+
+  kq_status_t st = check_cuda(cudaMemsetAsync(counts, 0, E * sizeof(int), s), "moe counts");
+  if (st) return st;
+  route_kernel<<<(T + 127) / 128, 128, 0, s>>>(logits, T, E, topk, idx, wts, counts);
+  if ((st = check_launch("moe route"))) return st;
+  expert_rank_kernel<<<E, 1024, 0, s>>>(idx, counts, P, E, row_of_pair, pair_of_row);
+  if ((st = check_launch("moe rank"))) return st;
+  int hc[kMaxExperts];
+  if ((st = check_cuda(cudaMemcpyAsync(hc, counts, E * sizeof(int), cudaMemcpyDeviceToHost, s), "moe counts d2h")))
+    return st;
+  if ((st = check_cuda(cudaStreamSynchronize(s), "moe counts sync"))) return st;
+  if ((st = launch_quantize_act_gather(x, pair_of_row, topk, ax, P, H, act_mode, s))) return st;
+
+  const size_t gate_bytes = (size_t)I * (H / 32) * 18, down_bytes = (size_t)H * (I / 32) * 18;
+  auto rows = [](Act8 a, int r0, int K) { return Act8{a.qs + (size_t)r0 * K, a.ds + (size_t)r0 * (K / 32)}; };
+  int r0 = 0;
+  for (int e = 0; e < E; ++e) {
+    const int m = hc[e];
+    if (m > 0) {
+      const Act8 a = rows(ax, r0, H);
+      if ((st = gemm_any(KQ_Q4_0, static_cast<const uint8_t*>(w_gate) + e * gate_bytes, a, G + (size_t)r0 * I, m, I,
+                         H, s)))
+        return st;
+      if ((st = gemm_any(KQ_Q4_0, static_cast<const uint8_t*>(w_up) + e * gate_bytes, a, U + (size_t)r0 * I, m, I, H,
+                         s)))
+        return st;
+    }
+    r0 += m;
+  }
+  if ((st = launch_silu_mul_quantize(G, U, ah, P, I, act_mode, s))) return st;
+  r0 = 0;
+  for (int e = 0; e < E; ++e) {
+    const int m = hc[e];
+    if (m > 0) {
+      if ((st = gemm_any(KQ_Q4_0, static_cast<const uint8_t*>(w_down) + e * down_bytes, rows(ah, r0, I),
+                         Y + (size_t)r0 * H, m, H, I, s)))
+        return st;
+    }
+    r0 += m;
+  }
+  combine_kernel<<<T, 256, 0, s>>>(Y, row_of_pair, wts, T, topk, H, out);
+  return check_launch("moe combine");
+}
+
+}  // namespace kq

@@ -78,11 +78,38 @@ __device__ __forceinline__ BlockQ quantize_octet(float4 v, int lane) {
   return r;
 }
 
+// Where a block's 32 input values come from.
+enum Src : int {
+  SRC_X = 0,       // x[blk * 32 ..]
+  SRC_GATHER = 1,  // row r of the output reads row rowmap[r] / div of x (K values per row)
+  SRC_SILU = 2,    // silu(x[..]) * y[..] (x = gate, y = up), same indexing as SRC_X
+};
+
+template <int SRC>
+__device__ __forceinline__ float4 load_octet(const float* __restrict__ x, const float* __restrict__ y,
+                                             const int* __restrict__ rowmap, int div, int nb, long long blk,
+                                             int sub) {
+  if constexpr (SRC == SRC_GATHER) {
+    const long long r = blk / nb, b = blk % nb;
+    const long long src = (long long)(rowmap[r] / div) * nb + b;
+    return __ldg(reinterpret_cast<const float4*>(x + src * 32) + sub);
+  } else if constexpr (SRC == SRC_SILU) {
+    const float4 g = __ldg(reinterpret_cast<const float4*>(x + blk * 32) + sub);
+    const float4 u = __ldg(reinterpret_cast<const float4*>(y + blk * 32) + sub);
+    auto f = [](float gv, float uv) { return gv / (1.0f + expf(-gv)) * uv; };
+    return make_float4(f(g.x, u.x), f(g.y, u.y), f(g.z, u.z), f(g.w, u.w));
+  } else {
+    return __ldg(reinterpret_cast<const float4*>(x + blk * 32) + sub);
+  }
+}
+
 // One warp quantises 4 consecutive blocks per step (grid-stride).
-template <int MODE, bool BYTES>
+template <int MODE, bool BYTES, int SRC = SRC_X>
 __global__ void __launch_bounds__(256) quantize_kernel(const float* __restrict__ x, int8_t* __restrict__ qs,
                                                        float2* __restrict__ ds, uint8_t* __restrict__ q81,
-                                                       long long total_blocks) {
+                                                       long long total_blocks, const float* __restrict__ y = nullptr,
+                                                       const int* __restrict__ rowmap = nullptr, int div = 1,
+                                                       int nb = 1) {
   const int lane = threadIdx.x & 31;
   const int grp = lane >> 3;
   const int sub = lane & 7;
@@ -92,7 +119,7 @@ __global__ void __launch_bounds__(256) quantize_kernel(const float* __restrict__
     const long long blk = b0 + grp;
     const bool valid = blk < total_blocks;
     const long long src = valid ? blk : b0;  // keep all lanes in the shuffles
-    const float4 v = __ldg(reinterpret_cast<const float4*>(x + src * 32) + sub);
+    const float4 v = load_octet<SRC>(x, y, rowmap, div, nb, src, sub);
     const BlockQ r = quantize_octet<MODE>(v, lane);
     if (!valid) continue;
     if (BYTES) {
@@ -251,6 +278,39 @@ kq_status_t launch_quantize_rows(int wtype, const float* x, void* y, int64_t row
     default: return fail(KQ_ERR_INVALID, "unknown weight type %d", wtype);
   }
   return check_launch("quantize_rows");
+}
+
+template <int SRC>
+kq_status_t launch_staging(const float* x, const float* y, const int* rowmap, int div, Act8 act, int M, int K, int mode,
+                           cudaStream_t s) {
+  const long long nb = (long long)M * (K / 32);
+  if (nb == 0) return KQ_OK;
+  const int grid = grid_for(nb);
+  const int nbr = K / 32;
+  switch (mode) {
+    case KQ_ACT_SUM_X:
+      quantize_kernel<KQ_ACT_SUM_X, false, SRC><<<grid, 256, 0, s>>>(x, act.qs, act.ds, nullptr, nb, y, rowmap, div, nbr);
+      break;
+    case KQ_ACT_SUM_DQ:
+      quantize_kernel<KQ_ACT_SUM_DQ, false, SRC><<<grid, 256, 0, s>>>(x, act.qs, act.ds, nullptr, nb, y, rowmap, div, nbr);
+      break;
+    case KQ_ACT_F32:
+      quantize_kernel<KQ_ACT_F32, false, SRC><<<grid, 256, 0, s>>>(x, act.qs, act.ds, nullptr, nb, y, rowmap, div, nbr);
+      break;
+    default:
+      return fail(KQ_ERR_INVALID, "unknown activation mode %d", mode);
+  }
+  return check_launch("quantize_staging");
+}
+
+kq_status_t launch_quantize_act_gather(const float* x, const int* rowmap, int div, Act8 act, int M, int K, int mode,
+                                       cudaStream_t s) {
+  return launch_staging<SRC_GATHER>(x, nullptr, rowmap, div, act, M, K, mode, s);
+}
+
+kq_status_t launch_silu_mul_quantize(const float* gate, const float* up, Act8 act, int M, int K, int mode,
+                                     cudaStream_t s) {
+  return launch_staging<SRC_SILU>(gate, up, nullptr, 1, act, M, K, mode, s);
 }
 
 kq_status_t launch_q8_1_to_act(const void* a_q8_1, Act8 act, int M, int K, cudaStream_t s) {

@@ -116,6 +116,28 @@ def mul_mat_q8x(weight: torch.Tensor, a_qs: torch.Tensor, a_ds: torch.Tensor, M:
     return out
 
 
+def moe_q4_0(x: torch.Tensor, router_logits: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
+             w_down: torch.Tensor, topk: int = 2, act_mode="sum_dq", out: torch.Tensor | None = None) -> torch.Tensor:
+    """Grouped q4_0 MoE FFN: x fp32 [T, H], logits fp32 [T, E]; w_gate / w_up uint8
+    [E, I, H/32, 18], w_down uint8 [E, H, I/32, 18]. Returns fp32 [T, H]."""
+    _cuda(x, "x", torch.float32)
+    T, H = x.shape
+    _cuda(router_logits, "router_logits", torch.float32)
+    E = router_logits.shape[1]
+    _cuda(w_gate, "w_gate", torch.uint8)
+    _cuda(w_up, "w_up", torch.uint8)
+    _cuda(w_down, "w_down", torch.uint8)
+    I = w_gate.numel() // (E * (H // 32) * 18)
+    if w_gate.numel() != E * I * (H // 32) * 18 or w_up.numel() != w_gate.numel() or w_down.numel() != E * H * (I // 32) * 18:
+        raise ValueError("expert weight sizes do not match [E, I, H/32, 18] / [E, H, I/32, 18]")
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.float32, device=x.device)
+    check(lib().kq_moe_q4_0(x.data_ptr(), router_logits.data_ptr(), w_gate.data_ptr(), w_up.data_ptr(),
+                            w_down.data_ptr(), E, topk, T, H, I, _act_mode(act_mode), out.data_ptr(), _stream(x)),
+          "kq_moe_q4_0")
+    return out
+
+
 def block_sums_i32(weight: torch.Tensor, a_q8_1: torch.Tensor, M: int, N: int, K: int, wtype="q4_0") -> torch.Tensor:
     """int32 sumi [M, N, K/32] (the bit-exact parity quantity)."""
     wt = _wtype(wtype)
