@@ -47,6 +47,8 @@ CONFIGS = {
             workload="configs[2]: q4_0 x q8_1 M=1 N=14336 K=4096"),
     3: dict(kind="fa", B=32, Hq=32, Hkv=8, D=128, Lmin=64, Lmax=8192,
             workload="configs[3]: ragged GQA flash decode, q8_0 KV, B=32 Hq=32 Hkv=8 D=128 L~U[64,8192]"),
+    4: dict(kind="moe", T=4096, E=8, topk=2, H=4096, I=14336, act="sum_dq",
+            workload="configs[4]: q4_0 MoE FFN, 8 experts top-2, T=4096 H=4096 I=14336"),
 }
 
 
@@ -430,6 +432,63 @@ def bench_fa(args, cfg, rank, world):
     return line
 
 
+def bench_moe(args, cfg, rank, world):
+    import torch
+    import kq
+    from kq import synth
+
+    T, E, topk, H, I = cfg["T"], cfg["E"], cfg["topk"], cfg["H"], cfg["I"]
+    dev = torch.device("cuda", torch.cuda.current_device())
+    rng = np.random.default_rng(4321 + rank)
+    wg = torch.from_numpy(np.stack([synth.q4_0_blocks(rng, I, H) for _ in range(E)])).to(dev)
+    wu = torch.from_numpy(np.stack([synth.q4_0_blocks(rng, I, H) for _ in range(E)])).to(dev)
+    wd = torch.from_numpy(np.stack([synth.q4_0_blocks(rng, H, I) for _ in range(E)])).to(dev)
+    g = torch.Generator(device="cpu").manual_seed(77 + rank)
+    x = torch.randn((T, H), generator=g).to(dev)
+    logits = torch.randn((T, E), generator=g).to(dev)
+    out = torch.empty((T, H), dtype=torch.float32, device=dev)
+
+    def step(i):
+        kq.moe_q4_0(x, logits, wg, wu, wd, topk, cfg["act"], out=out)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    barrier(world)
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    clk = clocks.stop() if clocks else None
+    ops = 2.0 * (T * topk) * (2 * H * I + I * H)
+    value = world * ops * args.steps / (ms * 1e-3) / 1e12
+    _, bf16, src = load_peaks()
+    line = {
+        "metric": "MoE W4A8 GEMM TOPS (q4_0 x q8_1, grouped)", "value": round(value, 3), "unit": "TOPS",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (seeded; weights drawn directly as q4_0 blocks)",
+        "config": {"workload": cfg["workload"], "T": T, "E": E, "topk": topk, "H": H, "I": I,
+                   "l2": "expert weights 792 MB > L2"},
+        "roofline": {"bound": "tensor", "achieved": round(value / world, 2), "peak": round(2 * bf16, 1),
+                     "unit": "TFLOP/s", "frac": round(value / world / (2 * bf16), 4), "traffic": None,
+                     "kernel": "whole MoE step (route + 24 expert GEMMs + SiLU + combine)",
+                     "peak_source": f"int8 dense = 2 x {src} bf16_tflops"},
+        "gpu_launches": (5 + 3 * E) * args.steps,
+    }
+    if clk is not None:
+        line["clocks"] = clk
+    return line
+
+
 def reference_arm(args, cfg):
     """The reference's CPU implementation of the same operator, all host threads.
     Each step is a bounded sample of the workload (a slice of activation rows)
@@ -481,6 +540,9 @@ def main():
     if cfg["kind"] == "fa":
         line = bench_fa(args, cfg, rank, world)
         cpu = (lambda: cpu_fa_baseline(cfg)) if (rank == 0 and world == 1) else None
+    elif cfg["kind"] == "moe":
+        line = bench_moe(args, cfg, rank, world)
+        cpu = None
     else:
         line = bench_gemm(args, cfg, rank, world)
         cpu = (lambda: cpu_gemm_baseline(cfg)) if (rank == 0 and world == 1) else None

@@ -161,6 +161,26 @@ kq_status_t kq_moe_q4_0(const float* x, const float* router_logits, const void* 
                        const void* w_down, int E, int topk, int T, int H, int I, int act_mode, float* out,
                        kq_stream_t stream);
 
+/* The three stages of kq_moe_q4_0 as separate calls, for expert parallelism
+ * (routed rows cross ranks between them). No reference counterpart: the
+ * reference has no MoE operator; the math is exactly kq_moe_q4_0's.
+ *
+ * kq_moe_route: idx int32 [T, topk] and wts fp32 [T, topk] from router_logits
+ * fp32 [T, E] (softmax, top-k with ties to the lower index, renormalised). */
+kq_status_t kq_moe_route(const float* router_logits, int T, int E, int topk, int32_t* idx, float* wts,
+                         kq_stream_t stream);
+
+/* Expert FFNs of P routed rows: row p of x_rows fp32 [P, H] goes through
+ * expert expert_of_row[p] (0 <= e < E; int32, device) of this call's weights
+ * (same layout as kq_moe_q4_0); y_rows fp32 [P, H] keeps the row order. Reads
+ * the per-expert row counts back to the host once per call. */
+kq_status_t kq_moe_experts_q4_0(const float* x_rows, const int32_t* expert_of_row, const void* w_gate,
+                                const void* w_up, const void* w_down, int E, int P, int H, int I, int act_mode,
+                                float* y_rows, kq_stream_t stream);
+
+/* out[t] = sum_k wts[t, k] * y[t * topk + k]  (fp32, slots in order k = 0..topk-1). */
+kq_status_t kq_moe_combine(const float* y, const float* wts, int T, int topk, int H, float* out, kq_stream_t stream);
+
 /* Debug / parity: int32 sumi[m, n, b] = sum_i q_w[n, b, i] * q_a[m, b, i] with
  * q_w the stored code (0..15 for q4_0/q4_1, int8 for q8_0), as the reference
  * forms it (gemm_ref.py:146, gemm_reference.h:200-211). */

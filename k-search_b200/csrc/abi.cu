@@ -252,6 +252,35 @@ kq_status_t kq_moe_q4_0(const float* x, const float* router_logits, const void* 
                          static_cast<cudaStream_t>(stream));
 }
 
+kq_status_t kq_moe_route(const float* router_logits, int T, int E, int topk, int32_t* idx, float* wts,
+                         kq_stream_t stream) {
+  if (T < 0) return fail(KQ_ERR_INVALID, "moe route: T=%d", T);
+  if (T == 0) return KQ_OK;
+  if (!router_logits || !idx || !wts) return fail(KQ_ERR_INVALID, "moe route: null pointer");
+  return launch_moe_route(router_logits, T, E, topk, idx, wts, static_cast<cudaStream_t>(stream));
+}
+
+kq_status_t kq_moe_experts_q4_0(const float* x_rows, const int32_t* expert_of_row, const void* w_gate,
+                                const void* w_up, const void* w_down, int E, int P, int H, int I, int act_mode,
+                                float* y_rows, kq_stream_t stream) {
+  if (P < 0 || H <= 0 || I <= 0 || H % 32 || I % 32) return fail(KQ_ERR_INVALID, "moe experts: bad shape P=%d H=%d I=%d", P, H, I);
+  if (act_mode < KQ_ACT_SUM_X || act_mode > KQ_ACT_F32) return fail(KQ_ERR_INVALID, "unknown activation mode %d", act_mode);
+  if (P == 0) return KQ_OK;
+  if (!x_rows || !expert_of_row || !w_gate || !w_up || !w_down || !y_rows)
+    return fail(KQ_ERR_INVALID, "moe experts: null pointer");
+  if (!aligned(x_rows, 16) || !aligned(y_rows, 16)) return fail(KQ_ERR_INVALID, "moe experts: rows must be 16-byte aligned");
+  return launch_moe_experts_q4_0(x_rows, expert_of_row, w_gate, w_up, w_down, E, P, H, I, act_mode, y_rows,
+                                 static_cast<cudaStream_t>(stream));
+}
+
+kq_status_t kq_moe_combine(const float* y, const float* wts, int T, int topk, int H, float* out, kq_stream_t stream) {
+  if (T < 0 || topk < 1 || H <= 0 || H % 4) return fail(KQ_ERR_INVALID, "moe combine: bad shape T=%d topk=%d H=%d", T, topk, H);
+  if (T == 0) return KQ_OK;
+  if (!y || !wts || !out) return fail(KQ_ERR_INVALID, "moe combine: null pointer");
+  if (!aligned(y, 16) || !aligned(out, 16)) return fail(KQ_ERR_INVALID, "moe combine: y and out must be 16-byte aligned");
+  return launch_moe_combine(y, wts, T, topk, H, out, static_cast<cudaStream_t>(stream));
+}
+
 kq_status_t kq_block_sums_i32(int wtype, const void* w, const void* a_q8_1, int32_t* sumi, int M, int N, int K,
                               kq_stream_t stream) {
   if (block_bytes(wtype) == 0) return fail(KQ_ERR_INVALID, "unknown weight type %d", wtype);

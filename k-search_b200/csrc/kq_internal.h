@@ -84,7 +84,12 @@ kq_status_t launch_gemm_simt(int wtype, const void* w, Act8 act, float* out, int
 // any shape: GEMV (M <= 8), tcgen05 GEMM, else the generic kernel (no PDL)
 kq_status_t gemm_any(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, cudaStream_t s);
 // moe.cu
-size_t moe_workspace_bytes(int T, int E, int topk, int H, int I);
+size_t moe_workspace_bytes(int P, int E, int H, int I);
+kq_status_t launch_moe_route(const float* logits, int T, int E, int topk, int* idx, float* wts, cudaStream_t s);
+kq_status_t launch_moe_experts_q4_0(const float* x_rows, const int* expert_of_row, const void* w_gate,
+                                    const void* w_up, const void* w_down, int E, int P, int H, int I, int act_mode,
+                                    float* y_rows, cudaStream_t s);
+kq_status_t launch_moe_combine(const float* y, const float* wts, int T, int topk, int H, float* out, cudaStream_t s);
 kq_status_t launch_moe_q4_0(const float* x, const float* logits, const void* w_gate, const void* w_up,
                             const void* w_down, int E, int topk, int T, int H, int I, int act_mode, float* out,
                             cudaStream_t s);

@@ -117,7 +117,8 @@ __global__ void __launch_bounds__(1024) expert_rank_kernel(const int* __restrict
   }
 }
 
-// y[t] = sum_k w[t,k] * Y[row_of_pair[t*topk+k]]   (fp32, fixed slot order)
+// y[t] = sum_k w[t,k] * Y[row_of_pair[t*topk+k]]   (fp32, fixed slot order;
+// row_of_pair == nullptr: Y is already in (token, slot) order)
 __global__ void combine_kernel(const float* __restrict__ Y, const int* __restrict__ row_of_pair,
                                const float* __restrict__ wts, int T, int topk, int H, float* __restrict__ out) {
   const int t = blockIdx.x;
@@ -125,7 +126,9 @@ __global__ void combine_kernel(const float* __restrict__ Y, const int* __restric
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int k = 0; k < topk; ++k) {
       const float w = wts[(size_t)t * topk + k];
-      const float4 y = *reinterpret_cast<const float4*>(Y + (size_t)row_of_pair[(size_t)t * topk + k] * H + h);
+      const size_t pr = (size_t)t * topk + k;
+      const size_t r = row_of_pair ? (size_t)row_of_pair[pr] : pr;
+      const float4 y = *reinterpret_cast<const float4*>(Y + r * H + h);
       acc.x = fmaf(w, y.x, acc.x);
       acc.y = fmaf(w, y.y, acc.y);
       acc.z = fmaf(w, y.z, acc.z);
@@ -135,92 +138,173 @@ __global__ void combine_kernel(const float* __restrict__ Y, const int* __restric
   }
 }
 
+// Per-row unsort: y[p] = Y[row_of_pair[p]].
+__global__ void unsort_kernel(const float* __restrict__ Y, const int* __restrict__ row_of_pair, int H,
+                              float* __restrict__ y) {
+  const int p = blockIdx.x;
+  const float* src = Y + (size_t)row_of_pair[p] * H;
+  float* dst = y + (size_t)p * H;
+  for (int h = threadIdx.x * 4; h < H; h += blockDim.x * 4)
+    *reinterpret_cast<float4*>(dst + h) = *reinterpret_cast<const float4*>(src + h);
+}
+
+__global__ void count_kernel(const int* __restrict__ expert_of_pair, int P, int* __restrict__ counts) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < P) atomicAdd(&counts[expert_of_pair[i]], 1);
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
-size_t moe_workspace_bytes(int T, int E, int topk, int H, int I) {
-  const size_t P = (size_t)T * topk;
+size_t moe_workspace_bytes(int P, int E, int H, int I) {
   size_t b = 0;
   auto add = [&](size_t n) { b += (n + 255) & ~(size_t)255; };
   add(E * sizeof(int));                 // counts
-  add(P * sizeof(int));                 // idx
-  add(P * sizeof(float));               // wts
-  add(P * sizeof(int));                 // row_of_pair
-  add(P * sizeof(int));                 // pair_of_row
-  add(act8_bytes((int)P, H));           // staged x rows
-  add(P * (size_t)I * sizeof(float));   // gate
-  add(P * (size_t)I * sizeof(float));   // up
-  add(act8_bytes((int)P, I));           // staged h
-  add(P * (size_t)H * sizeof(float));   // y
+  add((size_t)P * sizeof(int));         // idx (routing) / expert of pair
+  add((size_t)P * sizeof(float));       // wts
+  add((size_t)P * sizeof(int));         // row_of_pair
+  add((size_t)P * sizeof(int));         // pair_of_row
+  add(act8_bytes(P, H));                // staged x rows
+  add((size_t)P * I * sizeof(float));   // gate
+  add((size_t)P * I * sizeof(float));   // up
+  add(act8_bytes(P, I));                // staged h
+  add((size_t)P * H * sizeof(float));   // y (grouped)
   return b;
 }
 
-kq_status_t launch_moe_q4_0(const float* x, const float* logits, const void* w_gate, const void* w_up,
-                            const void* w_down, int E, int topk, int T, int H, int I, int act_mode, float* out,
-                            cudaStream_t s) {
-  if (E < 1 || E > kMaxExperts || topk < 1 || topk > kMaxTopk || topk > E)
-    return fail(KQ_ERR_INVALID, "moe: unsupported E=%d topk=%d", E, topk);
-  if (H % 32 || I % 32 || H % 4) return fail(KQ_ERR_INVALID, "moe: H and I must be multiples of 32");
-  const int P = T * topk;
-  uint8_t* ws = static_cast<uint8_t*>(workspace(WS_MOE, moe_workspace_bytes(T, E, topk, H, I)));
-  if (!ws) return KQ_ERR_NOMEM;
+namespace {
+
+struct MoeWs {
+  int* counts;
+  int* idx;
+  float* wts;
+  int* row_of_pair;
+  int* pair_of_row;
+  Act8 ax;
+  float* G;
+  float* U;
+  Act8 ah;
+  float* Y;
+};
+
+bool moe_ws(int P, int E, int H, int I, MoeWs* w) {
+  uint8_t* ws = static_cast<uint8_t*>(workspace(WS_MOE, moe_workspace_bytes(P, E, H, I)));
+  if (!ws) return false;
   size_t off = 0;
   auto take = [&](size_t n) {
-    uint8_t* p = ws + off;
+    uint8_t* q = ws + off;
     off += (n + 255) & ~(size_t)255;
-    return p;
+    return q;
   };
-  int* counts = reinterpret_cast<int*>(take(E * sizeof(int)));
-  int* idx = reinterpret_cast<int*>(take((size_t)P * sizeof(int)));
-  float* wts = reinterpret_cast<float*>(take((size_t)P * sizeof(float)));
-  int* row_of_pair = reinterpret_cast<int*>(take((size_t)P * sizeof(int)));
-  int* pair_of_row = reinterpret_cast<int*>(take((size_t)P * sizeof(int)));
-  Act8 ax = act8_view(take(act8_bytes(P, H)), P, H);
-  float* G = reinterpret_cast<float*>(take((size_t)P * I * sizeof(float)));
-  float* U = reinterpret_cast<float*>(take((size_t)P * I * sizeof(float)));
-  Act8 ah = act8_view(take(act8_bytes(P, I)), P, I);
-  float* Y = reinterpret_cast<float*>(take((size_t)P * H * sizeof(float)));
+  w->counts = reinterpret_cast<int*>(take(E * sizeof(int)));
+  w->idx = reinterpret_cast<int*>(take((size_t)P * sizeof(int)));
+  w->wts = reinterpret_cast<float*>(take((size_t)P * sizeof(float)));
+  w->row_of_pair = reinterpret_cast<int*>(take((size_t)P * sizeof(int)));
+  w->pair_of_row = reinterpret_cast<int*>(take((size_t)P * sizeof(int)));
+  w->ax = act8_view(take(act8_bytes(P, H)), P, H);
+  w->G = reinterpret_cast<float*>(take((size_t)P * I * sizeof(float)));
+  w->U = reinterpret_cast<float*>(take((size_t)P * I * sizeof(float)));
+  w->ah = act8_view(take(act8_bytes(P, I)), P, I);
+  w->Y = reinterpret_cast<float*>(take((size_t)P * H * sizeof(float)));
+  return true;
+}
 
-  kq_status_t st = check_cuda(cudaMemsetAsync(counts, 0, E * sizeof(int), s), "moe counts");
+// Expert FFNs of P routed rows. Row p reads x row p / div and goes to expert
+// expert_of_pair[p] (w.counts already holds the per-expert row counts). The
+// result for row p lands in w.Y[w.row_of_pair[p]].
+kq_status_t moe_core(const float* x, int div, const int* expert_of_pair, int P, int E, const void* w_gate,
+                     const void* w_up, const void* w_down, int H, int I, int act_mode, MoeWs& w, cudaStream_t s) {
+  expert_rank_kernel<<<E, 1024, 0, s>>>(expert_of_pair, w.counts, P, E, w.row_of_pair, w.pair_of_row);
+  kq_status_t st = check_launch("moe rank");
   if (st) return st;
-  route_kernel<<<(T + 127) / 128, 128, 0, s>>>(logits, T, E, topk, idx, wts, counts);
-  if ((st = check_launch("moe route"))) return st;
-  expert_rank_kernel<<<E, 1024, 0, s>>>(idx, counts, P, E, row_of_pair, pair_of_row);
-  if ((st = check_launch("moe rank"))) return st;
   int hc[kMaxExperts];
-  if ((st = check_cuda(cudaMemcpyAsync(hc, counts, E * sizeof(int), cudaMemcpyDeviceToHost, s), "moe counts d2h")))
+  if ((st = check_cuda(cudaMemcpyAsync(hc, w.counts, E * sizeof(int), cudaMemcpyDeviceToHost, s), "moe counts d2h")))
     return st;
   if ((st = check_cuda(cudaStreamSynchronize(s), "moe counts sync"))) return st;
-  if ((st = launch_quantize_act_gather(x, pair_of_row, topk, ax, P, H, act_mode, s))) return st;
-
+  if ((st = launch_quantize_act_gather(x, w.pair_of_row, div, w.ax, P, H, act_mode, s))) return st;
   const size_t gate_bytes = (size_t)I * (H / 32) * 18, down_bytes = (size_t)H * (I / 32) * 18;
   auto rows = [](Act8 a, int r0, int K) { return Act8{a.qs + (size_t)r0 * K, a.ds + (size_t)r0 * (K / 32)}; };
   int r0 = 0;
   for (int e = 0; e < E; ++e) {
     const int m = hc[e];
     if (m > 0) {
-      const Act8 a = rows(ax, r0, H);
-      if ((st = gemm_any(KQ_Q4_0, static_cast<const uint8_t*>(w_gate) + e * gate_bytes, a, G + (size_t)r0 * I, m, I,
-                         H, s)))
+      const Act8 a = rows(w.ax, r0, H);
+      if ((st = gemm_any(KQ_Q4_0, static_cast<const uint8_t*>(w_gate) + e * gate_bytes, a, w.G + (size_t)r0 * I, m,
+                         I, H, s)))
         return st;
-      if ((st = gemm_any(KQ_Q4_0, static_cast<const uint8_t*>(w_up) + e * gate_bytes, a, U + (size_t)r0 * I, m, I, H,
-                         s)))
+      if ((st = gemm_any(KQ_Q4_0, static_cast<const uint8_t*>(w_up) + e * gate_bytes, a, w.U + (size_t)r0 * I, m, I,
+                         H, s)))
         return st;
     }
     r0 += m;
   }
-  if ((st = launch_silu_mul_quantize(G, U, ah, P, I, act_mode, s))) return st;
+  if ((st = launch_silu_mul_quantize(w.G, w.U, w.ah, P, I, act_mode, s))) return st;
   r0 = 0;
   for (int e = 0; e < E; ++e) {
     const int m = hc[e];
     if (m > 0) {
-      if ((st = gemm_any(KQ_Q4_0, static_cast<const uint8_t*>(w_down) + e * down_bytes, rows(ah, r0, I),
-                         Y + (size_t)r0 * H, m, H, I, s)))
+      if ((st = gemm_any(KQ_Q4_0, static_cast<const uint8_t*>(w_down) + e * down_bytes, rows(w.ah, r0, I),
+                         w.Y + (size_t)r0 * H, m, H, I, s)))
         return st;
     }
     r0 += m;
   }
-  combine_kernel<<<T, 256, 0, s>>>(Y, row_of_pair, wts, T, topk, H, out);
+  return KQ_OK;
+}
+
+kq_status_t check_moe(int E, int topk, int H, int I) {
+  if (E < 1 || E > kMaxExperts || topk < 1 || topk > kMaxTopk || topk > E)
+    return fail(KQ_ERR_INVALID, "moe: unsupported E=%d topk=%d", E, topk);
+  if (H % 32 || I % 32) return fail(KQ_ERR_INVALID, "moe: H and I must be multiples of 32");
+  return KQ_OK;
+}
+
+}  // namespace
+
+kq_status_t launch_moe_route(const float* logits, int T, int E, int topk, int* idx, float* wts, cudaStream_t s) {
+  kq_status_t st = check_moe(E, topk, 32, 32);
+  if (st || T == 0) return st;
+  int* counts = static_cast<int*>(workspace(WS_MOE2, E * sizeof(int)));
+  if (!counts) return KQ_ERR_NOMEM;
+  if ((st = check_cuda(cudaMemsetAsync(counts, 0, E * sizeof(int), s), "moe counts"))) return st;
+  route_kernel<<<(T + 127) / 128, 128, 0, s>>>(logits, T, E, topk, idx, wts, counts);
+  return check_launch("moe route");
+}
+
+kq_status_t launch_moe_combine(const float* y, const float* wts, int T, int topk, int H, float* out, cudaStream_t s) {
+  if (T == 0) return KQ_OK;
+  combine_kernel<<<T, 256, 0, s>>>(y, nullptr, wts, T, topk, H, out);
+  return check_launch("moe combine");
+}
+
+kq_status_t launch_moe_experts_q4_0(const float* x_rows, const int* expert_of_row, const void* w_gate,
+                                    const void* w_up, const void* w_down, int E, int P, int H, int I, int act_mode,
+                                    float* y_rows, cudaStream_t s) {
+  kq_status_t st = check_moe(E, 1, H, I);
+  if (st || P == 0) return st;
+  MoeWs w;
+  if (!moe_ws(P, E, H, I, &w)) return KQ_ERR_NOMEM;
+  if ((st = check_cuda(cudaMemsetAsync(w.counts, 0, E * sizeof(int), s), "moe counts"))) return st;
+  count_kernel<<<(P + 255) / 256, 256, 0, s>>>(expert_of_row, P, w.counts);
+  if ((st = check_launch("moe count"))) return st;
+  if ((st = moe_core(x_rows, 1, expert_of_row, P, E, w_gate, w_up, w_down, H, I, act_mode, w, s))) return st;
+  unsort_kernel<<<P, 256, 0, s>>>(w.Y, w.row_of_pair, H, y_rows);
+  return check_launch("moe unsort");
+}
+
+kq_status_t launch_moe_q4_0(const float* x, const float* logits, const void* w_gate, const void* w_up,
+                            const void* w_down, int E, int topk, int T, int H, int I, int act_mode, float* out,
+                            cudaStream_t s) {
+  kq_status_t st = check_moe(E, topk, H, I);
+  if (st) return st;
+  const int P = T * topk;
+  MoeWs w;
+  if (!moe_ws(P, E, H, I, &w)) return KQ_ERR_NOMEM;
+  if ((st = check_cuda(cudaMemsetAsync(w.counts, 0, E * sizeof(int), s), "moe counts"))) return st;
+  route_kernel<<<(T + 127) / 128, 128, 0, s>>>(logits, T, E, topk, w.idx, w.wts, w.counts);
+  if ((st = check_launch("moe route"))) return st;
+  if ((st = moe_core(x, topk, w.idx, P, E, w_gate, w_up, w_down, H, I, act_mode, w, s))) return st;
+  combine_kernel<<<T, 256, 0, s>>>(w.Y, w.row_of_pair, w.wts, T, topk, H, out);
   return check_launch("moe combine");
 }
 

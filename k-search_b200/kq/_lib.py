@@ -37,6 +37,9 @@ SIGNATURES = {
     "kq_gemm_f32act_noalloc": (_i, [_i, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "kq_mul_mat_q8x": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "kq_moe_q4_0": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp]),
+    "kq_moe_route": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp]),
+    "kq_moe_experts_q4_0": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp]),
+    "kq_moe_combine": (_i, [_vp, _vp, _i, _i, _i, _vp, _vp]),
     "kq_block_sums_i32": (_i, [_i, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "kq_fa_decode_q8_0_mha": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "kq_fa_decode_q8_0_ragged": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp, _vp]),

@@ -138,6 +138,53 @@ def moe_q4_0(x: torch.Tensor, router_logits: torch.Tensor, w_gate: torch.Tensor,
     return out
 
 
+def moe_route(router_logits: torch.Tensor, topk: int = 2) -> tuple[torch.Tensor, torch.Tensor]:
+    """Router: (idx int32 [T, topk], wts fp32 [T, topk]) from logits fp32 [T, E]."""
+    _cuda(router_logits, "router_logits", torch.float32)
+    T, E = router_logits.shape
+    idx = torch.empty((T, topk), dtype=torch.int32, device=router_logits.device)
+    wts = torch.empty((T, topk), dtype=torch.float32, device=router_logits.device)
+    check(lib().kq_moe_route(router_logits.data_ptr(), T, E, topk, idx.data_ptr(), wts.data_ptr(),
+                             _stream(router_logits)), "kq_moe_route")
+    return idx, wts
+
+
+def moe_experts_q4_0(x_rows: torch.Tensor, expert_of_row: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
+                     w_down: torch.Tensor, act_mode="sum_dq", out: torch.Tensor | None = None) -> torch.Tensor:
+    """Expert FFNs of routed rows: x_rows fp32 [P, H], expert_of_row int32 [P]
+    (indices into this call's experts); weights as in moe_q4_0. fp32 [P, H]."""
+    _cuda(x_rows, "x_rows", torch.float32)
+    P, H = x_rows.shape
+    _cuda(expert_of_row, "expert_of_row", torch.int32, P)
+    _cuda(w_gate, "w_gate", torch.uint8)
+    _cuda(w_up, "w_up", torch.uint8)
+    _cuda(w_down, "w_down", torch.uint8)
+    E = w_gate.shape[0]
+    I = w_gate.numel() // (E * (H // 32) * 18)
+    if w_gate.numel() != E * I * (H // 32) * 18 or w_up.numel() != w_gate.numel() or w_down.numel() != E * H * (I // 32) * 18:
+        raise ValueError("expert weight sizes do not match [E, I, H/32, 18] / [E, H, I/32, 18]")
+    if out is None:
+        out = torch.empty((P, H), dtype=torch.float32, device=x_rows.device)
+    check(lib().kq_moe_experts_q4_0(x_rows.data_ptr(), expert_of_row.data_ptr(), w_gate.data_ptr(), w_up.data_ptr(),
+                                    w_down.data_ptr(), E, P, H, I, _act_mode(act_mode), out.data_ptr(),
+                                    _stream(x_rows)), "kq_moe_experts_q4_0")
+    return out
+
+
+def moe_combine(y: torch.Tensor, wts: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[t] = sum_k wts[t, k] * y[t * topk + k]; y fp32 [T * topk, H]."""
+    _cuda(wts, "wts", torch.float32)
+    T, topk = wts.shape
+    _cuda(y, "y", torch.float32)
+    if y.dim() != 2 or y.shape[0] != T * topk:
+        raise ValueError(f"y must be [T * topk, H] = [{T * topk}, H], got {tuple(y.shape)}")
+    H = y.shape[1]
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.float32, device=y.device)
+    check(lib().kq_moe_combine(y.data_ptr(), wts.data_ptr(), T, topk, H, out.data_ptr(), _stream(y)), "kq_moe_combine")
+    return out
+
+
 def block_sums_i32(weight: torch.Tensor, a_q8_1: torch.Tensor, M: int, N: int, K: int, wtype="q4_0") -> torch.Tensor:
     """int32 sumi [M, N, K/32] (the bit-exact parity quantity)."""
     wt = _wtype(wtype)
