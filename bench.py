@@ -6,17 +6,20 @@ Workload (default): BASELINE configuration 1, the q8_0 x q8_1 W8A8 GEMM
 M=512, N=11008, K=4096 with fp32 activations quantised on the fly. One step
 is one call of the operator (activation quantisation + GEMM) on one batch of
 synthetic, seeded input already resident in HBM. Other --config values
-(0: q4_0 GEMV, 2: q4_0 sweep point, 3: ragged q8_0-KV flash decode) are for
-DESIGN.md tables, not the headline line.
+(0: q4_0 GEMV, 2: q4_0 sweep point, 3: ragged q8_0-KV flash decode,
+4: grouped q4_0 MoE) measure the other operators of the path.
 
 Timing: W untimed warm-up steps, then K steps bracketed by a barrier and
 torch.cuda.synchronize(), timed with CUDA events on the launching stream,
 max over ranks. Consecutive steps rotate through input sets whose combined
 size exceeds 2x the L2 cache, so every step reads its operands from HBM.
 
-Multi-GPU (torchrun, one rank per GPU): weak scaling. Every rank runs the same
-per-GPU workload on its own shard of output columns (the N-sharded GEMM); the
-shards are independent, so the timed step has no collective.
+Multi-GPU (torchrun, one rank per GPU): weak scaling of the N-sharded GEMM.
+Rank r holds the weight rows of output columns [r*N, (r+1)*N) of an
+[M, world*N] product; each timed step is the local operator plus the NCCL
+all-gather that assembles the full output on every rank (eager, event-timed).
+--config 3 (decode) shards whole sequences (no collective); --config 4 (MoE)
+runs expert-parallel with all-to-all dispatch and combine.
 
 --impl reference times the reference's own CPU implementation of the same
 operator (kernelevalplus-main/include/gemm_reference.h gemm_w8a8_reference,
@@ -202,6 +205,32 @@ def graph_time_ms(step, steps: int, warmup: int, world: int, clocks=None) -> tup
 # CPU baseline (reference C++ routines or the oracle port)
 # ---------------------------------------------------------------------------
 
+def eager_time_ms(step, steps: int, warmup: int, world: int, clocks=None) -> tuple[float, dict | None]:
+    """Time `steps` eager calls of step(i) with CUDA events on the current
+    stream (used where a step holds a collective: no graph capture of NCCL)."""
+    import torch
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop() if clocks else None
+    return max_over_ranks(ms, world), clk
+
+
 def cpu_threads() -> int:
     try:
         return len(os.sched_getaffinity(0))
@@ -293,14 +322,32 @@ def bench_gemm(args, cfg, rank, world):
     L = kq.lib()
     wtc = kq.WTYPES[wt]
     act_mode = kq.ACT_MODES[cfg["act"]]
-    def step(i):
-        j = i % nsets
-        sp = torch.cuda.current_stream().cuda_stream
-        _lib.check(L.kq_gemm_f32act(wtc, ws[j].data_ptr(), xs[j].data_ptr(), outs[j].data_ptr(), M, N, K, act_mode, sp),
-                   "kq_gemm_f32act")
-
     clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
-    ms, clk = graph_time_ms(step, args.steps, args.warmup, world, clocks)
+    if world == 1:
+        def step(i):
+            j = i % nsets
+            sp = torch.cuda.current_stream().cuda_stream
+            _lib.check(L.kq_gemm_f32act(wtc, ws[j].data_ptr(), xs[j].data_ptr(), outs[j].data_ptr(), M, N, K,
+                                        act_mode, sp), "kq_gemm_f32act")
+
+        ms, clk = graph_time_ms(step, args.steps, args.warmup, world, clocks)
+    else:
+        # rank r holds output columns [r*N, (r+1)*N) of an [M, world*N] product
+        # (its own weight shard); each step ends with the all-gather that
+        # assembles the full [M, world*N] output on every rank.
+        import torch.distributed as dist
+        full = [torch.empty((M, world * N), dtype=torch.float32, device=dev) for _ in range(2)]
+        gath = torch.empty((world * M, N), dtype=torch.float32, device=dev)
+
+        def step(i):
+            j = i % nsets
+            sp = torch.cuda.current_stream().cuda_stream
+            _lib.check(L.kq_gemm_f32act(wtc, ws[j].data_ptr(), xs[j].data_ptr(), outs[j].data_ptr(), M, N, K,
+                                        act_mode, sp), "kq_gemm_f32act")
+            dist.all_gather_into_tensor(gath, outs[j])
+            full[i % 2].view(M, world, N).copy_(gath.view(world, M, N).permute(1, 0, 2))
+
+        ms, clk = eager_time_ms(step, args.steps, args.warmup, world, clocks)
     ops = 2.0 * M * N * K
     value = world * ops * args.steps / (ms * 1e-3) / 1e12
 
@@ -325,21 +372,30 @@ def bench_gemm(args, cfg, rank, world):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
     # ---- end to end through the public API with host buffers ----
+    # world > 1: kq.dist.NShardedGemm (local GEMM + all-gather), full
+    # [M, world*N] output read back on every rank.
+    from kq import dist as kd
+    NT = world * N
+    sharded = kd.NShardedGemm(ws[0], NT, K, wtype=wt, act_mode=cfg["act"], align=N) if world > 1 else None
     xh = [torch.randn((M, K), generator=g, dtype=torch.float32).pin_memory() for _ in range(2)]
-    oh = [torch.empty((M, N), dtype=torch.float32).pin_memory() for _ in range(2)]
+    oh = [torch.empty((M, NT), dtype=torch.float32).pin_memory() for _ in range(2)]
     xd = torch.empty((M, K), dtype=torch.float32, device=dev)
+    od = torch.empty((M, NT), dtype=torch.float32, device=dev)
 
     def estep(i):
         j = i % nsets
         xd.copy_(xh[i % 2], non_blocking=True)
-        kq.gemm_f32act(ws[j], xd, M, N, K, wt, cfg["act"], out=outs[j])
-        oh[i % 2].copy_(outs[j], non_blocking=True)
+        if sharded is None:
+            kq.gemm_f32act(ws[j], xd, M, N, K, wt, cfg["act"], out=od)
+        else:
+            sharded.weight = ws[j]
+            sharded(xd, out=od)
+        oh[i % 2].copy_(od, non_blocking=True)
 
     for i in range(3):
         estep(i)
     torch.cuda.synchronize()
     barrier(world)
-    t0 = time.perf_counter()
     e0.record(stream)
     for i in range(args.steps):
         estep(i)
@@ -347,7 +403,8 @@ def bench_gemm(args, cfg, rank, world):
     torch.cuda.synchronize()
     ems = max_over_ranks(e0.elapsed_time(e1), world)
     e2e = {"value": world * ops * args.steps / (ems * 1e-3) / 1e12, "unit": "TOPS",
-           "h2d_bytes_per_step": M * K * 4, "d2h_bytes_per_step": M * N * 4}
+           "h2d_bytes_per_step": M * K * 4, "d2h_bytes_per_step": M * NT * 4,
+           "api": "kq.gemm_f32act" if world == 1 else "kq.dist.NShardedGemm"}
 
     hbm, bf16, src = load_peaks()
     kernel_bytes = N * nb * bb + M * K + M * nb * 8 + M * N * 4
@@ -371,7 +428,9 @@ def bench_gemm(args, cfg, rank, world):
         "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded; weights drawn directly as q-blocks)",
         "config": {"workload": cfg["workload"], "M": M, "N": N, "K": K, "wtype": wt, "act_quant": cfg["act"],
                    "l2": f"{nsets} rotating input sets ({nsets * step_bytes / 1e6:.0f} MB > 2x L2)",
-                   "parallelism": f"N-sharded weak scaling x{world} (independent column shards)"},
+                   "parallelism": ("single GPU" if world == 1 else
+                                   f"N-sharded x{world}: rank r computes columns [r*N, (r+1)*N) of an "
+                                   f"[M, {world}*N] product, NCCL all-gather of the output each step")},
         "roofline": roof,
         "e2e": e2e,
         "gpu_launches": launches_per_step * args.steps,
@@ -386,10 +445,18 @@ def bench_fa(args, cfg, rank, world):
     import torch
     import kq
 
-    B, Hq, Hkv, D = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["D"]
+    from kq import dist as kd
+
+    B0, Hq, Hkv, D = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["D"]
     dev = torch.device("cuda", torch.cuda.current_device())
-    rng = np.random.default_rng(99 + rank)
-    lens = rng.integers(cfg["Lmin"], cfg["Lmax"] + 1, size=B).astype(np.int32)
+    # weak scaling: a batch of world*B0 ragged sequences, whole sequences
+    # assigned to ranks by kq.dist.plan_decode (longest first, least loaded)
+    rng = np.random.default_rng(99)
+    all_lens = rng.integers(cfg["Lmin"], cfg["Lmax"] + 1, size=B0 * world).astype(np.int32)
+    plan = kd.plan_decode(all_lens, Hkv, world)
+    mine = [u.seq for u in plan.units[rank]]
+    lens = all_lens[mine]
+    B = len(mine)
     cu = np.zeros(B + 1, dtype=np.int32)
     cu[1:] = np.cumsum(lens)
     T = int(cu[-1])
@@ -412,7 +479,7 @@ def bench_fa(args, cfg, rank, world):
 
     clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
     ms, clk = graph_time_ms(step, args.steps, args.warmup, world, clocks)
-    value = world * B * args.steps / (ms * 1e-3)
+    value = world * B0 * args.steps / (ms * 1e-3)
     per = ms / args.steps
     hbm, _, src = load_peaks()
     algo = 2 * kv_bytes + B * Hq * D * 2 * 2
@@ -421,7 +488,10 @@ def bench_fa(args, cfg, rank, world):
         "metric": "q8_0-KV flash-decode tok/s", "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per, 5), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp32", "data": "synthetic (seeded)",
-        "config": {"workload": cfg["workload"], "sum_L": T, "l2": f"{nsets} rotating KV caches"},
+        "config": {"workload": cfg["workload"], "sum_L": T, "l2": f"{nsets} rotating KV caches",
+                   "parallelism": "single GPU" if world == 1 else
+                   f"{world * B0} sequences over {world} ranks (kq.dist.plan_decode), no collective; "
+                   f"rank loads {plan.load()}"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": None, "kernel": "fa decode (partial+combine)",
                      "peak_source": f"{src} hbm_gbs"},
@@ -439,17 +509,27 @@ def bench_moe(args, cfg, rank, world):
 
     T, E, topk, H, I = cfg["T"], cfg["E"], cfg["topk"], cfg["H"], cfg["I"]
     dev = torch.device("cuda", torch.cuda.current_device())
-    rng = np.random.default_rng(4321 + rank)
-    wg = torch.from_numpy(np.stack([synth.q4_0_blocks(rng, I, H) for _ in range(E)])).to(dev)
-    wu = torch.from_numpy(np.stack([synth.q4_0_blocks(rng, I, H) for _ in range(E)])).to(dev)
-    wd = torch.from_numpy(np.stack([synth.q4_0_blocks(rng, H, I) for _ in range(E)])).to(dev)
+    from kq import dist as kd
+    # expert e's weights are seeded by e, so every rank count sees the same experts;
+    # world > 1: rank r owns experts kd.expert_range(E, world, r) and T tokens of its own
+    first, per = kd.expert_range(E, world, rank)
+
+    def expert_w(e, which, rows, cols):
+        return synth.q4_0_blocks(np.random.default_rng([4321, e, which]), rows, cols)
+
+    wg = torch.from_numpy(np.stack([expert_w(e, 0, I, H) for e in range(first, first + per)])).to(dev)
+    wu = torch.from_numpy(np.stack([expert_w(e, 1, I, H) for e in range(first, first + per)])).to(dev)
+    wd = torch.from_numpy(np.stack([expert_w(e, 2, H, I) for e in range(first, first + per)])).to(dev)
     g = torch.Generator(device="cpu").manual_seed(77 + rank)
     x = torch.randn((T, H), generator=g).to(dev)
     logits = torch.randn((T, E), generator=g).to(dev)
     out = torch.empty((T, H), dtype=torch.float32, device=dev)
 
     def step(i):
-        kq.moe_q4_0(x, logits, wg, wu, wd, topk, cfg["act"], out=out)
+        if world == 1:
+            kq.moe_q4_0(x, logits, wg, wu, wd, topk, cfg["act"], out=out)
+        else:
+            kd.moe_expert_parallel(x, logits, wg, wu, wd, E, topk, cfg["act"])
 
     for i in range(args.warmup):
         step(i)
@@ -477,12 +557,15 @@ def bench_moe(args, cfg, rank, world):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic (seeded; weights drawn directly as q4_0 blocks)",
         "config": {"workload": cfg["workload"], "T": T, "E": E, "topk": topk, "H": H, "I": I,
-                   "l2": "expert weights 792 MB > L2"},
+                   "l2": "expert weights 792 MB > L2",
+                   "parallelism": "single GPU" if world == 1 else
+                   f"expert-parallel x{world} ({per} experts per rank, {T} tokens per rank), "
+                   "NCCL all-to-all dispatch and combine"},
         "roofline": {"bound": "tensor", "achieved": round(value / world, 2), "peak": round(2 * bf16, 1),
                      "unit": "TFLOP/s", "frac": round(value / world / (2 * bf16), 4), "traffic": None,
                      "kernel": "whole MoE step (route + 24 expert GEMMs + SiLU + combine)",
                      "peak_source": f"int8 dense = 2 x {src} bf16_tflops"},
-        "gpu_launches": (5 + 3 * E) * args.steps,
+        "gpu_launches": ((5 + 3 * E) if world == 1 else (7 + 3 * per)) * args.steps,
     }
     if clk is not None:
         line["clocks"] = clk

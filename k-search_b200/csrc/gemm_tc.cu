@@ -16,7 +16,7 @@
 //   warp 0      TMA producer: activation codes (int8 [M, K], 128B-swizzled
 //               boxes of 128 rows x 128 B = 4 blocks), activation (d, s)
 //               pairs, and raw weight rows (the unchanged AoS q-blocks,
-//               128 rows x 8 blocks per box). No multicast anywhere.
+//               128 rows x 8 blocks per box); every CTA loads its own tiles.
 //   warps 1-2   MMA issuers (one thread each): warp 1+i issues K blocks
 //               i, i+2 of every stage into TMEM buffers i, i+2, so two
 //               issue/commit latency chains run side by side; warp 1 also

@@ -123,7 +123,7 @@ __device__ __forceinline__ void mbar_wait_or_poison(uint64_t* bar, uint32_t pari
   if (!dead && !mbar_wait(bar, parity, err, code)) dead = true;
 }
 
-// ---- bulk async copy global -> shared (no multicast) ------------------------
+// ---- bulk async copy global -> shared (this CTA only) -----------------------
 // dst, src 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
