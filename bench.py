@@ -55,6 +55,17 @@ CONFIGS = {
 }
 
 
+# DRAM traffic per launch of the dominant kernel (dram__bytes_read.sum +
+# dram__bytes_write.sum from one ncu capture; profiles/*.md give the commands).
+# Keys: (kernel, workload). Per-unit figures scale with the units a launch
+# processes (weight rows for the GEMV, token rows for the decode).
+NCU_TRAFFIC = {
+    ("gemm_tc", "q8_0 M=512 N=11008 K=4096"): 51.29e6,     # profiles/gemm_tc_q8_0_m512_n11008_k4096.md
+    ("gemv", "q4_0 per weight row, K=4096"): 33.06e6 / 14336,  # profiles/gemv_q4_0_m1_n14336_k4096.md
+    ("fa_fast", "per token row, Hkv=8 D=128"): 319.06e6 / 139124,  # profiles/fa_fast_decode_b32_hkv8_d128.md
+}
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -411,13 +422,16 @@ def bench_gemm(args, cfg, rank, world):
     if M <= 8:
         achieved = kernel_bytes / (kms * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                "frac": round(achieved / hbm, 4), "traffic": None,
+                "frac": round(achieved / hbm, 4),
+                "traffic": (round(NCU_TRAFFIC[("gemv", "q4_0 per weight row, K=4096")] * N)
+                            if (wt == "q4_0" and K == 4096) else None),
                 "kernel": "gemv_kernel", "peak_source": f"{src} hbm_gbs (copy)"}
     else:
         achieved = ops / (kms * 1e-3) / 1e12
         peak = 2.0 * bf16
         roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
-                "frac": round(achieved / peak, 4), "traffic": None,
+                "frac": round(achieved / peak, 4),
+                "traffic": NCU_TRAFFIC.get(("gemm_tc", f"{wt} M={M} N={N} K={K}")),
                 "kernel": "quantised GEMM (M > 8)",
                 "peak_source": f"int8 dense = 2 x {src} bf16_tflops (cuBLAS bf16 burst)"}
     launches_per_step = 2
@@ -493,7 +507,10 @@ def bench_fa(args, cfg, rank, world):
                    f"{world * B0} sequences over {world} ranks (kq.dist.plan_decode), no collective; "
                    f"rank loads {plan.load()}"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(achieved / hbm, 4), "traffic": None, "kernel": "fa decode (partial+combine)",
+                     "frac": round(achieved / hbm, 4),
+                     "traffic": round(NCU_TRAFFIC[("fa_fast", "per token row, Hkv=8 D=128")] * T)
+                     if (Hkv == 8 and D == 128) else None,
+                     "kernel": "fa decode (partial+combine)",
                      "peak_source": f"{src} hbm_gbs"},
         "gpu_launches": 2 * args.steps,
     }
