@@ -1,4 +1,5 @@
 // libkq C ABI: argument checks, dispatch, per-device workspace, error state.
+#include <cstdlib>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -130,9 +131,24 @@ kq_status_t check_gemm_args(int wtype, const void* w, const void* a, const float
 }
 
 // Quantised activations are staged; choose the GEMM kernel for the shape.
+// M > 8 path: the int8 tcgen05 kernel (exact per-block arithmetic) by default;
+// KQ_GEMM_PATH=dequant selects the fp16-dequantised kind::f16 kernel, faster
+// but with fp16 operand rounding (rel-L2 about 3e-4 against the exact result).
+// Read once per process.
+enum class GemmPath { kDequant, kInt8 };
+GemmPath gemm_path() {
+  static const GemmPath p = [] {
+    const char* e = std::getenv("KQ_GEMM_PATH");
+    return (e && std::string(e) == "dequant") ? GemmPath::kDequant : GemmPath::kInt8;
+  }();
+  return p;
+}
+
 kq_status_t dispatch_gemm(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, cudaStream_t s,
                           bool pdl) {
   if (gemv_supported(wtype, M, N, K) && aligned(w, 16)) return launch_gemv(wtype, w, act, out, M, N, K, pdl, s);
+  if (gemm_path() == GemmPath::kDequant && gemm_hx_supported(wtype, M, N, K, w, act))
+    return launch_gemm_hx(wtype, w, act, out, M, N, K, pdl, s);
   if (gemm_tc_supported(wtype, M, N, K, w, act)) return launch_gemm_tc(wtype, w, act, out, M, N, K, pdl, s);
   return launch_gemm_simt(wtype, w, act, out, M, N, K, s);
 }

@@ -11,24 +11,23 @@
 // separate MMA (K = 32, one instruction) into a fresh TMEM buffer; the fp32
 // accumulation across blocks happens in the epilogue warps' registers.
 //
-// CTA = 11 warps, one CTA per SM, persistent over 128 x 128 output tiles
+// CTA = 20 warps, one CTA per SM, persistent over 128 x 128 output tiles
 // (tokens x weight rows), tokens fastest so co-running CTAs share weights in L2:
 //   warp 0      TMA producer: activation codes (int8 [M, K], 128B-swizzled
 //               boxes of 128 rows x 128 B = 4 blocks), activation (d, s)
 //               pairs, and raw weight rows (the unchanged AoS q-blocks,
 //               128 rows x 8 blocks per box); every CTA loads its own tiles.
-//   warps 1-2   MMA issuers (one thread each): warp 1+i issues K blocks
-//               i, i+2 of every stage into TMEM buffers i, i+2, so two
-//               issue/commit latency chains run side by side; warp 1 also
-//               owns the TMEM allocation.
-//   warps 3-10  workers. For K stage s they first convert the raw weight
-//               blocks of stage s+1 (two blocks of one row per thread) into
-//               int8 codes in the UMMA K-major SWIZZLE_128B layout plus fp32
-//               scale rows (then fence.proxy.async and release it to the MMA),
-//               then run the epilogue of stage s: read each block's int32
-//               result from TMEM (tcgen05.ld 32x32b, 64 columns per thread),
-//               apply the block's scales and accumulate in fp32 registers.
-//               4 TMEM buffers of 128 columns let the MMA run ahead.
+//   warp 1      MMA issuer (one thread), owns the TMEM allocation. Per block:
+//               a kind::f16 MMA writes the bias words (see kBias), then the
+//               block's kind::i8 MMA accumulates onto them; one commit.
+//   warps 2-3   converters: two weight rows per thread, the 4 blocks of a stage
+//               into int8 codes in the UMMA K-major SWIZZLE_128B layout plus
+//               fp32 scale rows, running ahead of the MMA by up to SWS stages.
+//   warps 4-19  epilogue: read each block's result from TMEM (tcgen05.ld,
+//               32 columns per thread, one half-load ahead), hand the buffer
+//               back, apply the block's scales and accumulate in fp32 registers.
+//               4 TMEM buffers of 128 columns let the MMA run a stage ahead.
+// Every hand-off is an mbarrier; every wait is bounded (kq_device.cuh).
 #include <cuda.h>
 
 #include <algorithm>
@@ -36,37 +35,31 @@
 
 #include "kq_internal.h"
 #include "kq_device.cuh"
+#include "kq_tc.cuh"
 
 namespace kq {
 namespace {
 
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+using namespace tc;
 
-CUresult encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, cuuint32_t rank, void* base, const cuuint64_t* dims,
-                      const cuuint64_t* strides, const cuuint32_t* box, const cuuint32_t* estr,
-                      CUtensorMapInterleave il, CUtensorMapSwizzle sw, CUtensorMapL2promotion l2,
-                      CUtensorMapFloatOOBfill oob) {
-  auto fn = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
-  if (!fn) return CUDA_ERROR_NOT_SUPPORTED;
-  return fn(map, dt, rank, base, dims, strides, box, estr, il, sw, l2, oob);
-}
 
 constexpr int TM = 128;        // tokens per tile (TMEM lanes)
 constexpr int TN = 128;        // weight rows per tile (TMEM columns per buffer)
 constexpr int KSUB = 4;        // blocks per activation / converted-weight stage (128 B of K)
 constexpr int KRAW = 8;        // blocks per raw weight stage (16-byte aligned for all block sizes)
-constexpr int SA = 3;          // activation stages
-constexpr int SWS = 3;         // converted weight stages
+constexpr int SA = 4;          // activation stages (codes + scales)
+constexpr int SWS = 4;         // converted weight stages (codes + scales)
 constexpr int SRAW = 2;        // raw weight stages
-constexpr int NBUF = 4;        // TMEM buffers
-constexpr int kWarpTma = 0, kWarpMma = 1, kMmaWarps = 2, kWarpWork = kWarpMma + kMmaWarps, kWorkWarps = 8;
-constexpr int kEpiCols = TN / (kWorkWarps / 4);  // columns per worker thread in the epilogue (32)
-constexpr int kWarps = kWarpWork + kWorkWarps;
+constexpr int NBUF = 4;        // TMEM buffers (one per block of a stage)
+constexpr int kWarpTma = 0, kWarpMma = 1, kWarpConv = 2, kConvWarps = 2, kWarpEpi = kWarpConv + kConvWarps,
+              kEpiWarps = 16;
+constexpr int kEpiCols = TN / (kEpiWarps / 4);  // columns per epilogue thread (32)
+constexpr int kHalf = kEpiCols / 2;             // columns per TMEM load (16)
+constexpr int kWarps = kWarpEpi + kEpiWarps;
 constexpr int kThreads = kWarps * 32;
 constexpr int kTmemCols = NBUF * TN;  // 512
-static_assert(NBUF == KSUB && NBUF % kMmaWarps == 0, "one TMEM buffer per K block of a stage, split over the issuers");
+static_assert(NBUF == KSUB, "one TMEM buffer per K block of a stage");
+constexpr int kConvRows = TN / (kConvWarps * 32);  // weight rows per converter thread (2)
 
 template <int WT>
 struct TcTraits {
@@ -79,13 +72,15 @@ struct TcTraits {
   static constexpr int W_TILE = TN * 128;                   // 16 KB
   static constexpr int ASC_STAGE = TM * KSUB * 8;           // (d, s) per row and block
   static constexpr int WSC_STAGE = KSUB * TN * 4 * (kHasMin ? 2 : 1);
+  static constexpr int PRE_TILE = 8 * 128;   // one 8-row swizzle atom, repeated over 128 rows (SBO 0)
   // byte offsets in dynamic shared memory (base aligned to 1024)
   static constexpr int OFF_ACT = 0;
   static constexpr int OFF_W = OFF_ACT + SA * ACT_TILE;
   static constexpr int OFF_RAW = OFF_W + SWS * W_TILE;
   static constexpr int OFF_ASC = OFF_RAW + SRAW * RAW_STAGE;
   static constexpr int OFF_WSC = OFF_ASC + SA * ASC_STAGE;
-  static constexpr int OFF_BAR = (OFF_WSC + SWS * WSC_STAGE + 15) / 16 * 16;
+  static constexpr int OFF_PRE = (OFF_WSC + SWS * WSC_STAGE + 1023) / 1024 * 1024;  // bias-preset operands
+  static constexpr int OFF_BAR = OFF_PRE + 2 * PRE_TILE;
   static constexpr int NBARS = 2 * SA + 2 * SWS + 2 * SRAW + 2 * NBUF;
   static constexpr int OFF_TMEM = OFF_BAR + NBARS * 8;
   static constexpr int SMEM = OFF_TMEM + 16 + 1024;  // + alignment slack
@@ -93,31 +88,6 @@ struct TcTraits {
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
-// ---- tcgen05 / TMA primitives ---------------------------------------------
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
-  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
-}
-
-__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(ncols)
-               : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
 __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
   asm volatile(
@@ -128,44 +98,7 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t
       : "memory");
 }
 
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
-        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
-        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-      : "r"(taddr)
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
-      "[%16];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-      : "r"(taddr)
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// Writes the same 32-bit value to 32 consecutive columns of this thread's lane.
-__device__ __forceinline__ void tmem_st32_const(uint32_t taddr, uint32_t v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
-      "%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
-      "r"(v)
-      : "memory");
-}
-__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Packed fp32 pairs (one instruction, two lanes of math each).
 __device__ __forceinline__ uint64_t pk2(float lo, float hi) {
@@ -203,22 +136,25 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
 // are, fp32 scales are rounded to 22 bits, a relative change below 2^-22).
 constexpr uint32_t kBias = 0x4B400000u;
 constexpr float kBiasF = 12582912.0f;
+
+// The bias is written by the tensor core itself: before each block's int8 MMA
+// a kind::f16 MMA with accumulate off computes A_pre x B_pre^T, where every row
+// of A_pre is (3072, 0, ..., 0) and every row of B_pre is (4096, 0, ..., 0):
+// 3072 * 4096 = 12582912 exactly, so each fp32 word becomes kBias. The int8
+// MMA then accumulates (integer add) onto those bits.
+constexpr uint16_t kPreA = 0x6A00;  // fp16 3072
+constexpr uint16_t kPreB = 0x6C00;  // fp16 4096
+
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
 __device__ __forceinline__ float round22(float d) {
   return __uint_as_float((__float_as_uint(d) + 2u) & ~3u);
-}
-
-__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-// UMMA shared-memory descriptor: K-major, SWIZZLE_128B, 8-row groups 1024 B
-// apart (SBO), version 1 (sm_100).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
-  d |= (uint64_t)1 << 16;                 // LBO (unused for swizzled K-major)
-  d |= (uint64_t)(1024 >> 4) << 32;       // SBO
-  d |= (uint64_t)1 << 46;                 // version
-  d |= (uint64_t)2 << 61;                 // SWIZZLE_128B
-  return d;
 }
 
 // Instruction descriptor, kind::i8: D s32, A = activations (signed),
@@ -231,8 +167,20 @@ __host__ __device__ constexpr uint32_t idesc_i8(bool b_signed) {
          | ((uint32_t)(TM >> 4) << 24);   // M
 }
 
-// byte offset of (row r, 16-byte chunk c) in a 128B-swizzled K-major tile
-__device__ __forceinline__ int sw128_off(int r, int c) { return (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4); }
+// Instruction descriptor, kind::f16: D f32, A = B = f16, both K-major.
+__host__ __device__ constexpr uint32_t idesc_f16() {
+  return (1u << 4) | ((uint32_t)(TN >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
+}
+
+template <int NC>
+__device__ __forceinline__ void tmem_ldh(uint32_t taddr, uint32_t (&v)[NC]) {
+  if constexpr (NC == 32) {
+    tmem_ld32(taddr, v);
+  } else {
+    static_assert(NC == 16, "TMEM load width");
+    tmem_ld16(taddr, v);
+  }
+}
 
 struct TcParams {
   int M, N, K, nb;
@@ -240,6 +188,17 @@ struct TcParams {
   float* out;
   int* err;
 };
+
+// SWIZZLE_128B K-major descriptor whose 8-row groups all alias one 1 KB atom
+// (SBO = 0): 128 identical-pattern rows from 8 stored ones.
+__device__ __forceinline__ uint64_t sw128_desc_rep8(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;    // LBO (unused for swizzled K-major)
+  d |= (uint64_t)1 << 46;    // version
+  d |= (uint64_t)2 << 61;    // SWIZZLE_128B
+  return d;
+}
 
 template <int WT>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -261,25 +220,38 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkb8 = p.nb / KRAW;
+  const int spt = p.nb / KSUB;  // K stages per tile (even: nb % 8 == 0)
+  const int my_tiles = (p.num_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int total = my_tiles * spt;  // K stages this CTA runs
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < SA; ++i) {
       mbar_init(&act_full[i], 1);
-      mbar_init(&act_empty[i], kMmaWarps + kWorkWarps);  // MMA commits + workers (they read the scales)
+      mbar_init(&act_empty[i], 1 + kEpiWarps);  // MMA commit + epilogue warps (they read the scales)
     }
     for (int i = 0; i < SWS; ++i) {
-      mbar_init(&w_full[i], kWorkWarps);
-      mbar_init(&w_empty[i], kMmaWarps + kWorkWarps);
+      mbar_init(&w_full[i], kConvWarps);
+      mbar_init(&w_empty[i], 1 + kEpiWarps);
     }
     for (int i = 0; i < SRAW; ++i) {
       mbar_init(&raw_full[i], 1);
-      mbar_init(&raw_empty[i], kWorkWarps);
+      mbar_init(&raw_empty[i], kConvWarps);
     }
     for (int i = 0; i < NBUF; ++i) {
       mbar_init(&tm_full[i], 1);
-      mbar_init(&tm_empty[i], kWorkWarps);
+      mbar_init(&tm_empty[i], kEpiWarps);
     }
     fence_mbar_init();
+  }
+  {
+    // bias-preset operands: rows (c, 0, ..., 0), c = 3072 (A) / 4096 (B);
+    // logical chunk 0 of row r sits in physical chunk r (128B swizzle)
+    uint4* pre = reinterpret_cast<uint4*>(smem + T::OFF_PRE);
+    for (int i = threadIdx.x; i < 2 * T::PRE_TILE / 16; i += kThreads) {
+      const int tile = i / (T::PRE_TILE / 16), r = (i % (T::PRE_TILE / 16)) / 8, c = i % 8;
+      pre[i] = make_uint4(c == r ? (uint32_t)(tile == 0 ? kPreA : kPreB) : 0u, 0u, 0u, 0u);
+    }
+    fence_proxy_async_smem();
   }
   if (warp == kWarpMma) tmem_alloc(tmem_slot, kTmemCols);
   tc_fence_before();
@@ -318,200 +290,211 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp < kWarpWork) {
-    // ------------------------------------------------------------ MMA issuers
+  } else if (warp == kWarpMma) {
+    // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_i8(T::kSignedW);
-      const int i0 = warp - kWarpMma;  // this thread issues K blocks i0, i0 + kMmaWarps, ... of every stage
+      constexpr uint32_t idesc_pre = idesc_f16();
       const uint32_t act_base = smem_u32(smem + T::OFF_ACT);
       const uint32_t w_base = smem_u32(smem + T::OFF_W);
-      int ia = 0;
-      for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
-        for (int s = 0; s < p.nb / KSUB; ++s, ++ia) {
-          const int as = ia % SA, ws = ia % SWS;
-          mbar_wait_or_poison(&act_full[as], (ia / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-          mbar_wait_or_poison(&w_full[ws], (ia / SWS) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-          const uint64_t adesc = sw128_desc(act_base + as * T::ACT_TILE);
-          const uint64_t bdesc = sw128_desc(w_base + ws * T::W_TILE);
+      const uint64_t pre_a = sw128_desc_rep8(smem_u32(smem + T::OFF_PRE));
+      const uint64_t pre_b = sw128_desc_rep8(smem_u32(smem + T::OFF_PRE + T::PRE_TILE));
+      for (int gs = 0; gs < total; ++gs) {
+        const int as = gs % SA, ws = gs % SWS;
+        mbar_wait_or_poison(&act_full[as], (gs / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+        mbar_wait_or_poison(&w_full[ws], (gs / SWS) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+        const uint64_t adesc = sw128_desc(act_base + as * T::ACT_TILE);
+        const uint64_t bdesc = sw128_desc(w_base + ws * T::W_TILE);
 #pragma unroll
-          for (int j = i0; j < KSUB; j += kMmaWarps) {
-            mbar_wait_or_poison(&tm_empty[j], ia & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
-            tc_fence_after();
-            // K block j of the stage: +32 bytes inside the 128-byte swizzle atom;
-            // accumulate onto the bias words the workers left in the buffer.
-            mma_i8(tmem_base + j * TN, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), idesc, 1u);
-            mma_commit(&tm_full[j]);
-          }
-          mma_commit(&act_empty[as]);
-          mma_commit(&w_empty[ws]);
+        for (int j = 0; j < KSUB; ++j) {
+          if (gs > 0) mbar_wait_or_poison(&tm_empty[j], (gs - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+          tc_fence_after();
+          // bias words from the tensor core, then K block j of the stage
+          // (+32 bytes inside the 128-byte swizzle atom) accumulated onto them
+          mma_f16(tmem_base + j * TN, pre_a, pre_b, idesc_pre, 0u);
+          mma_i8(tmem_base + j * TN, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), idesc, 1u);
+          mma_commit(&tm_full[j]);
         }
+        mma_commit(&act_empty[as]);
+        mma_commit(&w_empty[ws]);
       }
     }
-  } else {
-    // ------------------------------------------------------------ workers
-    const int wi = warp - kWarpWork;        // 0..7
-    const int quarter = warp & 3;           // TMEM lane quarter this warp may access
-    const int cg = wi >> 2;                 // column half of the epilogue
-    const int row = quarter * 32 + lane;    // token row in the tile (epilogue)
-    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    const int crow = (wi * 32 + lane) >> 1; // weight row converted by this thread
-    const int chalf = lane & 1;             // blocks 2*chalf, 2*chalf+1 of the 4-block stage
-    const int coff0 = sw128_off(crow, 4 * chalf), coff1 = sw128_off(crow, 4 * chalf + 1);
-    const int coff2 = sw128_off(crow, 4 * chalf + 2), coff3 = sw128_off(crow, 4 * chalf + 3);
-    const int spt = p.nb / KSUB;            // K stages per tile (even: nb % 8 == 0)
-    const int my_tiles = (p.num_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
-    const int total = my_tiles * spt;
-
-    // Convert global stage gs: blocks 2*chalf, 2*chalf+1 of row crow.
-    auto convert = [&](int gs) {
+  } else if (warp < kWarpEpi) {
+    // ------------------------------------------------------------ converters
+    const int crow0 = (warp - kWarpConv) * 32 + lane;  // rows crow0 + kConvWarps * 32 * r are converted here
+    constexpr int SB = KSUB * T::BB;                  // bytes of one stage of a raw row
+    constexpr int HB = 2 * T::BB;                     // two blocks (36 / 40 / 68 bytes: 4-byte aligned)
+    constexpr int NW = HB / 4;
+    for (int gs = 0; gs < total; ++gs) {
       const int irr = gs >> 1, sub = gs & 1;
       const int rs = irr % SRAW;
       mbar_wait_or_poison(&raw_full[rs], (irr / SRAW) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-      constexpr int HB = 2 * T::BB;  // 36 / 40 / 68 bytes, 4-byte aligned
-      const uint32_t* src = reinterpret_cast<const uint32_t*>(smem + T::OFF_RAW + rs * T::RAW_STAGE +
-                                                              crow * T::RAW_ROW + (sub * KSUB + 2 * chalf) * T::BB);
-      uint32_t w[HB / 4 + 1];
-#pragma unroll
-      for (int i = 0; i < HB / 4; ++i) w[i] = src[i];
-      w[HB / 4] = 0;
       const int ws = gs % SWS;
       if (gs >= SWS) mbar_wait_or_poison(&w_empty[ws], ((gs / SWS) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
       uint8_t* wt = smem + T::OFF_W + ws * T::W_TILE;
       float* wsc = reinterpret_cast<float*>(smem + T::OFF_WSC + ws * T::WSC_STAGE);
+#pragma unroll 1
+      for (int rr = 0; rr < kConvRows; ++rr) {
+      const int crow = crow0 + rr * kConvWarps * 32;
+      const uint32_t* src =
+          reinterpret_cast<const uint32_t*>(smem + T::OFF_RAW + rs * T::RAW_STAGE + crow * T::RAW_ROW + sub * SB);
 #pragma unroll
-      for (int jj = 0; jj < 2; ++jj) {
-        const int o = jj * T::BB;  // compile-time after unrolling
+      for (int hh = 0; hh < 2; ++hh) {  // blocks 2hh, 2hh + 1 of the stage
+        uint32_t w[NW + 1];
+#pragma unroll
+        for (int i = 0; i < NW; ++i) w[i] = src[hh * NW + i];
+        w[NW] = 0;
         auto u32 = [&](int off) -> uint32_t {
           return (off & 3) ? __funnelshift_r(w[off >> 2], w[(off >> 2) + 1], 16) : w[off >> 2];
         };
         auto u16 = [&](int off) -> uint32_t { return (off & 3) ? (w[off >> 2] >> 16) : (w[off >> 2] & 0xFFFFu); };
-        uint4 c0, c1;
-        float mn = 0.0f;
-        const float d = half_bits_to_float(u16(o));
-        if constexpr (WT == KQ_Q8_0) {
-          c0 = make_uint4(u32(o + 2), u32(o + 6), u32(o + 10), u32(o + 14));
-          c1 = make_uint4(u32(o + 18), u32(o + 22), u32(o + 26), u32(o + 30));
-        } else {
-          const int q = o + (WT == KQ_Q4_0 ? 2 : 4);
-          if constexpr (WT == KQ_Q4_1) mn = half_bits_to_float(u16(o + 2));
-          const uint32_t a0 = u32(q), a1 = u32(q + 4), a2 = u32(q + 8), a3 = u32(q + 12);
-          c0 = make_uint4(a0 & 0x0F0F0F0Fu, a1 & 0x0F0F0F0Fu, a2 & 0x0F0F0F0Fu, a3 & 0x0F0F0F0Fu);
-          c1 = make_uint4((a0 >> 4) & 0x0F0F0F0Fu, (a1 >> 4) & 0x0F0F0F0Fu, (a2 >> 4) & 0x0F0F0F0Fu,
-                          (a3 >> 4) & 0x0F0F0F0Fu);
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const int o = jj * T::BB;  // compile-time after unrolling
+          const int j = 2 * hh + jj;
+          uint4 c0, c1;
+          float mn = 0.0f;
+          const float d = half_bits_to_float(u16(o));
+          if constexpr (WT == KQ_Q8_0) {
+            c0 = make_uint4(u32(o + 2), u32(o + 6), u32(o + 10), u32(o + 14));
+            c1 = make_uint4(u32(o + 18), u32(o + 22), u32(o + 26), u32(o + 30));
+          } else {
+            const int q = o + (WT == KQ_Q4_0 ? 2 : 4);
+            if constexpr (WT == KQ_Q4_1) mn = half_bits_to_float(u16(o + 2));
+            const uint32_t a0 = u32(q), a1 = u32(q + 4), a2 = u32(q + 8), a3 = u32(q + 12);
+            c0 = make_uint4(a0 & 0x0F0F0F0Fu, a1 & 0x0F0F0F0Fu, a2 & 0x0F0F0F0Fu, a3 & 0x0F0F0F0Fu);
+            c1 = make_uint4((a0 >> 4) & 0x0F0F0F0Fu, (a1 >> 4) & 0x0F0F0F0Fu, (a2 >> 4) & 0x0F0F0F0Fu,
+                            (a3 >> 4) & 0x0F0F0F0Fu);
+          }
+          // block j = bytes 32j .. 32j+31 of the 128-byte row: chunks 2j, 2j+1
+          *reinterpret_cast<uint4*>(wt + sw128_off(crow, 2 * j)) = c0;
+          *reinterpret_cast<uint4*>(wt + sw128_off(crow, 2 * j + 1)) = c1;
+          wsc[j * TN + crow] = d;
+          if constexpr (T::kHasMin) wsc[KSUB * TN + j * TN + crow] = mn;
         }
-        *reinterpret_cast<uint4*>(wt + (jj == 0 ? coff0 : coff2)) = c0;
-        *reinterpret_cast<uint4*>(wt + (jj == 0 ? coff1 : coff3)) = c1;
-        const int j = 2 * chalf + jj;
-        wsc[j * TN + crow] = d;
-        if constexpr (T::kHasMin) wsc[KSUB * TN + j * TN + crow] = mn;
       }
+      }
+
+      __syncwarp();
+      if (sub == 1 && lane == 0) mbar_arrive(&raw_empty[rs]);  // both stages of the raw box are read
       fence_proxy_async_smem();  // generic-proxy writes -> tensor-core reads
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&w_full[ws]);
-        if (sub == 1) mbar_arrive(&raw_empty[rs]);  // both halves of the raw stage are converted
-      }
-    };
-
-    // every TMEM buffer starts free, preset to the bias
-    for (int b = 0; b < NBUF; ++b)
-      for (int c32 = 0; c32 < kEpiCols / 32; ++c32)
-        tmem_st32_const(tmem_base + lane_addr + b * TN + cg * kEpiCols + 32 * c32, kBias);
-    tmem_st_wait();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) {
-      for (int b = 0; b < NBUF; ++b) mbar_arrive(&tm_empty[b]);
+      if (lane == 0) mbar_arrive(&w_full[ws]);
     }
-
-    if (total > 0) convert(0);
-    float acc[kEpiCols];  // fp32 accumulators
-    int ib = 0;
-    for (int es = 0; es < total; ++es) {
-      if (es + 1 < total) convert(es + 1);
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - kWarpEpi;          // 0..15
+    const int quarter = warp & 3;            // TMEM lane quarter this warp may access
+    const int cg = ew >> 2;                  // column group of kEpiCols
+    const int row = quarter * 32 + lane;     // token row in the tile
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    // fp32 accumulators as packed pairs. TMEM is read in halves of kHalf
+    // columns, one half ahead: the load of the next half (of this block, or
+    // the first half of the next block) is in flight while the current half's
+    // math runs; a buffer goes back to the MMA as soon as both halves are in
+    // registers.
+    constexpr int NP = kEpiCols / 2;
+    uint64_t acc[NP];
+    uint32_t va[kHalf], vb[kHalf];
+    const int nblk = total * KSUB;
+    auto tm_addr = [&](int gb, int h) -> uint32_t {
+      return tmem_base + lane_addr + (uint32_t)((gb % NBUF) * TN + cg * kEpiCols + kHalf * h);
+    };
+    auto wait_full = [&](int gb) {
+      mbar_wait_or_poison(&tm_full[gb % NBUF], (gb / NBUF) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+      tc_fence_after();
+    };
+    if (nblk > 0) {
+      wait_full(0);
+      tmem_ldh(tm_addr(0, 0), va);
+      tmem_ld_wait();
+    }
+    for (int gb = 0; gb < nblk; ++gb) {
+      const int es = gb / KSUB, j = gb % KSUB;
       const int s = es % spt;
-      const int t = (int)blockIdx.x + (es / spt) * (int)gridDim.x;
-      if (s == 0) {
-#pragma unroll
-        for (int c = 0; c < kEpiCols; ++c) acc[c] = 0.0f;
-      }
       const int as = es % SA, ws = es % SWS;
-      mbar_wait_or_poison(&act_full[as], (es / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-      mbar_wait_or_poison(&w_full[ws], (es / SWS) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-      const float2* asc = reinterpret_cast<const float2*>(smem + T::OFF_ASC + as * T::ASC_STAGE) + row * KSUB;
+      if (j == 0) {
+        if (s == 0) {
+#pragma unroll
+          for (int c = 0; c < NP; ++c) acc[c] = 0ull;
+        }
+        mbar_wait_or_poison(&act_full[as], (es / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+        mbar_wait_or_poison(&w_full[ws], (es / SWS) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+      }
+      const float2 dsj = reinterpret_cast<const float2*>(smem + T::OFF_ASC + as * T::ASC_STAGE)[row * KSUB + j];
+      const float d = round22(dsj.x);
+      const uint64_t d2 = pk2(d, d);
+      const uint64_t c2 = pk2(-kBiasF * d, -kBiasF * d);
+      const uint64_t ms8 = pk2(-8.0f * dsj.y, -8.0f * dsj.y);
+      const uint64_t sy2 = pk2(dsj.y, dsj.y);
       const float* wsc = reinterpret_cast<const float*>(smem + T::OFF_WSC + ws * T::WSC_STAGE);
-#pragma unroll 1
-      for (int j = 0; j < KSUB; ++j, ++ib) {
-        const int buf = ib % NBUF;
-        const float2 dsj = asc[j];
-        const float d = round22(dsj.x);
-        const float ncs = -kBiasF * d;
-        const float ms8 = -8.0f * dsj.y;
-        const float sy = dsj.y;
-        const float* dw = wsc + j * TN + cg * kEpiCols;
-        const float* mw = wsc + KSUB * TN + j * TN + cg * kEpiCols;
-        mbar_wait_or_poison(&tm_full[buf], (ib / NBUF) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-        tc_fence_after();
-        const uint32_t taddr = tmem_base + lane_addr + buf * TN + cg * kEpiCols;
-        // 16 columns per TMEM round trip; re-arm the bias (asynchronously) and
-        // hand the buffer back after the math
+      const ulonglong2* dw = reinterpret_cast<const ulonglong2*>(wsc + j * TN + cg * kEpiCols);
+      const ulonglong2* mw = reinterpret_cast<const ulonglong2*>(wsc + KSUB * TN + j * TN + cg * kEpiCols);
+
+      auto math = [&](const uint32_t(&v)[kHalf], int h) {
 #pragma unroll
-        for (int h = 0; h < kEpiCols / 16; ++h) {
-          uint32_t v[16];
-          tmem_ld16(taddr + 16 * h, v);
-          tmem_ld_wait();
-          if (h == kEpiCols / 16 - 1) {
-#pragma unroll
-            for (int c32 = 0; c32 < kEpiCols / 32; ++c32) tmem_st32_const(taddr + 32 * c32, kBias);
+        for (int q = 0; q < kHalf / 4; ++q) {  // 4 columns per step
+          const ulonglong2 w4 = dw[(kHalf / 4) * h + q];
+          const int c = (kHalf / 2) * h + 2 * q;  // pair index
+          uint64_t u0 = fma2(pk2u(v[4 * q], v[4 * q + 1]), d2, c2);  // d_a * sumi (exact)
+          uint64_t u1 = fma2(pk2u(v[4 * q + 2], v[4 * q + 3]), d2, c2);
+          if constexpr (WT == KQ_Q4_0) {
+            u0 = add2(u0, ms8);  // d_a sumi - 8 s_a
+            u1 = add2(u1, ms8);
           }
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float4 w4 = reinterpret_cast<const float4*>(dw + 16 * h)[q];  // scales of 4 columns (broadcast)
-            const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
-            float mv[4] = {0.f, 0.f, 0.f, 0.f};
-            if constexpr (WT == KQ_Q4_1) {
-              const float4 m4 = reinterpret_cast<const float4*>(mw + 16 * h)[q];
-              mv[0] = m4.x; mv[1] = m4.y; mv[2] = m4.z; mv[3] = m4.w;
-            }
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int c = 16 * h + 4 * q + e;
-              const float pr = fmaf(__uint_as_float(v[4 * q + e]), d, ncs);  // d_a * sumi
-              if constexpr (WT == KQ_Q8_0) {
-                acc[c] = fmaf(pr, wv[e], acc[c]);
-              } else if constexpr (WT == KQ_Q4_0) {
-                acc[c] = fmaf(pr + ms8, wv[e], acc[c]);  // d_w * (d_a sumi - 8 s_a)
-              } else {
-                acc[c] = fmaf(mv[e], sy, fmaf(pr, wv[e], acc[c]));  // d_w d_a sumi + m_w s_a
-              }
-            }
+          acc[c] = fma2(u0, w4.x, acc[c]);
+          acc[c + 1] = fma2(u1, w4.y, acc[c + 1]);
+          if constexpr (WT == KQ_Q4_1) {
+            const ulonglong2 m4 = mw[(kHalf / 4) * h + q];
+            acc[c] = fma2(m4.x, sy2, acc[c]);  // + m_w s_a
+            acc[c + 1] = fma2(m4.y, sy2, acc[c + 1]);
           }
         }
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tm_empty[buf]);
-      }
+      };
+
+      // half 0 (in va): prefetch half 1, compute, then release the buffer
+      tmem_ldh(tm_addr(gb, 1), vb);
+      math(va, 0);
+      tmem_ld_wait();
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&act_empty[as]);
-        mbar_arrive(&w_empty[ws]);
+      if (lane == 0) mbar_arrive(&tm_empty[gb % NBUF]);
+      // half 1 (in vb): prefetch the next block's half 0
+      if (gb + 1 < nblk) {
+        wait_full(gb + 1);
+        tmem_ldh(tm_addr(gb + 1, 0), va);
       }
-      if (s == spt - 1) {
-        // ---- store this tile's rows ----
-        const int m0 = (t % p.num_m_tiles) * TM, n0 = (t / p.num_m_tiles) * TN;
-        const int m = m0 + row;
-        const int nc0 = n0 + cg * kEpiCols;
-        if (m < p.M) {
-          float* o = p.out + (size_t)m * p.N + nc0;
-          if (nc0 + kEpiCols <= p.N && (p.N & 3) == 0) {
+      math(vb, 1);
+      tmem_ld_wait();
+
+      if (j == KSUB - 1) {
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&act_empty[as]);
+          mbar_arrive(&w_empty[ws]);
+        }
+        if (s == spt - 1) {
+          // ---- store this tile's rows ----
+          const int t = (int)blockIdx.x + (es / spt) * (int)gridDim.x;
+          const int m0 = (t % p.num_m_tiles) * TM, n0 = (t / p.num_m_tiles) * TN;
+          const int m = m0 + row;
+          const int nc0 = n0 + cg * kEpiCols;
+          if (m < p.M) {
+            float* o = p.out + (size_t)m * p.N + nc0;
+            if (nc0 + kEpiCols <= p.N && (p.N & 3) == 0) {
 #pragma unroll
-            for (int c = 0; c < kEpiCols; c += 4)
-              *reinterpret_cast<float4*>(o + c) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
-          } else {
+              for (int c = 0; c < NP; c += 2) {
+                const float2 a = upk2(acc[c]), b = upk2(acc[c + 1]);
+                *reinterpret_cast<float4*>(o + 2 * c) = make_float4(a.x, a.y, b.x, b.y);
+              }
+            } else {
 #pragma unroll
-            for (int c = 0; c < kEpiCols; ++c)
-              if (nc0 + c < p.N) o[c] = acc[c];
+              for (int c = 0; c < NP; ++c) {
+                const float2 a = upk2(acc[c]);
+                if (nc0 + 2 * c < p.N) o[2 * c] = a.x;
+                if (nc0 + 2 * c + 1 < p.N) o[2 * c + 1] = a.y;
+              }
+            }
           }
         }
       }
@@ -527,17 +510,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---- host side -----------------------------------------------------------------
-bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t dim0, uint64_t dim1,
-                uint64_t stride1_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle swz) {
-  cuuint64_t dims[2] = {dim0, dim1};
-  cuuint64_t strides[1] = {stride1_bytes};
-  cuuint32_t box[2] = {box0, box1};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode_tiled(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
-                                      CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
 
 template <int WT>
 kq_status_t launch_tc(const void* w, Act8 act, float* out, int M, int N, int K, bool pdl, cudaStream_t s, int* err) {

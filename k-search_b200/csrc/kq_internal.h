@@ -33,7 +33,7 @@ void* tensor_map_encoder();
 // shrunk). The buffer is ordered on `stream`: growing it synchronises the
 // device before the old buffer is freed. Returns nullptr (and records the
 // error) on allocation failure.
-enum WsSlot { WS_ACT = 0, WS_FA = 1, WS_MOE = 2, WS_MOE2 = 3, WS_NSLOTS = 8 };
+enum WsSlot { WS_ACT = 0, WS_FA = 1, WS_MOE = 2, WS_MOE2 = 3, WS_A16 = 4, WS_NSLOTS = 8 };
 void* workspace(WsSlot slot, size_t bytes);
 // Device error word of the current device (zeroed at allocation).
 int* device_error_word();
@@ -78,6 +78,10 @@ kq_status_t launch_gemv(int wtype, const void* w, Act8 act, float* out, int M, i
 // gemm_tc.cu (M > 8, K % 256 == 0, 16-byte aligned operands): tcgen05 int8 MMA
 bool gemm_tc_supported(int wtype, int M, int N, int K, const void* w, Act8 act);
 kq_status_t launch_gemm_tc(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, bool pdl,
+                           cudaStream_t s, int* err = nullptr);
+// gemm_hx.cu (M > 8, K % 256 == 0: fp16-dequantised operands, tcgen05 kind::f16)
+bool gemm_hx_supported(int wtype, int M, int N, int K, const void* w, Act8 act);
+kq_status_t launch_gemm_hx(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, bool pdl,
                            cudaStream_t s, int* err = nullptr);
 // gemm_simt.cu (any shape; the generic path)
 kq_status_t launch_gemm_simt(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, cudaStream_t s);
