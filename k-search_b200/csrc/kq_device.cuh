@@ -92,6 +92,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-suspending probe of a phase.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -100,10 +113,16 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 // Bounded wait for the phase with the given parity to complete. Returns false
 // (and records `code`) once kWaitLimitNs of wall time has passed: any legal
-// wait in these kernels ends within microseconds.
+// wait in these kernels ends within microseconds. A short spin on the
+// non-suspending probe comes first: a suspended try_wait resumes about 90
+// cycles later than a spinning probe sees the phase complete, and most
+// hand-offs here complete within a few hundred cycles.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr int kSpinProbes = 32;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
-  if (mbar_try_wait(bar, parity)) return true;
+#pragma unroll 1
+  for (int i = 0; i < kSpinProbes; ++i)
+    if (mbar_test_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
