@@ -305,6 +305,53 @@ def cpu_fa_baseline(cfg: dict, seconds: float = 10.0) -> dict:
             "sample": f"{nseq} of {B} sequences decoded one by one with the numpy oracle, {t_all:.2f} s"}
 
 
+def cpu_moe_baseline(cfg: dict, seconds: float = 12.0) -> dict:
+    """The MoE step on the host cores: the reference's C++ W4A8 GEMM
+    (gemm_w4a8_reference through oracle/_ref) run through one expert's gate,
+    up and down projections for a bounded number of routed rows; the rate is
+    the same TOPS metric (2 * rows * 3 * H * I per sample)."""
+    from oracle import native, quant as Q
+
+    H, I = cfg["H"], cfg["I"]
+    threads = cpu_threads()
+    key = ("moe", H, I)
+    if key not in _CPU_INPUTS:
+        rng = np.random.default_rng(0)
+        _CPU_INPUTS[key] = (Q.make_q4_0_blocks(rng, I, H), Q.make_q4_0_blocks(rng, I, H),
+                            Q.make_q4_0_blocks(rng, H, I), rng.standard_normal((64, H)).astype(np.float32))
+    wg, wu, wd, x = _CPU_INPUTS[key]
+    if native.available():
+        kind = "reference"
+
+        def run(rows):
+            a = native.quantize_q8_1(x[:rows], threads)
+            g = native.gemm("q4_0", wg, a, rows, I, H, threads)
+            u = native.gemm("q4_0", wu, a, rows, I, H, threads)
+            h = (Q.silu(g) * u).astype(np.float32)
+            return native.gemm("q4_0", wd, native.quantize_q8_1(h, threads), rows, H, I, threads)
+    else:
+        kind = "port"
+
+        def run(rows):
+            g = Q.gemm_f32act("q4_0", wg, x[:rows], rows, I, H, Q.SUM_DQ)
+            u = Q.gemm_f32act("q4_0", wu, x[:rows], rows, I, H, Q.SUM_DQ)
+            h = (Q.silu(g) * u).astype(np.float32)
+            return Q.gemm_f32act("q4_0", wd, h, rows, H, I, Q.SUM_DQ)
+    rows = 1
+    t0 = time.perf_counter()
+    run(rows)
+    dt = time.perf_counter() - t0
+    while rows < x.shape[0] and dt * 2 < seconds:
+        rows = min(x.shape[0], rows * 2)
+        t0 = time.perf_counter()
+        run(rows)
+        dt = time.perf_counter() - t0
+    ops = 2.0 * rows * 3 * H * I
+    return {"value": ops / dt / 1e12, "unit": "TOPS", "cores": threads, "kind": kind,
+            "sample": f"{rows} routed rows through one expert (gate, up, down; H={H} I={I}), q8_1 quantise + "
+                      f"W4A8 GEMMs, {dt:.2f} s"}
+
+
 # ---------------------------------------------------------------------------
 # GPU arms
 # ---------------------------------------------------------------------------
@@ -604,6 +651,13 @@ def reference_arm(args, cfg):
             if i >= args.warmup:
                 vals.append(cb["value"])
         unit, metric = "tok/s", "q8_0-KV flash-decode tok/s"
+    elif cfg["kind"] == "moe":
+        vals, cb = [], None
+        for i in range(args.warmup + args.steps):
+            cb = cpu_moe_baseline(cfg, seconds=budget)
+            if i >= args.warmup:
+                vals.append(cb["value"])
+        unit, metric = "TOPS", "MoE W4A8 GEMM TOPS (q4_0 x q8_1, grouped)"
     else:
         vals, cb = [], None
         for i in range(args.warmup + args.steps):
@@ -642,7 +696,7 @@ def main():
         cpu = (lambda: cpu_fa_baseline(cfg)) if (rank == 0 and world == 1) else None
     elif cfg["kind"] == "moe":
         line = bench_moe(args, cfg, rank, world)
-        cpu = None
+        cpu = (lambda: cpu_moe_baseline(cfg)) if (rank == 0 and world == 1) else None
     else:
         line = bench_gemm(args, cfg, rank, world)
         cpu = (lambda: cpu_gemm_baseline(cfg)) if (rank == 0 and world == 1) else None
