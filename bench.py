@@ -16,8 +16,10 @@ size exceeds 2x the L2 cache, so every step reads its operands from HBM.
 
 Multi-GPU (torchrun, one rank per GPU): weak scaling of the N-sharded GEMM.
 Rank r holds the weight rows of output columns [r*N, (r+1)*N) of an
-[M, world*N] product; each timed step is the local operator plus the NCCL
-all-gather that assembles the full output on every rank (eager, event-timed).
+[M, world*N] product; each timed step is the operator whose epilogue stores
+those columns into every rank's full-width output over NVLink (CUDA IPC peer
+mappings), plus a one-element NCCL all-reduce that orders the stores (eager,
+event-timed).
 --config 3 (decode) shards whole sequences (no collective); --config 4 (MoE)
 runs expert-parallel with all-to-all dispatch and combine.
 
@@ -391,19 +393,16 @@ def bench_gemm(args, cfg, rank, world):
         ms, clk = graph_time_ms(step, args.steps, args.warmup, world, clocks)
     else:
         # rank r holds output columns [r*N, (r+1)*N) of an [M, world*N] product
-        # (its own weight shard); each step ends with the all-gather that
-        # assembles the full [M, world*N] output on every rank.
-        import torch.distributed as dist
-        full = [torch.empty((M, world * N), dtype=torch.float32, device=dev) for _ in range(2)]
-        gath = torch.empty((world * M, N), dtype=torch.float32, device=dev)
+        # (its own weight shard); each step's epilogue stores its columns into
+        # every rank's full-width output over NVLink (CUDA IPC mappings), then
+        # a one-element all-reduce orders those stores (kq.dist.NShardedGemm p2p).
+        from kq import dist as kd
+        sharded_t = kd.NShardedGemm(ws[0], world * N, K, wtype=wt, act_mode=cfg["act"], align=N, mode="p2p")
 
         def step(i):
             j = i % nsets
-            sp = torch.cuda.current_stream().cuda_stream
-            _lib.check(L.kq_gemm_f32act(wtc, ws[j].data_ptr(), xs[j].data_ptr(), outs[j].data_ptr(), M, N, K,
-                                        act_mode, sp), "kq_gemm_f32act")
-            dist.all_gather_into_tensor(gath, outs[j])
-            full[i % 2].view(M, world, N).copy_(gath.view(world, M, N).permute(1, 0, 2))
+            sharded_t.weight = ws[j]
+            sharded_t(xs[j])
 
         ms, clk = eager_time_ms(step, args.steps, args.warmup, world, clocks)
     ops = 2.0 * M * N * K
@@ -434,7 +433,8 @@ def bench_gemm(args, cfg, rank, world):
     # [M, world*N] output read back on every rank.
     from kq import dist as kd
     NT = world * N
-    sharded = kd.NShardedGemm(ws[0], NT, K, wtype=wt, act_mode=cfg["act"], align=N) if world > 1 else None
+    sharded = (kd.NShardedGemm(ws[0], NT, K, wtype=wt, act_mode=cfg["act"], align=N, mode="p2p")
+               if world > 1 else None)
     xh = [torch.randn((M, K), generator=g, dtype=torch.float32).pin_memory() for _ in range(2)]
     oh = [torch.empty((M, NT), dtype=torch.float32).pin_memory() for _ in range(2)]
     xd = torch.empty((M, K), dtype=torch.float32, device=dev)
@@ -460,6 +460,9 @@ def bench_gemm(args, cfg, rank, world):
     e1.record(stream)
     torch.cuda.synchronize()
     ems = max_over_ranks(e0.elapsed_time(e1), world)
+    if world > 1:  # collective teardown of the peer-mapped outputs (same order on every rank)
+        sharded_t.close()
+        sharded.close()
     e2e = {"value": world * ops * args.steps / (ems * 1e-3) / 1e12, "unit": "TOPS",
            "h2d_bytes_per_step": M * K * 4, "d2h_bytes_per_step": M * NT * 4,
            "api": "kq.gemm_f32act" if world == 1 else "kq.dist.NShardedGemm"}
@@ -491,7 +494,8 @@ def bench_gemm(args, cfg, rank, world):
                    "l2": f"{nsets} rotating input sets ({nsets * step_bytes / 1e6:.0f} MB > 2x L2)",
                    "parallelism": ("single GPU" if world == 1 else
                                    f"N-sharded x{world}: rank r computes columns [r*N, (r+1)*N) of an "
-                                   f"[M, {world}*N] product, NCCL all-gather of the output each step")},
+                                   f"[M, {world}*N] product; its epilogue stores them into every rank's "
+                                   f"output over NVLink (CUDA IPC), then a 1-element NCCL all-reduce")},
         "roofline": roof,
         "e2e": e2e,
         "gpu_launches": launches_per_step * args.steps,

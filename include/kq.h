@@ -140,6 +140,35 @@ kq_status_t kq_gemm_f32act(int wtype, const void* w, const float* x, float* out,
 kq_status_t kq_gemm_f32act_noalloc(int wtype, const void* w, const float* x, float* out, int M, int N, int K,
                                    int act_mode, kq_stream_t stream);
 
+/* The fused fp32-activation GEMM writing each output element to several
+ * destinations: element (m, n) goes to outs[d][m * ldo + col0 + n] for every
+ * d < n_out (1 <= n_out <= 8). For N-sharded multi-GPU use: a rank computes
+ * its columns and stores them straight into every rank's full-width output
+ * (pointers to peer memory mapped with CUDA IPC); the epilogue ends with a
+ * system-scope fence, so a barrier after the call (stream-ordered) makes the
+ * peers' data visible. Supported on the GEMV (M <= 8) and tensor-core
+ * (M > 8, K % 256 == 0) paths; other shapes return KQ_ERR_UNSUPPORTED. ldo,
+ * col0 and every pointer must keep 16-byte alignment for the vector stores
+ * (ldo and col0 multiples of 4). No reference counterpart: the reference is
+ * single-device. */
+kq_status_t kq_gemm_f32act_scatter(int wtype, const void* w, const float* x, float* const* outs, int n_out, int ldo,
+                                   int col0, int M, int N, int K, int act_mode, kq_stream_t stream);
+
+/* Peer-mapped buffers for kq_gemm_f32act_scatter (CUDA IPC, one process per
+ * GPU on one node). kq_peer_alloc allocates `bytes` on the current device and
+ * writes its 64-byte IPC handle; another process opens it with kq_peer_open
+ * (the mapping is usable from that process's current device) and releases it
+ * with kq_peer_close; the owner frees it with kq_peer_free. */
+kq_status_t kq_peer_alloc(size_t bytes, void** ptr, void* handle64);
+kq_status_t kq_peer_open(const void* handle64, void** ptr);
+kq_status_t kq_peer_close(void* ptr);
+kq_status_t kq_peer_free(void* ptr);
+/* Strided device copy (rows of `width_bytes`, `height` rows), either side may
+ * be a peer mapping: the push of one rank's column block into a peer's
+ * full-width output. Stream-ordered on `stream`. */
+kq_status_t kq_copy_2d(void* dst, size_t dst_pitch, const void* src, size_t src_pitch, size_t width_bytes,
+                       size_t height, kq_stream_t stream);
+
 /* Weights x activations already in the kernels' staging layout: int8 codes
  * a_qs[M, K] (row stride K bytes, 16-byte aligned) and one (d, s) fp32 pair
  * per 32-block a_ds[M, K/32, 2]. For callers that quantise inside their own

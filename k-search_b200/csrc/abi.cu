@@ -243,6 +243,74 @@ kq_status_t kq_gemm_f32act(int wtype, const void* w, const float* x, float* out,
   return dispatch_gemm(wtype, w, act, out, M, N, K, s, true);
 }
 
+kq_status_t kq_peer_alloc(size_t bytes, void** ptr, void* handle64) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  if (!ptr || !handle64 || bytes == 0) return fail(KQ_ERR_INVALID, "peer_alloc: bad arguments");
+  *ptr = nullptr;
+  void* p = nullptr;
+  kq_status_t st = check_cuda(cudaMalloc(&p, bytes), "peer_alloc cudaMalloc");
+  if (st) return st;
+  cudaIpcMemHandle_t h;
+  st = check_cuda(cudaIpcGetMemHandle(&h, p), "cudaIpcGetMemHandle");
+  if (st) {
+    cudaFree(p);
+    return st;
+  }
+  std::memcpy(handle64, &h, sizeof(h));
+  *ptr = p;
+  return KQ_OK;
+}
+
+kq_status_t kq_peer_open(const void* handle64, void** ptr) {
+  if (!ptr || !handle64) return fail(KQ_ERR_INVALID, "peer_open: bad arguments");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle64, sizeof(h));
+  return check_cuda(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+}
+
+kq_status_t kq_peer_close(void* ptr) { return check_cuda(cudaIpcCloseMemHandle(ptr), "cudaIpcCloseMemHandle"); }
+
+kq_status_t kq_peer_free(void* ptr) { return check_cuda(cudaFree(ptr), "peer_free cudaFree"); }
+
+kq_status_t kq_copy_2d(void* dst, size_t dst_pitch, const void* src, size_t src_pitch, size_t width_bytes,
+                       size_t height, kq_stream_t stream) {
+  if (width_bytes == 0 || height == 0) return KQ_OK;
+  if (!dst || !src || width_bytes > dst_pitch || width_bytes > src_pitch) return fail(KQ_ERR_INVALID, "copy_2d: bad arguments");
+  return check_cuda(cudaMemcpy2DAsync(dst, dst_pitch, src, src_pitch, width_bytes, height, cudaMemcpyDeviceToDevice,
+                                      static_cast<cudaStream_t>(stream)),
+                    "cudaMemcpy2DAsync");
+}
+
+kq_status_t kq_gemm_f32act_scatter(int wtype, const void* w, const float* x, float* const* outs, int n_out, int ldo,
+                                   int col0, int M, int N, int K, int act_mode, kq_stream_t stream) {
+  if (n_out < 1 || n_out > kMaxOut || !outs) return fail(KQ_ERR_INVALID, "scatter: n_out=%d (1..%d)", n_out, kMaxOut);
+  kq_status_t st = check_gemm_args(wtype, w, x, outs[0], M, N, K);
+  if (st) return st;
+  if (act_mode < KQ_ACT_SUM_X || act_mode > KQ_ACT_F32) return fail(KQ_ERR_INVALID, "unknown activation mode %d", act_mode);
+  if (col0 < 0 || ldo < col0 + N) return fail(KQ_ERR_INVALID, "scatter: ldo=%d col0=%d N=%d (ldo >= col0 + N)", ldo, col0, N);
+  OutSpec o{};
+  for (int d = 0; d < n_out; ++d) {
+    if (!outs[d] || !aligned(outs[d], 16)) return fail(KQ_ERR_INVALID, "scatter: destination %d null or unaligned", d);
+    o.ptr[d] = outs[d];
+  }
+  o.n_out = n_out;
+  o.ld = ldo;
+  o.col0 = col0;
+  if ((long long)M * N == 0) return KQ_OK;
+  if (K == 0) return fail(KQ_ERR_UNSUPPORTED, "scatter: K == 0");
+  if (!aligned(x, 16)) return fail(KQ_ERR_INVALID, "activations must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  void* ws = workspace(WS_ACT, act8_bytes(M, K));
+  if (!ws) return KQ_ERR_NOMEM;
+  Act8 act = act8_view(ws, M, K);
+  const bool gemv = gemv_supported(wtype, M, N, K) && aligned(w, 16);
+  const bool tc = !gemv && gemm_tc_supported(wtype, M, N, K, w, act);
+  if (!gemv && !tc) return fail(KQ_ERR_UNSUPPORTED, "scatter: shape M=%d N=%d K=%d has no scatter epilogue", M, N, K);
+  st = launch_quantize_act(x, act, M, K, act_mode, s);
+  if (st) return st;
+  return gemv ? launch_gemv(wtype, w, act, o, M, N, K, true, s) : launch_gemm_tc(wtype, w, act, o, M, N, K, true, s);
+}
+
 kq_status_t kq_mul_mat_q8x(int wtype, const void* w, const int8_t* a_qs, const float* a_ds, float* out, int M, int N,
                            int K, kq_stream_t stream) {
   kq_status_t st = check_gemm_args(wtype, w, a_qs, out, M, N, K);

@@ -185,7 +185,7 @@ __device__ __forceinline__ void tmem_ldh(uint32_t taddr, uint32_t (&v)[NC]) {
 struct TcParams {
   int M, N, K, nb;
   int num_m_tiles, num_tiles;
-  float* out;
+  OutSpec out;
   int* err;
 };
 
@@ -203,7 +203,7 @@ __device__ __forceinline__ uint64_t sw128_desc_rep8(uint32_t saddr) {
 template <int WT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_act, const __grid_constant__ CUtensorMap map_asc,
-                   const __grid_constant__ CUtensorMap map_raw, TcParams p) {
+                   const __grid_constant__ CUtensorMap map_raw, const __grid_constant__ TcParams p) {
   using T = TcTraits<WT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -480,25 +480,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int m = m0 + row;
           const int nc0 = n0 + cg * kEpiCols;
           if (m < p.M) {
-            float* o = p.out + (size_t)m * p.N + nc0;
-            if (nc0 + kEpiCols <= p.N && (p.N & 3) == 0) {
+            const size_t off = (size_t)m * p.out.ld + p.out.col0 + nc0;
+            const bool vec = nc0 + kEpiCols <= p.N && ((p.out.ld | p.out.col0) & 3) == 0;
+            for (int dd = 0; dd < p.out.n_out; ++dd) {
+              float* o = p.out.ptr[dd] + off;
+              if (vec) {
 #pragma unroll
-              for (int c = 0; c < NP; c += 2) {
-                const float2 a = upk2(acc[c]), b = upk2(acc[c + 1]);
-                *reinterpret_cast<float4*>(o + 2 * c) = make_float4(a.x, a.y, b.x, b.y);
-              }
-            } else {
+                for (int c = 0; c < NP; c += 2) {
+                  const float2 a = upk2(acc[c]), b = upk2(acc[c + 1]);
+                  *reinterpret_cast<float4*>(o + 2 * c) = make_float4(a.x, a.y, b.x, b.y);
+                }
+              } else {
 #pragma unroll
-              for (int c = 0; c < NP; ++c) {
-                const float2 a = upk2(acc[c]);
-                if (nc0 + 2 * c < p.N) o[2 * c] = a.x;
-                if (nc0 + 2 * c + 1 < p.N) o[2 * c + 1] = a.y;
+                for (int c = 0; c < NP; ++c) {
+                  const float2 a = upk2(acc[c]);
+                  if (nc0 + 2 * c < p.N) o[2 * c] = a.x;
+                  if (nc0 + 2 * c + 1 < p.N) o[2 * c + 1] = a.y;
+                }
               }
             }
           }
         }
       }
     }
+    if (p.out.n_out > 1) __threadfence_system();  // peer stores visible before the host-side barrier
   }
 
   tc_fence_before();
@@ -512,7 +517,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---- host side -----------------------------------------------------------------
 
 template <int WT>
-kq_status_t launch_tc(const void* w, Act8 act, float* out, int M, int N, int K, bool pdl, cudaStream_t s, int* err) {
+kq_status_t launch_tc(const void* w, Act8 act, const OutSpec& out, int M, int N, int K, bool pdl, cudaStream_t s,
+                      int* err) {
   using T = TcTraits<WT>;
   const int nb = K / 32;
   CUtensorMap m_act, m_asc, m_raw;
@@ -567,6 +573,11 @@ bool gemm_tc_supported(int wtype, int M, int N, int K, const void* w, Act8 act) 
 }
 
 kq_status_t launch_gemm_tc(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, bool pdl,
+                           cudaStream_t s, int* err) {
+  return launch_gemm_tc(wtype, w, act, OutSpec::plain(out, N), M, N, K, pdl, s, err);
+}
+
+kq_status_t launch_gemm_tc(int wtype, const void* w, Act8 act, const OutSpec& out, int M, int N, int K, bool pdl,
                            cudaStream_t s, int* err) {
   switch (wtype) {
     case KQ_Q4_0: return launch_tc<KQ_Q4_0>(w, act, out, M, N, K, pdl, s, err);

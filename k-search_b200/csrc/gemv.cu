@@ -187,10 +187,17 @@ struct GemvCfg {
   static_assert(KS % 8 == 0, "K slice must keep 16-byte alignment");
 };
 
+// one output element to every destination of the epilogue
+__device__ __forceinline__ void put_out(const OutSpec& o, int m, int n, float v) {
+  const size_t off = (size_t)m * o.ld + o.col0 + n;
+  o.ptr[0][off] = v;
+  for (int d = 1; d < o.n_out; ++d) o.ptr[d][off] = v;
+}
+
 template <int WT, int MR, int BPL, int KW, int SR>
 __global__ void __launch_bounds__(32 * (kConsumerWarps + 1), 1)
     gemv_kernel(const uint8_t* __restrict__ w, const int8_t* __restrict__ aqs, const float2* __restrict__ ads,
-                float* __restrict__ out, int M, int N, int K, int* __restrict__ err) {
+                const __grid_constant__ OutSpec out, int M, int N, int K, int* __restrict__ err) {
   using C = GemvCfg<WT, MR, BPL, KW, SR>;
   constexpr int BB = C::BB;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -335,7 +342,7 @@ __global__ void __launch_bounds__(32 * (kConsumerWarps + 1), 1)
           const int idx = idx0 + c;
           const int rr = idx / MR, m = idx % MR;
           const int r = rg + rr * C::RG;
-          if (idx < C::V && r < rows && m < mvalid) out[(size_t)m * N + n0 + r] = part[c];
+          if (idx < C::V && r < rows && m < mvalid) put_out(out, m, n0 + r, part[c]);
         }
       }
     } else {
@@ -352,15 +359,17 @@ __global__ void __launch_bounds__(32 * (kConsumerWarps + 1), 1)
           for (int q = 0; q < KW; ++q) s += rbuf[q * C::VPOW + idx];
           const int rr = idx / MR, m = idx % MR;
           const int r = rg + rr * C::RG;
-          if (r < rows && m < mvalid) out[(size_t)m * N + n0 + r] = s;
+          if (r < rows && m < mvalid) put_out(out, m, n0 + r, s);
         }
       }
     }
   }
+  if (out.n_out > 1) __threadfence_system();  // peer stores visible before the host-side barrier
 }
 
 template <int WT, int MR, int BPL, int KW, int SR>
-kq_status_t launch_cfg(const void* w, Act8 act, float* out, int M, int N, int K, bool pdl, cudaStream_t s, int* err) {
+kq_status_t launch_cfg(const void* w, Act8 act, const OutSpec& out, int M, int N, int K, bool pdl, cudaStream_t s,
+                       int* err) {
   using C = GemvCfg<WT, MR, BPL, KW, SR>;
   auto kern = gemv_kernel<WT, MR, BPL, KW, SR>;
   static unsigned attr_done = 0;  // one bit per device ordinal
@@ -388,7 +397,8 @@ kq_status_t launch_cfg(const void* w, Act8 act, float* out, int M, int N, int K,
 }
 
 template <int WT>
-kq_status_t launch_wt(const void* w, Act8 act, float* out, int M, int N, int K, bool pdl, cudaStream_t s, int* err) {
+kq_status_t launch_wt(const void* w, Act8 act, const OutSpec& out, int M, int N, int K, bool pdl, cudaStream_t s,
+                      int* err) {
   constexpr int SR = (WT == KQ_Q8_0) ? 8 : 16;
   if (M <= 1) return launch_cfg<WT, 1, 4, 1, SR>(w, act, out, M, N, K, pdl, s, err);
   if (M <= 2) return launch_cfg<WT, 2, 4, 1, SR>(w, act, out, M, N, K, pdl, s, err);
@@ -404,6 +414,11 @@ bool gemv_supported(int wtype, int M, int N, int K) {
 }
 
 kq_status_t launch_gemv(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, bool pdl,
+                        cudaStream_t s, int* err) {
+  return launch_gemv(wtype, w, act, OutSpec::plain(out, N), M, N, K, pdl, s, err);
+}
+
+kq_status_t launch_gemv(int wtype, const void* w, Act8 act, const OutSpec& out, int M, int N, int K, bool pdl,
                         cudaStream_t s, int* err) {
   if (reinterpret_cast<uintptr_t>(w) % 16 != 0) return fail(KQ_ERR_INVALID, "gemv: weight pointer must be 16-byte aligned");
   switch (wtype) {

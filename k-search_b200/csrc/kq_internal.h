@@ -41,6 +41,26 @@ int* device_error_word();
 // ---- activation staging ---------------------------------------------------
 // Quantised activations as the kernels consume them: int8 codes row-major
 // [M, K] (row stride K bytes) and one float2 (d, s) per 32-block [M, K/32].
+// Output destinations of a GEMM epilogue: element (m, n) goes to
+// ptr[d][m * ld + col0 + n] for every d < n_out. One destination is the plain
+// case; several are the N-sharded multi-GPU case (this rank's columns written
+// into every rank's full-width output over peer mappings).
+constexpr int kMaxOut = 8;
+struct OutSpec {
+  float* ptr[kMaxOut];
+  int n_out;
+  int ld;
+  int col0;
+  static OutSpec plain(float* out, int N) {
+    OutSpec o{};
+    o.ptr[0] = out;
+    o.n_out = 1;
+    o.ld = N;
+    o.col0 = 0;
+    return o;
+  }
+};
+
 struct Act8 {
   int8_t* qs;
   float2* ds;
@@ -73,10 +93,14 @@ kq_status_t launch_silu_mul_quantize(const float* gate, const float* up, Act8 ac
 // gemv.cu (M <= 8, K % 256 == 0); `pdl` = launched as a programmatic
 // dependent of the preceding kernel on `s` (the activation producer).
 bool gemv_supported(int wtype, int M, int N, int K);
+kq_status_t launch_gemv(int wtype, const void* w, Act8 act, const OutSpec& out, int M, int N, int K, bool pdl,
+                        cudaStream_t s, int* err = nullptr);
 kq_status_t launch_gemv(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, bool pdl,
                         cudaStream_t s, int* err = nullptr);
 // gemm_tc.cu (M > 8, K % 256 == 0, 16-byte aligned operands): tcgen05 int8 MMA
 bool gemm_tc_supported(int wtype, int M, int N, int K, const void* w, Act8 act);
+kq_status_t launch_gemm_tc(int wtype, const void* w, Act8 act, const OutSpec& out, int M, int N, int K, bool pdl,
+                           cudaStream_t s, int* err = nullptr);
 kq_status_t launch_gemm_tc(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, bool pdl,
                            cudaStream_t s, int* err = nullptr);
 // gemm_hx.cu (M > 8, K % 256 == 0: fp16-dequantised operands, tcgen05 kind::f16)

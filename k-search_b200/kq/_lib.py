@@ -37,6 +37,12 @@ SIGNATURES = {
     "kq_gemm_f32act_noalloc": (_i, [_i, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "kq_mul_mat_q8x": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "kq_moe_q4_0": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp]),
+    "kq_gemm_f32act_scatter": (_i, [_i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),
+    "kq_peer_alloc": (_i, [ctypes.c_size_t, _vp, _vp]),
+    "kq_peer_open": (_i, [_vp, _vp]),
+    "kq_peer_close": (_i, [_vp]),
+    "kq_peer_free": (_i, [_vp]),
+    "kq_copy_2d": (_i, [_vp, ctypes.c_size_t, _vp, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t, _vp]),
     "kq_moe_route": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp]),
     "kq_moe_experts_q4_0": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp]),
     "kq_moe_combine": (_i, [_vp, _vp, _i, _i, _i, _vp, _vp]),

@@ -39,7 +39,7 @@ import torch
 import torch.distributed as dist
 
 __all__ = [
-    "init_from_env", "split_range", "NShardedGemm", "DecodeUnit", "plan_decode", "decode_shard",
+    "init_from_env", "split_range", "PeerBuffer", "NShardedGemm", "DecodeUnit", "plan_decode", "decode_shard",
     "gather_decode_outputs", "moe_expert_parallel", "expert_range",
 ]
 
@@ -82,6 +82,68 @@ def split_range(n: int, world: int, rank: int, align: int = 1) -> tuple[int, int
 # GEMM: output dimension N sharded, all-gather of output columns
 # ---------------------------------------------------------------------------
 
+class _CudaArray:
+    """Zero-copy view of a device allocation for torch.as_tensor."""
+
+    def __init__(self, ptr: int, numel: int):
+        self.__cuda_array_interface__ = {"shape": (numel,), "typestr": "<f4", "data": (ptr, False), "version": 3}
+
+
+class PeerBuffer:
+    """An fp32 buffer of `numel` elements on every rank, each mapped into every
+    other rank's address space with CUDA IPC (one process per GPU, one node).
+    `ptrs[r]` is rank r's buffer as seen from this process; `local` is this
+    rank's buffer as a tensor. The library owns the memory (kq_peer_alloc);
+    close() unmaps and frees it."""
+
+    def __init__(self, numel: int, device: torch.device, group=None):
+        import ctypes
+        from ._lib import check, lib
+
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self._group = group
+        self._lib, self._check = lib, check
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * 64)()
+        with torch.cuda.device(device):
+            check(lib().kq_peer_alloc(numel * 4, ctypes.byref(ptr), handle), "kq_peer_alloc")
+        self._own = ptr.value
+        handles = [bytes(handle)]
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+        self.ptrs: list[int] = []
+        self._opened: list[int] = []
+        with torch.cuda.device(device):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    self.ptrs.append(self._own)
+                    continue
+                p = ctypes.c_void_p()
+                hb = (ctypes.c_uint8 * 64).from_buffer_copy(h)
+                check(lib().kq_peer_open(hb, ctypes.byref(p)), "kq_peer_open")
+                self.ptrs.append(p.value)
+                self._opened.append(p.value)
+        self.local = torch.as_tensor(_CudaArray(self._own, numel), device=device)
+        self.numel = numel
+
+    def close(self) -> None:
+        """Collective: every rank unmaps its peers' buffers, then (after a
+        barrier, so no mapping of it remains) frees its own."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize()
+        for p in self._opened:
+            self._check(self._lib().kq_peer_close(p), "kq_peer_close")
+        self._opened = []
+        self.local = None
+        if self.world > 1:
+            dist.barrier(group=self._group)
+        self._check(self._lib().kq_peer_free(self._own), "kq_peer_free")
+        self._own = None
+
+
 def _default_gemm(weight, x, M, N, K, wtype, act_mode):
     from . import ops
     return ops.gemm_f32act(weight, x, M, N, K, wtype=wtype, act_mode=act_mode)
@@ -98,7 +160,7 @@ class NShardedGemm:
     is the per-rank compute (libkq by default)."""
 
     def __init__(self, weight_shard: torch.Tensor, N: int, K: int, wtype: str = "q4_0", act_mode: str = "sum_dq",
-                 group=None, align: int = 128, gemm_fn: Callable | None = None):
+                 group=None, align: int = 128, gemm_fn: Callable | None = None, mode: str = "nccl"):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -108,6 +170,12 @@ class NShardedGemm:
         self.n_max = max(c for _, c in self.splits)
         self.weight = weight_shard
         self.gemm_fn = gemm_fn or _default_gemm
+        if mode not in ("nccl", "p2p"):
+            raise ValueError("mode is 'nccl' or 'p2p'")
+        self.mode = mode
+        self._bufs: list[PeerBuffer] = []   # p2p: two full-width outputs, used alternately
+        self._buf_rows = 0
+        self._calls = 0
 
     @staticmethod
     def shard_weight(weight_full: torch.Tensor, N: int, world: int, rank: int, align: int = 128) -> torch.Tensor:
@@ -120,8 +188,75 @@ class NShardedGemm:
         M = x.shape[0]
         return self.gemm_fn(self.weight, x, M, self.n_local, self.K, self.wtype, self.act_mode)
 
+    def close(self) -> None:
+        for b in self._bufs:
+            b.close()
+        self._bufs = []
+
+    def _forward_p2p(self, x: torch.Tensor) -> torch.Tensor | None:
+        """The output lands in every rank's full-width buffer (CUDA IPC
+        mappings of two alternating buffers) without a collective on the data:
+        for GEMV shapes (M <= 8) the epilogue itself stores this rank's columns
+        into every rank's buffer (kq_gemm_f32act_scatter); for larger M the
+        epilogue writes them in place into the local buffer and one strided
+        copy per peer (copy engines over NVLink, one stream each) pushes the
+        block. A one-element all-reduce then orders all of it before anything
+        later on any rank's stream. The returned tensor stays valid until the
+        call after next. None if the shape has no scatter epilogue."""
+        from . import ops
+        from ._lib import KQError, check, lib
+        M = x.shape[0]
+        if M > self._buf_rows:
+            self.close()
+            self._buf_rows = max(M, 2 * self._buf_rows)
+            self._bufs = [PeerBuffer(self._buf_rows * self.N, x.device, self.group) for _ in range(2)]
+        buf = self._bufs[self._calls & 1]
+        s, c = self.splits[self.rank]
+        push = M > 8 and self.world > 1
+        dests = [buf.ptrs[self.rank]] if push else buf.ptrs
+        try:
+            ops.gemm_f32act_scatter(self.weight, x, dests, self.N, s, M, c, self.K, self.wtype, self.act_mode,
+                                    stream_of=x)
+        except KQError as e:
+            if e.status == 2:  # KQ_ERR_UNSUPPORTED: no scatter epilogue for this shape
+                return None
+            raise
+        self._calls += 1
+        if push and c > 0:
+            main = torch.cuda.current_stream(x.device)
+            if not hasattr(self, "_streams"):
+                self._streams = [torch.cuda.Stream(x.device) for _ in range(self.world)]
+            ready = torch.cuda.Event()
+            ready.record(main)
+            done = []
+            pitch = self.N * 4
+            for d in range(self.world):
+                if d == self.rank:
+                    continue
+                st = self._streams[d]
+                st.wait_event(ready)
+                check(lib().kq_copy_2d(buf.ptrs[d] + s * 4, pitch, buf.ptrs[self.rank] + s * 4, pitch, c * 4, M,
+                                       st.cuda_stream), "kq_copy_2d")
+                ev = torch.cuda.Event()
+                ev.record(st)
+                done.append(ev)
+            for ev in done:
+                main.wait_event(ev)
+        if self.world > 1:
+            if not hasattr(self, "_flag"):
+                self._flag = torch.zeros(1, dtype=torch.int32, device=x.device)
+            dist.all_reduce(self._flag, group=self.group)
+        return buf.local[:M * self.N].view(M, self.N)
+
     def forward(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         M = x.shape[0]
+        if self.mode == "p2p":
+            y = self._forward_p2p(x)
+            if y is not None:
+                if out is None:
+                    return y
+                out.copy_(y)
+                return out
         part = self.local(x)
         if self.world == 1:
             if out is None:

@@ -10,6 +10,7 @@ element count is N * K/32 * block_bytes), q8_1 activations likewise.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -99,6 +100,22 @@ def gemm_f32act(weight: torch.Tensor, activation: torch.Tensor, M: int, N: int, 
     check(lib().kq_gemm_f32act(wt, weight.data_ptr(), activation.data_ptr(), out.data_ptr(), M, N, K,
                                _act_mode(act_mode), _stream(weight)), "kq_gemm_f32act")
     return out
+
+
+def gemm_f32act_scatter(weight: torch.Tensor, activation: torch.Tensor, outs: list[int], ldo: int, col0: int, M: int,
+                        N: int, K: int, wtype="q4_0", act_mode="sum_dq", stream_of: torch.Tensor | None = None) -> None:
+    """kq_gemm_f32act_scatter: the fused GEMM writing element (m, n) to
+    outs[d] + (m * ldo + col0 + n) * 4 bytes for every destination address d
+    (device pointers, e.g. peer mappings from kq.dist.PeerBuffer)."""
+    wt = _wtype(wtype)
+    _cuda(weight, "weight", torch.uint8, N * (K // 32) * lib().kq_block_bytes(wt))
+    _cuda(activation, "activation", torch.float32, M * K)
+    if not 1 <= len(outs) <= 8:
+        raise ValueError("1 to 8 destinations")
+    arr = (ctypes.c_void_p * len(outs))(*[int(o) for o in outs])
+    check(lib().kq_gemm_f32act_scatter(wt, weight.data_ptr(), activation.data_ptr(), arr, len(outs), ldo, col0, M, N,
+                                       K, _act_mode(act_mode), _stream(stream_of if stream_of is not None else weight)),
+          "kq_gemm_f32act_scatter")
 
 
 def mul_mat_q8x(weight: torch.Tensor, a_qs: torch.Tensor, a_ds: torch.Tensor, M: int, N: int, K: int, wtype="q4_0",

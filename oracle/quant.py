@@ -344,6 +344,27 @@ def check_close(out: np.ndarray, ref: np.ndarray, rel_l2_tol: float = 1e-3,
     return ok, f"rel_l2={r:.3e} bad_elems={nbad}/{out.size}"
 
 
+def check_close_requant(out: np.ndarray, ref: np.ndarray, max_bad_frac: float = 1e-3) -> tuple[bool, str]:
+    """The fp32 bar for outputs that pass through an intermediate q8_1
+    re-quantisation (the MoE's silu(gate) * up before the down projection):
+    rel-L2 <= 1e-3, and the per-element bar of check_close on all but
+    `max_bad_frac` of the elements. The intermediate is formed from fp32 GEMM
+    outputs on the GPU and fp64 ones here, so a value sitting on a rounding
+    boundary can quantise to the neighbouring code; such a flip moves a few
+    near-zero outputs past the 1e-3 rms floor while leaving rel-L2 near 1e-5."""
+    out = np.asarray(out, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    if out.shape != ref.shape:
+        return False, f"shape {out.shape} != {ref.shape}"
+    if not np.all(np.isfinite(out)):
+        return False, "non-finite output"
+    r = rel_l2(out, ref)
+    rms = float(np.sqrt(np.mean(ref ** 2))) if ref.size else 0.0
+    nbad = int(np.count_nonzero(np.abs(out - ref) > 1e-2 * np.abs(ref) + 1e-3 * rms))
+    ok = r <= 1e-3 and nbad <= max_bad_frac * out.size
+    return ok, f"rel_l2={r:.3e} bad_elems={nbad}/{out.size} (allowed {int(max_bad_frac * out.size)})"
+
+
 # ---------------------------------------------------------------------------
 # Flash-attention decode over a q8_0 KV cache
 # ---------------------------------------------------------------------------

@@ -15,6 +15,11 @@ from oracle import quant as Q
 pytestmark = pytest.mark.gpu
 
 
+def _assert_close(out, ref, what="", requant=False):
+    ok, msg = (Q.check_close_requant if requant else Q.check_close)(out, ref)
+    assert ok, f"{what} {msg}"
+
+
 def _moe_case(rng, T, E, H, I):
     x = rng.standard_normal((T, H)).astype(np.float32)
     logits = rng.standard_normal((T, E)).astype(np.float32)
@@ -39,8 +44,8 @@ def test_moe_stages_world1(cuda):
     out = kd.moe_expert_parallel(t(x), t(logits), t(wg), t(wu), t(wd), E, topk)
     fused = kq.moe_q4_0(t(x), t(logits), t(wg), t(wu), t(wd), topk=topk)
     ref = Q.moe_forward(x, logits, list(wg), list(wu), list(wd), topk, H, I, Q.SUM_DQ)
-    Q.check_close(out.cpu().numpy(), ref)
-    Q.check_close(fused.cpu().numpy(), ref)
+    _assert_close(out.cpu().numpy(), ref, "expert-parallel", requant=True)
+    _assert_close(fused.cpu().numpy(), ref, "fused", requant=True)
 
 
 def test_nsharded_gemm_world1(cuda):
@@ -52,12 +57,125 @@ def test_nsharded_gemm_world1(cuda):
     x = rng.standard_normal((M, K)).astype(np.float32)
     g = kd.NShardedGemm(torch.from_numpy(w.reshape(N, -1)).to(cuda), N, K, wtype="q4_0", act_mode="sum_dq")
     out = g(torch.from_numpy(x).to(cuda))
-    Q.check_close(out.cpu().numpy(), Q.gemm_f32act("q4_0", w.reshape(-1), x, M, N, K, Q.SUM_DQ))
+    _assert_close(out.cpu().numpy(), Q.gemm_f32act("q4_0", w.reshape(-1), x, M, N, K, Q.SUM_DQ))
+
+
+@pytest.mark.parametrize("wtype,M,N,K", [("q4_0", 1, 512, 1024), ("q8_0", 4, 256, 512), ("q8_0", 200, 384, 1024),
+                                         ("q4_1", 130, 136, 512)])
+def test_scatter_epilogue_world1(cuda, wtype, M, N, K):
+    """kq_gemm_f32act_scatter into two destinations at a column offset inside
+    wider rows: every destination gets the same (correct) columns, nothing else
+    is touched."""
+    import kq
+
+    rng = np.random.default_rng(M + N)
+    w = Q.make_blocks(wtype, rng, N, K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    ldo, col0 = N + 24, 12
+    outs = [torch.full((M, ldo), -7.0, device=cuda) for _ in range(2)]
+    kq.gemm_f32act_scatter(torch.from_numpy(w).to(cuda), torch.from_numpy(x).to(cuda), [o.data_ptr() for o in outs],
+                           ldo, col0, M, N, K, wtype, "sum_dq")
+    ref = Q.gemm_f32act(wtype, w, x, M, N, K, Q.SUM_DQ)
+    for o in outs:
+        o = o.cpu().numpy()
+        ok, msg = Q.check_close(o[:, col0:col0 + N], ref)
+        assert ok, msg
+        assert np.all(o[:, :col0] == -7.0) and np.all(o[:, col0 + N:] == -7.0)
+
+
+def test_peer_buffer_and_p2p_gemm_world1(cuda):
+    from kq import dist as kd
+
+    rng = np.random.default_rng(4)
+    M, N, K = 64, 1024, 512
+    w = Q.make_blocks("q8_0", rng, N, K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    g = kd.NShardedGemm(torch.from_numpy(w.reshape(N, -1)).to(cuda), N, K, wtype="q8_0", mode="p2p")
+    y = g(torch.from_numpy(x).to(cuda))
+    ok, msg = Q.check_close(y.cpu().numpy(), Q.gemm_f32act("q8_0", w.reshape(-1), x, M, N, K, Q.SUM_DQ))
+    g.close()
+    assert ok, msg
 
 
 # ---------------------------------------------------------------------------
-# two ranks over NCCL
+# two ranks over NCCL (this file run by torchrun as a script; see _ranks_main)
 # ---------------------------------------------------------------------------
+
+def _ranks_main(which: str) -> None:
+    """One rank of a two-rank case; launched by test_two_ranks_nccl through
+    torch.distributed.run with a bounded runtime. Prints progress per rank."""
+    import datetime
+    import sys
+
+    import torch.distributed as dist
+
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
+    dev = torch.device("cuda", torch.cuda.current_device())
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    say = lambda *a: print(f"[rank {rank}]", *a, flush=True)  # noqa: E731
+    failures = []
+    try:
+        from kq import dist as kd
+
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
+        if which in ("gemm", "gemm_p2p"):
+            rng = np.random.default_rng(12)
+            mode = "p2p" if which == "gemm_p2p" else "nccl"
+            for (M, N, K) in ((64, 2048, 1024), (3, 1024, 512)):   # tensor-core and GEMV epilogues
+                w = Q.make_blocks("q8_0", rng, N, K)
+                x = rng.standard_normal((M, K)).astype(np.float32)
+                shard = kd.NShardedGemm.shard_weight(torch.from_numpy(w.reshape(N, -1)), N, world, rank).to(dev)
+                g = kd.NShardedGemm(shard, N, K, wtype="q8_0", act_mode="sum_dq", mode=mode)
+                for rep in range(3):   # alternating buffers
+                    out = g(t(x)).cpu().numpy()
+                    ok, msg = Q.check_close(out, Q.gemm_f32act("q8_0", w.reshape(-1), x, M, N, K, Q.SUM_DQ))
+                    say(which, M, N, K, rep, msg)
+                    if not ok:
+                        failures.append((M, N, K, rep, msg))
+                dist.barrier()
+                g.close()
+        elif which == "moe":
+            rng = np.random.default_rng(13)
+            T_per, E, topk, H, I = 96, 8, 2, 256, 512
+            x, logits, wg, wu, wd = _moe_case(rng, T_per * world, E, H, I)
+            first, per = kd.expert_range(E, world, rank)
+            sl = slice(rank * T_per, (rank + 1) * T_per)
+            stats = {}
+            out = kd.moe_expert_parallel(t(x[sl]), t(logits[sl]), t(wg[first:first + per]), t(wu[first:first + per]),
+                                         t(wd[first:first + per]), E, topk, stats=stats)
+            ref = Q.moe_forward(x, logits, list(wg), list(wu), list(wd), topk, H, I, Q.SUM_DQ,
+                                tokens=np.arange(sl.start, sl.stop))
+            ok, msg = Q.check_close_requant(out.cpu().numpy(), ref)
+            say("moe", stats, msg)
+            if not ok:
+                failures.append(msg)
+        # every rank reaches this point on every path: the exit status carries the verdict
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+    say("failures:", failures)
+    sys.exit(1 if failures else 0)
+
+
+@pytest.mark.parametrize("which", ["gemm", "gemm_p2p", "moe"])
+def test_two_ranks_nccl(cuda, which):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import subprocess
+    import sys
+
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", KQ_DIST_CASE=which,
+               PYTHONPATH=os.pathsep.join([p for p in sys.path if p]))
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", f"--master-port={_free_port()}", os.path.abspath(__file__)]
+    try:
+        r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=240, start_new_session=True)
+    except subprocess.TimeoutExpired as e:
+        pytest.fail(f"two-rank case {which} did not finish in 240 s:\n{e.stdout}\n{e.stderr}")
+    assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-4000:]
+
 
 def _free_port() -> int:
     with socket.socket() as s:
@@ -65,49 +183,11 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, which):
-    import datetime
+if __name__ == "__main__":
+    import sys
 
-    import torch.distributed as dist
-
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
-    torch.cuda.set_device(rank)
-    dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
-                            device_id=dev)
-    try:
-        from kq import dist as kd
-
-        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
-        if which == "gemm":
-            rng = np.random.default_rng(12)
-            M, N, K = 64, 2048, 1024
-            w = Q.make_blocks("q8_0", rng, N, K)
-            x = rng.standard_normal((M, K)).astype(np.float32)
-            shard = kd.NShardedGemm.shard_weight(torch.from_numpy(w.reshape(N, -1)), N, world, rank).to(dev)
-            out = kd.NShardedGemm(shard, N, K, wtype="q8_0", act_mode="sum_dq")(t(x))
-            if rank == 0:
-                Q.check_close(out.cpu().numpy(), Q.gemm_f32act("q8_0", w.reshape(-1), x, M, N, K, Q.SUM_DQ))
-        elif which == "moe":
-            rng = np.random.default_rng(13)
-            T_per, E, topk, H, I = 96, 8, 2, 256, 512
-            x, logits, wg, wu, wd = _moe_case(rng, T_per * world, E, H, I)
-            first, per = kd.expert_range(E, world, rank)
-            sl = slice(rank * T_per, (rank + 1) * T_per)
-            out = kd.moe_expert_parallel(t(x[sl]), t(logits[sl]), t(wg[first:first + per]), t(wu[first:first + per]),
-                                         t(wd[first:first + per]), E, topk)
-            ref = Q.moe_forward(x, logits, list(wg), list(wu), list(wd), topk, H, I, Q.SUM_DQ,
-                                tokens=np.arange(sl.start, sl.stop))
-            Q.check_close(out.cpu().numpy(), ref)
-        dist.barrier()
-    finally:
-        dist.destroy_process_group()
-
-
-@pytest.mark.parametrize("which", ["gemm", "moe"])
-def test_two_ranks_nccl(cuda, which):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    import torch.multiprocessing as mp
-
-    mp.start_processes(_rank_main, args=(2, _free_port(), which), nprocs=2, join=True, start_method="spawn")
+    here = os.path.dirname(os.path.abspath(__file__))
+    for p in (os.path.dirname(here), os.path.join(os.path.dirname(here), "k-search_b200")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    _ranks_main(os.environ["KQ_DIST_CASE"])
