@@ -200,7 +200,7 @@ __device__ __forceinline__ uint64_t sw128_desc_rep8(uint32_t saddr) {
   return d;
 }
 
-template <int WT>
+template <int WT, bool SCATTER>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_act, const __grid_constant__ CUtensorMap map_asc,
                    const __grid_constant__ CUtensorMap map_raw, const __grid_constant__ TcParams p) {
@@ -480,11 +480,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int m = m0 + row;
           const int nc0 = n0 + cg * kEpiCols;
           if (m < p.M) {
-            const size_t off = (size_t)m * p.out.ld + p.out.col0 + nc0;
-            const bool vec = nc0 + kEpiCols <= p.N && ((p.out.ld | p.out.col0) & 3) == 0;
-            for (int dd = 0; dd < p.out.n_out; ++dd) {
-              float* o = p.out.ptr[dd] + off;
-              if (vec) {
+            if constexpr (!SCATTER) {
+              float* o = p.out.ptr[0] + (size_t)m * p.N + nc0;
+              if (nc0 + kEpiCols <= p.N && (p.N & 3) == 0) {
 #pragma unroll
                 for (int c = 0; c < NP; c += 2) {
                   const float2 a = upk2(acc[c]), b = upk2(acc[c + 1]);
@@ -498,12 +496,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                   if (nc0 + 2 * c + 1 < p.N) o[2 * c + 1] = a.y;
                 }
               }
+            } else {
+              const size_t off = (size_t)m * p.out.ld + p.out.col0 + nc0;
+              const bool vec = nc0 + kEpiCols <= p.N && ((p.out.ld | p.out.col0) & 3) == 0;
+              for (int dd = 0; dd < p.out.n_out; ++dd) {
+                float* o = p.out.ptr[dd] + off;
+                if (vec) {
+#pragma unroll
+                  for (int c = 0; c < NP; c += 2) {
+                    const float2 a = upk2(acc[c]), b = upk2(acc[c + 1]);
+                    *reinterpret_cast<float4*>(o + 2 * c) = make_float4(a.x, a.y, b.x, b.y);
+                  }
+                } else {
+#pragma unroll
+                  for (int c = 0; c < NP; ++c) {
+                    const float2 a = upk2(acc[c]);
+                    if (nc0 + 2 * c < p.N) o[2 * c] = a.x;
+                    if (nc0 + 2 * c + 1 < p.N) o[2 * c + 1] = a.y;
+                  }
+                }
+              }
             }
           }
         }
       }
     }
-    if (p.out.n_out > 1) __threadfence_system();  // peer stores visible before the host-side barrier
+    if constexpr (SCATTER) __threadfence_system();  // peer stores visible before the host-side barrier
   }
 
   tc_fence_before();
@@ -533,13 +551,14 @@ kq_status_t launch_tc(const void* w, Act8 act, const OutSpec& out, int M, int N,
                   CU_TENSOR_MAP_SWIZZLE_NONE))
     return fail(KQ_ERR_CUDA, "tensor map (weights) rejected");
 
-  auto kern = gemm_tc_kernel<WT>;
-  static unsigned attr_done = 0;
+  const bool scatter = out.n_out > 1 || out.ld != N || out.col0 != 0;
+  auto kern = scatter ? gemm_tc_kernel<WT, true> : gemm_tc_kernel<WT, false>;
+  static unsigned attr_done[2] = {0, 0};
   const int dev = current_device();
-  if (!(attr_done & (1u << (dev & 31)))) {
+  if (!(attr_done[scatter] & (1u << (dev & 31)))) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::SMEM);
     if (e != cudaSuccess) return check_cuda(e, "gemm_tc smem attribute");
-    attr_done |= 1u << (dev & 31);
+    attr_done[scatter] |= 1u << (dev & 31);
   }
   TcParams p;
   p.M = M; p.N = N; p.K = K; p.nb = nb;

@@ -85,7 +85,7 @@ def _ragged_case(rng, lens, Hq, Hkv, D):
     return q, k, v, cu
 
 
-@pytest.mark.parametrize("lens,Hq,Hkv,D", [
+RAGGED_CASES = [
     ([64, 8192, 1000, 3], 32, 8, 128),
     ([1, 2, 300, 257], 8, 8, 64),
     ([500, 0, 77], 16, 2, 128),        # an empty sequence
@@ -95,7 +95,10 @@ def _ragged_case(rng, lens, Hq, Hkv, D):
     ([7, 4097, 64], 16, 8, 128),
     ([31, 32, 33], 8, 8, 128),
     ([2000, 5], 32, 16, 128),
-])
+]
+
+
+@pytest.mark.parametrize("lens,Hq,Hkv,D", RAGGED_CASES)
 def test_ragged_parity(cuda, lens, Hq, Hkv, D):
     import kq
     rng = np.random.default_rng(sum(lens) + Hq)
@@ -106,3 +109,22 @@ def test_ragged_parity(cuda, lens, Hq, Hkv, D):
     ref = Q.flash_decode_ragged(q, k, v, cu, Hq, Hkv, D, scale)
     ok, msg = Q.check_close(got, ref)
     assert ok, msg
+
+
+def test_mma_decode_path_opt_in(cuda):
+    """KQ_FA_PATH=mma (warp-level MMA decode: int8 QK on the raw codes, fp16 PV)
+    against the oracle, in a child process (the path is chosen once per process)."""
+    import os
+    import subprocess
+    import sys
+    code = (
+        "import sys; sys.path[:0] = %r\n"
+        "import test_flash_decode_gpu as T, torch\n"
+        "dev = torch.device('cuda:0')\n"
+        "for fn in (T.test_ragged_parity, ):\n"
+        "    for args in T.RAGGED_CASES:\n"
+        "        fn(dev, *args)\n"
+        "print('ok')\n" % ([os.path.dirname(os.path.abspath(__file__))] + [p for p in sys.path if p],))
+    env = dict(os.environ, KQ_FA_PATH="mma")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
