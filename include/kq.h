@@ -136,7 +136,9 @@ kq_status_t kq_gemm_f32act(int wtype, const void* w, const float* x, float* out,
  * above 1 MiB are rejected with KQ_ERR_INVALID. The first call on a device
  * resolves the array's device address (cudaGetSymbolAddress) and should come
  * before any stream capture. All calls share the array: calls that overlap on
- * the GPU race. Same arguments and results as kq_gemm_f32act. */
+ * the GPU race. Same arguments as kq_gemm_f32act; for M > 8 it runs the int8
+ * tensor-core kernel (no fp16 operand workspace), whose results agree with
+ * kq_gemm_f32act's to the parity bar rather than bit for bit. */
 kq_status_t kq_gemm_f32act_noalloc(int wtype, const void* w, const float* x, float* out, int M, int N, int K,
                                    int act_mode, kq_stream_t stream);
 

@@ -131,17 +131,36 @@ kq_status_t check_gemm_args(int wtype, const void* w, const void* a, const float
 }
 
 // Quantised activations are staged; choose the GEMM kernel for the shape.
-// M > 8 path: the int8 tcgen05 kernel (exact per-block arithmetic) by default;
-// KQ_GEMM_PATH=dequant selects the fp16-dequantised kind::f16 kernel, faster
-// but with fp16 operand rounding (rel-L2 about 3e-4 against the exact result).
-// Read once per process.
-enum class GemmPath { kDequant, kInt8 };
+// M > 8 path: the exact split-fp16 tcgen05 kernel by default;
+// KQ_GEMM_PATH=int8 selects the int8 tcgen05 kernel (per-block int32 sums
+// rescaled on the FP32 pipe, slower); KQ_GEMM_PATH=dequant the single-rounding
+// fp16 kernel (fp16 operand rounding: rel-L2 about 3e-4 against the exact
+// result, outside the per-element bar). Read once per process.
+enum class GemmPath { kSplit, kDequant, kInt8 };
 GemmPath gemm_path() {
   static const GemmPath p = [] {
     const char* e = std::getenv("KQ_GEMM_PATH");
-    return (e && std::string(e) == "dequant") ? GemmPath::kDequant : GemmPath::kInt8;
+    if (e && std::string(e) == "dequant") return GemmPath::kDequant;
+    if (e && std::string(e) == "int8") return GemmPath::kInt8;
+    return GemmPath::kSplit;
   }();
   return p;
+}
+
+// The tensor-core kernel for M > 8 with the given output destinations, or
+// KQ_ERR_UNSUPPORTED (no error recorded) when neither fits the shape.
+kq_status_t dispatch_gemm_tc(int wtype, const void* w, Act8 act, const OutSpec& out, int M, int N, int K,
+                             cudaStream_t s, bool pdl) {
+  const GemmPath path = gemm_path();
+  if (path == GemmPath::kSplit && gemm_split_supported(wtype, M, N, K, w, act))
+    return launch_gemm_split(wtype, w, act, out, M, N, K, s);
+  if (gemm_tc_supported(wtype, M, N, K, w, act)) return launch_gemm_tc(wtype, w, act, out, M, N, K, pdl, s);
+  return KQ_ERR_UNSUPPORTED;
+}
+
+bool gemm_tc_any_supported(int wtype, int M, int N, int K, const void* w, Act8 act) {
+  return (gemm_path() == GemmPath::kSplit && gemm_split_supported(wtype, M, N, K, w, act)) ||
+         gemm_tc_supported(wtype, M, N, K, w, act);
 }
 
 kq_status_t dispatch_gemm(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, cudaStream_t s,
@@ -149,7 +168,8 @@ kq_status_t dispatch_gemm(int wtype, const void* w, Act8 act, float* out, int M,
   if (gemv_supported(wtype, M, N, K) && aligned(w, 16)) return launch_gemv(wtype, w, act, out, M, N, K, pdl, s);
   if (gemm_path() == GemmPath::kDequant && gemm_hx_supported(wtype, M, N, K, w, act))
     return launch_gemm_hx(wtype, w, act, out, M, N, K, pdl, s);
-  if (gemm_tc_supported(wtype, M, N, K, w, act)) return launch_gemm_tc(wtype, w, act, out, M, N, K, pdl, s);
+  if (gemm_tc_any_supported(wtype, M, N, K, w, act))
+    return dispatch_gemm_tc(wtype, w, act, OutSpec::plain(out, N), M, N, K, s, pdl);
   return launch_gemm_simt(wtype, w, act, out, M, N, K, s);
 }
 
@@ -304,11 +324,11 @@ kq_status_t kq_gemm_f32act_scatter(int wtype, const void* w, const float* x, flo
   if (!ws) return KQ_ERR_NOMEM;
   Act8 act = act8_view(ws, M, K);
   const bool gemv = gemv_supported(wtype, M, N, K) && aligned(w, 16);
-  const bool tc = !gemv && gemm_tc_supported(wtype, M, N, K, w, act);
+  const bool tc = !gemv && gemm_tc_any_supported(wtype, M, N, K, w, act);
   if (!gemv && !tc) return fail(KQ_ERR_UNSUPPORTED, "scatter: shape M=%d N=%d K=%d has no scatter epilogue", M, N, K);
   st = launch_quantize_act(x, act, M, K, act_mode, s);
   if (st) return st;
-  return gemv ? launch_gemv(wtype, w, act, o, M, N, K, true, s) : launch_gemm_tc(wtype, w, act, o, M, N, K, true, s);
+  return gemv ? launch_gemv(wtype, w, act, o, M, N, K, true, s) : dispatch_gemm_tc(wtype, w, act, o, M, N, K, s, true);
 }
 
 kq_status_t kq_mul_mat_q8x(int wtype, const void* w, const int8_t* a_qs, const float* a_ds, float* out, int M, int N,

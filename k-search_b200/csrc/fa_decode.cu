@@ -407,6 +407,7 @@ __global__ void __launch_bounds__(kFastThreads, 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[j][i] = fmaf(pv[j], vf[i], acc[j][i]);
     }
+    fence_proxy_async_smem();  // generic reads of the TMA-refilled tile, before its release
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
@@ -725,6 +726,7 @@ __global__ void __launch_bounds__(kFastThreads, 1)
         }
       }
     }
+    fence_proxy_async_smem();  // generic reads of the TMA-refilled tile, before its release
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }

@@ -382,6 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             win[4 * i + 3] = v.w;
           }
         }
+        fence_proxy_async_smem();  // generic reads of a TMA-refilled stage, before its release
         __syncwarp();
         if (lane == 0) mbar_arrive(&raw_empty[rs]);
         uint32_t vals[4][16];

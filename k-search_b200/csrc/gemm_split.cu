@@ -1,0 +1,701 @@
+// Tensor-core quantised GEMM for M > 8 activation rows in exact split-fp16
+// form: the reference's per-block integer formulas (gemm_ref.py:100-153
+// q4_0, :274-331 q4_1; include/gemm_reference.h:311-336 q8_0) evaluated as
+// fp16 tensor-core products whose operands carry every bit of the
+// dequantised values.
+//
+// Both operands are dequantised and split into a high fp16 part and a
+// low fp16 part scaled by 2^11 (so it never falls into fp16 subnormals):
+//   a = q_a * d_a * 2^-e_m          (per activation row, e_m puts the row's
+//                                     largest |a| in [2^14, 2^15))
+//   A_hi = fp16(a),  A_lo = fp16((a - A_hi) * 2^11)         exact: a has 19 bits
+//   W    = (q_w - 8) d_w  (q4_0),  q_w d_w + m_w  (q4_1),  q_w d_w  (q8_0)
+//   W_hi = fp16(W),  W_lo = fp16((W - W_hi) * 2^11)          exact for q4_0 / q8_0
+// and three tcgen05.mma.kind::f16 chains accumulate in fp32 TMEM:
+//   main = sum_k A_hi W_hi (+ the extra columns below)
+//   corr = sum_k A_lo W_hi + A_hi W_lo
+//   out[m, n] = 2^e_m (main + 2^-11 corr)
+// The dropped A_lo W_lo term is 2^-22 of the products, so the result equals
+// the exact per-block sum up to fp32 accumulation order. For q4_0 / q4_1 the
+// difference between the plain product and the reference's formulas (its
+// stored block sum s_a instead of d_a sum q_a) rides in extra K columns:
+//   X_a = (s_a - d_a sum_i q_a) 2^-e_m,  X_w = -8 d_w (q4_0) | m_w (q4_1).
+//
+// Why this form: an int8 kind::i8 pipeline has to rescale a fresh int32 tile
+// per 32-wide K block on the FP32 pipe (at least two FMAs per element and
+// block); a single fp16 rounding of each operand is 2x faster but leaves a
+// relative error of ~3e-4 per element, outside the parity bar. The split
+// costs three kind::f16 MMAs per K chunk but no per-block epilogue, and each
+// converted weight chunk feeds three MMAs, which keeps the tensor pipe ahead
+// of the warp-to-warp hand-offs.
+//
+// CTA: 128 tokens x HN weight rows, persistent over tiles (tokens fastest, so
+// co-running CTAs share weight tiles in L2). Warps (each loop runs on the
+// whole warp; lane 0 issues):
+//   0            A producer: A_hi and A_lo chunks (128 rows x 64 K, 128B-swizzled)
+//   1            raw weight producer: unchanged AoS q-blocks, HN rows x 8 blocks
+//   2            MMA issuer, owns the TMEM allocation
+//   3 .. 3+CW-1  converters: two threads per weight row, one 32-block of each
+//                64-wide K chunk, writing W_hi and W_lo (and X_w)
+//   next 4       epilogue: TMEM -> registers -> global fp32; two accumulator
+//                pairs so the next tile's MMAs overlap the stores
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "kq_internal.h"
+#include "kq_device.cuh"
+#include "kq_tc.cuh"
+
+namespace kq {
+namespace {
+
+using namespace tc;
+
+constexpr int TM = 128;                  // tokens per tile (TMEM lanes)
+constexpr int CK = 64;                   // K elements per chunk: one 128-byte swizzle atom of fp16
+constexpr int RB = 8;                    // blocks per raw weight stage (= 4 chunks)
+constexpr int GRP = 32;                  // main chunks per extra chunk (64 blocks)
+constexpr int SA = 3;                    // A stages (hi + lo)
+constexpr int A_PART = TM * 128;         // one 128-row x 128-byte tile
+constexpr int A_STAGE = 2 * A_PART;
+constexpr int kSmemLimit = 232448;
+
+template <int WT, int HN>
+struct SxTraits {
+  static_assert(HN % 16 == 0 && HN >= 32 && HN <= 128, "MMA N");
+  static constexpr int BB = WT == KQ_Q4_0 ? 18 : WT == KQ_Q4_1 ? 20 : 34;
+  static constexpr bool kExtra = WT != KQ_Q8_0;
+  static constexpr int RAW_ROW = RB * BB;  // 144 / 160 / 272 bytes
+  static constexpr int RAW_STAGE = HN * RAW_ROW;
+  static constexpr int W_PART = HN * 128;
+  static constexpr int W_STAGE = 2 * W_PART;
+  static constexpr int X_BYTES = kExtra ? W_PART : 0;
+  // 32-bit words a converter reads for one block: from the 4-byte boundary at
+  // or below the block start (blocks are 2-byte aligned) to its end
+  static constexpr int NW = WT == KQ_Q4_1 ? 5 : (BB + 2 + 3) / 4;
+  static constexpr int CW = HN / 16;       // converter warps: 2 threads per weight row
+  static constexpr int kWarpA = 0, kWarpRaw = 1, kWarpMma = 2, kWarpConv = 3, kWarpEpi = 3 + CW;
+  static constexpr int kWarps = kWarpEpi + 4;
+  static constexpr int kThreads = kWarps * 32;
+  static constexpr int kFixed = 1024 + 16 + 8 * (2 * SA + 2 * 3 + 2 * 2 + 2 * 2 + 1);
+  static constexpr int SR = (SA * A_STAGE + 3 * W_STAGE + X_BYTES + 2 * RAW_STAGE + kFixed <= kSmemLimit) ? 2 : 1;
+  static constexpr int SW = (SA * A_STAGE + 3 * W_STAGE + X_BYTES + SR * RAW_STAGE + kFixed <= kSmemLimit) ? 3 : 2;
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_W = OFF_A + SA * A_STAGE;
+  static constexpr int OFF_X = OFF_W + SW * W_STAGE;
+  static constexpr int OFF_RAW = OFF_X + X_BYTES;
+  static constexpr int OFF_BAR = OFF_RAW + SR * RAW_STAGE;
+  static constexpr int NBARS = 2 * SA + 2 * SW + 2 * SR + 2 * 2 + 1;
+  static constexpr int OFF_TMEM = OFF_BAR + NBARS * 8;
+  static constexpr int SMEM = OFF_TMEM + 16 + 1024;
+  static constexpr uint32_t kTmemCols = 4 * HN <= 256 ? 256 : 512;
+  static_assert(RAW_ROW % 16 == 0 && RAW_STAGE % 16 == 0, "raw stages stay 16-byte aligned");
+  static_assert(W_PART % 1024 == 0, "swizzled tiles stay 1024-byte aligned");
+  static_assert(SMEM <= kSmemLimit, "shared memory budget");
+  static_assert(4 * HN <= 512, "two accumulator pairs fit in TMEM");
+};
+
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// Instruction descriptor, kind::f16: D f32, A = B = f16, both K-major, M = 128.
+template <int HN>
+__host__ __device__ constexpr uint32_t idesc_f16() {
+  return (1u << 4) | ((uint32_t)(HN >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
+}
+
+__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// Bounded spin on the non-suspending probe (the hand-offs in this kernel
+// complete within a few hundred cycles; a suspended wait resumes later).
+// Gives up after kWaitLimitNs, records `code` and poisons the caller.
+__device__ __forceinline__ void spin_wait(uint64_t* bar, uint32_t parity, int* err, int code, bool& dead) {
+  if (dead) return;
+  const uint64_t t0 = globaltimer_ns();
+#pragma unroll 1
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_test_wait(bar, parity)) return;
+    if ((i & 1023u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+      record_error(err, code);
+      dead = true;
+      return;
+    }
+  }
+}
+
+// One weight block -> 16 packed fp16 pairs of W_hi and of W_lo (element pairs
+// 2i, 2i+1 in K order) and the block's X_w. `w` holds the block's bytes from
+// the 4-byte boundary at or below its start; `sh` = 8 * (start & 3).
+//
+// W_lo exactness for q4_0 / q8_0: c and d are fp16 (c an integer of at most 8
+// bits), so c*d is a multiple of d's unit in the last place and so is
+// r = c*d - fp16(c*d); |r| is at most half an ulp of fp16(c*d), hence r is an
+// fp16 value (normal or subnormal) and the fma below returns it exactly.
+// Scaling by -2^11 is exact (|r| * 2^11 <= 2^15).
+template <int WT, int NW>
+__device__ __forceinline__ void convert_block(const uint32_t (&w)[NW], uint32_t sh, uint32_t (&hi)[16],
+                                              uint32_t (&lo)[16], uint16_t& xw) {
+  constexpr uint32_t kNeg2048 = 0xE800E800u;  // (-2048, -2048)
+  const uint32_t dh = __funnelshift_r(w[0], w[1], sh) & 0xFFFFu;
+  const uint32_t d2 = dh | (dh << 16);
+  if constexpr (WT == KQ_Q8_0) {
+    const uint32_t nd2 = d2 ^ 0x80008000u;
+    constexpr uint32_t kOff = 0x64806480u;  // (1152, 1152): M + (c ^ 0x80) - 1152 = c
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t cw = __funnelshift_rc(w[k], w[k + 1], sh + 16) ^ 0x80808080u;
+      const uint32_t c01 = hsub2(__byte_perm(cw, 0x64646464u, 0x4140), kOff);
+      const uint32_t c23 = hsub2(__byte_perm(cw, 0x64646464u, 0x4342), kOff);
+      const uint32_t h01 = hmul2(c01, d2), h23 = hmul2(c23, d2);
+      hi[2 * k] = h01;
+      hi[2 * k + 1] = h23;
+      lo[2 * k] = hmul2(hfma2(c01, nd2, h01), kNeg2048);      // (h - c d) * -2^11 = r * 2^11
+      lo[2 * k + 1] = hmul2(hfma2(c23, nd2, h23), kNeg2048);
+    }
+    xw = 0;
+  } else if constexpr (WT == KQ_Q4_0) {
+    const uint32_t nd2 = d2 ^ 0x80008000u;
+    constexpr uint32_t k1032 = 0x64086408u;  // (1032, 1032): M + c - 1032 = c - 8
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t cw = __funnelshift_rc(w[k], w[k + 1], sh + 16);
+      const uint32_t lw = cw & 0x0F0F0F0Fu, hw = (cw >> 4) & 0x0F0F0F0Fu;
+      uint32_t c[4];
+      c[0] = hsub2(__byte_perm(lw, 0x64646464u, 0x4140), k1032);  // elements 4k, 4k+1
+      c[1] = hsub2(__byte_perm(lw, 0x64646464u, 0x4342), k1032);  // 4k+2, 4k+3
+      c[2] = hsub2(__byte_perm(hw, 0x64646464u, 0x4140), k1032);  // 16+4k, 16+4k+1
+      c[3] = hsub2(__byte_perm(hw, 0x64646464u, 0x4342), k1032);
+      const int idx[4] = {2 * k, 2 * k + 1, 8 + 2 * k, 8 + 2 * k + 1};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t h = hmul2(c[i], d2);
+        hi[idx[i]] = h;
+        lo[idx[i]] = hmul2(hfma2(c[i], nd2, h), kNeg2048);
+      }
+    }
+    xw = (uint16_t)(hmul2(dh, 0xC800u) & 0xFFFFu);  // -8 d (exact)
+  } else {
+    // q4_1: W = c d + m (one rounding for W_hi); the residual in fp32, where
+    // c d + m is exact whenever it fits 24 bits
+    const uint32_t mh = w[0] >> 16;
+    const uint32_t m2 = mh | (mh << 16);
+    const float df = __half2float(__ushort_as_half((uint16_t)dh));
+    const float mf = __half2float(__ushort_as_half((uint16_t)mh));
+    constexpr uint32_t k1024 = 0x64006400u;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t cw = w[k + 1];
+      const uint32_t lw = cw & 0x0F0F0F0Fu, hw = (cw >> 4) & 0x0F0F0F0Fu;
+      uint32_t c[4];
+      c[0] = hsub2(__byte_perm(lw, 0x64646464u, 0x4140), k1024);
+      c[1] = hsub2(__byte_perm(lw, 0x64646464u, 0x4342), k1024);
+      c[2] = hsub2(__byte_perm(hw, 0x64646464u, 0x4140), k1024);
+      c[3] = hsub2(__byte_perm(hw, 0x64646464u, 0x4342), k1024);
+      const int idx[4] = {2 * k, 2 * k + 1, 8 + 2 * k, 8 + 2 * k + 1};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t h = hfma2(c[i], d2, m2);
+        hi[idx[i]] = h;
+        const float2 cf = __half22float2(*reinterpret_cast<const __half2*>(&c[i]));
+        const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&h));
+        const __half2 l = __floats2half2_rn((fmaf(cf.x, df, mf) - hf.x) * 2048.0f, (fmaf(cf.y, df, mf) - hf.y) * 2048.0f);
+        lo[idx[i]] = *reinterpret_cast<const uint32_t*>(&l);
+      }
+    }
+    xw = (uint16_t)mh;
+  }
+}
+
+struct SxParams {
+  int M, N, K;
+  int nmain, ngrp;
+  int num_m_tiles, num_tiles;
+  OutSpec out;
+  const float* rscale;  // per activation row: 2^e undoing the prep kernel's scaling
+  int* err;
+};
+
+// main chunk c is followed by an extra chunk (last of its group of GRP, or the last chunk)
+__device__ __forceinline__ bool extra_after(int c, int nmain) { return (c % GRP) == GRP - 1 || c == nmain - 1; }
+
+template <int WT, int HN, bool SCATTER>
+__global__ void __launch_bounds__(SxTraits<WT, HN>::kThreads, 1)
+    gemm_split_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo,
+                      const __grid_constant__ CUtensorMap map_raw, const __grid_constant__ SxParams p) {
+  using T = SxTraits<WT, HN>;
+  constexpr int SW = T::SW, SR = T::SR;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + T::OFF_BAR);
+  uint64_t* a_full = bars;
+  uint64_t* a_empty = a_full + SA;
+  uint64_t* w_full = a_empty + SA;
+  uint64_t* w_empty = w_full + SW;
+  uint64_t* raw_full = w_empty + SW;
+  uint64_t* raw_empty = raw_full + SR;
+  uint64_t* tm_full = raw_empty + SR;
+  uint64_t* tm_empty = tm_full + 2;
+  uint64_t* x_empty = tm_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + T::OFF_TMEM);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nraw = p.nmain / 4;
+  const int my_tiles = (p.num_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < SA; ++i) {
+      mbar_init(&a_full[i], 1);
+      mbar_init(&a_empty[i], 1);
+    }
+    for (int i = 0; i < SW; ++i) {
+      mbar_init(&w_full[i], T::CW);
+      mbar_init(&w_empty[i], 1);
+    }
+    for (int i = 0; i < SR; ++i) {
+      mbar_init(&raw_full[i], 1);
+      mbar_init(&raw_empty[i], T::CW);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tm_full[i], 1);
+      mbar_init(&tm_empty[i], 4);
+    }
+    mbar_init(x_empty, 1);
+    fence_mbar_init();
+  }
+  if constexpr (T::kExtra) {
+    // the X tile starts zeroed: columns past the last block stay finite (x 0 in A_hi)
+    for (int i = threadIdx.x; i < T::X_BYTES / 16; i += T::kThreads)
+      reinterpret_cast<uint4*>(smem + T::OFF_X)[i] = make_uint4(0, 0, 0, 0);
+    fence_proxy_async_smem();
+  }
+  if (warp == T::kWarpMma) tmem_alloc(tmem_slot, T::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  bool dead = false;
+  if (warp == T::kWarpA) {
+    // ------------------------------------------------------------ A producer
+    if (lane == 0) {
+      prefetch_tmap(&map_hi);
+      prefetch_tmap(&map_lo);
+      pdl_wait();  // A_hi / A_lo come from the preceding prep kernel
+    }
+    __syncwarp();
+    int ia = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+      const int m0 = (t % p.num_m_tiles) * TM;
+      for (int c = 0; c < p.nmain; ++c) {
+        const int nx = (T::kExtra && extra_after(c, p.nmain)) ? 2 : 1;
+        for (int e = 0; e < nx; ++e, ++ia) {
+          const int as = ia % SA;
+          if (ia >= SA) spin_wait(&a_empty[as], ((ia / SA) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+          if (lane == 0) {
+            uint8_t* dst = smem + T::OFF_A + as * A_STAGE;
+            if (e == 0) {
+              mbar_arrive_expect_tx(&a_full[as], A_STAGE);
+              tma_load_2d(dst, &map_hi, c * CK, m0, &a_full[as]);
+              tma_load_2d(dst + A_PART, &map_lo, c * CK, m0, &a_full[as]);
+            } else {
+              mbar_arrive_expect_tx(&a_full[as], A_PART);
+              tma_load_2d(dst, &map_hi, p.K + (c / GRP) * CK, m0, &a_full[as]);
+            }
+          }
+          __syncwarp();
+        }
+      }
+    }
+  } else if (warp == T::kWarpRaw) {
+    // ------------------------------------------------------------ raw weight producer
+    if (lane == 0) prefetch_tmap(&map_raw);
+    __syncwarp();
+    int ir = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+      const int n0 = (t / p.num_m_tiles) * HN;
+      for (int r = 0; r < nraw; ++r, ++ir) {
+        const int rs = ir % SR;
+        if (ir >= SR) spin_wait(&raw_empty[rs], ((ir / SR) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&raw_full[rs], T::RAW_STAGE);
+          tma_load_2d(smem + T::OFF_RAW + rs * T::RAW_STAGE, &map_raw, r * (T::RAW_ROW / 2), n0, &raw_full[rs]);
+        }
+        __syncwarp();
+      }
+    }
+  } else if (warp == T::kWarpMma) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = idesc_f16<HN>();
+    const uint32_t a_base = smem_u32(smem + T::OFF_A);
+    const uint32_t w_base = smem_u32(smem + T::OFF_W);
+    const uint32_t x_base = smem_u32(smem + T::OFF_X);
+    int ia = 0, iw = 0;
+    for (int it = 0; it < my_tiles; ++it) {
+      const int acc = it & 1;
+      if (it >= 2) spin_wait(&tm_empty[acc], ((it >> 1) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+      tc_fence_after();
+      const uint32_t d_main = tmem_base + (uint32_t)(acc * 2 * HN);
+      const uint32_t d_corr = d_main + HN;
+      for (int c = 0; c < p.nmain; ++c, ++ia, ++iw) {
+        const int as = ia % SA, ws = iw % SW;
+        spin_wait(&a_full[as], (ia / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+        spin_wait(&w_full[ws], (iw / SW) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+        tc_fence_after();
+        if (lane == 0) {
+          const uint64_t ahi = sw128_desc(a_base + as * A_STAGE);
+          const uint64_t alo = sw128_desc(a_base + as * A_STAGE + A_PART);
+          const uint64_t whi = sw128_desc(w_base + ws * T::W_STAGE);
+          const uint64_t wlo = sw128_desc(w_base + ws * T::W_STAGE + T::W_PART);
+#pragma unroll
+          for (int j = 0; j < CK / 16; ++j)
+            mma_f16(d_main, ahi + (uint64_t)(2 * j), whi + (uint64_t)(2 * j), idesc, (c | j) ? 1u : 0u);
+#pragma unroll
+          for (int j = 0; j < CK / 16; ++j)
+            mma_f16(d_corr, alo + (uint64_t)(2 * j), whi + (uint64_t)(2 * j), idesc, (c | j) ? 1u : 0u);
+#pragma unroll
+          for (int j = 0; j < CK / 16; ++j)
+            mma_f16(d_corr, ahi + (uint64_t)(2 * j), wlo + (uint64_t)(2 * j), idesc, 1u);
+          mma_commit(&a_empty[as]);
+          mma_commit(&w_empty[ws]);
+        }
+        __syncwarp();
+        if (T::kExtra && extra_after(c, p.nmain)) {
+          // the group's X_w columns are complete: every converter arrived on
+          // w_full for the group's chunks after writing them
+          ++ia;
+          const int as2 = ia % SA;
+          spin_wait(&a_full[as2], (ia / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+          tc_fence_after();
+          if (lane == 0) {
+            const uint64_t ax = sw128_desc(a_base + as2 * A_STAGE);
+            const uint64_t xd = sw128_desc(x_base);
+#pragma unroll
+            for (int j = 0; j < CK / 16; ++j)
+              mma_f16(d_main, ax + (uint64_t)(2 * j), xd + (uint64_t)(2 * j), idesc, 1u);
+            mma_commit(&a_empty[as2]);
+            mma_commit(x_empty);
+          }
+          __syncwarp();
+        }
+      }
+      if (lane == 0) mma_commit(&tm_full[acc]);
+      __syncwarp();
+    }
+  } else if (warp < T::kWarpEpi) {
+    // ------------------------------------------------------------ converters
+    const int ct = threadIdx.x - T::kWarpConv * 32;  // 0 .. 2*HN-1
+    const int row = ct % HN;
+    const int b = ct / HN;                           // which 32-block of each 64-wide chunk
+    const int off0 = sw128_off(row, 0);
+    const uint32_t sh = (uint32_t)((b * T::BB) & 3) * 8;  // 16 * b for q4_0 / q8_0, 0 for q4_1
+    int ir = 0, gc = 0, gx = 0;
+    for (int it = 0; it < my_tiles; ++it) {
+      for (int r = 0; r < nraw; ++r, ++ir) {
+        const int rs = ir % SR;
+        spin_wait(&raw_full[rs], (ir / SR) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+        uint32_t w[4][T::NW];
+        {
+          const uint8_t* src = smem + T::OFF_RAW + rs * T::RAW_STAGE + row * T::RAW_ROW;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int o = (2 * j + b) * T::BB;
+            const uint32_t* s32 = reinterpret_cast<const uint32_t*>(src + (o & ~3));
+#pragma unroll
+            for (int i = 0; i < T::NW; ++i) w[j][i] = s32[i];
+          }
+        }
+        // the stage is refilled by TMA (async proxy): order these generic
+        // reads before the release, or a late read can see the next stage
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[rs]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j, ++gc) {
+          const int c = 4 * r + j;  // chunk within the tile
+          uint32_t hi[16], lo[16];
+          uint16_t xw;
+          convert_block<WT, T::NW>(w[j], sh, hi, lo, xw);
+          const int ws = gc % SW;
+          if (gc >= SW) spin_wait(&w_empty[ws], ((gc / SW) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+          uint8_t* th = smem + T::OFF_W + ws * T::W_STAGE;
+          uint8_t* tl = th + T::W_PART;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int o = off0 ^ ((4 * b + q) << 4);
+            *reinterpret_cast<uint4*>(th + o) = make_uint4(hi[4 * q], hi[4 * q + 1], hi[4 * q + 2], hi[4 * q + 3]);
+            *reinterpret_cast<uint4*>(tl + o) = make_uint4(lo[4 * q], lo[4 * q + 1], lo[4 * q + 2], lo[4 * q + 3]);
+          }
+          if constexpr (T::kExtra) {
+            if (c % GRP == 0) {  // first write of a group: the MMA must be done with the X tile
+              if (gx >= 1) spin_wait(x_empty, (gx - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+              ++gx;
+            }
+            const int col = (2 * c + b) & 63;
+            *reinterpret_cast<uint16_t*>(smem + T::OFF_X + (off0 ^ ((col >> 3) << 4)) + (col & 7) * 2) = xw;
+          }
+          fence_proxy_async_smem();  // generic-proxy writes -> tensor-core reads
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&w_full[ws]);
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    pdl_wait();  // rscale comes from the prep kernel
+    int it = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++it) {
+      const int acc = it & 1;
+      spin_wait(&tm_full[acc], (it >> 1) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+      tc_fence_after();
+      const int m0 = (t % p.num_m_tiles) * TM, n0 = (t / p.num_m_tiles) * HN;
+      const int m = m0 + row;
+      const float rs = m < p.M ? p.rscale[m] : 1.0f;
+      const uint32_t ta = tmem_base + lane_addr + (uint32_t)(acc * 2 * HN);
+#pragma unroll 1
+      for (int cg = 0; cg < HN / 16; ++cg) {
+        uint32_t v[16], u[16];
+        tmem_ld16(ta + cg * 16, v);
+        tmem_ld16(ta + HN + cg * 16, u);
+        tmem_ld_wait();
+        if (cg == HN / 16 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tm_empty[acc]);
+        }
+        if (m >= p.M) continue;
+        float o[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] = fmaf(__uint_as_float(u[i]), 1.0f / 2048.0f, __uint_as_float(v[i])) * rs;
+        const int nc = n0 + cg * 16;
+        const bool vec = nc + 16 <= p.N && ((p.out.ld | p.out.col0) & 3) == 0;
+        const size_t off = (size_t)m * p.out.ld + p.out.col0 + nc;
+        const int nd = SCATTER ? p.out.n_out : 1;
+        for (int dd = 0; dd < nd; ++dd) {
+          float* dst = p.out.ptr[dd] + off;
+          if (vec) {
+#pragma unroll
+            for (int i = 0; i < 16; i += 4)
+              *reinterpret_cast<float4*>(dst + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (nc + i < p.N) dst[i] = o[i];
+          }
+        }
+      }
+    }
+    if constexpr (SCATTER) __threadfence_system();  // peer stores visible before the host-side barrier
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == T::kWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, T::kTmemCols);
+  }
+}
+
+// A_hi[m, k] = fp16(a), A_lo[m, k] = fp16((a - A_hi) 2^11) with
+// a = q * d * 2^-e_m from the staging layout, plus the extra columns of
+// A_hi (scaled alike; zero past the last block); rscale[m] = 2^e_m. One CTA
+// per activation row. The per-row power of two puts the row's largest
+// magnitude in [2^14, 2^15), so nothing overflows fp16 and A_lo stays clear
+// of fp16 subnormals except for elements below 2^-17 of the row maximum.
+template <int WT>
+__global__ void __launch_bounds__(128) split_act_kernel(Act8 act, int M, int K, int Kp, __half* __restrict__ a_hi,
+                                                        __half* __restrict__ a_lo, float* __restrict__ rscale) {
+  pdl_launch_dependents();
+  const int nb = K / 32;
+  const int m = blockIdx.x;
+  if (m >= M) return;
+  const float2* ds = act.ds + (size_t)m * nb;
+  // block sum of the codes (the residual column's d sum q)
+  auto code_sum = [&](int b) {
+    const int4* src = reinterpret_cast<const int4*>(act.qs + (size_t)m * K + 32 * b);
+    const int4 c01 = src[0], c23 = src[1];
+    int q = 0;
+    q = __dp4a(c01.x, 0x01010101, q); q = __dp4a(c01.y, 0x01010101, q);
+    q = __dp4a(c01.z, 0x01010101, q); q = __dp4a(c01.w, 0x01010101, q);
+    q = __dp4a(c23.x, 0x01010101, q); q = __dp4a(c23.y, 0x01010101, q);
+    q = __dp4a(c23.z, 0x01010101, q); q = __dp4a(c23.w, 0x01010101, q);
+    return q;
+  };
+  // largest magnitude of the row: |q d| <= 127 |d|, and the residual column
+  // s - d sum q (usually below 32 |d|, but not when the stored fp16 d is a
+  // coarse subnormal far from the d the codes were quantised with)
+  float amax = 0.0f;
+  for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+    const float2 v = ds[b];
+    amax = fmaxf(amax, 127.0f * fabsf(v.x));
+    if constexpr (WT != KQ_Q8_0) amax = fmaxf(amax, fabsf(v.y - v.x * (float)code_sum(b)));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  __shared__ float wmax[4];
+  if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = fmaxf(fmaxf(wmax[0], wmax[1]), fmaxf(wmax[2], wmax[3]));
+  int e = 0;  // amax in [2^E, 2^(E+1)) -> e = E - 14
+  if (amax > 0.0f && isfinite(amax)) e = max(-100, min(100, (int)((__float_as_uint(amax) >> 23) & 0xFF) - 127 - 14));
+  const float down = __uint_as_float((uint32_t)(127 - e) << 23);  // 2^-e
+  if (threadIdx.x == 0) rscale[m] = __uint_as_float((uint32_t)(127 + e) << 23);
+  __half* hrow = a_hi + (size_t)m * Kp;
+  __half* lrow = a_lo + (size_t)m * K;
+  for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+    const float2 v = ds[b];
+    const float d = v.x * down;  // exact (power-of-two scaling)
+    const int4* src = reinterpret_cast<const int4*>(act.qs + (size_t)m * K + 32 * b);
+    const int4 c01 = src[0], c23 = src[1];
+    const int cw[8] = {c01.x, c01.y, c01.z, c01.w, c23.x, c23.y, c23.z, c23.w};
+    uint32_t hw[16], lw[16];
+    int qsum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+#pragma unroll
+      for (int e2 = 0; e2 < 4; e2 += 2) {
+        const int q0 = (int)(int8_t)((cw[i] >> (8 * e2)) & 0xFF);
+        const int q1 = (int)(int8_t)((cw[i] >> (8 * e2 + 8)) & 0xFF);
+        qsum += q0 + q1;
+        const float a0 = (float)q0 * d, a1 = (float)q1 * d;  // exact for an fp16 d
+        const __half2 h = __floats2half2_rn(a0, a1);
+        const float2 hf = __half22float2(h);
+        const __half2 l = __floats2half2_rn((a0 - hf.x) * 2048.0f, (a1 - hf.y) * 2048.0f);
+        hw[2 * i + e2 / 2] = *reinterpret_cast<const uint32_t*>(&h);
+        lw[2 * i + e2 / 2] = *reinterpret_cast<const uint32_t*>(&l);
+      }
+    }
+    uint4* dh = reinterpret_cast<uint4*>(hrow + 32 * b);
+    uint4* dl = reinterpret_cast<uint4*>(lrow + 32 * b);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      dh[i] = make_uint4(hw[4 * i], hw[4 * i + 1], hw[4 * i + 2], hw[4 * i + 3]);
+      dl[i] = make_uint4(lw[4 * i], lw[4 * i + 1], lw[4 * i + 2], lw[4 * i + 3]);
+    }
+    if constexpr (WT != KQ_Q8_0) hrow[K + b] = __float2half_rn((v.y - v.x * (float)qsum) * down);
+  }
+  for (int b = nb + threadIdx.x; b < Kp - K; b += blockDim.x) hrow[K + b] = __float2half_rn(0.0f);
+}
+
+template <int WT, int HN>
+kq_status_t launch_split(const void* w, Act8 act, const OutSpec& out, int M, int N, int K, cudaStream_t s, int* err) {
+  using T = SxTraits<WT, HN>;
+  const int nb = K / 32;
+  const int nmain = K / CK;
+  const int ngrp = T::kExtra ? (nmain + GRP - 1) / GRP : 0;
+  const int Kp = K + ngrp * CK;
+  const size_t hi_bytes = ((size_t)M * Kp * sizeof(__half) + 255) & ~(size_t)255;
+  const size_t lo_bytes = ((size_t)M * K * sizeof(__half) + 255) & ~(size_t)255;
+  uint8_t* ws = static_cast<uint8_t*>(workspace(WS_A16, hi_bytes + lo_bytes + (size_t)M * sizeof(float)));
+  if (!ws) return KQ_ERR_NOMEM;
+  __half* a_hi = reinterpret_cast<__half*>(ws);
+  __half* a_lo = reinterpret_cast<__half*>(ws + hi_bytes);
+  float* rscale = reinterpret_cast<float*>(ws + hi_bytes + lo_bytes);
+  split_act_kernel<WT><<<M, 128, 0, s>>>(act, M, K, Kp, a_hi, a_lo, rscale);
+  kq_status_t st = check_launch("split_act");
+  if (st) return st;
+  CUtensorMap m_hi, m_lo, m_raw;
+  if (!encode_map(&m_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a_hi, (uint64_t)Kp, (uint64_t)M, (uint64_t)Kp * 2, CK, TM,
+                  CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map(&m_lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a_lo, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, CK, TM,
+                  CU_TENSOR_MAP_SWIZZLE_128B))
+    return fail(KQ_ERR_CUDA, "tensor map (split activations) rejected");
+  const uint64_t rowbytes = (uint64_t)nb * T::BB;
+  if (!encode_map(&m_raw, CU_TENSOR_MAP_DATA_TYPE_UINT16, w, rowbytes / 2, (uint64_t)N, rowbytes, T::RAW_ROW / 2, HN,
+                  CU_TENSOR_MAP_SWIZZLE_NONE))
+    return fail(KQ_ERR_CUDA, "tensor map (weights) rejected");
+
+  const bool scatter = out.n_out > 1 || out.ld != N || out.col0 != 0;
+  auto kern = scatter ? gemm_split_kernel<WT, HN, true> : gemm_split_kernel<WT, HN, false>;
+  static unsigned attr_done[2] = {0, 0};
+  const int dev = current_device();
+  if (!(attr_done[scatter] & (1u << (dev & 31)))) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::SMEM);
+    if (e != cudaSuccess) return check_cuda(e, "gemm_split smem attribute");
+    attr_done[scatter] |= 1u << (dev & 31);
+  }
+  SxParams p;
+  p.M = M; p.N = N; p.K = K;
+  p.nmain = nmain; p.ngrp = ngrp;
+  p.num_m_tiles = (M + TM - 1) / TM;
+  p.num_tiles = p.num_m_tiles * ((N + HN - 1) / HN);
+  p.out = out;
+  p.rscale = rscale;
+  p.err = err ? err : device_error_word();
+  const int grid = std::max(1, std::min(sm_count(), p.num_tiles));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(T::kThreads);
+  cfg.dynamicSmemBytes = T::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;  // the prep kernel precedes on this stream
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, m_hi, m_lo, m_raw, p);
+  if (e != cudaSuccess) return check_cuda(e, "gemm_split launch");
+  return check_launch("gemm_split");
+}
+
+// Tile width for the shape: fewest tile rounds over the SMs, weighted by the
+// width (a round's time grows with it); ties go to the wider tile.
+int choose_hn(int M, int N) {
+  const int sms = std::max(1, sm_count());
+  const long long mt = (M + TM - 1) / TM;
+  auto cost = [&](int hn) {
+    const long long tiles = mt * ((N + hn - 1) / hn);
+    return ((tiles + sms - 1) / sms) * hn;
+  };
+  return cost(112) < cost(128) ? 112 : 128;
+}
+
+template <int WT>
+kq_status_t launch_split_wt(const void* w, Act8 act, const OutSpec& out, int M, int N, int K, cudaStream_t s,
+                            int* err) {
+  return choose_hn(M, N) == 112 ? launch_split<WT, 112>(w, act, out, M, N, K, s, err)
+                                : launch_split<WT, 128>(w, act, out, M, N, K, s, err);
+}
+
+}  // namespace
+
+bool gemm_split_supported(int wtype, int M, int N, int K, const void* w, Act8 act) {
+  (void)act;
+  return (wtype == KQ_Q4_0 || wtype == KQ_Q4_1 || wtype == KQ_Q8_0) && M > 8 && N >= 1 && K >= 256 &&
+         K % 256 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+}
+
+kq_status_t launch_gemm_split(int wtype, const void* w, Act8 act, const OutSpec& out, int M, int N, int K,
+                              cudaStream_t s, int* err) {
+  switch (wtype) {
+    case KQ_Q4_0: return launch_split_wt<KQ_Q4_0>(w, act, out, M, N, K, s, err);
+    case KQ_Q4_1: return launch_split_wt<KQ_Q4_1>(w, act, out, M, N, K, s, err);
+    case KQ_Q8_0: return launch_split_wt<KQ_Q8_0>(w, act, out, M, N, K, s, err);
+    default: return fail(KQ_ERR_INVALID, "unknown weight type %d", wtype);
+  }
+}
+
+}  // namespace kq

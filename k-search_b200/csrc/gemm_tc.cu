@@ -375,10 +375,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       }
 
+      // generic-proxy writes -> tensor-core reads, and generic reads of the
+      // TMA-refilled raw stage before its release
+      fence_proxy_async_smem();
       __syncwarp();
       if (sub == 1 && lane == 0) mbar_arrive(&raw_empty[rs]);  // both stages of the raw box are read
-      fence_proxy_async_smem();  // generic-proxy writes -> tensor-core reads
-      __syncwarp();
       if (lane == 0) mbar_arrive(&w_full[ws]);
     }
   } else {
@@ -468,6 +469,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld_wait();
 
       if (j == KSUB - 1) {
+        fence_proxy_async_smem();  // generic reads of the TMA-refilled scale stage, before its release
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&act_empty[as]);

@@ -325,6 +325,7 @@ __global__ void __launch_bounds__(32 * (kConsumerWarps + 1), 1)
           for (int m = 0; m < MR; ++m) part[rr * MR + m] += acc[m];
         }
       }
+      fence_proxy_async_smem();  // generic reads of the bulk-copy-refilled stage, before its release
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
     }

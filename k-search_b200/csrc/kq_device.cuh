@@ -142,6 +142,12 @@ __device__ __forceinline__ void mbar_wait_or_poison(uint64_t* bar, uint32_t pari
   if (!dead && !mbar_wait(bar, parity, err, code)) dead = true;
 }
 
+// Orders this thread's generic-proxy shared-memory accesses with later
+// async-proxy ones (TMA / bulk copies, tensor-core operand reads): after
+// writing an operand tile, and after reading a stage that a TMA refills once
+// it is released.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // ---- bulk async copy global -> shared (this CTA only) -----------------------
 // dst, src 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

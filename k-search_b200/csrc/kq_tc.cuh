@@ -101,7 +101,6 @@ __device__ __forceinline__ void tmem_st32_const(uint32_t taddr, uint32_t v) {
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // UMMA shared-memory descriptor: K-major, SWIZZLE_128B, 8-row groups 1024 B
 // apart (SBO), version 1 (sm_100).

@@ -146,6 +146,34 @@ def test_dequant_path_opt_in(cuda):
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
 
 
+def test_int8_path_opt_in(cuda):
+    """KQ_GEMM_PATH=int8 (int8 tcgen05 MMA per 32-block, int32 block sums
+    rescaled on the FP32 pipe), in a child process: the full parity bar on
+    every row, including rows of very small and very large magnitude."""
+    import os
+    import subprocess
+    import sys
+    code = (
+        "import sys, numpy as np, torch; sys.path[:0] = %r\n"
+        "import kq; from oracle import quant as Q\n"
+        "for wt in ('q4_0', 'q4_1', 'q8_0'):\n"
+        "  for (M, N, K) in ((16, 256, 512), (129, 200, 512), (256, 384, 4096), (40, 256, 2304)):\n"
+        "    rng = np.random.default_rng(M + N + K)\n"
+        "    w = Q.make_blocks(wt, rng, N, K); x = rng.standard_normal((M, K)).astype(np.float32)\n"
+        "    x[3] *= np.float32(1e-6); x[5] *= np.float32(1e3)\n"
+        "    for mode in ('f32', 'sum_x', 'sum_dq'):\n"
+        "      got = kq.gemm_f32act(torch.from_numpy(w).cuda(), torch.from_numpy(x).cuda(), M, N, K, wt, mode)\n"
+        "      ref = Q.gemm_f32act(wt, w, x, M, N, K, {'f32': Q.ACT_F32, 'sum_x': Q.SUM_X, 'sum_dq': Q.SUM_DQ}[mode])\n"
+        "      g = got.cpu().numpy().astype(np.float64)\n"
+        "      for m in range(M):\n"
+        "        ok, msg = Q.check_close(g[m:m + 1], ref[m:m + 1])\n"
+        "        assert ok, (wt, M, N, K, mode, m, msg)\n"
+        "print('ok')\n" % ([p for p in sys.path if p],))
+    env = dict(os.environ, KQ_GEMM_PATH="int8")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
+
+
 @pytest.mark.parametrize("wtype", ["q4_0", "q4_1", "q8_0"])
 @pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (4, 300, 1024), (8, 128, 256), (12, 64, 512)])
 def test_mul_mat_q_parity(cuda, wtype, M, N, K):
@@ -268,7 +296,7 @@ def test_quantize_rows_bit_exact(cuda, wtype):
     assert np.array_equal(got, g[wtype])
 
 
-@pytest.mark.parametrize("wtype", ["q4_0", "q8_0"])
+@pytest.mark.parametrize("wtype", ["q4_0", "q4_1", "q8_0"])
 def test_full_size_config_sampled_rows(cuda, wtype):
     """BASELINE configuration 1 shape (M=512, N=11008, K=4096): rows of the
     output are independent, so the oracle checks a sample of token rows that
@@ -286,6 +314,25 @@ def test_full_size_config_sampled_rows(cuda, wtype):
     ok, msg = Q.check_close(got[rows], ref)
     assert ok, msg
     assert Q.nmse(got[rows], Q.gemm_dequant_f32(wtype, w, x[rows], len(rows), N, K)) < 0.05
+
+
+@pytest.mark.parametrize("wtype", ["q4_0", "q4_1", "q8_0"])
+def test_gemm_several_tiles_per_cta(cuda, wtype):
+    """More output tiles than SMs (each persistent CTA runs two or three, so
+    both TMEM accumulator pairs and every ring wrap around), a partial last
+    tile in N and a partial last group of extra columns in K; every row is
+    checked, three calls in a row."""
+    import kq
+    M, N, K = 256, 10000, 2304   # 180 tiles of 128 x 112 on 148 SMs; K: 36 chunks, groups of 32 + 4
+    rng = np.random.default_rng(77)
+    w = Q.make_blocks(wtype, rng, N, K)
+    x = _x(rng, M, K)
+    ref = Q.gemm_f32act(wtype, w, x, M, N, K, Q.SUM_DQ)
+    wd, xd = _t(w, cuda), _t(x, cuda)
+    for rep in range(3):
+        got = kq.gemm_f32act(wd, xd, M, N, K, wtype, "sum_dq").cpu().numpy()
+        ok, msg = Q.check_close(got, ref)
+        assert ok, f"call {rep}: {msg}"
 
 
 def test_harness_mirror(cuda):

@@ -5,10 +5,13 @@ already reserved nearly all of HBM, or a latency-critical step that must not
 synchronise the device on a first-call allocation. This entry point stages the
 quantised activations in a fixed 1 MiB __device__ array instead. The test calls
 it through the C ABI twice in a row (different inputs, so a stale staging
-buffer would show) and compares each result with the allocating entry point
-kq_gemm_f32act, bit for bit and against the oracle tolerance the other tests
-use. It lives in its own file, collected last, and passes alone or after the
-rest of the suite.
+buffer would show) and checks each result against the oracle with the bar the
+other tests use. For GEMV shapes (M <= 8) both entry points run the same
+kernel, so the result must also equal kq_gemm_f32act's bit for bit; for
+M > 8 the allocating entry point runs the split-fp16 kernel (its fp16
+operands need workspace) while this one runs the int8 tensor-core kernel, so
+the two agree to the parity bar, not bitwise. It lives in its own file,
+collected last, and passes alone or after the rest of the suite.
 """
 import numpy as np
 import pytest
@@ -43,11 +46,14 @@ def test_noalloc_matches_allocating_entry(cuda, wtype, M, N, K):
         xh = rng.standard_normal((M, K)).astype(np.float32) * (1 + call)
         x = _dev(xh, cuda)
         got = _call(L.kq_gemm_f32act_noalloc, wtype, w, x, M, N, K, "f32")
-        ref = _call(L.kq_gemm_f32act, wtype, w, x, M, N, K, "f32")
+        alloc = _call(L.kq_gemm_f32act, wtype, w, x, M, N, K, "f32")
         torch.cuda.synchronize()
-        ok, msg = Q.check_close(got.cpu().numpy(), ref.cpu().numpy())
-        assert ok, f"call {call}: {msg}"
-        assert torch.equal(got, ref), f"call {call}: not bit-identical to kq_gemm_f32act"
+        ref = Q.gemm_f32act(wtype, w.cpu().numpy(), xh, M, N, K, Q.ACT_F32)
+        for name, t in (("noalloc", got), ("allocating", alloc)):
+            ok, msg = Q.check_close(t.cpu().numpy(), ref)
+            assert ok, f"call {call} {name}: {msg}"
+        if M <= 8:
+            assert torch.equal(got, alloc), f"call {call}: not bit-identical to kq_gemm_f32act"
     assert kq.device_error() == 0
 
 
