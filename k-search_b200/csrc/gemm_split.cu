@@ -11,11 +11,12 @@
 //   A_hi = fp16(a),  A_lo = fp16((a - A_hi) * 2^11)         exact: a has 19 bits
 //   W    = (q_w - 8) d_w  (q4_0),  q_w d_w + m_w  (q4_1),  q_w d_w  (q8_0)
 //   W_hi = fp16(W),  W_lo = fp16((W - W_hi) * 2^11)          exact for q4_0 / q8_0
-// and three tcgen05.mma.kind::f16 chains accumulate in fp32 TMEM:
-//   main = sum_k A_hi W_hi (+ the extra columns below)
-//   corr = sum_k A_lo W_hi + A_hi W_lo
+// and tcgen05.mma.kind::f16 accumulates in fp32 TMEM, per weight row n and
+// token m:
+//   main = sum_k W_hi A_hi (+ the extra columns below)
+//   corr = sum_k W_hi A_lo + W_lo A_hi
 //   out[m, n] = 2^e_m (main + 2^-11 corr)
-// The dropped A_lo W_lo term is 2^-22 of the products, so the result equals
+// The dropped W_lo A_lo term is 2^-22 of the products, so the result equals
 // the exact per-block sum up to fp32 accumulation order. For q4_0 / q4_1 the
 // difference between the plain product and the reference's formulas (its
 // stored block sum s_a instead of d_a sum q_a) rides in extra K columns:
@@ -24,21 +25,30 @@
 // Why this form: an int8 kind::i8 pipeline has to rescale a fresh int32 tile
 // per 32-wide K block on the FP32 pipe (at least two FMAs per element and
 // block); a single fp16 rounding of each operand is 2x faster but leaves a
-// relative error of ~3e-4 per element, outside the parity bar. The split
-// costs three kind::f16 MMAs per K chunk but no per-block epilogue, and each
-// converted weight chunk feeds three MMAs, which keeps the tensor pipe ahead
-// of the warp-to-warp hand-offs.
+// relative error of ~3e-4 per element, outside the parity bar.
 //
-// CTA: 128 tokens x HN weight rows, persistent over tiles (tokens fastest, so
-// co-running CTAs share weight tiles in L2). Warps (each loop runs on the
-// whole warp; lane 0 issues):
-//   0            A producer: A_hi and A_lo chunks (128 rows x 64 K, 128B-swizzled)
-//   1            raw weight producer: unchanged AoS q-blocks, HN rows x 8 blocks
-//   2            MMA issuer, owns the TMEM allocation
-//   3 .. 3+CW-1  converters: two threads per weight row, one 32-block of each
-//                64-wide K chunk, writing W_hi and W_lo (and X_w)
-//   next 4       epilogue: TMEM -> registers -> global fp32; two accumulator
-//                pairs so the next tile's MMAs overlap the stores
+// Operand placement: shared-memory bandwidth, not the tensor pipe, limits a
+// split GEMM whose operands all live in shared memory (every MMA re-reads
+// both operands there, and the converted weights are written there first).
+// Here the weights are the MMA's A operand and live in TMEM: converter
+// threads write W_hi / W_lo straight from registers with tcgen05.st, so they
+// never touch shared memory. The activations are the B operand (TMA into
+// 128B-swizzled shared memory, A_hi and A_lo tiles adjacent), so per 16-wide
+// K step two MMAs cover all three products:
+//   D[:, 0:256]   (+)= W_hi x [A_hi; A_lo]^T    main | first corr term
+//   D[:, 128:256]  += W_lo x A_hi^T             second corr term
+//
+// CTA: 128 weight rows (TMEM lanes, MMA M) x 128 tokens, persistent over
+// tiles (tokens fastest, so co-running CTAs share weight tiles in L2). Warps
+// (each loop runs on the whole warp; lane 0 issues):
+//   0       activation producer: A_hi + A_lo chunks (128 tokens x 64 K each)
+//   1       raw weight producer: unchanged AoS q-blocks, 128 rows x 8 blocks
+//   2       MMA issuer, owns the TMEM allocation
+//   3..10   converters: warp w serves the TMEM lane quarter w % 4 (32 weight
+//           rows) and one 32-block of each 64-wide K chunk
+//   11..14  epilogue: TMEM -> registers -> global fp32, one lane quarter each
+// TMEM: D = 256 columns (main 0..127, corr 128..255); four weight stages of
+// 64 columns (W_hi 32 | W_lo 32) behind it.
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -52,51 +62,52 @@ namespace {
 
 using namespace tc;
 
-constexpr int TM = 128;                  // tokens per tile (TMEM lanes)
+constexpr int TW = 128;                  // weight rows per tile (TMEM lanes, MMA M)
+constexpr int TT = 128;                  // tokens per tile
 constexpr int CK = 64;                   // K elements per chunk: one 128-byte swizzle atom of fp16
 constexpr int RB = 8;                    // blocks per raw weight stage (= 4 chunks)
 constexpr int GRP = 32;                  // main chunks per extra chunk (64 blocks)
-constexpr int SA = 3;                    // A stages (hi + lo)
-constexpr int A_PART = TM * 128;         // one 128-row x 128-byte tile
+constexpr int SA = 4;                    // activation stages (A_hi + A_lo)
+constexpr int SR = 2;                    // raw weight stages
+constexpr int SWT = 4;                   // weight stages in TMEM
+constexpr int A_PART = TT * 128;         // one 128-token x 128-byte tile
 constexpr int A_STAGE = 2 * A_PART;
 constexpr int kSmemLimit = 232448;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColD = 0;            // main 0..127, corr 128..255
+constexpr uint32_t kColW = 2 * TT;       // weight stage s at kColW + 64 s: W_hi 32 | W_lo 32
+constexpr int kWarpA = 0, kWarpRaw = 1, kWarpMma = 2, kWarpConv = 3, kConvWarps = 8, kWarpEpi = 11;
+constexpr int kWarps = kWarpEpi + 4;
+constexpr int kThreads = kWarps * 32;
 
-template <int WT, int HN>
+template <int WT>
 struct SxTraits {
-  static_assert(HN % 16 == 0 && HN >= 32 && HN <= 128, "MMA N");
   static constexpr int BB = WT == KQ_Q4_0 ? 18 : WT == KQ_Q4_1 ? 20 : 34;
   static constexpr bool kExtra = WT != KQ_Q8_0;
   static constexpr int RAW_ROW = RB * BB;  // 144 / 160 / 272 bytes
-  static constexpr int RAW_STAGE = HN * RAW_ROW;
-  static constexpr int W_PART = HN * 128;
-  static constexpr int W_STAGE = 2 * W_PART;
-  static constexpr int X_BYTES = kExtra ? W_PART : 0;
+  static constexpr int RAW_STAGE = TW * RAW_ROW;
+  static constexpr int X_BYTES = kExtra ? TW * 128 : 0;
   // 32-bit words a converter reads for one block: from the 4-byte boundary at
   // or below the block start (blocks are 2-byte aligned) to its end
   static constexpr int NW = WT == KQ_Q4_1 ? 5 : (BB + 2 + 3) / 4;
-  static constexpr int CW = HN / 16;       // converter warps: 2 threads per weight row
-  static constexpr int kWarpA = 0, kWarpRaw = 1, kWarpMma = 2, kWarpConv = 3, kWarpEpi = 3 + CW;
-  static constexpr int kWarps = kWarpEpi + 4;
-  static constexpr int kThreads = kWarps * 32;
-  static constexpr int kFixed = 1024 + 16 + 8 * (2 * SA + 2 * 3 + 2 * 2 + 2 * 2 + 1);
-  static constexpr int SR = (SA * A_STAGE + 3 * W_STAGE + X_BYTES + 2 * RAW_STAGE + kFixed <= kSmemLimit) ? 2 : 1;
-  static constexpr int SW = (SA * A_STAGE + 3 * W_STAGE + X_BYTES + SR * RAW_STAGE + kFixed <= kSmemLimit) ? 3 : 2;
+  // 16-byte loads per block window (from the 16-byte boundary at or below the
+  // block start): the block's words start at word ((start & 15) >> 2) < 4
+  static constexpr int NV = (3 + NW + 3) / 4;
   static constexpr int OFF_A = 0;
-  static constexpr int OFF_W = OFF_A + SA * A_STAGE;
-  static constexpr int OFF_X = OFF_W + SW * W_STAGE;
+  static constexpr int OFF_X = OFF_A + SA * A_STAGE;
   static constexpr int OFF_RAW = OFF_X + X_BYTES;
   static constexpr int OFF_BAR = OFF_RAW + SR * RAW_STAGE;
-  static constexpr int NBARS = 2 * SA + 2 * SW + 2 * SR + 2 * 2 + 1;
+  static constexpr int NBARS = 2 * SA + 2 * SR + 2 * SWT + 2 + 1;
   static constexpr int OFF_TMEM = OFF_BAR + NBARS * 8;
   static constexpr int SMEM = OFF_TMEM + 16 + 1024;
-  static constexpr uint32_t kTmemCols = 4 * HN <= 256 ? 256 : 512;
   static_assert(RAW_ROW % 16 == 0 && RAW_STAGE % 16 == 0, "raw stages stay 16-byte aligned");
-  static_assert(W_PART % 1024 == 0, "swizzled tiles stay 1024-byte aligned");
+  static_assert(OFF_RAW % 1024 == 0, "swizzled tiles stay 1024-byte aligned");
   static_assert(SMEM <= kSmemLimit, "shared memory budget");
-  static_assert(4 * HN <= 512, "two accumulator pairs fit in TMEM");
+  static_assert(kColW + 64 * SWT <= kTmemCols, "TMEM budget");
 };
 
-__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+// D (+)= A x B^T, A from shared memory (descriptor)
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
@@ -105,10 +116,31 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_
       : "memory");
 }
 
+// D (+)= A x B^T, A from TMEM (lane = row, two fp16 per 32-bit column)
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
 // Instruction descriptor, kind::f16: D f32, A = B = f16, both K-major, M = 128.
-template <int HN>
+template <int N>
 __host__ __device__ constexpr uint32_t idesc_f16() {
-  return (1u << 4) | ((uint32_t)(HN >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
+  static_assert(N % 16 == 0 && N >= 16 && N <= 256, "MMA N");
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(TW >> 4) << 24);
+}
+
+// 16 consecutive 32-bit TMEM columns of this thread's lane <- v
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
 }
 
 __device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
@@ -230,7 +262,7 @@ __device__ __forceinline__ void convert_block(const uint32_t (&w)[NW], uint32_t 
 struct SxParams {
   int M, N, K;
   int nmain, ngrp;
-  int num_m_tiles, num_tiles;
+  int num_t_tiles, num_tiles;
   OutSpec out;
   const float* rscale;  // per activation row: 2^e undoing the prep kernel's scaling
   int* err;
@@ -239,24 +271,23 @@ struct SxParams {
 // main chunk c is followed by an extra chunk (last of its group of GRP, or the last chunk)
 __device__ __forceinline__ bool extra_after(int c, int nmain) { return (c % GRP) == GRP - 1 || c == nmain - 1; }
 
-template <int WT, int HN, bool SCATTER>
-__global__ void __launch_bounds__(SxTraits<WT, HN>::kThreads, 1)
+template <int WT, bool SCATTER>
+__global__ void __launch_bounds__(kThreads, 1)
     gemm_split_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo,
                       const __grid_constant__ CUtensorMap map_raw, const __grid_constant__ SxParams p) {
-  using T = SxTraits<WT, HN>;
-  constexpr int SW = T::SW, SR = T::SR;
+  using T = SxTraits<WT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + T::OFF_BAR);
   uint64_t* a_full = bars;
   uint64_t* a_empty = a_full + SA;
-  uint64_t* w_full = a_empty + SA;
-  uint64_t* w_empty = w_full + SW;
-  uint64_t* raw_full = w_empty + SW;
+  uint64_t* raw_full = a_empty + SA;
   uint64_t* raw_empty = raw_full + SR;
-  uint64_t* tm_full = raw_empty + SR;
-  uint64_t* tm_empty = tm_full + 2;
-  uint64_t* x_empty = tm_empty + 2;
+  uint64_t* w_full = raw_empty + SR;
+  uint64_t* w_empty = w_full + SWT;
+  uint64_t* d_full = w_empty + SWT;
+  uint64_t* d_empty = d_full + 1;
+  uint64_t* x_empty = d_empty + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + T::OFF_TMEM);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -268,36 +299,34 @@ __global__ void __launch_bounds__(SxTraits<WT, HN>::kThreads, 1)
       mbar_init(&a_full[i], 1);
       mbar_init(&a_empty[i], 1);
     }
-    for (int i = 0; i < SW; ++i) {
-      mbar_init(&w_full[i], T::CW);
-      mbar_init(&w_empty[i], 1);
-    }
     for (int i = 0; i < SR; ++i) {
       mbar_init(&raw_full[i], 1);
-      mbar_init(&raw_empty[i], T::CW);
+      mbar_init(&raw_empty[i], kConvWarps);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&tm_full[i], 1);
-      mbar_init(&tm_empty[i], 4);
+    for (int i = 0; i < SWT; ++i) {
+      mbar_init(&w_full[i], kConvWarps);
+      mbar_init(&w_empty[i], 1);
     }
+    mbar_init(d_full, 1);
+    mbar_init(d_empty, 4);
     mbar_init(x_empty, 1);
     fence_mbar_init();
   }
   if constexpr (T::kExtra) {
     // the X tile starts zeroed: columns past the last block stay finite (x 0 in A_hi)
-    for (int i = threadIdx.x; i < T::X_BYTES / 16; i += T::kThreads)
+    for (int i = threadIdx.x; i < T::X_BYTES / 16; i += kThreads)
       reinterpret_cast<uint4*>(smem + T::OFF_X)[i] = make_uint4(0, 0, 0, 0);
     fence_proxy_async_smem();
   }
-  if (warp == T::kWarpMma) tmem_alloc(tmem_slot, T::kTmemCols);
+  if (warp == kWarpMma) tmem_alloc(tmem_slot, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   bool dead = false;
-  if (warp == T::kWarpA) {
-    // ------------------------------------------------------------ A producer
+  if (warp == kWarpA) {
+    // ------------------------------------------------------------ activation producer
     if (lane == 0) {
       prefetch_tmap(&map_hi);
       prefetch_tmap(&map_lo);
@@ -306,7 +335,7 @@ __global__ void __launch_bounds__(SxTraits<WT, HN>::kThreads, 1)
     __syncwarp();
     int ia = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
-      const int m0 = (t % p.num_m_tiles) * TM;
+      const int m0 = (t % p.num_t_tiles) * TT;
       for (int c = 0; c < p.nmain; ++c) {
         const int nx = (T::kExtra && extra_after(c, p.nmain)) ? 2 : 1;
         for (int e = 0; e < nx; ++e, ++ia) {
@@ -327,13 +356,13 @@ __global__ void __launch_bounds__(SxTraits<WT, HN>::kThreads, 1)
         }
       }
     }
-  } else if (warp == T::kWarpRaw) {
+  } else if (warp == kWarpRaw) {
     // ------------------------------------------------------------ raw weight producer
     if (lane == 0) prefetch_tmap(&map_raw);
     __syncwarp();
     int ir = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
-      const int n0 = (t / p.num_m_tiles) * HN;
+      const int n0 = (t / p.num_t_tiles) * TW;
       for (int r = 0; r < nraw; ++r, ++ir) {
         const int rs = ir % SR;
         if (ir >= SR) spin_wait(&raw_empty[rs], ((ir / SR) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
@@ -344,38 +373,30 @@ __global__ void __launch_bounds__(SxTraits<WT, HN>::kThreads, 1)
         __syncwarp();
       }
     }
-  } else if (warp == T::kWarpMma) {
+  } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
-    constexpr uint32_t idesc = idesc_f16<HN>();
+    constexpr uint32_t idesc2 = idesc_f16<2 * TT>();  // B = [A_hi; A_lo]: 256 rows, adjacent in the stage
+    constexpr uint32_t idesc1 = idesc_f16<TT>();
     const uint32_t a_base = smem_u32(smem + T::OFF_A);
-    const uint32_t w_base = smem_u32(smem + T::OFF_W);
     const uint32_t x_base = smem_u32(smem + T::OFF_X);
+    const uint32_t d_main = tmem_base + kColD, d_corr = tmem_base + kColD + TT;
     int ia = 0, iw = 0;
     for (int it = 0; it < my_tiles; ++it) {
-      const int acc = it & 1;
-      if (it >= 2) spin_wait(&tm_empty[acc], ((it >> 1) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+      if (it >= 1) spin_wait(d_empty, (it - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
       tc_fence_after();
-      const uint32_t d_main = tmem_base + (uint32_t)(acc * 2 * HN);
-      const uint32_t d_corr = d_main + HN;
       for (int c = 0; c < p.nmain; ++c, ++ia, ++iw) {
-        const int as = ia % SA, ws = iw % SW;
+        const int as = ia % SA, ws = iw % SWT;
         spin_wait(&a_full[as], (ia / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-        spin_wait(&w_full[ws], (iw / SW) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+        spin_wait(&w_full[ws], (iw / SWT) & 1, p.err, DEV_TIMEOUT_FULL, dead);
         tc_fence_after();
         if (lane == 0) {
-          const uint64_t ahi = sw128_desc(a_base + as * A_STAGE);
-          const uint64_t alo = sw128_desc(a_base + as * A_STAGE + A_PART);
-          const uint64_t whi = sw128_desc(w_base + ws * T::W_STAGE);
-          const uint64_t wlo = sw128_desc(w_base + ws * T::W_STAGE + T::W_PART);
+          const uint64_t bdesc = sw128_desc(a_base + as * A_STAGE);  // A_hi rows, then A_lo rows
+          const uint32_t whi = tmem_base + kColW + 64 * ws, wlo = whi + 32;
 #pragma unroll
-          for (int j = 0; j < CK / 16; ++j)
-            mma_f16(d_main, ahi + (uint64_t)(2 * j), whi + (uint64_t)(2 * j), idesc, (c | j) ? 1u : 0u);
-#pragma unroll
-          for (int j = 0; j < CK / 16; ++j)
-            mma_f16(d_corr, alo + (uint64_t)(2 * j), whi + (uint64_t)(2 * j), idesc, (c | j) ? 1u : 0u);
-#pragma unroll
-          for (int j = 0; j < CK / 16; ++j)
-            mma_f16(d_corr, ahi + (uint64_t)(2 * j), wlo + (uint64_t)(2 * j), idesc, 1u);
+          for (int j = 0; j < CK / 16; ++j) {
+            mma_ts(d_main, whi + 8 * j, bdesc + (uint64_t)(2 * j), idesc2, (c | j) ? 1u : 0u);
+            mma_ts(d_corr, wlo + 8 * j, bdesc + (uint64_t)(2 * j), idesc1, 1u);
+          }
           mma_commit(&a_empty[as]);
           mma_commit(&w_empty[ws]);
         }
@@ -388,41 +409,56 @@ __global__ void __launch_bounds__(SxTraits<WT, HN>::kThreads, 1)
           spin_wait(&a_full[as2], (ia / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
           tc_fence_after();
           if (lane == 0) {
-            const uint64_t ax = sw128_desc(a_base + as2 * A_STAGE);
             const uint64_t xd = sw128_desc(x_base);
+            const uint64_t bx = sw128_desc(a_base + as2 * A_STAGE);
 #pragma unroll
             for (int j = 0; j < CK / 16; ++j)
-              mma_f16(d_main, ax + (uint64_t)(2 * j), xd + (uint64_t)(2 * j), idesc, 1u);
+              mma_ss(d_main, xd + (uint64_t)(2 * j), bx + (uint64_t)(2 * j), idesc1, 1u);
             mma_commit(&a_empty[as2]);
             mma_commit(x_empty);
           }
           __syncwarp();
         }
       }
-      if (lane == 0) mma_commit(&tm_full[acc]);
+      if (lane == 0) mma_commit(d_full);
       __syncwarp();
     }
-  } else if (warp < T::kWarpEpi) {
+  } else if (warp < kWarpEpi) {
     // ------------------------------------------------------------ converters
-    const int ct = threadIdx.x - T::kWarpConv * 32;  // 0 .. 2*HN-1
-    const int row = ct % HN;
-    const int b = ct / HN;                           // which 32-block of each 64-wide chunk
-    const int off0 = sw128_off(row, 0);
+    const int cw = warp - kWarpConv;                 // 0..7
+    const int quarter = warp & 3;                    // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;             // weight row within the tile
+    const int b = cw >> 2;                           // which 32-block of each 64-wide chunk
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    const int offx = (row >> 3) * 1024 + (row & 7) * 128;  // X tile row (128B-swizzled, K-major)
     const uint32_t sh = (uint32_t)((b * T::BB) & 3) * 8;  // 16 * b for q4_0 / q8_0, 0 for q4_1
     int ir = 0, gc = 0, gx = 0;
     for (int it = 0; it < my_tiles; ++it) {
       for (int r = 0; r < nraw; ++r, ++ir) {
         const int rs = ir % SR;
         spin_wait(&raw_full[rs], (ir / SR) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+        // 16-byte window loads: rows are 16-byte multiples apart, so eight
+        // consecutive rows read eight distinct bank groups
         uint32_t w[4][T::NW];
         {
           const uint8_t* src = smem + T::OFF_RAW + rs * T::RAW_STAGE + row * T::RAW_ROW;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int o = (2 * j + b) * T::BB;
-            const uint32_t* s32 = reinterpret_cast<const uint32_t*>(src + (o & ~3));
+            const uint4* s4 = reinterpret_cast<const uint4*>(src + (o & ~15));
+            uint32_t win[4 * T::NV];
 #pragma unroll
-            for (int i = 0; i < T::NW; ++i) w[j][i] = s32[i];
+            for (int v = 0; v < T::NV; ++v) {
+              const uint4 q = s4[v];
+              win[4 * v] = q.x;
+              win[4 * v + 1] = q.y;
+              win[4 * v + 2] = q.z;
+              win[4 * v + 3] = q.w;
+            }
+            const int wo0 = (((2 * j) * T::BB) & 15) >> 2;      // compile-time after unrolling
+            const int wo1 = (((2 * j + 1) * T::BB) & 15) >> 2;
+#pragma unroll
+            for (int i = 0; i < T::NW; ++i) w[j][i] = b ? win[wo1 + i] : win[wo0 + i];
           }
         }
         // the stage is refilled by TMA (async proxy): order these generic
@@ -436,25 +472,24 @@ __global__ void __launch_bounds__(SxTraits<WT, HN>::kThreads, 1)
           uint32_t hi[16], lo[16];
           uint16_t xw;
           convert_block<WT, T::NW>(w[j], sh, hi, lo, xw);
-          const int ws = gc % SW;
-          if (gc >= SW) spin_wait(&w_empty[ws], ((gc / SW) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
-          uint8_t* th = smem + T::OFF_W + ws * T::W_STAGE;
-          uint8_t* tl = th + T::W_PART;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int o = off0 ^ ((4 * b + q) << 4);
-            *reinterpret_cast<uint4*>(th + o) = make_uint4(hi[4 * q], hi[4 * q + 1], hi[4 * q + 2], hi[4 * q + 3]);
-            *reinterpret_cast<uint4*>(tl + o) = make_uint4(lo[4 * q], lo[4 * q + 1], lo[4 * q + 2], lo[4 * q + 3]);
-          }
+          const int ws = gc % SWT;
+          if (gc >= SWT) spin_wait(&w_empty[ws], ((gc / SWT) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+          tc_fence_after();
+          const uint32_t wcol = tmem_base + lane_addr + kColW + 64 * ws + 16 * b;
+          tmem_st16(wcol, hi);
+          tmem_st16(wcol + 32, lo);
           if constexpr (T::kExtra) {
             if (c % GRP == 0) {  // first write of a group: the MMA must be done with the X tile
               if (gx >= 1) spin_wait(x_empty, (gx - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
               ++gx;
             }
             const int col = (2 * c + b) & 63;
-            *reinterpret_cast<uint16_t*>(smem + T::OFF_X + (off0 ^ ((col >> 3) << 4)) + (col & 7) * 2) = xw;
+            *reinterpret_cast<uint16_t*>(smem + T::OFF_X + (offx + ((((col >> 3) ^ (row & 7))) << 4)) + (col & 7) * 2) =
+                xw;
+            fence_proxy_async_smem();  // generic-proxy write -> tensor-core read
           }
-          fence_proxy_async_smem();  // generic-proxy writes -> tensor-core reads
+          tmem_st_wait();
+          tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&w_full[ws]);
         }
@@ -463,47 +498,38 @@ __global__ void __launch_bounds__(SxTraits<WT, HN>::kThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
+    const int row = quarter * 32 + lane;  // weight row within the tile
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
     pdl_wait();  // rscale comes from the prep kernel
     int it = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++it) {
-      const int acc = it & 1;
-      spin_wait(&tm_full[acc], (it >> 1) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+      spin_wait(d_full, it & 1, p.err, DEV_TIMEOUT_FULL, dead);
       tc_fence_after();
-      const int m0 = (t % p.num_m_tiles) * TM, n0 = (t / p.num_m_tiles) * HN;
-      const int m = m0 + row;
-      const float rs = m < p.M ? p.rscale[m] : 1.0f;
-      const uint32_t ta = tmem_base + lane_addr + (uint32_t)(acc * 2 * HN);
+      const int m0 = (t % p.num_t_tiles) * TT, n0 = (t / p.num_t_tiles) * TW;
+      const int n = n0 + row;
+      const int tokens = min(TT, p.M - m0);
+      const int nd = SCATTER ? p.out.n_out : 1;
+      // 16 tokens at a time; D is released after the last group's loads
 #pragma unroll 1
-      for (int cg = 0; cg < HN / 16; ++cg) {
+      for (int g = 0; g < TT / 16; ++g) {
         uint32_t v[16], u[16];
-        tmem_ld16(ta + cg * 16, v);
-        tmem_ld16(ta + HN + cg * 16, u);
+        tmem_ld16(tmem_base + lane_addr + kColD + 16 * g, v);
+        tmem_ld16(tmem_base + lane_addr + kColD + TT + 16 * g, u);
         tmem_ld_wait();
-        if (cg == HN / 16 - 1) {
+        if (g == TT / 16 - 1) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&tm_empty[acc]);
+          if (lane == 0) mbar_arrive(d_empty);
         }
-        if (m >= p.M) continue;
-        float o[16];
+        if (n < p.N) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) o[i] = fmaf(__uint_as_float(u[i]), 1.0f / 2048.0f, __uint_as_float(v[i])) * rs;
-        const int nc = n0 + cg * 16;
-        const bool vec = nc + 16 <= p.N && ((p.out.ld | p.out.col0) & 3) == 0;
-        const size_t off = (size_t)m * p.out.ld + p.out.col0 + nc;
-        const int nd = SCATTER ? p.out.n_out : 1;
-        for (int dd = 0; dd < nd; ++dd) {
-          float* dst = p.out.ptr[dd] + off;
-          if (vec) {
-#pragma unroll
-            for (int i = 0; i < 16; i += 4)
-              *reinterpret_cast<float4*>(dst + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
-          } else {
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              if (nc + i < p.N) dst[i] = o[i];
+          for (int i = 0; i < 16; ++i) {
+            const int tk = 16 * g + i;
+            if (tk < tokens) {
+              const float o = fmaf(__uint_as_float(u[i]), 1.0f / 2048.0f, __uint_as_float(v[i])) * p.rscale[m0 + tk];
+              const size_t off = (size_t)(m0 + tk) * p.out.ld + p.out.col0 + n;
+              for (int dd = 0; dd < nd; ++dd) p.out.ptr[dd][off] = o;
+            }
           }
         }
       }
@@ -513,9 +539,9 @@ __global__ void __launch_bounds__(SxTraits<WT, HN>::kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == T::kWarpMma) {
+  if (warp == kWarpMma) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, T::kTmemCols);
+    tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
@@ -600,9 +626,9 @@ __global__ void __launch_bounds__(128) split_act_kernel(Act8 act, int M, int K, 
   for (int b = nb + threadIdx.x; b < Kp - K; b += blockDim.x) hrow[K + b] = __float2half_rn(0.0f);
 }
 
-template <int WT, int HN>
+template <int WT>
 kq_status_t launch_split(const void* w, Act8 act, const OutSpec& out, int M, int N, int K, cudaStream_t s, int* err) {
-  using T = SxTraits<WT, HN>;
+  using T = SxTraits<WT>;
   const int nb = K / 32;
   const int nmain = K / CK;
   const int ngrp = T::kExtra ? (nmain + GRP - 1) / GRP : 0;
@@ -618,18 +644,18 @@ kq_status_t launch_split(const void* w, Act8 act, const OutSpec& out, int M, int
   kq_status_t st = check_launch("split_act");
   if (st) return st;
   CUtensorMap m_hi, m_lo, m_raw;
-  if (!encode_map(&m_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a_hi, (uint64_t)Kp, (uint64_t)M, (uint64_t)Kp * 2, CK, TM,
+  if (!encode_map(&m_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a_hi, (uint64_t)Kp, (uint64_t)M, (uint64_t)Kp * 2, CK, TT,
                   CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_map(&m_lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a_lo, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, CK, TM,
+      !encode_map(&m_lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a_lo, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, CK, TT,
                   CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(KQ_ERR_CUDA, "tensor map (split activations) rejected");
   const uint64_t rowbytes = (uint64_t)nb * T::BB;
-  if (!encode_map(&m_raw, CU_TENSOR_MAP_DATA_TYPE_UINT16, w, rowbytes / 2, (uint64_t)N, rowbytes, T::RAW_ROW / 2, HN,
+  if (!encode_map(&m_raw, CU_TENSOR_MAP_DATA_TYPE_UINT16, w, rowbytes / 2, (uint64_t)N, rowbytes, T::RAW_ROW / 2, TW,
                   CU_TENSOR_MAP_SWIZZLE_NONE))
     return fail(KQ_ERR_CUDA, "tensor map (weights) rejected");
 
   const bool scatter = out.n_out > 1 || out.ld != N || out.col0 != 0;
-  auto kern = scatter ? gemm_split_kernel<WT, HN, true> : gemm_split_kernel<WT, HN, false>;
+  auto kern = scatter ? gemm_split_kernel<WT, true> : gemm_split_kernel<WT, false>;
   static unsigned attr_done[2] = {0, 0};
   const int dev = current_device();
   if (!(attr_done[scatter] & (1u << (dev & 31)))) {
@@ -640,15 +666,15 @@ kq_status_t launch_split(const void* w, Act8 act, const OutSpec& out, int M, int
   SxParams p;
   p.M = M; p.N = N; p.K = K;
   p.nmain = nmain; p.ngrp = ngrp;
-  p.num_m_tiles = (M + TM - 1) / TM;
-  p.num_tiles = p.num_m_tiles * ((N + HN - 1) / HN);
+  p.num_t_tiles = (M + TT - 1) / TT;
+  p.num_tiles = p.num_t_tiles * ((N + TW - 1) / TW);
   p.out = out;
   p.rscale = rscale;
   p.err = err ? err : device_error_word();
   const int grid = std::max(1, std::min(sm_count(), p.num_tiles));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(T::kThreads);
+  cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = T::SMEM;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -659,25 +685,6 @@ kq_status_t launch_split(const void* w, Act8 act, const OutSpec& out, int M, int
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, m_hi, m_lo, m_raw, p);
   if (e != cudaSuccess) return check_cuda(e, "gemm_split launch");
   return check_launch("gemm_split");
-}
-
-// Tile width for the shape: fewest tile rounds over the SMs, weighted by the
-// width (a round's time grows with it); ties go to the wider tile.
-int choose_hn(int M, int N) {
-  const int sms = std::max(1, sm_count());
-  const long long mt = (M + TM - 1) / TM;
-  auto cost = [&](int hn) {
-    const long long tiles = mt * ((N + hn - 1) / hn);
-    return ((tiles + sms - 1) / sms) * hn;
-  };
-  return cost(112) < cost(128) ? 112 : 128;
-}
-
-template <int WT>
-kq_status_t launch_split_wt(const void* w, Act8 act, const OutSpec& out, int M, int N, int K, cudaStream_t s,
-                            int* err) {
-  return choose_hn(M, N) == 112 ? launch_split<WT, 112>(w, act, out, M, N, K, s, err)
-                                : launch_split<WT, 128>(w, act, out, M, N, K, s, err);
 }
 
 }  // namespace
@@ -691,9 +698,9 @@ bool gemm_split_supported(int wtype, int M, int N, int K, const void* w, Act8 ac
 kq_status_t launch_gemm_split(int wtype, const void* w, Act8 act, const OutSpec& out, int M, int N, int K,
                               cudaStream_t s, int* err) {
   switch (wtype) {
-    case KQ_Q4_0: return launch_split_wt<KQ_Q4_0>(w, act, out, M, N, K, s, err);
-    case KQ_Q4_1: return launch_split_wt<KQ_Q4_1>(w, act, out, M, N, K, s, err);
-    case KQ_Q8_0: return launch_split_wt<KQ_Q8_0>(w, act, out, M, N, K, s, err);
+    case KQ_Q4_0: return launch_split<KQ_Q4_0>(w, act, out, M, N, K, s, err);
+    case KQ_Q4_1: return launch_split<KQ_Q4_1>(w, act, out, M, N, K, s, err);
+    case KQ_Q8_0: return launch_split<KQ_Q8_0>(w, act, out, M, N, K, s, err);
     default: return fail(KQ_ERR_INVALID, "unknown weight type %d", wtype);
   }
 }
