@@ -17,9 +17,10 @@
 // device current, resolves the device addresses with cudaGetSymbolAddress and
 // caches them; make that first call before any stream capture. Every call
 // shares the array and it keeps the last call's contents: the quantiser
-// overwrites every staging byte a call reads, so nothing needs clearing, but
-// two calls whose executions overlap on the GPU (different streams, no
-// ordering between them) race on the array.
+// overwrites every staging byte a call reads, and the error word the kernels
+// record timeouts in is cleared at the start of each call; two calls whose
+// executions overlap on the GPU (different streams, no ordering between
+// them) race on both.
 #include <cstdio>
 #include <mutex>
 
@@ -30,8 +31,8 @@ namespace {
 
 constexpr size_t kNoAllocScratchBytes = 1u << 20;  // activation staging limit (1 MiB)
 
-__device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
-__device__ int g_noalloc_error;  // device error word of the kernels launched from here
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+static __device__ int g_noalloc_error;  // device error word of the kernels launched from here
 
 constexpr int kMaxDev = 64;
 struct NoAllocPtrs {
@@ -91,6 +92,8 @@ extern "C" kq_status_t kq_gemm_f32act_noalloc(int wtype, const void* w, const fl
   kq_status_t st = device_ptrs(&p);
   if (st) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = check_cuda(cudaMemsetAsync(p.err, 0, sizeof(int), s), "clear the no-alloc error word");
+  if (st) return st;
   Act8 act = act8_view(p.scratch, M, K);
   st = launch_quantize_act(x, act, M, K, act_mode, s);
   if (st) return st;

@@ -52,6 +52,8 @@ def test_noalloc_matches_allocating_entry(cuda, wtype, M, N, K):
         for name, t in (("noalloc", got), ("allocating", alloc)):
             ok, msg = Q.check_close(t.cpu().numpy(), ref)
             assert ok, f"call {call} {name}: {msg}"
+        ok, msg = Q.check_close(got.cpu().numpy(), alloc.cpu().numpy())  # the two entry points, directly
+        assert ok, f"call {call} noalloc vs kq_gemm_f32act: {msg}"
         if M <= 8:
             assert torch.equal(got, alloc), f"call {call}: not bit-identical to kq_gemm_f32act"
     assert kq.device_error() == 0
