@@ -38,15 +38,18 @@
 //   D[:, 0:256]   (+)= W_hi x [A_hi; A_lo]^T    main | first corr term
 //   D[:, 128:256]  += W_lo x A_hi^T             second corr term
 //
-// CTA: 128 weight rows (TMEM lanes, MMA M) x 128 tokens, persistent over
-// tiles (tokens fastest, so co-running CTAs share weight tiles in L2). Warps
-// (each loop runs on the whole warp; lane 0 issues):
+// CTA: 128 weight rows (TMEM lanes, MMA M) x 128 tokens per tile, one
+// persistent CTA per SM; each CTA runs an equal share of all tiles' K groups
+// (stream-K, see for_items), so a tile can be split between CTAs and summed
+// by its owner from the others' partials. Warps (each loop runs on the whole
+// warp; lane 0 issues):
 //   0       activation producer: A_hi + A_lo chunks (128 tokens x 64 K each)
 //   1       raw weight producer: unchanged AoS q-blocks, 128 rows x 8 blocks
 //   2       MMA issuer, owns the TMEM allocation
 //   3..10   converters: warp w serves the TMEM lane quarter w % 4 (32 weight
 //           rows) and one 32-block of each 64-wide K chunk
-//   11..14  epilogue: TMEM -> registers -> global fp32, one lane quarter each
+//   11..18  epilogue: TMEM -> registers -> global fp32, two warps per lane
+//           quarter (64 tokens each)
 // TMEM: D = 256 columns (main 0..127, corr 128..255); four weight stages of
 // 64 columns (W_hi 32 | W_lo 32) behind it.
 #include <cuda_fp16.h>
@@ -77,7 +80,9 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColD = 0;            // main 0..127, corr 128..255
 constexpr uint32_t kColW = 2 * TT;       // weight stage s at kColW + 64 s: W_hi 32 | W_lo 32
 constexpr int kWarpA = 0, kWarpRaw = 1, kWarpMma = 2, kWarpConv = 3, kConvWarps = 8, kWarpEpi = 11;
-constexpr int kWarps = kWarpEpi + 4;
+constexpr int kEpiWarps = 8;             // two per TMEM lane quarter
+constexpr int kEpiTok = TT / 2;          // tokens per epilogue warp
+constexpr int kWarps = kWarpEpi + kEpiWarps;
 constexpr int kThreads = kWarps * 32;
 
 template <int WT>
@@ -176,6 +181,23 @@ __device__ __forceinline__ void spin_wait(uint64_t* bar, uint32_t parity, int* e
   }
 }
 
+// Bounded wait on the suspending probe, for waits that usually last long
+// (a role idle until a whole tile or stage ring has moved on): the warp
+// yields its issue slots to the warps doing the work instead of spinning.
+__device__ __forceinline__ void sleep_wait(uint64_t* bar, uint32_t parity, int* err, int code, bool& dead) {
+  if (dead) return;
+  const uint64_t t0 = globaltimer_ns();
+#pragma unroll 1
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return;
+    if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+      record_error(err, code);
+      dead = true;
+      return;
+    }
+  }
+}
+
 // One weight block -> 16 packed fp16 pairs of W_hi and of W_lo (element pairs
 // 2i, 2i+1 in K order) and the block's X_w. `w` holds the block's bytes from
 // the 4-byte boundary at or below its start; `sh` = 8 * (start & 3).
@@ -263,10 +285,38 @@ struct SxParams {
   int M, N, K;
   int nmain, ngrp;
   int num_t_tiles, num_tiles;
+  int upt, num_units;   // K units (groups of GRP chunks) per tile, units in all
   OutSpec out;
   const float* rscale;  // per activation row: 2^e undoing the prep kernel's scaling
+  int* flags;           // per CTA: epilogue warps done writing its partial tile (zeroed by the prep kernel)
+  float* partial;       // per CTA: [TT tokens][TW rows] partial sums of the tile it starts inside
   int* err;
 };
+
+// Work schedule (stream-K over K groups): every tile's K range is cut into
+// units of GRP chunks (one extra-column group each); CTA b takes units
+// [U b / G, U (b + 1) / G) in order, so the SMs get equal work whatever the
+// tile count. A work item is the part of one tile inside a CTA's range. The
+// CTA holding a tile's first unit owns the tile; the others (whose ranges
+// start inside it: each CTA at most once, on its first item) write partial
+// sums that the owner adds, in CTA order, after its own part.
+__device__ __forceinline__ int unit_begin(const SxParams& p, int b) {
+  return (int)(((long long)p.num_units * b) / (long long)gridDim.x);
+}
+struct Item {
+  int t, c0, c1;  // tile, chunk range [c0, c1)
+};
+// Calls f(item) for each work item of this CTA, in order.
+template <typename F>
+__device__ __forceinline__ void for_items(const SxParams& p, F&& f) {
+  const int ue = unit_begin(p, blockIdx.x + 1);
+  for (int u = unit_begin(p, blockIdx.x); u < ue;) {
+    const int t = u / p.upt;
+    const int uend = min(ue, (t + 1) * p.upt);
+    f(Item{t, (u - t * p.upt) * GRP, min((uend - t * p.upt) * GRP, p.nmain)});
+    u = uend;
+  }
+}
 
 // main chunk c is followed by an extra chunk (last of its group of GRP, or the last chunk)
 __device__ __forceinline__ bool extra_after(int c, int nmain) { return (c % GRP) == GRP - 1 || c == nmain - 1; }
@@ -291,8 +341,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + T::OFF_TMEM);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nraw = p.nmain / 4;
-  const int my_tiles = (p.num_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < SA; ++i) {
@@ -308,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&w_empty[i], 1);
     }
     mbar_init(d_full, 1);
-    mbar_init(d_empty, 4);
+    mbar_init(d_empty, kEpiWarps);
     mbar_init(x_empty, 1);
     fence_mbar_init();
   }
@@ -334,9 +382,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
     int ia = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
-      const int m0 = (t % p.num_t_tiles) * TT;
-      for (int c = 0; c < p.nmain; ++c) {
+    for_items(p, [&](const Item& w) {
+      const int m0 = (w.t % p.num_t_tiles) * TT;
+      for (int c = w.c0; c < w.c1; ++c) {
         const int nx = (T::kExtra && extra_after(c, p.nmain)) ? 2 : 1;
         for (int e = 0; e < nx; ++e, ++ia) {
           const int as = ia % SA;
@@ -355,15 +403,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
         }
       }
-    }
+    });
   } else if (warp == kWarpRaw) {
     // ------------------------------------------------------------ raw weight producer
     if (lane == 0) prefetch_tmap(&map_raw);
     __syncwarp();
     int ir = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
-      const int n0 = (t / p.num_t_tiles) * TW;
-      for (int r = 0; r < nraw; ++r, ++ir) {
+    for_items(p, [&](const Item& w) {
+      const int n0 = (w.t / p.num_t_tiles) * TW;
+      for (int r = w.c0 / 4; r < w.c1 / 4; ++r, ++ir) {
         const int rs = ir % SR;
         if (ir >= SR) spin_wait(&raw_empty[rs], ((ir / SR) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
         if (lane == 0) {
@@ -372,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
       }
-    }
+    });
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t idesc2 = idesc_f16<2 * TT>();  // B = [A_hi; A_lo]: 256 rows, adjacent in the stage
@@ -380,11 +428,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t a_base = smem_u32(smem + T::OFF_A);
     const uint32_t x_base = smem_u32(smem + T::OFF_X);
     const uint32_t d_main = tmem_base + kColD, d_corr = tmem_base + kColD + TT;
-    int ia = 0, iw = 0;
-    for (int it = 0; it < my_tiles; ++it) {
+    int ia = 0, iw = 0, it = 0;
+    for_items(p, [&](const Item& w) {
       if (it >= 1) spin_wait(d_empty, (it - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
       tc_fence_after();
-      for (int c = 0; c < p.nmain; ++c, ++ia, ++iw) {
+      for (int c = w.c0; c < w.c1; ++c, ++ia, ++iw) {
         const int as = ia % SA, ws = iw % SWT;
         spin_wait(&a_full[as], (ia / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
         spin_wait(&w_full[ws], (iw / SWT) & 1, p.err, DEV_TIMEOUT_FULL, dead);
@@ -394,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t whi = tmem_base + kColW + 64 * ws, wlo = whi + 32;
 #pragma unroll
           for (int j = 0; j < CK / 16; ++j) {
-            mma_ts(d_main, whi + 8 * j, bdesc + (uint64_t)(2 * j), idesc2, (c | j) ? 1u : 0u);
+            mma_ts(d_main, whi + 8 * j, bdesc + (uint64_t)(2 * j), idesc2, (c > w.c0 || j > 0) ? 1u : 0u);
             mma_ts(d_corr, wlo + 8 * j, bdesc + (uint64_t)(2 * j), idesc1, 1u);
           }
           mma_commit(&a_empty[as]);
@@ -422,7 +470,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (lane == 0) mma_commit(d_full);
       __syncwarp();
-    }
+      ++it;
+    });
   } else if (warp < kWarpEpi) {
     // ------------------------------------------------------------ converters
     const int cw = warp - kWarpConv;                 // 0..7
@@ -433,17 +482,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int offx = (row >> 3) * 1024 + (row & 7) * 128;  // X tile row (128B-swizzled, K-major)
     const uint32_t sh = (uint32_t)((b * T::BB) & 3) * 8;  // 16 * b for q4_0 / q8_0, 0 for q4_1
     int ir = 0, gc = 0, gx = 0;
-    for (int it = 0; it < my_tiles; ++it) {
-      for (int r = 0; r < nraw; ++r, ++ir) {
+    for_items(p, [&](const Item& wi) {
+      for (int r = wi.c0 / 4; r < wi.c1 / 4; ++r, ++ir) {
         const int rs = ir % SR;
         spin_wait(&raw_full[rs], (ir / SR) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-        // 16-byte window loads: rows are 16-byte multiples apart, so eight
-        // consecutive rows read eight distinct bank groups
-        uint32_t w[4][T::NW];
-        {
-          const uint8_t* src = smem + T::OFF_RAW + rs * T::RAW_STAGE + row * T::RAW_ROW;
+        const uint8_t* src = smem + T::OFF_RAW + rs * T::RAW_STAGE + row * T::RAW_ROW;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < 4; ++j, ++gc) {
+          const int c = 4 * r + j;  // chunk within the tile
+          // this chunk's block: a 16-byte window load (rows are 16-byte
+          // multiples apart, so eight consecutive rows read eight distinct
+          // bank groups)
+          uint32_t w[T::NW];
+          {
             const int o = (2 * j + b) * T::BB;
             const uint4* s4 = reinterpret_cast<const uint4*>(src + (o & ~15));
             uint32_t win[4 * T::NV];
@@ -458,20 +509,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int wo0 = (((2 * j) * T::BB) & 15) >> 2;      // compile-time after unrolling
             const int wo1 = (((2 * j + 1) * T::BB) & 15) >> 2;
 #pragma unroll
-            for (int i = 0; i < T::NW; ++i) w[j][i] = b ? win[wo1 + i] : win[wo0 + i];
+            for (int i = 0; i < T::NW; ++i) w[i] = b ? win[wo1 + i] : win[wo0 + i];
           }
-        }
-        // the stage is refilled by TMA (async proxy): order these generic
-        // reads before the release, or a late read can see the next stage
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&raw_empty[rs]);
-#pragma unroll
-        for (int j = 0; j < 4; ++j, ++gc) {
-          const int c = 4 * r + j;  // chunk within the tile
+          if (j == 3) {
+            // the stage is refilled by TMA (async proxy): order these generic
+            // reads before the release, or a late read can see the next stage
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&raw_empty[rs]);
+          }
           uint32_t hi[16], lo[16];
           uint16_t xw;
-          convert_block<WT, T::NW>(w[j], sh, hi, lo, xw);
+          convert_block<WT, T::NW>(w, sh, hi, lo, xw);
           const int ws = gc % SWT;
           if (gc >= SWT) spin_wait(&w_empty[ws], ((gc / SWT) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
           tc_fence_after();
@@ -494,46 +543,85 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) mbar_arrive(&w_full[ws]);
         }
       }
-    }
+    });
   } else {
     // ------------------------------------------------------------ epilogue
+    // two warps per TMEM lane quarter, one half of the tile's tokens each: a
+    // warp pulls its 64 tokens of D into registers and releases D to the next
+    // item's MMAs before any global traffic
+    const int ew = warp - kWarpEpi;             // 0..7
     const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;  // weight row within the tile
-    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    pdl_wait();  // rscale comes from the prep kernel
+    const int half = ew >> 2;
+    const int row = quarter * 32 + lane;        // weight row within the tile
+    const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + kColD + (uint32_t)(half * kEpiTok);
+    pdl_wait();  // rscale and the zeroed flags come from the prep kernel
     int it = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++it) {
-      spin_wait(d_full, it & 1, p.err, DEV_TIMEOUT_FULL, dead);
+    for_items(p, [&](const Item& w) {
+      sleep_wait(d_full, it & 1, p.err, DEV_TIMEOUT_FULL, dead);
       tc_fence_after();
-      const int m0 = (t % p.num_t_tiles) * TT, n0 = (t / p.num_t_tiles) * TW;
-      const int n = n0 + row;
-      const int tokens = min(TT, p.M - m0);
-      const int nd = SCATTER ? p.out.n_out : 1;
-      // 16 tokens at a time; D is released after the last group's loads
-#pragma unroll 1
-      for (int g = 0; g < TT / 16; ++g) {
-        uint32_t v[16], u[16];
-        tmem_ld16(tmem_base + lane_addr + kColD + 16 * g, v);
-        tmem_ld16(tmem_base + lane_addr + kColD + TT + 16 * g, u);
-        tmem_ld_wait();
-        if (g == TT / 16 - 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(d_empty);
-        }
-        if (n < p.N) {
+      // main straight into the output registers, then corr 16 columns at a time
+      uint32_t ov[kEpiTok / 16][16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int tk = 16 * g + i;
-            if (tk < tokens) {
-              const float o = fmaf(__uint_as_float(u[i]), 1.0f / 2048.0f, __uint_as_float(v[i])) * p.rscale[m0 + tk];
-              const size_t off = (size_t)(m0 + tk) * p.out.ld + p.out.col0 + n;
-              for (int dd = 0; dd < nd; ++dd) p.out.ptr[dd][off] = o;
+      for (int g = 0; g < kEpiTok / 16; ++g) tmem_ld16(taddr + 16 * g, ov[g]);
+      tmem_ld_wait();
+      float o[kEpiTok];
+#pragma unroll
+      for (int g = 0; g < kEpiTok / 16; ++g) {
+        uint32_t u[16];
+        tmem_ld16(taddr + TT + 16 * g, u);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[16 * g + i] = fmaf(__uint_as_float(u[i]), 1.0f / 2048.0f, __uint_as_float(ov[g][i]));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(d_empty);
+      ++it;
+
+      const int m0 = (w.t % p.num_t_tiles) * TT + half * kEpiTok, n0 = (w.t / p.num_t_tiles) * TW;
+      const int n = n0 + row;
+      const int tokens = min(kEpiTok, p.M - m0);
+      const int tbase = half * kEpiTok;           // token offset inside the tile
+      if (w.c0 > 0) {                             // helper: partial sums for the tile's owner
+        float* part = p.partial + (size_t)blockIdx.x * (TT * TW);
+#pragma unroll
+        for (int j = 0; j < kEpiTok; ++j) __stcg(part + (tbase + j) * TW + row, o[j]);
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(p.flags + blockIdx.x, 1);
+        return;
+      }
+      if (w.c1 < p.nmain) {                       // owner of a split tile: add the helpers' partials
+        const int tile_end = (w.t + 1) * p.upt;
+        for (int k = (int)blockIdx.x + 1; k < (int)gridDim.x && unit_begin(p, k) < tile_end; ++k) {
+          const uint64_t t0 = globaltimer_ns();
+          for (uint32_t i = 1;; ++i) {  // written early in the helper's run: normally already complete
+            uint32_t v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.flags + k) : "memory");
+            if (v >= (uint32_t)kEpiWarps || dead) break;
+            if ((i & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+              record_error(p.err, DEV_TIMEOUT_FULL);
+              dead = true;
+              break;
             }
+          }
+          const float* hp = p.partial + (size_t)k * (TT * TW);
+#pragma unroll
+          for (int j = 0; j < kEpiTok; ++j) o[j] += __ldcg(hp + (tbase + j) * TW + row);
+        }
+      }
+      if (n < p.N) {
+        const int nd = SCATTER ? p.out.n_out : 1;
+#pragma unroll
+        for (int j = 0; j < kEpiTok; ++j) {
+          if (j < tokens) {
+            const float r = o[j] * p.rscale[m0 + j];
+            const size_t off = (size_t)(m0 + j) * p.out.ld + p.out.col0 + n;
+            for (int dd = 0; dd < nd; ++dd) p.out.ptr[dd][off] = r;
           }
         }
       }
-    }
+    });
     if constexpr (SCATTER) __threadfence_system();  // peer stores visible before the host-side barrier
   }
 
@@ -553,8 +641,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 // of fp16 subnormals except for elements below 2^-17 of the row maximum.
 template <int WT>
 __global__ void __launch_bounds__(128) split_act_kernel(Act8 act, int M, int K, int Kp, __half* __restrict__ a_hi,
-                                                        __half* __restrict__ a_lo, float* __restrict__ rscale) {
+                                                        __half* __restrict__ a_lo, float* __restrict__ rscale,
+                                                        int* __restrict__ flags, int nflags) {
   pdl_launch_dependents();
+  if (blockIdx.x == 0)  // the GEMM's partial-tile flags start at zero every call
+    for (int i = threadIdx.x; i < nflags; i += blockDim.x) flags[i] = 0;
   const int nb = K / 32;
   const int m = blockIdx.x;
   if (m >= M) return;
@@ -633,14 +724,25 @@ kq_status_t launch_split(const void* w, Act8 act, const OutSpec& out, int M, int
   const int nmain = K / CK;
   const int ngrp = T::kExtra ? (nmain + GRP - 1) / GRP : 0;
   const int Kp = K + ngrp * CK;
-  const size_t hi_bytes = ((size_t)M * Kp * sizeof(__half) + 255) & ~(size_t)255;
-  const size_t lo_bytes = ((size_t)M * K * sizeof(__half) + 255) & ~(size_t)255;
-  uint8_t* ws = static_cast<uint8_t*>(workspace(WS_A16, hi_bytes + lo_bytes + (size_t)M * sizeof(float)));
+  const int num_t_tiles = (M + TT - 1) / TT;
+  const int num_tiles = num_t_tiles * ((N + TW - 1) / TW);
+  const int upt = (nmain + GRP - 1) / GRP;
+  const int num_units = num_tiles * upt;
+  const int grid = std::max(1, std::min(sm_count(), num_units));
+  auto up = [](size_t b) { return (b + 255) & ~(size_t)255; };
+  const size_t hi_bytes = up((size_t)M * Kp * sizeof(__half));
+  const size_t lo_bytes = up((size_t)M * K * sizeof(__half));
+  const size_t rs_bytes = up((size_t)M * sizeof(float));
+  const size_t fl_bytes = up((size_t)grid * sizeof(int));
+  const size_t pt_bytes = (size_t)grid * TT * TW * sizeof(float);
+  uint8_t* ws = static_cast<uint8_t*>(workspace(WS_A16, hi_bytes + lo_bytes + rs_bytes + fl_bytes + pt_bytes));
   if (!ws) return KQ_ERR_NOMEM;
   __half* a_hi = reinterpret_cast<__half*>(ws);
   __half* a_lo = reinterpret_cast<__half*>(ws + hi_bytes);
   float* rscale = reinterpret_cast<float*>(ws + hi_bytes + lo_bytes);
-  split_act_kernel<WT><<<M, 128, 0, s>>>(act, M, K, Kp, a_hi, a_lo, rscale);
+  int* flags = reinterpret_cast<int*>(ws + hi_bytes + lo_bytes + rs_bytes);
+  float* partial = reinterpret_cast<float*>(ws + hi_bytes + lo_bytes + rs_bytes + fl_bytes);
+  split_act_kernel<WT><<<M, 128, 0, s>>>(act, M, K, Kp, a_hi, a_lo, rscale, flags, grid);
   kq_status_t st = check_launch("split_act");
   if (st) return st;
   CUtensorMap m_hi, m_lo, m_raw;
@@ -666,12 +768,15 @@ kq_status_t launch_split(const void* w, Act8 act, const OutSpec& out, int M, int
   SxParams p;
   p.M = M; p.N = N; p.K = K;
   p.nmain = nmain; p.ngrp = ngrp;
-  p.num_t_tiles = (M + TT - 1) / TT;
-  p.num_tiles = p.num_t_tiles * ((N + TW - 1) / TW);
+  p.num_t_tiles = num_t_tiles;
+  p.num_tiles = num_tiles;
+  p.upt = upt;
+  p.num_units = num_units;
   p.out = out;
   p.rscale = rscale;
+  p.flags = flags;
+  p.partial = partial;
   p.err = err ? err : device_error_word();
-  const int grid = std::max(1, std::min(sm_count(), p.num_tiles));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
