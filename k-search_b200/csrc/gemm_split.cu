@@ -70,12 +70,12 @@ constexpr int TT = 128;                  // tokens per tile
 constexpr int CK = 64;                   // K elements per chunk: one 128-byte swizzle atom of fp16
 constexpr int RB = 8;                    // blocks per raw weight stage (= 4 chunks)
 constexpr int GRP = 32;                  // main chunks per extra chunk (64 blocks)
-constexpr int SA = 4;                    // activation stages (A_hi + A_lo)
-constexpr int SR = 2;                    // raw weight stages
+constexpr int UNIT = 4;                  // chunks per schedule unit (one raw weight stage)
 constexpr int SWT = 4;                   // weight stages in TMEM
 constexpr int A_PART = TT * 128;         // one 128-token x 128-byte tile
 constexpr int A_STAGE = 2 * A_PART;
 constexpr int kSmemLimit = 232448;
+
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColD = 0;            // main 0..127, corr 128..255
 constexpr uint32_t kColW = 2 * TT;       // weight stage s at kColW + 64 s: W_hi 32 | W_lo 32
@@ -98,6 +98,14 @@ struct SxTraits {
   // 16-byte loads per block window (from the 16-byte boundary at or below the
   // block start): the block's words start at word ((start & 15) >> 2) < 4
   static constexpr int NV = (3 + NW + 3) / 4;
+  // stages: activations (A_hi + A_lo per 64-wide chunk) and raw weight boxes;
+  // two raw stages keep a box in flight while the other is converted, and the
+  // activation ring takes a fifth stage where shared memory allows (q4_0 /
+  // q4_1; q8_0's raw boxes are larger)
+  static constexpr int kFix = 1024 + 16 + 8 * 32;
+  static constexpr bool kFit52 = 5 * A_STAGE + X_BYTES + 2 * RAW_STAGE + kFix <= kSmemLimit;
+  static constexpr int SA = kFit52 ? 5 : 4;
+  static constexpr int SR = 2;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_X = OFF_A + SA * A_STAGE;
   static constexpr int OFF_RAW = OFF_X + X_BYTES;
@@ -285,7 +293,7 @@ struct SxParams {
   int M, N, K;
   int nmain, ngrp;
   int num_t_tiles, num_tiles;
-  int upt, num_units;   // K units (groups of GRP chunks) per tile, units in all
+  int upt, num_units;   // K units (UNIT chunks each) per tile, units in all
   OutSpec out;
   const float* rscale;  // per activation row: 2^e undoing the prep kernel's scaling
   int* flags;           // per CTA: epilogue warps done writing its partial tile (zeroed by the prep kernel)
@@ -293,13 +301,15 @@ struct SxParams {
   int* err;
 };
 
-// Work schedule (stream-K over K groups): every tile's K range is cut into
-// units of GRP chunks (one extra-column group each); CTA b takes units
-// [U b / G, U (b + 1) / G) in order, so the SMs get equal work whatever the
-// tile count. A work item is the part of one tile inside a CTA's range. The
-// CTA holding a tile's first unit owns the tile; the others (whose ranges
-// start inside it: each CTA at most once, on its first item) write partial
-// sums that the owner adds, in CTA order, after its own part.
+// Work schedule (stream-K): every tile's K range is cut into units of UNIT
+// chunks; CTA b takes units [U b / G, U (b + 1) / G) in order, so the SMs
+// get equal work whatever the tile count. A work item is the part of one
+// tile inside a CTA's range. The CTA holding a tile's first unit owns the
+// tile; the others (whose ranges start inside it: each CTA at most once, on
+// its first item) write partial sums that the owner adds, in CTA order,
+// after its own part. The extra columns follow the same split: a CTA applies
+// them for the blocks it converted, at the end of each group segment of an
+// item (its X tile holds zero for the group's other blocks).
 __device__ __forceinline__ int unit_begin(const SxParams& p, int b) {
   return (int)(((long long)p.num_units * b) / (long long)gridDim.x);
 }
@@ -313,19 +323,21 @@ __device__ __forceinline__ void for_items(const SxParams& p, F&& f) {
   for (int u = unit_begin(p, blockIdx.x); u < ue;) {
     const int t = u / p.upt;
     const int uend = min(ue, (t + 1) * p.upt);
-    f(Item{t, (u - t * p.upt) * GRP, min((uend - t * p.upt) * GRP, p.nmain)});
+    f(Item{t, (u - t * p.upt) * UNIT, min((uend - t * p.upt) * UNIT, p.nmain)});
     u = uend;
   }
 }
 
-// main chunk c is followed by an extra chunk (last of its group of GRP, or the last chunk)
-__device__ __forceinline__ bool extra_after(int c, int nmain) { return (c % GRP) == GRP - 1 || c == nmain - 1; }
+// main chunk c of an item ending at chunk c1 is followed by an extra chunk:
+// the last chunk of its group of GRP, or of the item
+__device__ __forceinline__ bool x_after(int c, int c1) { return (c % GRP) == GRP - 1 || c == c1 - 1; }
 
 template <int WT, bool SCATTER>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_split_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo,
                       const __grid_constant__ CUtensorMap map_raw, const __grid_constant__ SxParams p) {
   using T = SxTraits<WT>;
+  constexpr int SA = T::SA, SR = T::SR;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + T::OFF_BAR);
@@ -385,7 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for_items(p, [&](const Item& w) {
       const int m0 = (w.t % p.num_t_tiles) * TT;
       for (int c = w.c0; c < w.c1; ++c) {
-        const int nx = (T::kExtra && extra_after(c, p.nmain)) ? 2 : 1;
+        const int nx = (T::kExtra && x_after(c, w.c1)) ? 2 : 1;
         for (int e = 0; e < nx; ++e, ++ia) {
           const int as = ia % SA;
           if (ia >= SA) spin_wait(&a_empty[as], ((ia / SA) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
@@ -449,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_commit(&w_empty[ws]);
         }
         __syncwarp();
-        if (T::kExtra && extra_after(c, p.nmain)) {
+        if (T::kExtra && x_after(c, w.c1)) {
           // the group's X_w columns are complete: every converter arrived on
           // w_full for the group's chunks after writing them
           ++ia;
@@ -528,9 +540,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st16(wcol, hi);
           tmem_st16(wcol + 32, lo);
           if constexpr (T::kExtra) {
-            if (c % GRP == 0) {  // first write of a group: the MMA must be done with the X tile
+            if (c % GRP == 0 || c == wi.c0) {
+              // first chunk of a group segment: once the MMA is done with the X
+              // tile, clear this thread's columns (those of parity b: the
+              // blocks 2c + b it converts), so blocks of the group that other
+              // CTAs convert count zero here
               if (gx >= 1) spin_wait(x_empty, (gx - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
               ++gx;
+#pragma unroll 4
+              for (int z = b; z < 64; z += 2)
+                *reinterpret_cast<uint16_t*>(smem + T::OFF_X + (offx + (((z >> 3) ^ (row & 7)) << 4)) + (z & 7) * 2) = 0;
             }
             const int col = (2 * c + b) & 63;
             *reinterpret_cast<uint16_t*>(smem + T::OFF_X + (offx + ((((col >> 3) ^ (row & 7))) << 4)) + (col & 7) * 2) =
@@ -726,7 +745,7 @@ kq_status_t launch_split(const void* w, Act8 act, const OutSpec& out, int M, int
   const int Kp = K + ngrp * CK;
   const int num_t_tiles = (M + TT - 1) / TT;
   const int num_tiles = num_t_tiles * ((N + TW - 1) / TW);
-  const int upt = (nmain + GRP - 1) / GRP;
+  const int upt = nmain / UNIT;
   const int num_units = num_tiles * upt;
   const int grid = std::max(1, std::min(sm_count(), num_units));
   auto up = [](size_t b) { return (b + 255) & ~(size_t)255; };
