@@ -630,13 +630,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (n < p.N) {
+#pragma unroll
+        for (int j = 0; j < kEpiTok; ++j) o[j] *= p.rscale[m0 + min(j, tokens - 1)];
+        const size_t ld = (size_t)p.out.ld;
         const int nd = SCATTER ? p.out.n_out : 1;
 #pragma unroll
-        for (int j = 0; j < kEpiTok; ++j) {
-          if (j < tokens) {
-            const float r = o[j] * p.rscale[m0 + j];
-            const size_t off = (size_t)(m0 + j) * p.out.ld + p.out.col0 + n;
-            for (int dd = 0; dd < nd; ++dd) p.out.ptr[dd][off] = r;
+        for (int dd = 0; dd < (SCATTER ? kMaxOut : 1); ++dd) {  // destinations outermost, static indices
+          if (dd < nd) {
+            float* dst = p.out.ptr[dd] + (size_t)m0 * ld + p.out.col0 + n;
+#pragma unroll
+            for (int j = 0; j < kEpiTok; ++j)
+              if (j < tokens) dst[j * ld] = o[j];
           }
         }
       }

@@ -157,10 +157,14 @@ class NShardedGemm:
     quantises x on the fly, computes the local [M, n_r] columns and
     all-gathers them; shards of unequal width are padded to the widest for the
     collective and trimmed. ``gemm_fn(weight, x, M, n, K, wtype, act_mode)``
-    is the per-rank compute (libkq by default)."""
+    is the per-rank compute (libkq by default). ``mode="p2p"`` instead stores
+    the columns straight into every rank's output over peer mappings (see
+    _forward_p2p); ``push_min_rows`` (p2p only) switches calls with more rows
+    than that to local stores plus one strided copy per peer."""
 
     def __init__(self, weight_shard: torch.Tensor, N: int, K: int, wtype: str = "q4_0", act_mode: str = "sum_dq",
-                 group=None, align: int = 128, gemm_fn: Callable | None = None, mode: str = "nccl"):
+                 group=None, align: int = 128, gemm_fn: Callable | None = None, mode: str = "nccl",
+                 push_min_rows: int | None = None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -173,6 +177,7 @@ class NShardedGemm:
         if mode not in ("nccl", "p2p"):
             raise ValueError("mode is 'nccl' or 'p2p'")
         self.mode = mode
+        self.push_min_rows = push_min_rows
         self._bufs: list[PeerBuffer] = []   # p2p: two full-width outputs, used alternately
         self._buf_rows = 0
         self._calls = 0
@@ -196,13 +201,15 @@ class NShardedGemm:
     def _forward_p2p(self, x: torch.Tensor) -> torch.Tensor | None:
         """The output lands in every rank's full-width buffer (CUDA IPC
         mappings of two alternating buffers) without a collective on the data:
-        for GEMV shapes (M <= 8) the epilogue itself stores this rank's columns
-        into every rank's buffer (kq_gemm_f32act_scatter); for larger M the
-        epilogue writes them in place into the local buffer and one strided
-        copy per peer (copy engines over NVLink, one stream each) pushes the
-        block. A one-element all-reduce then orders all of it before anything
-        later on any rank's stream. The returned tensor stays valid until the
-        call after next. None if the shape has no scatter epilogue."""
+        the GEMM's epilogue stores this rank's columns into every rank's
+        buffer (kq_gemm_f32act_scatter: P2P stores over NVLink, overlapped
+        with the MMAs of the next tiles). With push_min_rows set and more rows
+        than that, the epilogue writes the local buffer only and one strided
+        copy per peer (copy engines, one stream each) pushes the block
+        afterwards. A one-element all-reduce then orders all of it before
+        anything later on any rank's stream. The returned tensor stays valid
+        until the call after next. None if the shape has no scatter
+        epilogue."""
         from . import ops
         from ._lib import KQError, check, lib
         M = x.shape[0]
@@ -212,7 +219,7 @@ class NShardedGemm:
             self._bufs = [PeerBuffer(self._buf_rows * self.N, x.device, self.group) for _ in range(2)]
         buf = self._bufs[self._calls & 1]
         s, c = self.splits[self.rank]
-        push = M > 8 and self.world > 1
+        push = self.push_min_rows is not None and M > self.push_min_rows and self.world > 1
         dests = [buf.ptrs[self.rank]] if push else buf.ptrs
         try:
             ops.gemm_f32act_scatter(self.weight, x, dests, self.N, s, M, c, self.K, self.wtype, self.act_mode,
