@@ -71,7 +71,7 @@ constexpr int CK = 64;                   // K elements per chunk: one 128-byte s
 constexpr int RB = 8;                    // blocks per raw weight stage (= 4 chunks)
 constexpr int GRP = 32;                  // main chunks per extra chunk (64 blocks)
 constexpr int UNIT = 4;                  // chunks per schedule unit (one raw weight stage)
-constexpr int SWT = 4;                   // weight stages in TMEM
+constexpr int SS = 4;                    // chunk stages: activations (shared memory) + weights (TMEM), paired
 constexpr int A_PART = TT * 128;         // one 128-token x 128-byte tile
 constexpr int A_STAGE = 2 * A_PART;
 constexpr int kSmemLimit = 232448;
@@ -91,32 +91,28 @@ struct SxTraits {
   static constexpr bool kExtra = WT != KQ_Q8_0;
   static constexpr int RAW_ROW = RB * BB;  // 144 / 160 / 272 bytes
   static constexpr int RAW_STAGE = TW * RAW_ROW;
-  static constexpr int X_BYTES = kExtra ? TW * 128 : 0;
+  static constexpr int X_BYTES = kExtra ? TW * 128 : 0;   // X_w tile (converters)
+  static constexpr int XA_BYTES = kExtra ? A_PART : 0;    // X_a tile of the activations (TMA)
   // 32-bit words a converter reads for one block: from the 4-byte boundary at
   // or below the block start (blocks are 2-byte aligned) to its end
   static constexpr int NW = WT == KQ_Q4_1 ? 5 : (BB + 2 + 3) / 4;
   // 16-byte loads per block window (from the 16-byte boundary at or below the
   // block start): the block's words start at word ((start & 15) >> 2) < 4
   static constexpr int NV = (3 + NW + 3) / 4;
-  // stages: activations (A_hi + A_lo per 64-wide chunk) and raw weight boxes;
-  // two raw stages keep a box in flight while the other is converted, and the
-  // activation ring takes a fifth stage where shared memory allows (q4_0 /
-  // q4_1; q8_0's raw boxes are larger)
-  static constexpr int kFix = 1024 + 16 + 8 * 32;
-  static constexpr bool kFit52 = 5 * A_STAGE + X_BYTES + 2 * RAW_STAGE + kFix <= kSmemLimit;
-  static constexpr int SA = kFit52 ? 5 : 4;
+  // two raw stages keep a weight box in flight while the other is converted
   static constexpr int SR = 2;
   static constexpr int OFF_A = 0;
-  static constexpr int OFF_X = OFF_A + SA * A_STAGE;
-  static constexpr int OFF_RAW = OFF_X + X_BYTES;
+  static constexpr int OFF_X = OFF_A + SS * A_STAGE;
+  static constexpr int OFF_XA = OFF_X + X_BYTES;
+  static constexpr int OFF_RAW = OFF_XA + XA_BYTES;
   static constexpr int OFF_BAR = OFF_RAW + SR * RAW_STAGE;
-  static constexpr int NBARS = 2 * SA + 2 * SR + 2 * SWT + 2 + 1;
+  static constexpr int NBARS = 2 * SS + 2 * SR + 2 + 2;
   static constexpr int OFF_TMEM = OFF_BAR + NBARS * 8;
   static constexpr int SMEM = OFF_TMEM + 16 + 1024;
   static_assert(RAW_ROW % 16 == 0 && RAW_STAGE % 16 == 0, "raw stages stay 16-byte aligned");
   static_assert(OFF_RAW % 1024 == 0, "swizzled tiles stay 1024-byte aligned");
   static_assert(SMEM <= kSmemLimit, "shared memory budget");
-  static_assert(kColW + 64 * SWT <= kTmemCols, "TMEM budget");
+  static_assert(kColW + 64 * SS <= kTmemCols, "TMEM budget");
 };
 
 // D (+)= A x B^T, A from shared memory (descriptor)
@@ -337,39 +333,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_split_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo,
                       const __grid_constant__ CUtensorMap map_raw, const __grid_constant__ SxParams p) {
   using T = SxTraits<WT>;
-  constexpr int SA = T::SA, SR = T::SR;
+  constexpr int SR = T::SR;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + T::OFF_BAR);
-  uint64_t* a_full = bars;
-  uint64_t* a_empty = a_full + SA;
-  uint64_t* raw_full = a_empty + SA;
+  // chunk stage s: full[s] completes when the activation tiles have landed
+  // (TMA bytes) and every converter warp has written the weight stage;
+  // empty[s] when the MMAs that read both are done (one commit)
+  uint64_t* full = bars;
+  uint64_t* empty = full + SS;
+  uint64_t* raw_full = empty + SS;
   uint64_t* raw_empty = raw_full + SR;
-  uint64_t* w_full = raw_empty + SR;
-  uint64_t* w_empty = w_full + SWT;
-  uint64_t* d_full = w_empty + SWT;
+  uint64_t* d_full = raw_empty + SR;
   uint64_t* d_empty = d_full + 1;
-  uint64_t* x_empty = d_empty + 1;
+  uint64_t* x_empty = d_empty + 1;   // the X MMA of a group segment is done (X_w and X_a tiles free)
+  uint64_t* xa_full = x_empty + 1;   // the X_a tile has landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + T::OFF_TMEM);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < SA; ++i) {
-      mbar_init(&a_full[i], 1);
-      mbar_init(&a_empty[i], 1);
+    for (int i = 0; i < SS; ++i) {
+      mbar_init(&full[i], kConvWarps + 1);
+      mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < SR; ++i) {
       mbar_init(&raw_full[i], 1);
       mbar_init(&raw_empty[i], kConvWarps);
     }
-    for (int i = 0; i < SWT; ++i) {
-      mbar_init(&w_full[i], kConvWarps);
-      mbar_init(&w_empty[i], 1);
-    }
     mbar_init(d_full, 1);
     mbar_init(d_empty, kEpiWarps);
     mbar_init(x_empty, 1);
+    mbar_init(xa_full, 1);
     fence_mbar_init();
   }
   if constexpr (T::kExtra) {
@@ -393,26 +388,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       pdl_wait();  // A_hi / A_lo come from the preceding prep kernel
     }
     __syncwarp();
-    int ia = 0;
+    int k = 0, gxa = 0;
     for_items(p, [&](const Item& w) {
       const int m0 = (w.t % p.num_t_tiles) * TT;
-      for (int c = w.c0; c < w.c1; ++c) {
-        const int nx = (T::kExtra && x_after(c, w.c1)) ? 2 : 1;
-        for (int e = 0; e < nx; ++e, ++ia) {
-          const int as = ia % SA;
-          if (ia >= SA) spin_wait(&a_empty[as], ((ia / SA) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+      for (int c = w.c0; c < w.c1; ++c, ++k) {
+        const int st = k % SS;
+        if (k >= SS) spin_wait(&empty[st], ((k / SS) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+        if (lane == 0) {
+          uint8_t* dst = smem + T::OFF_A + st * A_STAGE;
+          mbar_arrive_expect_tx(&full[st], A_STAGE);
+          tma_load_2d(dst, &map_hi, c * CK, m0, &full[st]);
+          tma_load_2d(dst + A_PART, &map_lo, c * CK, m0, &full[st]);
+        }
+        __syncwarp();
+        if (T::kExtra && x_after(c, w.c1)) {  // the group's X_a columns, once the previous X MMA is done
+          if (gxa >= 1) spin_wait(x_empty, (gxa - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
           if (lane == 0) {
-            uint8_t* dst = smem + T::OFF_A + as * A_STAGE;
-            if (e == 0) {
-              mbar_arrive_expect_tx(&a_full[as], A_STAGE);
-              tma_load_2d(dst, &map_hi, c * CK, m0, &a_full[as]);
-              tma_load_2d(dst + A_PART, &map_lo, c * CK, m0, &a_full[as]);
-            } else {
-              mbar_arrive_expect_tx(&a_full[as], A_PART);
-              tma_load_2d(dst, &map_hi, p.K + (c / GRP) * CK, m0, &a_full[as]);
-            }
+            mbar_arrive_expect_tx(xa_full, A_PART);
+            tma_load_2d(smem + T::OFF_XA, &map_hi, p.K + (c / GRP) * CK, m0, xa_full);
           }
           __syncwarp();
+          ++gxa;
         }
       }
     });
@@ -439,45 +435,42 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr uint32_t idesc1 = idesc_f16<TT>();
     const uint32_t a_base = smem_u32(smem + T::OFF_A);
     const uint32_t x_base = smem_u32(smem + T::OFF_X);
+    const uint32_t xa_base = smem_u32(smem + T::OFF_XA);
     const uint32_t d_main = tmem_base + kColD, d_corr = tmem_base + kColD + TT;
-    int ia = 0, iw = 0, it = 0;
+    int k = 0, gx = 0, it = 0;
     for_items(p, [&](const Item& w) {
       if (it >= 1) spin_wait(d_empty, (it - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
       tc_fence_after();
-      for (int c = w.c0; c < w.c1; ++c, ++ia, ++iw) {
-        const int as = ia % SA, ws = iw % SWT;
-        spin_wait(&a_full[as], (ia / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-        spin_wait(&w_full[ws], (iw / SWT) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+      for (int c = w.c0; c < w.c1; ++c, ++k) {
+        const int st = k % SS;
+        spin_wait(&full[st], (k / SS) & 1, p.err, DEV_TIMEOUT_FULL, dead);
         tc_fence_after();
         if (lane == 0) {
-          const uint64_t bdesc = sw128_desc(a_base + as * A_STAGE);  // A_hi rows, then A_lo rows
-          const uint32_t whi = tmem_base + kColW + 64 * ws, wlo = whi + 32;
+          const uint64_t bdesc = sw128_desc(a_base + st * A_STAGE);  // A_hi rows, then A_lo rows
+          const uint32_t whi = tmem_base + kColW + 64 * st, wlo = whi + 32;
 #pragma unroll
           for (int j = 0; j < CK / 16; ++j) {
             mma_ts(d_main, whi + 8 * j, bdesc + (uint64_t)(2 * j), idesc2, (c > w.c0 || j > 0) ? 1u : 0u);
             mma_ts(d_corr, wlo + 8 * j, bdesc + (uint64_t)(2 * j), idesc1, 1u);
           }
-          mma_commit(&a_empty[as]);
-          mma_commit(&w_empty[ws]);
+          mma_commit(&empty[st]);
         }
         __syncwarp();
         if (T::kExtra && x_after(c, w.c1)) {
-          // the group's X_w columns are complete: every converter arrived on
-          // w_full for the group's chunks after writing them
-          ++ia;
-          const int as2 = ia % SA;
-          spin_wait(&a_full[as2], (ia / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+          // the segment's X_w columns are complete: every converter arrived on
+          // full[] for the segment's chunks after writing them
+          spin_wait(xa_full, gx & 1, p.err, DEV_TIMEOUT_FULL, dead);
           tc_fence_after();
           if (lane == 0) {
             const uint64_t xd = sw128_desc(x_base);
-            const uint64_t bx = sw128_desc(a_base + as2 * A_STAGE);
+            const uint64_t bx = sw128_desc(xa_base);
 #pragma unroll
             for (int j = 0; j < CK / 16; ++j)
               mma_ss(d_main, xd + (uint64_t)(2 * j), bx + (uint64_t)(2 * j), idesc1, 1u);
-            mma_commit(&a_empty[as2]);
             mma_commit(x_empty);
           }
           __syncwarp();
+          ++gx;
         }
       }
       if (lane == 0) mma_commit(d_full);
@@ -533,8 +526,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t hi[16], lo[16];
           uint16_t xw;
           convert_block<WT, T::NW>(w, sh, hi, lo, xw);
-          const int ws = gc % SWT;
-          if (gc >= SWT) spin_wait(&w_empty[ws], ((gc / SWT) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+          const int ws = gc % SS;
+          if (gc >= SS) spin_wait(&empty[ws], ((gc / SS) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
           tc_fence_after();
           const uint32_t wcol = tmem_base + lane_addr + kColW + 64 * ws + 16 * b;
           tmem_st16(wcol, hi);
@@ -559,7 +552,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st_wait();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&w_full[ws]);
+          if (lane == 0) mbar_arrive(&full[ws]);
         }
       }
     });
