@@ -594,18 +594,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n = n0 + row;
       const int tokens = min(kEpiTok, p.M - m0);
       const int tbase = half * kEpiTok;           // token offset inside the tile
-      if (w.c0 > 0) {                             // helper: partial sums for the tile's owner
-        float* part = p.partial + (size_t)blockIdx.x * (TT * TW);
-#pragma unroll
-        for (int j = 0; j < kEpiTok; ++j) __stcg(part + (tbase + j) * TW + row, o[j]);
+      // per-token row scales (powers of two): two per lane, broadcast by shuffle
+      const int last = max(tokens - 1, 0);
+      const float rs_a = tokens > 0 ? p.rscale[m0 + min(lane, last)] : 1.0f;
+      const float rs_b = tokens > 0 ? p.rscale[m0 + min(32 + lane, last)] : 1.0f;
+      const int tile_u0 = w.t * p.upt, tile_end = (w.t + 1) * p.upt;
+      // A split tile with exactly two contributors skips the partial buffer:
+      // the helper, which finishes its part early in its run, stores its
+      // scaled sums into the output; the owner adds its own with
+      // red.global.add after the helper's flag. The scale is a power of two,
+      // so this equals scaling the two-term sum once.
+      const bool pair_helper = !SCATTER && w.c0 > 0 && w.c1 == p.nmain && blockIdx.x >= 1 &&
+                               unit_begin(p, (int)blockIdx.x - 1) <= tile_u0;
+      auto signal = [&]() {  // this warp's rows are written
         __threadfence();
         __syncwarp();
         if (lane == 0) atomicAdd(p.flags + blockIdx.x, 1);
+      };
+      if (w.c0 > 0 && !pair_helper) {             // helper: partial sums for the tile's owner
+        float* part = p.partial + (size_t)blockIdx.x * (TT * TW);
+#pragma unroll
+        for (int j = 0; j < kEpiTok; ++j) __stcg(part + (tbase + j) * TW + row, o[j]);
+        signal();
         return;
       }
-      if (w.c1 < p.nmain) {                       // owner of a split tile: add the helpers' partials
-        const int tile_end = (w.t + 1) * p.upt;
-        for (int k = (int)blockIdx.x + 1; k < (int)gridDim.x && unit_begin(p, k) < tile_end; ++k) {
+      bool pair_owner = false;
+      if (w.c0 == 0 && w.c1 < p.nmain) {          // owner of a split tile
+        int h_end = (int)blockIdx.x + 1;          // helpers: CTAs blockIdx.x + 1 .. h_end - 1
+        while (h_end < (int)gridDim.x && unit_begin(p, h_end) < tile_end) ++h_end;
+        pair_owner = !SCATTER && h_end == (int)blockIdx.x + 2;
+        for (int k = (int)blockIdx.x + 1; k < h_end; ++k) {
           const uint64_t t0 = globaltimer_ns();
           for (uint32_t i = 1;; ++i) {  // written early in the helper's run: normally already complete
             uint32_t v;
@@ -617,26 +635,36 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
           }
-          const float* hp = p.partial + (size_t)k * (TT * TW);
+          if (!pair_owner) {
+            const float* hp = p.partial + (size_t)k * (TT * TW);
 #pragma unroll
-          for (int j = 0; j < kEpiTok; ++j) o[j] += __ldcg(hp + (tbase + j) * TW + row);
-        }
-      }
-      if (n < p.N) {
-#pragma unroll
-        for (int j = 0; j < kEpiTok; ++j) o[j] *= p.rscale[m0 + min(j, tokens - 1)];
-        const size_t ld = (size_t)p.out.ld;
-        const int nd = SCATTER ? p.out.n_out : 1;
-#pragma unroll
-        for (int dd = 0; dd < (SCATTER ? kMaxOut : 1); ++dd) {  // destinations outermost, static indices
-          if (dd < nd) {
-            float* dst = p.out.ptr[dd] + (size_t)m0 * ld + p.out.col0 + n;
-#pragma unroll
-            for (int j = 0; j < kEpiTok; ++j)
-              if (j < tokens) dst[j * ld] = o[j];
+            for (int j = 0; j < kEpiTok; ++j) o[j] += __ldcg(hp + (tbase + j) * TW + row);
           }
         }
       }
+#pragma unroll
+      for (int j = 0; j < kEpiTok; ++j) o[j] *= __shfl_sync(0xffffffffu, j < 32 ? rs_a : rs_b, j & 31);
+      if (n < p.N) {
+        const size_t ld = (size_t)p.out.ld;
+        if (pair_owner) {
+          float* dst = p.out.ptr[0] + (size_t)m0 * ld + p.out.col0 + n;
+#pragma unroll
+          for (int j = 0; j < kEpiTok; ++j)
+            if (j < tokens) atomicAdd(dst + j * ld, o[j]);
+        } else {
+          const int nd = SCATTER ? p.out.n_out : 1;
+#pragma unroll
+          for (int dd = 0; dd < (SCATTER ? kMaxOut : 1); ++dd) {  // destinations outermost, static indices
+            if (dd < nd) {
+              float* dst = p.out.ptr[dd] + (size_t)m0 * ld + p.out.col0 + n;
+#pragma unroll
+              for (int j = 0; j < kEpiTok; ++j)
+                if (j < tokens) dst[j * ld] = o[j];
+            }
+          }
+        }
+      }
+      if (pair_helper) signal();
     });
     if constexpr (SCATTER) __threadfence_system();  // peer stores visible before the host-side barrier
   }
