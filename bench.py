@@ -406,6 +406,21 @@ def bench_gemm(args, cfg, rank, world):
             sharded_t(xs[j])
 
         ms, clk = eager_time_ms(step, args.steps, args.warmup, world, clocks)
+    exchange = None
+    if world > 1:
+        # the same rank-local GEMM without the exchange (every rank's own
+        # columns only), to report compute and exchange time separately
+        def lstep(i):
+            j = i % nsets
+            sp = torch.cuda.current_stream().cuda_stream
+            _lib.check(L.kq_gemm_f32act(wtc, ws[j].data_ptr(), xs[j].data_ptr(), outs[j].data_ptr(), M, N, K,
+                                        act_mode, sp), "kq_gemm_f32act")
+
+        lms, _ = graph_time_ms(lstep, args.steps, args.warmup, world)
+        exchange = {"local_ms_per_step": round(lms / args.steps, 5),
+                    "exchange_ms_per_step": round((ms - lms) / args.steps, 5),
+                    "note": "step = rank-local GEMM + epilogue peer stores of its columns to every rank + "
+                            "1-element all-reduce; the received bytes per rank grow as (world-1) x M x N x 4"}
     ops = 2.0 * M * N * K
     value = world * ops * args.steps / (ms * 1e-3) / 1e12
 
@@ -490,7 +505,7 @@ def bench_gemm(args, cfg, rank, world):
                 "kernel": "gemm_split_kernel (+ split_act_kernel prep)",
                 "peak_source": f"f16 dense = {src} bf16_tflops (cuBLAS bf16 burst); achieved counts the "
                                f"algorithmic 2MNK, executed_frac the 3 f16 MMAs per product"}
-    launches_per_step = 2
+    launches_per_step = 2 if M <= 8 else 3  # quantiser + GEMV | quantiser + split prep + split GEMM
     line = {
         "metric": "W8A8 GEMM TOPS (q8_0 x q8_1)" if wt == "q8_0" else "W4A8 GEMM TOPS (q4_0 x q8_1)",
         "value": round(value, 3), "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -508,6 +523,8 @@ def bench_gemm(args, cfg, rank, world):
         "gpu_launches": launches_per_step * args.steps,
         "kernel_ms": round(kms, 5),
     }
+    if exchange is not None:
+        line["exchange"] = exchange
     if clk is not None:
         line["clocks"] = clk
     return line

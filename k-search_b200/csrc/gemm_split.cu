@@ -688,6 +688,7 @@ __global__ void __launch_bounds__(128) split_act_kernel(Act8 act, int M, int K, 
                                                         __half* __restrict__ a_lo, float* __restrict__ rscale,
                                                         int* __restrict__ flags, int nflags) {
   pdl_launch_dependents();
+  pdl_wait();  // the staged activations come from the preceding quantiser
   if (blockIdx.x == 0)  // the GEMM's partial-tile flags start at zero every call
     for (int i = threadIdx.x; i < nflags; i += blockDim.x) flags[i] = 0;
   const int nb = K / 32;
@@ -786,7 +787,21 @@ kq_status_t launch_split(const void* w, Act8 act, const OutSpec& out, int M, int
   float* rscale = reinterpret_cast<float*>(ws + hi_bytes + lo_bytes);
   int* flags = reinterpret_cast<int*>(ws + hi_bytes + lo_bytes + rs_bytes);
   float* partial = reinterpret_cast<float*>(ws + hi_bytes + lo_bytes + rs_bytes + fl_bytes);
-  split_act_kernel<WT><<<M, 128, 0, s>>>(act, M, K, Kp, a_hi, a_lo, rscale, flags, grid);
+  {
+    // a programmatic dependent of the quantiser that usually precedes it: its
+    // launch overlaps the quantiser's tail, its reads wait for its results
+    cudaLaunchConfig_t pc = {};
+    pc.gridDim = dim3(M);
+    pc.blockDim = dim3(128);
+    pc.stream = s;
+    cudaLaunchAttribute pa[1];
+    pa[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pa[0].val.programmaticStreamSerializationAllowed = 1;
+    pc.attrs = pa;
+    pc.numAttrs = 1;
+    cudaError_t pe = cudaLaunchKernelEx(&pc, split_act_kernel<WT>, act, M, K, Kp, a_hi, a_lo, rscale, flags, grid);
+    if (pe != cudaSuccess) return check_cuda(pe, "split_act launch");
+  }
   kq_status_t st = check_launch("split_act");
   if (st) return st;
   CUtensorMap m_hi, m_lo, m_raw;
