@@ -453,26 +453,51 @@ def bench_gemm(args, cfg, rank, world):
                if world > 1 else None)
     xh = [torch.randn((M, K), generator=g, dtype=torch.float32).pin_memory() for _ in range(2)]
     oh = [torch.empty((M, NT), dtype=torch.float32).pin_memory() for _ in range(2)]
-    xd = torch.empty((M, K), dtype=torch.float32, device=dev)
-    od = torch.empty((M, NT), dtype=torch.float32, device=dev)
+    # two device input/output buffers: step i's host->device copy (copy
+    # stream), GEMM (compute stream) and device->host read-back (second copy
+    # stream) are ordered by events, so copies of neighbouring steps overlap
+    # this step's GEMM; every step still moves its own input and result
+    xd = [torch.empty((M, K), dtype=torch.float32, device=dev) for _ in range(2)]
+    od = [torch.empty((M, NT), dtype=torch.float32, device=dev) for _ in range(2)]
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_c = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    ev_start = torch.cuda.Event()
 
     def estep(i):
-        j = i % nsets
-        xd.copy_(xh[i % 2], non_blocking=True)
+        j, b = i % nsets, i % 2
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(ev_start)
+            s_in.wait_event(ev_c[b])            # step i-2's GEMM is done with this input buffer
+            xd[b].copy_(xh[b], non_blocking=True)
+            ev_in[b].record(s_in)
+        stream.wait_event(ev_in[b])
+        stream.wait_event(ev_out[b])            # step i-2's read-back is done with this output buffer
         if sharded is None:
-            kq.gemm_f32act(ws[j], xd, M, N, K, wt, cfg["act"], out=od)
+            kq.gemm_f32act(ws[j], xd[b], M, N, K, wt, cfg["act"], out=od[b])
         else:
             sharded.weight = ws[j]
-            sharded(xd, out=od)
-        oh[i % 2].copy_(od, non_blocking=True)
+            sharded(xd[b], out=od[b])
+        ev_c[b].record(stream)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_c[b])
+            oh[b].copy_(od[b], non_blocking=True)
+            ev_out[b].record(s_out)
 
+    ev_start.record(stream)
     for i in range(3):
         estep(i)
+    stream.wait_event(ev_out[0])
+    stream.wait_event(ev_out[1])
     torch.cuda.synchronize()
     barrier(world)
     e0.record(stream)
+    ev_start.record(stream)
     for i in range(args.steps):
         estep(i)
+    stream.wait_event(ev_out[0])
+    stream.wait_event(ev_out[1])
     e1.record(stream)
     torch.cuda.synchronize()
     ems = max_over_ranks(e0.elapsed_time(e1), world)
@@ -677,23 +702,51 @@ def bench_moe(args, cfg, rank, world):
     xh = [torch.randn((T, H), generator=g).pin_memory() for _ in range(2)]
     lh = [torch.randn((T, E), generator=g).pin_memory() for _ in range(2)]
     oh = [torch.empty((T, H), dtype=torch.float32).pin_memory() for _ in range(2)]
+    # double-buffered device inputs/outputs, copies on their own streams
+    # (ordered by events), so neighbouring steps' copies overlap this step
+    xd = [torch.empty_like(x) for _ in range(2)]
+    ld = [torch.empty_like(logits) for _ in range(2)]
+    od = [torch.empty_like(out) for _ in range(2)]
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_c = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    ev_start = torch.cuda.Event()
 
     def estep(i):
-        x.copy_(xh[i % 2], non_blocking=True)
-        logits.copy_(lh[i % 2], non_blocking=True)
+        b = i % 2
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(ev_start)
+            s_in.wait_event(ev_c[b])
+            xd[b].copy_(xh[b], non_blocking=True)
+            ld[b].copy_(lh[b], non_blocking=True)
+            ev_in[b].record(s_in)
+        stream.wait_event(ev_in[b])
+        stream.wait_event(ev_out[b])
         if world == 1:
-            y = kq.moe_q4_0(x, logits, wg, wu, wd, topk, cfg["act"], out=out)
+            y = kq.moe_q4_0(xd[b], ld[b], wg, wu, wd, topk, cfg["act"], out=od[b])
         else:
-            y = kd.moe_expert_parallel(x, logits, wg, wu, wd, E, topk, cfg["act"])
-        oh[i % 2].copy_(y, non_blocking=True)
+            y = kd.moe_expert_parallel(xd[b], ld[b], wg, wu, wd, E, topk, cfg["act"])
+            od[b].copy_(y)
+        ev_c[b].record(stream)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_c[b])
+            oh[b].copy_(od[b], non_blocking=True)
+            ev_out[b].record(s_out)
 
+    ev_start.record(stream)
     for i in range(2):
         estep(i)
+    stream.wait_event(ev_out[0])
+    stream.wait_event(ev_out[1])
     torch.cuda.synchronize()
     barrier(world)
     e0.record(stream)
+    ev_start.record(stream)
     for i in range(args.steps):
         estep(i)
+    stream.wait_event(ev_out[0])
+    stream.wait_event(ev_out[1])
     e1.record(stream)
     torch.cuda.synchronize()
     ems = max_over_ranks(e0.elapsed_time(e1), world)
