@@ -1,0 +1,55 @@
+"""Record the shapes of the reference's quant_gemm definitions as a fixture.
+
+Runs ONLY where the qhy991/K-Search checkout is present (pass its path as
+argv[1] or set KSEARCH_REF). Reads every JSON under
+kernelevalplus-main/definitions/quant_gemm*/ (the harness's operator
+definitions: weight type, the constant N and K axes, the test_configs' M
+values) and writes definition_shapes.json next to this script, one entry per
+distinct (weight type, N, K) with the definition names that use it. The
+sweep test (tests/test_definition_shapes_gpu.py) reads only that file.
+
+    python tests/golden/make_definition_shapes.py /path/to/K-Search
+"""
+from __future__ import annotations
+
+import glob
+import json
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+WTYPES = {"q4_0": "q4_0", "block_q4_0": "q4_0", "q4_1": "q4_1", "block_q4_1": "q4_1", "q8_0": "q8_0",
+          "block_q8_0": "q8_0"}
+
+
+def main() -> None:
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("KSEARCH_REF")
+    if not root:
+        raise SystemExit("usage: make_definition_shapes.py /path/to/K-Search")
+    pattern = os.path.join(root, "kernelevalplus-main", "definitions", "quant_gemm*", "**", "*.json")
+    shapes: dict[tuple, dict] = {}
+    skipped = []
+    for f in sorted(glob.glob(pattern, recursive=True)):
+        rel = os.path.relpath(f, os.path.join(root, "kernelevalplus-main", "definitions"))
+        try:
+            d = json.load(open(f))
+        except (json.JSONDecodeError, OSError):
+            skipped.append(rel)
+            continue
+        wt = WTYPES.get(d["inputs"]["weight"]["dtype"])
+        N, K = d["axes"]["N"]["value"], d["axes"]["K"]["value"]
+        ms = sorted({int(t["M"]) for t in d.get("test_configs", [])})
+        e = shapes.setdefault((wt, N, K), {"wtype": wt, "N": N, "K": K, "M": [], "definitions": []})
+        e["M"] = sorted(set(e["M"]) | set(ms))
+        e["definitions"].append(rel)
+    out = {"source": "kernelevalplus-main/definitions/quant_gemm*/ (read by make_definition_shapes.py)",
+           "skipped_unparsable": skipped,
+           "shapes": [shapes[k] for k in sorted(shapes)]}
+    with open(os.path.join(HERE, "definition_shapes.json"), "w") as fh:
+        json.dump(out, fh, indent=1)
+    print(f"{len(out['shapes'])} shapes from {sum(len(s['definitions']) for s in out['shapes'])} definitions; "
+          f"skipped {len(skipped)}")
+
+
+if __name__ == "__main__":
+    main()
