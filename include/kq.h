@@ -62,6 +62,14 @@ typedef int kq_status_t;
 #define KQ_ACT_SUM_DQ 1
 #define KQ_ACT_F32 2
 
+/* KV cache formats of the flash_attention definitions, as the harness builds
+ * them from fp32 [S, H, D] (op_test_handler.py:485-534): q8_0 blocks of each
+ * D-long row (quantize_to_q8_0), q4_0 blocks (quantize_to_q4_0, quantize.py:56-102:
+ * d = amax/7, value d (q - 8)), or fp16. */
+#define KQ_KV_Q8_0 0
+#define KQ_KV_Q4_0 1
+#define KQ_KV_F16 2
+
 typedef void* kq_stream_t; /* cudaStream_t */
 
 /* ---- library ------------------------------------------------------------ */
@@ -102,6 +110,16 @@ void kq_w4a8_q4_0_q8_1(const uint8_t* weight, const uint8_t* activation, float* 
  * unified_test_runner.py:298-303. */
 void kq_flash_attn_q8_0(const float* query, const void* key_cache, const void* value_cache, float* output,
                         int batch_size, int seq_len, int num_heads, int head_dim);
+/* The same operator for the q4_0-cache definitions
+ * (definitions/flash_attention/<model>/fp32_flash_attention_*_q4_0_cache*.json):
+ * key_cache / value_cache = q4_0 blocks (18 B) of the [S, H, D] rows. */
+void kq_flash_attn_q4_0(const float* query, const void* key_cache, const void* value_cache, float* output,
+                        int batch_size, int seq_len, int num_heads, int head_dim);
+/* The same operator for the f16-cache definitions
+ * (definitions/flash_attention/<model>/fp32_flash_attention_*_f16_cache*.json):
+ * key_cache / value_cache = fp16 [S, H, D]. */
+void kq_flash_attn_f16(const float* query, const void* key_cache, const void* value_cache, float* output,
+                       int batch_size, int seq_len, int num_heads, int head_dim);
 
 /* ---- 2. Status-returning entry points ------------------------------------ */
 
@@ -221,6 +239,10 @@ kq_status_t kq_block_sums_i32(int wtype, const void* w, const void* a_q8_1, int3
 /* Flash-attention decode, harness semantics (see kq_flash_attn_q8_0). */
 kq_status_t kq_fa_decode_q8_0_mha(const float* q, const void* k, const void* v, float* out, int B, int S, int H,
                                   int D, kq_stream_t stream);
+/* The same for any KV format (KQ_KV_*): the status form of kq_flash_attn_q8_0,
+ * kq_flash_attn_q4_0 and kq_flash_attn_f16. */
+kq_status_t kq_fa_decode_mha(int kv_format, const float* q, const void* k, const void* v, float* out, int B, int S,
+                             int H, int D, kq_stream_t stream);
 
 /* Ragged GQA flash-decode over a q8_0 KV cache (benchmark configuration 3).
  * q fp16 [B, Hq, D]; k, v = q8_0 blocks of [total_rows, Hkv, D] (total_rows =

@@ -394,14 +394,20 @@ kq_status_t kq_block_sums_i32(int wtype, const void* w, const void* a_q8_1, int3
   return launch_block_sums(wtype, w, a_q8_1, sumi, M, N, K, static_cast<cudaStream_t>(stream));
 }
 
-kq_status_t kq_fa_decode_q8_0_mha(const float* q, const void* k, const void* v, float* out, int B, int S, int H,
-                                  int D, kq_stream_t stream) {
+kq_status_t kq_fa_decode_mha(int kv_format, const float* q, const void* k, const void* v, float* out, int B, int S,
+                             int H, int D, kq_stream_t stream) {
+  if (kv_format < KQ_KV_Q8_0 || kv_format > KQ_KV_F16) return fail(KQ_ERR_INVALID, "fa_mha: unknown KV format %d", kv_format);
   if (B < 0 || S < 0 || H < 0 || D <= 0 || D % 32 || D > 256)
     return fail(KQ_ERR_INVALID, "fa_mha: bad shape B=%d S=%d H=%d D=%d (D must be a multiple of 32, <= 256)", B, S, H, D);
   if ((long long)B * H == 0) return KQ_OK;
   if (!q || !out || (S > 0 && (!k || !v))) return fail(KQ_ERR_INVALID, "fa_mha: null pointer");
   if (!aligned(k, 2) || !aligned(v, 2)) return fail(KQ_ERR_INVALID, "fa_mha: caches must be 2-byte aligned");
-  return launch_fa_mha(q, k, v, out, B, S, H, D, static_cast<cudaStream_t>(stream));
+  return launch_fa_mha(kv_format, q, k, v, out, B, S, H, D, static_cast<cudaStream_t>(stream));
+}
+
+kq_status_t kq_fa_decode_q8_0_mha(const float* q, const void* k, const void* v, float* out, int B, int S, int H,
+                                  int D, kq_stream_t stream) {
+  return kq_fa_decode_mha(KQ_KV_Q8_0, q, k, v, out, B, S, H, D, stream);
 }
 
 kq_status_t kq_fa_decode_q8_0_ragged(const void* q_f16, const void* k, const void* v, const int32_t* cu_seqlens,
@@ -442,6 +448,20 @@ void kq_flash_attn_q8_0(const float* query, const void* key_cache, const void* v
                         int batch_size, int seq_len, int num_heads, int head_dim) {
   g_last_error.clear();  // the harness shim reports a non-empty message as a failure
   kq_fa_decode_q8_0_mha(query, key_cache, value_cache, output, batch_size, seq_len, num_heads, head_dim, nullptr);
+}
+
+void kq_flash_attn_q4_0(const float* query, const void* key_cache, const void* value_cache, float* output,
+                        int batch_size, int seq_len, int num_heads, int head_dim) {
+  g_last_error.clear();
+  kq_fa_decode_mha(KQ_KV_Q4_0, query, key_cache, value_cache, output, batch_size, seq_len, num_heads, head_dim,
+                   nullptr);
+}
+
+void kq_flash_attn_f16(const float* query, const void* key_cache, const void* value_cache, float* output,
+                       int batch_size, int seq_len, int num_heads, int head_dim) {
+  g_last_error.clear();
+  kq_fa_decode_mha(KQ_KV_F16, query, key_cache, value_cache, output, batch_size, seq_len, num_heads, head_dim,
+                   nullptr);
 }
 
 }  // extern "C"

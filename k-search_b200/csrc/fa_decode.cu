@@ -71,14 +71,35 @@ __device__ __forceinline__ float load_q(const __half* q, size_t i) { return __ha
 __device__ __forceinline__ void store_o(float* o, size_t i, float v) { o[i] = v; }
 __device__ __forceinline__ void store_o(__half* o, size_t i, float v) { o[i] = __float2half_rn(v); }
 
+// KV cache element (dimension 32 j + lane) of one cache row, per format:
+//   q8_0: D/32 blocks of 34 B (fp16 d, 32 int8), value d q
+//   q4_0: D/32 blocks of 18 B (fp16 d, byte i = q[i] | q[i+16] << 4), value d (q - 8)
+//         (op_test_handler.py:502-516 builds it with quantize_to_q4_0, quantize.py:56-102)
+//   f16:  D halves
+template <int KVF>
+__device__ __forceinline__ float kv_elem(const uint8_t* row, int j, int lane) {
+  if constexpr (KVF == KQ_KV_Q8_0) {
+    const uint8_t* b = row + j * 34;
+    return half_bits_to_float(*reinterpret_cast<const uint16_t*>(b)) * (float)(int8_t)b[2 + lane];
+  } else if constexpr (KVF == KQ_KV_Q4_0) {
+    const uint8_t* b = row + j * 18;
+    const uint32_t byte = b[2 + (lane & 15)];
+    const int q = (int)(lane < 16 ? (byte & 15u) : (byte >> 4)) - 8;
+    return half_bits_to_float(*reinterpret_cast<const uint16_t*>(b)) * (float)q;
+  } else {
+    return __half2float(reinterpret_cast<const __half*>(row)[j * 32 + lane]);
+  }
+}
+__host__ __device__ constexpr int kv_block_bytes(int kvf) { return kvf == KQ_KV_Q8_0 ? 34 : kvf == KQ_KV_Q4_0 ? 18 : 64; }
+
 // RAGGED = false: grid (NC, H, ceil(B/4)); queries b of head h share KV head h.
 // RAGGED = true:  grid (NC, B*Hkv, ceil(g/4)); query heads of KV head hk.
-template <typename QT, bool RAGGED>
+template <typename QT, bool RAGGED, int KVF>
 __global__ void __launch_bounds__(32 * kQPerCta) fa_partial_kernel(FaParams p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = blockIdx.x;
   const int dj = p.D / 32;
-  const size_t row_bytes = (size_t)dj * 34;
+  const size_t row_bytes = (size_t)dj * kv_block_bytes(KVF);
 
   int qg, L, row0, row_stride;  // query index, stream length, first KV row, rows per token
   if (!RAGGED) {
@@ -116,13 +137,8 @@ __global__ void __launch_bounds__(32 * kQPerCta) fa_partial_kernel(FaParams p) {
     const uint8_t* vb = p.v + row * row_bytes;
     float s = 0.0f;
 #pragma unroll
-    for (int j = 0; j < kMaxDJ; ++j) {
-      if (j < dj) {
-        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(kb + j * 34));
-        const float kq = (float)(int8_t)kb[j * 34 + 2 + lane];
-        s = fmaf(d, qv[j] * kq, s);
-      }
-    }
+    for (int j = 0; j < kMaxDJ; ++j)
+      if (j < dj) s = fmaf(qv[j], kv_elem<KVF>(kb, j, lane), s);
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     const float mn = fmaxf(m, s);
@@ -130,13 +146,8 @@ __global__ void __launch_bounds__(32 * kQPerCta) fa_partial_kernel(FaParams p) {
     const float pr = exp2f(s - mn);
     l = fmaf(l, corr, pr);
 #pragma unroll
-    for (int j = 0; j < kMaxDJ; ++j) {
-      if (j < dj) {
-        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(vb + j * 34));
-        const float vq = (float)(int8_t)vb[j * 34 + 2 + lane];
-        acc[j] = fmaf(acc[j], corr, pr * d * vq);
-      }
-    }
+    for (int j = 0; j < kMaxDJ; ++j)
+      if (j < dj) acc[j] = fmaf(acc[j], corr, pr * kv_elem<KVF>(vb, j, lane));
     m = mn;
   }
   const size_t pi = (size_t)qg * p.NC + c;
@@ -807,8 +818,8 @@ constexpr size_t kPartialBudget = 64ull << 20;
 
 }  // namespace
 
-kq_status_t launch_fa_mha(const float* q, const void* k, const void* v, float* out, int B, int S, int H, int D,
-                          cudaStream_t s) {
+kq_status_t launch_fa_mha(int kvf, const float* q, const void* k, const void* v, float* out, int B, int S, int H,
+                          int D, cudaStream_t s) {
   const long long Q = (long long)B * H;
   if (Q == 0) return KQ_OK;
   int chunk = 0;
@@ -821,7 +832,7 @@ kq_status_t launch_fa_mha(const float* q, const void* k, const void* v, float* o
   p.pm = ws; p.pl = ws + Q * NC; p.pacc = ws + 2 * Q * NC; p.out = out;
   p.B = B; p.H = H; p.Hkv = H; p.D = D; p.S = S; p.NC = NC; p.chunk = chunk;
   p.qscale = (float)(1.0 / std::sqrt((double)D) * 1.4426950408889634);
-  if (fast_ok(k, v, D, H, 1) && S > 0) {
+  if (kvf == KQ_KV_Q8_0 && fast_ok(k, v, D, H, 1) && S > 0) {
     FastParams f{q, nullptr, p.pm, p.pl, p.pacc, B, H, H, S, NC, chunk, H / kHpc, p.qscale};
     const long long items = (long long)((B + kG - 1) / kG) * (H / kHpc);
     if (items <= 65535) {
@@ -833,7 +844,12 @@ kq_status_t launch_fa_mha(const float* q, const void* k, const void* v, float* o
   }
   dim3 grid(NC, H, (B + kQPerCta - 1) / kQPerCta);
   if (grid.z > 65535 || grid.y > 65535) return fail(KQ_ERR_UNSUPPORTED, "fa_mha: grid too large");
-  fa_partial_kernel<float, false><<<grid, 32 * kQPerCta, 0, s>>>(p);
+  switch (kvf) {
+    case KQ_KV_Q8_0: fa_partial_kernel<float, false, KQ_KV_Q8_0><<<grid, 32 * kQPerCta, 0, s>>>(p); break;
+    case KQ_KV_Q4_0: fa_partial_kernel<float, false, KQ_KV_Q4_0><<<grid, 32 * kQPerCta, 0, s>>>(p); break;
+    case KQ_KV_F16: fa_partial_kernel<float, false, KQ_KV_F16><<<grid, 32 * kQPerCta, 0, s>>>(p); break;
+    default: return fail(KQ_ERR_INVALID, "fa_mha: unknown KV format %d", kvf);
+  }
   kq_status_t st = check_launch("fa_partial(mha)");
   if (st) return st;
   fa_combine_kernel<float><<<(unsigned)((Q + 3) / 4), 128, 0, s>>>(p, (int)Q);
@@ -865,7 +881,7 @@ kq_status_t launch_fa_ragged(const void* q, const void* k, const void* v, const 
   }
   dim3 grid(NC, (unsigned)((long long)B * Hkv), (g + kQPerCta - 1) / kQPerCta);
   if (grid.y > 65535) return fail(KQ_ERR_UNSUPPORTED, "fa_ragged: B*Hkv too large");
-  fa_partial_kernel<__half, true><<<grid, 32 * kQPerCta, 0, s>>>(p);
+  fa_partial_kernel<__half, true, KQ_KV_Q8_0><<<grid, 32 * kQPerCta, 0, s>>>(p);
   kq_status_t st = check_launch("fa_partial(ragged)");
   if (st) return st;
   fa_combine_kernel<__half><<<(unsigned)((Q + 3) / 4), 128, 0, s>>>(p, (int)Q);

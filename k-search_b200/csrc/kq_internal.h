@@ -128,8 +128,9 @@ kq_status_t launch_moe_q4_0(const float* x, const float* logits, const void* w_g
 kq_status_t launch_block_sums(int wtype, const void* w, const void* a_q8_1, int32_t* sumi, int M, int N, int K,
                               cudaStream_t s);
 // fa_decode.cu
-kq_status_t launch_fa_mha(const float* q, const void* k, const void* v, float* out, int B, int S, int H, int D,
-                          cudaStream_t s);
+// kv_format: KQ_KV_Q8_0 / KQ_KV_Q4_0 / KQ_KV_F16
+kq_status_t launch_fa_mha(int kv_format, const float* q, const void* k, const void* v, float* out, int B, int S, int H,
+                          int D, cudaStream_t s);
 kq_status_t launch_fa_ragged(const void* q, const void* k, const void* v, const int32_t* cu, int B, int Hq, int Hkv,
                              int D, int max_seqlen, int total_rows, float scale, void* out, cudaStream_t s);
 

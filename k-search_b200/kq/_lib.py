@@ -30,6 +30,8 @@ SIGNATURES = {
     "kq_w8a32c8_q8_0_fp32_int8": (None, [_vp, _vp, _vp, _i, _i, _i]),
     "kq_w4a8_q4_0_q8_1": (None, [_vp, _vp, _vp, _i, _i, _i]),
     "kq_flash_attn_q8_0": (None, [_vp, _vp, _vp, _vp, _i, _i, _i, _i]),
+    "kq_flash_attn_q4_0": (None, [_vp, _vp, _vp, _vp, _i, _i, _i, _i]),
+    "kq_flash_attn_f16": (None, [_vp, _vp, _vp, _vp, _i, _i, _i, _i]),
     "kq_quantize_q8_1": (_i, [_vp, _vp, _i64, _i64, _i, _vp]),
     "kq_quantize_rows": (_i, [_i, _vp, _vp, _i64, _i64, _vp]),
     "kq_mul_mat_q": (_i, [_i, _vp, _vp, _vp, _i, _i, _i, _vp]),
@@ -48,6 +50,7 @@ SIGNATURES = {
     "kq_moe_combine": (_i, [_vp, _vp, _i, _i, _i, _vp, _vp]),
     "kq_block_sums_i32": (_i, [_i, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "kq_fa_decode_q8_0_mha": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "kq_fa_decode_mha": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "kq_fa_decode_q8_0_ragged": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp, _vp]),
 }
 

@@ -31,10 +31,28 @@ def quant_gemm_forward(weight: torch.Tensor, activation: torch.Tensor, M: int, N
     raise ValueError(f"unsupported activation dtype {activation_dtype!r}")
 
 
+def flash_attention_kv_format(spec: dict) -> str:
+    """KV cache format of a flash_attention definition, decided as the harness
+    decides it (op_test_handler.py:483-534): key_cache dtype "int8" means q8_0
+    when the variant or a tag names q8, else q4_0; "float16" (and any other
+    dtype but "float32") means fp16. fp32 caches are not a format of any
+    shipped definition and are rejected."""
+    dtype = spec.get("inputs", {}).get("key_cache", {}).get("dtype", "float16")
+    if dtype == "int8":
+        variant = spec.get("variant", "").lower()
+        tags = spec.get("tags", [])
+        return "q8_0" if ("q8" in variant or any("q8" in t for t in tags)) else "q4_0"
+    if dtype == "float32":
+        raise ValueError("fp32 KV caches are not supported (no flash_attention definition uses them)")
+    return "f16"
+
+
 def flash_attention_forward(query: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
-                            batch_size: int, seq_len: int, num_heads: int, head_dim: int) -> torch.Tensor:
-    """forward(q, k, v, B, S, H, D) -> fp32 [B, H, D] for q8_0 caches (op_test_handler.py:565-579)."""
-    return ops.flash_attn_q8_0(query, key_cache, value_cache, batch_size, seq_len, num_heads, head_dim)
+                            batch_size: int, seq_len: int, num_heads: int, head_dim: int,
+                            kv_format: str = "q8_0") -> torch.Tensor:
+    """forward(q, k, v, B, S, H, D) -> fp32 [B, H, D] (op_test_handler.py:565-579);
+    ``kv_format`` is ``flash_attention_kv_format(spec)`` of the definition."""
+    return ops.flash_attn(query, key_cache, value_cache, batch_size, seq_len, num_heads, head_dim, kv_format)
 
 
 def quant_gemm_test_configs(N: int, K: int) -> list[dict]:

@@ -214,20 +214,37 @@ def block_sums_i32(weight: torch.Tensor, a_q8_1: torch.Tensor, M: int, N: int, K
     return out
 
 
-def flash_attn_q8_0(query: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor, batch_size: int,
-                    seq_len: int, num_heads: int, head_dim: int) -> torch.Tensor:
-    """Harness flash_attention with q8_0 caches -> fp32 [B, H, D]."""
+# KV cache formats of the flash_attention definitions (include/kq.h KQ_KV_*)
+# and the bytes of one 32-element group of a cache row in each.
+KV_FORMATS = {"q8_0": 0, "q4_0": 1, "f16": 2}
+KV_GROUP_BYTES = {"q8_0": 34, "q4_0": 18, "f16": 64}
+
+
+def flash_attn(query: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor, batch_size: int,
+               seq_len: int, num_heads: int, head_dim: int, kv_format: str = "q8_0") -> torch.Tensor:
+    """Harness flash_attention -> fp32 [B, H, D]. query fp32 [B, H, D]; the
+    caches are the [S, H, D] rows as q8_0 blocks, q4_0 blocks or fp16."""
+    if kv_format not in KV_FORMATS:
+        raise ValueError(f"unknown KV format {kv_format!r} (expected one of {sorted(KV_FORMATS)})")
     _cuda(query, "query", torch.float32, batch_size * num_heads * head_dim)
-    nbytes = seq_len * num_heads * (head_dim // 32) * 34
+    nbytes = seq_len * num_heads * (head_dim // 32) * KV_GROUP_BYTES[kv_format]
     _cuda(key_cache, "key_cache", None, None)
     _cuda(value_cache, "value_cache", None, None)
     if key_cache.numel() * key_cache.element_size() != nbytes or value_cache.numel() * value_cache.element_size() != nbytes:
-        raise ValueError("q8_0 cache size does not match seq_len * num_heads * head_dim/32 * 34 bytes")
+        raise ValueError(f"{kv_format} cache size does not match seq_len * num_heads * head_dim/32 * "
+                         f"{KV_GROUP_BYTES[kv_format]} bytes")
     out = torch.empty((batch_size, num_heads, head_dim), dtype=torch.float32, device=query.device)
-    check(lib().kq_fa_decode_q8_0_mha(query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), out.data_ptr(),
-                                      batch_size, seq_len, num_heads, head_dim, _stream(query)),
-          "kq_fa_decode_q8_0_mha")
+    check(lib().kq_fa_decode_mha(KV_FORMATS[kv_format], query.data_ptr(), key_cache.data_ptr(),
+                                 value_cache.data_ptr(), out.data_ptr(), batch_size, seq_len, num_heads, head_dim,
+                                 _stream(query)),
+          "kq_fa_decode_mha")
     return out
+
+
+def flash_attn_q8_0(query: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor, batch_size: int,
+                    seq_len: int, num_heads: int, head_dim: int) -> torch.Tensor:
+    """Harness flash_attention with q8_0 caches -> fp32 [B, H, D]."""
+    return flash_attn(query, key_cache, value_cache, batch_size, seq_len, num_heads, head_dim, "q8_0")
 
 
 def flash_decode_ragged(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: torch.Tensor, num_kv_heads: int,

@@ -374,14 +374,34 @@ def dequant_q8_0_rows(kv: np.ndarray, rows: int, D: int) -> np.ndarray:
     return dequantize("q8_0", kv, rows, D)
 
 
-def flash_decode_mha(q: np.ndarray, k: np.ndarray, v: np.ndarray, S: int, H: int, D: int) -> np.ndarray:
-    """Harness flash_attention op with a q8_0 cache
-    (llm_kernel_test/op_test_handler.py:489-508 builds the cache as q8_0 of
-    the [S*H, D] rows; :543-563 is the attention). K/V are dequantised from the
-    q8_0 bytes; scores, softmax and the weighted sum are in fp64.
-    q: fp32 [B, H, D]; k, v: bytes of [S, H, D/32, 34]. Returns fp32 [B, H, D]."""
-    K_ = dequant_q8_0_rows(k, S * H, D).reshape(S, H, D).astype(np.float64)
-    V_ = dequant_q8_0_rows(v, S * H, D).reshape(S, H, D).astype(np.float64)
+def dequant_q4_0_rows(kv: np.ndarray, rows: int, D: int) -> np.ndarray:
+    """q4_0 bytes of [rows, D] -> fp32 [rows, D] (value d (q - 8); low nibbles
+    are elements 0-15 of a block, high nibbles 16-31: quantize.py:56-102)."""
+    return dequantize("q4_0", np.asarray(kv, dtype=np.uint8).reshape(rows, -1), rows, D)
+
+
+def dequant_kv_rows(kv_format: str, kv: np.ndarray, rows: int, D: int) -> np.ndarray:
+    """A KV cache of one of the flash_attention definitions' formats
+    (op_test_handler.py:489-534: q8_0 or q4_0 blocks of each D-long row, or
+    fp16) -> fp32 [rows, D]."""
+    if kv_format == "q8_0":
+        return dequant_q8_0_rows(kv, rows, D)
+    if kv_format == "q4_0":
+        return dequant_q4_0_rows(kv, rows, D)
+    if kv_format == "f16":
+        return np.asarray(kv).view(np.float16).reshape(rows, D).astype(np.float32)
+    raise ValueError(f"unknown KV format {kv_format!r}")
+
+
+def flash_decode_mha(q: np.ndarray, k: np.ndarray, v: np.ndarray, S: int, H: int, D: int,
+                     kv_format: str = "q8_0") -> np.ndarray:
+    """Harness flash_attention op (llm_kernel_test/op_test_handler.py:489-534
+    builds the cache from fp32 [S, H, D] as q8_0 / q4_0 blocks of the [S*H, D]
+    rows or as fp16; :543-563 is the attention). K/V are dequantised from the
+    cache bytes; scores, softmax and the weighted sum are in fp64.
+    q: fp32 [B, H, D]; k, v: cache bytes. Returns fp32 [B, H, D]."""
+    K_ = dequant_kv_rows(kv_format, k, S * H, D).reshape(S, H, D).astype(np.float64)
+    V_ = dequant_kv_rows(kv_format, v, S * H, D).reshape(S, H, D).astype(np.float64)
     qq = np.asarray(q, dtype=np.float64)
     sc = np.einsum("bhd,shd->bhs", qq, K_) / np.sqrt(D)
     sc -= sc.max(axis=-1, keepdims=True)

@@ -1,4 +1,5 @@
-"""Record the shapes of the reference's quant_gemm definitions as a fixture.
+"""Record the shapes of the reference's quant_gemm and flash_attention
+definitions as fixtures.
 
 Runs ONLY where the qhy991/K-Search checkout is present (pass its path as
 argv[1] or set KSEARCH_REF). Reads every JSON under
@@ -7,6 +8,11 @@ definitions: weight type, the constant N and K axes, the test_configs' M
 values) and writes definition_shapes.json next to this script, one entry per
 distinct (weight type, N, K) with the definition names that use it. The
 sweep test (tests/test_definition_shapes_gpu.py) reads only that file.
+Also writes flash_attention_definitions.json: for every JSON under
+definitions/flash_attention/, the fields the harness reads to build the
+inputs (key_cache dtype, variant, tags, the S / H / D axes, the test_configs'
+batch sizes); tests/test_flash_decode_gpu.py and tests/test_harness_mirror.py
+read that file.
 
     python tests/golden/make_definition_shapes.py /path/to/K-Search
 """
@@ -49,6 +55,24 @@ def main() -> None:
         json.dump(out, fh, indent=1)
     print(f"{len(out['shapes'])} shapes from {sum(len(s['definitions']) for s in out['shapes'])} definitions; "
           f"skipped {len(skipped)}")
+    fa_defs(root)
+
+
+def fa_defs(root: str) -> None:
+    base = os.path.join(root, "kernelevalplus-main", "definitions")
+    defs = []
+    for f in sorted(glob.glob(os.path.join(base, "flash_attention", "**", "*.json"), recursive=True)):
+        d = json.load(open(f))
+        defs.append({"definition": os.path.relpath(f, base),
+                     "key_cache_dtype": d["inputs"]["key_cache"]["dtype"],
+                     "variant": d.get("variant", ""), "tags": d.get("tags", []),
+                     "S": d["axes"]["seq_len"]["value"], "H": d["axes"]["num_heads"]["value"],
+                     "D": d["axes"]["head_dim"]["value"],
+                     "B": sorted({int(t["batch_size"]) for t in d.get("test_configs", [])})})
+    with open(os.path.join(HERE, "flash_attention_definitions.json"), "w") as fh:
+        json.dump({"source": "kernelevalplus-main/definitions/flash_attention/ (read by make_definition_shapes.py)",
+                   "definitions": defs}, fh, indent=1)
+    print(f"{len(defs)} flash_attention definitions")
 
 
 if __name__ == "__main__":

@@ -121,6 +121,43 @@ def main() -> None:
         ref_on_q8_0=h.get_reference_output(spec, inputs_deq).numpy(),
         ref_on_fp32=h.get_reference_output(spec, inputs_raw).numpy(),
     )
+
+    # --- flash-attention decode, every KV format: the harness's own input
+    # builder (op_test_handler.py:472-541) picks the format from the spec
+    # fields and quantises the fp32 caches; the attention is then its oracle
+    # (:543-563) on the dequantised cache (q4_0 dequantised by the reference's
+    # q4_0 GEMM against an identity, gemm_ref.py:51-99, exact in fp32; fp16
+    # through the handler's key_cache path) and on the fp32 caches.
+    B, S, H, D = 2, 48, 3, 64
+    specs = {
+        "q8_0": ("int8", "FP32_Q8_0", ["kv_cache:q8_0"]),
+        "q4_0": ("int8", "FP32_Q4_0", ["kv_cache:q4_0"]),
+        "f16": ("float16", "FP32", ["kv_cache:f16"]),
+    }
+    fa = {"B": B, "S": S, "H": H, "D": D}
+    for i, (fmt, (dtype, variant, tags)) in enumerate(specs.items()):
+        spec = {"axes": {"seq_len": {"value": S}, "num_heads": {"value": H}, "head_dim": {"value": D}},
+                "inputs": {"key_cache": {"dtype": dtype}}, "variant": variant, "tags": tags}
+        torch.manual_seed(1000 + i)
+        inp = h.generate_inputs(spec, {"batch_size": B}, "cpu")
+        kc, vc = inp["key_cache"].numpy(), inp["value_cache"].numpy()
+        if fmt == "q8_0":
+            kd, vd = deq(kc.reshape(-1)), deq(vc.reshape(-1))
+        elif fmt == "q4_0":
+            eye = torch.eye(D, dtype=torch.float32)
+            kd = reference_q4_0_fp32_gemm(T(kc), eye, D, S * H, D).numpy().T.reshape(S, H, D)
+            vd = reference_q4_0_fp32_gemm(T(vc), eye, D, S * H, D).numpy().T.reshape(S, H, D)
+        else:
+            kd, vd = kc.astype(np.float32), vc.astype(np.float32)
+        on_cache = {"query": inp["query"], "key_cache_fp32": T(np.ascontiguousarray(kd)),
+                    "value_cache_fp32": T(np.ascontiguousarray(vd))}
+        fa.update({f"{fmt}_spec_dtype": dtype, f"{fmt}_spec_variant": variant,
+                   f"{fmt}_q": inp["query"].numpy(),
+                   f"{fmt}_k_fp32": inp["key_cache_fp32"].numpy(), f"{fmt}_v_fp32": inp["value_cache_fp32"].numpy(),
+                   f"{fmt}_k": kc, f"{fmt}_v": vc,
+                   f"{fmt}_ref_on_cache": h.get_reference_output(spec, on_cache).numpy(),
+                   f"{fmt}_ref_on_fp32": h.get_reference_output(spec, inp).numpy()})
+    np.savez_compressed(os.path.join(HERE, "flash_attn_kv.npz"), **fa)
     print("golden fixtures written to", HERE)
 
 

@@ -53,5 +53,48 @@ def test_host_only_entry_points(libkq):
     assert "multiple of 32" in _lib.last_error()
     assert L.kq_quantize_q8_1(None, None, 1, 31, 0, None) == 1
     assert L.kq_fa_decode_q8_0_mha(None, None, None, None, 1, 1, 1, 48, None) == 1
+    assert L.kq_fa_decode_mha(3, None, None, None, None, 1, 1, 1, 32, None) == 1
+    assert "unknown KV format" in _lib.last_error()
+    assert L.kq_fa_decode_mha(1, None, None, None, None, 1, 1, 1, 48, None) == 1
     # empty problems are no-ops
     assert L.kq_gemm_f32act(0, None, None, None, 0, 16, 64, 2, None) == 0
+
+
+def test_harness_kv_format_of_every_definition():
+    """The harness mirror picks each flash_attention definition's KV format
+    as the harness does (key_cache dtype, then q8 in variant or tags); the
+    shipped definitions name their format in the file name."""
+    import json
+    from kq import harness
+    here = os.path.join(REPO, "tests", "golden")
+    defs = json.load(open(os.path.join(here, "flash_attention_definitions.json")))["definitions"]
+    assert len(defs) == 18
+    seen = set()
+    for d in defs:
+        spec = {"inputs": {"key_cache": {"dtype": d["key_cache_dtype"]}}, "variant": d["variant"], "tags": d["tags"]}
+        fmt = harness.flash_attention_kv_format(spec)
+        assert f"_{fmt}_cache" in d["definition"], d["definition"]
+        seen.add(fmt)
+    assert seen == {"q8_0", "q4_0", "f16"}
+    import numpy as np
+    g = np.load(os.path.join(here, "flash_attn_kv.npz"))
+    for fmt in ("q8_0", "q4_0", "f16"):
+        spec = {"inputs": {"key_cache": {"dtype": str(g[f"{fmt}_spec_dtype"])}},
+                "variant": str(g[f"{fmt}_spec_variant"]), "tags": []}
+        assert harness.flash_attention_kv_format(spec) == fmt
+
+
+@pytest.mark.parametrize("name", ["kernel_quant_gemm.cu", "kernel_flash_attn.cu", "kernel_flash_attn_q4_0.cu",
+                                  "kernel_flash_attn_f16.cu"])
+def test_harness_forwarders_build(name, tmp_path):
+    """The attempt files are host-only C++: they compile with g++ and export
+    the entry the harness binds."""
+    import shutil
+    import subprocess
+    if not shutil.which("g++"):
+        pytest.skip("g++ not available")
+    src = os.path.join(REPO, "k-search_b200", "harness", name)
+    so = str(tmp_path / "attempt.so")
+    subprocess.run(["g++", "-x", "c++", "-std=c++17", "-O1", "-fPIC", "-shared", src, "-o", so, "-ldl"], check=True)
+    entry = re.search(r'extern "C" void (\w+)\(', open(src).read()).group(1)
+    assert hasattr(ctypes.CDLL(so), entry)

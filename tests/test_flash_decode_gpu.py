@@ -1,10 +1,11 @@
-"""GPU parity of flash-attention decode over a q8_0 KV cache.
+"""GPU parity of flash-attention decode over q8_0 / q4_0 / fp16 KV caches.
 
 Bar: rel-L2 <= 1e-3 and per element |out - ref| <= 1e-2 |ref| + 1e-3 rms(ref)
 against the fp64 oracle on the same q8_0 bytes; fp16 outputs are compared
 after the oracle's fp64 result (the fp16 rounding of the output is inside
 the bar). Plus the harness's NMSE <= 0.05 gate against unquantised K/V.
 """
+import json
 import os
 
 import numpy as np
@@ -66,6 +67,78 @@ def test_harness_void_entry(cuda):
     # harness gate: attention on the unquantised caches
     ref = np.einsum("bhs,shd->bhd", _softmax(np.einsum("bhd,shd->bhs", q, kf) / np.sqrt(D)), vf)
     assert Q.nmse(got, ref) < 0.05
+
+
+_FA_DEFS = json.load(open(os.path.join(os.path.dirname(__file__), "golden",
+                                      "flash_attention_definitions.json")))["definitions"]
+
+
+def _cache(fmt, x, D):
+    """fp32 [S, H, D] -> cache bytes as the harness builds them (op_test_handler.py:489-534)."""
+    if fmt == "q8_0":
+        return Q.quantize_q8_0(x.reshape(-1, D))
+    if fmt == "q4_0":
+        return Q.quantize_q4_0(x.reshape(-1, D))
+    return x.astype(np.float16)
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "f16"])
+@pytest.mark.parametrize("B,S,H,D", [(1, 512, 32, 128), (8, 1000, 4, 128), (3, 4096, 2, 64), (2, 1, 3, 32),
+                                     (16, 300, 2, 256), (5, 77, 28, 128)])
+def test_mha_parity_kv_formats(cuda, fmt, B, S, H, D):
+    import kq
+    rng = np.random.default_rng(B * S + H + len(fmt))
+    q = rng.standard_normal((B, H, D)).astype(np.float32)
+    k = _cache(fmt, rng.standard_normal((S, H, D)).astype(np.float32), D)
+    v = _cache(fmt, rng.standard_normal((S, H, D)).astype(np.float32), D)
+    got = kq.flash_attn(_t(q, cuda), _t(k, cuda), _t(v, cuda), B, S, H, D, fmt).cpu().numpy()
+    ok, msg = Q.check_close(got, Q.flash_decode_mha(q, k, v, S, H, D, fmt))
+    assert ok, msg
+
+
+@pytest.mark.parametrize("defn", _FA_DEFS, ids=lambda d: os.path.basename(d["definition"])[:-5])
+def test_definition_flash_attention(cuda, defn):
+    """Every flash_attention definition the reference ships, at each of its
+    batch sizes, through the harness mirror (KV format decided from the
+    definition as the harness decides it). Queries are independent, so the
+    full batch runs and up to four query rows are checked against the oracle
+    on the cache bytes and against the harness's NMSE gate on fp32 K/V."""
+    import kq
+    S, H, D = defn["S"], defn["H"], defn["D"]
+    spec = {"inputs": {"key_cache": {"dtype": defn["key_cache_dtype"]}}, "variant": defn["variant"],
+            "tags": defn["tags"]}
+    fmt = kq.harness.flash_attention_kv_format(spec)
+    rng = np.random.default_rng(S + H + len(defn["definition"]))
+    kf = rng.standard_normal((S, H, D)).astype(np.float32)
+    vf = rng.standard_normal((S, H, D)).astype(np.float32)
+    k, v = _cache(fmt, kf, D), _cache(fmt, vf, D)
+    kd, vd = _t(k, cuda), _t(v, cuda)
+    for B in defn["B"]:
+        q = rng.standard_normal((B, H, D)).astype(np.float32)
+        got = kq.harness.flash_attention_forward(_t(q, cuda), kd, vd, B, S, H, D, fmt).cpu().numpy()
+        rows = np.unique(np.array([0, B // 3, (2 * B) // 3, B - 1]))
+        ok, msg = Q.check_close(got[rows], Q.flash_decode_mha(q[rows], k, v, S, H, D, fmt))
+        assert ok, f"B={B}: {msg}"
+        ref = np.einsum("bhs,shd->bhd", _softmax(np.einsum("bhd,shd->bhs", q[rows], kf) / np.sqrt(D)), vf)
+        assert Q.nmse(got[rows], ref) < 0.05, f"B={B}"
+
+
+@pytest.mark.parametrize("fmt,entry", [("q4_0", "kq_flash_attn_q4_0"), ("f16", "kq_flash_attn_f16")])
+def test_harness_void_entry_kv_formats(cuda, fmt, entry):
+    import kq
+    rng = np.random.default_rng(11)
+    B, S, H, D = 3, 512, 28, 128
+    q = rng.standard_normal((B, H, D)).astype(np.float32)
+    k = _cache(fmt, rng.standard_normal((S, H, D)).astype(np.float32), D)
+    v = _cache(fmt, rng.standard_normal((S, H, D)).astype(np.float32), D)
+    out = torch.empty((B, H, D), dtype=torch.float32, device=cuda)
+    qd, kd, vd = _t(q, cuda), _t(k, cuda), _t(v, cuda)
+    torch.cuda.synchronize()
+    getattr(kq.lib(), entry)(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), out.data_ptr(), B, S, H, D)
+    torch.cuda.synchronize()
+    assert kq.lib().kq_last_error() == b""
+    ok, msg = Q.check_close(out.cpu().numpy(), Q.flash_decode_mha(q, k, v, S, H, D, fmt))
+    assert ok, msg
 
 
 def _softmax(x):

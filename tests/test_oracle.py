@@ -109,6 +109,26 @@ def test_flash_attention_matches_reference():
     assert Q.nmse(out, g["ref_on_fp32"]) < 0.05
 
 
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0", "f16"])
+def test_flash_attention_kv_formats_match_reference(fmt):
+    """Cache bytes from the harness's own input builder (format chosen from the
+    spec, fp32 caches quantised by the reference): the oracle's quantiser
+    reproduces them bit for bit and its attention on them matches the
+    harness's attention on the dequantised cache."""
+    g = _load("flash_attn_kv.npz")
+    B, S, H, D = (int(g[k]) for k in "BSHD")
+    k, v = g[f"{fmt}_k"], g[f"{fmt}_v"]
+    if fmt == "f16":
+        assert np.array_equal(g[f"{fmt}_k_fp32"].astype(np.float16), k)
+    else:
+        quant = Q.quantize_q8_0 if fmt == "q8_0" else Q.quantize_q4_0
+        assert np.array_equal(quant(g[f"{fmt}_k_fp32"].reshape(-1, D)).reshape(-1), k.reshape(-1))
+        assert np.array_equal(quant(g[f"{fmt}_v_fp32"].reshape(-1, D)).reshape(-1), v.reshape(-1))
+    out = Q.flash_decode_mha(g[f"{fmt}_q"], k, v, S, H, D, fmt)
+    np.testing.assert_allclose(out, g[f"{fmt}_ref_on_cache"], rtol=1e-5, atol=1e-6)
+    assert Q.nmse(out, g[f"{fmt}_ref_on_fp32"]) < 0.05
+
+
 def test_ragged_decode_reduces_to_mha():
     g = _load("flash_attn.npz")
     B, S, H, D = (int(g[k]) for k in "BSHD")
