@@ -1,10 +1,11 @@
-// Flash-attention decode over a q8_0 KV cache (split-KV "flash decoding").
+// Flash-attention decode over a q8_0, q4_0 or fp16 KV cache (split-KV "flash
+// decoding").
 //
 // Semantics: the harness flash_attention operator
 // (kernelevalplus-main/llm_kernel_test/op_test_handler.py:543-563):
 // out = softmax(q . K^T / sqrt(D)) . V per (query, head), with K and V stored
 // as q8_0 blocks along head_dim (op_test_handler.py:489-508), dequantised as
-// x = q * d. The ragged GQA form (one KV stream per (sequence, KV head),
+// x = q * d, as q4_0 blocks (x = d (q - 8)) or as fp16. The ragged GQA form (one KV stream per (sequence, KV head),
 // shared by Hq/Hkv query heads) follows the same arithmetic.
 //
 // Fast path (head_dim 128, KV heads in groups of 8, <= 4 queries per KV
@@ -20,9 +21,11 @@
 // Generic path: pass 1 gives every (KV stream, token chunk, query group) to one
 // CTA, one warp per query; each warp keeps an online-softmax state (running
 // max in the log2 domain, running sum, fp32 accumulator) and writes it as a
-// partial. Pass 2 merges the partials of each query. Lanes own head-dim
-// elements {32 j + lane}, so every q8_0 block row is read as 32 consecutive
-// bytes by the warp.
+// partial; it takes 8 tokens per step (independent loads, interleaved
+// reductions, one rescale). Pass 2 merges the partials of each query. For
+// head_dim 64, 128 or 256 a lane owns D/32 consecutive elements (one vector
+// load of fp16, or 2-byte loads of codes inside one block plus its scale);
+// otherwise lanes own elements {32 j + lane}.
 #include <cuda.h>
 
 #include <algorithm>
@@ -52,6 +55,7 @@ CUresult encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, cuuint32_t rank,
 
 constexpr int kQPerCta = 4;  // queries (warps) per CTA
 constexpr int kMaxDJ = 8;    // head_dim <= 256
+constexpr int kTokU = 8;     // tokens per step of the generic kernel
 
 struct FaParams {
   const void* q;
@@ -92,20 +96,65 @@ __device__ __forceinline__ float kv_elem(const uint8_t* row, int j, int lane) {
 }
 __host__ __device__ constexpr int kv_block_bytes(int kvf) { return kvf == KQ_KV_Q8_0 ? 34 : kvf == KQ_KV_Q4_0 ? 18 : 64; }
 
+// Elements DJ*lane .. DJ*lane + DJ - 1 of a cache row with D = 32 DJ,
+// DJ in {2, 4, 8}: they lie in one 32-element block. fp16 rows need 2 DJ-byte
+// alignment; block codes start at an even offset (2-byte loads).
+template <int KVF, int DJ>
+__device__ __forceinline__ void kv_lane(const uint8_t* row, int lane, float (&x)[DJ]) {
+  static_assert(DJ == 2 || DJ == 4 || DJ == 8, "DJ");
+  const int e0 = DJ * lane;
+  if constexpr (KVF == KQ_KV_F16) {
+    const uint8_t* p = row + 2 * e0;
+    auto cvt = [](uint32_t w, float& a, float& b) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+      a = f.x;
+      b = f.y;
+    };
+    if constexpr (DJ == 8) {
+      const uint4 u = *reinterpret_cast<const uint4*>(p);
+      cvt(u.x, x[0], x[1]); cvt(u.y, x[2], x[3]); cvt(u.z, x[4], x[5]); cvt(u.w, x[6], x[7]);
+    } else if constexpr (DJ == 4) {
+      const uint2 u = *reinterpret_cast<const uint2*>(p);
+      cvt(u.x, x[0], x[1]); cvt(u.y, x[2], x[3]);
+    } else {
+      cvt(*reinterpret_cast<const uint32_t*>(p), x[0], x[1]);
+    }
+  } else {
+    const int o = e0 & 31;
+    const uint8_t* blk = row + (e0 >> 5) * kv_block_bytes(KVF);
+    const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(blk));
+    if constexpr (KVF == KQ_KV_Q8_0) {
+      const uint16_t* c = reinterpret_cast<const uint16_t*>(blk + 2 + o);
+#pragma unroll
+      for (int i = 0; i < DJ / 2; ++i) {
+        const uint32_t v = c[i];
+        x[2 * i] = d * (float)(int8_t)(v & 0xffu);
+        x[2 * i + 1] = d * (float)(int8_t)(v >> 8);
+      }
+    } else {
+      // byte i of a block holds element i (low nibble) and i + 16 (high)
+      const int sh = o < 16 ? 0 : 4;
+      const uint16_t* c = reinterpret_cast<const uint16_t*>(blk + 2 + (o & 15));
+#pragma unroll
+      for (int i = 0; i < DJ / 2; ++i) {
+        const uint32_t v = c[i];
+        x[2 * i] = d * (float)((int)((v >> sh) & 15u) - 8);
+        x[2 * i + 1] = d * (float)((int)((v >> (8 + sh)) & 15u) - 8);
+      }
+    }
+  }
+}
+
 // RAGGED = false: grid (NC, H, ceil(B/4)); queries b of head h share KV head h.
 // RAGGED = true:  grid (NC, B*Hkv, ceil(g/4)); query heads of KV head hk.
-template <typename QT, bool RAGGED, int KVF>
-__global__ void __launch_bounds__(32 * kQPerCta) fa_partial_kernel(FaParams p) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int c = blockIdx.x;
-  const int dj = p.D / 32;
-  const size_t row_bytes = (size_t)dj * kv_block_bytes(KVF);
-
-  int qg, L, row0, row_stride;  // query index, stream length, first KV row, rows per token
+// This warp's query of a generic-path CTA: query index, stream length, first
+// KV row, rows per token. False when the warp has no query.
+template <bool RAGGED>
+__device__ __forceinline__ bool fa_query(const FaParams& p, int warp, int& qg, int& L, int& row0, int& row_stride) {
   if (!RAGGED) {
     const int h = blockIdx.y;
     const int b = blockIdx.z * kQPerCta + warp;
-    if (b >= p.B) return;
+    if (b >= p.B) return false;
     qg = b * p.H + h;
     L = p.S;
     row0 = h;
@@ -114,13 +163,25 @@ __global__ void __launch_bounds__(32 * kQPerCta) fa_partial_kernel(FaParams p) {
     const int b = blockIdx.y / p.Hkv, hk = blockIdx.y % p.Hkv;
     const int g = p.H / p.Hkv;
     const int j = blockIdx.z * kQPerCta + warp;
-    if (j >= g) return;
+    if (j >= g) return false;
     qg = b * p.H + hk * g + j;
     const int s0 = p.cu[b];
     L = p.cu[b + 1] - s0;
     row0 = s0 * p.Hkv + hk;
     row_stride = p.Hkv;
   }
+  return true;
+}
+
+template <typename QT, bool RAGGED, int KVF>
+__global__ void __launch_bounds__(32 * kQPerCta) fa_partial_kernel(FaParams p) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x;
+  const int dj = p.D / 32;
+  const size_t row_bytes = (size_t)dj * kv_block_bytes(KVF);
+
+  int qg, L, row0, row_stride;
+  if (!fa_query<RAGGED>(p, warp, qg, L, row0, row_stride)) return;
 
   float qv[kMaxDJ], acc[kMaxDJ];
   const QT* q = static_cast<const QT*>(p.q) + (size_t)qg * p.D;
@@ -129,25 +190,45 @@ __global__ void __launch_bounds__(32 * kQPerCta) fa_partial_kernel(FaParams p) {
     qv[j] = (j < dj) ? load_q(q, (size_t)j * 32 + lane) * p.qscale : 0.0f;
     acc[j] = 0.0f;
   }
+  // Tokens in groups of kTokU. Loads are unconditional (a token past the
+  // chunk re-reads its last row and is masked out of the softmax), so the
+  // group's loads issue back to back instead of one round trip per token;
+  // then kTokU score reductions interleave, one rescale per group, V likewise.
   float m = -INFINITY, l = 0.0f;
   const int t0 = c * p.chunk, t1 = min(L, t0 + p.chunk);
-  for (int t = t0; t < t1; ++t) {
-    const size_t row = (size_t)row0 + (size_t)t * row_stride;
-    const uint8_t* kb = p.k + row * row_bytes;
-    const uint8_t* vb = p.v + row * row_bytes;
-    float s = 0.0f;
+  for (int t = t0; t < t1; t += kTokU) {
+    float sc[kTokU];
 #pragma unroll
-    for (int j = 0; j < kMaxDJ; ++j)
-      if (j < dj) s = fmaf(qv[j], kv_elem<KVF>(kb, j, lane), s);
+    for (int u = 0; u < kTokU; ++u) {
+      const uint8_t* kb = p.k + ((size_t)row0 + (size_t)min(t + u, t1 - 1) * row_stride) * row_bytes;
+      sc[u] = 0.0f;
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    const float mn = fmaxf(m, s);
-    const float corr = exp2f(m - mn);
-    const float pr = exp2f(s - mn);
-    l = fmaf(l, corr, pr);
+      for (int j = 0; j < kMaxDJ; ++j)
+        if (j < dj) sc[u] = fmaf(qv[j], kv_elem<KVF>(kb, j, lane), sc[u]);
+    }
 #pragma unroll
-    for (int j = 0; j < kMaxDJ; ++j)
-      if (j < dj) acc[j] = fmaf(acc[j], corr, pr * kv_elem<KVF>(vb, j, lane));
+    for (int o = 16; o >= 1; o >>= 1)
+#pragma unroll
+      for (int u = 0; u < kTokU; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], o);
+    float mn = m;
+#pragma unroll
+    for (int u = 0; u < kTokU; ++u) {
+      if (t + u >= t1) sc[u] = -INFINITY;
+      mn = fmaxf(mn, sc[u]);
+    }
+    const float corr = exp2f(m - mn);  // 0 on the first group (m = -inf, mn finite)
+    l *= corr;
+#pragma unroll
+    for (int j = 0; j < kMaxDJ; ++j) acc[j] *= corr;
+#pragma unroll
+    for (int u = 0; u < kTokU; ++u) {
+      const float pr = exp2f(sc[u] - mn);  // 0 for a masked token
+      l += pr;
+      const uint8_t* vb = p.v + ((size_t)row0 + (size_t)min(t + u, t1 - 1) * row_stride) * row_bytes;
+#pragma unroll
+      for (int j = 0; j < kMaxDJ; ++j)
+        if (j < dj) acc[j] = fmaf(pr, kv_elem<KVF>(vb, j, lane), acc[j]);
+    }
     m = mn;
   }
   const size_t pi = (size_t)qg * p.NC + c;
@@ -160,27 +241,110 @@ __global__ void __launch_bounds__(32 * kQPerCta) fa_partial_kernel(FaParams p) {
     if (j < dj) p.pacc[pi * p.D + j * 32 + lane] = acc[j];
 }
 
+// The same pass with lanes owning DJ consecutive elements (D = 32 DJ).
+template <typename QT, bool RAGGED, int KVF, int DJ>
+__global__ void __launch_bounds__(32 * kQPerCta, 4) fa_partial_vec_kernel(FaParams p) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x;
+  const size_t row_bytes = (size_t)DJ * kv_block_bytes(KVF);
+
+  int qg, L, row0, row_stride;
+  if (!fa_query<RAGGED>(p, warp, qg, L, row0, row_stride)) return;
+
+  float qv[DJ], acc[DJ];
+  const QT* q = static_cast<const QT*>(p.q) + (size_t)qg * p.D + DJ * lane;
+#pragma unroll
+  for (int i = 0; i < DJ; ++i) {
+    qv[i] = load_q(q, i) * p.qscale;
+    acc[i] = 0.0f;
+  }
+  float m = -INFINITY, l = 0.0f;
+  const int t0 = c * p.chunk, t1 = min(L, t0 + p.chunk);
+  for (int t = t0; t < t1; t += kTokU) {
+    float kx[kTokU][DJ];
+#pragma unroll
+    for (int u = 0; u < kTokU; ++u)
+      kv_lane<KVF, DJ>(p.k + ((size_t)row0 + (size_t)min(t + u, t1 - 1) * row_stride) * row_bytes, lane, kx[u]);
+    float sc[kTokU];
+#pragma unroll
+    for (int u = 0; u < kTokU; ++u) {
+      sc[u] = 0.0f;
+#pragma unroll
+      for (int i = 0; i < DJ; ++i) sc[u] = fmaf(qv[i], kx[u][i], sc[u]);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1)
+#pragma unroll
+      for (int u = 0; u < kTokU; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], o);
+    float mn = m;
+#pragma unroll
+    for (int u = 0; u < kTokU; ++u) {
+      if (t + u >= t1) sc[u] = -INFINITY;
+      mn = fmaxf(mn, sc[u]);
+    }
+    const float corr = exp2f(m - mn);
+    l *= corr;
+#pragma unroll
+    for (int i = 0; i < DJ; ++i) acc[i] *= corr;
+#pragma unroll
+    for (int u = 0; u < kTokU; ++u)
+      kv_lane<KVF, DJ>(p.v + ((size_t)row0 + (size_t)min(t + u, t1 - 1) * row_stride) * row_bytes, lane, kx[u]);
+#pragma unroll
+    for (int u = 0; u < kTokU; ++u) {
+      const float pr = exp2f(sc[u] - mn);  // 0 for a masked token
+      l += pr;
+#pragma unroll
+      for (int i = 0; i < DJ; ++i) acc[i] = fmaf(pr, kx[u][i], acc[i]);
+    }
+    m = mn;
+  }
+  const size_t pi = (size_t)qg * p.NC + c;
+  if (lane == 0) {
+    p.pm[pi] = m;
+    p.pl[pi] = l;
+  }
+  float* pa = p.pacc + pi * p.D + DJ * lane;
+#pragma unroll
+  for (int i = 0; i < DJ; ++i) pa[i] = acc[i];
+}
+
 // One warp per query: merge the NC partial states.
+// One warp per query: merge the NC partial states. The lanes take the
+// partials' maxima and sums 32 at a time; the accumulator pass selects (no
+// branch) so its loads do not wait on the scale loads. A partial with
+// m = -inf (no tokens) weighs 0 whatever its accumulator holds.
 template <typename OT>
 __global__ void __launch_bounds__(128) fa_combine_kernel(FaParams p, int Q) {
   const int qg = blockIdx.x * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (qg >= Q) return;
   const int dj = p.D / 32;
+  const float* pm = p.pm + (size_t)qg * p.NC;
+  const float* pl = p.pl + (size_t)qg * p.NC;
   float M = -INFINITY;
-  for (int c = 0; c < p.NC; ++c) M = fmaxf(M, p.pm[(size_t)qg * p.NC + c]);
+  for (int c = lane; c < p.NC; c += 32) M = fmaxf(M, pm[c]);
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
   float acc[kMaxDJ] = {};
   float L = 0.0f;
   if (M != -INFINITY) {
+    for (int c = lane; c < p.NC; c += 32) {
+      const float mc = pm[c];
+      L += mc == -INFINITY ? 0.0f : pl[c] * exp2f(mc - M);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    const float* pa = p.pacc + (size_t)qg * p.NC * p.D + lane;
+#pragma unroll 4
     for (int c = 0; c < p.NC; ++c) {
-      const size_t pi = (size_t)qg * p.NC + c;
-      const float mc = p.pm[pi];
-      if (mc == -INFINITY) continue;
-      const float w = exp2f(mc - M);
-      L = fmaf(p.pl[pi], w, L);
+      const float mc = pm[c];
+      const float w = mc == -INFINITY ? 0.0f : exp2f(mc - M);
 #pragma unroll
       for (int j = 0; j < kMaxDJ; ++j)
-        if (j < dj) acc[j] = fmaf(p.pacc[pi * p.D + j * 32 + lane], w, acc[j]);
+        if (j < dj) {
+          const float a = pa[(size_t)c * p.D + j * 32];
+          acc[j] = fmaf(w == 0.0f ? 0.0f : a, w, acc[j]);
+        }
     }
   }
   const float inv = L > 0.0f ? 1.0f / L : 0.0f;
@@ -770,19 +934,29 @@ bool encode_kv_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t h
                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Decode kernel family for q8_0 caches in the TMA-able shapes, read once per
+// process from KQ_FA_PATH: the TMA CUDA-core kernel by default; "mma" = the
+// warp-MMA kernel (same results within fp16 rounding of p * d_v; fewer
+// instructions, latency-bound at the same speed); "generic" = the split-KV
+// kernel every other shape uses.
+enum class FaPath { kTma, kMma, kGeneric };
+FaPath fa_path() {
+  static const FaPath p = [] {
+    const char* e = std::getenv("KQ_FA_PATH");
+    if (e && std::string(e) == "mma") return FaPath::kMma;
+    if (e && std::string(e) == "generic") return FaPath::kGeneric;
+    return FaPath::kTma;
+  }();
+  return p;
+}
+
 template <typename QT, bool RAGGED>
 kq_status_t launch_fast(const FastParams& p, const void* k, const void* v, uint64_t rows, int heads, int items,
                         cudaStream_t s) {
   CUtensorMap km, vm;
   if (!encode_kv_map(&km, k, rows, heads) || !encode_kv_map(&vm, v, rows, heads))
     return fail(KQ_ERR_CUDA, "fa: KV tensor map rejected");
-  // CUDA-core kernel by default; KQ_FA_PATH=mma selects the warp-MMA one (same
-  // results within fp16 rounding of p * d_v; fewer instructions, currently
-  // latency-bound at the same speed)
-  static const bool simt = [] {
-    const char* e = std::getenv("KQ_FA_PATH");
-    return !(e && std::string(e) == "mma");
-  }();
+  const bool simt = fa_path() != FaPath::kMma;
   auto kern = simt ? fa_fast_kernel<QT, RAGGED> : fa_mma_kernel<QT, RAGGED>;
   const size_t smem = simt ? kFastSmem : kMmaSmem;
   static unsigned attr_done = 0;
@@ -798,7 +972,7 @@ kq_status_t launch_fast(const FastParams& p, const void* k, const void* v, uint6
 }
 
 bool fast_ok(const void* k, const void* v, int D, int Hkv, int g) {
-  return D == 128 && Hkv % kHpc == 0 && g <= kG && (reinterpret_cast<uintptr_t>(k) & 15) == 0 &&
+  return fa_path() != FaPath::kGeneric && D == 128 && Hkv % kHpc == 0 && g <= kG && (reinterpret_cast<uintptr_t>(k) & 15) == 0 &&
          (reinterpret_cast<uintptr_t>(v) & 15) == 0;
 }
 
@@ -816,14 +990,51 @@ int choose_chunks(long long Q, int D, int max_len, size_t budget, int* chunk) {
 
 constexpr size_t kPartialBudget = 64ull << 20;
 
+// Pass 1 of the generic path: the lane-vector kernel when head_dim is 64, 128
+// or 256 (and fp16 caches are aligned for its vector loads), else the
+// per-element one. `qpc` = queries per CTA (warps; fewer than kQPerCta when
+// there are fewer queries per KV stream).
+template <typename QT, bool RAGGED, int KVF>
+void launch_partial(const FaParams& p, dim3 grid, int qpc, cudaStream_t s) {
+  const int dj = p.D / 32;
+  const int threads = 32 * std::max(1, std::min(qpc, kQPerCta));
+  const uintptr_t al = reinterpret_cast<uintptr_t>(p.k) | reinterpret_cast<uintptr_t>(p.v);
+  auto fits = [&](int DJ) { return dj == DJ && (KVF != KQ_KV_F16 || al % (2 * DJ) == 0); };
+  if (fits(8))
+    fa_partial_vec_kernel<QT, RAGGED, KVF, 8><<<grid, threads, 0, s>>>(p);
+  else if (fits(4))
+    fa_partial_vec_kernel<QT, RAGGED, KVF, 4><<<grid, threads, 0, s>>>(p);
+  else if (fits(2))
+    fa_partial_vec_kernel<QT, RAGGED, KVF, 2><<<grid, threads, 0, s>>>(p);
+  else
+    fa_partial_kernel<QT, RAGGED, KVF><<<grid, threads, 0, s>>>(p);
+}
+
+// Chunks for the generic kernel: about one resident wave of (query, chunk)
+// warps (16 per SM at its ~100-128 registers per thread), at least 4 token
+// groups per chunk, partials within `budget`.
+int choose_chunks_generic(long long Q, int D, int max_len, size_t budget, int* chunk) {
+  const long long target = (long long)sm_count() * 16;
+  long long nc = std::max<long long>(1, (target + Q - 1) / Q);
+  nc = std::min<long long>(nc, std::max(1, max_len / (4 * kTokU)));
+  const long long per = (long long)Q * (D + 2) * 4;
+  nc = std::min<long long>(nc, std::max<long long>(1, (long long)budget / std::max<long long>(per, 1)));
+  nc = std::min<long long>(nc, 65535);
+  *chunk = (int)std::max<long long>(1, (max_len + nc - 1) / nc);
+  return std::max(1, (max_len + *chunk - 1) / *chunk);
+}
+
 }  // namespace
 
 kq_status_t launch_fa_mha(int kvf, const float* q, const void* k, const void* v, float* out, int B, int S, int H,
                           int D, cudaStream_t s) {
   const long long Q = (long long)B * H;
   if (Q == 0) return KQ_OK;
+  const bool fast = kvf == KQ_KV_Q8_0 && fast_ok(k, v, D, H, 1) && S > 0 &&
+                    (long long)((B + kG - 1) / kG) * (H / kHpc) <= 65535;
   int chunk = 0;
-  const int NC = choose_chunks(Q, D, std::max(S, 1), kPartialBudget, &chunk);
+  const int NC = fast ? choose_chunks(Q, D, std::max(S, 1), kPartialBudget, &chunk)
+                      : choose_chunks_generic(Q, D, std::max(S, 1), kPartialBudget, &chunk);
   const size_t bytes = (size_t)Q * NC * (D + 2) * sizeof(float);
   float* ws = static_cast<float*>(workspace(WS_FA, bytes));
   if (!ws) return KQ_ERR_NOMEM;
@@ -832,22 +1043,20 @@ kq_status_t launch_fa_mha(int kvf, const float* q, const void* k, const void* v,
   p.pm = ws; p.pl = ws + Q * NC; p.pacc = ws + 2 * Q * NC; p.out = out;
   p.B = B; p.H = H; p.Hkv = H; p.D = D; p.S = S; p.NC = NC; p.chunk = chunk;
   p.qscale = (float)(1.0 / std::sqrt((double)D) * 1.4426950408889634);
-  if (kvf == KQ_KV_Q8_0 && fast_ok(k, v, D, H, 1) && S > 0) {
+  if (fast) {
     FastParams f{q, nullptr, p.pm, p.pl, p.pacc, B, H, H, S, NC, chunk, H / kHpc, p.qscale};
-    const long long items = (long long)((B + kG - 1) / kG) * (H / kHpc);
-    if (items <= 65535) {
-      kq_status_t st = launch_fast<float, false>(f, k, v, (uint64_t)S, H, (int)items, s);
-      if (st) return st;
-      fa_combine_kernel<float><<<(unsigned)((Q + 3) / 4), 128, 0, s>>>(p, (int)Q);
-      return check_launch("fa_combine(mha)");
-    }
+    const int items = ((B + kG - 1) / kG) * (H / kHpc);
+    kq_status_t st = launch_fast<float, false>(f, k, v, (uint64_t)S, H, items, s);
+    if (st) return st;
+    fa_combine_kernel<float><<<(unsigned)((Q + 3) / 4), 128, 0, s>>>(p, (int)Q);
+    return check_launch("fa_combine(mha)");
   }
   dim3 grid(NC, H, (B + kQPerCta - 1) / kQPerCta);
   if (grid.z > 65535 || grid.y > 65535) return fail(KQ_ERR_UNSUPPORTED, "fa_mha: grid too large");
   switch (kvf) {
-    case KQ_KV_Q8_0: fa_partial_kernel<float, false, KQ_KV_Q8_0><<<grid, 32 * kQPerCta, 0, s>>>(p); break;
-    case KQ_KV_Q4_0: fa_partial_kernel<float, false, KQ_KV_Q4_0><<<grid, 32 * kQPerCta, 0, s>>>(p); break;
-    case KQ_KV_F16: fa_partial_kernel<float, false, KQ_KV_F16><<<grid, 32 * kQPerCta, 0, s>>>(p); break;
+    case KQ_KV_Q8_0: launch_partial<float, false, KQ_KV_Q8_0>(p, grid, B, s); break;
+    case KQ_KV_Q4_0: launch_partial<float, false, KQ_KV_Q4_0>(p, grid, B, s); break;
+    case KQ_KV_F16: launch_partial<float, false, KQ_KV_F16>(p, grid, B, s); break;
     default: return fail(KQ_ERR_INVALID, "fa_mha: unknown KV format %d", kvf);
   }
   kq_status_t st = check_launch("fa_partial(mha)");
@@ -860,8 +1069,11 @@ kq_status_t launch_fa_ragged(const void* q, const void* k, const void* v, const 
                              int D, int max_seqlen, int total_rows, float scale, void* out, cudaStream_t s) {
   const long long Q = (long long)B * Hq;
   if (Q == 0) return KQ_OK;
+  const int g = Hq / Hkv;
+  const bool fast = fast_ok(k, v, D, Hkv, g) && total_rows > 0 && (long long)B * (Hkv / kHpc) <= 65535;
   int chunk = 0;
-  const int NC = choose_chunks(Q, D, std::max(max_seqlen, 1), kPartialBudget, &chunk);
+  const int NC = fast ? choose_chunks(Q, D, std::max(max_seqlen, 1), kPartialBudget, &chunk)
+                      : choose_chunks_generic(Q, D, std::max(max_seqlen, 1), kPartialBudget, &chunk);
   const size_t bytes = (size_t)Q * NC * (D + 2) * sizeof(float);
   float* ws = static_cast<float*>(workspace(WS_FA, bytes));
   if (!ws) return KQ_ERR_NOMEM;
@@ -870,8 +1082,7 @@ kq_status_t launch_fa_ragged(const void* q, const void* k, const void* v, const 
   p.pm = ws; p.pl = ws + Q * NC; p.pacc = ws + 2 * Q * NC; p.out = out;
   p.B = B; p.H = Hq; p.Hkv = Hkv; p.D = D; p.S = max_seqlen; p.NC = NC; p.chunk = chunk;
   p.qscale = (float)((double)scale * 1.4426950408889634);
-  const int g = Hq / Hkv;
-  if (fast_ok(k, v, D, Hkv, g) && total_rows > 0 && (long long)B * (Hkv / kHpc) <= 65535) {
+  if (fast) {
     // total_rows bounds the TMA map: no tile reads past the cache allocation
     FastParams f{q, cu, p.pm, p.pl, p.pacc, B, Hq, Hkv, max_seqlen, NC, chunk, Hkv / kHpc, p.qscale};
     kq_status_t st = launch_fast<__half, true>(f, k, v, (uint64_t)total_rows, Hkv, B * (Hkv / kHpc), s);
@@ -881,7 +1092,7 @@ kq_status_t launch_fa_ragged(const void* q, const void* k, const void* v, const 
   }
   dim3 grid(NC, (unsigned)((long long)B * Hkv), (g + kQPerCta - 1) / kQPerCta);
   if (grid.y > 65535) return fail(KQ_ERR_UNSUPPORTED, "fa_ragged: B*Hkv too large");
-  fa_partial_kernel<__half, true, KQ_KV_Q8_0><<<grid, 32 * kQPerCta, 0, s>>>(p);
+  launch_partial<__half, true, KQ_KV_Q8_0>(p, grid, g, s);
   kq_status_t st = check_launch("fa_partial(ragged)");
   if (st) return st;
   fa_combine_kernel<__half><<<(unsigned)((Q + 3) / 4), 128, 0, s>>>(p, (int)Q);

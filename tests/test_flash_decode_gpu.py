@@ -32,7 +32,7 @@ def test_golden_fixture(cuda):
 
 
 @pytest.mark.parametrize("B,S,H,D", [(1, 512, 32, 128), (8, 1000, 4, 128), (3, 4096, 2, 64), (2, 1, 3, 32),
-                                     (16, 300, 2, 256),
+                                     (16, 300, 2, 256), (2, 100, 3, 96), (6, 2000, 5, 160),
                                      # TMA fast path (D = 128, heads in groups of 8): partial tiles,
                                      # partial query groups, one-token cache
                                      (5, 77, 8, 128), (12, 1000, 16, 128), (3, 1, 8, 128), (4, 33, 32, 128)])
@@ -84,7 +84,7 @@ def _cache(fmt, x, D):
 
 @pytest.mark.parametrize("fmt", ["q4_0", "f16"])
 @pytest.mark.parametrize("B,S,H,D", [(1, 512, 32, 128), (8, 1000, 4, 128), (3, 4096, 2, 64), (2, 1, 3, 32),
-                                     (16, 300, 2, 256), (5, 77, 28, 128)])
+                                     (16, 300, 2, 256), (5, 77, 28, 128), (2, 100, 3, 96), (1, 8192, 28, 128)])
 def test_mha_parity_kv_formats(cuda, fmt, B, S, H, D):
     import kq
     rng = np.random.default_rng(B * S + H + len(fmt))
@@ -92,6 +92,26 @@ def test_mha_parity_kv_formats(cuda, fmt, B, S, H, D):
     k = _cache(fmt, rng.standard_normal((S, H, D)).astype(np.float32), D)
     v = _cache(fmt, rng.standard_normal((S, H, D)).astype(np.float32), D)
     got = kq.flash_attn(_t(q, cuda), _t(k, cuda), _t(v, cuda), B, S, H, D, fmt).cpu().numpy()
+    ok, msg = Q.check_close(got, Q.flash_decode_mha(q, k, v, S, H, D, fmt))
+    assert ok, msg
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0", "f16"])
+def test_mha_unaligned_caches(cuda, fmt):
+    """Caches that start 2 bytes past an aligned address (the ABI asks for
+    2-byte alignment only): the fp16 vector loads give way to element loads."""
+    import kq
+    rng = np.random.default_rng(3)
+    B, S, H, D = 3, 700, 4, 128
+    q = rng.standard_normal((B, H, D)).astype(np.float32)
+    k = _cache(fmt, rng.standard_normal((S, H, D)).astype(np.float32), D)
+    v = _cache(fmt, rng.standard_normal((S, H, D)).astype(np.float32), D)
+    nb = k.nbytes
+    kbuf = torch.zeros(nb + 16, dtype=torch.uint8, device=cuda)
+    vbuf = torch.zeros(nb + 16, dtype=torch.uint8, device=cuda)
+    kbuf[2:2 + nb] = _t(np.frombuffer(k.tobytes(), dtype=np.uint8), cuda)
+    vbuf[2:2 + nb] = _t(np.frombuffer(v.tobytes(), dtype=np.uint8), cuda)
+    got = kq.flash_attn(_t(q, cuda), kbuf[2:2 + nb], vbuf[2:2 + nb], B, S, H, D, fmt).cpu().numpy()
     ok, msg = Q.check_close(got, Q.flash_decode_mha(q, k, v, S, H, D, fmt))
     assert ok, msg
 
