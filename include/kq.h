@@ -121,6 +121,13 @@ void kq_flash_attn_q4_0(const float* query, const void* key_cache, const void* v
 void kq_flash_attn_f16(const float* query, const void* key_cache, const void* value_cache, float* output,
                        int batch_size, int seq_len, int num_heads, int head_dim);
 
+/* rms_norm: output[b, :] = input[b, :] / sqrt(mean(input[b, :]^2) + 1e-6) * weight
+ * (fp32; RMSNormHandler op_test_handler.py:641-690, every rms_norm definition
+ * has epsilon 1e-6 and the bound signature carries none).
+ * Replaces `extern "C" void rms_norm_kernel(const float* input, const float* weight,
+ * float* output, int batch_size, int hidden_size)` bound by unified_test_runner.py:330-350. */
+void kq_rms_norm(const float* input, const float* weight, float* output, int batch_size, int hidden_size);
+
 /* ---- 2. Status-returning entry points ------------------------------------ */
 
 /* fp32 x[M, K] -> q8_1 blocks y[M, K/32] (36 B each), sum_mode KQ_ACT_SUM_X
@@ -139,6 +146,25 @@ kq_status_t kq_quantize_rows(int wtype, const float* x, void* y, int64_t rows, i
  * gemm_ref.py:274-331, vec_dot_q8_0_q8_1 gemm_reference.h:311-336). */
 kq_status_t kq_mul_mat_q(int wtype, const void* w, const void* a_q8_1, float* out, int M, int N, int K,
                          kq_stream_t stream);
+
+/* RMSNorm with an explicit epsilon: out[M, K] from x[M, K] and weight[K]
+ * (the status form of kq_rms_norm). */
+kq_status_t kq_rms_norm_f32(const float* x, const float* weight, float* out, int M, int K, float eps,
+                            kq_stream_t stream);
+
+/* RMSNorm fused into quantize_q8_1: y = q8_1 blocks [M, K/32] (36 B) of
+ * x[m] / sqrt(mean(x[m]^2) + eps) * weight, sum_mode KQ_ACT_SUM_X or
+ * KQ_ACT_SUM_DQ. The normalised fp32 row never goes to memory. K % 32 == 0;
+ * x and weight 16-byte aligned. No reference counterpart: the reference runs
+ * rms_norm and quantize_q8_1 as separate operators. */
+kq_status_t kq_rms_norm_quantize_q8_1(const float* x, const float* weight, void* y, int M, int K, float eps,
+                                      int sum_mode, kq_stream_t stream);
+
+/* kq_gemm_f32act on RMSNorm(x): out[M, N] = q8_1(x / rms(x) * norm_weight) x W^T
+ * in one call (the normalised activation is quantised as it is produced).
+ * No reference counterpart: rms_norm followed by the quant_gemm operator. */
+kq_status_t kq_gemm_f32act_rmsnorm(int wtype, const void* w, const float* x, const float* norm_weight, float eps,
+                                   float* out, int M, int N, int K, int act_mode, kq_stream_t stream);
 
 /* Weights x fp32 activations quantised on the fly (the harness operator).
  * act_mode is one of KQ_ACT_*; the status form of the void entries above. */

@@ -263,6 +263,56 @@ kq_status_t kq_gemm_f32act(int wtype, const void* w, const float* x, float* out,
   return dispatch_gemm(wtype, w, act, out, M, N, K, s, true);
 }
 
+kq_status_t kq_rms_norm_f32(const float* x, const float* weight, float* out, int M, int K, float eps,
+                            kq_stream_t stream) {
+  if (M < 0 || K < 0) return fail(KQ_ERR_INVALID, "rms_norm: negative dimension (M=%d K=%d)", M, K);
+  if ((long long)M * K == 0) return KQ_OK;
+  if (!x || !weight || !out) return fail(KQ_ERR_INVALID, "rms_norm: null pointer");
+  if (!(eps >= 0.0f)) return fail(KQ_ERR_INVALID, "rms_norm: eps must be >= 0");
+  return launch_rms_norm(x, weight, out, M, K, eps, static_cast<cudaStream_t>(stream));
+}
+
+namespace {
+kq_status_t check_norm_quant_args(const float* x, const float* weight, int M, int K, float eps) {
+  if (M < 0 || K < 0 || K % 32) return fail(KQ_ERR_INVALID, "rms_norm_quantize: bad shape M=%d K=%d (K %% 32 == 0)", M, K);
+  if ((long long)M * K > 0 && (!x || !weight)) return fail(KQ_ERR_INVALID, "rms_norm_quantize: null pointer");
+  if (!aligned(x, 16) || !aligned(weight, 16))
+    return fail(KQ_ERR_INVALID, "rms_norm_quantize: x and weight must be 16-byte aligned");
+  if (!(eps >= 0.0f)) return fail(KQ_ERR_INVALID, "rms_norm_quantize: eps must be >= 0");
+  return KQ_OK;
+}
+}  // namespace
+
+kq_status_t kq_rms_norm_quantize_q8_1(const float* x, const float* weight, void* y, int M, int K, float eps,
+                                      int sum_mode, kq_stream_t stream) {
+  kq_status_t st = check_norm_quant_args(x, weight, M, K, eps);
+  if (st) return st;
+  if (sum_mode != KQ_ACT_SUM_X && sum_mode != KQ_ACT_SUM_DQ)
+    return fail(KQ_ERR_INVALID, "q8_1 bytes hold fp16 d and s: sum_mode must be KQ_ACT_SUM_X or KQ_ACT_SUM_DQ");
+  if ((long long)M * K == 0) return KQ_OK;
+  if (!y) return fail(KQ_ERR_INVALID, "rms_norm_quantize: null output");
+  return launch_rms_norm_quantize(x, weight, eps, Act8{nullptr, nullptr}, y, M, K, sum_mode,
+                                  static_cast<cudaStream_t>(stream));
+}
+
+kq_status_t kq_gemm_f32act_rmsnorm(int wtype, const void* w, const float* x, const float* norm_weight, float eps,
+                                   float* out, int M, int N, int K, int act_mode, kq_stream_t stream) {
+  kq_status_t st = check_gemm_args(wtype, w, x, out, M, N, K);
+  if (st) return st;
+  if (act_mode < KQ_ACT_SUM_X || act_mode > KQ_ACT_F32) return fail(KQ_ERR_INVALID, "unknown activation mode %d", act_mode);
+  st = check_norm_quant_args(x, norm_weight, M, K, eps);
+  if (st) return st;
+  if ((long long)M * N == 0) return KQ_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (K == 0) return zero_output(out, M, N, s);
+  void* ws = workspace(WS_ACT, act8_bytes(M, K));
+  if (!ws) return KQ_ERR_NOMEM;
+  Act8 act = act8_view(ws, M, K);
+  st = launch_rms_norm_quantize(x, norm_weight, eps, act, nullptr, M, K, act_mode, s);
+  if (st) return st;
+  return dispatch_gemm(wtype, w, act, out, M, N, K, s, true);
+}
+
 kq_status_t kq_peer_alloc(size_t bytes, void** ptr, void* handle64) {
   static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
   if (!ptr || !handle64 || bytes == 0) return fail(KQ_ERR_INVALID, "peer_alloc: bad arguments");
@@ -448,6 +498,11 @@ void kq_flash_attn_q8_0(const float* query, const void* key_cache, const void* v
                         int batch_size, int seq_len, int num_heads, int head_dim) {
   g_last_error.clear();  // the harness shim reports a non-empty message as a failure
   kq_fa_decode_q8_0_mha(query, key_cache, value_cache, output, batch_size, seq_len, num_heads, head_dim, nullptr);
+}
+
+void kq_rms_norm(const float* input, const float* weight, float* output, int batch_size, int hidden_size) {
+  g_last_error.clear();
+  kq_rms_norm_f32(input, weight, output, batch_size, hidden_size, 1e-6f, nullptr);
 }
 
 void kq_flash_attn_q4_0(const float* query, const void* key_cache, const void* value_cache, float* output,

@@ -364,7 +364,12 @@ constexpr int kStages = 2;
 constexpr int kRowBytes = kHpc * 136;  // one token row of 8 heads x (4 q8_0 blocks of 34 B)
 constexpr int kTile = kSt * kRowBytes;
 constexpr int kFastThreads = (kHpc + 1) * 32;
-constexpr size_t kFastSmem = 2 * kStages * kTile + kHpc * kG * 128 * 4 + kHpc * kSt * kG * 4 + 4 * kStages * 8 + 128;
+// The CUDA-core kernel streams 16-token tiles so two CTAs (18 warps) fit on an
+// SM; the warp-MMA kernel keeps 32-token tiles.
+constexpr int kStF = 16;
+constexpr int kTileF = kStF * kRowBytes;
+constexpr int kGrpF = kStF / 8;  // 8-token score groups per tile
+constexpr size_t kFastSmem = 2 * kStages * kTileF + kHpc * kG * 128 * 4 + kHpc * kStF * kG * 4 + 4 * kStages * 8 + 128;
 
 struct FastParams {
   const void* q;
@@ -429,15 +434,15 @@ __device__ __forceinline__ uint32_t row_codes(const uint8_t* row, int w, int lan
 }
 
 template <typename QT, bool RAGGED>
-__global__ void __launch_bounds__(kFastThreads, 1)
+__global__ void __launch_bounds__(kFastThreads, 2)
     fa_fast_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, FastParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~(uintptr_t)127);
   uint8_t* ktile = smem;
-  uint8_t* vtile = smem + kStages * kTile;
-  float* qs = reinterpret_cast<float*>(smem + 2 * kStages * kTile);      // [8][4][128]
-  float* ps = qs + kHpc * kG * 128;                                       // [8][32 tokens][4]
-  uint64_t* full = reinterpret_cast<uint64_t*>(ps + kHpc * kSt * kG);
+  uint8_t* vtile = smem + kStages * kTileF;
+  float* qs = reinterpret_cast<float*>(smem + 2 * kStages * kTileF);      // [8][4][128]
+  float* ps = qs + kHpc * kG * 128;                                       // [8][kStF tokens][4]
+  uint64_t* full = reinterpret_cast<uint64_t*>(ps + kHpc * kStF * kG);
   uint64_t* empty = full + kStages;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -456,7 +461,7 @@ __global__ void __launch_bounds__(kFastThreads, 1)
     nq = min(kG, p.B - grp * kG);
   }
   const int t0 = c * p.chunk, t1 = min(L, t0 + p.chunk);
-  const int nsub = t1 > t0 ? (t1 - t0 + kSt - 1) / kSt : 0;
+  const int nsub = t1 > t0 ? (t1 - t0 + kStF - 1) / kStF : 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -487,10 +492,10 @@ __global__ void __launch_bounds__(kFastThreads, 1)
       for (int i = 0; i < nsub; ++i) {
         const int s = i % kStages;
         if (i >= kStages) mbar_wait_or_poison(&empty[s], ((i / kStages) - 1) & 1, nullptr, 0, dead);
-        mbar_arrive_expect_tx(&full[s], 2 * kTile);
-        const int y = row0 + t0 + i * kSt;
-        tma_load_2d_u64(ktile + s * kTile, &kmap, hg * (kRowBytes / 8), y, &full[s]);
-        tma_load_2d_u64(vtile + s * kTile, &vmap, hg * (kRowBytes / 8), y, &full[s]);
+        mbar_arrive_expect_tx(&full[s], 2 * kTileF);
+        const int y = row0 + t0 + i * kStF;
+        tma_load_2d_u64(ktile + s * kTileF, &kmap, hg * (kRowBytes / 8), y, &full[s]);
+        tma_load_2d_u64(vtile + s * kTileF, &vmap, hg * (kRowBytes / 8), y, &full[s]);
       }
       // drain: every issued tile must be consumed before the CTA exits
       for (int i = max(0, nsub - kStages); i < nsub; ++i)
@@ -513,19 +518,19 @@ __global__ void __launch_bounds__(kFastThreads, 1)
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[j][i] = 0.0f;
   float m_run = -INFINITY, l_run = 0.0f;  // for query (lane & 3)
-  float* pw = ps + w * kSt * kG;
+  float* pw = ps + w * kStF * kG;
 
   for (int it = 0; it < nsub; ++it) {
     const int s = it % kStages;
     mbar_wait_or_poison(&full[s], (it / kStages) & 1, nullptr, 0, dead);
-    const uint8_t* kt = ktile + s * kTile;
-    const uint8_t* vt = vtile + s * kTile;
-    const int tb = t0 + it * kSt;  // first token of the tile
+    const uint8_t* kt = ktile + s * kTileF;
+    const uint8_t* vt = vtile + s * kTileF;
+    const int tb = t0 + it * kStF;  // first token of the tile
 
-    // ---- scores: 4 groups of 8 tokens x 4 queries ----
-    float sc[4];
+    // ---- scores: kGrpF groups of 8 tokens x 4 queries ----
+    float sc[kGrpF];
 #pragma unroll 1
-    for (int g = 0; g < 4; ++g) {
+    for (int g = 0; g < kGrpF; ++g) {
       float part[32];
 #pragma unroll
       for (int tt = 0; tt < 8; ++tt) {
@@ -542,14 +547,16 @@ __global__ void __launch_bounds__(kFastThreads, 1)
       sc[g] = (tok < t1 && (lane & 3) < nq) ? sv : -INFINITY;
     }
     // ---- online softmax for query (lane & 3) ----
-    float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+    float mx = sc[0];
+#pragma unroll
+    for (int g = 1; g < kGrpF; ++g) mx = fmaxf(mx, sc[g]);
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
     const float m_new = fmaxf(m_run, mx);
-    float pr[4], ls = 0.0f;
+    float pr[kGrpF], ls = 0.0f;
 #pragma unroll
-    for (int g = 0; g < 4; ++g) {
+    for (int g = 0; g < kGrpF; ++g) {
       pr[g] = (m_new == -INFINITY) ? 0.0f : exp2f(sc[g] - m_new);
       ls += pr[g];
     }
@@ -560,7 +567,7 @@ __global__ void __launch_bounds__(kFastThreads, 1)
     l_run = fmaf(l_run, corr, ls);
     m_run = m_new;
 #pragma unroll
-    for (int g = 0; g < 4; ++g) pw[(8 * g + (lane >> 2)) * kG + (lane & 3)] = pr[g];
+    for (int g = 0; g < kGrpF; ++g) pw[(8 * g + (lane >> 2)) * kG + (lane & 3)] = pr[g];
     __syncwarp();
     // ---- rescale and accumulate P . V ----
 #pragma unroll
@@ -570,7 +577,7 @@ __global__ void __launch_bounds__(kFastThreads, 1)
       for (int i = 0; i < 4; ++i) acc[j][i] *= cj;
     }
 #pragma unroll 4
-    for (int tt = 0; tt < kSt; ++tt) {
+    for (int tt = 0; tt < kStF; ++tt) {
       float d;
       const uint32_t cw = row_codes(vt + tt * kRowBytes, w, lane, d);
       float vf[4];
@@ -923,11 +930,12 @@ __global__ void __launch_bounds__(kFastThreads, 1)
   }
 }
 
-bool encode_kv_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t heads) {
-  // [rows][heads * 136 bytes] as uint64 elements; boxes of 32 rows x 8 heads
+bool encode_kv_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t heads, uint32_t box_rows) {
+  // [rows][heads * 136 bytes] as uint64 elements; boxes of box_rows rows x 8
+  // heads (the kernel's tile: its expected transaction bytes match the box)
   cuuint64_t dims[2] = {heads * 17, rows};
   cuuint64_t strides[1] = {heads * 136};
-  cuuint32_t box[2] = {kRowBytes / 8, kSt};
+  cuuint32_t box[2] = {kRowBytes / 8, box_rows};
   cuuint32_t estr[2] = {1, 1};
   return encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(base), dims, strides, box,
                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -953,10 +961,11 @@ FaPath fa_path() {
 template <typename QT, bool RAGGED>
 kq_status_t launch_fast(const FastParams& p, const void* k, const void* v, uint64_t rows, int heads, int items,
                         cudaStream_t s) {
-  CUtensorMap km, vm;
-  if (!encode_kv_map(&km, k, rows, heads) || !encode_kv_map(&vm, v, rows, heads))
-    return fail(KQ_ERR_CUDA, "fa: KV tensor map rejected");
   const bool simt = fa_path() != FaPath::kMma;
+  const uint32_t box_rows = simt ? kStF : kSt;
+  CUtensorMap km, vm;
+  if (!encode_kv_map(&km, k, rows, heads, box_rows) || !encode_kv_map(&vm, v, rows, heads, box_rows))
+    return fail(KQ_ERR_CUDA, "fa: KV tensor map rejected");
   auto kern = simt ? fa_fast_kernel<QT, RAGGED> : fa_mma_kernel<QT, RAGGED>;
   const size_t smem = simt ? kFastSmem : kMmaSmem;
   static unsigned attr_done = 0;
@@ -972,8 +981,8 @@ kq_status_t launch_fast(const FastParams& p, const void* k, const void* v, uint6
 }
 
 bool fast_ok(const void* k, const void* v, int D, int Hkv, int g) {
-  return fa_path() != FaPath::kGeneric && D == 128 && Hkv % kHpc == 0 && g <= kG && (reinterpret_cast<uintptr_t>(k) & 15) == 0 &&
-         (reinterpret_cast<uintptr_t>(v) & 15) == 0;
+  return fa_path() != FaPath::kGeneric && D == 128 && Hkv % kHpc == 0 && g <= kG &&
+         (reinterpret_cast<uintptr_t>(k) & 15) == 0 && (reinterpret_cast<uintptr_t>(v) & 15) == 0;
 }
 
 // Choose the number of chunks so the partial buffers stay within `budget`.

@@ -84,6 +84,12 @@ kq_status_t launch_quantize_act(const float* x, Act8 act, int M, int K, int mode
 kq_status_t launch_quantize_q8_1_bytes(const float* x, void* y, int64_t M, int64_t K, int mode, cudaStream_t s);
 kq_status_t launch_quantize_rows(int wtype, const float* x, void* y, int64_t rows, int64_t K, cudaStream_t s);
 kq_status_t launch_q8_1_to_act(const void* a_q8_1, Act8 act, int M, int K, cudaStream_t s);
+// out = x / sqrt(mean(x^2) + eps) * w per row of x fp32 [M, K]
+kq_status_t launch_rms_norm(const float* x, const float* w, float* out, int M, int K, float eps, cudaStream_t s);
+// RMSNorm then q8_1: into the staging `act` (q81 == nullptr) or as q8_1 bytes
+// q81 [M, K/32, 36]. K % 32 == 0; x, w 16-byte aligned.
+kq_status_t launch_rms_norm_quantize(const float* x, const float* w, float eps, Act8 act, void* q81, int M, int K,
+                                     int mode, cudaStream_t s);
 // staging row r <- quantise(x row rowmap[r] / div)
 kq_status_t launch_quantize_act_gather(const float* x, const int* rowmap, int div, Act8 act, int M, int K, int mode,
                                        cudaStream_t s);

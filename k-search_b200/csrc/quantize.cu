@@ -10,6 +10,10 @@
 // The reference's GPU kernel (include/quantize.h:302-340) uses one thread per
 // block, x * (1/d) and a serial sum; this one uses 8 lanes per block with
 // 16-byte loads and reproduces the Python oracle bit for bit instead.
+//
+// Also RMSNorm (the harness's rms_norm operator, op_test_handler.py:641-690:
+// out = x / sqrt(mean(x^2) + eps) * weight in fp32), alone and fused in front
+// of the quantiser so a normalised activation row goes straight to q8_1.
 #include <algorithm>
 
 #include "kq_internal.h"
@@ -226,6 +230,109 @@ int grid_for(long long total_blocks) {
   return (int)std::max(1LL, std::min(ctas, cap));
 }
 
+// ---- RMSNorm -------------------------------------------------------------
+// One CTA per row. rms = sqrt(sum(x^2) / K + eps) (fp32, correctly rounded
+// divide and square root; the sum in this kernel's order), then x / rms * w
+// with the harness's two roundings.
+constexpr int kNormThreads = 256;
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const unsigned full = 0xffffffffu;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(full, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    v = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.0f;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(full, v, o);
+    if (lane == 0) red[32] = v;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+// VEC: K % 4 == 0 and 16-byte aligned rows (float4 loads).
+template <bool VEC>
+__device__ __forceinline__ float row_rms(const float* __restrict__ xr, int K, float eps, float* red) {
+  float ss = 0.0f;
+  if (VEC) {
+    const float4* x4 = reinterpret_cast<const float4*>(xr);
+    for (int i = threadIdx.x; i < K / 4; i += blockDim.x) {
+      const float4 v = __ldg(x4 + i);
+      ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+    }
+  } else {
+    for (int i = threadIdx.x; i < K; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+  }
+  ss = block_sum(ss, red);
+  return __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), eps));
+}
+
+__device__ __forceinline__ float norm1(float x, float rms, float w) { return __fmul_rn(__fdiv_rn(x, rms), w); }
+__device__ __forceinline__ float4 norm4(float4 v, float rms, float4 w) {
+  return make_float4(norm1(v.x, rms, w.x), norm1(v.y, rms, w.y), norm1(v.z, rms, w.z), norm1(v.w, rms, w.w));
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                                float* __restrict__ out, int K, float eps) {
+  __shared__ float red[33];
+  const size_t off = (size_t)blockIdx.x * K;
+  const float rms = row_rms<VEC>(x + off, K, eps, red);
+  if (VEC) {
+    const float4* x4 = reinterpret_cast<const float4*>(x + off);
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    float4* o4 = reinterpret_cast<float4*>(out + off);
+    for (int i = threadIdx.x; i < K / 4; i += blockDim.x) o4[i] = norm4(__ldg(x4 + i), rms, __ldg(w4 + i));
+  } else {
+    for (int i = threadIdx.x; i < K; i += blockDim.x) out[off + i] = norm1(x[off + i], rms, w[i]);
+  }
+}
+
+// RMSNorm then q8_1 of the normalised row: staging layout (BYTES = false) or
+// q8_1 bytes. K % 32 == 0, x and w 16-byte aligned. Each warp quantises 4
+// blocks per step with the same per-block arithmetic as quantize_kernel.
+template <int MODE, bool BYTES>
+__global__ void __launch_bounds__(kNormThreads) rms_norm_quantize_kernel(const float* __restrict__ x,
+                                                                         const float* __restrict__ w, float eps, int K,
+                                                                         int8_t* __restrict__ qs,
+                                                                         float2* __restrict__ ds,
+                                                                         uint8_t* __restrict__ q81) {
+  __shared__ float red[33];
+  const size_t row = blockIdx.x;
+  const float* xr = x + row * K;
+  const float rms = row_rms<true>(xr, K, eps, red);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int grp = lane >> 3, sub = lane & 7;
+  const int nb = K / 32;
+  const int nwarps = blockDim.x >> 5;
+  const float4* x4 = reinterpret_cast<const float4*>(xr);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  for (int b0 = warp * 4; b0 < nb; b0 += nwarps * 4) {
+    const int b = b0 + grp;
+    const bool valid = b < nb;
+    const int src = valid ? b : b0;  // keep all lanes in the shuffles
+    const float4 v = norm4(__ldg(x4 + src * 8 + sub), rms, __ldg(w4 + src * 8 + sub));
+    const BlockQ r = quantize_octet<MODE>(v, lane);
+    if (!valid) continue;
+    const long long blk = (long long)row * nb + b;
+    if (BYTES) {
+      uint8_t* dst = q81 + blk * 36;
+      reinterpret_cast<uint32_t*>(dst + 4)[sub] = r.qs;
+      if (sub == 0) *reinterpret_cast<uint32_t*>(dst) = float_to_half_bits(r.d) | (float_to_half_bits(r.s) << 16);
+    } else {
+      reinterpret_cast<uint32_t*>(qs + blk * 32)[sub] = r.qs;
+      if (sub == 0)
+        ds[blk] = MODE == KQ_ACT_F32
+                      ? make_float2(r.d, r.s)
+                      : make_float2(__half2float(__float2half_rn(r.d)), __half2float(__float2half_rn(r.s)));
+    }
+  }
+  pdl_launch_dependents();
+}
+
 }  // namespace
 
 kq_status_t launch_quantize_act(const float* x, Act8 act, int M, int K, int mode, cudaStream_t s) {
@@ -319,6 +426,45 @@ kq_status_t launch_q8_1_to_act(const void* a_q8_1, Act8 act, int M, int K, cudaS
   const int grid = (int)((nb + 255) / 256);
   q8_1_to_act_kernel<<<grid, 256, 0, s>>>(static_cast<const uint8_t*>(a_q8_1), act.qs, act.ds, nb);
   return check_launch("q8_1_to_act");
+}
+
+kq_status_t launch_rms_norm(const float* x, const float* w, float* out, int M, int K, float eps, cudaStream_t s) {
+  if ((long long)M * K == 0) return KQ_OK;
+  const bool vec = K % 4 == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
+                                   reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+  if (vec)
+    rms_norm_kernel<true><<<M, kNormThreads, 0, s>>>(x, w, out, K, eps);
+  else
+    rms_norm_kernel<false><<<M, kNormThreads, 0, s>>>(x, w, out, K, eps);
+  return check_launch("rms_norm");
+}
+
+kq_status_t launch_rms_norm_quantize(const float* x, const float* w, float eps, Act8 act, void* q81, int M, int K,
+                                     int mode, cudaStream_t s) {
+  if ((long long)M * K == 0) return KQ_OK;
+  uint8_t* y = static_cast<uint8_t*>(q81);
+  const bool bytes = y != nullptr;
+  switch (mode) {
+    case KQ_ACT_SUM_X:
+      if (bytes)
+        rms_norm_quantize_kernel<KQ_ACT_SUM_X, true><<<M, kNormThreads, 0, s>>>(x, w, eps, K, nullptr, nullptr, y);
+      else
+        rms_norm_quantize_kernel<KQ_ACT_SUM_X, false><<<M, kNormThreads, 0, s>>>(x, w, eps, K, act.qs, act.ds, nullptr);
+      break;
+    case KQ_ACT_SUM_DQ:
+      if (bytes)
+        rms_norm_quantize_kernel<KQ_ACT_SUM_DQ, true><<<M, kNormThreads, 0, s>>>(x, w, eps, K, nullptr, nullptr, y);
+      else
+        rms_norm_quantize_kernel<KQ_ACT_SUM_DQ, false><<<M, kNormThreads, 0, s>>>(x, w, eps, K, act.qs, act.ds, nullptr);
+      break;
+    case KQ_ACT_F32:
+      if (bytes) return fail(KQ_ERR_INVALID, "q8_1 bytes hold fp16 d and s: sum_mode must be KQ_ACT_SUM_X or KQ_ACT_SUM_DQ");
+      rms_norm_quantize_kernel<KQ_ACT_F32, false><<<M, kNormThreads, 0, s>>>(x, w, eps, K, act.qs, act.ds, nullptr);
+      break;
+    default:
+      return fail(KQ_ERR_INVALID, "unknown activation mode %d", mode);
+  }
+  return check_launch("rms_norm_quantize");
 }
 
 }  // namespace kq

@@ -32,6 +32,10 @@ SIGNATURES = {
     "kq_flash_attn_q8_0": (None, [_vp, _vp, _vp, _vp, _i, _i, _i, _i]),
     "kq_flash_attn_q4_0": (None, [_vp, _vp, _vp, _vp, _i, _i, _i, _i]),
     "kq_flash_attn_f16": (None, [_vp, _vp, _vp, _vp, _i, _i, _i, _i]),
+    "kq_rms_norm": (None, [_vp, _vp, _vp, _i, _i]),
+    "kq_rms_norm_f32": (_i, [_vp, _vp, _vp, _i, _i, _f, _vp]),
+    "kq_rms_norm_quantize_q8_1": (_i, [_vp, _vp, _vp, _i, _i, _f, _i, _vp]),
+    "kq_gemm_f32act_rmsnorm": (_i, [_i, _vp, _vp, _vp, _f, _vp, _i, _i, _i, _i, _vp]),
     "kq_quantize_q8_1": (_i, [_vp, _vp, _i64, _i64, _i, _vp]),
     "kq_quantize_rows": (_i, [_i, _vp, _vp, _i64, _i64, _vp]),
     "kq_mul_mat_q": (_i, [_i, _vp, _vp, _vp, _i, _i, _i, _vp]),

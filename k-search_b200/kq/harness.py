@@ -1,8 +1,9 @@
 """Mirror of the KernelEvalPlus operator interface for this path.
 
-``quant_gemm_forward`` and ``flash_attention_forward`` have the signatures of
-the ``module.forward`` the harness calls
-(kernelevalplus-main/llm_kernel_test/op_test_handler.py:251-256 and :565-579);
+``quant_gemm_forward``, ``flash_attention_forward`` and ``rms_norm_forward``
+have the signatures of the ``module.forward`` the harness calls
+(kernelevalplus-main/llm_kernel_test/op_test_handler.py:251-256, :565-579 and
+:677-679);
 ``quant_gemm_test_configs`` / ``*_performance`` restate the harness's test
 configurations and FLOP accounting (op_test_handler.py:258-266, :449-458,
 :581-596) so runs here report the same numbers the harness would.
@@ -53,6 +54,33 @@ def flash_attention_forward(query: torch.Tensor, key_cache: torch.Tensor, value_
     """forward(q, k, v, B, S, H, D) -> fp32 [B, H, D] (op_test_handler.py:565-579);
     ``kv_format`` is ``flash_attention_kv_format(spec)`` of the definition."""
     return ops.flash_attn(query, key_cache, value_cache, batch_size, seq_len, num_heads, head_dim, kv_format)
+
+
+def rms_norm_forward(hidden_states: torch.Tensor, weight: torch.Tensor, epsilon: float = 1e-6) -> torch.Tensor:
+    """forward(hidden_states, weight) -> fp32 [batch, hidden] (op_test_handler.py:677-679;
+    every rms_norm definition has epsilon 1e-6)."""
+    return ops.rms_norm(hidden_states, weight, epsilon)
+
+
+def rms_norm_performance(latency_ms: float, batch_size: int, hidden_size: int) -> dict:
+    """GB/s as the harness reports them: (2 B H + H + B H) * 4 bytes / latency
+    (op_test_handler.py:681-690: the input is counted twice)."""
+    nbytes = (batch_size * hidden_size * 2 + hidden_size + batch_size * hidden_size) * 4
+    return {"gbps": round(nbytes / (latency_ms / 1000) / 1e9, 2)}
+
+
+def definition_test_configs(spec: dict) -> list[dict]:
+    """The test configurations a definition lists itself. The harness's
+    quant_gemm handler ignores them and always runs M = 1, 8, 512
+    (op_test_handler.py:449-458); this returns the definition's own list
+    (its M values for quant_gemm, batch sizes for flash_attention and
+    rms_norm), falling back to the handler's fixed list."""
+    cfgs = [dict(c) for c in spec.get("test_configs", [])]
+    if cfgs:
+        return cfgs
+    if spec.get("op_type") == "quant_gemm":
+        return quant_gemm_test_configs(spec["axes"]["N"]["value"], spec["axes"]["K"]["value"])
+    return [{"name": "batch_1", "batch_size": 1}]
 
 
 def quant_gemm_test_configs(N: int, K: int) -> list[dict]:

@@ -102,6 +102,51 @@ def gemm_f32act(weight: torch.Tensor, activation: torch.Tensor, M: int, N: int, 
     return out
 
 
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, out: torch.Tensor | None = None) -> torch.Tensor:
+    """x fp32 [M, K], weight fp32 [K] -> x / sqrt(mean(x^2) + eps) * weight
+    (the harness rms_norm operator, op_test_handler.py:641-690)."""
+    _cuda(x, "x", torch.float32)
+    if x.dim() != 2:
+        raise ValueError(f"x must be [M, K], got {tuple(x.shape)}")
+    M, K = x.shape
+    _cuda(weight, "weight", torch.float32, K)
+    if out is None:
+        out = torch.empty_like(x)
+    check(lib().kq_rms_norm_f32(x.data_ptr(), weight.data_ptr(), out.data_ptr(), M, K, float(eps), _stream(x)),
+          "kq_rms_norm_f32")
+    return out
+
+
+def rms_norm_quantize_q8_1(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6,
+                           sum_mode: str = "sum_x") -> torch.Tensor:
+    """RMSNorm fused into quantize_q8_1: fp32 [M, K] -> q8_1 bytes uint8
+    [M, K/32, 36] of the normalised rows."""
+    _cuda(x, "x", torch.float32)
+    M, K = x.shape
+    _cuda(weight, "weight", torch.float32, K)
+    y = torch.empty((M, K // 32, 36), dtype=torch.uint8, device=x.device)
+    check(lib().kq_rms_norm_quantize_q8_1(x.data_ptr(), weight.data_ptr(), y.data_ptr(), M, K, float(eps),
+                                          _act_mode(sum_mode), _stream(x)), "kq_rms_norm_quantize_q8_1")
+    return y
+
+
+def gemm_f32act_rmsnorm(weight: torch.Tensor, activation: torch.Tensor, norm_weight: torch.Tensor, M: int, N: int,
+                        K: int, wtype="q4_0", act_mode="f32", eps: float = 1e-6,
+                        out: torch.Tensor | None = None) -> torch.Tensor:
+    """gemm_f32act on rms_norm(activation, norm_weight, eps), the RMSNorm
+    fused into the on-the-fly quantisation -> fp32 [M, N]."""
+    wt = _wtype(wtype)
+    _cuda(weight, "weight", torch.uint8, N * (K // 32) * lib().kq_block_bytes(wt))
+    _cuda(activation, "activation", torch.float32, M * K)
+    _cuda(norm_weight, "norm_weight", torch.float32, K)
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=weight.device)
+    check(lib().kq_gemm_f32act_rmsnorm(wt, weight.data_ptr(), activation.data_ptr(), norm_weight.data_ptr(),
+                                       float(eps), out.data_ptr(), M, N, K, _act_mode(act_mode), _stream(weight)),
+          "kq_gemm_f32act_rmsnorm")
+    return out
+
+
 def gemm_f32act_scatter(weight: torch.Tensor, activation: torch.Tensor, outs: list[int], ldo: int, col0: int, M: int,
                         N: int, K: int, wtype="q4_0", act_mode="sum_dq", stream_of: torch.Tensor | None = None) -> None:
     """kq_gemm_f32act_scatter: the fused GEMM writing element (m, n) to

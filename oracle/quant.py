@@ -313,6 +313,18 @@ def gemm_dequant_f32(wtype: str, w: np.ndarray, x: np.ndarray, M: int, N: int, K
     return (np.asarray(x, dtype=np.float32) @ W.T).astype(np.float32)
 
 
+def rms_norm(x: np.ndarray, w: np.ndarray, eps: float = 1e-6) -> np.ndarray:
+    """RMSNormHandler.get_reference_output (llm_kernel_test/op_test_handler.py:662-673):
+    rms = sqrt(mean(x^2) + eps) per row, out = x / rms * weight. The mean and
+    square root here are fp64 rounded once to fp32; the divide and the
+    multiply are fp32, as torch does them. x fp32 [M, K], w fp32 [K]."""
+    x = np.asarray(x, dtype=np.float32)
+    w = np.asarray(w, dtype=np.float32)
+    ms = np.mean(x.astype(np.float64) ** 2, axis=-1, keepdims=True)
+    rms = np.sqrt(ms + eps).astype(np.float32)
+    return ((x / rms).astype(np.float32) * w).astype(np.float32)
+
+
 def nmse(out: np.ndarray, ref: np.ndarray) -> float:
     """NMSE as the harness computes it (llm_kernel_test/unified_test_runner.py:426-428)."""
     out = np.asarray(out, dtype=np.float64)

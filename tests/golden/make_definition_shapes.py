@@ -11,8 +11,9 @@ sweep test (tests/test_definition_shapes_gpu.py) reads only that file.
 Also writes flash_attention_definitions.json: for every JSON under
 definitions/flash_attention/, the fields the harness reads to build the
 inputs (key_cache dtype, variant, tags, the S / H / D axes, the test_configs'
-batch sizes); tests/test_flash_decode_gpu.py and tests/test_harness_mirror.py
-read that file.
+batch sizes) and rms_norm_definitions.json (hidden size, epsilon, batch
+sizes); tests/test_flash_decode_gpu.py, tests/test_rms_norm_gpu.py and
+tests/test_abi_cpu.py read them.
 
     python tests/golden/make_definition_shapes.py /path/to/K-Search
 """
@@ -73,6 +74,16 @@ def fa_defs(root: str) -> None:
         json.dump({"source": "kernelevalplus-main/definitions/flash_attention/ (read by make_definition_shapes.py)",
                    "definitions": defs}, fh, indent=1)
     print(f"{len(defs)} flash_attention definitions")
+    rdefs = []
+    for f in sorted(glob.glob(os.path.join(base, "rms_norm", "**", "*.json"), recursive=True)):
+        d = json.load(open(f))
+        rdefs.append({"definition": os.path.relpath(f, base), "hidden_size": d["axes"]["hidden_size"]["value"],
+                      "epsilon": d["axes"].get("epsilon", {}).get("value", 1e-6),
+                      "B": sorted({int(t["batch_size"]) for t in d.get("test_configs", [])})})
+    with open(os.path.join(HERE, "rms_norm_definitions.json"), "w") as fh:
+        json.dump({"source": "kernelevalplus-main/definitions/rms_norm/ (read by make_definition_shapes.py)",
+                   "definitions": rdefs}, fh, indent=1)
+    print(f"{len(rdefs)} rms_norm definitions")
 
 
 if __name__ == "__main__":

@@ -158,6 +158,19 @@ def main() -> None:
                    f"{fmt}_ref_on_cache": h.get_reference_output(spec, on_cache).numpy(),
                    f"{fmt}_ref_on_fp32": h.get_reference_output(spec, inp).numpy()})
     np.savez_compressed(os.path.join(HERE, "flash_attn_kv.npz"), **fa)
+
+    # --- rms_norm (op_test_handler.py:641-690): the handler's own inputs and
+    # reference output at two hidden sizes of the shipped definitions.
+    from llm_kernel_test.op_test_handler import RMSNormHandler  # noqa: E402
+    rh = RMSNormHandler()
+    rn = {}
+    for i, (hs, bs) in enumerate([(128, 3), (4096, 2)]):
+        spec = {"axes": {"hidden_size": {"value": hs}, "epsilon": {"value": 1e-6}}}
+        torch.manual_seed(2000 + i)
+        inp = rh.generate_inputs(spec, {"batch_size": bs}, "cpu")
+        rn.update({f"x{hs}": inp["hidden_states"].numpy(), f"w{hs}": inp["weight"].numpy(),
+                   f"out{hs}": rh.get_reference_output(spec, inp).numpy()})
+    np.savez_compressed(os.path.join(HERE, "rms_norm.npz"), **rn)
     print("golden fixtures written to", HERE)
 
 

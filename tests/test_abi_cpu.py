@@ -56,6 +56,12 @@ def test_host_only_entry_points(libkq):
     assert L.kq_fa_decode_mha(3, None, None, None, None, 1, 1, 1, 32, None) == 1
     assert "unknown KV format" in _lib.last_error()
     assert L.kq_fa_decode_mha(1, None, None, None, None, 1, 1, 1, 48, None) == 1
+    assert L.kq_rms_norm_quantize_q8_1(None, None, None, 2, 48, ctypes.c_float(1e-6), 0, None) == 1
+    assert "K % 32" in _lib.last_error()
+    assert L.kq_rms_norm_quantize_q8_1(None, None, None, 2, 64, ctypes.c_float(1e-6), 2, None) == 1
+    assert L.kq_rms_norm_f32(None, None, None, -1, 64, ctypes.c_float(1e-6), None) == 1
+    assert L.kq_rms_norm_f32(None, None, None, 0, 64, ctypes.c_float(1e-6), None) == 0
+    assert L.kq_gemm_f32act_rmsnorm(0, None, None, None, ctypes.c_float(1e-6), None, 1, 1, 33, 2, None) == 1
     # empty problems are no-ops
     assert L.kq_gemm_f32act(0, None, None, None, 0, 16, 64, 2, None) == 0
 
@@ -85,7 +91,7 @@ def test_harness_kv_format_of_every_definition():
 
 
 @pytest.mark.parametrize("name", ["kernel_quant_gemm.cu", "kernel_flash_attn.cu", "kernel_flash_attn_q4_0.cu",
-                                  "kernel_flash_attn_f16.cu"])
+                                  "kernel_flash_attn_f16.cu", "kernel_rms_norm.cu"])
 def test_harness_forwarders_build(name, tmp_path):
     """The attempt files are host-only C++: they compile with g++ and export
     the entry the harness binds."""
@@ -98,3 +104,18 @@ def test_harness_forwarders_build(name, tmp_path):
     subprocess.run(["g++", "-x", "c++", "-std=c++17", "-O1", "-fPIC", "-shared", src, "-o", so, "-ldl"], check=True)
     entry = re.search(r'extern "C" void (\w+)\(', open(src).read()).group(1)
     assert hasattr(ctypes.CDLL(so), entry)
+
+
+def test_definition_test_configs():
+    """The harness mirror returns a definition's own test configurations
+    (the quant_gemm handler's fixed M = 1, 8, 512 only when it lists none)."""
+    import json
+    from kq import harness
+    here = os.path.join(REPO, "tests", "golden")
+    rdefs = json.load(open(os.path.join(here, "rms_norm_definitions.json")))["definitions"]
+    assert len(rdefs) == 9 and all(d["epsilon"] == 1e-6 for d in rdefs)
+    spec = {"op_type": "rms_norm", "test_configs": [{"name": f"batch_{b}", "batch_size": b} for b in (1, 8, 32, 512)]}
+    assert [c["batch_size"] for c in harness.definition_test_configs(spec)] == [1, 8, 32, 512]
+    qspec = {"op_type": "quant_gemm", "axes": {"N": {"value": 4096}, "K": {"value": 4096}}}
+    assert [c["M"] for c in harness.definition_test_configs(qspec)] == [1, 8, 512]
+    assert harness.rms_norm_performance(1.0, 512, 4096)["gbps"] == round((512 * 4096 * 3 + 4096) * 4 / 1e-3 / 1e9, 2)

@@ -147,3 +147,12 @@ def test_moe_route():
     assert idx.tolist() == [[1, 3], [0, 2]]   # tie -> lower expert first
     np.testing.assert_allclose(w.sum(1), 1.0)
     np.testing.assert_allclose(w[1, 0], 1 / (1 + np.exp(-2.0)))
+
+
+@pytest.mark.parametrize("hs", [128, 4096])
+def test_rms_norm_matches_reference(hs):
+    """The oracle against the harness's RMSNormHandler on its own inputs."""
+    g = _load("rms_norm.npz")
+    out = Q.rms_norm(g[f"x{hs}"], g[f"w{hs}"], 1e-6)
+    ref = g[f"out{hs}"]
+    np.testing.assert_allclose(out, ref, rtol=2e-6, atol=1e-6 * float(np.sqrt(np.mean(ref ** 2))))
