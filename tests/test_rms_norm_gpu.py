@@ -7,8 +7,8 @@ the row's mean of squares is summed in a different order).
 RMSNorm -> q8_1: scales within 1e-5 relative of the oracle's quantisation of
 the oracle's normalised rows, codes equal except a step of 1 where a
 normalised value sits within rounding of a code boundary (<= 0.1% of codes).
-Fused GEMM: the usual GEMM bar against the oracle GEMM on the oracle's
-normalised activations.
+Fused GEMM: the usual GEMM bar against the oracle GEMM on the library's
+normalised rows, rel-L2 against the oracle's own normalisation.
 """
 import json
 import os
@@ -100,17 +100,22 @@ def test_rms_norm_quantize_q8_1(cuda, sum_mode, M, K):
 @pytest.mark.parametrize("wtype", ["q4_0", "q8_0", "q4_1"])
 @pytest.mark.parametrize("M", [1, 5, 512])
 def test_gemm_f32act_rmsnorm(cuda, wtype, M):
+    """The fused call against the oracle GEMM on the library's normalised rows
+    (themselves pinned to the oracle's RMSNorm to fp32 rounding), with the
+    usual bar; against the oracle's own normalisation the bar is rel-L2 only,
+    since a normalised value an ulp away can move its q8_1 code by one."""
     import kq
     N, K = 1024, 4096
     rng = np.random.default_rng(M + N + len(wtype))
     x = rng.standard_normal((M, K)).astype(np.float32)
     g = rng.uniform(0.5, 1.5, K).astype(np.float32)
     wq = Q.quantize_weights(wtype, (rng.standard_normal((N, K)) * 0.02).astype(np.float32))
-    got = kq.gemm_f32act_rmsnorm(_t(wq, cuda), _t(x, cuda), _t(g, cuda), M, N, K, wtype, "f32").cpu().numpy()
+    xd, gd = _t(x, cuda), _t(g, cuda)
+    got = kq.gemm_f32act_rmsnorm(_t(wq, cuda), xd, gd, M, N, K, wtype, "f32").cpu().numpy()
+    xn = kq.rms_norm(xd, gd).cpu().numpy()
+    _check_norm(xn, Q.rms_norm(x, g))
+    ok, msg = Q.check_close(got, Q.gemm_f32act(wtype, wq, xn, M, N, K, Q.ACT_F32))
+    assert ok, msg
     ref = Q.gemm_f32act(wtype, wq, Q.rms_norm(x, g), M, N, K, Q.ACT_F32)
-    ok, msg = Q.check_close(got, ref)
-    assert ok, msg
-    # the same as the two-call form on the library's own normalised rows
-    two = kq.gemm_f32act(_t(wq, cuda), kq.rms_norm(_t(x, cuda), _t(g, cuda)), M, N, K, wtype, "f32").cpu().numpy()
-    ok, msg = Q.check_close(got, two)
-    assert ok, msg
+    rel = float(np.linalg.norm(got.astype(np.float64) - ref) / np.linalg.norm(ref.astype(np.float64)))
+    assert rel <= 1e-3, rel
