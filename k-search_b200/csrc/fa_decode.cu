@@ -985,19 +985,20 @@ bool fast_ok(const void* k, const void* v, int D, int Hkv, int g) {
          (reinterpret_cast<uintptr_t>(k) & 15) == 0 && (reinterpret_cast<uintptr_t>(v) & 15) == 0;
 }
 
-// Choose the number of chunks so the partial buffers stay within `budget`.
-int choose_chunks(long long Q, int D, int max_len, size_t budget, int* chunk) {
-  int nc = std::max(1, (max_len + 255) / 256);
-  const long long per = (long long)Q * (D + 2) * 4;
-  const long long cap = std::max<long long>(1, (long long)budget / std::max<long long>(per, 1));
-  nc = (int)std::min<long long>(nc, cap);
-  nc = std::min(nc, 65535);
-  *chunk = std::max(1, (max_len + nc - 1) / nc);
-  nc = std::max(1, (max_len + *chunk - 1) / *chunk);
-  return nc;
-}
-
 constexpr size_t kPartialBudget = 64ull << 20;
+
+// Chunks for the TMA kernels: 256-token chunks, more (down to one tile each)
+// when `items` CTAs per chunk would leave the GPU short of two CTAs per SM.
+int choose_chunks_fast(long long Q, int D, int max_len, size_t budget, int items, int* chunk) {
+  long long nc = std::max(1, (max_len + 255) / 256);
+  nc = std::max<long long>(nc, (2LL * sm_count() + items - 1) / std::max(items, 1));
+  nc = std::min<long long>(nc, std::max(1, (max_len + kStF - 1) / kStF));
+  const long long per = (long long)Q * (D + 2) * 4;
+  nc = std::min<long long>(nc, std::max<long long>(1, (long long)budget / std::max<long long>(per, 1)));
+  nc = std::min<long long>(nc, 65535);
+  *chunk = (int)std::max<long long>(1, (max_len + nc - 1) / nc);
+  return std::max(1, (max_len + *chunk - 1) / *chunk);
+}
 
 // Pass 1 of the generic path: the lane-vector kernel when head_dim is 64, 128
 // or 256 (and fp16 caches are aligned for its vector loads), else the
@@ -1042,7 +1043,8 @@ kq_status_t launch_fa_mha(int kvf, const float* q, const void* k, const void* v,
   const bool fast = kvf == KQ_KV_Q8_0 && fast_ok(k, v, D, H, 1) && S > 0 &&
                     (long long)((B + kG - 1) / kG) * (H / kHpc) <= 65535;
   int chunk = 0;
-  const int NC = fast ? choose_chunks(Q, D, std::max(S, 1), kPartialBudget, &chunk)
+  const int NC = fast ? choose_chunks_fast(Q, D, std::max(S, 1), kPartialBudget, ((B + kG - 1) / kG) * (H / kHpc),
+                                           &chunk)
                       : choose_chunks_generic(Q, D, std::max(S, 1), kPartialBudget, &chunk);
   const size_t bytes = (size_t)Q * NC * (D + 2) * sizeof(float);
   float* ws = static_cast<float*>(workspace(WS_FA, bytes));
@@ -1081,7 +1083,7 @@ kq_status_t launch_fa_ragged(const void* q, const void* k, const void* v, const 
   const int g = Hq / Hkv;
   const bool fast = fast_ok(k, v, D, Hkv, g) && total_rows > 0 && (long long)B * (Hkv / kHpc) <= 65535;
   int chunk = 0;
-  const int NC = fast ? choose_chunks(Q, D, std::max(max_seqlen, 1), kPartialBudget, &chunk)
+  const int NC = fast ? choose_chunks_fast(Q, D, std::max(max_seqlen, 1), kPartialBudget, B * (Hkv / kHpc), &chunk)
                       : choose_chunks_generic(Q, D, std::max(max_seqlen, 1), kPartialBudget, &chunk);
   const size_t bytes = (size_t)Q * NC * (D + 2) * sizeof(float);
   float* ws = static_cast<float*>(workspace(WS_FA, bytes));
