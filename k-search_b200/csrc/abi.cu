@@ -5,6 +5,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "kq_internal.h"
 
@@ -101,6 +102,26 @@ int* device_error_word() {
     cudaMemset(st.err_word, 0, sizeof(int));
   }
   return st.err_word;
+}
+
+namespace {
+struct SmemAttr {
+  int dev;
+  const void* func;
+  int bytes;
+};
+std::vector<SmemAttr> g_smem_attrs;  // guarded by g_mu
+}  // namespace
+
+kq_status_t ensure_dynamic_smem(const void* func, int bytes, const char* what) {
+  const int d = current_device();
+  std::lock_guard<std::mutex> lk(g_mu);
+  for (const SmemAttr& a : g_smem_attrs)
+    if (a.dev == d && a.func == func && a.bytes >= bytes) return KQ_OK;
+  kq_status_t st = check_cuda(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), what);
+  if (st) return st;
+  g_smem_attrs.push_back(SmemAttr{d, func, bytes});
+  return KQ_OK;
 }
 
 void* tensor_map_encoder() {

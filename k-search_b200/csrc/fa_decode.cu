@@ -968,13 +968,8 @@ kq_status_t launch_fast(const FastParams& p, const void* k, const void* v, uint6
     return fail(KQ_ERR_CUDA, "fa: KV tensor map rejected");
   auto kern = simt ? fa_fast_kernel<QT, RAGGED> : fa_mma_kernel<QT, RAGGED>;
   const size_t smem = simt ? kFastSmem : kMmaSmem;
-  static unsigned attr_done = 0;
-  const int dev = current_device();
-  if (!(attr_done & (1u << (dev & 31)))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return check_cuda(e, "fa smem attribute");
-    attr_done |= 1u << (dev & 31);
-  }
+  kq_status_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)smem, "fa smem attribute");
+  if (st) return st;
   dim3 grid(p.NC, items);
   kern<<<grid, kFastThreads, smem, s>>>(km, vm, p);
   return check_launch("fa_fast");

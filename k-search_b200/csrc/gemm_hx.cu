@@ -570,13 +570,8 @@ kq_status_t launch_hx(const void* w, Act8 act, float* out, int M, int N, int K, 
     return fail(KQ_ERR_CUDA, "tensor map (weights) rejected");
 
   auto kern = gemm_hx_kernel<WT>;
-  static unsigned attr_done = 0;
-  const int dev = current_device();
-  if (!(attr_done & (1u << (dev & 31)))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::SMEM);
-    if (e != cudaSuccess) return check_cuda(e, "gemm_hx smem attribute");
-    attr_done |= 1u << (dev & 31);
-  }
+  if (kq_status_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), T::SMEM, "gemm_hx smem attribute"))
+    return st;
   HxParams p;
   p.M = M; p.N = N; p.K = K; p.Kp = Kp;
   p.nmain = nmain; p.ngrp = ngrp; p.nb = nb;

@@ -817,13 +817,8 @@ kq_status_t launch_split(const void* w, Act8 act, const OutSpec& out, int M, int
 
   const bool scatter = out.n_out > 1 || out.ld != N || out.col0 != 0;
   auto kern = scatter ? gemm_split_kernel<WT, true> : gemm_split_kernel<WT, false>;
-  static unsigned attr_done[2] = {0, 0};
-  const int dev = current_device();
-  if (!(attr_done[scatter] & (1u << (dev & 31)))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::SMEM);
-    if (e != cudaSuccess) return check_cuda(e, "gemm_split smem attribute");
-    attr_done[scatter] |= 1u << (dev & 31);
-  }
+  if (kq_status_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), T::SMEM, "gemm_split smem attribute"))
+    return st;
   SxParams p;
   p.M = M; p.N = N; p.K = K;
   p.nmain = nmain; p.ngrp = ngrp;

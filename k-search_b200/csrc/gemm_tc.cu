@@ -555,13 +555,8 @@ kq_status_t launch_tc(const void* w, Act8 act, const OutSpec& out, int M, int N,
 
   const bool scatter = out.n_out > 1 || out.ld != N || out.col0 != 0;
   auto kern = scatter ? gemm_tc_kernel<WT, true> : gemm_tc_kernel<WT, false>;
-  static unsigned attr_done[2] = {0, 0};
-  const int dev = current_device();
-  if (!(attr_done[scatter] & (1u << (dev & 31)))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::SMEM);
-    if (e != cudaSuccess) return check_cuda(e, "gemm_tc smem attribute");
-    attr_done[scatter] |= 1u << (dev & 31);
-  }
+  if (kq_status_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), T::SMEM, "gemm_tc smem attribute"))
+    return st;
   TcParams p;
   p.M = M; p.N = N; p.K = K; p.nb = nb;
   p.num_m_tiles = (M + TM - 1) / TM;

@@ -373,13 +373,8 @@ kq_status_t launch_cfg(const void* w, Act8 act, const OutSpec& out, int M, int N
                        int* err) {
   using C = GemvCfg<WT, MR, BPL, KW, SR>;
   auto kern = gemv_kernel<WT, MR, BPL, KW, SR>;
-  static unsigned attr_done = 0;  // one bit per device ordinal
-  const int dev = current_device();
-  if (!(attr_done & (1u << (dev & 31)))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
-    if (e != cudaSuccess) return check_cuda(e, "gemv smem attribute");
-    attr_done |= 1u << (dev & 31);
-  }
+  if (kq_status_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)C::SMEM, "gemv smem attribute"))
+    return st;
   const int grid = std::max(1, std::min(sm_count(), (N + SR - 1) / SR));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);

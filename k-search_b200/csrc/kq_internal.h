@@ -28,6 +28,12 @@ int sm_count();
 // nullptr if unavailable.
 void* tensor_map_encoder();
 
+// ---- kernel attributes ------------------------------------------------------
+// Raises `func`'s dynamic shared-memory limit to `bytes` on the current
+// device, once per (device, kernel); thread-safe. `what` names the kernel in
+// the error message.
+kq_status_t ensure_dynamic_smem(const void* func, int bytes, const char* what);
+
 // ---- workspace ------------------------------------------------------------
 // Per-device cached scratch, one buffer per slot, grown on demand (never
 // shrunk). The buffer is ordered on `stream`: growing it synchronises the
