@@ -1,4 +1,5 @@
 // libkq C ABI: argument checks, dispatch, per-device workspace, error state.
+#include <atomic>
 #include <cstdlib>
 #include <cstdarg>
 #include <cstdio>
@@ -19,7 +20,7 @@ struct DeviceState {
   void* ws[WS_NSLOTS] = {};
   size_t ws_size[WS_NSLOTS] = {};
   int* err_word = nullptr;
-  int sms = 0;
+  std::atomic<int> sms{0};  // read without g_mu
 };
 DeviceState g_dev[kMaxDevices];
 std::mutex g_mu;
@@ -51,12 +52,13 @@ int current_device() {
 int sm_count() {
   const int d = current_device();
   if (d < 0 || d >= kMaxDevices) return 148;
-  if (g_dev[d].sms == 0) {
-    int n = 0;
+  int n = g_dev[d].sms.load(std::memory_order_relaxed);
+  if (n == 0) {
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
-    g_dev[d].sms = n > 0 ? n : 148;
+    if (n <= 0) n = 148;
+    g_dev[d].sms.store(n, std::memory_order_relaxed);
   }
-  return g_dev[d].sms;
+  return n;
 }
 
 void* workspace(WsSlot slot, size_t bytes) {
