@@ -156,3 +156,33 @@ def test_rms_norm_matches_reference(hs):
     out = Q.rms_norm(g[f"x{hs}"], g[f"w{hs}"], 1e-6)
     ref = g[f"out{hs}"]
     np.testing.assert_allclose(out, ref, rtol=2e-6, atol=1e-6 * float(np.sqrt(np.mean(ref ** 2))))
+
+
+def test_kv_dequant_round_trip_bounds():
+    """q4_0 / q8_0 caches dequantise to within half a step of the fp32 rows
+    (q4_0 step d = amax/7, q8_0 step d = amax/127) plus the fp16 rounding of
+    the stored scale (|code| * 2^-11 * d); fp16 to fp16 rounding."""
+    rng = np.random.default_rng(21)
+    D = 128
+    x = (rng.standard_normal((64, D)) * rng.uniform(0.01, 10.0, (64, 1))).astype(np.float32)
+    for fmt, steps, qmax, quant in (("q4_0", 7.0, 8.0, Q.quantize_q4_0), ("q8_0", 127.0, 127.0, Q.quantize_q8_0)):
+        back = Q.dequant_kv_rows(fmt, quant(x), 64, D)
+        amax = np.abs(x.reshape(64, D // 32, 32)).max(-1, keepdims=True)
+        step = np.broadcast_to(amax / steps, (64, D // 32, 32)).reshape(64, D)
+        err = np.abs(back.astype(np.float64) - x)
+        assert np.all(err <= step * (0.5 + qmax * 2.0 ** -11) * (1 + 1e-6) + 1e-6), (fmt, float((err / step).max()))
+    h = x.astype(np.float16)
+    np.testing.assert_array_equal(Q.dequant_kv_rows("f16", h, 64, D), h.astype(np.float32))
+
+
+def test_rms_norm_properties():
+    """Unit weights give rows of unit root mean square (eps aside); the result
+    is invariant to scaling a row by c > 0 (eps aside) and linear in the weight."""
+    rng = np.random.default_rng(22)
+    x = rng.standard_normal((5, 256)).astype(np.float32) * 3.0
+    ones = np.ones(256, dtype=np.float32)
+    y = Q.rms_norm(x, ones, 0.0)
+    np.testing.assert_allclose(np.sqrt(np.mean(y.astype(np.float64) ** 2, axis=-1)), 1.0, rtol=1e-5)
+    np.testing.assert_allclose(Q.rms_norm(np.float32(7.5) * x, ones, 0.0), y, rtol=1e-5, atol=1e-6)
+    w = rng.standard_normal(256).astype(np.float32)
+    np.testing.assert_allclose(Q.rms_norm(x, w, 1e-6), Q.rms_norm(x, ones, 1e-6) * w, rtol=1e-6, atol=1e-6)
