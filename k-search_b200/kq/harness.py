@@ -69,6 +69,33 @@ def rms_norm_performance(latency_ms: float, batch_size: int, hidden_size: int) -
     return {"gbps": round(nbytes / (latency_ms / 1000) / 1e9, 2)}
 
 
+# GPUs with a GGML baseline table in the reference (unified_test_runner.py:593-604).
+_BASELINE_GPUS = ("RTX4090", "RTX4070", "A100", "RTX5090")
+
+
+def baseline_hardware(gpu_name: str) -> str | None:
+    """The baseline table for a GPU, or None when the reference has none.
+    The harness strips "NVIDIA", spaces, "Laptop" and "Mobile" from the name
+    and falls back to RTX4090 for any GPU it does not list, so a B200 run
+    would be compared with RTX 4090 numbers; this returns None instead."""
+    key = gpu_name.replace(" ", "").replace("NVIDIA", "").replace("Laptop", "").replace("Mobile", "")
+    for hw in _BASELINE_GPUS:
+        if hw in key:
+            return hw
+    return None
+
+
+def quant_gemm_baseline_case(weight_dtype: str, M: int, N: int, K: int, activation: str = "f32") -> str:
+    """Case id of the GGML baseline table for a quant_gemm call. GGML's m is
+    the output features (our N) and its n the batch (our M)
+    (op_test_handler.py:274-281); the id format is BaselineAPI.get_gemm's
+    (core/tools/baseline_api.py:121-123). The handler calls a method the API
+    does not have (`get_baseline`), so its lookups always fail; this is the
+    key `get_gemm` reads."""
+    wt = _WEIGHT[weight_dtype]
+    return f"w{4 if 'q4' in wt else 8}a32c8_{wt}_{activation.replace('float', 'f')}_m{N}_n{M}_k{K}"
+
+
 def definition_test_configs(spec: dict) -> list[dict]:
     """The test configurations a definition lists itself. The harness's
     quant_gemm handler ignores them and always runs M = 1, 8, 512

@@ -119,3 +119,14 @@ def test_definition_test_configs():
     qspec = {"op_type": "quant_gemm", "axes": {"N": {"value": 4096}, "K": {"value": 4096}}}
     assert [c["M"] for c in harness.definition_test_configs(qspec)] == [1, 8, 512]
     assert harness.rms_norm_performance(1.0, 512, 4096)["gbps"] == round((512 * 4096 * 3 + 4096) * 4 / 1e-3 / 1e9, 2)
+
+
+def test_baseline_lookup_fixups():
+    """Baseline reporting as the harness means it: no RTX 4090 fallback for
+    GPUs without a table, and the GGML case id with m = N, n = M."""
+    from kq import harness
+    assert harness.baseline_hardware("NVIDIA GeForce RTX 4090") == "RTX4090"
+    assert harness.baseline_hardware("NVIDIA A100-SXM4-80GB") == "A100"
+    assert harness.baseline_hardware("NVIDIA B200") is None
+    assert harness.quant_gemm_baseline_case("block_q4_0", 1, 4096, 14336) == "w4a32c8_q4_0_f32_m4096_n1_k14336"
+    assert harness.quant_gemm_baseline_case("block_q8_0", 512, 11008, 4096) == "w8a32c8_q8_0_f32_m11008_n512_k4096"
