@@ -176,8 +176,10 @@ kq_status_t kq_gemm_f32act(int wtype, const void* w, const float* x, float* out,
  * allocator already owns nearly all of HBM, or code that must not synchronise
  * the device on a first-call allocation). The activation staging lives in a
  * fixed 1 MiB file-scope __device__ array held by every GPU that loads libkq:
- * calls with act staging M*K + M*(K/32)*8 bytes (K rounded as in the library)
- * above 1 MiB are rejected with KQ_ERR_INVALID. The first call on a device
+ * calls whose staging, round_up(M*K, 256) + M*(K/32)*8 bytes, is above 1 MiB
+ * are rejected with KQ_ERR_INVALID. Device-side wait timeouts of these calls
+ * go to a word of their own, read with kq_noalloc_device_error (which, unlike
+ * kq_device_error, allocates nothing). The first call on a device
  * resolves the array's device address (cudaGetSymbolAddress) and should come
  * before any stream capture. All calls share the array: calls that overlap on
  * the GPU race. Same arguments as kq_gemm_f32act; for M > 8 it runs the int8
@@ -185,6 +187,10 @@ kq_status_t kq_gemm_f32act(int wtype, const void* w, const float* x, float* out,
  * kq_gemm_f32act's to the parity bar rather than bit for bit. */
 kq_status_t kq_gemm_f32act_noalloc(int wtype, const void* w, const float* x, float* out, int M, int N, int K,
                                    int act_mode, kq_stream_t stream);
+/* Reads and clears the device error word of kq_gemm_f32act_noalloc's kernels
+ * on the current device (synchronises `stream`); *code = 0 when no wait timed
+ * out. Allocates nothing. No reference counterpart. */
+kq_status_t kq_noalloc_device_error(int* code, kq_stream_t stream);
 
 /* The fused fp32-activation GEMM writing each output element to several
  * destinations: element (m, n) goes to outs[d][m * ldo + col0 + n] for every

@@ -171,14 +171,14 @@ GemmPath gemm_path() {
 }
 
 // The tensor-core kernel for M > 8 with the given output destinations, or
-// KQ_ERR_UNSUPPORTED (no error recorded) when neither fits the shape.
+// KQ_ERR_UNSUPPORTED when neither fits the shape.
 kq_status_t dispatch_gemm_tc(int wtype, const void* w, Act8 act, const OutSpec& out, int M, int N, int K,
                              cudaStream_t s, bool pdl) {
   const GemmPath path = gemm_path();
   if (path == GemmPath::kSplit && gemm_split_supported(wtype, M, N, K, w, act))
     return launch_gemm_split(wtype, w, act, out, M, N, K, s);
   if (gemm_tc_supported(wtype, M, N, K, w, act)) return launch_gemm_tc(wtype, w, act, out, M, N, K, pdl, s);
-  return KQ_ERR_UNSUPPORTED;
+  return fail(KQ_ERR_UNSUPPORTED, "no tensor-core GEMM for M=%d N=%d K=%d", M, N, K);
 }
 
 bool gemm_tc_any_supported(int wtype, int M, int N, int K, const void* w, Act8 act) {

@@ -484,7 +484,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (m < p.M) {
             if constexpr (!SCATTER) {
               float* o = p.out.ptr[0] + (size_t)m * p.N + nc0;
-              if (nc0 + kEpiCols <= p.N && (p.N & 3) == 0) {
+              // float4 stores only when every row start is 16-byte aligned
+              // (an offset output view falls back to scalar stores)
+              if (nc0 + kEpiCols <= p.N && (p.N & 3) == 0 && (reinterpret_cast<uintptr_t>(p.out.ptr[0]) & 15) == 0) {
 #pragma unroll
                 for (int c = 0; c < NP; c += 2) {
                   const float2 a = upk2(acc[c]), b = upk2(acc[c + 1]);

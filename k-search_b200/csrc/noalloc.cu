@@ -102,3 +102,23 @@ extern "C" kq_status_t kq_gemm_f32act_noalloc(int wtype, const void* w, const fl
   if (gemm_tc_supported(wtype, M, N, K, w, act)) return launch_gemm_tc(wtype, w, act, out, M, N, K, true, s, p.err);
   return launch_gemm_simt(wtype, w, act, out, M, N, K, s);
 }
+
+// The error word of kq_gemm_f32act_noalloc's kernels, read without any
+// allocation (kq_device_error reads the library's own word, which it
+// allocates on first use). Reads it on `stream`, synchronises that stream,
+// and clears a non-zero word.
+extern "C" kq_status_t kq_noalloc_device_error(int* code, kq_stream_t stream) {
+  if (!code) return fail(KQ_ERR_INVALID, "null code pointer");
+  NoAllocPtrs p;
+  kq_status_t st = device_ptrs(&p);
+  if (st) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int v = 0;
+  st = check_cuda(cudaMemcpyAsync(&v, p.err, sizeof(int), cudaMemcpyDeviceToHost, s), "read the no-alloc error word");
+  if (st) return st;
+  st = check_cuda(cudaStreamSynchronize(s), "sync");
+  if (st) return st;
+  *code = v;
+  if (v) return check_cuda(cudaMemsetAsync(p.err, 0, sizeof(int), s), "clear the no-alloc error word");
+  return KQ_OK;
+}

@@ -41,6 +41,7 @@ SIGNATURES = {
     "kq_mul_mat_q": (_i, [_i, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "kq_gemm_f32act": (_i, [_i, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "kq_gemm_f32act_noalloc": (_i, [_i, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "kq_noalloc_device_error": (_i, [_vp, _vp]),
     "kq_mul_mat_q8x": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "kq_moe_q4_0": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp]),
     "kq_gemm_f32act_scatter": (_i, [_i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),

@@ -207,9 +207,12 @@ class NShardedGemm:
         than that, the epilogue writes the local buffer only and one strided
         copy per peer (copy engines, one stream each) pushes the block
         afterwards. A one-element all-reduce then orders all of it before
-        anything later on any rank's stream. The returned tensor stays valid
-        until the call after next. None if the shape has no scatter
-        epilogue."""
+        anything later on any rank's stream. The returned tensor is valid
+        only until this object's next call: a peer that has passed that
+        call's all-reduce may already be storing into the other buffer's
+        successor, and a call with more rows than any before frees both
+        buffers before allocating larger ones. Copy it out to keep it. None
+        if the shape has no scatter epilogue."""
         from . import ops
         from ._lib import KQError, check, lib
         M = x.shape[0]

@@ -13,6 +13,8 @@ operands need workspace) while this one runs the int8 tensor-core kernel, so
 the two agree to the parity bar, not bitwise. It lives in its own file,
 collected last, and passes alone or after the rest of the suite.
 """
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -56,6 +58,10 @@ def test_noalloc_matches_allocating_entry(cuda, wtype, M, N, K):
         assert ok, f"call {call} noalloc vs kq_gemm_f32act: {msg}"
         if M <= 8:
             assert torch.equal(got, alloc), f"call {call}: not bit-identical to kq_gemm_f32act"
+        # the no-alloc kernels record wait timeouts in a word of their own
+        code = ctypes.c_int(-1)
+        assert L.kq_noalloc_device_error(ctypes.byref(code), torch.cuda.current_stream().cuda_stream) == 0
+        assert code.value == 0, f"call {call}: no-alloc device error word {code.value}"
     assert kq.device_error() == 0
 
 
