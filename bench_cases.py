@@ -1,10 +1,10 @@
 """Run one operator of the path on seeded synthetic device inputs, a few
 times, for profilers (ncu) and quick timing:
 
-    python k-search_b200/kq/cases.py gemm --wtype q8_0 --M 512 --N 11008 --K 4096 --reps 3
-    python k-search_b200/kq/cases.py gemv --wtype q4_0 --N 14336 --K 4096
-    python k-search_b200/kq/cases.py decode --B 32 --Lmax 8192
-    python k-search_b200/kq/cases.py moe --T 1024
+    python bench_cases.py gemm --wtype q8_0 --M 512 --N 11008 --K 4096 --reps 3
+    python bench_cases.py gemv --wtype q4_0 --N 14336 --K 4096
+    python bench_cases.py decode --B 32 --Lmax 8192
+    python bench_cases.py moe --T 1024
 
 Inputs are generated on the GPU (weights drawn as q-blocks with the
 benchmark configurations' distributions), then the operator runs --warmup
@@ -22,7 +22,7 @@ import sys
 import numpy as np
 import torch
 
-sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "k-search_b200"))
 import kq  # noqa: E402
 from kq import synth  # noqa: E402
 

@@ -156,14 +156,11 @@ kq_status_t check_gemm_args(int wtype, const void* w, const void* a, const float
 // Quantised activations are staged; choose the GEMM kernel for the shape.
 // M > 8 path: the exact split-fp16 tcgen05 kernel by default;
 // KQ_GEMM_PATH=int8 selects the int8 tcgen05 kernel (per-block int32 sums
-// rescaled on the FP32 pipe, slower); KQ_GEMM_PATH=dequant the single-rounding
-// fp16 kernel (fp16 operand rounding: rel-L2 about 3e-4 against the exact
-// result, outside the per-element bar). Read once per process.
-enum class GemmPath { kSplit, kDequant, kInt8 };
+// rescaled on the FP32 pipe). Read once per process.
+enum class GemmPath { kSplit, kInt8 };
 GemmPath gemm_path() {
   static const GemmPath p = [] {
     const char* e = std::getenv("KQ_GEMM_PATH");
-    if (e && std::string(e) == "dequant") return GemmPath::kDequant;
     if (e && std::string(e) == "int8") return GemmPath::kInt8;
     return GemmPath::kSplit;
   }();
@@ -189,8 +186,6 @@ bool gemm_tc_any_supported(int wtype, int M, int N, int K, const void* w, Act8 a
 kq_status_t dispatch_gemm(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, cudaStream_t s,
                           bool pdl) {
   if (gemv_supported(wtype, M, N, K) && aligned(w, 16)) return launch_gemv(wtype, w, act, out, M, N, K, pdl, s);
-  if (gemm_path() == GemmPath::kDequant && gemm_hx_supported(wtype, M, N, K, w, act))
-    return launch_gemm_hx(wtype, w, act, out, M, N, K, pdl, s);
   if (gemm_tc_any_supported(wtype, M, N, K, w, act))
     return dispatch_gemm_tc(wtype, w, act, OutSpec::plain(out, N), M, N, K, s, pdl);
   return launch_gemm_simt(wtype, w, act, out, M, N, K, s);

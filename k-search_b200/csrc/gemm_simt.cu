@@ -2,8 +2,8 @@
 // the int32 block-sum parity kernel. CUDA cores, dp4a.
 //
 // This is the shape-generic path (odd K, unaligned weight slices) and the
-// cross-check for the tensor-core GEMM; the hot paths are gemv.cu (M <= 8)
-// and gemm_tc.cu (tcgen05).
+// cross-check for the tensor-core GEMMs; the hot paths are gemv.cu (M <= 8)
+// and gemm_split.cu (M > 8, tcgen05; gemm_tc.cu is the int8 alternative).
 // Formulas: gemm_ref.py:100-153 (q4_0), :274-331 (q4_1),
 // gemm_reference.h:311-336 (q8_0).
 #include <algorithm>

@@ -119,10 +119,6 @@ kq_status_t launch_gemm_tc(int wtype, const void* w, Act8 act, float* out, int M
 bool gemm_split_supported(int wtype, int M, int N, int K, const void* w, Act8 act);
 kq_status_t launch_gemm_split(int wtype, const void* w, Act8 act, const OutSpec& out, int M, int N, int K,
                               cudaStream_t s, int* err = nullptr);
-// gemm_hx.cu (M > 8, K % 256 == 0: fp16-dequantised operands, tcgen05 kind::f16)
-bool gemm_hx_supported(int wtype, int M, int N, int K, const void* w, Act8 act);
-kq_status_t launch_gemm_hx(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, bool pdl,
-                           cudaStream_t s, int* err = nullptr);
 // gemm_simt.cu (any shape; the generic path)
 kq_status_t launch_gemm_simt(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, cudaStream_t s);
 // any shape: GEMV (M <= 8), tcgen05 GEMM, else the generic kernel (no PDL)

@@ -116,36 +116,6 @@ def test_gemm_row_magnitudes(cuda, wtype):
             assert ok, f"{mode} row {m}: {msg}"
 
 
-def test_dequant_path_opt_in(cuda):
-    """KQ_GEMM_PATH=dequant (fp16-dequantised operands, tcgen05 kind::f16), in a
-    child process. Its fp16 operand rounding gives rel-L2 ~3e-4 against the
-    exact per-block result: it meets the rel-L2 <= 1e-3 bar, not the
-    per-element one, which is why it is not the default."""
-    import os
-    import subprocess
-    import sys
-    code = (
-        "import sys, numpy as np, torch; sys.path[:0] = %r\n"
-        "import kq; from oracle import quant as Q\n"
-        "for wt in ('q4_0', 'q4_1', 'q8_0'):\n"
-        "  for (M, N, K) in ((16, 256, 512), (129, 200, 512), (256, 384, 4096), (40, 256, 2304), (24, 64, 256)):\n"
-        "    rng = np.random.default_rng(M + N + K)\n"
-        "    w = Q.make_blocks(wt, rng, N, K); x = rng.standard_normal((M, K)).astype(np.float32)\n"
-        "    x[3] *= np.float32(1e-6); x[5] *= np.float32(1e3)\n"
-        "    for mode in ('f32', 'sum_x', 'sum_dq'):\n"
-        "      got = kq.gemm_f32act(torch.from_numpy(w).cuda(), torch.from_numpy(x).cuda(), M, N, K, wt, mode)\n"
-        "      ref = Q.gemm_f32act(wt, w, x, M, N, K, {'f32': Q.ACT_F32, 'sum_x': Q.SUM_X, 'sum_dq': Q.SUM_DQ}[mode])\n"
-        "      g = got.cpu().numpy().astype(np.float64)\n"
-        "      assert np.all(np.isfinite(g)), (wt, M, N, K, mode)\n"
-        "      for m in range(M):\n"
-        "        r = Q.rel_l2(g[m], ref[m])\n"
-        "        assert r <= 1e-3, (wt, M, N, K, mode, m, r)\n"
-        "print('ok')\n" % ([p for p in sys.path if p],))
-    env = dict(os.environ, KQ_GEMM_PATH="dequant")
-    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=900)
-    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
-
-
 def test_int8_path_opt_in(cuda):
     """KQ_GEMM_PATH=int8 (int8 tcgen05 MMA per 32-block, int32 block sums
     rescaled on the FP32 pipe), in a child process: the full parity bar on
