@@ -1,31 +1,40 @@
 """Benchmark of the quantized-inference hot path (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kq|reference] [--config 1]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kq|reference]
+                    [--config C] [--headline-only]
 
-Workload (default): BASELINE configuration 1, the q8_0 x q8_1 W8A8 GEMM
+Headline (`value`): BASELINE configuration 1, the q8_0 x q8_1 W8A8 GEMM
 M=512, N=11008, K=4096 with fp32 activations quantised on the fly. One step
 is one call of the operator (activation quantisation + GEMM) on one batch of
-synthetic, seeded input already resident in HBM. Other --config values
-(0: q4_0 GEMV, 2: q4_0 sweep point, 3: ragged q8_0-KV flash decode,
-4: grouped q4_0 MoE) measure the other operators of the path.
+synthetic, seeded input already resident in HBM.
+
+The same line carries, under "configs", one object per other BASELINE
+configuration, each measured the same way with its own ms_per_step,
+roofline, e2e and (1 GPU) cpu_baseline: configs[0] (q4_0 GEMV M=1 N=4096),
+configs[2] at M = 1, 16, 128 and 2048 (q4_0, N=14336, K=4096), configs[3]
+(ragged GQA flash decode over a q8_0 KV cache) and configs[4] (grouped q4_0
+MoE); under "ggml_cases" the GGML timings the reference ships for shapes of
+this path next to this build's time for the same call. --config C makes
+configuration C the headline alone (dev runs); --headline-only skips the rest.
 
 Timing: W untimed warm-up steps, then K steps bracketed by a barrier and
-torch.cuda.synchronize(), timed with CUDA events on the launching stream,
+torch.cuda.synchronize(), timed with CUDA events on the launching stream
+(CUDA-graph replays where the step holds no collective and no host read),
 max over ranks. Consecutive steps rotate through input sets whose combined
-size exceeds 2x the L2 cache, so every step reads its operands from HBM.
+size exceeds 2.5x the L2 cache, so every step reads its operands from HBM.
+Clocks are sampled with nvidia-smi during each timed region.
 
-Multi-GPU (torchrun, one rank per GPU): weak scaling of the N-sharded GEMM.
-Rank r holds the weight rows of output columns [r*N, (r+1)*N) of an
-[M, world*N] product; each timed step is the operator whose epilogue stores
-those columns into every rank's full-width output over NVLink (CUDA IPC peer
-mappings), plus a one-element NCCL all-reduce that orders the stores (eager,
-event-timed).
---config 3 (decode) shards whole sequences (no collective); --config 4 (MoE)
-runs expert-parallel with all-to-all dispatch and combine.
+Multi-GPU (torchrun, one rank per GPU), weak scaling: the GEMMs are
+N-sharded (rank r computes columns [r*N, (r+1)*N) of an [M, world*N]
+product; its epilogue stores them into every rank's full-width output over
+NVLink, then a one-element NCCL all-reduce orders the stores); the decode
+shards whole sequences (no collective); the MoE runs expert-parallel with
+all-to-all dispatch and combine.
 
 --impl reference times the reference's own CPU implementation of the same
-operator (kernelevalplus-main/include/gemm_reference.h gemm_w8a8_reference,
-built into oracle/_ref/libkqref.so) on the host cores, on rank 0 only.
+operators on the host cores, on rank 0 only (the C++ routines of
+kernelevalplus-main/include/gemm_reference.h built into oracle/_ref for the
+GEMMs and the MoE's expert GEMMs; the restated attention for the decode).
 """
 from __future__ import annotations
 
@@ -55,17 +64,26 @@ CONFIGS = {
     4: dict(kind="moe", T=4096, E=8, topk=2, H=4096, I=14336, act="sum_dq",
             workload="configs[4]: q4_0 MoE FFN, 8 experts top-2, T=4096 H=4096 I=14336"),
 }
+SWEEP_M = (1, 16, 128, 2048)  # configs[2]
+
+
+def sub_configs():
+    """(name, config) of every configuration reported beside the headline."""
+    yield "configs[0]", CONFIGS[0]
+    for M in SWEEP_M:
+        yield f"configs[2] M={M}", dict(CONFIGS[2], M=M, workload=f"configs[2]: q4_0 x q8_1 M={M} N=14336 K=4096")
+    yield "configs[3]", CONFIGS[3]
+    yield "configs[4]", CONFIGS[4]
 
 
 # DRAM traffic per launch of the dominant kernel (dram__bytes_read.sum +
-# dram__bytes_write.sum from one ncu capture; profiles/*.md give the commands).
-# Keys: (kernel, workload). Per-unit figures scale with the units a launch
-# processes (weight rows for the GEMV, token rows for the decode).
+# dram__bytes_write.sum from one ncu capture of that kernel and workload).
+# Per-unit entries scale with the units a launch processes (weight rows for
+# the GEMV, token rows for the decode).
 NCU_TRAFFIC = {
-    ("gemm_tc", "q8_0 M=512 N=11008 K=4096"): 51.29e6,     # profiles/gemm_tc_q8_0_m512_n11008_k4096.md
-    ("gemm_split", "q8_0 M=512 N=11008 K=4096"): 61.47e6,  # profiles/gemm_split_q8_0_m512_n11008_k4096.md
-    ("gemv", "q4_0 per weight row, K=4096"): 33.06e6 / 14336,  # profiles/gemv_q4_0_m1_n14336_k4096.md
-    ("fa_fast", "per token row, Hkv=8 D=128"): 319.06e6 / 139124,  # profiles/fa_fast_decode_b32_hkv8_d128.md
+    ("gemm_split", "q8_0 M=512 N=11008 K=4096"): 61.47e6,
+    ("gemv", "q4_0 per weight row, K=4096"): 33.06e6 / 14336,
+    ("fa_fast", "per token row, Hkv=8 D=128"): 327.5e6 / 139124,
 }
 
 
@@ -75,8 +93,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="kq", choices=["kq", "reference"])
-    ap.add_argument("--config", type=int, default=1)
+    ap.add_argument("--config", type=int, default=None, help="run configuration C alone as the headline")
     ap.add_argument("--M", type=int, default=None, help="override M for gemm configs")
+    ap.add_argument("--headline-only", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -91,6 +110,37 @@ def load_peaks():
         d = json.load(open(p))
         return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
     return 6650.0, 1590.0, "fallback"
+
+
+_INT8_PEAK = {}
+
+
+def int8_peak_tops() -> dict:
+    """Dense int8 tensor peak of this GPU, measured like the bf16 figure in
+    MEASURED_PEAKS.json: a library int8 GEMM (torch._int_mm, cuBLASLt) at
+    8192^3 in isolation, best of 10 after warm-up."""
+    import torch
+    if "v" not in _INT8_PEAK:
+        n = 8192
+        g = torch.Generator(device="cuda").manual_seed(3)
+        a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda", generator=g)
+        b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda", generator=g)
+        for _ in range(3):
+            torch._int_mm(a, b)
+        torch.cuda.synchronize()
+        best = float("inf")
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, b)
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        del a, b
+        torch.cuda.empty_cache()
+        _INT8_PEAK["v"] = {"tops": round(2.0 * n ** 3 / (best * 1e-3) / 1e12, 1),
+                           "how": "torch._int_mm int8 8192^3 (cuBLASLt), best of 10, CUDA events"}
+    return _INT8_PEAK["v"]
 
 
 class ClockSampler:
@@ -215,13 +265,9 @@ def graph_time_ms(step, steps: int, warmup: int, world: int, clocks=None) -> tup
     return max_over_ranks(ms, world), clk
 
 
-# ---------------------------------------------------------------------------
-# CPU baseline (reference C++ routines or the oracle port)
-# ---------------------------------------------------------------------------
-
 def eager_time_ms(step, steps: int, warmup: int, world: int, clocks=None) -> tuple[float, dict | None]:
     """Time `steps` eager calls of step(i) with CUDA events on the current
-    stream (used where a step holds a collective: no graph capture of NCCL)."""
+    stream (used where a step holds a collective or a host read)."""
     import torch
 
     for i in range(warmup):
@@ -244,6 +290,10 @@ def eager_time_ms(step, steps: int, warmup: int, world: int, clocks=None) -> tup
     clk = clocks.stop() if clocks else None
     return max_over_ranks(ms, world), clk
 
+
+# ---------------------------------------------------------------------------
+# CPU baseline (reference C++ routines or the oracle port)
+# ---------------------------------------------------------------------------
 
 def cpu_threads() -> int:
     try:
@@ -284,8 +334,15 @@ def cpu_gemm_baseline(cfg: dict, seconds: float = 12.0) -> dict:
         run(rows)
         dt = time.perf_counter() - t0
     ops = 2.0 * rows * N * K
-    return {"value": ops / dt / 1e12, "unit": "TOPS", "cores": threads, "kind": kind,
-            "sample": f"{rows} of {M} activation rows x N={N} x K={K} ({wt}), q8_1 quantise + GEMM, {dt:.2f} s"}
+    out = {"value": ops / dt / 1e12, "unit": "TOPS", "cores": threads, "kind": kind,
+           "sample": f"{rows} of {M} activation rows x N={N} x K={K} ({wt}), q8_1 quantise + GEMM, {dt:.2f} s"}
+    if gemm_metric(cfg, M)[2]:
+        # weight-streaming shapes: in the GPU line's unit, the algorithmic
+        # bytes of the rows sampled per second
+        nbytes = N * (K // 32) * (18 if wt == "q4_0" else 34) + rows * K * 4 + rows * N * 4
+        out["tops"] = out["value"]
+        out["value"], out["unit"] = nbytes / dt / 1e12, "TB/s"
+    return out
 
 
 def cpu_fa_baseline(cfg: dict, seconds: float = 10.0) -> dict:
@@ -293,7 +350,7 @@ def cpu_fa_baseline(cfg: dict, seconds: float = 10.0) -> dict:
     rng = np.random.default_rng(0)
     B, Hq, Hkv, D = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["D"]
     lens = rng.integers(cfg["Lmin"], cfg["Lmax"] + 1, size=B)
-    done, t_all, nseq = 0, 0.0, 0
+    t_all, nseq = 0.0, 0
     while t_all < seconds and nseq < B:
         L = int(lens[nseq])
         q = rng.standard_normal((1, Hq, D)).astype(np.float16)
@@ -355,24 +412,42 @@ def cpu_moe_baseline(cfg: dict, seconds: float = 12.0) -> dict:
                       f"W4A8 GEMMs, {dt:.2f} s"}
 
 
+def cpu_baseline(cfg: dict, seconds: float) -> dict:
+    if cfg["kind"] == "fa":
+        return cpu_fa_baseline(cfg, seconds)
+    if cfg["kind"] == "moe":
+        return cpu_moe_baseline(cfg, seconds)
+    return cpu_gemm_baseline(cfg, seconds)
+
+
 # ---------------------------------------------------------------------------
 # GPU arms
 # ---------------------------------------------------------------------------
 
-def bench_gemm(args, cfg, rank, world):
+def gemm_metric(cfg: dict, M: int) -> tuple[str, str, bool]:
+    """(metric, unit, hbm_bound) of a GEMM configuration: the weight-streaming
+    shapes (M <= 128) in HBM TB/s, the others in TOPS."""
+    wt = cfg["wtype"]
+    if M <= 128 and wt == "q4_0":
+        return f"q4_0 x q8_1 M={M} HBM TB/s", "TB/s", True
+    if wt == "q8_0":
+        return "W8A8 GEMM TOPS (q8_0 x q8_1)", "TOPS", False
+    return "W4A8 GEMM TOPS (q4_0 x q8_1)", "TOPS", False
+
+
+def bench_gemm(args, cfg, rank, world, *, steps, warmup, clocks_on=True):
     import torch
     import kq
-    from kq import _lib
+    from kq import _lib, harness, synth
 
-    M = args.M or cfg["M"]
+    M = args.M if (args.M and args.config is not None) else cfg["M"]
     N, K, wt = cfg["N"], cfg["K"], cfg["wtype"]
     dev = torch.device("cuda", torch.cuda.current_device())
     g = torch.Generator(device="cpu").manual_seed(1234 + rank)
     nb = K // 32
     bb = kq.BLOCK_BYTES[wt]
-    # synthetic weights drawn directly as blocks (configs[0]/[1] distributions)
-    from kq import synth
     rng = np.random.default_rng(1234 + rank)
+    # synthetic weights drawn directly as blocks (the configurations' distributions)
     w_host = synth.blocks(wt, rng, N, K)
     step_bytes = N * nb * bb + M * K * 4 + M * N * 4
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
@@ -383,7 +458,8 @@ def bench_gemm(args, cfg, rank, world):
     L = kq.lib()
     wtc = kq.WTYPES[wt]
     act_mode = kq.ACT_MODES[cfg["act"]]
-    clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    clocks = ClockSampler(torch.cuda.current_device()) if (rank == 0 and clocks_on) else None
+    sharded_t = None
     if world == 1:
         def step(i):
             j = i % nsets
@@ -391,7 +467,7 @@ def bench_gemm(args, cfg, rank, world):
             _lib.check(L.kq_gemm_f32act(wtc, ws[j].data_ptr(), xs[j].data_ptr(), outs[j].data_ptr(), M, N, K,
                                         act_mode, sp), "kq_gemm_f32act")
 
-        ms, clk = graph_time_ms(step, args.steps, args.warmup, world, clocks)
+        ms, clk = graph_time_ms(step, steps, warmup, world, clocks)
     else:
         # rank r holds output columns [r*N, (r+1)*N) of an [M, world*N] product
         # (its own weight shard); each step's epilogue stores its columns into
@@ -405,7 +481,7 @@ def bench_gemm(args, cfg, rank, world):
             sharded_t.weight = ws[j]
             sharded_t(xs[j])
 
-        ms, clk = eager_time_ms(step, args.steps, args.warmup, world, clocks)
+        ms, clk = eager_time_ms(step, steps, warmup, world, clocks)
     exchange = None
     if world > 1:
         # the same rank-local GEMM without the exchange (every rank's own
@@ -416,13 +492,20 @@ def bench_gemm(args, cfg, rank, world):
             _lib.check(L.kq_gemm_f32act(wtc, ws[j].data_ptr(), xs[j].data_ptr(), outs[j].data_ptr(), M, N, K,
                                         act_mode, sp), "kq_gemm_f32act")
 
-        lms, _ = graph_time_ms(lstep, args.steps, args.warmup, world)
-        exchange = {"local_ms_per_step": round(lms / args.steps, 5),
-                    "exchange_ms_per_step": round((ms - lms) / args.steps, 5),
+        lms, _ = graph_time_ms(lstep, steps, warmup, world)
+        exchange = {"local_ms_per_step": round(lms / steps, 5),
+                    "exchange_ms_per_step": round((ms - lms) / steps, 5),
+                    "exchange_share": round(max(0.0, ms - lms) / ms, 3),
                     "note": "step = rank-local GEMM + epilogue peer stores of its columns to every rank + "
                             "1-element all-reduce; the received bytes per rank grow as (world-1) x M x N x 4"}
+    per = ms / steps
     ops = 2.0 * M * N * K
-    value = world * ops * args.steps / (ms * 1e-3) / 1e12
+    metric, unit, hbm_bound = gemm_metric(cfg, M)
+    algo_bytes = N * nb * bb + M * K * 4 + M * N * 4   # weights + fp32 activations + fp32 output
+    if hbm_bound:
+        value = world * algo_bytes / (per * 1e-3) / 1e12
+    else:
+        value = world * ops / (per * 1e-3) / 1e12
 
     # ---- dominant kernel alone (the GEMM on pre-staged activations) ----
     qs = [torch.empty((M, K), dtype=torch.int8, device=dev) for _ in range(nsets)]
@@ -432,6 +515,7 @@ def bench_gemm(args, cfg, rank, world):
         dss[j].copy_(torch.stack([a8[:, :, 0:2].contiguous().view(torch.float16).float().squeeze(-1),
                                   a8[:, :, 2:4].contiguous().view(torch.float16).float().squeeze(-1)], dim=-1))
         qs[j].copy_(a8[:, :, 4:].contiguous().view(torch.int8).reshape(M, K))
+        del a8
 
     def kstep(i):
         j = i % nsets
@@ -439,20 +523,21 @@ def bench_gemm(args, cfg, rank, world):
         _lib.check(L.kq_mul_mat_q8x(wtc, ws[j].data_ptr(), qs[j].data_ptr(), dss[j].data_ptr(), outs[j].data_ptr(),
                                     M, N, K, sp), "kq_mul_mat_q8x")
 
-    kms, _ = graph_time_ms(kstep, args.steps, 3, world)
-    kms /= args.steps
-    stream = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    kms, _ = graph_time_ms(kstep, steps, 3, world)
+    kms /= steps
+    del qs, dss
 
     # ---- end to end through the public API with host buffers ----
-    # world > 1: kq.dist.NShardedGemm (local GEMM + all-gather), full
-    # [M, world*N] output read back on every rank.
+    # world > 1: kq.dist.NShardedGemm; every rank reads back its own column
+    # block (together one copy of the [M, world*N] output).
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     from kq import dist as kd
     NT = world * N
     sharded = (kd.NShardedGemm(ws[0], NT, K, wtype=wt, act_mode=cfg["act"], align=N, mode="p2p")
                if world > 1 else None)
     xh = [torch.randn((M, K), generator=g, dtype=torch.float32).pin_memory() for _ in range(2)]
-    oh = [torch.empty((M, NT), dtype=torch.float32).pin_memory() for _ in range(2)]
+    oh = [torch.empty((M, N), dtype=torch.float32).pin_memory() for _ in range(2)]
     # two device input/output buffers: step i's host->device copy (copy
     # stream), GEMM (compute stream) and device->host read-back (second copy
     # stream) are ordered by events, so copies of neighbouring steps overlap
@@ -464,6 +549,7 @@ def bench_gemm(args, cfg, rank, world):
     ev_c = [torch.cuda.Event() for _ in range(2)]
     ev_out = [torch.cuda.Event() for _ in range(2)]
     ev_start = torch.cuda.Event()
+    c0 = rank * N
 
     def estep(i):
         j, b = i % nsets, i % 2
@@ -482,7 +568,7 @@ def bench_gemm(args, cfg, rank, world):
         ev_c[b].record(stream)
         with torch.cuda.stream(s_out):
             s_out.wait_event(ev_c[b])
-            oh[b].copy_(od[b], non_blocking=True)
+            oh[b].copy_(od[b][:, c0:c0 + N], non_blocking=True)
             ev_out[b].record(s_out)
 
     ev_start.record(stream)
@@ -494,7 +580,7 @@ def bench_gemm(args, cfg, rank, world):
     barrier(world)
     e0.record(stream)
     ev_start.record(stream)
-    for i in range(args.steps):
+    for i in range(steps):
         estep(i)
     stream.wait_event(ev_out[0])
     stream.wait_event(ev_out[1])
@@ -504,58 +590,79 @@ def bench_gemm(args, cfg, rank, world):
     if world > 1:  # collective teardown of the peer-mapped outputs (same order on every rank)
         sharded_t.close()
         sharded.close()
-    e2e = {"value": world * ops * args.steps / (ems * 1e-3) / 1e12, "unit": "TOPS",
-           "h2d_bytes_per_step": M * K * 4, "d2h_bytes_per_step": M * NT * 4,
-           "api": "kq.gemm_f32act" if world == 1 else "kq.dist.NShardedGemm"}
+    eper = ems / steps
+    e2e_value = world * (algo_bytes if hbm_bound else ops) / (eper * 1e-3) / 1e12
+    e2e = {"value": round(e2e_value, 4), "unit": unit,
+           "h2d_bytes_per_step": M * K * 4, "d2h_bytes_per_step": M * N * 4,
+           "api": "kq.gemm_f32act" if world == 1 else "kq.dist.NShardedGemm (own column block read back)"}
 
     hbm, bf16, src = load_peaks()
-    kernel_bytes = N * nb * bb + M * K + M * nb * 8 + M * N * 4
+    staged_bytes = N * nb * bb + M * K + M * nb * 8 + M * N * 4
     if M <= 8:
-        achieved = kernel_bytes / (kms * 1e-3) / 1e9
+        achieved = staged_bytes / (kms * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(achieved / hbm, 4),
                 "traffic": (round(NCU_TRAFFIC[("gemv", "q4_0 per weight row, K=4096")] * N)
                             if (wt == "q4_0" and K == 4096) else None),
-                "kernel": "gemv_kernel", "peak_source": f"{src} hbm_gbs (copy)"}
+                "kernel": "gemv_kernel", "algorithmic_bytes": staged_bytes, "peak_source": f"{src} hbm_gbs (copy)"}
+    elif hbm_bound:
+        achieved = staged_bytes / (kms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(achieved / hbm, 4), "traffic": None,
+                "kernel": "gemm_split_kernel (+ split_act_kernel prep)", "algorithmic_bytes": staged_bytes,
+                "tops": round(ops / (kms * 1e-3) / 1e12, 2), "peak_source": f"{src} hbm_gbs (copy)"}
     else:
         # gemm_split_kernel: exact split-fp16 operands, three kind::f16 MMAs
         # per product (A_hi W_hi, A_lo W_hi, A_hi W_lo); the f16 dense rate
         # is the bf16 one
         achieved = ops / (kms * 1e-3) / 1e12
-        peak = bf16
-        roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
-                "frac": round(achieved / peak, 4),
-                "executed_frac": round(3.0 * achieved / peak, 4),
+        i8 = int8_peak_tops()
+        roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(bf16, 1), "unit": "TFLOP/s",
+                "frac": round(achieved / bf16, 4),
+                "executed_frac": round(3.0 * achieved / bf16, 4),
+                "int8_peak": i8["tops"], "frac_of_int8_peak": round(achieved / i8["tops"], 4),
                 "traffic": NCU_TRAFFIC.get(("gemm_split", f"{wt} M={M} N={N} K={K}")),
                 "kernel": "gemm_split_kernel (+ split_act_kernel prep)",
                 "peak_source": f"f16 dense = {src} bf16_tflops (cuBLAS bf16 burst); achieved counts the "
-                               f"algorithmic 2MNK, executed_frac the 3 f16 MMAs per product"}
+                               f"algorithmic 2MNK, executed_frac the 3 f16 MMAs per product; int8_peak: "
+                               f"{i8['how']}"}
     launches_per_step = 2 if M <= 8 else 3  # quantiser + GEMV | quantiser + split prep + split GEMM
     line = {
-        "metric": "W8A8 GEMM TOPS (q8_0 x q8_1)" if wt == "q8_0" else "W4A8 GEMM TOPS (q4_0 x q8_1)",
-        "value": round(value, 3), "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
+        "metric": metric, "value": round(value, 4), "unit": unit, "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": round(per, 5), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8" if M <= 8 else "f16 (exact split of the int8 x int8 block products)",
         "data": "synthetic (seeded; weights drawn directly as q-blocks)",
         "config": {"workload": cfg["workload"], "M": M, "N": N, "K": K, "wtype": wt, "act_quant": cfg["act"],
-                   "l2": f"{nsets} rotating input sets ({nsets * step_bytes / 1e6:.0f} MB > 2x L2)",
+                   "l2": f"{nsets} rotating input sets ({nsets * step_bytes / 1e6:.0f} MB > 2.5x L2)",
                    "parallelism": ("single GPU" if world == 1 else
                                    f"N-sharded x{world}: rank r computes columns [r*N, (r+1)*N) of an "
                                    f"[M, {world}*N] product; its epilogue stores them into every rank's "
                                    f"output over NVLink (CUDA IPC), then a 1-element NCCL all-reduce")},
         "roofline": roof,
         "e2e": e2e,
-        "gpu_launches": launches_per_step * args.steps,
+        "gpu_launches": launches_per_step * steps,
         "kernel_ms": round(kms, 5),
     }
+    if hbm_bound:
+        line["tops"] = round(world * ops / (per * 1e-3) / 1e12, 3)
+    ggml = harness.ggml_gemm_us(wt, M, N, K)
+    if ggml is not None and world == 1:
+        # GGML's published time for the same call on other GPUs; vs_baseline =
+        # this step's throughput / GGML's H800 throughput on the same workload
+        line["ggml_us"] = ggml
+        line["vs_baseline"] = round(ggml["H800"] / (per * 1e3), 3)
+        line["vs_baseline_source"] = ("GGML H800, kernelevalplus-main/data/baseline/baseline_data_compact.json "
+                                      f"case {harness.quant_gemm_baseline_case(wt, M, N, K)}")
     if exchange is not None:
         line["exchange"] = exchange
     if clk is not None:
         line["clocks"] = clk
+    del ws, xs, outs
+    torch.cuda.empty_cache()
     return line
 
 
-def bench_fa(args, cfg, rank, world):
+def bench_fa(args, cfg, rank, world, *, steps, warmup, clocks_on=True):
     import torch
     import kq
 
@@ -591,10 +698,10 @@ def bench_fa(args, cfg, rank, world):
         j = i % nsets
         kq.flash_decode_ragged(q, ks[j], vs[j], cud, Hkv, maxlen, out=out)
 
-    clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
-    ms, clk = graph_time_ms(step, args.steps, args.warmup, world, clocks)
-    value = world * B0 * args.steps / (ms * 1e-3)
-    per = ms / args.steps
+    clocks = ClockSampler(torch.cuda.current_device()) if (rank == 0 and clocks_on) else None
+    ms, clk = graph_time_ms(step, steps, warmup, world, clocks)
+    value = world * B0 * steps / (ms * 1e-3)
+    per = ms / steps
     # ---- end to end through the public API: each step's queries in from
     # pinned host memory and its outputs back (the KV cache stays resident,
     # as it does across decode steps)
@@ -615,12 +722,12 @@ def bench_fa(args, cfg, rank, world):
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(args.steps):
+    for i in range(steps):
         estep(i)
     e1.record(stream)
     torch.cuda.synchronize()
     ems = max_over_ranks(e0.elapsed_time(e1), world)
-    e2e = {"value": round(world * B0 * args.steps / (ems * 1e-3), 1), "unit": "tok/s",
+    e2e = {"value": round(world * B0 * steps / (ems * 1e-3), 1), "unit": "tok/s",
            "h2d_bytes_per_step": B * Hq * D * 2, "d2h_bytes_per_step": B * Hq * D * 2,
            "api": "kq.flash_decode_ragged"}
     hbm, _, src = load_peaks()
@@ -628,27 +735,29 @@ def bench_fa(args, cfg, rank, world):
     achieved = algo / (per * 1e-3) / 1e9
     line = {
         "metric": "q8_0-KV flash-decode tok/s", "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per, 5), "higher_is_better": True,
+        "steps": steps, "warmup": warmup, "ms_per_step": round(per, 5), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp32", "data": "synthetic (seeded)",
         "config": {"workload": cfg["workload"], "sum_L": T, "l2": f"{nsets} rotating KV caches",
                    "parallelism": "single GPU" if world == 1 else
                    f"{world * B0} sequences over {world} ranks (kq.dist.plan_decode), no collective; "
                    f"rank loads {plan.load()}"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(achieved / hbm, 4),
+                     "frac": round(achieved / hbm, 4), "algorithmic_bytes": algo,
                      "traffic": round(NCU_TRAFFIC[("fa_fast", "per token row, Hkv=8 D=128")] * T)
                      if (Hkv == 8 and D == 128) else None,
-                     "kernel": "fa decode (partial+combine)",
+                     "kernel": "fa decode (partial + combine), timed together",
                      "peak_source": f"{src} hbm_gbs"},
         "e2e": e2e,
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": 2 * steps,
     }
     if clk is not None:
         line["clocks"] = clk
+    del ks, vs
+    torch.cuda.empty_cache()
     return line
 
 
-def bench_moe(args, cfg, rank, world):
+def bench_moe(args, cfg, rank, world, *, steps, warmup, clocks_on=True):
     import torch
     import kq
     from kq import synth
@@ -677,28 +786,14 @@ def bench_moe(args, cfg, rank, world):
         else:
             kd.moe_expert_parallel(x, logits, wg, wu, wd, E, topk, cfg["act"])
 
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize()
-    clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
-    if clocks:
-        clocks.start()
-        time.sleep(0.3)
-    barrier(world)
-    stream = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(args.steps):
-        step(i)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms = max_over_ranks(e0.elapsed_time(e1), world)
-    clk = clocks.stop() if clocks else None
+    clocks = ClockSampler(torch.cuda.current_device()) if (rank == 0 and clocks_on) else None
+    ms, clk = eager_time_ms(step, steps, warmup, world, clocks)
     ops = 2.0 * (T * topk) * (2 * H * I + I * H)
-    value = world * ops * args.steps / (ms * 1e-3) / 1e12
+    value = world * ops * steps / (ms * 1e-3) / 1e12
 
     # ---- end to end through the public API: tokens and router logits in from
     # pinned host memory, the combined outputs back, every step
+    stream = torch.cuda.current_stream()
     xh = [torch.randn((T, H), generator=g).pin_memory() for _ in range(2)]
     lh = [torch.randn((T, E), generator=g).pin_memory() for _ in range(2)]
     oh = [torch.empty((T, H), dtype=torch.float32).pin_memory() for _ in range(2)]
@@ -724,7 +819,7 @@ def bench_moe(args, cfg, rank, world):
         stream.wait_event(ev_in[b])
         stream.wait_event(ev_out[b])
         if world == 1:
-            y = kq.moe_q4_0(xd[b], ld[b], wg, wu, wd, topk, cfg["act"], out=od[b])
+            kq.moe_q4_0(xd[b], ld[b], wg, wu, wd, topk, cfg["act"], out=od[b])
         else:
             y = kd.moe_expert_parallel(xd[b], ld[b], wg, wu, wd, E, topk, cfg["act"])
             od[b].copy_(y)
@@ -734,6 +829,7 @@ def bench_moe(args, cfg, rank, world):
             oh[b].copy_(od[b], non_blocking=True)
             ev_out[b].record(s_out)
 
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev_start.record(stream)
     for i in range(2):
         estep(i)
@@ -743,20 +839,21 @@ def bench_moe(args, cfg, rank, world):
     barrier(world)
     e0.record(stream)
     ev_start.record(stream)
-    for i in range(args.steps):
+    for i in range(steps):
         estep(i)
     stream.wait_event(ev_out[0])
     stream.wait_event(ev_out[1])
     e1.record(stream)
     torch.cuda.synchronize()
     ems = max_over_ranks(e0.elapsed_time(e1), world)
-    e2e = {"value": round(world * ops * args.steps / (ems * 1e-3) / 1e12, 3), "unit": "TOPS",
+    e2e = {"value": round(world * ops * steps / (ems * 1e-3) / 1e12, 3), "unit": "TOPS",
            "h2d_bytes_per_step": T * H * 4 + T * E * 4, "d2h_bytes_per_step": T * H * 4,
            "api": "kq.moe_q4_0" if world == 1 else "kq.dist.moe_expert_parallel"}
     _, bf16, src = load_peaks()
+    i8 = int8_peak_tops()
     line = {
         "metric": "MoE W4A8 GEMM TOPS (q4_0 x q8_1, grouped)", "value": round(value, 3), "unit": "TOPS",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+        "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": round(ms / steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f16 (exact split of the int8 x int8 block products)",
         "data": "synthetic (seeded; weights drawn directly as q4_0 blocks)",
@@ -767,19 +864,97 @@ def bench_moe(args, cfg, rank, world):
                    "NCCL all-to-all dispatch and combine"},
         "roofline": {"bound": "tensor", "achieved": round(value / world, 2), "peak": round(bf16, 1),
                      "unit": "TFLOP/s", "frac": round(value / world / bf16, 4),
-                     "executed_frac": round(3.0 * value / world / bf16, 4), "traffic": None,
+                     "executed_frac": round(3.0 * value / world / bf16, 4),
+                     "int8_peak": i8["tops"], "frac_of_int8_peak": round(value / world / i8["tops"], 4),
+                     "traffic": None,
                      "kernel": "whole MoE step (route + 24 expert GEMMs on gemm_split_kernel + SiLU + combine)",
-                     "peak_source": f"f16 dense = {src} bf16_tflops; the expert GEMMs run 3 f16 MMAs per product"},
+                     "peak_source": f"f16 dense = {src} bf16_tflops; the expert GEMMs run 3 f16 MMAs per product; "
+                                    f"int8_peak: {i8['how']}"},
         "e2e": e2e,
         # expert GEMMs are two launches each (operand prep + GEMM)
-        "gpu_launches": ((5 + 6 * E) if world == 1 else (7 + 6 * per)) * args.steps,
+        "gpu_launches": ((5 + 6 * E) if world == 1 else (7 + 6 * per)) * steps,
     }
     if clk is not None:
         line["clocks"] = clk
+    del wg, wu, wd
+    torch.cuda.empty_cache()
     return line
 
 
-def reference_arm(args, cfg):
+# GGML flash-attention timings the reference ships (Llama3-8B, q8_0 KV,
+# H = 32, D = 128; kernelevalplus-main/data/baseline/flash_attn_baseline.json
+# entries at lines 422, 662, 702, 802, 822; RTX 4090 only). GGML's nb = the
+# number of queries sharing the cache, the harness's batch.
+GGML_FA_US = {(512, 1): 7.64, (4096, 8): 62.64, (8192, 1): 28.74, (8192, 8): 99.37, (8192, 512): 491.79}
+
+
+def bench_ggml_cases(steps: int) -> dict:
+    """This build's device time for the shapes GGML's baseline tables list,
+    beside GGML's published times (other GPUs; there are no B200 entries)."""
+    import torch
+    import kq
+    from kq import harness, synth
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    gemm, fa = [], []
+    for case, hw in harness.GGML_GEMM_US.items():
+        wt = "q4_0" if "_q4_0_" in case else "q8_0"
+        dims = {p[0]: int(p[1:]) for p in case.split("_")[-3:]}  # GGML m = our N, n = our M
+        N, M, K = dims["m"], dims["n"], dims["k"]
+        nb = K // 32
+        step_bytes = N * nb * kq.BLOCK_BYTES[wt] + M * K * 4 + M * N * 4
+        nsets = max(2, int(np.ceil(2.5 * l2 / step_bytes)))
+        rng = np.random.default_rng(11)
+        w = torch.from_numpy(synth.blocks(wt, rng, N, K)).to(dev)
+        ws = [w.clone() for _ in range(nsets)]
+        xs = [torch.randn((M, K), device=dev) for _ in range(nsets)]
+        os_ = [torch.empty((M, N), device=dev) for _ in range(nsets)]
+
+        def step(i):
+            j = i % nsets
+            kq.gemm_f32act(ws[j], xs[j], M, N, K, wt, "sum_x", out=os_[j])
+
+        ms, _ = graph_time_ms(step, steps, 3, 1)
+        us = ms / steps * 1e3
+        gemm.append({"case": case, "M": M, "N": N, "K": K, "wtype": wt, "ours_us": round(us, 2), "ggml_us": hw,
+                     "speedup_vs": {k: round(v / us, 2) for k, v in hw.items()}})
+        del ws, xs, os_, w
+    H, D = 32, 128
+    for (S, B), us_ggml in GGML_FA_US.items():
+        g = torch.Generator(device=dev).manual_seed(S + B)
+        nsets = max(2, int(np.ceil(2.5 * l2 / (2 * S * H * 4 * 34))))
+        ks = [kq.quantize_rows(torch.randn((S * H, D), generator=g, device=dev), "q8_0") for _ in range(nsets)]
+        vs = [kq.quantize_rows(torch.randn((S * H, D), generator=g, device=dev), "q8_0") for _ in range(nsets)]
+        q = torch.randn((B, H, D), generator=g, device=dev)
+
+        def fstep(i):
+            j = i % nsets
+            kq.flash_attn(q, ks[j], vs[j], B, S, H, D, "q8_0")
+
+        ms, _ = graph_time_ms(fstep, steps, 3, 1)
+        us = ms / steps * 1e3
+        fa.append({"cache": S, "batch": B, "ours_us": round(us, 2), "ggml_us": {"RTX4090": us_ggml},
+                   "speedup_vs": {"RTX4090": round(us_ggml / us, 2)}})
+        del ks, vs
+    torch.cuda.empty_cache()
+    return {"quant_gemm": gemm, "flash_attention_q8_0": fa,
+            "source": "kernelevalplus-main/data/baseline/baseline_data_compact.json, flash_attn_baseline.json "
+                      "(GGML / llama.cpp; no B200 entries); ours: CUDA-graph device time per call, act mode sum_x"}
+
+
+def run_config(args, cfg, rank, world, *, steps, warmup):
+    if cfg["kind"] == "fa":
+        return bench_fa(args, cfg, rank, world, steps=steps, warmup=warmup)
+    if cfg["kind"] == "moe":
+        return bench_moe(args, cfg, rank, world, steps=steps, warmup=warmup)
+    return bench_gemm(args, cfg, rank, world, steps=steps, warmup=warmup)
+
+
+_SUB_DROP = ("n_gpus", "steps", "warmup", "scaling", "data")
+
+
+def reference_arm(args, cfg, subs: bool):
     """The reference's CPU implementation of the same operator, all host threads.
     Each step is a bounded sample of the workload (a slice of activation rows)
     so that the whole --warmup W --steps K run ends within a few minutes."""
@@ -787,32 +962,21 @@ def reference_arm(args, cfg):
     if rank != 0:
         return None
     budget = min(2.0, 120.0 / max(1, args.warmup + args.steps))
+    vals, cb = [], None
+    for i in range(args.warmup + args.steps):
+        cb = cpu_baseline(cfg, budget)
+        if i >= args.warmup:
+            vals.append(cb["value"])
     if cfg["kind"] == "fa":
-        vals, cb = [], None
-        for i in range(args.warmup + args.steps):
-            cb = cpu_fa_baseline(cfg, seconds=budget)
-            if i >= args.warmup:
-                vals.append(cb["value"])
         unit, metric = "tok/s", "q8_0-KV flash-decode tok/s"
     elif cfg["kind"] == "moe":
-        vals, cb = [], None
-        for i in range(args.warmup + args.steps):
-            cb = cpu_moe_baseline(cfg, seconds=budget)
-            if i >= args.warmup:
-                vals.append(cb["value"])
         unit, metric = "TOPS", "MoE W4A8 GEMM TOPS (q4_0 x q8_1, grouped)"
     else:
-        vals, cb = [], None
-        for i in range(args.warmup + args.steps):
-            cb = cpu_gemm_baseline(cfg, seconds=budget)
-            if i >= args.warmup:
-                vals.append(cb["value"])
-        unit = "TOPS"
-        metric = "W8A8 GEMM TOPS (q8_0 x q8_1)" if cfg["wtype"] == "q8_0" else "W4A8 GEMM TOPS (q4_0 x q8_1)"
+        metric, unit, _ = gemm_metric(cfg, cfg["M"])
     value = float(np.median(vals)) if vals else cb["value"]
     cb = dict(cb)
     cb["value"] = value
-    return {
+    line = {
         "impl": "reference", "metric": metric, "value": round(value, 6), "unit": unit, "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded)",
@@ -820,13 +984,21 @@ def reference_arm(args, cfg):
         "cpu_baseline": cb,
         "e2e": {"value": round(value, 6), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if subs:
+        # one bounded sample per other configuration (the GPU line's "configs")
+        line["configs"] = {}
+        for name, c in sub_configs():
+            s = cpu_baseline(c, 3.0)
+            line["configs"][name] = {"value": s["value"], "unit": s["unit"], "cpu_baseline": s}
+    return line
 
 
 def main():
     args = parse()
-    cfg = CONFIGS[args.config]
+    cfg = CONFIGS[1 if args.config is None else args.config]
+    subs = args.config is None and not args.headline_only
     if args.impl == "reference":
-        line = reference_arm(args, cfg)
+        line = reference_arm(args, cfg, subs)
         if line is not None:
             print(json.dumps(line), flush=True)
         return
@@ -834,17 +1006,18 @@ def main():
     if not torch.cuda.is_available():
         raise SystemExit("bench.py needs a CUDA device (the kernels have no CPU path)")
     rank, world, _ = dist_setup(args.gpus)
-    if cfg["kind"] == "fa":
-        line = bench_fa(args, cfg, rank, world)
-        cpu = (lambda: cpu_fa_baseline(cfg)) if (rank == 0 and world == 1) else None
-    elif cfg["kind"] == "moe":
-        line = bench_moe(args, cfg, rank, world)
-        cpu = (lambda: cpu_moe_baseline(cfg)) if (rank == 0 and world == 1) else None
-    else:
-        line = bench_gemm(args, cfg, rank, world)
-        cpu = (lambda: cpu_gemm_baseline(cfg)) if (rank == 0 and world == 1) else None
-    if cpu is not None and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu()
+    line = run_config(args, cfg, rank, world, steps=args.steps, warmup=args.warmup)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg, 12.0)
+    if subs:
+        line["configs"] = {}
+        for name, c in sub_configs():
+            sub = run_config(args, c, rank, world, steps=args.steps, warmup=min(args.warmup, 3))
+            if rank == 0 and world == 1 and not args.no_cpu_baseline:
+                sub["cpu_baseline"] = cpu_baseline(c, 4.0)
+            line["configs"][name] = {k: v for k, v in sub.items() if k not in _SUB_DROP}
+        if world == 1:
+            line["ggml_cases"] = bench_ggml_cases(args.steps)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -96,6 +96,28 @@ def quant_gemm_baseline_case(weight_dtype: str, M: int, N: int, K: int, activati
     return f"w{4 if 'q4' in wt else 8}a32c8_{wt}_{activation.replace('float', 'f')}_m{N}_n{M}_k{K}"
 
 
+# GGML (llama.cpp) timings the reference ships as its quant_gemm baseline,
+# microseconds per run, for the cases that share a shape with the benchmark
+# configurations (kernelevalplus-main/data/baseline/baseline_data_compact.json:
+# entries at lines 2, 41, 15346, 18407, 1996, 20362, 20401; GGML's m is our N
+# and its n our M). There are no B200 entries.
+GGML_GEMM_US = {
+    "w4a32c8_q4_0_f32_m4096_n1_k4096": {"H800": 8.83, "A100": 13.2, "RTX4090": 6.77},
+    "w4a32c8_q4_0_f32_m14336_n1_k4096": {"H800": 19.57, "A100": 30.08, "RTX4090": 14.26},
+    "w4a32c8_q4_0_f32_m14336_n8_k4096": {"H800": 42.8, "A100": 69.44, "RTX4090": 47.09},
+    "w4a32c8_q4_0_f32_m14336_n512_k4096": {"H800": 325.27, "A100": 718.44, "RTX4090": 266.66},
+    "w8a32c8_q8_0_f32_m4096_n1_k4096": {"H800": 10.35},
+    "w8a32c8_q8_0_f32_m4096_n512_k4096": {"H800": 106.13, "A100": 235.47, "RTX4090": 77.58},
+    "w8a32c8_q8_0_f32_m14336_n512_k4096": {"H800": 320.25, "A100": 743.74, "RTX4090": 291.89},
+}
+
+
+def ggml_gemm_us(weight_dtype: str, M: int, N: int, K: int) -> dict | None:
+    """GGML's published time per run (us, by GPU) for a quant_gemm call with
+    fp32 activations, or None when the baseline data has no such case."""
+    return GGML_GEMM_US.get(quant_gemm_baseline_case(weight_dtype, M, N, K))
+
+
 def definition_test_configs(spec: dict) -> list[dict]:
     """The test configurations a definition lists itself. The harness's
     quant_gemm handler ignores them and always runs M = 1, 8, 512
