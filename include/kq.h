@@ -259,6 +259,17 @@ kq_status_t kq_moe_experts_q4_0(const float* x_rows, const int32_t* expert_of_ro
                                 const void* w_up, const void* w_down, int E, int P, int H, int I, int act_mode,
                                 float* y_rows, kq_stream_t stream);
 
+/* Parity debugging: kq_moe_experts_q4_0 that also writes the pipeline's own
+ * intermediates in the input row order: gate = x W_gate^T and up = x W_up^T
+ * fp32 [P, I], h = silu(gate) * up fp32 [P, I] exactly as the quantiser forms
+ * it, and h's quantised codes h_qs int8 [P, I] with (d, s) fp32 pairs
+ * h_ds [P, I/32, 2] (the down projection's input). All buffers 16-byte
+ * aligned. No reference counterpart (the reference has no MoE operator). */
+kq_status_t kq_moe_experts_stages_q4_0(const float* x_rows, const int32_t* expert_of_row, const void* w_gate,
+                                       const void* w_up, const void* w_down, int E, int P, int H, int I, int act_mode,
+                                       float* gate, float* up, float* h, int8_t* h_qs, float* h_ds, float* y_rows,
+                                       kq_stream_t stream);
+
 /* out[t] = sum_k wts[t, k] * y[t * topk + k]  (fp32, slots in order k = 0..topk-1). */
 kq_status_t kq_moe_combine(const float* y, const float* wts, int T, int topk, int H, float* out, kq_stream_t stream);
 

@@ -154,32 +154,37 @@ kq_status_t check_gemm_args(int wtype, const void* w, const void* a, const float
 }
 
 // Quantised activations are staged; choose the GEMM kernel for the shape.
-// M > 8 path: the exact split-fp16 tcgen05 kernel by default;
-// KQ_GEMM_PATH=int8 selects the int8 tcgen05 kernel (per-block int32 sums
-// rescaled on the FP32 pipe). Read once per process.
-enum class GemmPath { kSplit, kInt8 };
+// M > 8 path: the skinny int8 kernel (weights streamed once) for M <= 128,
+// the exact split-fp16 tcgen05 kernel above; KQ_GEMM_PATH=split runs the
+// split kernel for every M > 8, KQ_GEMM_PATH=int8 the int8 tcgen05 kernel
+// (per-block int32 sums rescaled on the FP32 pipe). Read once per process.
+enum class GemmPath { kDefault, kSplit, kInt8 };
 GemmPath gemm_path() {
   static const GemmPath p = [] {
     const char* e = std::getenv("KQ_GEMM_PATH");
     if (e && std::string(e) == "int8") return GemmPath::kInt8;
-    return GemmPath::kSplit;
+    if (e && std::string(e) == "split") return GemmPath::kSplit;
+    return GemmPath::kDefault;
   }();
   return p;
 }
 
 // The tensor-core kernel for M > 8 with the given output destinations, or
-// KQ_ERR_UNSUPPORTED when neither fits the shape.
+// KQ_ERR_UNSUPPORTED when none fits the shape.
 kq_status_t dispatch_gemm_tc(int wtype, const void* w, Act8 act, const OutSpec& out, int M, int N, int K,
                              cudaStream_t s, bool pdl) {
   const GemmPath path = gemm_path();
-  if (path == GemmPath::kSplit && gemm_split_supported(wtype, M, N, K, w, act))
+  if (path == GemmPath::kDefault && gemm_skinny_supported(wtype, M, N, K, w, act))
+    return launch_gemm_skinny(wtype, w, act, out, M, N, K, s);
+  if (path != GemmPath::kInt8 && gemm_split_supported(wtype, M, N, K, w, act))
     return launch_gemm_split(wtype, w, act, out, M, N, K, s);
   if (gemm_tc_supported(wtype, M, N, K, w, act)) return launch_gemm_tc(wtype, w, act, out, M, N, K, pdl, s);
   return fail(KQ_ERR_UNSUPPORTED, "no tensor-core GEMM for M=%d N=%d K=%d", M, N, K);
 }
 
 bool gemm_tc_any_supported(int wtype, int M, int N, int K, const void* w, Act8 act) {
-  return (gemm_path() == GemmPath::kSplit && gemm_split_supported(wtype, M, N, K, w, act)) ||
+  return (gemm_path() == GemmPath::kDefault && gemm_skinny_supported(wtype, M, N, K, w, act)) ||
+         (gemm_path() != GemmPath::kInt8 && gemm_split_supported(wtype, M, N, K, w, act)) ||
          gemm_tc_supported(wtype, M, N, K, w, act);
 }
 
@@ -443,6 +448,24 @@ kq_status_t kq_moe_experts_q4_0(const float* x_rows, const int32_t* expert_of_ro
   if (!aligned(x_rows, 16) || !aligned(y_rows, 16)) return fail(KQ_ERR_INVALID, "moe experts: rows must be 16-byte aligned");
   return launch_moe_experts_q4_0(x_rows, expert_of_row, w_gate, w_up, w_down, E, P, H, I, act_mode, y_rows,
                                  static_cast<cudaStream_t>(stream));
+}
+
+kq_status_t kq_moe_experts_stages_q4_0(const float* x_rows, const int32_t* expert_of_row, const void* w_gate,
+                                       const void* w_up, const void* w_down, int E, int P, int H, int I, int act_mode,
+                                       float* gate, float* up, float* h, int8_t* h_qs, float* h_ds, float* y_rows,
+                                       kq_stream_t stream) {
+  if (P < 0 || H <= 0 || I <= 0 || H % 32 || I % 32)
+    return fail(KQ_ERR_INVALID, "moe stages: bad shape P=%d H=%d I=%d", P, H, I);
+  if (act_mode < KQ_ACT_SUM_X || act_mode > KQ_ACT_F32) return fail(KQ_ERR_INVALID, "unknown activation mode %d", act_mode);
+  if (P == 0) return KQ_OK;
+  if (!x_rows || !expert_of_row || !w_gate || !w_up || !w_down || !y_rows || !gate || !up || !h || !h_qs || !h_ds)
+    return fail(KQ_ERR_INVALID, "moe stages: null pointer");
+  for (const void* p : {(const void*)x_rows, (const void*)y_rows, (const void*)gate, (const void*)up, (const void*)h,
+                        (const void*)h_qs, (const void*)h_ds})
+    if (!aligned(p, 16)) return fail(KQ_ERR_INVALID, "moe stages: buffers must be 16-byte aligned");
+  MoeStages st{gate, up, h, h_qs, h_ds};
+  return launch_moe_experts_q4_0(x_rows, expert_of_row, w_gate, w_up, w_down, E, P, H, I, act_mode, y_rows,
+                                 static_cast<cudaStream_t>(stream), &st);
 }
 
 kq_status_t kq_moe_combine(const float* y, const float* wts, int T, int topk, int H, float* out, kq_stream_t stream) {

@@ -947,13 +947,14 @@ bool encode_kv_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t h
 // warp-MMA kernel (same results within fp16 rounding of p * d_v; fewer
 // instructions, latency-bound at the same speed); "generic" = the split-KV
 // kernel every other shape uses.
-enum class FaPath { kTma, kMma, kGeneric };
+enum class FaPath { kStream, kTma, kMma, kGeneric };
 FaPath fa_path() {
   static const FaPath p = [] {
     const char* e = std::getenv("KQ_FA_PATH");
+    if (e && std::string(e) == "tma") return FaPath::kTma;
     if (e && std::string(e) == "mma") return FaPath::kMma;
     if (e && std::string(e) == "generic") return FaPath::kGeneric;
-    return FaPath::kTma;
+    return FaPath::kStream;
   }();
   return p;
 }
@@ -976,7 +977,8 @@ kq_status_t launch_fast(const FastParams& p, const void* k, const void* v, uint6
 }
 
 bool fast_ok(const void* k, const void* v, int D, int Hkv, int g) {
-  return fa_path() != FaPath::kGeneric && D == 128 && Hkv % kHpc == 0 && g <= kG &&
+  return (fa_path() == FaPath::kTma || fa_path() == FaPath::kMma || fa_path() == FaPath::kStream) && D == 128 &&
+         Hkv % kHpc == 0 && g <= kG &&
          (reinterpret_cast<uintptr_t>(k) & 15) == 0 && (reinterpret_cast<uintptr_t>(v) & 15) == 0;
 }
 
@@ -1035,6 +1037,8 @@ kq_status_t launch_fa_mha(int kvf, const float* q, const void* k, const void* v,
                           int D, cudaStream_t s) {
   const long long Q = (long long)B * H;
   if (Q == 0) return KQ_OK;
+  if (kvf == KQ_KV_Q8_0 && fa_path() == FaPath::kStream && S > 0 && fa_stream_supported(q, k, v, out, D, H, 1, 0))
+    return launch_fa_stream_mha(q, k, v, out, B, S, H, s);
   const bool fast = kvf == KQ_KV_Q8_0 && fast_ok(k, v, D, H, 1) && S > 0 &&
                     (long long)((B + kG - 1) / kG) * (H / kHpc) <= 65535;
   int chunk = 0;
@@ -1076,6 +1080,8 @@ kq_status_t launch_fa_ragged(const void* q, const void* k, const void* v, const 
   const long long Q = (long long)B * Hq;
   if (Q == 0) return KQ_OK;
   const int g = Hq / Hkv;
+  if (fa_path() == FaPath::kStream && fa_stream_supported(q, k, v, out, D, Hkv, g, B))
+    return launch_fa_stream_ragged(q, k, v, cu, B, Hq, Hkv, total_rows, scale, out, s);
   const bool fast = fast_ok(k, v, D, Hkv, g) && total_rows > 0 && (long long)B * (Hkv / kHpc) <= 65535;
   int chunk = 0;
   const int NC = fast ? choose_chunks_fast(Q, D, std::max(max_seqlen, 1), kPartialBudget, B * (Hkv / kHpc), &chunk)

@@ -16,6 +16,10 @@ __device__ __forceinline__ void record_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
 
+// silu(g) * u as the MoE's SiLU quantiser forms it (kernels/activation/silu.cuh:97
+// semantics); one definition so every kernel that needs h computes the same bits.
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
+
 __device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
   return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xFFFFu)));
 }

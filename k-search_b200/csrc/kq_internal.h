@@ -119,6 +119,11 @@ kq_status_t launch_gemm_tc(int wtype, const void* w, Act8 act, float* out, int M
 bool gemm_split_supported(int wtype, int M, int N, int K, const void* w, Act8 act);
 kq_status_t launch_gemm_split(int wtype, const void* w, Act8 act, const OutSpec& out, int M, int N, int K,
                               cudaStream_t s, int* err = nullptr);
+// gemm_skinny.cu (8 < M <= 128, K % 256 == 0, 16-byte aligned weights and
+// staging): weights streamed once, mma.sync int8 per 32-block, fp32 epilogue
+bool gemm_skinny_supported(int wtype, int M, int N, int K, const void* w, Act8 act);
+kq_status_t launch_gemm_skinny(int wtype, const void* w, Act8 act, const OutSpec& out, int M, int N, int K,
+                               cudaStream_t s, int* err = nullptr);
 // gemm_simt.cu (any shape; the generic path)
 kq_status_t launch_gemm_simt(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, cudaStream_t s);
 // any shape: GEMV (M <= 8), tcgen05 GEMM, else the generic kernel (no PDL)
@@ -126,9 +131,19 @@ kq_status_t gemm_any(int wtype, const void* w, Act8 act, float* out, int M, int 
 // moe.cu
 size_t moe_workspace_bytes(int P, int E, int H, int I);
 kq_status_t launch_moe_route(const float* logits, int T, int E, int topk, int* idx, float* wts, cudaStream_t s);
+// Intermediates of the expert FFNs in the input row order (parity debugging):
+// gate / up / h = silu(gate) * up fp32 [P, I], h's staged codes [P, I] and
+// (d, s) pairs [P, I/32].
+struct MoeStages {
+  float* gate;
+  float* up;
+  float* h;
+  int8_t* h_qs;
+  float* h_ds;
+};
 kq_status_t launch_moe_experts_q4_0(const float* x_rows, const int* expert_of_row, const void* w_gate,
                                     const void* w_up, const void* w_down, int E, int P, int H, int I, int act_mode,
-                                    float* y_rows, cudaStream_t s);
+                                    float* y_rows, cudaStream_t s, const MoeStages* stages = nullptr);
 kq_status_t launch_moe_combine(const float* y, const float* wts, int T, int topk, int H, float* out, cudaStream_t s);
 kq_status_t launch_moe_q4_0(const float* x, const float* logits, const void* w_gate, const void* w_up,
                             const void* w_down, int E, int topk, int T, int H, int I, int act_mode, float* out,
@@ -139,6 +154,15 @@ kq_status_t launch_block_sums(int wtype, const void* w, const void* a_q8_1, int3
 // kv_format: KQ_KV_Q8_0 / KQ_KV_Q4_0 / KQ_KV_F16
 kq_status_t launch_fa_mha(int kv_format, const float* q, const void* k, const void* v, float* out, int B, int S, int H,
                           int D, cudaStream_t s);
+// fa_stream.cu: the tensor-core decode with the balanced persistent schedule
+// (q8_0 caches, D = 128, KV heads in groups of 8, <= 4 queries per KV head,
+// <= 512 ragged sequences, 16-byte aligned q, k, v and out)
+bool fa_stream_supported(const void* q, const void* k, const void* v, const void* out, int D, int Hkv,
+                         int queries_per_kv_head, int nseq_ragged);
+kq_status_t launch_fa_stream_ragged(const void* q, const void* k, const void* v, const int32_t* cu, int B, int Hq,
+                                    int Hkv, int total_rows, float scale, void* out, cudaStream_t s);
+kq_status_t launch_fa_stream_mha(const float* q, const void* k, const void* v, float* out, int B, int S, int H,
+                                 cudaStream_t s);
 kq_status_t launch_fa_ragged(const void* q, const void* k, const void* v, const int32_t* cu, int B, int Hq, int Hkv,
                              int D, int max_seqlen, int total_rows, float scale, void* out, cudaStream_t s);
 

@@ -148,6 +148,22 @@ __global__ void unsort_kernel(const float* __restrict__ Y, const int* __restrict
     *reinterpret_cast<float4*>(dst + h) = *reinterpret_cast<const float4*>(src + h);
 }
 
+// Row unsort of any row width (16-byte multiple): dst row p = src row row_of_pair[p].
+__global__ void unsort_rows_kernel(const uint8_t* __restrict__ src, const int* __restrict__ row_of_pair,
+                                   size_t row_bytes, uint8_t* __restrict__ dst) {
+  const int p = blockIdx.x;
+  const uint4* s = reinterpret_cast<const uint4*>(src + (size_t)row_of_pair[p] * row_bytes);
+  uint4* d = reinterpret_cast<uint4*>(dst + (size_t)p * row_bytes);
+  for (size_t i = threadIdx.x; i < row_bytes / 16; i += blockDim.x) d[i] = s[i];
+}
+
+// h = silu(gate) * up elementwise, the value the SiLU quantiser quantises.
+__global__ void silu_mul_kernel(const float* __restrict__ g, const float* __restrict__ u, long long n,
+                                float* __restrict__ h) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    h[i] = silu_mul(g[i], u[i]);
+}
+
 __global__ void count_kernel(const int* __restrict__ expert_of_pair, int P, int* __restrict__ counts) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < P) atomicAdd(&counts[expert_of_pair[i]], 1);
@@ -279,7 +295,7 @@ kq_status_t launch_moe_combine(const float* y, const float* wts, int T, int topk
 
 kq_status_t launch_moe_experts_q4_0(const float* x_rows, const int* expert_of_row, const void* w_gate,
                                     const void* w_up, const void* w_down, int E, int P, int H, int I, int act_mode,
-                                    float* y_rows, cudaStream_t s) {
+                                    float* y_rows, cudaStream_t s, const MoeStages* stages) {
   kq_status_t st = check_moe(E, 1, H, I);
   if (st || P == 0) return st;
   MoeWs w;
@@ -289,7 +305,26 @@ kq_status_t launch_moe_experts_q4_0(const float* x_rows, const int* expert_of_ro
   if ((st = check_launch("moe count"))) return st;
   if ((st = moe_core(x_rows, 1, expert_of_row, P, E, w_gate, w_up, w_down, H, I, act_mode, w, s))) return st;
   unsort_kernel<<<P, 256, 0, s>>>(w.Y, w.row_of_pair, H, y_rows);
-  return check_launch("moe unsort");
+  if ((st = check_launch("moe unsort"))) return st;
+  if (stages) {
+    // the pipeline's own intermediates, back in the input row order
+    const size_t fbytes = (size_t)I * sizeof(float);
+    auto unsort = [&](const void* src, size_t row_bytes, void* dst) {
+      unsort_rows_kernel<<<P, 128, 0, s>>>(static_cast<const uint8_t*>(src), w.row_of_pair, row_bytes,
+                                           static_cast<uint8_t*>(dst));
+      return check_launch("moe stage unsort");
+    };
+    if ((st = unsort(w.G, fbytes, stages->gate)) || (st = unsort(w.U, fbytes, stages->up))) return st;
+    // h of the grouped rows, formed by the same function as the quantiser, into the gate buffer's
+    // successor (the grouped G is no longer needed once it has been copied out)
+    silu_mul_kernel<<<std::min<long long>(4096, ((long long)P * I + 255) / 256), 256, 0, s>>>(w.G, w.U,
+                                                                                            (long long)P * I, w.G);
+    if ((st = check_launch("moe stage silu"))) return st;
+    if ((st = unsort(w.G, fbytes, stages->h))) return st;
+    if ((st = unsort(w.ah.qs, (size_t)I, stages->h_qs))) return st;
+    if ((st = unsort(w.ah.ds, (size_t)(I / 32) * sizeof(float2), stages->h_ds))) return st;
+  }
+  return KQ_OK;
 }
 
 kq_status_t launch_moe_q4_0(const float* x, const float* logits, const void* w_gate, const void* w_up,

@@ -100,8 +100,7 @@ __device__ __forceinline__ float4 load_octet(const float* __restrict__ x, const 
   } else if constexpr (SRC == SRC_SILU) {
     const float4 g = __ldg(reinterpret_cast<const float4*>(x + blk * 32) + sub);
     const float4 u = __ldg(reinterpret_cast<const float4*>(y + blk * 32) + sub);
-    auto f = [](float gv, float uv) { return gv / (1.0f + expf(-gv)) * uv; };
-    return make_float4(f(g.x, u.x), f(g.y, u.y), f(g.z, u.z), f(g.w, u.w));
+    return make_float4(silu_mul(g.x, u.x), silu_mul(g.y, u.y), silu_mul(g.z, u.z), silu_mul(g.w, u.w));
   } else {
     return __ldg(reinterpret_cast<const float4*>(x + blk * 32) + sub);
   }

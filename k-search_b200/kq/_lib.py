@@ -52,6 +52,8 @@ SIGNATURES = {
     "kq_copy_2d": (_i, [_vp, ctypes.c_size_t, _vp, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t, _vp]),
     "kq_moe_route": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp]),
     "kq_moe_experts_q4_0": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp]),
+    "kq_moe_experts_stages_q4_0": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp,
+                                        _vp]),
     "kq_moe_combine": (_i, [_vp, _vp, _i, _i, _i, _vp, _vp]),
     "kq_block_sums_i32": (_i, [_i, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "kq_fa_decode_q8_0_mha": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),

@@ -294,6 +294,18 @@ def block_sums_codes(wtype: str, w: np.ndarray, qa: np.ndarray, N: int, K: int) 
     return np.ascontiguousarray(np.matmul(A, B).transpose(1, 2, 0)).astype(np.int32)
 
 
+def gemm_codes(wtype: str, w: np.ndarray, qa: np.ndarray, da: np.ndarray, sa: np.ndarray, M: int, N: int,
+               K: int) -> np.ndarray:
+    """The per-block formula on given activation codes qa int8 [M, K/32, 32]
+    and block scales / sums da, sa [M, K/32] (fp32): the GEMM a kernel runs on
+    activations it quantised itself (gemm_ref.py:100-153, 274-331;
+    gemm_reference.h:311-336)."""
+    dw, mw, _ = unpack_weights(wtype, w, N, K)
+    sumi = block_sums_codes(wtype, w, np.asarray(qa, dtype=np.int8).reshape(M, K // QK, QK), N, K)
+    return _formula(wtype, dw, mw, np.asarray(da, dtype=np.float32), np.asarray(sa, dtype=np.float32), sumi, M, N,
+                    K // QK)
+
+
 def gemm_f32act(wtype: str, w: np.ndarray, x: np.ndarray, M: int, N: int, K: int,
                 mode: int = ACT_F32) -> np.ndarray:
     """The harness operator: fp32 activations quantised on the fly, then the
@@ -355,31 +367,6 @@ def check_close(out: np.ndarray, ref: np.ndarray, rel_l2_tol: float = 1e-3,
     ok = (r <= rel_l2_tol) and nbad == 0
     return ok, f"rel_l2={r:.3e} bad_elems={nbad}/{out.size}"
 
-
-def check_close_requant(out: np.ndarray, ref: np.ndarray, max_bad_frac: float = 1e-3) -> tuple[bool, str]:
-    """The fp32 bar for outputs that pass through an intermediate q8_1
-    re-quantisation (the MoE's silu(gate) * up before the down projection):
-    rel-L2 <= 1e-3, and the per-element bar of check_close on all but
-    `max_bad_frac` of the elements. The intermediate is formed from fp32 GEMM
-    outputs on the GPU and fp64 ones here, so a value sitting on a rounding
-    boundary can quantise to the neighbouring code; such a flip moves a few
-    near-zero outputs past the 1e-3 rms floor while leaving rel-L2 near 1e-5."""
-    out = np.asarray(out, dtype=np.float64)
-    ref = np.asarray(ref, dtype=np.float64)
-    if out.shape != ref.shape:
-        return False, f"shape {out.shape} != {ref.shape}"
-    if not np.all(np.isfinite(out)):
-        return False, "non-finite output"
-    r = rel_l2(out, ref)
-    rms = float(np.sqrt(np.mean(ref ** 2))) if ref.size else 0.0
-    nbad = int(np.count_nonzero(np.abs(out - ref) > 1e-2 * np.abs(ref) + 1e-3 * rms))
-    ok = r <= 1e-3 and nbad <= max_bad_frac * out.size
-    return ok, f"rel_l2={r:.3e} bad_elems={nbad}/{out.size} (allowed {int(max_bad_frac * out.size)})"
-
-
-# ---------------------------------------------------------------------------
-# Flash-attention decode over a q8_0 KV cache
-# ---------------------------------------------------------------------------
 
 def dequant_q8_0_rows(kv: np.ndarray, rows: int, D: int) -> np.ndarray:
     """q8_0 bytes [rows, D/32, 34] -> fp32 [rows, D] (x = q * d)."""

@@ -2,7 +2,11 @@
 math: world 1 in-process (the MoE stage entry points kq_moe_route /
 kq_moe_experts_q4_0 / kq_moe_combine), and world 2 over NCCL in spawned
 processes when two GPUs are visible. Bar for fp32 outputs: rel-L2 <= 1e-3 and
-per element |out - ref| <= 1e-2 |ref| + 1e-3 rms(ref) against the oracle."""
+per element |out - ref| <= 1e-2 |ref| + 1e-3 rms(ref), against the oracle for
+the GEMMs and, for the expert-parallel MoE, against the single-GPU fused
+operator on the whole batch (stage-checked against the oracle in
+test_moe_gpu.py): every expert sees the same rows either way, so the two runs
+quantise identical intermediates."""
 import os
 import socket
 
@@ -15,8 +19,8 @@ from oracle import quant as Q
 pytestmark = pytest.mark.gpu
 
 
-def _assert_close(out, ref, what="", requant=False):
-    ok, msg = (Q.check_close_requant if requant else Q.check_close)(out, ref)
+def _assert_close(out, ref, what=""):
+    ok, msg = Q.check_close(out, ref)
     assert ok, f"{what} {msg}"
 
 
@@ -43,9 +47,7 @@ def test_moe_stages_world1(cuda):
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
     out = kd.moe_expert_parallel(t(x), t(logits), t(wg), t(wu), t(wd), E, topk)
     fused = kq.moe_q4_0(t(x), t(logits), t(wg), t(wu), t(wd), topk=topk)
-    ref = Q.moe_forward(x, logits, list(wg), list(wu), list(wd), topk, H, I, Q.SUM_DQ)
-    _assert_close(out.cpu().numpy(), ref, "expert-parallel", requant=True)
-    _assert_close(fused.cpu().numpy(), ref, "fused", requant=True)
+    _assert_close(out.cpu().numpy(), fused.cpu().numpy().astype(np.float64), "expert-parallel vs fused")
 
 
 def test_nsharded_gemm_world1(cuda):
@@ -117,6 +119,7 @@ def _ranks_main(which: str) -> None:
     say = lambda *a: print(f"[rank {rank}]", *a, flush=True)  # noqa: E731
     failures = []
     try:
+        import kq
         from kq import dist as kd
 
         t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
@@ -145,9 +148,9 @@ def _ranks_main(which: str) -> None:
             stats = {}
             out = kd.moe_expert_parallel(t(x[sl]), t(logits[sl]), t(wg[first:first + per]), t(wu[first:first + per]),
                                          t(wd[first:first + per]), E, topk, stats=stats)
-            ref = Q.moe_forward(x, logits, list(wg), list(wu), list(wd), topk, H, I, Q.SUM_DQ,
-                                tokens=np.arange(sl.start, sl.stop))
-            ok, msg = Q.check_close_requant(out.cpu().numpy(), ref)
+            # the fused single-GPU operator on the whole batch with every expert
+            ref = kq.moe_q4_0(t(x), t(logits), t(wg), t(wu), t(wd), topk=topk)[sl]
+            ok, msg = Q.check_close(out.cpu().numpy(), ref.cpu().numpy().astype(np.float64))
             say("moe", stats, msg)
             if not ok:
                 failures.append(msg)

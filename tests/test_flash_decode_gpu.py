@@ -33,9 +33,10 @@ def test_golden_fixture(cuda):
 
 @pytest.mark.parametrize("B,S,H,D", [(1, 512, 32, 128), (8, 1000, 4, 128), (3, 4096, 2, 64), (2, 1, 3, 32),
                                      (16, 300, 2, 256), (2, 100, 3, 96), (6, 2000, 5, 160),
-                                     # TMA fast path (D = 128, heads in groups of 8): partial tiles,
-                                     # partial query groups, one-token cache
-                                     (5, 77, 8, 128), (12, 1000, 16, 128), (3, 1, 8, 128), (4, 33, 32, 128)])
+                                     # tensor-core path (D = 128, heads in groups of 8): partial tiles,
+                                     # partial query groups, one-token cache, many query groups
+                                     (5, 77, 8, 128), (12, 1000, 16, 128), (3, 1, 8, 128), (4, 33, 32, 128),
+                                     (512, 64, 8, 128), (9, 8192, 8, 128)])
 def test_mha_parity(cuda, B, S, H, D):
     import kq
     rng = np.random.default_rng(B * S + H)
@@ -188,6 +189,13 @@ RAGGED_CASES = [
     ([7, 4097, 64], 16, 8, 128),
     ([31, 32, 33], 8, 8, 128),
     ([2000, 5], 32, 16, 128),
+    # stream schedule: fewer tiles than CTAs, tile-boundary lengths, two and
+    # four KV-head groups per token row, many sequences (ranges crossing items)
+    ([1, 2, 3], 32, 8, 128),
+    ([15, 16, 17, 0, 48, 1], 8, 8, 128),
+    ([300, 700], 32, 32, 128),
+    ([129, 4000, 64], 64, 16, 128),
+    (list(np.random.default_rng(3).integers(0, 600, size=200)), 32, 8, 128),
 ]
 
 
@@ -204,9 +212,64 @@ def test_ragged_parity(cuda, lens, Hq, Hkv, D):
     assert ok, msg
 
 
-def test_mma_decode_path_opt_in(cuda):
-    """KQ_FA_PATH=mma (warp-level MMA decode: int8 QK on the raw codes, fp16 PV)
-    against the oracle, in a child process (the path is chosen once per process)."""
+def test_ragged_garbage_rows_masked(cuda):
+    """Cache rows past the last sequence (total_rows > cu_seqlens[B]) hold
+    arbitrary bytes, here NaN scales: a tile that reaches into them must mask
+    them out (scores to -inf, p * d_v to zero), not propagate them."""
+    import kq
+    rng = np.random.default_rng(17)
+    lens, Hq, Hkv, D = [37, 250, 9], 32, 8, 128
+    q, k, v, cu = _ragged_case(rng, lens, Hq, Hkv, D)
+    pad = np.full((40 * Hkv, D // 32, 34), 0xFF, dtype=np.uint8)  # fp16 0xFFFF = NaN, codes -1
+    kp = np.concatenate([k.reshape(-1, D // 32, 34), pad]).reshape(-1)
+    vp = np.concatenate([v.reshape(-1, D // 32, 34), pad]).reshape(-1)
+    scale = 1.0 / np.sqrt(D)
+    got = kq.flash_decode_ragged(_t(q, cuda), _t(kp, cuda), _t(vp, cuda), _t(cu, cuda), Hkv, scale=scale)
+    ok, msg = Q.check_close(got.float().cpu().numpy(), Q.flash_decode_ragged(q, k, v, cu, Hq, Hkv, D, scale))
+    assert ok, msg
+
+
+def _seq_rows(x, cu, b, Hkv, D):
+    """Cache bytes of sequence b alone (rows cu[b] .. cu[b+1] - 1)."""
+    r = x.reshape(-1, Hkv, D // 32, 34)
+    return np.ascontiguousarray(r[cu[b]:cu[b + 1]]).reshape(-1)
+
+
+def test_full_size_config3_sampled_sequences(cuda):
+    """configs[3] at full size: B = 32 sequences with lengths U[64, 8192]
+    (seeded), Hq = 32, Hkv = 8, D = 128, fp16 queries and output. The whole
+    batch runs in one call; the fp64 oracle checks the shortest, the longest
+    and four more sequences (each sequence's output depends only on its own
+    rows)."""
+    import kq
+    rng = np.random.default_rng(99)
+    B, Hq, Hkv, D = 32, 32, 8, 128
+    lens = rng.integers(64, 8193, size=B).astype(np.int32)
+    cu = np.zeros(B + 1, dtype=np.int32)
+    cu[1:] = np.cumsum(lens)
+    T = int(cu[-1])
+    dev = cuda
+    g = torch.Generator(device=dev).manual_seed(7)
+    kd = kq.quantize_rows(torch.randn((T * Hkv, D), generator=g, device=dev), "q8_0")
+    vd = kq.quantize_rows(torch.randn((T * Hkv, D), generator=g, device=dev), "q8_0")
+    q = rng.standard_normal((B, Hq, D)).astype(np.float16)
+    scale = 1.0 / np.sqrt(D)
+    got = kq.flash_decode_ragged(_t(q, dev), kd, vd, _t(cu, dev), Hkv, scale=scale).float().cpu().numpy()
+    kh, vh = kd.cpu().numpy(), vd.cpu().numpy()
+    pick = sorted({int(np.argmin(lens)), int(np.argmax(lens)), 0, 7, 19, B - 1})
+    for b in pick:
+        one = np.array([0, lens[b]], dtype=np.int32)
+        ref = Q.flash_decode_ragged(q[b:b + 1], _seq_rows(kh, cu, b, Hkv, D), _seq_rows(vh, cu, b, Hkv, D), one,
+                                    Hq, Hkv, D, scale)
+        ok, msg = Q.check_close(got[b:b + 1], ref)
+        assert ok, f"sequence {b} (L={lens[b]}): {msg}"
+
+
+@pytest.mark.parametrize("path", ["tma", "mma"])
+def test_earlier_decode_paths_opt_in(cuda, path):
+    """KQ_FA_PATH=tma (the CUDA-core TMA decode) and =mma (its warp-MMA
+    variant) against the oracle, in a child process (the path is chosen once
+    per process)."""
     import os
     import subprocess
     import sys
@@ -218,6 +281,6 @@ def test_mma_decode_path_opt_in(cuda):
         "    for args in T.RAGGED_CASES:\n"
         "        fn(dev, *args)\n"
         "print('ok')\n" % ([os.path.dirname(os.path.abspath(__file__))] + [p for p in sys.path if p],))
-    env = dict(os.environ, KQ_FA_PATH="mma")
+    env = dict(os.environ, KQ_FA_PATH=path)
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]

@@ -1,11 +1,28 @@
-"""GPU parity of the grouped q4_0 MoE expert FFN (kq_moe_q4_0) against the
-restated oracle (oracle.quant.moe_forward: softmax, top-k with lower-index
-ties, renormalised weights, silu(gate) * up, q8_1-quantised activations
-before each GEMM, fp64 accumulation). Bar: rel-L2 <= 1e-3 and per element
-|out - ref| <= 1e-2 |ref| + 1e-3 rms(ref) on all but 0.1% of the elements
-(oracle.quant.check_close_requant: silu(gate) * up is re-quantised to q8_1
-between the GEMMs, and a value on a rounding boundary may take the
-neighbouring code when formed from fp32 rather than fp64 GEMM outputs)."""
+"""GPU parity of the grouped q4_0 MoE expert FFN (kq_moe_q4_0 and its stages),
+stage by stage, each at the strict bar with no exempt element:
+
+1. routing (kq_moe_route): expert ids equal the restated routing's exactly,
+   ties included (lower expert index first), weights to fp32 rounding;
+2. gate and up projections, the pipeline's own outputs
+   (kq_moe_experts_stages_q4_0), against the oracle GEMM at the bar;
+3. h = silu(gate) * up as the GPU forms it, against the fp64 oracle of the
+   GPU's own gate and up; h's q8_1 codes and scales bit for bit against the
+   oracle quantiser applied to the GPU's own h;
+4. the down projection on those codes against the oracle GEMM on the same
+   codes, at the bar;
+5. the combine against the routing weights applied to the GPU's own rows, and
+   the fused kq_moe_q4_0 against the staged pipeline on the same rows.
+
+Checking the stages separately is what makes the strict bar possible: an
+end-to-end fp64 oracle re-quantises h from its own gate and up, and a value on
+a rounding boundary can take the neighbouring code. The reference has no MoE
+operator, so the routing and combine are restated semantics (softmax, top-k
+with lower-index ties, renormalised weights; kernels/activation/silu.cuh:97 for
+silu(g) * u) that no reference test pins; each expert GEMM is the W4A32C8
+operator the reference defines per expert (definitions/quant_gemm/mixtral8x7b/
+w4a32c8_q4_0_fp32_int8_mixtral8x7b_moe_up_n14336_k4096.json)."""
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -14,30 +31,134 @@ from oracle import quant as Q
 
 pytestmark = pytest.mark.gpu
 
+MODES = {"sum_x": Q.SUM_X, "sum_dq": Q.SUM_DQ, "f32": Q.ACT_F32}
 
-def _case(rng, T, E, H, I):
-    x = rng.standard_normal((T, H)).astype(np.float32)
-    logits = rng.standard_normal((T, E)).astype(np.float32)
+
+def _dev(a, cuda):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+
+
+def _weights(rng, E, H, I):
     wg = [Q.make_q4_0_blocks(rng, I, H) for _ in range(E)]
     wu = [Q.make_q4_0_blocks(rng, I, H) for _ in range(E)]
     wd = [Q.make_q4_0_blocks(rng, H, I) for _ in range(E)]
-    return x, logits, wg, wu, wd
+    return wg, wu, wd
+
+
+def _stages(cuda, x_rows, expert_of_row, wg_d, wu_d, wd_d, E, H, I, mode):
+    """kq_moe_experts_stages_q4_0 -> (gate, up, h, h_qs, h_ds, y) as numpy."""
+    import kq
+    P = x_rows.shape[0]
+    f = lambda *s: torch.empty(s, dtype=torch.float32, device=cuda)  # noqa: E731
+    gate, up, h, y = f(P, I), f(P, I), f(P, I), f(P, H)
+    h_qs = torch.empty((P, I), dtype=torch.int8, device=cuda)
+    h_ds = f(P, I // 32, 2)
+    xd, ed = _dev(x_rows, cuda), _dev(expert_of_row.astype(np.int32), cuda)
+    st = kq.lib().kq_moe_experts_stages_q4_0(
+        xd.data_ptr(), ed.data_ptr(), wg_d.data_ptr(), wu_d.data_ptr(), wd_d.data_ptr(), E, P, H, I,
+        kq.ACT_MODES[mode], gate.data_ptr(), up.data_ptr(), h.data_ptr(), h_qs.data_ptr(), h_ds.data_ptr(),
+        y.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert st == 0, kq._lib.last_error()
+    return tuple(t.cpu().numpy() for t in (gate, up, h, h_qs, h_ds, y))
+
+
+def _check_stages(x_rows, expert_of_row, wg, wu, wd, H, I, mode, got):
+    gate, up, h, h_qs, h_ds, y = got
+    m = MODES[mode]
+    for e in np.unique(expert_of_row):
+        r = np.nonzero(expert_of_row == e)[0]
+        xe = x_rows[r]
+        for name, w, t in (("gate", wg[e], gate), ("up", wu[e], up)):
+            ok, msg = Q.check_close(t[r], Q.gemm_f32act("q4_0", w, xe, len(r), I, H, m))
+            assert ok, f"expert {e} {name}: {msg}"
+    # h from the GPU's own gate and up (fp64 silu), then its codes bit for bit
+    ok, msg = Q.check_close(h, Q.silu(gate) * up.astype(np.float64), rel_l2_tol=1e-6, elem_rel=1e-5,
+                            elem_abs_rms=1e-6)
+    assert ok, f"h: {msg}"
+    qa, da, sa = Q.quantize_act(h, m)
+    assert np.array_equal(h_qs.reshape(qa.shape), qa), "h codes differ from the oracle quantiser on the GPU's h"
+    assert np.array_equal(h_ds[:, :, 0], da) and np.array_equal(h_ds[:, :, 1], sa), "h scales / sums differ"
+    # down projection on the GPU's own codes
+    for e in np.unique(expert_of_row):
+        r = np.nonzero(expert_of_row == e)[0]
+        ref = Q.gemm_codes("q4_0", wd[e], qa[r], da[r], sa[r], len(r), H, I)
+        ok, msg = Q.check_close(y[r], ref)
+        assert ok, f"expert {e} down: {msg}"
+
+
+TIE_LOGITS = np.array([
+    [0, 0, 0, 0, 0, 0, 0, 0],          # all equal: experts 0, 1 at 0.5 / 0.5
+    [1, 3, 3, 3, 0, 0, 0, 0],          # three-way tie at the top
+    [5, 1, 2, 2, 2, -1, 0, 5],         # tie between the first and the last expert
+    [0, 1, 0, 1, 0, 1, 0, 1],          # ties for both slots
+], dtype=np.float32)
 
 
 @pytest.mark.parametrize("T,E,topk,H,I,mode", [
     (64, 4, 2, 256, 512, "sum_dq"),
-    (300, 8, 2, 512, 1024, "sum_dq"),     # experts with > 8 rows take the tensor-core GEMM
+    (300, 8, 2, 512, 1024, "sum_dq"),     # experts with > 128 rows take the split tensor-core GEMM
     (5, 8, 2, 256, 256, "f32"),           # some experts receive no token
     (128, 8, 1, 256, 512, "sum_x"),
+    (40, 8, 2, 256, 512, "sum_x"),        # routing ties (rows 0-3)
 ])
-def test_moe_parity(cuda, T, E, topk, H, I, mode):
+def test_moe_stages(cuda, T, E, topk, H, I, mode):
     import kq
     rng = np.random.default_rng(T + E + H)
-    x, logits, wg, wu, wd = _case(rng, T, E, H, I)
-    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)  # noqa: E731
-    got = kq.moe_q4_0(dev(x), dev(logits), dev(np.stack(wg)), dev(np.stack(wu)), dev(np.stack(wd)), topk, mode)
-    modes = {"sum_x": Q.SUM_X, "sum_dq": Q.SUM_DQ, "f32": Q.ACT_F32}
-    ref = Q.moe_forward(x, logits, wg, wu, wd, topk, H, I, modes[mode])
-    ok, msg = Q.check_close_requant(got.cpu().numpy(), ref)
-    assert ok, msg
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    logits = rng.standard_normal((T, E)).astype(np.float32)
+    if E == 8:
+        logits[:len(TIE_LOGITS)] = TIE_LOGITS
+    wg, wu, wd = _weights(rng, E, H, I)
+    wg_d, wu_d, wd_d = (_dev(np.stack(a), cuda) for a in (wg, wu, wd))
+    # 1. routing
+    idx, wts = kq.moe_route(_dev(logits, cuda), topk)
+    idx, wts = idx.cpu().numpy(), wts.cpu().numpy()
+    ref_idx, ref_w = Q.moe_route(logits, topk)
+    assert np.array_equal(idx, ref_idx), "expert ids differ from the restated routing"
+    assert np.allclose(wts, ref_w, rtol=1e-6, atol=1e-7)
+    # 2-4. expert FFN stages on the routed (token, slot) rows
+    pairs = np.arange(T * topk)
+    x_rows = x[pairs // topk]
+    e_rows = idx.reshape(-1)
+    got = _stages(cuda, x_rows, e_rows, wg_d, wu_d, wd_d, E, H, I, mode)
+    _check_stages(x_rows, e_rows, wg, wu, wd, H, I, mode, got)
+    y = got[5]
+    # 5. combine with the GPU's weights, and the fused operator on the same inputs
+    comb = kq.moe_combine(_dev(y, cuda), _dev(wts, cuda)).cpu().numpy()
+    ref_comb = (wts[:, :, None].astype(np.float64) * y.reshape(T, topk, H)).sum(axis=1)
+    ok, msg = Q.check_close(comb, ref_comb, rel_l2_tol=1e-6, elem_rel=1e-5, elem_abs_rms=1e-6)
+    assert ok, f"combine: {msg}"
+    fused = kq.moe_q4_0(_dev(x, cuda), _dev(logits, cuda), wg_d, wu_d, wd_d, topk, mode).cpu().numpy()
+    ok, msg = Q.check_close(fused, comb)
+    assert ok, f"fused vs staged: {msg}"
     assert kq.device_error() == 0
+
+
+def test_full_size_config4_sampled_tokens(cuda):
+    """configs[4] at full size (T=4096 tokens, 8 experts, top-2, H=4096,
+    I=14336, q4_0 weights): the fused operator runs on the whole batch; the
+    routing is checked for every token, and six sampled tokens (12 routed
+    rows) go through the staged pipeline, each stage checked at the bar, and
+    their fused output rows against the staged result."""
+    import kq
+    T, E, topk, H, I, mode = 4096, 8, 2, 4096, 14336, "sum_dq"
+    rng = np.random.default_rng(4096)
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    logits = rng.standard_normal((T, E)).astype(np.float32)
+    wg, wu, wd = _weights(rng, E, H, I)
+    wg_d, wu_d, wd_d = (_dev(np.stack(a), cuda) for a in (wg, wu, wd))
+    fused = kq.moe_q4_0(_dev(x, cuda), _dev(logits, cuda), wg_d, wu_d, wd_d, topk, mode).cpu().numpy()
+    assert np.isfinite(fused).all()
+    idx, wts = kq.moe_route(_dev(logits, cuda), topk)
+    idx, wts = idx.cpu().numpy(), wts.cpu().numpy()
+    ref_idx, ref_w = Q.moe_route(logits, topk)
+    assert np.array_equal(idx, ref_idx)
+    assert np.allclose(wts, ref_w, rtol=1e-6, atol=1e-7)
+    toks = np.array([0, 1, 777, 2048, 4000, T - 1])
+    x_rows = np.repeat(x[toks], topk, axis=0)
+    e_rows = idx[toks].reshape(-1)
+    got = _stages(cuda, x_rows, e_rows, wg_d, wu_d, wd_d, E, H, I, mode)
+    _check_stages(x_rows, e_rows, wg, wu, wd, H, I, mode, got)
+    staged = (wts[toks][:, :, None].astype(np.float64) * got[5].reshape(len(toks), topk, H)).sum(axis=1)
+    ok, msg = Q.check_close(fused[toks], staged)
+    assert ok, f"fused rows vs staged: {msg}"

@@ -86,6 +86,20 @@ def test_sum_dq_equals_dequant_matmul():
     assert ok, msg
 
 
+def test_gemm_codes_equals_gemm_f32act():
+    """gemm_codes on the oracle quantiser's own codes and scales is the
+    quant_gemm formula bit for bit (the MoE down projection check uses it on
+    codes the GPU formed)."""
+    rng = np.random.default_rng(21)
+    M, N, K = 5, 64, 256
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    for wtype in ("q4_0", "q4_1", "q8_0"):
+        w = Q.make_blocks(wtype, rng, N, K)
+        for mode in (Q.SUM_X, Q.SUM_DQ, Q.ACT_F32):
+            qa, da, sa = Q.quantize_act(x, mode)
+            assert np.array_equal(Q.gemm_codes(wtype, w, qa, da, sa, M, N, K), Q.gemm_f32act(wtype, w, x, M, N, K, mode))
+
+
 def test_block_sums_direct():
     rng = np.random.default_rng(5)
     M, N, K = 2, 5, 96

@@ -116,6 +116,34 @@ def test_gemm_row_magnitudes(cuda, wtype):
             assert ok, f"{mode} row {m}: {msg}"
 
 
+def test_split_path_opt_in(cuda):
+    """KQ_GEMM_PATH=split (the split-fp16 tcgen05 kernel for every M > 8,
+    including the M <= 128 shapes the skinny kernel takes by default), in a
+    child process: the full parity bar on every row."""
+    import os
+    import subprocess
+    import sys
+    code = (
+        "import sys, numpy as np, torch; sys.path[:0] = %r\n"
+        "import kq; from oracle import quant as Q\n"
+        "for wt in ('q4_0', 'q4_1', 'q8_0'):\n"
+        "  for (M, N, K) in ((16, 256, 512), (129, 200, 512), (100, 384, 4096), (40, 256, 2304)):\n"
+        "    rng = np.random.default_rng(M + N + K)\n"
+        "    w = Q.make_blocks(wt, rng, N, K); x = rng.standard_normal((M, K)).astype(np.float32)\n"
+        "    x[3] *= np.float32(1e-6); x[5] *= np.float32(1e3)\n"
+        "    for mode in ('f32', 'sum_x', 'sum_dq'):\n"
+        "      got = kq.gemm_f32act(torch.from_numpy(w).cuda(), torch.from_numpy(x).cuda(), M, N, K, wt, mode)\n"
+        "      ref = Q.gemm_f32act(wt, w, x, M, N, K, {'f32': Q.ACT_F32, 'sum_x': Q.SUM_X, 'sum_dq': Q.SUM_DQ}[mode])\n"
+        "      g = got.cpu().numpy().astype(np.float64)\n"
+        "      for m in range(M):\n"
+        "        ok, msg = Q.check_close(g[m:m + 1], ref[m:m + 1])\n"
+        "        assert ok, (wt, M, N, K, mode, m, msg)\n"
+        "print('ok')\n" % ([p for p in sys.path if p],))
+    env = dict(os.environ, KQ_GEMM_PATH="split")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
+
+
 def test_int8_path_opt_in(cuda):
     """KQ_GEMM_PATH=int8 (int8 tcgen05 MMA per 32-block, int32 block sums
     rescaled on the FP32 pipe), in a child process: the full parity bar on
@@ -284,6 +312,33 @@ def test_full_size_config_sampled_rows(cuda, wtype):
     ok, msg = Q.check_close(got[rows], ref)
     assert ok, msg
     assert Q.nmse(got[rows], Q.gemm_dequant_f32(wtype, w, x[rows], len(rows), N, K)) < 0.05
+
+
+@pytest.mark.parametrize("M", [16, 128, 2048])
+def test_full_size_config2_sampled_rows(cuda, M):
+    """BASELINE configuration 2 at full size (q4_0, N=14336, K=4096) for
+    M = 16 and 128 (the weight-streaming kernel) and 2048 (the split-fp16
+    kernel, 16 token tiles): the whole product runs in one call and the
+    oracle checks sampled token rows, including every 128-row tile edge for
+    M = 2048 (output rows are independent)."""
+    import kq
+    N, K = 14336, 4096
+    rng = np.random.default_rng(14336 + M)
+    w = Q.make_q4_0_blocks(rng, N, K)
+    x = _x(rng, M, K)
+    got = kq.gemm_f32act(_t(w, cuda), _t(x, cuda), M, N, K, "q4_0", "sum_dq").cpu().numpy()
+    assert np.isfinite(got).all()
+    if M <= 128:
+        rows = np.array(sorted({0, 1, 7, 8, 9, M // 2, M - 2, M - 1}))
+    else:
+        rows = np.array(sorted({0, 1} | {t * 128 + o for t in range(M // 128) for o in (0, 127)} | {M - 1}))
+    ref = Q.gemm_f32act("q4_0", w, x[rows], len(rows), N, K, Q.SUM_DQ)
+    ok, msg = Q.check_close(got[rows], ref)
+    assert ok, msg
+    # int32 block sums of one sampled row, bit-exact against the oracle's
+    a = Q.quantize_q8_1(x[rows[:1]])
+    sumi = kq.block_sums_i32(_t(w, cuda), _t(a, cuda), 1, N, K, "q4_0").cpu().numpy()
+    assert np.array_equal(sumi, Q.block_sums_i32("q4_0", w, a, 1, N, K))
 
 
 @pytest.mark.parametrize("wtype", ["q4_0", "q4_1", "q8_0"])
