@@ -359,13 +359,10 @@ __global__ void __launch_bounds__(128) fa_combine_kernel(FaParams p, int Q) {
 // ---------------------------------------------------------------------------
 constexpr int kHpc = 8;        // KV heads per CTA (one compute warp each)
 constexpr int kG = 4;          // queries per KV head per CTA
-constexpr int kSt = 32;        // tokens per TMA tile
 constexpr int kStages = 2;
 constexpr int kRowBytes = kHpc * 136;  // one token row of 8 heads x (4 q8_0 blocks of 34 B)
-constexpr int kTile = kSt * kRowBytes;
 constexpr int kFastThreads = (kHpc + 1) * 32;
-// The CUDA-core kernel streams 16-token tiles so two CTAs (18 warps) fit on an
-// SM; the warp-MMA kernel keeps 32-token tiles.
+// 16-token tiles, so two CTAs (18 warps) fit on an SM.
 constexpr int kStF = 16;
 constexpr int kTileF = kStF * kRowBytes;
 constexpr int kGrpF = kStF / 8;  // 8-token score groups per tile
@@ -613,323 +610,6 @@ __global__ void __launch_bounds__(kFastThreads, 2)
   }
 }
 
-// ---------------------------------------------------------------------------
-// Tensor-core decode (warp-level MMA): same work split, staging and partial
-// outputs as fa_fast_kernel, with both products on the tensor pipe.
-//
-//   QK: mma.m16n8k32 s8. The raw q8_0 K codes in the TMA tile are the B
-//       operand as they are (4 consecutive codes of one token per register);
-//       the A operand holds each query twice as int8, q ~ s1 * q1 + s2 * q2
-//       with s2 = s1 / 127 (error below amax / 32258). One MMA per 32-dim
-//       block gives exact int32 block dots; score = sum_b d_k[t, b] *
-//       (s1 * dot1 + s2 * dot2) in fp32.
-//   PV: mma.m16n8k16 f16. A = p * d_v[t, block] (fp16), B = the V codes as
-//       fp16 (exact small integers) from a per-warp converted tile read with
-//       ldmatrix.trans; fp32 accumulation.
-// Rows: a query group of up to 4 heads occupies A rows 0-3 (and 4-7 for the
-// second int8 level in QK); rows 8-15 are zero.
-// ---------------------------------------------------------------------------
-constexpr int kVRowBytes = 256;                 // one token of one head as fp16 (128 dims)
-constexpr int kVTile = kSt * kVRowBytes;        // per compute warp
-constexpr size_t kMmaSmem = 2 * kStages * kTile + kHpc * kVTile + 2 * kHpc * kSt * 4 * sizeof(float) +
-                            4 * kStages * 8 + 128;
-static_assert(kHpc * kG * 128 * sizeof(float) <= kHpc * kVTile, "queries alias the fp16 V tiles");
-
-__device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%10, %10, %10, %10};"
-      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1), "r"(0));
-}
-
-// Accumulates rows 0-7 (c0, c1 of this lane); rows 8-15 of A are zero, their
-// outputs are discarded.
-__device__ __forceinline__ void mma_f16_16816(float (&c)[2], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
-  float z0, z1;
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %10, %10};"
-      : "+f"(c[0]), "+f"(c[1]), "=f"(z0), "=f"(z1)
-      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1), "f"(0.0f));
-}
-
-__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t saddr) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(saddr));
-}
-
-__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
-  uint32_t r;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  return r;
-}
-
-// 32-bit word at a 2-byte aligned shared address
-__device__ __forceinline__ uint32_t lds_u32_a2(const uint8_t* b) {
-  const uintptr_t a = reinterpret_cast<uintptr_t>(b);
-  const uint32_t* q = reinterpret_cast<const uint32_t*>(a & ~(uintptr_t)3);
-  return __funnelshift_r(q[0], q[1], (a & 2) ? 16u : 0u);
-}
-
-__device__ __forceinline__ float lds_half(const uint8_t* b) {
-  return __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(b)));
-}
-
-// int8 of v / s, round half to even, clamped
-__device__ __forceinline__ int q8(float v, float s) { return max(-127, min(127, __float2int_rn(v / s))); }
-
-template <typename QT, bool RAGGED>
-__global__ void __launch_bounds__(kFastThreads, 1)
-    fa_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, FastParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~(uintptr_t)127);
-  uint8_t* ktile = smem;
-  uint8_t* vtile = smem + kStages * kTile;
-  uint8_t* vh = smem + 2 * kStages * kTile;                    // [warp][32 tokens][256 B] fp16 V codes
-  float* qs = reinterpret_cast<float*>(vh);                      // prologue only: [8][4][128]
-  float* dks = reinterpret_cast<float*>(vh + kHpc * kVTile);    // [warp][32 tokens][4 blocks]
-  float* dvs = dks + kHpc * kSt * 4;
-  uint64_t* full = reinterpret_cast<uint64_t*>(dvs + kHpc * kSt * 4);
-  uint64_t* empty = full + kStages;
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int c = blockIdx.x;
-  const int item = blockIdx.y;
-  const int hg = item % p.n_hg;
-  const int grp = item / p.n_hg;  // RAGGED: sequence b; else query group
-  int L, row0, nq;
-  if (RAGGED) {
-    row0 = p.cu[grp];
-    L = p.cu[grp + 1] - row0;
-    nq = p.H / p.Hkv;
-  } else {
-    row0 = 0;
-    L = p.S;
-    nq = min(kG, p.B - grp * kG);
-  }
-  const int t0 = c * p.chunk, t1 = min(L, t0 + p.chunk);
-  const int nsub = t1 > t0 ? (t1 - t0 + kSt - 1) / kSt : 0;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kHpc);
-    }
-    fence_mbar_init();
-  }
-  // queries of this CTA into shared memory, pre-scaled by scale * log2(e)
-  for (int i = threadIdx.x; i < kHpc * kG * 128; i += blockDim.x) {
-    const int w = i / (kG * 128), j = (i / 128) % kG, dim = i % 128;
-    const int hk = hg * kHpc + w;
-    float v = 0.0f;
-    if (j < nq) {
-      size_t qi;
-      if (RAGGED) qi = ((size_t)grp * p.H + (size_t)hk * (p.H / p.Hkv) + j) * 128 + dim;
-      else qi = ((size_t)(grp * kG + j) * p.H + hk) * 128 + dim;
-      v = load_q(static_cast<const QT*>(p.q), qi) * p.qscale;
-    }
-    qs[i] = v;
-  }
-  __syncthreads();
-
-  bool dead = false;
-  if (warp == kHpc) {
-    // ---------------- producer ----------------
-    if (lane == 0) {
-      for (int i = 0; i < nsub; ++i) {
-        const int s = i % kStages;
-        if (i >= kStages) mbar_wait_or_poison(&empty[s], ((i / kStages) - 1) & 1, nullptr, 0, dead);
-        mbar_arrive_expect_tx(&full[s], 2 * kTile);
-        const int y = row0 + t0 + i * kSt;
-        tma_load_2d_u64(ktile + s * kTile, &kmap, hg * (kRowBytes / 8), y, &full[s]);
-        tma_load_2d_u64(vtile + s * kTile, &vmap, hg * (kRowBytes / 8), y, &full[s]);
-      }
-      for (int i = max(0, nsub - kStages); i < nsub; ++i)
-        mbar_wait_or_poison(&empty[i % kStages], (i / kStages) & 1, nullptr, 0, dead);
-    }
-    return;
-  }
-
-  // ---------------- compute warp: KV head hg*8 + warp ----------------
-  const int w = warp;
-  const int gid = lane >> 2, tig = lane & 3;
-  // two-level int8 queries: A rows 0-3 level 1, rows 4-7 level 2
-  float s1[kG];
-#pragma unroll
-  for (int j = 0; j < kG; ++j) {
-    const float4 t = reinterpret_cast<const float4*>(qs + (w * kG + j) * 128)[lane];
-    float a = fmaxf(fmaxf(fabsf(t.x), fabsf(t.y)), fmaxf(fabsf(t.z), fabsf(t.w)));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-    s1[j] = a > 0.0f ? a / 127.0f : 1.0f;
-  }
-  const int jrow = gid & 3, lvl = gid >> 2;
-  const float s1r = s1[0] * (jrow == 0) + s1[1] * (jrow == 1) + s1[2] * (jrow == 2) + s1[3] * (jrow == 3);
-  const float s2r = s1r / 127.0f;
-  const float sl = lvl ? s2r : s1r;  // this lane's level scale
-  uint32_t qa[4][2];
-  {
-    const float* qrow = qs + (w * kG + jrow) * 128;
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t word = 0;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float v = qrow[32 * b + 16 * h + 4 * tig + i];
-          const int q1 = q8(v, s1r);
-          const int qv = lvl ? q8(v - s1r * (float)q1, s2r) : q1;
-          word |= (uint32_t)(qv & 0xFF) << (8 * i);
-        }
-        qa[b][h] = word;
-      }
-    }
-  }
-  named_bar_sync(1, kHpc * 32);  // every warp is done with the queries: the fp16 V tiles reuse their space
-
-  float o[16][2];
-#pragma unroll
-  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = 0.0f;
-  float m_run = -INFINITY, l_run = 0.0f;
-  uint8_t* vw = vh + w * kVTile;
-  const uint32_t vw_s = smem_u32(vw);
-  float* dkw = dks + w * kSt * 4;
-  float* dvw = dvs + w * kSt * 4;
-
-  for (int it = 0; it < nsub; ++it) {
-    const int s = it % kStages;
-    mbar_wait_or_poison(&full[s], (it / kStages) & 1, nullptr, 0, dead);
-    const uint8_t* kt = ktile + s * kTile;
-    const uint8_t* vt = vtile + s * kTile;
-    const int tb = t0 + it * kSt;  // first token of the tile
-    const int nvalid = t1 - tb;    // tokens of this tile inside the chunk (>= 1)
-
-    // ---- per-token block scales (lane = token); invalid tokens get d_v = 0 ----
-    {
-      const uint8_t* kr = kt + lane * kRowBytes + w * 136;
-      const uint8_t* vr = vt + lane * kRowBytes + w * 136;
-      const bool ok = lane < nvalid;
-      reinterpret_cast<float4*>(dkw)[lane] =
-          make_float4(lds_half(kr), lds_half(kr + 34), lds_half(kr + 68), lds_half(kr + 102));
-      reinterpret_cast<float4*>(dvw)[lane] = ok ? make_float4(lds_half(vr), lds_half(vr + 34), lds_half(vr + 68),
-                                                               lds_half(vr + 102))
-                                                : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    // ---- V codes -> fp16 tile (lane = 4 dims; 128B-style XOR swizzle of 16-byte chunks) ----
-#pragma unroll 4
-    for (int t = 0; t < kSt; ++t) {
-      const uint32_t cw = lds_u32_a2(vt + t * kRowBytes + w * 136 + (lane >> 3) * 34 + 2 + 4 * (lane & 7)) ^ 0x80808080u;
-      const uint32_t lo = __byte_perm(cw, 0x64646464u, 0x4140), hi = __byte_perm(cw, 0x64646464u, 0x4342);
-      uint32_t l2, h2;
-      asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(l2) : "r"(lo), "r"(0x64806480u));
-      asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(h2) : "r"(hi), "r"(0x64806480u));
-      *reinterpret_cast<uint2*>(vw + t * kVRowBytes + ((((lane >> 1) ^ (t & 7))) << 4) + (lane & 1) * 8) =
-          make_uint2(l2, h2);
-    }
-    __syncwarp();
-
-    // ---- scores: 4 n-tiles of 8 tokens; lane holds tokens 8nt + 2tig, +1 of row gid ----
-    float sc[4][2];
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      const uint8_t* kr = kt + (8 * nt + gid) * kRowBytes + w * 136 + 2 + 4 * tig;  // B: token 8nt + gid
-      const float4 dka = reinterpret_cast<const float4*>(dkw)[8 * nt + 2 * tig];
-      const float4 dkb = reinterpret_cast<const float4*>(dkw)[8 * nt + 2 * tig + 1];
-      const float dk0[4] = {dka.x, dka.y, dka.z, dka.w}, dk1[4] = {dkb.x, dkb.y, dkb.z, dkb.w};
-      float a0 = 0.0f, a1 = 0.0f;
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        int d[4];
-        mma_s8_16832(d, qa[b][0], qa[b][1], lds_u32_a2(kr + 34 * b), lds_u32_a2(kr + 34 * b + 16));
-        a0 = fmaf((float)d[0], dk0[b] * sl, a0);
-        a1 = fmaf((float)d[1], dk1[b] * sl, a1);
-      }
-      a0 += __shfl_xor_sync(0xffffffffu, a0, 16);  // level 1 + level 2
-      a1 += __shfl_xor_sync(0xffffffffu, a1, 16);
-      const int tok = 8 * nt + 2 * tig;
-      sc[nt][0] = tok < nvalid ? a0 : -INFINITY;
-      sc[nt][1] = tok + 1 < nvalid ? a1 : -INFINITY;
-    }
-    // ---- online softmax for row jrow (lanes gid and gid+4 hold the same row) ----
-    float mx = -INFINITY;
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) mx = fmaxf(mx, fmaxf(sc[nt][0], sc[nt][1]));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    const float m_new = fmaxf(m_run, mx);
-    const float corr = (m_run == -INFINITY) ? 0.0f : exp2f(m_run - m_new);
-    float pr[4][2], ls = 0.0f;
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        pr[nt][i] = (m_new == -INFINITY) ? 0.0f : exp2f(sc[nt][i] - m_new);
-        ls += pr[nt][i];
-      }
-    ls += __shfl_xor_sync(0xffffffffu, ls, 1);
-    ls += __shfl_xor_sync(0xffffffffu, ls, 2);
-    l_run = fmaf(l_run, corr, ls);
-    m_run = m_new;
-#pragma unroll
-    for (int n = 0; n < 16; ++n) {
-      o[n][0] *= corr;
-      o[n][1] *= corr;
-    }
-    // ---- P . V: 2 k-steps of 16 tokens; A rows 0-3 from lanes 0-15, zero elsewhere ----
-    const bool arow = lane < 16;
-#pragma unroll
-    for (int ks = 0; ks < 2; ++ks) {
-      const int ta = 16 * ks + 2 * tig;
-      const float4 va = reinterpret_cast<const float4*>(dvw)[ta];
-      const float4 vb = reinterpret_cast<const float4*>(dvw)[ta + 1];
-      const float4 vc = reinterpret_cast<const float4*>(dvw)[ta + 8];
-      const float4 vd = reinterpret_cast<const float4*>(dvw)[ta + 9];
-      const float dva[4] = {va.x, va.y, va.z, va.w}, dvb[4] = {vb.x, vb.y, vb.z, vb.w};
-      const float dvc[4] = {vc.x, vc.y, vc.z, vc.w}, dvd[4] = {vd.x, vd.y, vd.z, vd.w};
-      const float p0 = arow ? pr[2 * ks][0] : 0.0f, p1 = arow ? pr[2 * ks][1] : 0.0f;
-      const float p2 = arow ? pr[2 * ks + 1][0] : 0.0f, p3 = arow ? pr[2 * ks + 1][1] : 0.0f;
-      // ldmatrix lane address: matrix mi = lane / 8 (token half, dim half), row r = lane % 8
-      const int mi = lane >> 3, r = lane & 7;
-      const int tok = 16 * ks + (mi & 1) * 8 + r;
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const uint32_t A0 = pack_half2(p0 * dva[b], p1 * dvb[b]);
-        const uint32_t A2 = pack_half2(p2 * dvc[b], p3 * dvd[b]);
-#pragma unroll
-        for (int np = 0; np < 2; ++np) {
-          const int chunk = (32 * b + 16 * np + (mi >> 1) * 8) >> 3;  // 16-byte chunk of 8 dims
-          uint32_t bf[4];
-          ldsm_x4_trans(bf, vw_s + tok * kVRowBytes + ((chunk ^ (tok & 7)) << 4));
-          mma_f16_16816(o[4 * b + 2 * np], A0, A2, bf[0], bf[1]);
-          mma_f16_16816(o[4 * b + 2 * np + 1], A0, A2, bf[2], bf[3]);
-        }
-      }
-    }
-    fence_proxy_async_smem();  // generic reads of the TMA-refilled tile, before its release
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-  }
-
-  // ---- partial state of each query of this warp (rows 0-3: lanes 0-15) ----
-  const int hk = hg * kHpc + w;
-  if (lane < 16 && jrow < nq) {
-    size_t qg;
-    if (RAGGED) qg = (size_t)grp * p.H + (size_t)hk * (p.H / p.Hkv) + jrow;
-    else qg = (size_t)(grp * kG + jrow) * p.H + hk;
-    const size_t pi = qg * p.NC + c;
-    if (tig == 0) {
-      p.pm[pi] = m_run;
-      p.pl[pi] = l_run;
-    }
-    float* acc = p.pacc + pi * 128;
-#pragma unroll
-    for (int n = 0; n < 16; ++n) *reinterpret_cast<float2*>(acc + 8 * n + 2 * tig) = make_float2(o[n][0], o[n][1]);
-  }
-}
-
 bool encode_kv_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t heads, uint32_t box_rows) {
   // [rows][heads * 136 bytes] as uint64 elements; boxes of box_rows rows x 8
   // heads (the kernel's tile: its expected transaction bytes match the box)
@@ -943,16 +623,14 @@ bool encode_kv_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t h
 }
 
 // Decode kernel family for q8_0 caches in the TMA-able shapes, read once per
-// process from KQ_FA_PATH: the TMA CUDA-core kernel by default; "mma" = the
-// warp-MMA kernel (same results within fp16 rounding of p * d_v; fewer
-// instructions, latency-bound at the same speed); "generic" = the split-KV
-// kernel every other shape uses.
-enum class FaPath { kStream, kTma, kMma, kGeneric };
+// process from KQ_FA_PATH: the tensor-pipe streaming kernel (fa_stream.cu) by
+// default; "tma" = the TMA CUDA-core kernel; "generic" = the split-KV kernel
+// every other shape uses.
+enum class FaPath { kStream, kTma, kGeneric };
 FaPath fa_path() {
   static const FaPath p = [] {
     const char* e = std::getenv("KQ_FA_PATH");
     if (e && std::string(e) == "tma") return FaPath::kTma;
-    if (e && std::string(e) == "mma") return FaPath::kMma;
     if (e && std::string(e) == "generic") return FaPath::kGeneric;
     return FaPath::kStream;
   }();
@@ -962,22 +640,19 @@ FaPath fa_path() {
 template <typename QT, bool RAGGED>
 kq_status_t launch_fast(const FastParams& p, const void* k, const void* v, uint64_t rows, int heads, int items,
                         cudaStream_t s) {
-  const bool simt = fa_path() != FaPath::kMma;
-  const uint32_t box_rows = simt ? kStF : kSt;
   CUtensorMap km, vm;
-  if (!encode_kv_map(&km, k, rows, heads, box_rows) || !encode_kv_map(&vm, v, rows, heads, box_rows))
+  if (!encode_kv_map(&km, k, rows, heads, kStF) || !encode_kv_map(&vm, v, rows, heads, kStF))
     return fail(KQ_ERR_CUDA, "fa: KV tensor map rejected");
-  auto kern = simt ? fa_fast_kernel<QT, RAGGED> : fa_mma_kernel<QT, RAGGED>;
-  const size_t smem = simt ? kFastSmem : kMmaSmem;
-  kq_status_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)smem, "fa smem attribute");
+  auto kern = fa_fast_kernel<QT, RAGGED>;
+  kq_status_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)kFastSmem, "fa smem attribute");
   if (st) return st;
   dim3 grid(p.NC, items);
-  kern<<<grid, kFastThreads, smem, s>>>(km, vm, p);
+  kern<<<grid, kFastThreads, kFastSmem, s>>>(km, vm, p);
   return check_launch("fa_fast");
 }
 
 bool fast_ok(const void* k, const void* v, int D, int Hkv, int g) {
-  return (fa_path() == FaPath::kTma || fa_path() == FaPath::kMma || fa_path() == FaPath::kStream) && D == 128 &&
+  return (fa_path() == FaPath::kTma || fa_path() == FaPath::kStream) && D == 128 &&
          Hkv % kHpc == 0 && g <= kG &&
          (reinterpret_cast<uintptr_t>(k) & 15) == 0 && (reinterpret_cast<uintptr_t>(v) & 15) == 0;
 }

@@ -265,11 +265,11 @@ def test_full_size_config3_sampled_sequences(cuda):
         assert ok, f"sequence {b} (L={lens[b]}): {msg}"
 
 
-@pytest.mark.parametrize("path", ["tma", "mma"])
+@pytest.mark.parametrize("path", ["tma", "generic"])
 def test_earlier_decode_paths_opt_in(cuda, path):
-    """KQ_FA_PATH=tma (the CUDA-core TMA decode) and =mma (its warp-MMA
-    variant) against the oracle, in a child process (the path is chosen once
-    per process)."""
+    """KQ_FA_PATH=tma (the CUDA-core TMA decode) and =generic (the split-KV
+    kernel) against the oracle on the ragged cases, in a child process (the
+    path is chosen once per process)."""
     import os
     import subprocess
     import sys
