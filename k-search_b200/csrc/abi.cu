@@ -154,16 +154,17 @@ kq_status_t check_gemm_args(int wtype, const void* w, const void* a, const float
 }
 
 // Quantised activations are staged; choose the GEMM kernel for the shape.
-// M > 8 path: the skinny int8 kernel (weights streamed once) for M <= 128,
-// the exact split-fp16 tcgen05 kernel above; KQ_GEMM_PATH=split runs the
-// split kernel for every M > 8, KQ_GEMM_PATH=int8 the int8 tcgen05 kernel
-// (per-block int32 sums rescaled on the FP32 pipe). Read once per process.
-enum class GemmPath { kDefault, kSplit, kInt8 };
+// M > 8 path: the exact split-fp16 tcgen05 kernel; KQ_GEMM_PATH=int8 runs
+// the int8 tcgen05 kernel (per-block int32 sums rescaled on the FP32 pipe)
+// for every M > 8, KQ_GEMM_PATH=skinny the warp-MMA kernel for 8 < M <= 128
+// (slower than the split kernel there: its unrolled code misses the
+// instruction cache). Read once per process.
+enum class GemmPath { kDefault, kSkinny, kInt8 };
 GemmPath gemm_path() {
   static const GemmPath p = [] {
     const char* e = std::getenv("KQ_GEMM_PATH");
     if (e && std::string(e) == "int8") return GemmPath::kInt8;
-    if (e && std::string(e) == "split") return GemmPath::kSplit;
+    if (e && std::string(e) == "skinny") return GemmPath::kSkinny;
     return GemmPath::kDefault;
   }();
   return p;
@@ -174,7 +175,7 @@ GemmPath gemm_path() {
 kq_status_t dispatch_gemm_tc(int wtype, const void* w, Act8 act, const OutSpec& out, int M, int N, int K,
                              cudaStream_t s, bool pdl) {
   const GemmPath path = gemm_path();
-  if (path == GemmPath::kDefault && gemm_skinny_supported(wtype, M, N, K, w, act))
+  if (path == GemmPath::kSkinny && gemm_skinny_supported(wtype, M, N, K, w, act))
     return launch_gemm_skinny(wtype, w, act, out, M, N, K, s);
   if (path != GemmPath::kInt8 && gemm_split_supported(wtype, M, N, K, w, act))
     return launch_gemm_split(wtype, w, act, out, M, N, K, s);
@@ -183,7 +184,7 @@ kq_status_t dispatch_gemm_tc(int wtype, const void* w, Act8 act, const OutSpec& 
 }
 
 bool gemm_tc_any_supported(int wtype, int M, int N, int K, const void* w, Act8 act) {
-  return (gemm_path() == GemmPath::kDefault && gemm_skinny_supported(wtype, M, N, K, w, act)) ||
+  return (gemm_path() == GemmPath::kSkinny && gemm_skinny_supported(wtype, M, N, K, w, act)) ||
          (gemm_path() != GemmPath::kInt8 && gemm_split_supported(wtype, M, N, K, w, act)) ||
          gemm_tc_supported(wtype, M, N, K, w, act);
 }

@@ -52,9 +52,10 @@ constexpr int SWS = 4;         // converted weight stages (codes + scales)
 constexpr int SRAW = 2;        // raw weight stages
 constexpr int NBUF = 4;        // TMEM buffers (one per block of a stage)
 constexpr int kWarpTma = 0, kWarpMma = 1, kWarpConv = 2, kConvWarps = 2, kWarpEpi = kWarpConv + kConvWarps,
-              kEpiWarps = 16;
-constexpr int kEpiCols = TN / (kEpiWarps / 4);  // columns per epilogue thread (32)
-constexpr int kHalf = kEpiCols / 2;             // columns per TMEM load (16)
+              kEpiWarps = 8;
+constexpr int kEpiCols = TN / (kEpiWarps / 4);  // columns per epilogue thread (64)
+constexpr int kChunk = 16;                      // columns per TMEM load
+constexpr int kChunks = kEpiCols / kChunk;      // loads per block (4)
 constexpr int kWarps = kWarpEpi + kEpiWarps;
 constexpr int kThreads = kWarps * 32;
 constexpr int kTmemCols = NBUF * TN;  // 512
@@ -272,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int m0 = (t % p.num_m_tiles) * TM, n0 = (t / p.num_m_tiles) * TN;
         for (int k8 = 0; k8 < nkb8; ++k8, ++ir) {
           const int rs = ir % SRAW;
-          if (ir >= SRAW) mbar_wait_or_poison(&raw_empty[rs], ((ir / SRAW) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+          if (ir >= SRAW) mbar_wait_idle_or_poison(&raw_empty[rs], ((ir / SRAW) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
           mbar_arrive_expect_tx(&raw_full[rs], T::RAW_STAGE);
           tma_load_2d(smem + T::OFF_RAW + rs * T::RAW_STAGE, &map_raw, k8 * (T::RAW_ROW / 2), n0, &raw_full[rs]);
           if (!waited_pdl) {  // activations are produced by the preceding kernel
@@ -281,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           for (int sub = 0; sub < KRAW / KSUB; ++sub, ++ia) {
             const int as = ia % SA;
-            if (ia >= SA) mbar_wait_or_poison(&act_empty[as], ((ia / SA) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+            if (ia >= SA) mbar_wait_idle_or_poison(&act_empty[as], ((ia / SA) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
             const int kb = k8 * KRAW + sub * KSUB;  // first block of this stage
             mbar_arrive_expect_tx(&act_full[as], T::ACT_TILE + T::ASC_STAGE);
             tma_load_2d(smem + T::OFF_ACT + as * T::ACT_TILE, &map_act, kb * 32, m0, &act_full[as]);
@@ -301,13 +302,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pre_b = sw128_desc_rep8(smem_u32(smem + T::OFF_PRE + T::PRE_TILE));
       for (int gs = 0; gs < total; ++gs) {
         const int as = gs % SA, ws = gs % SWS;
-        mbar_wait_or_poison(&act_full[as], (gs / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-        mbar_wait_or_poison(&w_full[ws], (gs / SWS) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+        mbar_wait_idle_or_poison(&act_full[as], (gs / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+        mbar_wait_idle_or_poison(&w_full[ws], (gs / SWS) & 1, p.err, DEV_TIMEOUT_FULL, dead);
         const uint64_t adesc = sw128_desc(act_base + as * T::ACT_TILE);
         const uint64_t bdesc = sw128_desc(w_base + ws * T::W_TILE);
 #pragma unroll
         for (int j = 0; j < KSUB; ++j) {
-          if (gs > 0) mbar_wait_or_poison(&tm_empty[j], (gs - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+          if (gs > 0) mbar_wait_idle_or_poison(&tm_empty[j], (gs - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
           tc_fence_after();
           // bias words from the tensor core, then K block j of the stage
           // (+32 bytes inside the 128-byte swizzle atom) accumulated onto them
@@ -328,9 +329,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int gs = 0; gs < total; ++gs) {
       const int irr = gs >> 1, sub = gs & 1;
       const int rs = irr % SRAW;
-      mbar_wait_or_poison(&raw_full[rs], (irr / SRAW) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+      mbar_wait_idle_or_poison(&raw_full[rs], (irr / SRAW) & 1, p.err, DEV_TIMEOUT_FULL, dead);
       const int ws = gs % SWS;
-      if (gs >= SWS) mbar_wait_or_poison(&w_empty[ws], ((gs / SWS) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+      if (gs >= SWS) mbar_wait_idle_or_poison(&w_empty[ws], ((gs / SWS) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
       uint8_t* wt = smem + T::OFF_W + ws * T::W_TILE;
       float* wsc = reinterpret_cast<float*>(smem + T::OFF_WSC + ws * T::WSC_STAGE);
 #pragma unroll 1
@@ -389,104 +390,127 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int cg = ew >> 2;                  // column group of kEpiCols
     const int row = quarter * 32 + lane;     // token row in the tile
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    // fp32 accumulators as packed pairs. TMEM is read in halves of kHalf
-    // columns, one half ahead: the load of the next half (of this block, or
-    // the first half of the next block) is in flight while the current half's
-    // math runs; a buffer goes back to the MMA as soon as both halves are in
-    // registers.
+    // fp32 accumulators as packed pairs. TMEM is read in chunks of kChunk
+    // columns, one chunk ahead: the load of the next chunk (of this block, or
+    // the first chunk of the next block) is in flight while the current
+    // chunk's math runs; a buffer goes back to the MMA as soon as all its
+    // chunks are in registers. Eight warps of 64 columns each (not sixteen of
+    // 32): the math needs ~170 registers per thread without moves, and fewer
+    // warps have to release every buffer before the MMA can refill it.
     constexpr int NP = kEpiCols / 2;
     uint64_t acc[NP];
-    uint32_t va[kHalf], vb[kHalf];
-    const int nblk = total * KSUB;
-    auto tm_addr = [&](int gb, int h) -> uint32_t {
-      return tmem_base + lane_addr + (uint32_t)((gb % NBUF) * TN + cg * kEpiCols + kHalf * h);
-    };
-    auto wait_full = [&](int gb) {
-      mbar_wait_or_poison(&tm_full[gb % NBUF], (gb / NBUF) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+    uint32_t vbuf[2][kChunk];
+    // Stage es (counted over all tiles) fills TMEM buffer j with its block j,
+    // so buffer j's phase parity at stage es is es & 1 (NBUF == KSUB).
+    const uint32_t tm_row = tmem_base + lane_addr + (uint32_t)(cg * kEpiCols);
+    if (total > 0) {
+      mbar_wait_idle_or_poison(&tm_full[0], 0, p.err, DEV_TIMEOUT_FULL, dead);
       tc_fence_after();
-    };
-    if (nblk > 0) {
-      wait_full(0);
-      tmem_ldh(tm_addr(0, 0), va);
+      tmem_ldh(tm_row, vbuf[0]);
       tmem_ld_wait();
     }
-    for (int gb = 0; gb < nblk; ++gb) {
-      const int es = gb / KSUB, j = gb % KSUB;
-      const int s = es % spt;
-      const int as = es % SA, ws = es % SWS;
-      if (j == 0) {
-        if (s == 0) {
+    int es = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
 #pragma unroll
-          for (int c = 0; c < NP; ++c) acc[c] = 0ull;
-        }
-        mbar_wait_or_poison(&act_full[as], (es / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-        mbar_wait_or_poison(&w_full[ws], (es / SWS) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-      }
-      const float2 dsj = reinterpret_cast<const float2*>(smem + T::OFF_ASC + as * T::ASC_STAGE)[row * KSUB + j];
-      const float d = round22(dsj.x);
-      const uint64_t d2 = pk2(d, d);
-      const uint64_t c2 = pk2(-kBiasF * d, -kBiasF * d);
-      const uint64_t ms8 = pk2(-8.0f * dsj.y, -8.0f * dsj.y);
-      const uint64_t sy2 = pk2(dsj.y, dsj.y);
-      const float* wsc = reinterpret_cast<const float*>(smem + T::OFF_WSC + ws * T::WSC_STAGE);
-      const ulonglong2* dw = reinterpret_cast<const ulonglong2*>(wsc + j * TN + cg * kEpiCols);
-      const ulonglong2* mw = reinterpret_cast<const ulonglong2*>(wsc + KSUB * TN + j * TN + cg * kEpiCols);
-
-      auto math = [&](const uint32_t(&v)[kHalf], int h) {
+      for (int c = 0; c < NP; ++c) acc[c] = 0ull;
+      const bool last_tile = t + (int)gridDim.x >= p.num_tiles;
+      for (int s = 0; s < spt; ++s, ++es) {
+        const int as = es % SA, ws = es % SWS;  // compile-time powers of two
+        const uint32_t par = (uint32_t)es & 1u;
+        mbar_wait_idle_or_poison(&act_full[as], (es / SA) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+        mbar_wait_idle_or_poison(&w_full[ws], (es / SWS) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+        const float2* dsp = reinterpret_cast<const float2*>(smem + T::OFF_ASC + as * T::ASC_STAGE) + row * KSUB;
+        const float* wsc = reinterpret_cast<const float*>(smem + T::OFF_WSC + ws * T::WSC_STAGE);
+        const bool last_stage = last_tile && s == spt - 1;
+#pragma unroll 1
+        for (int j = 0; j < KSUB; ++j) {
+          const float2 dsj = dsp[j];
+          const float dx = dsj.x, dy = dsj.y;
+          const float d = round22(dx);
+          const uint64_t d2 = pk2(d, d);
+          const uint64_t c2 = pk2(-kBiasF * d, -kBiasF * d);
+          const uint64_t ms8 = pk2(-8.0f * dy, -8.0f * dy);
+          const uint64_t sy2 = pk2(dy, dy);
+          const ulonglong2* dw = reinterpret_cast<const ulonglong2*>(wsc + j * TN + cg * kEpiCols);
+          const ulonglong2* mw = reinterpret_cast<const ulonglong2*>(wsc + KSUB * TN + j * TN + cg * kEpiCols);
 #pragma unroll
-        for (int q = 0; q < kHalf / 4; ++q) {  // 4 columns per step
-          const ulonglong2 w4 = dw[(kHalf / 4) * h + q];
-          const int c = (kHalf / 2) * h + 2 * q;  // pair index
-          uint64_t u0 = fma2(pk2u(v[4 * q], v[4 * q + 1]), d2, c2);  // d_a * sumi (exact)
-          uint64_t u1 = fma2(pk2u(v[4 * q + 2], v[4 * q + 3]), d2, c2);
-          if constexpr (WT == KQ_Q4_0) {
-            u0 = add2(u0, ms8);  // d_a sumi - 8 s_a
-            u1 = add2(u1, ms8);
-          }
-          acc[c] = fma2(u0, w4.x, acc[c]);
-          acc[c + 1] = fma2(u1, w4.y, acc[c + 1]);
-          if constexpr (WT == KQ_Q4_1) {
-            const ulonglong2 m4 = mw[(kHalf / 4) * h + q];
-            acc[c] = fma2(m4.x, sy2, acc[c]);  // + m_w s_a
-            acc[c + 1] = fma2(m4.y, sy2, acc[c + 1]);
+          for (int h = 0; h < kChunks; ++h) {
+            uint32_t(&cur)[kChunk] = vbuf[h & 1];
+            uint32_t(&nxt)[kChunk] = vbuf[(h + 1) & 1];
+            if (h + 1 < kChunks) {
+              tmem_ldh(tm_row + (uint32_t)(j * TN + kChunk * (h + 1)), nxt);
+            } else if (!(last_stage && j == KSUB - 1)) {
+              // the next block's first chunk (buffer j + 1 of this stage, or 0 of the next)
+              const int jn = (j + 1) & (KSUB - 1);
+              const uint32_t pn = j == KSUB - 1 ? (par ^ 1u) : par;
+              mbar_wait_idle_or_poison(&tm_full[jn], pn, p.err, DEV_TIMEOUT_FULL, dead);
+              tc_fence_after();
+              tmem_ldh(tm_row + (uint32_t)(jn * TN), nxt);
+            }
+#pragma unroll
+            for (int q = 0; q < kChunk / 4; ++q) {  // 4 columns per step
+              const ulonglong2 w4 = dw[(kChunk / 4) * h + q];
+              const int c = (kChunk / 2) * h + 2 * q;  // pair index
+              uint64_t u0 = fma2(pk2u(cur[4 * q], cur[4 * q + 1]), d2, c2);  // d_a * sumi (exact)
+              uint64_t u1 = fma2(pk2u(cur[4 * q + 2], cur[4 * q + 3]), d2, c2);
+              if constexpr (WT == KQ_Q4_0) {
+                u0 = add2(u0, ms8);  // d_a sumi - 8 s_a
+                u1 = add2(u1, ms8);
+              }
+              acc[c] = fma2(u0, w4.x, acc[c]);
+              acc[c + 1] = fma2(u1, w4.y, acc[c + 1]);
+              if constexpr (WT == KQ_Q4_1) {
+                const ulonglong2 m4 = mw[(kChunk / 4) * h + q];
+                acc[c] = fma2(m4.x, sy2, acc[c]);  // + m_w s_a
+                acc[c + 1] = fma2(m4.y, sy2, acc[c + 1]);
+              }
+            }
+            tmem_ld_wait();
+            if (h == kChunks - 2) {
+              // every chunk of block j is in registers: hand buffer j back
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&tm_empty[j]);
+            }
           }
         }
-      };
-
-      // half 0 (in va): prefetch half 1, compute, then release the buffer
-      tmem_ldh(tm_addr(gb, 1), vb);
-      math(va, 0);
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tm_empty[gb % NBUF]);
-      // half 1 (in vb): prefetch the next block's half 0
-      if (gb + 1 < nblk) {
-        wait_full(gb + 1);
-        tmem_ldh(tm_addr(gb + 1, 0), va);
-      }
-      math(vb, 1);
-      tmem_ld_wait();
-
-      if (j == KSUB - 1) {
         fence_proxy_async_smem();  // generic reads of the TMA-refilled scale stage, before its release
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&act_empty[as]);
           mbar_arrive(&w_empty[ws]);
         }
-        if (s == spt - 1) {
-          // ---- store this tile's rows ----
-          const int t = (int)blockIdx.x + (es / spt) * (int)gridDim.x;
-          const int m0 = (t % p.num_m_tiles) * TM, n0 = (t / p.num_m_tiles) * TN;
-          const int m = m0 + row;
-          const int nc0 = n0 + cg * kEpiCols;
-          if (m < p.M) {
-            if constexpr (!SCATTER) {
-              float* o = p.out.ptr[0] + (size_t)m * p.N + nc0;
-              // float4 stores only when every row start is 16-byte aligned
-              // (an offset output view falls back to scalar stores)
-              if (nc0 + kEpiCols <= p.N && (p.N & 3) == 0 && (reinterpret_cast<uintptr_t>(p.out.ptr[0]) & 15) == 0) {
+      }
+      // ---- store this tile's rows ----
+      {
+        const int m0 = (t % p.num_m_tiles) * TM, n0 = (t / p.num_m_tiles) * TN;
+        const int m = m0 + row;
+        const int nc0 = n0 + cg * kEpiCols;
+        if (m < p.M) {
+          if constexpr (!SCATTER) {
+            float* o = p.out.ptr[0] + (size_t)m * p.N + nc0;
+            // float4 stores only when every row start is 16-byte aligned
+            // (an offset output view falls back to scalar stores)
+            if (nc0 + kEpiCols <= p.N && (p.N & 3) == 0 && (reinterpret_cast<uintptr_t>(p.out.ptr[0]) & 15) == 0) {
+#pragma unroll
+              for (int c = 0; c < NP; c += 2) {
+                const float2 a = upk2(acc[c]), b = upk2(acc[c + 1]);
+                *reinterpret_cast<float4*>(o + 2 * c) = make_float4(a.x, a.y, b.x, b.y);
+              }
+            } else {
+#pragma unroll
+              for (int c = 0; c < NP; ++c) {
+                const float2 a = upk2(acc[c]);
+                if (nc0 + 2 * c < p.N) o[2 * c] = a.x;
+                if (nc0 + 2 * c + 1 < p.N) o[2 * c + 1] = a.y;
+              }
+            }
+          } else {
+            const size_t off = (size_t)m * p.out.ld + p.out.col0 + nc0;
+            const bool vec = nc0 + kEpiCols <= p.N && ((p.out.ld | p.out.col0) & 3) == 0;
+            for (int dd = 0; dd < p.out.n_out; ++dd) {
+              float* o = p.out.ptr[dd] + off;
+              if (vec) {
 #pragma unroll
                 for (int c = 0; c < NP; c += 2) {
                   const float2 a = upk2(acc[c]), b = upk2(acc[c + 1]);
@@ -498,26 +522,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const float2 a = upk2(acc[c]);
                   if (nc0 + 2 * c < p.N) o[2 * c] = a.x;
                   if (nc0 + 2 * c + 1 < p.N) o[2 * c + 1] = a.y;
-                }
-              }
-            } else {
-              const size_t off = (size_t)m * p.out.ld + p.out.col0 + nc0;
-              const bool vec = nc0 + kEpiCols <= p.N && ((p.out.ld | p.out.col0) & 3) == 0;
-              for (int dd = 0; dd < p.out.n_out; ++dd) {
-                float* o = p.out.ptr[dd] + off;
-                if (vec) {
-#pragma unroll
-                  for (int c = 0; c < NP; c += 2) {
-                    const float2 a = upk2(acc[c]), b = upk2(acc[c + 1]);
-                    *reinterpret_cast<float4*>(o + 2 * c) = make_float4(a.x, a.y, b.x, b.y);
-                  }
-                } else {
-#pragma unroll
-                  for (int c = 0; c < NP; ++c) {
-                    const float2 a = upk2(acc[c]);
-                    if (nc0 + 2 * c < p.N) o[2 * c] = a.x;
-                    if (nc0 + 2 * c + 1 < p.N) o[2 * c + 1] = a.y;
-                  }
                 }
               }
             }

@@ -146,6 +146,25 @@ __device__ __forceinline__ void mbar_wait_or_poison(uint64_t* bar, uint32_t pari
   if (!dead && !mbar_wait(bar, parity, err, code)) dead = true;
 }
 
+// The same bounded wait without the spinning probes: the thread suspends in
+// try_wait from the start. For producer / issuer / converter threads that
+// share an SM sub-partition with the warps doing the math: a spinning waiter
+// takes issue slots from them.
+__device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity, int* err, int code) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+      record_error(err, code);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void mbar_wait_idle_or_poison(uint64_t* bar, uint32_t parity, int* err, int code,
+                                                         bool& dead) {
+  if (!dead && !mbar_wait_idle(bar, parity, err, code)) dead = true;
+}
+
 // Orders this thread's generic-proxy shared-memory accesses with later
 // async-proxy ones (TMA / bulk copies, tensor-core operand reads): after
 // writing an operand tile, and after reading a stage that a TMA refills once

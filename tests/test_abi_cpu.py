@@ -90,7 +90,9 @@ def test_harness_kv_format_of_every_definition():
         assert harness.flash_attention_kv_format(spec) == fmt
 
 
-@pytest.mark.parametrize("name", ["kernel_quant_gemm.cu", "kernel_flash_attn.cu", "kernel_flash_attn_q4_0.cu",
+@pytest.mark.parametrize("name", ["kernel_quant_gemm_q4_0.cu", "kernel_quant_gemm_q4_1.cu",
+                                  "kernel_quant_gemm_q8_0.cu", "kernel_quant_gemm_w4a8_q8_1.cu",
+                                  "kernel_flash_attn.cu", "kernel_flash_attn_q4_0.cu",
                                   "kernel_flash_attn_f16.cu", "kernel_rms_norm.cu"])
 def test_harness_forwarders_build(name, tmp_path):
     """The attempt files are host-only C++: they compile with g++ and export

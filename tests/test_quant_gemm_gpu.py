@@ -116,10 +116,10 @@ def test_gemm_row_magnitudes(cuda, wtype):
             assert ok, f"{mode} row {m}: {msg}"
 
 
-def test_split_path_opt_in(cuda):
-    """KQ_GEMM_PATH=split (the split-fp16 tcgen05 kernel for every M > 8,
-    including the M <= 128 shapes the skinny kernel takes by default), in a
-    child process: the full parity bar on every row."""
+def test_skinny_path_opt_in(cuda):
+    """KQ_GEMM_PATH=skinny (the warp-MMA kernel for 8 < M <= 128; the
+    split-fp16 tcgen05 kernel takes those shapes by default), in a child
+    process: the full parity bar on every row."""
     import os
     import subprocess
     import sys
@@ -139,7 +139,7 @@ def test_split_path_opt_in(cuda):
         "        ok, msg = Q.check_close(g[m:m + 1], ref[m:m + 1])\n"
         "        assert ok, (wt, M, N, K, mode, m, msg)\n"
         "print('ok')\n" % ([p for p in sys.path if p],))
-    env = dict(os.environ, KQ_GEMM_PATH="split")
+    env = dict(os.environ, KQ_GEMM_PATH="skinny")
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=900)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
 
