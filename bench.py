@@ -609,7 +609,9 @@ def bench_gemm(args, cfg, rank, world, *, steps, warmup, clocks_on=True):
         achieved = staged_bytes / (kms * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(achieved / hbm, 4), "traffic": None,
-                "kernel": "gemm_split_kernel (+ split_act_kernel prep)", "algorithmic_bytes": staged_bytes,
+                "kernel": ("gemm_skinny_kernel (warp MMA m16n8k32 per 32-block)" if M <= 16 else
+                           "gemm_split_kernel (+ split_act_kernel prep)"),
+                "algorithmic_bytes": staged_bytes,
                 "tops": round(ops / (kms * 1e-3) / 1e12, 2), "peak_source": f"{src} hbm_gbs (copy)"}
     else:
         # gemm_split_kernel: exact split-fp16 operands, three kind::f16 MMAs
@@ -626,11 +628,12 @@ def bench_gemm(args, cfg, rank, world, *, steps, warmup, clocks_on=True):
                 "peak_source": f"f16 dense = {src} bf16_tflops (cuBLAS bf16 burst); achieved counts the "
                                f"algorithmic 2MNK, executed_frac the 3 f16 MMAs per product; int8_peak: "
                                f"{i8['how']}"}
-    launches_per_step = 2 if M <= 8 else 3  # quantiser + GEMV | quantiser + split prep + split GEMM
+    # quantiser + GEMV | quantiser + skinny GEMM | quantiser + split prep + split GEMM
+    launches_per_step = 2 if M <= 16 else 3
     line = {
         "metric": metric, "value": round(value, 4), "unit": unit, "n_gpus": world, "steps": steps,
         "warmup": warmup, "ms_per_step": round(per, 5), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "int8" if M <= 8 else "f16 (exact split of the int8 x int8 block products)",
+        "vs_baseline": None, "dtype": "int8" if M <= 16 else "f16 (exact split of the int8 x int8 block products)",
         "data": "synthetic (seeded; weights drawn directly as q-blocks)",
         "config": {"workload": cfg["workload"], "M": M, "N": N, "K": K, "wtype": wt, "act_quant": cfg["act"],
                    "l2": f"{nsets} rotating input sets ({nsets * step_bytes / 1e6:.0f} MB > 2.5x L2)",

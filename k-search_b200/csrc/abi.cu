@@ -154,11 +154,12 @@ kq_status_t check_gemm_args(int wtype, const void* w, const void* a, const float
 }
 
 // Quantised activations are staged; choose the GEMM kernel for the shape.
-// M > 8 path: the exact split-fp16 tcgen05 kernel; KQ_GEMM_PATH=int8 runs
-// the int8 tcgen05 kernel (per-block int32 sums rescaled on the FP32 pipe)
-// for every M > 8, KQ_GEMM_PATH=skinny the warp-MMA kernel for 8 < M <= 128
-// (slower than the split kernel there: its unrolled code misses the
-// instruction cache). Read once per process.
+// M > 8 path: the warp-MMA skinny kernel for 8 < M <= 16 (measured faster
+// than the split kernel there: 40.8 against 46.1 us at M=16, 40.4 against
+// 57.6 at M=9, N=14336 K=4096 q4_0), the exact split-fp16 tcgen05 kernel
+// above; KQ_GEMM_PATH=int8 runs the int8 tcgen05 kernel (per-block int32
+// sums rescaled on the FP32 pipe) for every M > 8, KQ_GEMM_PATH=skinny the
+// skinny kernel up to its limit of 128 rows. Read once per process.
 enum class GemmPath { kDefault, kSkinny, kInt8 };
 GemmPath gemm_path() {
   static const GemmPath p = [] {
@@ -169,13 +170,18 @@ GemmPath gemm_path() {
   }();
   return p;
 }
+constexpr int kSkinnyDefaultMaxM = 16;
+bool use_skinny(int M) {
+  const GemmPath p = gemm_path();
+  return p == GemmPath::kSkinny || (p == GemmPath::kDefault && M <= kSkinnyDefaultMaxM);
+}
 
 // The tensor-core kernel for M > 8 with the given output destinations, or
 // KQ_ERR_UNSUPPORTED when none fits the shape.
 kq_status_t dispatch_gemm_tc(int wtype, const void* w, Act8 act, const OutSpec& out, int M, int N, int K,
                              cudaStream_t s, bool pdl) {
   const GemmPath path = gemm_path();
-  if (path == GemmPath::kSkinny && gemm_skinny_supported(wtype, M, N, K, w, act))
+  if (use_skinny(M) && gemm_skinny_supported(wtype, M, N, K, w, act))
     return launch_gemm_skinny(wtype, w, act, out, M, N, K, s);
   if (path != GemmPath::kInt8 && gemm_split_supported(wtype, M, N, K, w, act))
     return launch_gemm_split(wtype, w, act, out, M, N, K, s);
@@ -184,7 +190,7 @@ kq_status_t dispatch_gemm_tc(int wtype, const void* w, Act8 act, const OutSpec& 
 }
 
 bool gemm_tc_any_supported(int wtype, int M, int N, int K, const void* w, Act8 act) {
-  return (gemm_path() == GemmPath::kSkinny && gemm_skinny_supported(wtype, M, N, K, w, act)) ||
+  return (use_skinny(M) && gemm_skinny_supported(wtype, M, N, K, w, act)) ||
          (gemm_path() != GemmPath::kInt8 && gemm_split_supported(wtype, M, N, K, w, act)) ||
          gemm_tc_supported(wtype, M, N, K, w, act);
 }

@@ -164,15 +164,18 @@ __device__ __forceinline__ void put_out(const OutSpec& o, int m, int n, float v)
 }
 
 // Warps form a WR x WTOK grid over (row group, token group): warp (wr, wt)
-// takes row groups wr, wr + WR, ... and token groups wt, wt + WTOK, ...
-template <int WT, int WTOK>
+// takes row groups wr, wr + WR, ... and token groups wt, wt + WTOK, ...;
+// TPW (token groups per warp) is a template parameter sized to the launch's
+// token count, so the unrolled block loop holds only the token groups that
+// exist (an instantiation for 128 tokens run at 16 missed the instruction
+// cache on the guarded-off copies).
+template <int WT, int WTOK, int TPW>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_skinny_kernel(const __grid_constant__ CUtensorMap m_w, const __grid_constant__ CUtensorMap m_a,
                        const __grid_constant__ CUtensorMap m_s, const __grid_constant__ SkParams p) {
   using T = SkTraits<WT>;
   constexpr int WR = kComputeWarps / WTOK;
   constexpr int RPW = (kMaxGroups + WR - 1) / WR;  // row groups per warp (at most)
-  constexpr int TPW = (kMaxTok / 8 + WTOK - 1) / WTOK;  // token groups per warp (at most)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.stages * p.stage_bytes);
@@ -339,10 +342,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (p.out.n_out > 1) __threadfence_system();  // peer stores visible before the host-side barrier
 }
 
-template <int WT, int WTOK>
+template <int WT, int WTOK, int TPW>
 kq_status_t launch_cfg(const CUtensorMap& mw, const CUtensorMap& ma, const CUtensorMap& ms, const SkParams& p,
                        int grid, size_t smem, cudaStream_t s) {
-  auto kern = gemm_skinny_kernel<WT, WTOK>;
+  auto kern = gemm_skinny_kernel<WT, WTOK, TPW>;
   if (kq_status_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)smem, "gemm_skinny smem attribute"))
     return st;
   cudaLaunchConfig_t cfg = {};
@@ -408,10 +411,23 @@ kq_status_t launch_wt(const void* w, Act8 act, const OutSpec& out, int M, int N,
       best = wtok;
     }
   }
-  switch (best) {
-    case 1: return launch_cfg<WT, 1>(mw, ma, ms, p, grid, smem, s);
-    case 2: return launch_cfg<WT, 2>(mw, ma, ms, p, grid, smem, s);
-    default: return launch_cfg<WT, 4>(mw, ma, ms, p, grid, smem, s);
+  // token groups per warp, rounded up to the instantiated sizes
+  const int tpw = (ntg + best - 1) / best;
+  const int tp = tpw <= 1 ? 1 : tpw <= 2 ? 2 : tpw <= 4 ? 4 : tpw <= 8 ? 8 : 16;
+  switch (best * 100 + tp) {
+    case 101: return launch_cfg<WT, 1, 1>(mw, ma, ms, p, grid, smem, s);
+    case 102: return launch_cfg<WT, 1, 2>(mw, ma, ms, p, grid, smem, s);
+    case 104: return launch_cfg<WT, 1, 4>(mw, ma, ms, p, grid, smem, s);
+    case 108: return launch_cfg<WT, 1, 8>(mw, ma, ms, p, grid, smem, s);
+    case 116: return launch_cfg<WT, 1, 16>(mw, ma, ms, p, grid, smem, s);
+    case 201: return launch_cfg<WT, 2, 1>(mw, ma, ms, p, grid, smem, s);
+    case 202: return launch_cfg<WT, 2, 2>(mw, ma, ms, p, grid, smem, s);
+    case 204: return launch_cfg<WT, 2, 4>(mw, ma, ms, p, grid, smem, s);
+    case 208: return launch_cfg<WT, 2, 8>(mw, ma, ms, p, grid, smem, s);
+    case 401: return launch_cfg<WT, 4, 1>(mw, ma, ms, p, grid, smem, s);
+    case 402: return launch_cfg<WT, 4, 2>(mw, ma, ms, p, grid, smem, s);
+    case 404: return launch_cfg<WT, 4, 4>(mw, ma, ms, p, grid, smem, s);
+    default: return fail(KQ_ERR_UNSUPPORTED, "gemm_skinny: no instantiation for %d token groups", ntg);
   }
 }
 

@@ -151,6 +151,7 @@ __device__ __forceinline__ void mbar_wait_or_poison(uint64_t* bar, uint32_t pari
 // share an SM sub-partition with the warps doing the math: a spinning waiter
 // takes issue slots from them.
 __device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity, int* err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;  // no timer read on the common path
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;

@@ -136,10 +136,14 @@ def test_moe_stages(cuda, T, E, topk, H, I, mode):
 
 def test_full_size_config4_sampled_tokens(cuda):
     """configs[4] at full size (T=4096 tokens, 8 experts, top-2, H=4096,
-    I=14336, q4_0 weights): the fused operator runs on the whole batch; the
-    routing is checked for every token, and six sampled tokens (12 routed
-    rows) go through the staged pipeline, each stage checked at the bar, and
-    their fused output rows against the staged result."""
+    I=14336, q4_0 weights). The staged pipeline runs on all T * top-k routed
+    rows in the fused operator's own order, so every expert GEMM sees the same
+    rows with the same kernel as inside kq_moe_q4_0 (a GEMM on a handful of rows
+    takes another kernel whose fp32 rounding of gate / up differs, and one h
+    value on a q8_1 rounding boundary then takes the neighbouring code). The
+    routing is checked for every token; the stages at the bar on the routed rows
+    of six sampled tokens; the fused output of every token against the staged
+    rows combined with the routing weights."""
     import kq
     T, E, topk, H, I, mode = 4096, 8, 2, 4096, 14336, "sum_dq"
     rng = np.random.default_rng(4096)
@@ -154,11 +158,29 @@ def test_full_size_config4_sampled_tokens(cuda):
     ref_idx, ref_w = Q.moe_route(logits, topk)
     assert np.array_equal(idx, ref_idx)
     assert np.allclose(wts, ref_w, rtol=1e-6, atol=1e-7)
+    # all routed rows, (token, slot) order
+    P = T * topk
+    e_rows = idx.reshape(-1).astype(np.int32)
+    xd = _dev(x, cuda).repeat_interleave(topk, dim=0).contiguous()
+    f = lambda *sh: torch.empty(sh, dtype=torch.float32, device=cuda)  # noqa: E731
+    gate, up, h, y = f(P, I), f(P, I), f(P, I), f(P, H)
+    h_qs = torch.empty((P, I), dtype=torch.int8, device=cuda)
+    h_ds = f(P, I // 32, 2)
+    ed = _dev(e_rows, cuda)
+    st = kq.lib().kq_moe_experts_stages_q4_0(
+        xd.data_ptr(), ed.data_ptr(), wg_d.data_ptr(), wu_d.data_ptr(), wd_d.data_ptr(), E, P, H, I,
+        kq.ACT_MODES[mode], gate.data_ptr(), up.data_ptr(), h.data_ptr(), h_qs.data_ptr(), h_ds.data_ptr(),
+        y.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert st == 0, kq._lib.last_error()
+    # stages at the bar on the sampled tokens' rows
     toks = np.array([0, 1, 777, 2048, 4000, T - 1])
-    x_rows = np.repeat(x[toks], topk, axis=0)
-    e_rows = idx[toks].reshape(-1)
-    got = _stages(cuda, x_rows, e_rows, wg_d, wu_d, wd_d, E, H, I, mode)
-    _check_stages(x_rows, e_rows, wg, wu, wd, H, I, mode, got)
-    staged = (wts[toks][:, :, None].astype(np.float64) * got[5].reshape(len(toks), topk, H)).sum(axis=1)
-    ok, msg = Q.check_close(fused[toks], staged)
-    assert ok, f"fused rows vs staged: {msg}"
+    rows = (toks[:, None] * topk + np.arange(topk)[None, :]).reshape(-1)
+    rt = torch.from_numpy(rows).to(cuda)
+    got = tuple(t.index_select(0, rt).cpu().numpy() for t in (gate, up, h, h_qs, h_ds, y))
+    _check_stages(x[toks].repeat(topk, axis=0), e_rows[rows], wg, wu, wd, H, I, mode, got)
+    del gate, up, h, h_qs, h_ds
+    # fused output of every token against the staged rows and the routing weights
+    yh = y.cpu().numpy().astype(np.float64).reshape(T, topk, H)
+    staged = (wts[:, :, None].astype(np.float64) * yh).sum(axis=1)
+    ok, msg = Q.check_close(fused, staged)
+    assert ok, f"fused vs staged: {msg}"
