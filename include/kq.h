@@ -83,6 +83,14 @@ size_t kq_block_bytes(int wtype);
 /* Reads and clears the device error word of the current device (synchronises
  * the given stream). *code receives the first recorded device error (0 = none). */
 kq_status_t kq_device_error(int* code, kq_stream_t stream);
+/* Failure-detection self-test (no counterpart in the reference, which has no
+ * device-side waits): runs the library's bounded mbarrier wait on a barrier
+ * that nothing ever arrives at, with a wait limit of limit_ns (0 < limit_ns <=
+ * 2e9; the kernels use 2e9). The wait gives up, records DEV_TIMEOUT_FULL (1)
+ * in the device error word (first writer wins; read and cleared with
+ * kq_device_error) and the kernel returns. Synchronises the stream; returns
+ * KQ_ERR_TIMEOUT when the error word holds a timeout code. */
+kq_status_t kq_selftest_wait_timeout(int64_t limit_ns, kq_stream_t stream);
 
 /* ---- 1. KernelEvalPlus operator ABI (void, legacy default stream) -------- */
 

@@ -123,18 +123,22 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // hand-offs here complete within a few hundred cycles.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr int kSpinProbes = 32;
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* err, int code,
+                                              uint64_t limit_ns) {
 #pragma unroll 1
   for (int i = 0; i < kSpinProbes; ++i)
     if (mbar_test_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+    if ((i & 255u) == 0 && globaltimer_ns() - t0 > limit_ns) {
       record_error(err, code);
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  return mbar_wait_for(bar, parity, err, code, kWaitLimitNs);
 }
 
 // Wait that never blocks again once one wait of this thread has timed out:

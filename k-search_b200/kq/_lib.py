@@ -25,6 +25,7 @@ SIGNATURES = {
     "kq_last_error": (ctypes.c_char_p, []),
     "kq_block_bytes": (_sz, [_i]),
     "kq_device_error": (_i, [_vp, _vp]),
+    "kq_selftest_wait_timeout": (_i, [_i64, _vp]),
     "kq_w4a32c8_q4_0_fp32_int8": (None, [_vp, _vp, _vp, _i, _i, _i]),
     "kq_w4a32c8_q4_1_fp32_int8": (None, [_vp, _vp, _vp, _i, _i, _i]),
     "kq_w8a32c8_q8_0_fp32_int8": (None, [_vp, _vp, _vp, _i, _i, _i]),

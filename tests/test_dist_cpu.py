@@ -190,3 +190,47 @@ def _moe_rank(rank, world, T_per, E, topk, H, I):
 @pytest.mark.parametrize("T_per,E,topk", [(12, 4, 2), (3, 8, 2), (7, 2, 1)])
 def test_moe_expert_parallel_gloo(T_per, E, topk):
     _spawn(_moe_rank, 2, T_per, E, topk, 64, 96)
+
+
+# ---------------------------------------------------------------------------
+# failure detection on the host: a rank that leaves between steps
+# ---------------------------------------------------------------------------
+
+def _leaver_rank(rank, world, port, q):
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
+                      MASTER_PORT=str(port))
+    import time
+    rk, wd, _ = kd.init_from_env(backend="gloo", timeout_s=3.0)
+    t = torch.ones(8)
+    dist.all_reduce(t)  # step 1: every rank takes part
+    if rank == 1:
+        os._exit(0)  # leaves between steps, with nothing in flight
+    t0 = time.monotonic()
+    try:
+        dist.all_reduce(t)  # step 2: the peer is gone
+        q.put(("completed", time.monotonic() - t0, float(t[0])))
+    except Exception as e:  # noqa: BLE001 - any error is the expected outcome
+        q.put((type(e).__name__, time.monotonic() - t0, str(e)[:200]))
+    os._exit(0)  # no collective teardown with a dead peer
+
+
+def test_rank_leaving_between_steps_errors_instead_of_hanging():
+    """kq.dist.init_from_env gives the group a short timeout: after rank 1
+    exits between two steps, rank 0's next collective ends with an error (the
+    peer's closed connection or the timeout) within seconds instead of
+    hanging."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaver_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        kind, secs, detail = q.get(timeout=90)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert kind != "completed", detail
+    assert secs < 30, (kind, secs, detail)
