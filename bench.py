@@ -83,7 +83,7 @@ def sub_configs():
 NCU_TRAFFIC = {
     ("gemm_split", "q8_0 M=512 N=11008 K=4096"): 61.47e6,
     ("gemv", "q4_0 per weight row, K=4096"): 33.06e6 / 14336,
-    ("fa_fast", "per token row, Hkv=8 D=128"): 327.5e6 / 139124,
+    ("fa_stream", "per token row, Hkv=8 D=128"): (303.26e6 + 3.49e6) / 139124,
 }
 
 
@@ -746,7 +746,7 @@ def bench_fa(args, cfg, rank, world, *, steps, warmup, clocks_on=True):
                    f"rank loads {plan.load()}"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "algorithmic_bytes": algo,
-                     "traffic": round(NCU_TRAFFIC[("fa_fast", "per token row, Hkv=8 D=128")] * T)
+                     "traffic": round(NCU_TRAFFIC[("fa_stream", "per token row, Hkv=8 D=128")] * T)
                      if (Hkv == 8 and D == 128) else None,
                      "kernel": "fa decode (partial + combine), timed together",
                      "peak_source": f"{src} hbm_gbs"},
