@@ -155,8 +155,9 @@ kq_status_t check_gemm_args(int wtype, const void* w, const void* a, const float
 
 // Quantised activations are staged; choose the GEMM kernel for the shape.
 // M > 8 path: the warp-MMA skinny kernel for 8 < M <= 16 (measured faster
-// than the split kernel there: 40.8 against 46.1 us at M=16, 40.4 against
-// 57.6 at M=9, N=14336 K=4096 q4_0), the exact split-fp16 tcgen05 kernel
+// than the split kernel there: 30.6 against 46.1 us at M=16, 30.5 against
+// 57.6 at M=9, N=14336 K=4096 q4_0; from M=24 the split kernel is faster,
+// 47 against 49 us), the exact split-fp16 tcgen05 kernel
 // above; KQ_GEMM_PATH=int8 runs the int8 tcgen05 kernel (per-block int32
 // sums rescaled on the FP32 pipe) for every M > 8, KQ_GEMM_PATH=skinny the
 // skinny kernel up to its limit of 128 rows. Read once per process.

@@ -35,8 +35,8 @@ constexpr int kRowsPerGroup = 16;
 constexpr int kMaxGroups = 8;            // row groups per CTA
 constexpr int kMaxTok = 128;             // activation rows
 constexpr int kChunkK = 256;             // K elements per stage (8 blocks)
-constexpr int kComputeWarps = 8;
-constexpr int kThreads = 32 * (kComputeWarps + 1);
+constexpr int kComputeWarps = 8;   // per K half
+constexpr int threads_of(int ks) { return 32 * (kComputeWarps * ks + 1); }
 constexpr uint32_t kMagic = 0x4B400000u; // bits of 12582912.0f = 1.5 * 2^23
 constexpr float kMagicF = 12582912.0f;
 
@@ -53,6 +53,7 @@ struct SkParams {
   int RG;             // row groups ceil(N / 16)
   int stages;
   int stage_bytes;    // one ring stage: A codes | scales | weights
+  int off_x;          // K split: partial-sum exchange buffer (after the ring and its barriers)
   int off_s, off_w;   // offsets of the scales and weights inside a stage
   int* err;
 };
@@ -168,12 +169,17 @@ __device__ __forceinline__ void put_out(const OutSpec& o, int m, int n, float v)
 // TPW (token groups per warp) is a template parameter sized to the launch's
 // token count, so the unrolled block loop holds only the token groups that
 // exist (an instantiation for 128 tokens run at 16 missed the instruction
-// cache on the guarded-off copies).
-template <int WT, int WTOK, int TPW>
-__global__ void __launch_bounds__(kThreads, 1)
+// cache on the guarded-off copies). KS = 2 splits every chunk's 8 blocks
+// between two warps per (row group, token group) - blocks 0-3 and 4-7 - so
+// twice as many warps hide the MMA -> FMA latency when there are few token
+// groups; the two partial sums meet in shared memory at the end.
+template <int WT, int WTOK, int TPW, int KS>
+__global__ void __launch_bounds__(threads_of(KS), 1)
     gemm_skinny_kernel(const __grid_constant__ CUtensorMap m_w, const __grid_constant__ CUtensorMap m_a,
                        const __grid_constant__ CUtensorMap m_s, const __grid_constant__ SkParams p) {
   using T = SkTraits<WT>;
+  constexpr int CW = kComputeWarps * KS;  // compute warps
+  constexpr int BPW = 8 / KS;             // blocks of a chunk per warp
   constexpr int WR = kComputeWarps / WTOK;
   constexpr int RPW = (kMaxGroups + WR - 1) / WR;  // row groups per warp (at most)
   extern __shared__ uint8_t smem_raw[];
@@ -192,14 +198,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kComputeWarps);
+      mbar_init(&empty[s], CW);
     }
     fence_mbar_init();
   }
   __syncthreads();
 
   bool dead = false;
-  if (warp == kComputeWarps) {
+  if (warp == CW) {
     // ---------------- producer ----------------
     if (lane == 0) {
       const uint32_t wbytes = (uint32_t)(GC * kRowsPerGroup * T::ROW);
@@ -237,7 +243,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // ---------------- compute warp ----------------
-  const int wr = warp % WR, wt = warp / WR;
+  const int kh = warp / kComputeWarps, w8 = warp % kComputeWarps;  // K half, warp within it
+  const int wr = w8 % WR, wt = w8 / WR;
   const int gid = lane >> 2, tid = lane & 3;
   uint64_t acc[RPW][TPW][2];  // [row group][token group][row g | row g + 8] x tokens 2 tid, 2 tid + 1
 #pragma unroll
@@ -253,7 +260,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float2* sc = reinterpret_cast<const float2*>(st + p.off_s);   // [Mp][8] (d, s)
     const uint8_t* wst = st + p.off_w;
 #pragma unroll
-    for (int blk = 0; blk < 8; ++blk) {
+    for (int bi = 0; bi < BPW; ++bi) {
+      const int blk = bi + kh * BPW;
       uint32_t a[RPW][4];
       uint64_t dwg[RPW], dwh[RPW], mwg[RPW] = {}, mwh[RPW] = {};
 #pragma unroll
@@ -318,6 +326,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) mbar_arrive(&empty[s]);
   }
 
+  if constexpr (KS == 2) {
+    // the second K half hands its partial sums to the first
+    uint64_t* xb = reinterpret_cast<uint64_t*>(smem + p.off_x) + ((size_t)w8 * 32 + lane) * (RPW * TPW * 2);
+    if (kh == 1) {
+#pragma unroll
+      for (int i = 0; i < RPW; ++i)
+#pragma unroll
+        for (int j = 0; j < TPW; ++j) {
+          xb[(i * TPW + j) * 2] = acc[i][j][0];
+          xb[(i * TPW + j) * 2 + 1] = acc[i][j][1];
+        }
+    }
+    named_bar_sync(1, CW * 32);
+    if (kh == 1) return;
+#pragma unroll
+    for (int i = 0; i < RPW; ++i)
+#pragma unroll
+      for (int j = 0; j < TPW; ++j) {
+        acc[i][j][0] = add2(acc[i][j][0], xb[(i * TPW + j) * 2]);
+        acc[i][j][1] = add2(acc[i][j][1], xb[(i * TPW + j) * 2 + 1]);
+      }
+  }
+
   // ---- store: rows 16 (rg0 + r) + gid (+ 8), tokens 8 t + 2 tid (+ 1) ----
 #pragma unroll
   for (int i = 0; i < RPW; ++i) {
@@ -342,15 +373,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (p.out.n_out > 1) __threadfence_system();  // peer stores visible before the host-side barrier
 }
 
-template <int WT, int WTOK, int TPW>
+template <int WT, int WTOK, int TPW, int KS>
 kq_status_t launch_cfg(const CUtensorMap& mw, const CUtensorMap& ma, const CUtensorMap& ms, const SkParams& p,
                        int grid, size_t smem, cudaStream_t s) {
-  auto kern = gemm_skinny_kernel<WT, WTOK, TPW>;
+  auto kern = gemm_skinny_kernel<WT, WTOK, TPW, KS>;
   if (kq_status_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)smem, "gemm_skinny smem attribute"))
     return st;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(threads_of(KS));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -379,10 +410,6 @@ kq_status_t launch_wt(const void* w, Act8 act, const OutSpec& out, int M, int N,
   p.off_s = 2 * p.Mp * 128;
   p.off_w = p.off_s + p.Mp * 64;
   p.stage_bytes = (p.off_w + gc * kRowsPerGroup * T::ROW + 1023) & ~1023;
-  const size_t budget = 227 * 1024 - 1024 - 256;
-  p.stages = (int)std::min<size_t>(4, budget / p.stage_bytes);
-  if (p.stages < 2) return fail(KQ_ERR_UNSUPPORTED, "gemm_skinny: stage of %d bytes does not fit twice", p.stage_bytes);
-  const size_t smem = (size_t)p.stages * p.stage_bytes + 2 * p.stages * 8 + 1024;
   p.err = err ? err : device_error_word();
 
   const int nb = K / 32;
@@ -414,19 +441,28 @@ kq_status_t launch_wt(const void* w, Act8 act, const OutSpec& out, int M, int N,
   // token groups per warp, rounded up to the instantiated sizes
   const int tpw = (ntg + best - 1) / best;
   const int tp = tpw <= 1 ? 1 : tpw <= 2 ? 2 : tpw <= 4 ? 4 : tpw <= 8 ? 8 : 16;
-  switch (best * 100 + tp) {
-    case 101: return launch_cfg<WT, 1, 1>(mw, ma, ms, p, grid, smem, s);
-    case 102: return launch_cfg<WT, 1, 2>(mw, ma, ms, p, grid, smem, s);
-    case 104: return launch_cfg<WT, 1, 4>(mw, ma, ms, p, grid, smem, s);
-    case 108: return launch_cfg<WT, 1, 8>(mw, ma, ms, p, grid, smem, s);
-    case 116: return launch_cfg<WT, 1, 16>(mw, ma, ms, p, grid, smem, s);
-    case 201: return launch_cfg<WT, 2, 1>(mw, ma, ms, p, grid, smem, s);
-    case 202: return launch_cfg<WT, 2, 2>(mw, ma, ms, p, grid, smem, s);
-    case 204: return launch_cfg<WT, 2, 4>(mw, ma, ms, p, grid, smem, s);
-    case 208: return launch_cfg<WT, 2, 8>(mw, ma, ms, p, grid, smem, s);
-    case 401: return launch_cfg<WT, 4, 1>(mw, ma, ms, p, grid, smem, s);
-    case 402: return launch_cfg<WT, 4, 2>(mw, ma, ms, p, grid, smem, s);
-    case 404: return launch_cfg<WT, 4, 4>(mw, ma, ms, p, grid, smem, s);
+  // few token groups: split each chunk's blocks between two warps
+  const int ks = (best == 1 && tp <= 2) ? 2 : 1;
+  const int rpw_max = (kMaxGroups + kComputeWarps / best - 1) / (kComputeWarps / best);
+  const size_t xbytes = ks == 2 ? (size_t)kComputeWarps * 32 * rpw_max * tp * 2 * 8 : 0;
+  const size_t budget = 227 * 1024 - 1024 - 256 - xbytes;
+  p.stages = (int)std::min<size_t>(4, budget / p.stage_bytes);
+  if (p.stages < 2) return fail(KQ_ERR_UNSUPPORTED, "gemm_skinny: stage of %d bytes does not fit twice", p.stage_bytes);
+  p.off_x = (p.stages * p.stage_bytes + 2 * p.stages * 8 + 15) & ~15;
+  const size_t smem = (size_t)p.off_x + xbytes + 1024;
+  switch (ks * 1000 + best * 100 + tp) {
+    case 2101: return launch_cfg<WT, 1, 1, 2>(mw, ma, ms, p, grid, smem, s);
+    case 2102: return launch_cfg<WT, 1, 2, 2>(mw, ma, ms, p, grid, smem, s);
+    case 1104: return launch_cfg<WT, 1, 4, 1>(mw, ma, ms, p, grid, smem, s);
+    case 1108: return launch_cfg<WT, 1, 8, 1>(mw, ma, ms, p, grid, smem, s);
+    case 1116: return launch_cfg<WT, 1, 16, 1>(mw, ma, ms, p, grid, smem, s);
+    case 1201: return launch_cfg<WT, 2, 1, 1>(mw, ma, ms, p, grid, smem, s);
+    case 1202: return launch_cfg<WT, 2, 2, 1>(mw, ma, ms, p, grid, smem, s);
+    case 1204: return launch_cfg<WT, 2, 4, 1>(mw, ma, ms, p, grid, smem, s);
+    case 1208: return launch_cfg<WT, 2, 8, 1>(mw, ma, ms, p, grid, smem, s);
+    case 1401: return launch_cfg<WT, 4, 1, 1>(mw, ma, ms, p, grid, smem, s);
+    case 1402: return launch_cfg<WT, 4, 2, 1>(mw, ma, ms, p, grid, smem, s);
+    case 1404: return launch_cfg<WT, 4, 4, 1>(mw, ma, ms, p, grid, smem, s);
     default: return fail(KQ_ERR_UNSUPPORTED, "gemm_skinny: no instantiation for %d token groups", ntg);
   }
 }
