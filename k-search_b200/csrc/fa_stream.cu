@@ -19,10 +19,10 @@
 // unique because ranges are contiguous), and the combine kernel merges the
 // partials of each query.
 //
-// CTA: one TMA producer warp streams K and V tiles (16 token rows x 8 heads,
-// the cache's own 1088-byte rows, landing at a 1104-byte pitch so that
-// fragment loads from different rows fall in different banks) into a
-// two-stage ring; 8 compute warps each own one KV head and its (up to 4)
+// CTA (two per SM): warp 0's lane 0 streams K and V tiles by TMA (16 token
+// rows x 8 heads, the cache's own 1088-byte rows, landing at a 1104-byte
+// pitch so that fragment loads from different rows fall in different banks)
+// into a two-stage ring, refilling a stage once all warps released it; 8 compute warps each own one KV head and its (up to 4)
 // queries:
 //   QK  mma.m16n8k32 s8: A = the raw K codes of 16 tokens x one 32-dim block
 //       (all 16 rows used), B = the queries as two int8 levels
@@ -60,7 +60,11 @@ constexpr int kHeadBytes = 136;             // one head's row: 4 q8_0 blocks of 
 constexpr int kBoxU64 = 138;                // TMA box width in 8-byte units: 1088 B of row + 16 B
 constexpr int kPitch = kBoxU64 * 8;         // 1104: smem row pitch (276 words = 20 mod 32 banks)
 constexpr int kTile = kTok * kPitch;        // 17664 bytes per K (or V) tile
-constexpr int kThreads = 32 * (kHeads + 1);
+// 8 warps, no separate producer warp: two CTAs per SM then fit the register
+// file of each SM sub-partition (a 9-warp CTA puts 3 warps on one, and two of
+// those at 112 registers do not fit), doubling the warps that hide the
+// per-tile latency chain. Warp 0's lane 0 issues the TMA loads.
+constexpr int kThreads = 32 * kHeads;
 constexpr int kMaxSeq = 512;                // ragged sequences the schedule table holds
 constexpr int kVhPitch = 272;               // fp16 V tile row: 256 B + 16 (ldmatrix rows in distinct banks)
 
@@ -268,27 +272,20 @@ __global__ void __maxnreg__(112)
   __syncthreads();
 
   bool dead = false;
-  if (warp == kHeads) {
-    // ---------------- producer ----------------
-    if (lane == 0) {
-      int b, hg, j;
-      sc.locate(t_begin, b, hg, j);
-      const int ntiles = (int)(t_end - t_begin);
-      for (int k = 0; k < ntiles; ++k) {
-        const int s = k % kStages;
-        if (k >= kStages) mbar_wait_or_poison(&empty[s], ((k / kStages) - 1) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
-        mbar_arrive_expect_tx(&full[s], 2 * kTile);
-        const int row0 = RAGGED ? p.cu[b] : 0;
-        const int y = row0 + j * kTok;
-        tma_load_2d(smem + s * kTile, &kmap, hg * (kHeads * kHeadBytes / 8), y, &full[s]);
-        tma_load_2d(smem + kOffV + s * kTile, &vmap, hg * (kHeads * kHeadBytes / 8), y, &full[s]);
-        sc.next(b, hg, j);
-      }
-      // every issued tile must be consumed before the CTA exits
-      for (int k = max(0, ntiles - kStages); k < ntiles; ++k)
-        mbar_wait_or_poison(&empty[k % kStages], (k / kStages) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
-    }
-    return;
+  // ---- TMA issue (warp 0, lane 0): tile k goes to stage k % kStages ----
+  int pb = 0, phg = 0, pj = 0;  // position of the next tile to issue
+  const int ntiles = (int)(t_end - t_begin);
+  auto issue = [&](int s) {
+    mbar_arrive_expect_tx(&full[s], 2 * kTile);
+    const int row0 = RAGGED ? p.cu[pb] : 0;
+    const int y = row0 + pj * kTok;
+    tma_load_2d(smem + s * kTile, &kmap, phg * (kHeads * kHeadBytes / 8), y, &full[s]);
+    tma_load_2d(smem + kOffV + s * kTile, &vmap, phg * (kHeads * kHeadBytes / 8), y, &full[s]);
+    sc.next(pb, phg, pj);
+  };
+  if (warp == 0 && lane == 0) {
+    sc.locate(t_begin, pb, phg, pj);
+    for (int k = 0; k < min(kStages, ntiles); ++k) issue(k);
   }
 
   // ---------------- compute warp w: KV head hg * 8 + w ----------------
@@ -396,7 +393,6 @@ __global__ void __maxnreg__(112)
 
   int b, hg, j;
   sc.locate(t_begin, b, hg, j);
-  const int ntiles = (int)(t_end - t_begin);
   for (int k = 0; k < ntiles; ++k) {
     if (b * p.n_hg + hg != cur_item) {
       if (cur_item >= 0) flush_item();
@@ -466,6 +462,11 @@ __global__ void __maxnreg__(112)
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
+    if (warp == 0 && lane == 0 && k + kStages < ntiles) {
+      // refill this stage once every warp has released it
+      mbar_wait_or_poison(&empty[s], (k / kStages) & 1, p.err, DEV_TIMEOUT_EMPTY, dead);
+      issue(s);
+    }
 
     // ---- online softmax for query tid ----
     float mx = fmaxf(sc0, sc1);
@@ -651,9 +652,17 @@ int grid_size(const void* kern, int slot) {
   return g;
 }
 
+// Tiles per CTA below which one CTA per SM is faster than two (the start of
+// the two-stage ring and each item's query setup are paid per CTA): at
+// S = 8192, B = 1 (~14 tiles per SM) one CTA per SM took 69 us and two 99 us,
+// at B = 8 (~28 tiles per SM) 76 and 83 us; the ragged configs[3] workload
+// (~59 tiles per SM: 118.7 -> 108.5 us) and B = 512 (2.88 -> 2.10 ms at
+// S = 8192) run faster with two.
+constexpr long long kTwoCtaMinTilesPerSm = 32;
+
 template <typename QT, typename OT, bool RAGGED>
 kq_status_t launch(StreamParams p, const void* k, const void* v, uint64_t rows, int heads, long long Q,
-                   cudaStream_t s) {
+                   long long tiles_estimate, cudaStream_t s) {
   CUtensorMap km, vm;
   if (!encode_map(&km, k, rows, heads) || !encode_map(&vm, v, rows, heads))
     return fail(KQ_ERR_CUDA, "fa_stream: KV tensor map rejected");
@@ -662,7 +671,8 @@ kq_status_t launch(StreamParams p, const void* k, const void* v, uint64_t rows, 
   if (st) return st;
   // one wave of resident CTAs (two per SM when the carveout allows it): the
   // schedule splits the tiles evenly over exactly the CTAs that run at once
-  const int G = grid_size(reinterpret_cast<const void*>(kern), RAGGED ? 0 : 1);
+  int G = grid_size(reinterpret_cast<const void*>(kern), RAGGED ? 0 : 1);
+  if (tiles_estimate < kTwoCtaMinTilesPerSm * sm_count()) G = std::min(G, sm_count());
   kern<<<G, kThreads, kSmem, s>>>(km, vm, p);
   if ((st = check_launch("fa_stream"))) return st;
   fa_stream_combine_kernel<OT, RAGGED><<<(unsigned)((Q + 3) / 4), 128, 0, s>>>(p, (int)Q, G);
@@ -715,7 +725,8 @@ kq_status_t launch_fa_stream_ragged(const void* q, const void* k, const void* v,
   p.S = 0;
   p.n_hg = n_hg;
   p.qscale = (float)((double)scale * 1.4426950408889634);
-  return launch<__half, __half, true>(p, k, v, (uint64_t)std::max(total_rows, 1), Hkv, (long long)B * Hq, s);
+  const long long tiles = ((long long)total_rows + (long long)B * (kTok - 1)) / kTok * n_hg;  // upper bound
+  return launch<__half, __half, true>(p, k, v, (uint64_t)std::max(total_rows, 1), Hkv, (long long)B * Hq, tiles, s);
 }
 
 kq_status_t launch_fa_stream_mha(const float* q, const void* k, const void* v, float* out, int B, int S, int H,
@@ -738,7 +749,8 @@ kq_status_t launch_fa_stream_mha(const float* q, const void* k, const void* v, f
   p.S = S;
   p.n_hg = n_hg;
   p.qscale = (float)(1.0 / std::sqrt(128.0) * 1.4426950408889634);
-  return launch<float, float, false>(p, k, v, (uint64_t)std::max(S, 1), H, (long long)B * H, s);
+  const long long tiles = (long long)items * ((S + kTok - 1) / kTok);
+  return launch<float, float, false>(p, k, v, (uint64_t)std::max(S, 1), H, (long long)B * H, tiles, s);
 }
 
 }  // namespace kq
