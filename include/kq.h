@@ -266,6 +266,17 @@ kq_status_t kq_moe_route(const float* router_logits, int T, int E, int topk, int
 kq_status_t kq_moe_experts_q4_0(const float* x_rows, const int32_t* expert_of_row, const void* w_gate,
                                 const void* w_up, const void* w_down, int E, int P, int H, int I, int act_mode,
                                 float* y_rows, kq_stream_t stream);
+/* kq_moe_experts_q4_0 on rows that arrive already quantised: a_rows are P
+ * rows of q8_1 blocks (H/32 blocks of 36 bytes each, the layout
+ * kq_quantize_q8_1 writes), for instance received from another rank in an
+ * expert-parallel dispatch (a third of the bytes of fp32 rows). act_mode
+ * applies to the re-quantisation of silu(gate) * up. Same results as
+ * kq_moe_experts_q4_0 on the fp32 rows those bytes were quantised from in the
+ * same mode (KQ_ACT_SUM_X or KQ_ACT_SUM_DQ). No counterpart in the reference
+ * (it has no MoE operator). */
+kq_status_t kq_moe_experts_q4_0_q8_1(const void* a_rows, const int32_t* expert_of_row, const void* w_gate,
+                                     const void* w_up, const void* w_down, int E, int P, int H, int I, int act_mode,
+                                     float* y_rows, kq_stream_t stream);
 
 /* Parity debugging: kq_moe_experts_q4_0 that also writes the pipeline's own
  * intermediates in the input row order: gate = x W_gate^T and up = x W_up^T

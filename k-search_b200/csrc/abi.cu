@@ -458,6 +458,21 @@ kq_status_t kq_moe_experts_q4_0(const float* x_rows, const int32_t* expert_of_ro
                                  static_cast<cudaStream_t>(stream));
 }
 
+kq_status_t kq_moe_experts_q4_0_q8_1(const void* a_rows, const int32_t* expert_of_row, const void* w_gate,
+                                     const void* w_up, const void* w_down, int E, int P, int H, int I, int act_mode,
+                                     float* y_rows, kq_stream_t stream) {
+  if (P < 0 || H <= 0 || I <= 0 || H % 32 || I % 32)
+    return fail(KQ_ERR_INVALID, "moe experts q8_1: bad shape P=%d H=%d I=%d", P, H, I);
+  if (act_mode < KQ_ACT_SUM_X || act_mode > KQ_ACT_F32) return fail(KQ_ERR_INVALID, "unknown activation mode %d", act_mode);
+  if (P == 0) return KQ_OK;
+  if (!a_rows || !expert_of_row || !w_gate || !w_up || !w_down || !y_rows)
+    return fail(KQ_ERR_INVALID, "moe experts q8_1: null pointer");
+  if (!aligned(a_rows, 4) || !aligned(y_rows, 16))
+    return fail(KQ_ERR_INVALID, "moe experts q8_1: rows must be 4-byte (q8_1) / 16-byte (output) aligned");
+  return launch_moe_experts_q4_0(nullptr, expert_of_row, w_gate, w_up, w_down, E, P, H, I, act_mode, y_rows,
+                                 static_cast<cudaStream_t>(stream), nullptr, a_rows);
+}
+
 kq_status_t kq_moe_experts_stages_q4_0(const float* x_rows, const int32_t* expert_of_row, const void* w_gate,
                                        const void* w_up, const void* w_down, int E, int P, int H, int I, int act_mode,
                                        float* gate, float* up, float* h, int8_t* h_qs, float* h_ds, float* y_rows,

@@ -90,6 +90,8 @@ kq_status_t launch_quantize_act(const float* x, Act8 act, int M, int K, int mode
 kq_status_t launch_quantize_q8_1_bytes(const float* x, void* y, int64_t M, int64_t K, int mode, cudaStream_t s);
 kq_status_t launch_quantize_rows(int wtype, const float* x, void* y, int64_t rows, int64_t K, cudaStream_t s);
 kq_status_t launch_q8_1_to_act(const void* a_q8_1, Act8 act, int M, int K, cudaStream_t s);
+// Row r of the staging takes q8_1 row rowmap[r] (K/32 blocks of 36 B per row).
+kq_status_t launch_q8_1_to_act_gather(const void* a_q8_1, const int* rowmap, Act8 act, int M, int K, cudaStream_t s);
 // out = x / sqrt(mean(x^2) + eps) * w per row of x fp32 [M, K]
 kq_status_t launch_rms_norm(const float* x, const float* w, float* out, int M, int K, float eps, cudaStream_t s);
 // RMSNorm then q8_1: into the staging `act` (q81 == nullptr) or as q8_1 bytes
@@ -143,7 +145,8 @@ struct MoeStages {
 };
 kq_status_t launch_moe_experts_q4_0(const float* x_rows, const int* expert_of_row, const void* w_gate,
                                     const void* w_up, const void* w_down, int E, int P, int H, int I, int act_mode,
-                                    float* y_rows, cudaStream_t s, const MoeStages* stages = nullptr);
+                                    float* y_rows, cudaStream_t s, const MoeStages* stages = nullptr,
+                                    const void* a_q8_1 = nullptr);  // a_q8_1: q8_1 rows replace x_rows
 kq_status_t launch_moe_combine(const float* y, const float* wts, int T, int topk, int H, float* out, cudaStream_t s);
 kq_status_t launch_moe_q4_0(const float* x, const float* logits, const void* w_gate, const void* w_up,
                             const void* w_down, int E, int topk, int T, int H, int I, int act_mode, float* out,

@@ -225,11 +225,13 @@ bool moe_ws(int P, int E, int H, int I, MoeWs* w) {
   return true;
 }
 
-// Expert FFNs of P routed rows. Row p reads x row p / div and goes to expert
+// Expert FFNs of P routed rows. Row p reads x row p / div (or, with a_q8_1,
+// row p of those pre-quantised q8_1 rows) and goes to expert
 // expert_of_pair[p] (w.counts already holds the per-expert row counts). The
 // result for row p lands in w.Y[w.row_of_pair[p]].
 kq_status_t moe_core(const float* x, int div, const int* expert_of_pair, int P, int E, const void* w_gate,
-                     const void* w_up, const void* w_down, int H, int I, int act_mode, MoeWs& w, cudaStream_t s) {
+                     const void* w_up, const void* w_down, int H, int I, int act_mode, MoeWs& w, cudaStream_t s,
+                     const void* a_q8_1 = nullptr) {
   expert_rank_kernel<<<E, 1024, 0, s>>>(expert_of_pair, w.counts, P, E, w.row_of_pair, w.pair_of_row);
   kq_status_t st = check_launch("moe rank");
   if (st) return st;
@@ -237,7 +239,11 @@ kq_status_t moe_core(const float* x, int div, const int* expert_of_pair, int P, 
   if ((st = check_cuda(cudaMemcpyAsync(hc, w.counts, E * sizeof(int), cudaMemcpyDeviceToHost, s), "moe counts d2h")))
     return st;
   if ((st = check_cuda(cudaStreamSynchronize(s), "moe counts sync"))) return st;
-  if ((st = launch_quantize_act_gather(x, w.pair_of_row, div, w.ax, P, H, act_mode, s))) return st;
+  if (a_q8_1) {
+    if ((st = launch_q8_1_to_act_gather(a_q8_1, w.pair_of_row, w.ax, P, H, s))) return st;
+  } else if ((st = launch_quantize_act_gather(x, w.pair_of_row, div, w.ax, P, H, act_mode, s))) {
+    return st;
+  }
   const size_t gate_bytes = (size_t)I * (H / 32) * 18, down_bytes = (size_t)H * (I / 32) * 18;
   auto rows = [](Act8 a, int r0, int K) { return Act8{a.qs + (size_t)r0 * K, a.ds + (size_t)r0 * (K / 32)}; };
   int r0 = 0;
@@ -295,7 +301,7 @@ kq_status_t launch_moe_combine(const float* y, const float* wts, int T, int topk
 
 kq_status_t launch_moe_experts_q4_0(const float* x_rows, const int* expert_of_row, const void* w_gate,
                                     const void* w_up, const void* w_down, int E, int P, int H, int I, int act_mode,
-                                    float* y_rows, cudaStream_t s, const MoeStages* stages) {
+                                    float* y_rows, cudaStream_t s, const MoeStages* stages, const void* a_q8_1) {
   kq_status_t st = check_moe(E, 1, H, I);
   if (st || P == 0) return st;
   MoeWs w;
@@ -303,7 +309,8 @@ kq_status_t launch_moe_experts_q4_0(const float* x_rows, const int* expert_of_ro
   if ((st = check_cuda(cudaMemsetAsync(w.counts, 0, E * sizeof(int), s), "moe counts"))) return st;
   count_kernel<<<(P + 255) / 256, 256, 0, s>>>(expert_of_row, P, w.counts);
   if ((st = check_launch("moe count"))) return st;
-  if ((st = moe_core(x_rows, 1, expert_of_row, P, E, w_gate, w_up, w_down, H, I, act_mode, w, s))) return st;
+  if ((st = moe_core(x_rows, 1, expert_of_row, P, E, w_gate, w_up, w_down, H, I, act_mode, w, s, a_q8_1)))
+    return st;
   unsort_kernel<<<P, 256, 0, s>>>(w.Y, w.row_of_pair, H, y_rows);
   if ((st = check_launch("moe unsort"))) return st;
   if (stages) {

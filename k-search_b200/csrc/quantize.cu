@@ -151,11 +151,16 @@ __global__ void __launch_bounds__(256) quantize_kernel(const float* __restrict__
 }
 
 // q8_1 bytes [blocks, 36] -> staging layout. One thread per block.
+// q8_1 bytes (36-byte blocks) -> staging. With a row map, output row r
+// reads row rowmap[r] of a (nb blocks per row): the MoE expert pipeline's
+// grouping of received q8_1 rows.
 __global__ void __launch_bounds__(256) q8_1_to_act_kernel(const uint8_t* __restrict__ a, int8_t* __restrict__ qs,
-                                                          float2* __restrict__ ds, long long total_blocks) {
+                                                          float2* __restrict__ ds, long long total_blocks,
+                                                          const int* __restrict__ rowmap = nullptr, int nb = 1) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < total_blocks) {
-    const uint32_t* src = reinterpret_cast<const uint32_t*>(a + i * 36);
+    const long long si = rowmap ? (long long)rowmap[i / nb] * nb + i % nb : i;
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(a + si * 36);
     const uint32_t h = src[0];
     uint4 lo = make_uint4(src[1], src[2], src[3], src[4]);
     uint4 hi = make_uint4(src[5], src[6], src[7], src[8]);
@@ -425,6 +430,15 @@ kq_status_t launch_q8_1_to_act(const void* a_q8_1, Act8 act, int M, int K, cudaS
   const int grid = (int)((nb + 255) / 256);
   q8_1_to_act_kernel<<<grid, 256, 0, s>>>(static_cast<const uint8_t*>(a_q8_1), act.qs, act.ds, nb);
   return check_launch("q8_1_to_act");
+}
+
+kq_status_t launch_q8_1_to_act_gather(const void* a_q8_1, const int* rowmap, Act8 act, int M, int K, cudaStream_t s) {
+  const long long total = (long long)M * (K / 32);
+  if (total == 0) return KQ_OK;
+  const int grid = (int)((total + 255) / 256);
+  q8_1_to_act_kernel<<<grid, 256, 0, s>>>(static_cast<const uint8_t*>(a_q8_1), act.qs, act.ds, total, rowmap,
+                                          K / 32);
+  return check_launch("q8_1_to_act_gather");
 }
 
 kq_status_t launch_rms_norm(const float* x, const float* w, float* out, int M, int K, float eps, cudaStream_t s) {

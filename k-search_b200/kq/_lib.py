@@ -53,6 +53,7 @@ SIGNATURES = {
     "kq_copy_2d": (_i, [_vp, ctypes.c_size_t, _vp, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t, _vp]),
     "kq_moe_route": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp]),
     "kq_moe_experts_q4_0": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp]),
+    "kq_moe_experts_q4_0_q8_1": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp]),
     "kq_moe_experts_stages_q4_0": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp,
                                         _vp]),
     "kq_moe_combine": (_i, [_vp, _vp, _i, _i, _i, _vp, _vp]),

@@ -395,7 +395,8 @@ def _ops():
 def moe_expert_parallel(x: torch.Tensor, router_logits: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
                         w_down: torch.Tensor, E: int, topk: int = 2, act_mode: str = "sum_dq", group=None,
                         route_fn: Callable | None = None, experts_fn: Callable | None = None,
-                        combine_fn: Callable | None = None, stats: dict | None = None) -> torch.Tensor:
+                        combine_fn: Callable | None = None, stats: dict | None = None,
+                        quant_fn: Callable | None = None, experts_q8_fn: Callable | None = None) -> torch.Tensor:
     """Expert-parallel grouped MoE FFN for this rank's tokens.
 
     x fp32 [T_r, H] and router_logits fp32 [T_r, E] are this rank's tokens;
@@ -403,12 +404,28 @@ def moe_expert_parallel(x: torch.Tensor, router_logits: torch.Tensor, w_gate: to
     laid out as for ``ops.moe_q4_0``. Returns fp32 [T_r, H], the same values
     the single-GPU operator gives for these tokens.
 
+    Dispatched rows travel as q8_1 blocks (H/32 blocks of 36 bytes: codes plus
+    fp16 d and s, 1.125 bytes per value instead of 4) when act_mode is
+    "sum_x" or "sum_dq": each token is quantised once where it lives and the
+    owning rank runs its experts on the received codes, which are the codes
+    the single-GPU operator forms (its staging holds the same fp16 d and s).
+    Mode "f32" keeps fp32 d and s, so its rows travel as fp32.
+
     route_fn(logits, topk) -> (idx int32 [T, k], wts fp32 [T, k]);
-    experts_fn(x_rows, local_expert int32 [P], w_gate, w_up, w_down, act_mode) -> [P, H];
-    combine_fn(y [T*k, H], wts) -> [T, H]. Defaults: libkq."""
-    ops = None if (route_fn and experts_fn and combine_fn) else _ops()
+    experts_fn(x_rows, local_expert int32 [P], w_gate, w_up, w_down, act_mode) -> [P, H] (fp32 rows);
+    quant_fn(x, act_mode) -> uint8 [T, H/32 * 36] and
+    experts_q8_fn(a_rows uint8, local_expert, w_gate, w_up, w_down, act_mode) -> [P, H] (q8_1 rows);
+    combine_fn(y [T*k, H], wts) -> [T, H]. Defaults: libkq. Injecting
+    experts_fn alone selects fp32 rows."""
+    use_q8 = act_mode in ("sum_x", "sum_dq") and (experts_q8_fn is not None or experts_fn is None)
+    needs_ops = not route_fn or not combine_fn or (use_q8 and not (quant_fn and experts_q8_fn)) or \
+        (not use_q8 and not experts_fn)
+    ops = _ops() if needs_ops else None
     route_fn = route_fn or (lambda lg, k: ops.moe_route(lg, k))
     experts_fn = experts_fn or (lambda xr, er, g, u, d, am: ops.moe_experts_q4_0(xr, er, g, u, d, act_mode=am))
+    quant_fn = quant_fn or (lambda xx, am: ops.quantize_q8_1(xx, am))
+    experts_q8_fn = experts_q8_fn or (
+        lambda ar, er, g, u, d, am: ops.moe_experts_q4_0_q8_1(ar, er, g, u, d, act_mode=am))
     combine_fn = combine_fn or (lambda y, w: ops.moe_combine(y, w))
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -419,7 +436,8 @@ def moe_expert_parallel(x: torch.Tensor, router_logits: torch.Tensor, w_gate: to
     dest = torch.div(flat, per, rounding_mode="floor")
     order = torch.argsort(dest, stable=True)                      # pairs grouped by owning rank
     send_counts = torch.bincount(dest, minlength=world).to(torch.int64)
-    x_send = x.index_select(0, torch.div(order, topk, rounding_mode="floor"))
+    rows = quant_fn(x, act_mode).reshape(T, -1) if use_q8 else x   # what travels per token
+    x_send = rows.index_select(0, torch.div(order, topk, rounding_mode="floor"))
     e_send = (flat - dest * per).index_select(0, order).to(torch.int32)
     if world == 1:
         x_recv, e_recv, recv_counts = x_send, e_send, send_counts
@@ -427,12 +445,13 @@ def moe_expert_parallel(x: torch.Tensor, router_logits: torch.Tensor, w_gate: to
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=group)
         sc, rc = send_counts.tolist(), recv_counts.tolist()
-        x_recv = torch.empty((sum(rc), H), dtype=x.dtype, device=x.device)
+        x_recv = torch.empty((sum(rc), rows.shape[1]), dtype=rows.dtype, device=x.device)
         e_recv = torch.empty((sum(rc),), dtype=torch.int32, device=x.device)
         dist.all_to_all_single(x_recv, x_send, rc, sc, group=group)
         dist.all_to_all_single(e_recv, e_send, rc, sc, group=group)
     if x_recv.shape[0]:
-        y_recv = experts_fn(x_recv, e_recv, w_gate, w_up, w_down, act_mode)
+        fn = experts_q8_fn if use_q8 else experts_fn
+        y_recv = fn(x_recv, e_recv, w_gate, w_up, w_down, act_mode)
     else:
         y_recv = torch.empty((0, H), dtype=x.dtype, device=x.device)
     if world == 1:
@@ -444,5 +463,6 @@ def moe_expert_parallel(x: torch.Tensor, router_logits: torch.Tensor, w_gate: to
     y_pairs[order] = y_back
     if stats is not None:
         stats.update(send_rows=int(send_counts.sum()), recv_rows=int(recv_counts.sum()),
-                     recv_counts=recv_counts.tolist())
+                     recv_counts=recv_counts.tolist(), row_bytes=int(rows.shape[1] * rows.element_size()),
+                     wire="q8_1" if use_q8 else "f32")
     return combine_fn(y_pairs, wts)

@@ -233,6 +233,33 @@ def moe_experts_q4_0(x_rows: torch.Tensor, expert_of_row: torch.Tensor, w_gate: 
     return out
 
 
+def moe_experts_q4_0_q8_1(a_rows: torch.Tensor, expert_of_row: torch.Tensor, w_gate: torch.Tensor,
+                          w_up: torch.Tensor, w_down: torch.Tensor, act_mode="sum_dq",
+                          out: torch.Tensor | None = None) -> torch.Tensor:
+    """moe_experts_q4_0 on pre-quantised rows: a_rows uint8 [P, H/32, 36] (or
+    [P, H/32 * 36]) q8_1 blocks as quantize_q8_1 writes them; act_mode is the
+    re-quantisation mode of silu(gate) * up. fp32 [P, H]."""
+    _cuda(a_rows, "a_rows", torch.uint8)
+    P = a_rows.shape[0]
+    H = a_rows.numel() // max(P, 1) // 36 * 32
+    if a_rows.numel() != P * (H // 32) * 36:
+        raise ValueError("a_rows must hold P rows of q8_1 blocks (36 bytes per 32 values)")
+    _cuda(expert_of_row, "expert_of_row", torch.int32, P)
+    _cuda(w_gate, "w_gate", torch.uint8)
+    _cuda(w_up, "w_up", torch.uint8)
+    _cuda(w_down, "w_down", torch.uint8)
+    E = w_gate.shape[0]
+    I = w_gate.numel() // (E * (H // 32) * 18)
+    if w_gate.numel() != E * I * (H // 32) * 18 or w_up.numel() != w_gate.numel() or w_down.numel() != E * H * (I // 32) * 18:
+        raise ValueError("expert weight sizes do not match [E, I, H/32, 18] / [E, H, I/32, 18]")
+    if out is None:
+        out = torch.empty((P, H), dtype=torch.float32, device=a_rows.device)
+    check(lib().kq_moe_experts_q4_0_q8_1(a_rows.data_ptr(), expert_of_row.data_ptr(), w_gate.data_ptr(),
+                                         w_up.data_ptr(), w_down.data_ptr(), E, P, H, I, _act_mode(act_mode),
+                                         out.data_ptr(), _stream(a_rows)), "kq_moe_experts_q4_0_q8_1")
+    return out
+
+
 def moe_combine(y: torch.Tensor, wts: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """out[t] = sum_k wts[t, k] * y[t * topk + k]; y fp32 [T * topk, H]."""
     _cuda(wts, "wts", torch.float32)

@@ -192,6 +192,65 @@ def test_moe_expert_parallel_gloo(T_per, E, topk):
     _spawn(_moe_rank, 2, T_per, E, topk, 64, 96)
 
 
+def _moe_q8_rank(rank, world, T_per, E, topk, H, I):
+    """As _moe_rank, with the rows travelling as q8_1 blocks (the default wire
+    for "sum_dq"): quant_fn and experts_q8_fn stand in for libkq."""
+    rng = np.random.default_rng(22)
+    T = T_per * world
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    logits = rng.standard_normal((T, E)).astype(np.float32)
+    wg = [Q.make_q4_0_blocks(rng, I, H) for _ in range(E)]
+    wu = [Q.make_q4_0_blocks(rng, I, H) for _ in range(E)]
+    wd = [Q.make_q4_0_blocks(rng, H, I) for _ in range(E)]
+    first, per = kd.expert_range(E, world, rank)
+    t0 = rank * T_per
+    xs, ls = x[t0:t0 + T_per], logits[t0:t0 + T_per]
+    nb = H // 32
+
+    def route_fn(lg, k):
+        idx, w = Q.moe_route(lg.numpy(), k)
+        return torch.from_numpy(idx), torch.from_numpy(w)
+
+    def quant_fn(xx, am):
+        assert am == "sum_dq"
+        return torch.from_numpy(Q.quantize_q8_1(xx.numpy(), Q.SUM_DQ).reshape(xx.shape[0], -1))
+
+    def experts_q8_fn(ar, er, g, u, d, am):
+        ar, er = ar.numpy().reshape(-1, nb, 36), er.numpy()
+        da = ar[:, :, 0:2].copy().view(np.float16)[:, :, 0].astype(np.float32)
+        sa = ar[:, :, 2:4].copy().view(np.float16)[:, :, 0].astype(np.float32)
+        qa = ar[:, :, 4:].copy().view(np.int8)
+        y = np.zeros((ar.shape[0], H), dtype=np.float64)
+        for e in range(per):
+            sel = np.nonzero(er == e)[0]
+            if len(sel) == 0:
+                continue
+            m = len(sel)
+            gg = Q.gemm_codes("q4_0", wg[first + e], qa[sel], da[sel], sa[sel], m, I, H)
+            uu = Q.gemm_codes("q4_0", wu[first + e], qa[sel], da[sel], sa[sel], m, I, H)
+            h = (Q.silu(gg) * uu.astype(np.float64)).astype(np.float32)
+            y[sel] = Q.gemm_f32act("q4_0", wd[first + e], h, m, H, I, Q.SUM_DQ)
+        return torch.from_numpy(y)
+
+    def combine_fn(y, w):
+        return (y.view(T_per, topk, H) * w.unsqueeze(-1)).sum(dim=1)
+
+    stats = {}
+    out = kd.moe_expert_parallel(torch.from_numpy(xs), torch.from_numpy(ls), None, None, None, E, topk,
+                                 route_fn=route_fn, combine_fn=combine_fn, stats=stats, quant_fn=quant_fn,
+                                 experts_q8_fn=experts_q8_fn)
+    ref = Q.moe_forward(x, logits, wg, wu, wd, topk, H, I, Q.SUM_DQ, tokens=np.arange(t0, t0 + T_per))
+    assert stats["wire"] == "q8_1" and stats["row_bytes"] == nb * 36
+    np.testing.assert_allclose(out.numpy(), ref, rtol=1e-12, atol=1e-12)
+
+
+@pytest.mark.parametrize("T_per,E,topk", [(12, 4, 2), (3, 8, 2)])
+def test_moe_expert_parallel_q8_1_rows_gloo(T_per, E, topk):
+    """Expert-parallel dispatch of q8_1 rows (36 bytes per 32 values instead of
+    128) gives the single-device oracle's result exactly."""
+    _spawn(_moe_q8_rank, 2, T_per, E, topk, 64, 96)
+
+
 # ---------------------------------------------------------------------------
 # failure detection on the host: a rank that leaves between steps
 # ---------------------------------------------------------------------------

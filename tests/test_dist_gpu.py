@@ -50,6 +50,31 @@ def test_moe_stages_world1(cuda):
     _assert_close(out.cpu().numpy(), fused.cpu().numpy().astype(np.float64), "expert-parallel vs fused")
 
 
+@pytest.mark.parametrize("mode", ["sum_dq", "sum_x"])
+def test_moe_experts_q8_1_rows_bit_exact(cuda, mode):
+    """kq_moe_experts_q4_0_q8_1 on rows quantised to q8_1 bytes equals
+    kq_moe_experts_q4_0 on the fp32 rows bit for bit (same codes and fp16
+    scales reach the same expert GEMMs), and the expert-parallel path with its
+    q8_1 wire equals the fused operator."""
+    import kq
+    from kq import dist as kd
+
+    rng = np.random.default_rng(5)
+    T, E, H, I = 150, 4, 256, 512
+    x, logits, wg, wu, wd = _moe_case(rng, T, E, H, I)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    er = t(rng.integers(0, E, size=T).astype(np.int32))
+    y32 = kq.moe_experts_q4_0(t(x), er, t(wg), t(wu), t(wd), act_mode=mode)
+    a8 = kq.quantize_q8_1(t(x), mode).reshape(T, -1)
+    y8 = kq.moe_experts_q4_0_q8_1(a8, er, t(wg), t(wu), t(wd), act_mode=mode)
+    assert np.array_equal(y32.cpu().numpy().view(np.uint32), y8.cpu().numpy().view(np.uint32))
+    stats = {}
+    out = kd.moe_expert_parallel(t(x), t(logits), t(wg), t(wu), t(wd), E, 2, act_mode=mode, stats=stats)
+    fused = kq.moe_q4_0(t(x), t(logits), t(wg), t(wu), t(wd), topk=2, act_mode=mode)
+    assert stats["wire"] == "q8_1"
+    _assert_close(out.cpu().numpy(), fused.cpu().numpy().astype(np.float64), "expert-parallel (q8_1 rows) vs fused")
+
+
 def test_nsharded_gemm_world1(cuda):
     from kq import dist as kd
 
