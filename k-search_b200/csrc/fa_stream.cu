@@ -261,6 +261,9 @@ __global__ void __maxnreg__(112)
   const long long TT = sc.total();
   const long long t_begin = TT * blockIdx.x / gridDim.x, t_end = TT * (blockIdx.x + 1) / gridDim.x;
   if (t_begin >= t_end) return;  // no tiles for this CTA (uniform exit: nothing initialised yet)
+  // the combine may launch now: it waits (griddepcontrol.wait) for this whole
+  // grid to finish, but its launch latency overlaps the decode
+  pdl_launch_dependents();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -546,6 +549,7 @@ __global__ void __maxnreg__(112)
 // + item .. owner(last tile) + item). Lane = 4 dims.
 template <typename OT, bool RAGGED>
 __global__ void __launch_bounds__(128) fa_stream_combine_kernel(StreamParams p, int Q, int G) {
+  pdl_wait();  // the decode grid's partials
   const int qg = blockIdx.x * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (qg >= Q) return;
@@ -675,7 +679,19 @@ kq_status_t launch(StreamParams p, const void* k, const void* v, uint64_t rows, 
   if (tiles_estimate < kTwoCtaMinTilesPerSm * sm_count()) G = std::min(G, sm_count());
   kern<<<G, kThreads, kSmem, s>>>(km, vm, p);
   if ((st = check_launch("fa_stream"))) return st;
-  fa_stream_combine_kernel<OT, RAGGED><<<(unsigned)((Q + 3) / 4), 128, 0, s>>>(p, (int)Q, G);
+  // a programmatic dependent of the decode kernel
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((Q + 3) / 4));
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fa_stream_combine_kernel<OT, RAGGED>, p, (int)Q, G);
+  if (e != cudaSuccess) return check_cuda(e, "fa_stream_combine launch");
   return check_launch("fa_stream_combine");
 }
 
