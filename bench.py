@@ -508,9 +508,12 @@ def bench_gemm(args, cfg, rank, world, *, steps, warmup, clocks_on=True):
         value = world * ops / (per * 1e-3) / 1e12
 
     # ---- dominant kernel alone (the GEMM on pre-staged activations) ----
-    qs = [torch.empty((M, K), dtype=torch.int8, device=dev) for _ in range(nsets)]
+    # One activation row with 4-bit weights is a single launch (gemv1_kernel
+    # quantises the row itself): the step is the kernel.
+    single = M == 1 and wt in ("q4_0", "q4_1") and K % 256 == 0
+    qs = [torch.empty((M, K), dtype=torch.int8, device=dev) for _ in range(0 if single else nsets)]
     dss = [torch.empty((M, nb, 2), dtype=torch.float32, device=dev) for _ in range(nsets)]
-    for j in range(nsets):  # stage once with the library's own quantiser (not timed)
+    for j in range(len(qs)):  # stage once with the library's own quantiser (not timed)
         a8 = kq.quantize_q8_1(xs[j], "sum_dq")
         dss[j].copy_(torch.stack([a8[:, :, 0:2].contiguous().view(torch.float16).float().squeeze(-1),
                                   a8[:, :, 2:4].contiguous().view(torch.float16).float().squeeze(-1)], dim=-1))
@@ -523,8 +526,11 @@ def bench_gemm(args, cfg, rank, world, *, steps, warmup, clocks_on=True):
         _lib.check(L.kq_mul_mat_q8x(wtc, ws[j].data_ptr(), qs[j].data_ptr(), dss[j].data_ptr(), outs[j].data_ptr(),
                                     M, N, K, sp), "kq_mul_mat_q8x")
 
-    kms, _ = graph_time_ms(kstep, steps, 3, world)
-    kms /= steps
+    if single:
+        kms = ms / steps
+    else:
+        kms, _ = graph_time_ms(kstep, steps, 3, world)
+        kms /= steps
     del qs, dss
 
     # ---- end to end through the public API with host buffers ----
@@ -598,7 +604,17 @@ def bench_gemm(args, cfg, rank, world, *, steps, warmup, clocks_on=True):
 
     hbm, bf16, src = load_peaks()
     staged_bytes = N * nb * bb + M * K + M * nb * 8 + M * N * 4
-    if M <= 8:
+    if single:
+        # algorithmic bytes: weights + the fp32 activation row + the fp32 output
+        achieved = algo_bytes / (kms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(achieved / hbm, 4),
+                "traffic": (round(NCU_TRAFFIC[("gemv1", "q4_0 per weight row, K=4096")] * N)
+                            if (wt == "q4_0" and K == 4096 and ("gemv1", "q4_0 per weight row, K=4096")
+                                in NCU_TRAFFIC) else None),
+                "kernel": "gemv1_kernel (one launch: in-kernel q8_1 of the row)", "algorithmic_bytes": algo_bytes,
+                "peak_source": f"{src} hbm_gbs (copy)"}
+    elif M <= 8:
         achieved = staged_bytes / (kms * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(achieved / hbm, 4),
@@ -628,8 +644,8 @@ def bench_gemm(args, cfg, rank, world, *, steps, warmup, clocks_on=True):
                 "peak_source": f"f16 dense = {src} bf16_tflops (cuBLAS bf16 burst); achieved counts the "
                                f"algorithmic 2MNK, executed_frac the 3 f16 MMAs per product; int8_peak: "
                                f"{i8['how']}"}
-    # quantiser + GEMV | quantiser + skinny GEMM | quantiser + split prep + split GEMM
-    launches_per_step = 2 if M <= 16 else 3
+    # single-launch GEMV | quantiser + GEMV or skinny GEMM | quantiser + split prep + split GEMM
+    launches_per_step = 1 if single else 2 if M <= 16 else 3
     line = {
         "metric": metric, "value": round(value, 4), "unit": unit, "n_gpus": world, "steps": steps,
         "warmup": warmup, "ms_per_step": round(per, 5), "higher_is_better": True, "scaling": "weak",

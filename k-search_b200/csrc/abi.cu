@@ -286,6 +286,8 @@ kq_status_t kq_gemm_f32act(int wtype, const void* w, const float* x, float* out,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (K == 0) return zero_output(out, M, N, s);
   if (!aligned(x, 16)) return fail(KQ_ERR_INVALID, "activations must be 16-byte aligned");
+  // one activation row, 4-bit weights: one launch that quantises the row itself
+  if (gemv1_supported(wtype, M, N, K, w, x)) return launch_gemv1(wtype, w, x, OutSpec::plain(out, N), N, K, act_mode, s);
   void* ws = workspace(WS_ACT, act8_bytes(M, K));
   if (!ws) return KQ_ERR_NOMEM;
   Act8 act = act8_view(ws, M, K);
@@ -401,6 +403,7 @@ kq_status_t kq_gemm_f32act_scatter(int wtype, const void* w, const float* x, flo
   if (K == 0) return fail(KQ_ERR_UNSUPPORTED, "scatter: K == 0");
   if (!aligned(x, 16)) return fail(KQ_ERR_INVALID, "activations must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (gemv1_supported(wtype, M, N, K, w, x)) return launch_gemv1(wtype, w, x, o, N, K, act_mode, s);
   void* ws = workspace(WS_ACT, act8_bytes(M, K));
   if (!ws) return KQ_ERR_NOMEM;
   Act8 act = act8_view(ws, M, K);

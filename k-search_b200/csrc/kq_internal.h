@@ -111,6 +111,12 @@ kq_status_t launch_gemv(int wtype, const void* w, Act8 act, const OutSpec& out, 
                         cudaStream_t s, int* err = nullptr);
 kq_status_t launch_gemv(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, bool pdl,
                         cudaStream_t s, int* err = nullptr);
+// gemv1.cu: one launch for M = 1 with 4-bit weights (q4_0 / q4_1): quantises
+// the fp32 row itself (bit-identical codes), no workspace. K % 256 == 0,
+// K <= 32768, w and x 16-byte aligned.
+bool gemv1_supported(int wtype, int M, int N, int K, const void* w, const float* x);
+kq_status_t launch_gemv1(int wtype, const void* w, const float* x, const OutSpec& out, int N, int K, int mode,
+                         cudaStream_t s, int* err = nullptr);
 // gemm_tc.cu (M > 8, K % 256 == 0, 16-byte aligned operands): tcgen05 int8 MMA
 bool gemm_tc_supported(int wtype, int M, int N, int K, const void* w, Act8 act);
 kq_status_t launch_gemm_tc(int wtype, const void* w, Act8 act, const OutSpec& out, int M, int N, int K, bool pdl,

@@ -94,6 +94,9 @@ extern "C" kq_status_t kq_gemm_f32act_noalloc(int wtype, const void* w, const fl
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   st = check_cuda(cudaMemsetAsync(p.err, 0, sizeof(int), s), "clear the no-alloc error word");
   if (st) return st;
+  // one activation row with 4-bit weights: the single-launch GEMV needs no
+  // staging at all (the same kernel kq_gemm_f32act runs for this shape)
+  if (gemv1_supported(wtype, M, N, K, w, x)) return launch_gemv1(wtype, w, x, OutSpec::plain(out, N), N, K, act_mode, s, p.err);
   Act8 act = act8_view(p.scratch, M, K);
   st = launch_quantize_act(x, act, M, K, act_mode, s);
   if (st) return st;

@@ -18,69 +18,10 @@
 
 #include "kq_internal.h"
 #include "kq_device.cuh"
+#include "kq_quant.cuh"
 
 namespace kq {
 namespace {
-
-struct BlockQ {
-  uint32_t qs;  // this lane's 4 codes, packed little endian
-  float d;      // fp32 scale (unrounded)
-  float s;      // fp32 sum per mode (unrounded)
-};
-
-// 8 lanes (an aligned octet of the warp) quantise one 32-value block; lane
-// `sub` holds values 4*sub .. 4*sub+3. All 32 lanes must call this.
-template <int MODE>
-__device__ __forceinline__ BlockQ quantize_octet(float4 v, int lane) {
-  const unsigned full = 0xffffffffu;
-  const int sub = lane & 7;
-  const int base = lane & ~7;
-
-  float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-  amax = fmaxf(amax, __shfl_xor_sync(full, amax, 1));
-  amax = fmaxf(amax, __shfl_xor_sync(full, amax, 2));
-  amax = fmaxf(amax, __shfl_xor_sync(full, amax, 4));
-  const float d = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
-
-  int q0 = max(-128, min(127, __float2int_rn(__fdiv_rn(v.x, d))));
-  int q1 = max(-128, min(127, __float2int_rn(__fdiv_rn(v.y, d))));
-  int q2 = max(-128, min(127, __float2int_rn(__fdiv_rn(v.z, d))));
-  int q3 = max(-128, min(127, __float2int_rn(__fdiv_rn(v.w, d))));
-  BlockQ r;
-  r.qs = (uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8) | ((uint32_t)(q2 & 0xff) << 16) |
-         ((uint32_t)(q3 & 0xff) << 24);
-  r.d = d;
-
-  if (MODE == KQ_ACT_SUM_DQ) {
-    int sq = q0 + q1 + q2 + q3;
-    sq += __shfl_xor_sync(full, sq, 1);
-    sq += __shfl_xor_sync(full, sq, 2);
-    sq += __shfl_xor_sync(full, sq, 4);
-    const float dh = __half2float(__float2half_rn(d));
-    r.s = __fmul_rn(dh, (float)sq);
-  } else {
-    // numpy pairwise order. Value j of the block is lane j/4, component j%4.
-    // Lanes sub=0 and sub=1 build r[4*sub + c] = x[4sub+c] + x[4sub+c+8]
-    // + x[4sub+c+16] + x[4sub+c+24] (lanes sub, sub+2, sub+4, sub+6).
-    const int a = sub & 1;
-    float t0 = v.x, t1 = v.y, t2 = v.z, t3 = v.w;
-#pragma unroll
-    for (int k = 1; k < 4; ++k) {
-      const int src = base + a + 2 * k;
-      t0 = __fadd_rn(t0, __shfl_sync(full, v.x, src));
-      t1 = __fadd_rn(t1, __shfl_sync(full, v.y, src));
-      t2 = __fadd_rn(t2, __shfl_sync(full, v.z, src));
-      t3 = __fadd_rn(t3, __shfl_sync(full, v.w, src));
-    }
-    const float p = __fadd_rn(__fadd_rn(t0, t1), __fadd_rn(t2, t3));
-    const float other = __shfl_xor_sync(full, p, 1);
-    // lane sub=0 holds the left half of the final addition, sub=1 the right.
-    const float res = (a == 0) ? __fadd_rn(p, other) : __fadd_rn(other, p);
-    r.s = __fadd_rn(res, 0.0f);
-    r.s = __shfl_sync(full, r.s, base);
-  }
-  return r;
-}
 
 // Where a block's 32 input values come from.
 enum Src : int {
@@ -134,15 +75,7 @@ __global__ void __launch_bounds__(256) quantize_kernel(const float* __restrict__
       }
     } else {
       reinterpret_cast<uint32_t*>(qs + blk * 32)[sub] = r.qs;
-      if (sub == 0) {
-        float2 o;
-        if (MODE == KQ_ACT_F32) {
-          o = make_float2(r.d, r.s);
-        } else {
-          o = make_float2(__half2float(__float2half_rn(r.d)), __half2float(__float2half_rn(r.s)));
-        }
-        ds[blk] = o;
-      }
+      if (sub == 0) ds[blk] = staging_ds<MODE>(r);
     }
   }
   // Let a programmatic dependent (the GEMV) start its weight prefetch; it
@@ -328,10 +261,7 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_quantize_kernel(const f
       if (sub == 0) *reinterpret_cast<uint32_t*>(dst) = float_to_half_bits(r.d) | (float_to_half_bits(r.s) << 16);
     } else {
       reinterpret_cast<uint32_t*>(qs + blk * 32)[sub] = r.qs;
-      if (sub == 0)
-        ds[blk] = MODE == KQ_ACT_F32
-                      ? make_float2(r.d, r.s)
-                      : make_float2(__half2float(__float2half_rn(r.d)), __half2float(__float2half_rn(r.s)));
+      if (sub == 0) ds[blk] = staging_ds<MODE>(r);
     }
   }
   pdl_launch_dependents();

@@ -376,3 +376,50 @@ def test_harness_mirror(cuda):
     assert got.shape == (M, N)
     perf = kq.harness.quant_gemm_performance(0.01, M, N, K)
     assert perf["tflops"] == round(2 * M * N * K / 1e-5 / 1e12, 3)
+
+
+@pytest.mark.parametrize("wtype", ["q4_0", "q4_1"])
+@pytest.mark.parametrize("N,K", [(1, 256), (7, 3584), (33, 4096), (4096, 4096), (300, 11008), (129, 14336),
+                                 (1000, 2048), (5, 65536)])
+def test_single_launch_gemv(cuda, wtype, N, K):
+    """M = 1 with 4-bit weights runs one kernel that quantises the row itself
+    (gemv1.cu). K sets the lanes per row (chunk counts 1, 14, 16, 43, 56, 8,
+    256: idle lanes, two chunks per lane, the 32-lane cap) and N the ragged
+    last warp. Checked against the oracle in every activation mode, and
+    against the two-launch path on the same q8_1 bytes (kq_quantize_q8_1 then
+    kq_mul_mat_q, the staged GEMV): both read identical codes and scales, so
+    they differ only in summation order."""
+    import kq
+    rng = np.random.default_rng(N + K)
+    w = Q.make_blocks(wtype, rng, N, K)
+    x = _x(rng, 1, K)
+    x[0, :32] = 0.0                                         # zero block: d = 1
+    x[0, 32:64] = np.float32(0.5) * (np.arange(32) % 5 - 2)  # exact .5 ties
+    if K >= 512:
+        x[0, 256:512] *= np.float32(1e-4)                    # mixed magnitudes
+    wd, xd = _t(w, cuda), _t(x, cuda)
+    for mode in ("f32", "sum_x", "sum_dq"):
+        got = kq.gemm_f32act(wd, xd, 1, N, K, wtype, mode).cpu().numpy()
+        ok, msg = Q.check_close(got, Q.gemm_f32act(wtype, w, x, 1, N, K, MODES[mode]))
+        assert ok, f"{mode}: {msg}"
+        if mode != "f32":
+            staged = kq.mul_mat_q(wd, kq.quantize_q8_1(xd, mode), 1, N, K, wtype).cpu().numpy()
+            scale = float(np.sqrt(np.mean(staged.astype(np.float64) ** 2))) + 1e-30
+            assert np.max(np.abs(got - staged)) <= 1e-5 * scale, f"{mode}: differs from the staged GEMV"
+    assert kq.device_error() == 0
+
+
+def test_single_launch_gemv_unaligned_falls_back(cuda):
+    """Weights off the 16-byte grid (2-byte aligned, as the block fields
+    allow) take the two-launch path (quantiser + generic kernel), with the
+    same result to the parity bar."""
+    import kq
+    rng = np.random.default_rng(5)
+    N, K = 64, 1024
+    w = Q.make_q4_0_blocks(rng, N, K).reshape(-1)
+    x = _x(rng, 1, K)
+    wbuf = torch.zeros(w.size + 16, dtype=torch.uint8, device=cuda)
+    wbuf[2:2 + w.size] = _t(w, cuda)
+    got = kq.gemm_f32act(wbuf[2:2 + w.size], _t(x, cuda), 1, N, K, "q4_0", "f32")
+    ok, msg = Q.check_close(got.cpu().numpy(), Q.gemm_f32act("q4_0", w.reshape(N, -1), x, 1, N, K, Q.ACT_F32))
+    assert ok, msg
