@@ -589,22 +589,50 @@ __global__ void __launch_bounds__(128) fa_stream_combine_kernel(StreamParams p, 
     // CTAs between the owners of the first and last tile whose ranges are
     // empty (fewer tiles than CTAs) wrote no partial
     auto has_tiles = [&](int c) { return TT * c / G < TT * (c + 1) / G; };
+    auto slot = [&](int c) { return ((size_t)(c + item) * kHeads + w) * kQ + j; };
+    const int np = c1 - c0 + 1;
+    // Lane i holds partial c0 + base + i: all maxima and sums arrive in one
+    // round of loads instead of a dependent chain per partial.
     float M = -INFINITY;
-    for (int c = c0; c <= c1; ++c)
-      if (has_tiles(c)) M = fmaxf(M, p.pm[((size_t)(c + item) * kHeads + w) * kQ + j]);
+    for (int base = 0; base < np; base += 32) {
+      const int c = c0 + base + lane;
+      const float mc = (base + lane < np && has_tiles(c)) ? p.pm[slot(c)] : -INFINITY;
+      M = fmaxf(M, warp_max(mc));
+    }
     if (M != -INFINITY) {
-      for (int c = c0; c <= c1; ++c) {
-        if (!has_tiles(c)) continue;
-        const size_t idx = ((size_t)(c + item) * kHeads + w) * kQ + j;
-        const float mc = p.pm[idx];
+      for (int base = 0; base < np; base += 32) {
+        const int c = c0 + base + lane;
+        const bool valid = base + lane < np && has_tiles(c);
+        const float mc = valid ? p.pm[slot(c)] : -INFINITY;
+        const float lc = valid ? p.pl[slot(c)] : 0.0f;
         const float wgt = mc == -INFINITY ? 0.0f : exp2f(mc - M);
-        if (wgt == 0.0f) continue;
-        L = fmaf(p.pl[idx], wgt, L);
-        const float4 a = *reinterpret_cast<const float4*>(p.pacc + idx * 128 + 4 * lane);
-        acc.x = fmaf(a.x, wgt, acc.x);
-        acc.y = fmaf(a.y, wgt, acc.y);
-        acc.z = fmaf(a.z, wgt, acc.z);
-        acc.w = fmaf(a.w, wgt, acc.w);
+        const int cnt = min(32, np - base);
+        // in partial order, as a sequential merge would: four accumulator
+        // loads in flight ahead of their FMAs
+        for (int k0 = 0; k0 < cnt; k0 += 4) {
+          float4 a[4];
+          float wk[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int k = k0 + u;
+            wk[u] = __shfl_sync(0xffffffffu, wgt, k & 31);
+            a[u] = (k < cnt && wk[u] != 0.0f)
+                       ? *reinterpret_cast<const float4*>(p.pacc + slot(c0 + base + k) * 128 + 4 * lane)
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int k = k0 + u;
+            const float lk = __shfl_sync(0xffffffffu, lc, k & 31);
+            if (k < cnt && wk[u] != 0.0f) {
+              L = fmaf(lk, wk[u], L);
+              acc.x = fmaf(a[u].x, wk[u], acc.x);
+              acc.y = fmaf(a[u].y, wk[u], acc.y);
+              acc.z = fmaf(a[u].z, wk[u], acc.z);
+              acc.w = fmaf(a[u].w, wk[u], acc.w);
+            }
+          }
+        }
       }
     }
   }
