@@ -83,6 +83,7 @@ def sub_configs():
 NCU_TRAFFIC = {
     ("gemm_split", "q8_0 M=512 N=11008 K=4096"): 61.47e6,
     ("gemv", "q4_0 per weight row, K=4096"): 33.06e6 / 14336,
+    ("gemv1", "q4_0 per weight row, K=4096"): 33.084416e6 / 14336,
     ("fa_stream", "per token row, Hkv=8 D=128"): (303.26e6 + 3.49e6) / 139124,
 }
 
