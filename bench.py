@@ -937,8 +937,12 @@ def bench_ggml_cases(steps: int) -> dict:
 
         ms, _ = graph_time_ms(step, steps, 3, 1)
         us = ms / steps * 1e3
-        gemm.append({"case": case, "M": M, "N": N, "K": K, "wtype": wt, "ours_us": round(us, 2), "ggml_us": hw,
-                     "speedup_vs": {k: round(v / us, 2) for k, v in hw.items()}})
+        wms, _ = graph_time_ms(lambda i: step(0), steps, 3, 1)  # one input set: L2-warm repeats
+        wus = wms / steps * 1e3
+        gemm.append({"case": case, "M": M, "N": N, "K": K, "wtype": wt, "ours_us": round(us, 2),
+                     "ours_us_warm": round(wus, 2), "ggml_us": hw,
+                     "speedup_vs": {k: round(v / us, 2) for k, v in hw.items()},
+                     "speedup_vs_warm": {k: round(v / wus, 2) for k, v in hw.items()}})
         del ws, xs, os_, w
     H, D = 32, 128
     for (S, B), us_ggml in GGML_FA_US.items():
@@ -954,13 +958,21 @@ def bench_ggml_cases(steps: int) -> dict:
 
         ms, _ = graph_time_ms(fstep, steps, 3, 1)
         us = ms / steps * 1e3
-        fa.append({"cache": S, "batch": B, "ours_us": round(us, 2), "ggml_us": {"RTX4090": us_ggml},
-                   "speedup_vs": {"RTX4090": round(us_ggml / us, 2)}})
+        wms, _ = graph_time_ms(lambda i: fstep(0), steps, 3, 1)  # one cache: L2-warm repeats
+        wus = wms / steps * 1e3
+        fa.append({"cache": S, "batch": B, "ours_us": round(us, 2), "ours_us_warm": round(wus, 2),
+                   "ggml_us": {"RTX4090": us_ggml}, "speedup_vs": {"RTX4090": round(us_ggml / us, 2)},
+                   "speedup_vs_warm": {"RTX4090": round(us_ggml / wus, 2)}})
         del ks, vs
     torch.cuda.empty_cache()
     return {"quant_gemm": gemm, "flash_attention_q8_0": fa,
             "source": "kernelevalplus-main/data/baseline/baseline_data_compact.json, flash_attn_baseline.json "
-                      "(GGML / llama.cpp; no B200 entries); ours: CUDA-graph device time per call, act mode sum_x"}
+                      "(GGML / llama.cpp; no B200 entries); ours: CUDA-graph device time per call, act mode sum_x; "
+                      "ours_us rotates inputs larger than L2 (every call reads HBM), ours_us_warm repeats one "
+                      "input set (L2-resident where it fits: 126 MB here)",
+            "note": "GGML's times fit only L2-resident repeats: e.g. the q8_0 cache of 8192 tokens (71 MB of K+V) "
+                    "in 28.74 us on an RTX 4090 is 2.5 TB/s, above that card's ~1 TB/s DRAM and within its "
+                    "72 MB L2; speedup_vs_warm compares like with like"}
 
 
 def run_config(args, cfg, rank, world, *, steps, warmup):
@@ -971,7 +983,15 @@ def run_config(args, cfg, rank, world, *, steps, warmup):
     return bench_gemm(args, cfg, rank, world, steps=steps, warmup=warmup)
 
 
-_SUB_DROP = ("n_gpus", "steps", "warmup", "scaling", "data")
+_SUB_DROP = ("n_gpus", "scaling", "data")
+
+
+def sub_steps(cfg: dict, steps: int) -> int:
+    """Timed steps of a configuration beside the headline: microsecond-scale
+    steps (GEMV-sized gemm calls) run 8x the steps, so the one graph launch
+    per timed region is spread over a region of milliseconds as for the
+    others."""
+    return steps * 8 if cfg["kind"] == "gemm" and cfg["M"] <= 16 else steps
 
 
 def reference_arm(args, cfg, subs: bool):
@@ -1032,7 +1052,7 @@ def main():
     if subs:
         line["configs"] = {}
         for name, c in sub_configs():
-            sub = run_config(args, c, rank, world, steps=args.steps, warmup=min(args.warmup, 3))
+            sub = run_config(args, c, rank, world, steps=sub_steps(c, args.steps), warmup=min(args.warmup, 3))
             if rank == 0 and world == 1 and not args.no_cpu_baseline:
                 sub["cpu_baseline"] = cpu_baseline(c, 4.0)
             line["configs"][name] = {k: v for k, v in sub.items() if k not in _SUB_DROP}

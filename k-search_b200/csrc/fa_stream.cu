@@ -684,13 +684,13 @@ int grid_size(const void* kern, int slot) {
   return g;
 }
 
-// Tiles per CTA below which one CTA per SM is faster than two (the start of
-// the two-stage ring and each item's query setup are paid per CTA): at
-// S = 8192, B = 1 (~14 tiles per SM) one CTA per SM took 69 us and two 99 us,
-// at B = 8 (~28 tiles per SM) 76 and 83 us; the ragged configs[3] workload
-// (~59 tiles per SM: 118.7 -> 108.5 us) and B = 512 (2.88 -> 2.10 ms at
-// S = 8192) run faster with two.
-constexpr long long kTwoCtaMinTilesPerSm = 32;
+// Tiles per SM below which one CTA per SM is faster than two (the start of
+// the two-stage ring and each item's query setup are paid per CTA). Harness
+// form, CUDA-graph device time with the current combine: ~14 tiles per SM
+// (S = 8192 B = 1, S = 4096 B = 8) one CTA 41.7 / 37.2 us, two 46.6 / 39.4;
+// ~28 tiles per SM (S = 8192 B = 8) one 62.3, two 56.2; the ragged configs[3]
+// workload (~59 tiles per SM) and B = 512 run faster with two.
+constexpr long long kTwoCtaMinTilesPerSm = 20;
 
 template <typename QT, typename OT, bool RAGGED>
 kq_status_t launch(StreamParams p, const void* k, const void* v, uint64_t rows, int heads, long long Q,
