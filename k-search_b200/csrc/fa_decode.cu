@@ -659,6 +659,19 @@ bool fast_ok(const void* k, const void* v, int D, int Hkv, int g) {
 
 constexpr size_t kPartialBudget = 64ull << 20;
 
+// The small-batch kernel (fa_small.cu) takes workloads with few stream tiles
+// (16 tokens x 8 KV heads) per SM, where the stream kernel runs one CTA per
+// SM through a long per-tile chain. With one or two queries per KV head it
+// wins below 20 tiles per SM; with three or four its CUDA-core QK / PV per
+// query cost more, and it wins below 4. CUDA-graph device time, q8_0, D = 128
+// (small vs stream): harness S = 8192 B = 1 28.2 vs 42.9 us, B = 2 32.6 vs
+// 46.2, B = 3 56.3 vs 46.4; S = 512 B = 4 10.0 vs 18.4; one ragged sequence
+// of 8192 tokens (Hq 32, Hkv 8) 21.7 vs 42.0; four of 8192 55.3 vs 41.8.
+bool small_batch(long long stream_tiles, int queries_per_kv_head) {
+  const long long per_sm = queries_per_kv_head <= 2 ? 20 : 4;
+  return stream_tiles < per_sm * sm_count();
+}
+
 // Chunks for the TMA kernels: 256-token chunks, more (down to one tile each)
 // when `items` CTAs per chunk would leave the GPU short of two CTAs per SM.
 int choose_chunks_fast(long long Q, int D, int max_len, size_t budget, int items, int* chunk) {
@@ -712,8 +725,12 @@ kq_status_t launch_fa_mha(int kvf, const float* q, const void* k, const void* v,
                           int D, cudaStream_t s) {
   const long long Q = (long long)B * H;
   if (Q == 0) return KQ_OK;
-  if (kvf == KQ_KV_Q8_0 && fa_path() == FaPath::kStream && S > 0 && fa_stream_supported(q, k, v, out, D, H, 1, 0))
-    return launch_fa_stream_mha(q, k, v, out, B, S, H, s);
+  if (kvf == KQ_KV_Q8_0 && fa_path() == FaPath::kStream && S > 0) {
+    const long long tiles = (long long)((B + 3) / 4) * (H / 8) * ((S + 15) / 16);
+    if (small_batch(tiles, std::min(B, 4)) && fa_small_supported(q, k, v, out, D, H, std::min(B, 4)))
+      return launch_fa_small_mha(q, k, v, out, B, S, H, s);
+    if (fa_stream_supported(q, k, v, out, D, H, 1, 0)) return launch_fa_stream_mha(q, k, v, out, B, S, H, s);
+  }
   const bool fast = kvf == KQ_KV_Q8_0 && fast_ok(k, v, D, H, 1) && S > 0 &&
                     (long long)((B + kG - 1) / kG) * (H / kHpc) <= 65535;
   int chunk = 0;
@@ -755,8 +772,13 @@ kq_status_t launch_fa_ragged(const void* q, const void* k, const void* v, const 
   const long long Q = (long long)B * Hq;
   if (Q == 0) return KQ_OK;
   const int g = Hq / Hkv;
-  if (fa_path() == FaPath::kStream && fa_stream_supported(q, k, v, out, D, Hkv, g, B))
-    return launch_fa_stream_ragged(q, k, v, cu, B, Hq, Hkv, total_rows, scale, out, s);
+  if (fa_path() == FaPath::kStream) {
+    const long long tiles = (long long)B * std::max(1, Hkv / 8) * ((std::max(max_seqlen, 1) + 15) / 16);
+    if (small_batch(tiles, g) && fa_small_supported(q, k, v, out, D, Hkv, g))
+      return launch_fa_small_ragged(q, k, v, cu, B, Hq, Hkv, max_seqlen, total_rows, scale, out, s);
+    if (fa_stream_supported(q, k, v, out, D, Hkv, g, B))
+      return launch_fa_stream_ragged(q, k, v, cu, B, Hq, Hkv, total_rows, scale, out, s);
+  }
   const bool fast = fast_ok(k, v, D, Hkv, g) && total_rows > 0 && (long long)B * (Hkv / kHpc) <= 65535;
   int chunk = 0;
   const int NC = fast ? choose_chunks_fast(Q, D, std::max(max_seqlen, 1), kPartialBudget, B * (Hkv / kHpc), &chunk)

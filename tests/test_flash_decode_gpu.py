@@ -284,3 +284,41 @@ def test_earlier_decode_paths_opt_in(cuda, path):
     env = dict(os.environ, KQ_FA_PATH=path)
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.parametrize("B,S,H", [(1, 8192, 32), (1, 512, 28), (2, 17, 32), (3, 16, 8), (4, 1, 32), (5, 300, 32),
+                                   (8, 512, 32), (2, 8192, 32), (1, 1000, 2), (3, 777, 6)])
+def test_small_batch_mha(cuda, B, S, H):
+    """Harness batches too small to fill the GPU through the stream kernel
+    (below 20 stream tiles per SM with one or two queries per head, below 4
+    with more) run the small-batch kernel (fa_small.cu): one warp per
+    (KV head, token chunk); every case here is below its bound. Covers one to five
+    queries per head (a second query group at B = 5, 8), lengths at and
+    around the 16-token tile, a one-token cache, and even head counts below 8
+    that the stream kernel does not take."""
+    import kq
+    rng = np.random.default_rng(B * 7 + S + H)
+    D = 128
+    q = rng.standard_normal((B, H, D)).astype(np.float32)
+    k = Q.quantize_q8_0(rng.standard_normal((S * H, D)).astype(np.float32))
+    v = Q.quantize_q8_0(rng.standard_normal((S * H, D)).astype(np.float32))
+    got = kq.flash_attn_q8_0(_t(q, cuda), _t(k, cuda), _t(v, cuda), B, S, H, D).cpu().numpy()
+    ok, msg = Q.check_close(got, Q.flash_decode_mha(q, k, v, S, H, D))
+    assert ok, msg
+    assert kq.device_error() == 0
+
+
+@pytest.mark.parametrize("lens,Hq,Hkv", [([8192], 32, 8), ([1], 32, 8), ([16], 8, 8), ([4097], 16, 8),
+                                         ([300, 0], 32, 8), ([2000], 4, 2), ([33, 700], 8, 4)])
+def test_small_batch_ragged(cuda, lens, Hq, Hkv):
+    """Single sequences and small ragged batches (the common one-user decode
+    step) on the small-batch kernel: g = 1, 2 and 4 queries per KV head, an
+    empty sequence, one-token and tile-boundary lengths."""
+    import kq
+    rng = np.random.default_rng(sum(lens) + Hq + Hkv)
+    D = 128
+    q, k, v, cu = _ragged_case(rng, lens, Hq, Hkv, D)
+    scale = 1.0 / np.sqrt(D)
+    got = kq.flash_decode_ragged(_t(q, cuda), _t(k, cuda), _t(v, cuda), _t(cu, cuda), Hkv, scale=scale)
+    ok, msg = Q.check_close(got.float().cpu().numpy(), Q.flash_decode_ragged(q, k, v, cu, Hq, Hkv, D, scale))
+    assert ok, msg
