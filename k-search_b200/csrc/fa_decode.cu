@@ -729,6 +729,7 @@ kq_status_t launch_fa_mha(int kvf, const float* q, const void* k, const void* v,
     const long long tiles = (long long)((B + 3) / 4) * (H / 8) * ((S + 15) / 16);
     if (small_batch(tiles, std::min(B, 4)) && fa_small_supported(q, k, v, out, D, H, std::min(B, 4)))
       return launch_fa_small_mha(q, k, v, out, B, S, H, s);
+    if (fa_batch_supported(q, k, v, out, B, S, H, D)) return launch_fa_batch_mha(q, k, v, out, B, S, H, s);
     if (fa_stream_supported(q, k, v, out, D, H, 1, 0)) return launch_fa_stream_mha(q, k, v, out, B, S, H, s);
   }
   const bool fast = kvf == KQ_KV_Q8_0 && fast_ok(k, v, D, H, 1) && S > 0 &&

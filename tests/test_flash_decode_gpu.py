@@ -322,3 +322,24 @@ def test_small_batch_ragged(cuda, lens, Hq, Hkv):
     got = kq.flash_decode_ragged(_t(q, cuda), _t(k, cuda), _t(v, cuda), _t(cu, cuda), Hkv, scale=scale)
     ok, msg = Q.check_close(got.float().cpu().numpy(), Q.flash_decode_ragged(q, k, v, cu, Hq, Hkv, D, scale))
     assert ok, msg
+
+
+@pytest.mark.parametrize("B,S,H", [(512, 64, 32), (300, 65, 32), (512, 1, 32), (1024, 100, 24), (512, 777, 28),
+                                   (320, 2048, 32)])
+def test_batch_mha(cuda, B, S, H):
+    """Harness batches whose (64-query tile, head) CTAs fill the GPU run the
+    fp16 tensor-core flash attention (fa_batch.cu): K and P carry an fp16
+    remainder, Q and V are rounded once. Partial query tiles (B = 300, 320),
+    lengths at and around the 64-token tile, a one-token cache, and odd
+    multiples of the head pair (H = 24, 28)."""
+    import kq
+    rng = np.random.default_rng(B + S + H)
+    D = 128
+    q = rng.standard_normal((B, H, D)).astype(np.float32)
+    k = Q.quantize_q8_0(rng.standard_normal((S * H, D)).astype(np.float32))
+    v = Q.quantize_q8_0(rng.standard_normal((S * H, D)).astype(np.float32))
+    got = kq.flash_attn_q8_0(_t(q, cuda), _t(k, cuda), _t(v, cuda), B, S, H, D).cpu().numpy()
+    ok, msg = Q.check_close(got, Q.flash_decode_mha(q, k, v, S, H, D))
+    assert ok, msg
+    assert Q.nmse(got, Q.flash_decode_mha(q, k, v, S, H, D)) < 0.05
+    assert kq.device_error() == 0
