@@ -4,6 +4,7 @@ times, for profilers (ncu) and quick timing:
     python bench_cases.py gemm --wtype q8_0 --M 512 --N 11008 --K 4096 --reps 3
     python bench_cases.py gemv --wtype q4_0 --N 14336 --K 4096
     python bench_cases.py decode --B 32 --Lmax 8192
+    python bench_cases.py mha --B 512 --S 8192
     python bench_cases.py moe --T 1024
 
 Inputs are generated on the GPU (weights drawn as q-blocks with the
@@ -83,6 +84,23 @@ def run_decode(a) -> str:
     return f"decode B={a.B} sum_L={T}: {ms * 1e3:.2f} us/call, {kv / (ms * 1e-3) / 1e9:.0f} GB/s of KV"
 
 
+def run_mha(a) -> str:
+    """The harness flash_attention form: fp32 queries [B, H, 128] over one
+    shared [S, H, 128] q8_0 cache."""
+    dev = torch.device("cuda")
+    gd = torch.Generator(device=dev).manual_seed(a.seed)
+    D = 128
+    k = kq.quantize_rows(torch.randn((a.S * a.H, D), generator=gd, device=dev), "q8_0")
+    v = kq.quantize_rows(torch.randn((a.S * a.H, D), generator=gd, device=dev), "q8_0")
+    q = torch.randn((a.B, a.H, D), generator=gd, device=dev)
+    fn = lambda: kq.flash_attn_q8_0(q, k, v, a.B, a.S, a.H, D)
+    ms = _time(fn, a.warmup, a.reps)
+    flop = 4.0 * a.B * a.H * a.S * D
+    kv = 2 * a.S * a.H * (D // 32) * 34
+    return (f"mha B={a.B} S={a.S} H={a.H}: {ms * 1e3:.2f} us/call, {flop / (ms * 1e-3) / 1e12:.1f} TFLOP/s, "
+            f"{kv / (ms * 1e-3) / 1e9:.0f} GB/s of KV")
+
+
 def run_moe(a) -> str:
     dev = torch.device("cuda")
     rng = np.random.default_rng(a.seed)
@@ -114,6 +132,9 @@ def main(argv=None) -> None:
     p = sub.add_parser("decode")
     for k, v in dict(B=32, Hq=32, Hkv=8, D=128, Lmin=64, Lmax=8192).items():
         p.add_argument(f"--{k}", type=int, default=v)
+    p = sub.add_parser("mha")
+    for k, v in dict(B=512, S=8192, H=32).items():
+        p.add_argument(f"--{k}", type=int, default=v)
     p = sub.add_parser("moe")
     for k, v in dict(T=4096, E=8, topk=2, H=4096, I=14336).items():
         p.add_argument(f"--{k}", type=int, default=v)
@@ -123,7 +144,7 @@ def main(argv=None) -> None:
         p.add_argument("--seed", type=int, default=0)
     a = ap.parse_args(argv)
     kq.lib()
-    fn = {"gemm": run_gemm, "gemv": run_gemm, "decode": run_decode, "moe": run_moe}[a.op]
+    fn = {"gemm": run_gemm, "gemv": run_gemm, "decode": run_decode, "mha": run_mha, "moe": run_moe}[a.op]
     print(fn(a), flush=True)
 
 
