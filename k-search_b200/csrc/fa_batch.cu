@@ -8,19 +8,22 @@
 // cache in 64-token tiles:
 //  * a TMA ring (two stages) brings the raw q8_0 rows of the head (boxes of
 //    64 rows x 144 bytes: the head's 136-byte row 0 or 8 bytes in);
-//  * the CTA dequantises each tile once into fp16 tiles in shared memory:
-//    K and V as a high part and its fp16 remainder (hi + lo carries ~22 bits
-//    of code * d);
-//  * QK on the tensor pipe (mma.m16n8k16, fp32 accumulation): S = Q_hi K_hi +
-//    Q_lo K_hi + Q_hi K_lo with Q = q * scale * log2(e) as fp16 plus remainder;
+//  * QK is exact on the raw K codes (mma.m16n8k32 s8, one MMA per 32-dim
+//    block and query level): the query q * scale * log2(e) is held as two int8
+//    levels (q ~ s1 c1 + s2 c2, s2 = s1 / 127, so 127 dot1 + dot2 is the exact
+//    block dot at scale s2), and the fp32 epilogue applies each (token, block)
+//    K scale, as the decode kernels do;
+//  * the CTA dequantises each V tile once into fp16 in shared memory, as a
+//    high part and its fp16 remainder (hi + lo carries ~22 bits of code * d);
 //  * online softmax per query row in registers (exp2), and P = p as fp16
 //    plus its fp16 remainder, taken straight from the S accumulators as the
 //    A operand of the PV products: O += P_hi V_hi + P_lo V_hi + P_hi V_lo.
-// Every operand is split: an fp64 emulation of this arithmetic against the
-// oracle (harness definitions' inputs and random ones) puts the worst
-// |error| / per-element bar at 1.02 with only K and P split and 0.71-0.78
-// with three of the four (which still missed on 1 of 2.1 M elements on the
-// GPU); with all four split it is 0.003.
+// Precision, from an fp64 emulation of each arithmetic against the oracle
+// (worst |error| / per-element bar): fp16 Q, K, P and V each rounded once
+// misses the bar on a few elements; with fp16 remainders on three of the four
+// operands 0.71-0.78 (still 1 miss in 2.1 M elements on the GPU), on all four
+// 0.003 (three f16 products per GEMM); this kernel's int8 QK with P and V
+// split 0.15-0.20.
 #include <cuda.h>
 
 #include <algorithm>
@@ -45,13 +48,12 @@ constexpr int kRawTile = kTTile * kRawRow;          // 9216 bytes
 constexpr int kHPitch = 272;             // fp16 tile row: 256 bytes + 16 (ldmatrix rows in distinct banks)
 constexpr int kHTile = kTTile * kHPitch;            // 17408 bytes
 constexpr int kOffRawV = kStages * kRawTile;
-constexpr int kOffKh = 2 * kStages * kRawTile;
-constexpr int kOffKl = kOffKh + kHTile;
-constexpr int kOffVh = kOffKl + kHTile;
+constexpr int kOffVh = 2 * kStages * kRawTile;
 constexpr int kOffVl = kOffVh + kHTile;
-constexpr int kOffBar = kOffVl + kHTile;
+constexpr int kOffDk = kOffVl + kHTile;               // K block scales of the tile, fp32 [4 blocks][64 tokens]
+constexpr int kOffBar = kOffDk + 4 * kTTile * 4;
 constexpr int kSmem = kOffBar + kStages * 8 + 128;  // + base alignment slack
-static_assert(kRawTile % 128 == 0 && kOffKh % 128 == 0 && kHTile % 128 == 0, "aligned tiles");
+static_assert(kRawTile % 128 == 0 && kOffVh % 128 == 0 && kHTile % 128 == 0, "aligned tiles");
 
 struct BatchParams {
   const float* q;   // [B, H, 128]
@@ -78,10 +80,16 @@ __device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1,
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t saddr) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(saddr));
+__device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%10, %10, %10, %10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+}
+
+__device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
+  return (uint32_t)(a & 0xFF) | ((uint32_t)(b & 0xFF) << 8) | ((uint32_t)(c & 0xFF) << 16) | ((uint32_t)d << 24);
 }
 
 __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t saddr) {
@@ -136,8 +144,8 @@ __global__ void __launch_bounds__(32 * kWarps, 2)
   const int ntiles = (p.S + kTTile - 1) / kTTile;
   const int xoff = (h & 1) * 8;                    // the head's first byte inside a raw row
   const int bx = 17 * h - (h & 1);                 // box start in 8-byte units (16-byte aligned)
-  const uint32_t kh_s = smem_u32(smem + kOffKh), kl_s = smem_u32(smem + kOffKl), vh_s = smem_u32(smem + kOffVh),
-                 vl_s = smem_u32(smem + kOffVl);
+  const uint32_t vh_s = smem_u32(smem + kOffVh), vl_s = smem_u32(smem + kOffVl);
+  float* dks = reinterpret_cast<float*>(smem + kOffDk);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
@@ -153,26 +161,59 @@ __global__ void __launch_bounds__(32 * kWarps, 2)
   if (threadIdx.x == 0)
     for (int i = 0; i < min(kStages, ntiles); ++i) issue(i);
 
-  // ---- Q fragments (A operand, 16 queries x 128 dims): fp16 of q * qscale and remainder ----
-  uint32_t qa[8][4], qr[8][4];
+  // ---- Q as two int8 levels (A operand of m16n8k32, rows g and g + 8): thread
+  // (g, t) holds dims 32 b + 4 t .. + 3 and 32 b + 16 + 4 t .. + 3 of each row ----
+  uint32_t qc[2][4][4];  // [level][block][A register]
+  float s2a, s2b;        // level-2 scales of rows g and g + 8
   {
-    const int ra = q0 + g, rb = q0 + g + 8;
-    const float* pa = p.q + ((size_t)ra * p.H + h) * 128;
-    const float* pb = p.q + ((size_t)rb * p.H + h) * 128;
-    const float s = p.qscale;
+    float v[2][4][8];
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      const int c = 16 * kk + 2 * t;
-      const float2 z = make_float2(0.f, 0.f);
-      const float2 x0 = ra < p.B ? *reinterpret_cast<const float2*>(pa + c) : z;
-      const float2 x1 = rb < p.B ? *reinterpret_cast<const float2*>(pb + c) : z;
-      const float2 x2 = ra < p.B ? *reinterpret_cast<const float2*>(pa + c + 8) : z;
-      const float2 x3 = rb < p.B ? *reinterpret_cast<const float2*>(pb + c + 8) : z;
-      split_half2(x0.x * s, x0.y * s, qa[kk][0], qr[kk][0]);
-      split_half2(x1.x * s, x1.y * s, qa[kk][1], qr[kk][1]);
-      split_half2(x2.x * s, x2.y * s, qa[kk][2], qr[kk][2]);
-      split_half2(x3.x * s, x3.y * s, qa[kk][3], qr[kk][3]);
+    for (int r = 0; r < 2; ++r) {
+      const int row = q0 + g + 8 * r;
+      const float* pr = p.q + ((size_t)row * p.H + h) * 128;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
+        if (row < p.B) {
+          x0 = *reinterpret_cast<const float4*>(pr + 32 * b + 4 * t);
+          x1 = *reinterpret_cast<const float4*>(pr + 32 * b + 16 + 4 * t);
+        }
+        v[r][b][0] = x0.x * p.qscale; v[r][b][1] = x0.y * p.qscale; v[r][b][2] = x0.z * p.qscale;
+        v[r][b][3] = x0.w * p.qscale; v[r][b][4] = x1.x * p.qscale; v[r][b][5] = x1.y * p.qscale;
+        v[r][b][6] = x1.z * p.qscale; v[r][b][7] = x1.w * p.qscale;
+      }
     }
+    float s2[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      float a = 0.0f;
+#pragma unroll
+      for (int b = 0; b < 4; ++b)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) a = fmaxf(a, fabsf(v[r][b][e]));
+      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));  // the row's 4 threads
+      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+      const float s1 = a > 0.0f ? a / 127.0f : 1.0f;
+      const float inv1 = a > 0.0f ? 127.0f / a : 0.0f;
+      const float inv2 = 127.0f * inv1;
+      s2[r] = s1 * (1.0f / 127.0f);
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        int c1[8], c2[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          c1[e] = max(-127, min(127, __float2int_rn(v[r][b][e] * inv1)));
+          c2[e] = max(-127, min(127, __float2int_rn(fmaf(-s1, (float)c1[e], v[r][b][e]) * inv2)));
+        }
+        // A registers: 0 = (row g, k 4t..), 1 = (row g + 8, k 4t..), 2 = (row g, k 16 + 4t..), 3 = (row g + 8, ..)
+        qc[0][b][r] = pack_s8x4(c1[0], c1[1], c1[2], c1[3]);
+        qc[0][b][2 + r] = pack_s8x4(c1[4], c1[5], c1[6], c1[7]);
+        qc[1][b][r] = pack_s8x4(c2[0], c2[1], c2[2], c2[3]);
+        qc[1][b][2 + r] = pack_s8x4(c2[4], c2[5], c2[6], c2[7]);
+      }
+    }
+    s2a = s2[0];
+    s2b = s2[1];
   }
 
   float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.0f, l_b = 0.0f;  // rows g and g + 8
@@ -182,7 +223,6 @@ __global__ void __launch_bounds__(32 * kWarps, 2)
   bool dead = false;
   // ldmatrix row addresses: matrix mi = lane / 8, row r = lane % 8
   const int mi = lane >> 3, r8 = lane & 7;
-  const uint32_t kq_off = (uint32_t)(((mi >> 1) * 8 + r8) * kHPitch + (mi & 1) * 16);  // K: tokens x dims
   const uint32_t v_off = (uint32_t)(((mi & 1) * 8 + r8) * kHPitch + (mi >> 1) * 16);   // V: tokens x dims, .trans
 
   for (int i = 0; i < ntiles; ++i) {
@@ -193,73 +233,70 @@ __global__ void __launch_bounds__(32 * kWarps, 2)
       const int tok = threadIdx.x >> 1, hb = threadIdx.x & 1;
       const uint8_t* rk = smem + s * kRawTile + tok * kRawRow + xoff;
       const uint8_t* rv = smem + kOffRawV + s * kRawTile + tok * kRawRow + xoff;
-      uint8_t* dkh = smem + kOffKh + tok * kHPitch;
-      uint8_t* dkl = smem + kOffKl + tok * kHPitch;
       uint8_t* dvh = smem + kOffVh + tok * kHPitch;
       uint8_t* dvl = smem + kOffVl + tok * kHPitch;
 #pragma unroll
       for (int bi = 0; bi < 2; ++bi) {
         const int blk = 2 * hb + bi;
-        // code * d rounded once to fp16 (mul.rn) and its remainder (fma.rn of
-        // the exact product minus the high part): the bits of rounding the
-        // exact fp32 product, in fp16 arithmetic
-        const __half sdk = *reinterpret_cast<const __half*>(rk + 34 * blk);
+        // V: code * d rounded once to fp16 (mul.rn) and its remainder (fma.rn
+        // of the exact product minus the high part): the bits of rounding the
+        // exact fp32 product, in fp16 arithmetic; K: its block scales only
+        dks[blk * kTTile + tok] = __half2float(*reinterpret_cast<const __half*>(rk + 34 * blk));
         const __half sdv = *reinterpret_cast<const __half*>(rv + 34 * blk);
-        const __half2 dk2 = __halves2half2(sdk, sdk), dv2 = __halves2half2(sdv, sdv);
+        const __half2 dv2 = __halves2half2(sdv, sdv);
 #pragma unroll
         for (int pr = 0; pr < 4; ++pr) {  // 8 codes
           const int co = 34 * blk + 2 + 8 * pr;
-          const uint32_t k0 = lds_u32_a2(rk + co), k1 = lds_u32_a2(rk + co + 4);
           const uint32_t v0 = lds_u32_a2(rv + co), v1 = lds_u32_a2(rv + co + 4);
-          __half2 c[4], e[4];
-          codes_f16(k0, c[0], c[1]);
-          codes_f16(k1, c[2], c[3]);
+          __half2 e[4];
           codes_f16(v0, e[0], e[1]);
           codes_f16(v1, e[2], e[3]);
-          __half2 h2[4], g2[4];
+          __half2 g2[4];
 #pragma unroll
-          for (int x = 0; x < 4; ++x) {
-            h2[x] = __hmul2(c[x], dk2);
-            g2[x] = __hmul2(e[x], dv2);
-          }
-          const uint4 hi = make_uint4(h2u(h2[0]), h2u(h2[1]), h2u(h2[2]), h2u(h2[3]));
-          const uint4 lo = make_uint4(h2u(__hfma2(c[0], dk2, __hneg2(h2[0]))), h2u(__hfma2(c[1], dk2, __hneg2(h2[1]))),
-                                      h2u(__hfma2(c[2], dk2, __hneg2(h2[2]))), h2u(__hfma2(c[3], dk2, __hneg2(h2[3]))));
+          for (int x = 0; x < 4; ++x) g2[x] = __hmul2(e[x], dv2);
           const uint4 vv = make_uint4(h2u(g2[0]), h2u(g2[1]), h2u(g2[2]), h2u(g2[3]));
           const uint4 vl = make_uint4(h2u(__hfma2(e[0], dv2, __hneg2(g2[0]))), h2u(__hfma2(e[1], dv2, __hneg2(g2[1]))),
                                       h2u(__hfma2(e[2], dv2, __hneg2(g2[2]))), h2u(__hfma2(e[3], dv2, __hneg2(g2[3]))));
           const int d = (32 * blk + 8 * pr) * 2;
-          *reinterpret_cast<uint4*>(dkh + d) = hi;
-          *reinterpret_cast<uint4*>(dkl + d) = lo;
           *reinterpret_cast<uint4*>(dvh + d) = vv;
           *reinterpret_cast<uint4*>(dvl + d) = vl;
         }
       }
     }
-    fence_proxy_async_smem();  // the raw stage's generic reads, before the TMA refills it
-    __syncthreads();           // fp16 tiles complete
-    if (threadIdx.x == 0 && i + kStages < ntiles) issue(i + kStages);
+    __syncthreads();  // V tiles and K scales complete
 
-    // ---- S = Q_hi K_hi + Q_lo K_hi + Q_hi K_lo: 16 queries x 64 tokens per warp ----
+    // ---- S: 16 queries x 64 tokens per warp; per 32-dim block two s8 MMAs
+    // (query levels) on the raw K codes, then the block's K scale ----
     float sc[8][4];
 #pragma unroll
     for (int j = 0; j < 8; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
+    {
+      const uint8_t* kraw = smem + s * kRawTile + xoff + 2 + 4 * t;
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
+      for (int j = 0; j < 8; ++j) {
+        const uint8_t* krow = kraw + (8 * j + g) * kRawRow;  // B column = token 8 j + g
 #pragma unroll
-      for (int np = 0; np < 4; ++np) {
-        const uint32_t off = kq_off + (uint32_t)(16 * np * kHPitch + 32 * kk);
-        uint32_t bh[4], bl[4];
-        ldsm_x4(bh, kh_s + off);
-        ldsm_x4(bl, kl_s + off);
-        mma_f16(sc[2 * np], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], bh[0], bh[1]);
-        mma_f16(sc[2 * np + 1], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], bh[2], bh[3]);
-        mma_f16(sc[2 * np], qr[kk][0], qr[kk][1], qr[kk][2], qr[kk][3], bh[0], bh[1]);
-        mma_f16(sc[2 * np + 1], qr[kk][0], qr[kk][1], qr[kk][2], qr[kk][3], bh[2], bh[3]);
-        mma_f16(sc[2 * np], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], bl[0], bl[1]);
-        mma_f16(sc[2 * np + 1], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], bl[2], bl[3]);
+        for (int b = 0; b < 4; ++b) {
+          const uint32_t b0 = lds_u32_a2(krow + 34 * b), b1 = lds_u32_a2(krow + 34 * b + 16);
+          int d1[4], d2[4];
+          mma_s8(d1, qc[0][b], b0, b1);
+          mma_s8(d2, qc[1][b], b0, b1);
+          const float2 dk = *reinterpret_cast<const float2*>(dks + b * kTTile + 8 * j + 2 * t);
+          sc[j][0] = fmaf((float)(127 * d1[0] + d2[0]), dk.x, sc[j][0]);
+          sc[j][1] = fmaf((float)(127 * d1[1] + d2[1]), dk.y, sc[j][1]);
+          sc[j][2] = fmaf((float)(127 * d1[2] + d2[2]), dk.x, sc[j][2]);
+          sc[j][3] = fmaf((float)(127 * d1[3] + d2[3]), dk.y, sc[j][3]);
+        }
+        sc[j][0] *= s2a;
+        sc[j][1] *= s2a;
+        sc[j][2] *= s2b;
+        sc[j][3] *= s2b;
       }
     }
+    // the raw stage is no longer read: refill it once every warp is past QK
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (threadIdx.x == 0 && i + kStages < ntiles) issue(i + kStages);
     // tokens past the cache end (the last tile) weigh nothing
     const int tbase = i * kTTile + 2 * t;
     if (i * kTTile + kTTile > p.S) {
@@ -326,7 +363,7 @@ __global__ void __launch_bounds__(32 * kWarps, 2)
         mma_f16(o[2 * np + 1], ph[0], ph[1], ph[2], ph[3], vr[2], vr[3]);
       }
     }
-    __syncthreads();  // the fp16 tiles are rewritten by the next tile
+    __syncthreads();  // the V tiles and K scales are rewritten by the next tile
   }
 
   // ---- out = O / l ----
