@@ -214,6 +214,12 @@ __global__ void __launch_bounds__(kG1Threads, 1)
     fence_mbar_init();
   }
   __syncwarp();
+  // Launched as a programmatic dependent: the set-up above overlaps the
+  // preceding kernel, and nothing in global memory is read before that
+  // kernel has completed (its output may be this call's row or weights).
+  // The next kernel may be scheduled now; it waits for this one likewise.
+  pdl_wait();
+  pdl_launch_dependents();
 
   // ---- q8_1 of the activation row into shared memory ----
   // The row's first values are requested before any weight byte: behind the
@@ -279,8 +285,19 @@ kq_status_t launch_mode(const void* w, const float* x, const OutSpec& out, int N
   const int rpw = 32 >> lpr_log;
   const int tasks = (N + rpw - 1) / rpw;
   const int grid = std::max(1, std::min(sm_count(), tasks));
-  kern<<<grid, kG1Threads, smem, s>>>(static_cast<const uint8_t*>(w), x, out, N, K, lpr_log,
-                                      err ? err : device_error_word());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kG1Threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<const uint8_t*>(w), x, out, N, K, lpr_log,
+                                     err ? err : device_error_word());
+  if (e != cudaSuccess) return check_cuda(e, "gemv1 launch");
   return check_launch("gemv1");
 }
 
