@@ -143,6 +143,9 @@ __global__ void __launch_bounds__(32 * kWarps)
                 warp * kWarpSmem;
   uint64_t* full = reinterpret_cast<uint64_t*>(ws + kOffBar);
   int8_t* qc = reinterpret_cast<int8_t*>(ws + kOffQ);  // [query][level][128]
+  // launched as a programmatic dependent: no global read before the
+  // preceding kernel (the previous call's merge, or the queries' producer) ends
+  pdl_wait();
 
   // the grid covers exactly nunits * nchunk tasks (nchunk % kWarps == 0), so
   // the CTA's warps hold consecutive chunks of one unit and all reach the
@@ -358,6 +361,7 @@ __global__ void __launch_bounds__(32 * kWarps)
 template <typename OT, bool RAGGED>
 __global__ void __launch_bounds__(128) fa_small_combine_kernel(SmallParams p, int Q) {
   pdl_wait();  // the decode grid's partials
+  pdl_launch_dependents();  // a following decode waits for this grid in turn
   const int qg = blockIdx.x * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (qg >= Q) return;
@@ -466,7 +470,20 @@ kq_status_t launch(SmallParams p, const void* k, const void* v, uint64_t rows, i
   kq_status_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), kSmem, "fa_small smem attribute");
   if (st) return st;
   const long long tasks = (long long)p.nunits * p.nchunk;
-  kern<<<(unsigned)((tasks + kWarps - 1) / kWarps), 32 * kWarps, kSmem, s>>>(km, vm, p);
+  {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((tasks + kWarps - 1) / kWarps));
+    cfg.blockDim = dim3(32 * kWarps);
+    cfg.dynamicSmemBytes = kSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, km, vm, p);
+    if (e != cudaSuccess) return check_cuda(e, "fa_small launch");
+  }
   if ((st = check_launch("fa_small"))) return st;
   // a programmatic dependent of the decode kernel: its launch overlaps the decode
   cudaLaunchConfig_t cfg = {};

@@ -223,6 +223,9 @@ __global__ void __maxnreg__(112)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* empty = full + kStages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // launched as a programmatic dependent: no global read before the
+  // preceding kernel (the previous call's merge, or the queries' producer) ends
+  pdl_wait();
 
   // ---- schedule: tile prefix over the sequences ----
   Sched sc;
@@ -550,6 +553,7 @@ __global__ void __maxnreg__(112)
 template <typename OT, bool RAGGED>
 __global__ void __launch_bounds__(128) fa_stream_combine_kernel(StreamParams p, int Q, int G) {
   pdl_wait();  // the decode grid's partials
+  pdl_launch_dependents();  // a following decode waits for this grid in turn
   const int qg = blockIdx.x * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (qg >= Q) return;
@@ -705,7 +709,20 @@ kq_status_t launch(StreamParams p, const void* k, const void* v, uint64_t rows, 
   // schedule splits the tiles evenly over exactly the CTAs that run at once
   int G = grid_size(reinterpret_cast<const void*>(kern), RAGGED ? 0 : 1);
   if (tiles_estimate < kTwoCtaMinTilesPerSm * sm_count()) G = std::min(G, sm_count());
-  kern<<<G, kThreads, kSmem, s>>>(km, vm, p);
+  {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(G);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, km, vm, p);
+    if (e != cudaSuccess) return check_cuda(e, "fa_stream launch");
+  }
   if ((st = check_launch("fa_stream"))) return st;
   // a programmatic dependent of the decode kernel
   cudaLaunchConfig_t cfg = {};
