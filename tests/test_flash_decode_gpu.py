@@ -343,3 +343,23 @@ def test_batch_mha(cuda, B, S, H):
     assert ok, msg
     assert Q.nmse(got, Q.flash_decode_mha(q, k, v, S, H, D)) < 0.05
     assert kq.device_error() == 0
+
+
+@pytest.mark.parametrize("lens,Hq,Hkv", [([8192], 32, 8), ([64] * 32 + [4096] * 8, 32, 8)])
+def test_decode_after_producer(cuda, lens, Hq, Hkv):
+    """The decode kernels are programmatic dependents of whatever precedes
+    them: each call here directly follows torch's copy of fresh queries into
+    the query buffer, and must see them (small-batch and stream kernels)."""
+    import kq
+    rng = np.random.default_rng(len(lens) + Hq)
+    D = 128
+    _, k, v, cu = _ragged_case(rng, lens, Hq, Hkv, D)
+    kd, vd, cud = _t(k, cuda), _t(v, cuda), _t(cu, cuda)
+    qd = torch.empty((len(lens), Hq, D), dtype=torch.float16, device=cuda)
+    scale = 1.0 / np.sqrt(D)
+    for it in range(3):
+        q = (rng.standard_normal((len(lens), Hq, D)) * (1 + it)).astype(np.float16)
+        qd.copy_(_t(q, cuda))
+        got = kq.flash_decode_ragged(qd, kd, vd, cud, Hkv, scale=scale).float().cpu().numpy()
+        ok, msg = Q.check_close(got, Q.flash_decode_ragged(q, k, v, cu, Hq, Hkv, D, scale))
+        assert ok, f"iteration {it}: {msg}"

@@ -423,3 +423,26 @@ def test_single_launch_gemv_unaligned_falls_back(cuda):
     got = kq.gemm_f32act(wbuf[2:2 + w.size], _t(x, cuda), 1, N, K, "q4_0", "f32")
     ok, msg = Q.check_close(got.cpu().numpy(), Q.gemm_f32act("q4_0", w.reshape(N, -1), x, 1, N, K, Q.ACT_F32))
     assert ok, msg
+
+
+def test_single_launch_gemv_after_producer(cuda):
+    """The single-launch GEMV is a programmatic dependent of whatever kernel
+    precedes it: it must not read the activation row or the weights before
+    that kernel ends. Here each call directly follows a device kernel that
+    rewrites its input (torch's copy of a new row, then the library's own
+    weight quantiser), with fresh values every time."""
+    import kq
+    rng = np.random.default_rng(31)
+    N, K = 2048, 4096
+    xd = torch.empty((1, K), dtype=torch.float32, device=cuda)
+    wf_d = torch.empty((N, K), dtype=torch.float32, device=cuda)
+    for it in range(4):
+        x = _x(rng, 1, K) * np.float32(1 + it)
+        wf = rng.standard_normal((N, K)).astype(np.float32)
+        wf_d.copy_(_t(wf, cuda))
+        w = kq.quantize_rows(wf_d, "q4_0")           # producer of the weights
+        xd.copy_(_t(x, cuda))                         # producer of the row, directly before the GEMV
+        got = kq.gemm_f32act(w.reshape(-1), xd, 1, N, K, "q4_0", "sum_x").cpu().numpy()
+        ref = Q.gemm_f32act("q4_0", Q.quantize_weights("q4_0", wf), x, 1, N, K, Q.SUM_X)
+        ok, msg = Q.check_close(got, ref)
+        assert ok, f"iteration {it}: {msg}"
