@@ -511,7 +511,7 @@ def bench_gemm(args, cfg, rank, world, *, steps, warmup, clocks_on=True):
     # ---- dominant kernel alone (the GEMM on pre-staged activations) ----
     # One activation row with 4-bit weights is a single launch (gemv1_kernel
     # quantises the row itself): the step is the kernel.
-    single = M == 1 and wt in ("q4_0", "q4_1") and K % 256 == 0
+    single = M == 1 and wt in ("q4_0", "q4_1", "q8_0") and K % 256 == 0
     qs = [torch.empty((M, K), dtype=torch.int8, device=dev) for _ in range(0 if single else nsets)]
     dss = [torch.empty((M, nb, 2), dtype=torch.float32, device=dev) for _ in range(nsets)]
     for j in range(len(qs)):  # stage once with the library's own quantiser (not timed)

@@ -192,8 +192,8 @@ kq_status_t kq_gemm_f32act(int wtype, const void* w, const float* x, float* out,
  * before any stream capture. All calls share the array: calls that overlap on
  * the GPU race. Same arguments as kq_gemm_f32act; for M > 8 it runs the int8
  * tensor-core kernel (no fp16 operand workspace), whose results agree with
- * kq_gemm_f32act's to the parity bar rather than bit for bit. For M = 1 with
- * q4_0 / q4_1 weights both entry points run the same single-launch GEMV,
+ * kq_gemm_f32act's to the parity bar rather than bit for bit. For M = 1 both
+ * entry points run the same single-launch GEMV,
  * which quantises the row in shared memory and touches no staging. */
 kq_status_t kq_gemm_f32act_noalloc(int wtype, const void* w, const float* x, float* out, int M, int N, int K,
                                    int act_mode, kq_stream_t stream);

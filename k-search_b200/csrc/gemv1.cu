@@ -1,9 +1,10 @@
-// Single-launch GEMV for one fp32 activation row over 4-bit weight rows
-// (q4_0 / q4_1): out[n] = sum_b f(weight block (n, b), q8_1(x) block b). This
-// is the W4A32C8 operator at M = 1 (the harness quant_gemm op,
+// Single-launch GEMV for one fp32 activation row over q4_0 / q4_1 / q8_0
+// weight rows: out[n] = sum_b f(weight block (n, b), q8_1(x) block b). This
+// is the W4A32C8 / W8A32C8 operator at M = 1 (the harness quant_gemm op,
 // llm_kernel_test/op_test_handler.py:128-458, with the per-block formulas of
-// vec_dot_q4_0_q8_1, kernelevalplus-main/include/gemm_reference.h:276-306,
-// and reference_q4_1_q8_1_gemm, llm_kernel_test/reference/gemm_ref.py:274-331).
+// vec_dot_q4_0_q8_1 and vec_dot_q8_0_q8_1, kernelevalplus-main/include/
+// gemm_reference.h:276-336, and reference_q4_1_q8_1_gemm,
+// llm_kernel_test/reference/gemm_ref.py:274-331).
 //
 // At M = 1 the operator is one HBM stream of the weights (9.4 MB at
 // N = K = 4096), and its time is mostly fixed costs: a quantiser launch in
@@ -19,10 +20,11 @@
 //  * then walks its rows with the next item's copies in flight while the
 //    current item is computed (two shared-memory slots per warp).
 // An item is the contiguous byte range a warp computes in one step: RPW
-// whole rows when a row has at most 32 chunks of 8 blocks (144 / 160 bytes),
+// whole rows when a row has at most 32 chunks (8 blocks of q4_0 / q4_1, 144 /
+// 160 bytes; 4 blocks of q8_0, 136 bytes),
 // else 32 chunks of one row. The LPR lanes of a row (a power of two <= 32)
 // each take one chunk of it, read it from the warp's slot with 16-byte loads
-// (lane stride 144 / 160 bytes: conflict-free), sum their blocks in order and
+// (lane stride 144 / 160 / 136 bytes: conflict-free), sum their blocks in order and
 // reduce with an xor tree, so results are deterministic.
 // Activation codes sit in shared memory as 16-byte pieces ordered
 // [block-in-chunk j][half h][chunk c]: the LPR lanes of a row read chunks
@@ -44,25 +46,31 @@ constexpr int kG1MaxK = 32768;  // shared memory: K code bytes + 8 bytes per blo
 
 template <int WT>
 struct G1Traits;
+// BB: bytes per block; CB: blocks per lane chunk (8 for the 4-bit formats,
+// 144 / 160 bytes; 4 for q8_0, 136 bytes, so an item keeps the same size)
 template <>
 struct G1Traits<KQ_Q4_0> {
-  static constexpr int BB = 18;
+  static constexpr int BB = 18, CB = 8;
 };
 template <>
 struct G1Traits<KQ_Q4_1> {
-  static constexpr int BB = 20;
+  static constexpr int BB = 20, CB = 8;
+};
+template <>
+struct G1Traits<KQ_Q8_0> {
+  static constexpr int BB = 34, CB = 4;
 };
 
 constexpr int kSlots = 2;  // weight slots per warp
 template <int WT>
-constexpr int kSlotBytes = 32 * 8 * G1Traits<WT>::BB;  // one item: 32 chunks of 8 blocks
+constexpr int kSlotBytes = 32 * G1Traits<WT>::CB * G1Traits<WT>::BB;  // one item: 32 chunks
 
 // Item q of a warp's sequence: task T = gw + (q / cpl) * tw, iteration
 // i = q % cpl. Its bytes are the contiguous range [start, start + len):
 // rows [T * RPW, T * RPW + RPW) whole when cpl == 1, else chunks
 // [32 i, 32 i + 32) of row T (then RPW = 1, LPR = 32). Lane (row-in-task
 // rho = lane / LPR, sub = lane % LPR) computes chunk c = sub + 32 i of row
-// r = T * RPW + rho, found at slot offset rho * rowbytes + sub * 8 * BB.
+// r = T * RPW + rho, found at slot offset rho * rowbytes + sub * CB * BB.
 // `last` marks the task's final item.
 struct Item {
   size_t start;
@@ -103,20 +111,35 @@ __device__ __forceinline__ void issue_item(uint8_t* slot, uint64_t* bar, const u
   bulk_g2s_hint(slot, w + it.start, it.len, bar, pol);
 }
 
-// Blocks J .. 7 of a chunk held in w[] against the activation pieces at
+// Blocks J .. CB - 1 of a chunk held in w[] against the activation pieces at
 // aq (chunk c's column; piece (j, h) at aq + (2j + h) * c16) and the (d, s')
 // pairs at ads[j * C].
 template <int WT, int J, int NW>
 __device__ __forceinline__ void chunk_dot(const uint32_t (&w)[NW], const uint8_t* aq, int c16, const float2* ads,
                                           int C, float& acc) {
-  if constexpr (J < 8) {
+  if constexpr (J < G1Traits<WT>::CB) {
     constexpr int OFF = J * G1Traits<WT>::BB;
-    constexpr int QOFF = (WT == KQ_Q4_0) ? OFF + 2 : OFF + 4;
-    uint32_t raw[4];
-    gather_u32<QOFF>(w, raw);
     const uint4 alo = *reinterpret_cast<const uint4*>(aq + (2 * J) * c16);
     const uint4 ahi = *reinterpret_cast<const uint4*>(aq + (2 * J + 1) * c16);
     const float2 ds = ads[J * C];
+    if constexpr (WT == KQ_Q8_0) {
+      // d_w * d_a * sumi over the block's 32 int8 codes
+      uint32_t q[8];
+      gather_u32<OFF + 2>(w, q);
+      int s0 = __dp4a((int)q[0], (int)alo.x, 0);
+      int s1 = __dp4a((int)q[4], (int)ahi.x, 0);
+      s0 = __dp4a((int)q[1], (int)alo.y, s0);
+      s1 = __dp4a((int)q[5], (int)ahi.y, s1);
+      s0 = __dp4a((int)q[2], (int)alo.z, s0);
+      s1 = __dp4a((int)q[6], (int)ahi.z, s1);
+      s0 = __dp4a((int)q[3], (int)alo.w, s0);
+      s1 = __dp4a((int)q[7], (int)ahi.w, s1);
+      const float dw = half_bits_to_float(get_u16<OFF>(w));
+      acc = fmaf(dw * ds.x, (float)(s0 + s1), acc);
+    } else {
+    constexpr int QOFF = (WT == KQ_Q4_0) ? OFF + 2 : OFF + 4;
+    uint32_t raw[4];
+    gather_u32<QOFF>(w, raw);
     // two independent dp4a chains (low and high nibbles), exact int32 sums
     int sl = __dp4a((int)(raw[0] & 0x0F0F0F0Fu), (int)alo.x, 0);
     int sh = __dp4a((int)((raw[0] >> 4) & 0x0F0F0F0Fu), (int)ahi.x, 0);
@@ -135,6 +158,7 @@ __device__ __forceinline__ void chunk_dot(const uint32_t (&w)[NW], const uint8_t
       // d_w * d_a * sumi + m_w * s_a
       const float mw = half_bits_to_float(get_u16<OFF + 2>(w));
       acc = fmaf(dw * ds.x, (float)s, fmaf(mw, ds.y, acc));
+    }
     }
     chunk_dot<WT, J + 1>(w, aq, c16, ads, C, acc);
   }
@@ -155,17 +179,27 @@ __device__ __forceinline__ void load_x_step(float4 (&v)[4], const float* __restr
 template <int WT>
 __device__ __forceinline__ void compute_item(const uint8_t* slot, const Item& it, const G1Geom& g, int lane,
                                              const uint8_t* sq, const float2* sds, const OutSpec& out, float& acc) {
-  constexpr int NW = 2 * G1Traits<WT>::BB;  // 32-bit words per 8-block chunk
+  constexpr int CBYTES = G1Traits<WT>::CB * G1Traits<WT>::BB;  // a lane's chunk (its stride in the slot)
+  constexpr int NW = CBYTES / 4;
   if (it.valid) {
-    const uint4* p = reinterpret_cast<const uint4*>(slot + (lane >> g.lpr_log) * g.rowbytes + g.sub * g.chunkbytes);
+    const uint8_t* src = slot + (lane >> g.lpr_log) * g.rowbytes + g.sub * CBYTES;
     uint32_t w[NW];
+    if constexpr (CBYTES % 16 == 0) {
 #pragma unroll
-    for (int i = 0; i < NW / 4; ++i) {
-      const uint4 v = p[i];
-      w[4 * i] = v.x;
-      w[4 * i + 1] = v.y;
-      w[4 * i + 2] = v.z;
-      w[4 * i + 3] = v.w;
+      for (int i = 0; i < NW / 4; ++i) {
+        const uint4 v = reinterpret_cast<const uint4*>(src)[i];
+        w[4 * i] = v.x;
+        w[4 * i + 1] = v.y;
+        w[4 * i + 2] = v.z;
+        w[4 * i + 3] = v.w;
+      }
+    } else {  // q8_0: 136-byte chunks, 8-byte aligned (lane stride 34 words: conflict-free 8-byte loads)
+#pragma unroll
+      for (int i = 0; i < NW / 2; ++i) {
+        const uint2 v = reinterpret_cast<const uint2*>(src)[i];
+        w[2 * i] = v.x;
+        w[2 * i + 1] = v.y;
+      }
     }
     const int c = it.c0 + g.sub;
     chunk_dot<WT, 0>(w, sq + c * 16, g.C * 16, sds + c, g.C, acc);
@@ -188,9 +222,10 @@ __global__ void __launch_bounds__(kG1Threads, 1)
   constexpr int BB = G1Traits<WT>::BB;
   extern __shared__ __align__(16) uint8_t smem[];
   const int nb = K >> 5;
-  const int C = nb >> 3;
+  constexpr int CB = G1Traits<WT>::CB;
+  const int C = nb / CB;
   uint8_t* sq = smem;                                  // piece (j, h, c) at ((2j + h) * C + c) * 16
-  float2* sds = reinterpret_cast<float2*>(smem + K);  // (d_a, s') of block 8c + j at j * C + c
+  float2* sds = reinterpret_cast<float2*>(smem + K);  // (d_a, s') of block CB c + j at j * C + c
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   G1Geom g;
@@ -201,7 +236,7 @@ __global__ void __launch_bounds__(kG1Threads, 1)
   g.gw = warp * gridDim.x + blockIdx.x;
   g.tw = gridDim.x * kG1Warps;
   g.sub = lane & ((1 << lpr_log) - 1);
-  g.chunkbytes = 8 * BB;
+  g.chunkbytes = CB * BB;
   g.rowbytes = (uint32_t)nb * BB;
   const int tasks = (N + (32 >> lpr_log) - 1) / (32 >> lpr_log);
   const int nitems = (g.gw < tasks ? (tasks - 1 - g.gw) / g.tw + 1 : 0) * g.cpl;
@@ -245,7 +280,7 @@ __global__ void __launch_bounds__(kG1Threads, 1)
     for (int u = 0; u < 4; ++u) {
       const int blk = b0 + u * kStep + grp;
       if (blk < nb) {
-        const int c = blk >> 3, j = blk & 7, h = osub >> 2;
+        const int c = blk / CB, j = blk % CB, h = osub >> 2;
         *reinterpret_cast<uint32_t*>(sq + ((2 * j + h) * C + c) * 16 + (osub & 3) * 4) = r[u].qs;
         if (osub == 0) {
           float2 ds = staging_ds<MODE>(r[u]);
@@ -279,7 +314,7 @@ kq_status_t launch_mode(const void* w, const float* x, const OutSpec& out, int N
   const int smem = K + (K / 32) * (int)sizeof(float2) + kG1Warps * kSlots * (kSlotBytes<WT> + (int)sizeof(uint64_t));
   if (kq_status_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem, "gemv1 smem attribute"))
     return st;
-  const int C = K / 256;
+  const int C = K / (32 * G1Traits<WT>::CB);
   int lpr_log = 0;
   while ((1 << lpr_log) < C && lpr_log < 5) ++lpr_log;
   const int rpw = 32 >> lpr_log;
@@ -315,7 +350,7 @@ kq_status_t launch_wt(const void* w, const float* x, const OutSpec& out, int N, 
 }  // namespace
 
 bool gemv1_supported(int wtype, int M, int N, int K, const void* w, const float* x) {
-  return M == 1 && (wtype == KQ_Q4_0 || wtype == KQ_Q4_1) && N >= 1 && K >= 256 && K % 256 == 0 && K <= kG1MaxK &&
+  return M == 1 && (wtype == KQ_Q4_0 || wtype == KQ_Q4_1 || wtype == KQ_Q8_0) && N >= 1 && K >= 256 && K % 256 == 0 && K <= kG1MaxK &&
          reinterpret_cast<uintptr_t>(w) % 16 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0;
 }
 
@@ -324,7 +359,8 @@ kq_status_t launch_gemv1(int wtype, const void* w, const float* x, const OutSpec
   switch (wtype) {
     case KQ_Q4_0: return launch_wt<KQ_Q4_0>(w, x, out, N, K, mode, s, err);
     case KQ_Q4_1: return launch_wt<KQ_Q4_1>(w, x, out, N, K, mode, s, err);
-    default: return fail(KQ_ERR_INVALID, "gemv1: weight type %d is not 4-bit", wtype);
+    case KQ_Q8_0: return launch_wt<KQ_Q8_0>(w, x, out, N, K, mode, s, err);
+    default: return fail(KQ_ERR_INVALID, "gemv1: unknown weight type %d", wtype);
   }
 }
 

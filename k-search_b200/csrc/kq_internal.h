@@ -111,7 +111,7 @@ kq_status_t launch_gemv(int wtype, const void* w, Act8 act, const OutSpec& out, 
                         cudaStream_t s, int* err = nullptr);
 kq_status_t launch_gemv(int wtype, const void* w, Act8 act, float* out, int M, int N, int K, bool pdl,
                         cudaStream_t s, int* err = nullptr);
-// gemv1.cu: one launch for M = 1 with 4-bit weights (q4_0 / q4_1): quantises
+// gemv1.cu: one launch for M = 1 (q4_0 / q4_1 / q8_0 weights): quantises
 // the fp32 row itself (bit-identical codes), no workspace. K % 256 == 0,
 // K <= 32768, w and x 16-byte aligned.
 bool gemv1_supported(int wtype, int M, int N, int K, const void* w, const float* x);

@@ -378,13 +378,14 @@ def test_harness_mirror(cuda):
     assert perf["tflops"] == round(2 * M * N * K / 1e-5 / 1e12, 3)
 
 
-@pytest.mark.parametrize("wtype", ["q4_0", "q4_1"])
+@pytest.mark.parametrize("wtype", ["q4_0", "q4_1", "q8_0"])
 @pytest.mark.parametrize("N,K", [(1, 256), (7, 3584), (33, 4096), (4096, 4096), (300, 11008), (129, 14336),
                                  (1000, 2048), (5, 65536)])
 def test_single_launch_gemv(cuda, wtype, N, K):
-    """M = 1 with 4-bit weights runs one kernel that quantises the row itself
-    (gemv1.cu). K sets the lanes per row (chunk counts 1, 14, 16, 43, 56, 8,
-    256: idle lanes, two chunks per lane, the 32-lane cap) and N the ragged
+    """M = 1 runs one kernel that quantises the row itself (gemv1.cu). K
+    sets the lanes per row (4-bit chunk counts 1, 14, 16, 43, 56, 8, 256,
+    twice as many for q8_0's 4-block chunks: idle lanes, several chunks per
+    lane, the 32-lane cap) and N the ragged
     last warp. Checked against the oracle in every activation mode, and
     against the two-launch path on the same q8_1 bytes (kq_quantize_q8_1 then
     kq_mul_mat_q, the staged GEMV): both read identical codes and scales, so
