@@ -667,6 +667,10 @@ constexpr size_t kPartialBudget = 64ull << 20;
 // (small vs stream): harness S = 8192 B = 1 28.2 vs 42.9 us, B = 2 32.6 vs
 // 46.2, B = 3 56.3 vs 46.4; S = 512 B = 4 10.0 vs 18.4; one ragged sequence
 // of 8192 tokens (Hq 32, Hkv 8) 21.7 vs 42.0; four of 8192 55.3 vs 41.8.
+// Shapes the stream kernel does not take (KV heads not in groups of 8) and
+// the batch kernel does not either go to the small-batch kernel at any size:
+// the generic split-KV kernel is about 3x slower there (harness H = 28,
+// B = 8, S = 8192: 250 vs 74 us; ragged Hkv = 4, 8 x 4096 tokens: 83 vs 33).
 bool small_batch(long long stream_tiles, int queries_per_kv_head) {
   const long long per_sm = queries_per_kv_head <= 2 ? 20 : 4;
   return stream_tiles < per_sm * sm_count();
@@ -727,10 +731,15 @@ kq_status_t launch_fa_mha(int kvf, const float* q, const void* k, const void* v,
   if (Q == 0) return KQ_OK;
   if (kvf == KQ_KV_Q8_0 && fa_path() == FaPath::kStream && S > 0) {
     const long long tiles = (long long)((B + 3) / 4) * (H / 8) * ((S + 15) / 16);
-    if (small_batch(tiles, std::min(B, 4)) && fa_small_supported(q, k, v, out, D, H, std::min(B, 4)))
+    const bool batch = fa_batch_supported(q, k, v, out, B, S, H, D);
+    const bool stream = fa_stream_supported(q, k, v, out, D, H, 1, 0);
+    // the small-batch kernel also takes what neither other kernel does (head
+    // counts not in groups of 8): the generic kernel is ~3x slower there
+    if ((small_batch(tiles, std::min(B, 4)) || (!batch && !stream)) &&
+        fa_small_supported(q, k, v, out, D, H, std::min(B, 4)))
       return launch_fa_small_mha(q, k, v, out, B, S, H, s);
-    if (fa_batch_supported(q, k, v, out, B, S, H, D)) return launch_fa_batch_mha(q, k, v, out, B, S, H, s);
-    if (fa_stream_supported(q, k, v, out, D, H, 1, 0)) return launch_fa_stream_mha(q, k, v, out, B, S, H, s);
+    if (batch) return launch_fa_batch_mha(q, k, v, out, B, S, H, s);
+    if (stream) return launch_fa_stream_mha(q, k, v, out, B, S, H, s);
   }
   const bool fast = kvf == KQ_KV_Q8_0 && fast_ok(k, v, D, H, 1) && S > 0 &&
                     (long long)((B + kG - 1) / kG) * (H / kHpc) <= 65535;
@@ -775,10 +784,10 @@ kq_status_t launch_fa_ragged(const void* q, const void* k, const void* v, const 
   const int g = Hq / Hkv;
   if (fa_path() == FaPath::kStream) {
     const long long tiles = (long long)B * std::max(1, Hkv / 8) * ((std::max(max_seqlen, 1) + 15) / 16);
-    if (small_batch(tiles, g) && fa_small_supported(q, k, v, out, D, Hkv, g))
+    const bool stream = fa_stream_supported(q, k, v, out, D, Hkv, g, B);
+    if ((small_batch(tiles, g) || !stream) && fa_small_supported(q, k, v, out, D, Hkv, g))
       return launch_fa_small_ragged(q, k, v, cu, B, Hq, Hkv, max_seqlen, total_rows, scale, out, s);
-    if (fa_stream_supported(q, k, v, out, D, Hkv, g, B))
-      return launch_fa_stream_ragged(q, k, v, cu, B, Hq, Hkv, total_rows, scale, out, s);
+    if (stream) return launch_fa_stream_ragged(q, k, v, cu, B, Hq, Hkv, total_rows, scale, out, s);
   }
   const bool fast = fast_ok(k, v, D, Hkv, g) && total_rows > 0 && (long long)B * (Hkv / kHpc) <= 65535;
   int chunk = 0;
