@@ -4,7 +4,7 @@ times, for profilers (ncu) and quick timing:
     python bench_cases.py gemm --wtype q8_0 --M 512 --N 11008 --K 4096 --reps 3
     python bench_cases.py gemv --wtype q4_0 --N 14336 --K 4096
     python bench_cases.py decode --B 32 --Lmax 8192
-    python bench_cases.py mha --B 512 --S 8192
+    python bench_cases.py mha --B 512 --S 8192 --fmt q4_0
     python bench_cases.py moe --T 1024
 
 Inputs are generated on the GPU (weights drawn as q-blocks with the
@@ -86,18 +86,22 @@ def run_decode(a) -> str:
 
 def run_mha(a) -> str:
     """The harness flash_attention form: fp32 queries [B, H, 128] over one
-    shared [S, H, 128] q8_0 cache."""
+    shared [S, H, 128] cache (--fmt q8_0, q4_0 or f16)."""
     dev = torch.device("cuda")
     gd = torch.Generator(device=dev).manual_seed(a.seed)
     D = 128
-    k = kq.quantize_rows(torch.randn((a.S * a.H, D), generator=gd, device=dev), "q8_0")
-    v = kq.quantize_rows(torch.randn((a.S * a.H, D), generator=gd, device=dev), "q8_0")
+    kf = torch.randn((a.S * a.H, D), generator=gd, device=dev)
+    vf = torch.randn((a.S * a.H, D), generator=gd, device=dev)
+    if a.fmt == "f16":
+        k, v = kf.half(), vf.half()
+    else:
+        k, v = kq.quantize_rows(kf, a.fmt), kq.quantize_rows(vf, a.fmt)
     q = torch.randn((a.B, a.H, D), generator=gd, device=dev)
-    fn = lambda: kq.flash_attn_q8_0(q, k, v, a.B, a.S, a.H, D)
+    fn = lambda: kq.flash_attn(q, k, v, a.B, a.S, a.H, D, a.fmt)
     ms = _time(fn, a.warmup, a.reps)
     flop = 4.0 * a.B * a.H * a.S * D
-    kv = 2 * a.S * a.H * (D // 32) * 34
-    return (f"mha B={a.B} S={a.S} H={a.H}: {ms * 1e3:.2f} us/call, {flop / (ms * 1e-3) / 1e12:.1f} TFLOP/s, "
+    kv = 2 * k.numel() * k.element_size()
+    return (f"mha {a.fmt} B={a.B} S={a.S} H={a.H}: {ms * 1e3:.2f} us/call, {flop / (ms * 1e-3) / 1e12:.1f} TFLOP/s, "
             f"{kv / (ms * 1e-3) / 1e9:.0f} GB/s of KV")
 
 
@@ -135,6 +139,7 @@ def main(argv=None) -> None:
     p = sub.add_parser("mha")
     for k, v in dict(B=512, S=8192, H=32).items():
         p.add_argument(f"--{k}", type=int, default=v)
+    p.add_argument("--fmt", default="q8_0", choices=["q8_0", "q4_0", "f16"])
     p = sub.add_parser("moe")
     for k, v in dict(T=4096, E=8, topk=2, H=4096, I=14336).items():
         p.add_argument(f"--{k}", type=int, default=v)

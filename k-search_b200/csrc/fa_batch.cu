@@ -1,29 +1,39 @@
-// Flash attention for the harness form with many queries per head over a
-// q8_0 KV cache (D = 128): the harness flash_attention operator
-// (kernelevalplus-main/llm_kernel_test/op_test_handler.py:543-563) shares one
-// [S, H, D] cache across all B queries of a head, so at B = 512 a head is a
-// GEMM pair (S = Q K^T, O = softmax(S) V) rather than a stream of the cache.
+// Flash attention for the harness form with many queries per head (D = 128)
+// over a q8_0, q4_0 or fp16 KV cache: the harness flash_attention operator
+// (kernelevalplus-main/llm_kernel_test/op_test_handler.py:543-563, cache
+// built at :489-534) shares one [S, H, D] cache across all B queries of a
+// head, so at B = 512 a head is a GEMM pair (S = Q K^T, O = softmax(S) V)
+// rather than a stream of the cache.
 //
 // CTA = 4 warps over 64 queries of one head (16 per warp); it walks the
-// cache in 64-token tiles:
-//  * a TMA ring (two stages) brings the raw q8_0 rows of the head (boxes of
-//    64 rows x 144 bytes: the head's 136-byte row 0 or 8 bytes in);
+// cache in 64-token tiles brought by a two-stage TMA ring.
+//
+// Block-quantised caches (fa_batch_kernel<KVF>, q8_0 and q4_0):
+//  * the boxes hold the raw rows of the head (64 rows x 144 bytes for q8_0,
+//    x 80 for q4_0: the head's 136- or 72-byte row sits 0 or 8 bytes in, so
+//    every box starts on a 16-byte boundary);
 //  * QK is exact on the raw K codes (mma.m16n8k32 s8, one MMA per 32-dim
-//    block and query level): the query q * scale * log2(e) is held as two int8
-//    levels (q ~ s1 c1 + s2 c2, s2 = s1 / 127, so 127 dot1 + dot2 is the exact
-//    block dot at scale s2), and the fp32 epilogue applies each (token, block)
-//    K scale, as the decode kernels do;
+//    block and query level; q4_0 nibbles become the int8 codes q - 8): the
+//    query q * scale * log2(e) is held as two int8 levels (q ~ s1 c1 + s2 c2,
+//    s2 = s1 / 127, so 127 dot1 + dot2 is the exact block dot at scale s2),
+//    and the fp32 epilogue applies each (token, block) K scale, as the decode
+//    kernels do;
 //  * the CTA dequantises each V tile once into fp16 in shared memory, as a
 //    high part and its fp16 remainder (hi + lo carries ~22 bits of code * d);
-//  * online softmax per query row in registers (exp2), and P = p as fp16
-//    plus its fp16 remainder, taken straight from the S accumulators as the
-//    A operand of the PV products: O += P_hi V_hi + P_lo V_hi + P_hi V_lo.
+//  * PV = P_hi V_hi + P_lo V_hi + P_hi V_lo (mma.m16n8k16 f16).
+// fp16 caches (fa_batch_f16_kernel): K and V are exact in fp16, so the TMA
+// boxes (two 64-dim halves, 128-byte swizzled) are read by ldmatrix in place;
+// the query is an fp16 high part plus its remainder in shared memory, and
+// QK = Q_hi K + Q_lo K, PV = P_hi V + P_lo V.
+// Both: online softmax per query row in registers (exp2); P = p as fp16 plus
+// its fp16 remainder, taken straight from the S accumulators as the A operand
+// of the PV products.
 // Precision, from an fp64 emulation of each arithmetic against the oracle
 // (worst |error| / per-element bar): fp16 Q, K, P and V each rounded once
 // misses the bar on a few elements; with fp16 remainders on three of the four
 // operands 0.71-0.78 (still 1 miss in 2.1 M elements on the GPU), on all four
-// 0.003 (three f16 products per GEMM); this kernel's int8 QK with P and V
-// split 0.15-0.20.
+// 0.003 (three f16 products per GEMM); the int8 QK with P and V split
+// 0.15-0.20. The fp16-cache form has every operand exact or split.
 #include <cuda.h>
 
 #include <algorithm>
@@ -43,17 +53,37 @@ constexpr int kWarps = 4;
 constexpr int kQTile = 16 * kWarps;      // queries per CTA
 constexpr int kTTile = 64;               // tokens per tile
 constexpr int kStages = 2;
-constexpr int kRawRow = 144;             // raw smem row: 136 bytes of the head (+8 before or after)
-constexpr int kRawTile = kTTile * kRawRow;          // 9216 bytes
 constexpr int kHPitch = 272;             // fp16 tile row: 256 bytes + 16 (ldmatrix rows in distinct banks)
 constexpr int kHTile = kTTile * kHPitch;            // 17408 bytes
-constexpr int kOffRawV = kStages * kRawTile;
-constexpr int kOffVh = 2 * kStages * kRawTile;
-constexpr int kOffVl = kOffVh + kHTile;
-constexpr int kOffDk = kOffVl + kHTile;               // K block scales of the tile, fp32 [4 blocks][64 tokens]
-constexpr int kOffBar = kOffDk + 4 * kTTile * 4;
-constexpr int kSmem = kOffBar + kStages * 8 + 128;  // + base alignment slack
-static_assert(kRawTile % 128 == 0 && kOffVh % 128 == 0 && kHTile % 128 == 0, "aligned tiles");
+
+// Shared-memory plan of the block-quantised kernels: the raw K and V rings,
+// the dequantised V (high parts, remainders) and the K block scales.
+template <int KVF>
+struct RawFmt {
+  static constexpr int kBlk = KVF == KQ_KV_Q8_0 ? 34 : 18;  // bytes per 32-dim block
+  static constexpr int kUnits = 4 * kBlk / 8;                // the head's row in 8-byte units (17, 9)
+  static constexpr int kRawRow = 8 * (kUnits + 1);           // box row: 144, 80 bytes
+  static constexpr int kRawTile = kTTile * kRawRow;
+  static constexpr int kOffRawV = kStages * kRawTile;
+  static constexpr int kOffVh = 2 * kStages * kRawTile;
+  static constexpr int kOffVl = kOffVh + kHTile;
+  static constexpr int kOffDk = kOffVl + kHTile;             // K block scales, fp32 [4 blocks][64 tokens]
+  static constexpr int kOffBar = kOffDk + 4 * kTTile * 4;
+  static constexpr int kSmem = kOffBar + kStages * 8 + 128;  // + base alignment slack
+  static_assert(kRawTile % 128 == 0 && kOffVh % 128 == 0 && kHTile % 128 == 0, "aligned tiles");
+};
+
+// Shared-memory plan of the fp16-cache kernel: per stage K then V, each two
+// 64-token x 128-byte swizzled halves (dims 0-63, 64-127; 1024-byte aligned
+// for the 128-byte swizzle), then per warp the query's high parts and
+// remainders [2][16 rows][kHPitch].
+constexpr int kF16Half = kTTile * 128;               // 8192 bytes
+constexpr int kF16Tile = 2 * kF16Half;               // one operand tile
+constexpr int kF16Stage = 2 * kF16Tile;              // K and V
+constexpr int kF16OffQ = kStages * kF16Stage;
+constexpr int kF16QWarp = 2 * 16 * kHPitch;
+constexpr int kF16OffBar = kF16OffQ + kWarps * kF16QWarp;
+constexpr int kF16Smem = kF16OffBar + kStages * 8 + 1024;  // + base alignment slack
 
 struct BatchParams {
   const float* q;   // [B, H, 128]
@@ -90,6 +120,12 @@ __device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint
 
 __device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
   return (uint32_t)(a & 0xFF) | ((uint32_t)(b & 0xFF) << 8) | ((uint32_t)(c & 0xFF) << 16) | ((uint32_t)d << 24);
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t saddr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(saddr));
 }
 
 __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t saddr) {
@@ -129,34 +165,137 @@ __device__ __forceinline__ void codes_f16(uint32_t w, __half2& c01, __half2& c23
   c01 = __hsub2(*reinterpret_cast<const __half2*>(&lo), bias);
   c23 = __hsub2(*reinterpret_cast<const __half2*>(&hi), bias);
 }
+// Four nibbles (one per byte, 0-15) -> two f16x2 of q - 8, exactly: 1024 + q
+// under the exponent bits 0x64, minus 1032.
+__device__ __forceinline__ void nibbles_f16(uint32_t x, __half2& c01, __half2& c23) {
+  const uint32_t lo = __byte_perm(x, 0x64646464u, 0x4140), hi = __byte_perm(x, 0x64646464u, 0x4342);
+  const __half2 bias = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
+  c01 = __hsub2(*reinterpret_cast<const __half2*>(&lo), bias);
+  c23 = __hsub2(*reinterpret_cast<const __half2*>(&hi), bias);
+}
+// Four nibbles (one per byte) -> four int8 codes q - 8 (no borrow between
+// bytes: every byte is at least 0x80 before the subtraction)
+__device__ __forceinline__ uint32_t nibbles_s8(uint32_t x) {
+  return ((x | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
+}
 __device__ __forceinline__ uint32_t h2u(__half2 x) { return *reinterpret_cast<const uint32_t*>(&x); }
 
+// The high part of code * d rounded once to fp16 (mul.rn) and its remainder
+// (fma.rn of the exact product minus the high part), four elements.
+__device__ __forceinline__ void scale_split4(const __half2 (&e)[2], __half2 d2, uint2& hi, uint2& lo) {
+  const __half2 g0 = __hmul2(e[0], d2), g1 = __hmul2(e[1], d2);
+  hi = make_uint2(h2u(g0), h2u(g1));
+  lo = make_uint2(h2u(__hfma2(e[0], d2, __hneg2(g0))), h2u(__hfma2(e[1], d2, __hneg2(g1))));
+}
+
+// Online softmax over one 64-token tile for rows g (a) and g + 8 (b) of the
+// warp's 16 queries: masks tokens at or past S (tile starting at token tok0),
+// turns the scores into p = exp2(s - m), updates the running maxima and sums
+// and rescales the O accumulators.
+__device__ __forceinline__ void softmax_tile(float (&sc)[8][4], int tok0, int S, int t, float& m_a, float& m_b,
+                                             float& l_a, float& l_b, float (&o)[16][4]) {
+  if (tok0 + kTTile > S) {
+    const int tbase = tok0 + 2 * t;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (tbase + 8 * j >= S) sc[j][0] = sc[j][2] = -INFINITY;
+      if (tbase + 8 * j + 1 >= S) sc[j][1] = sc[j][3] = -INFINITY;
+    }
+  }
+  float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    mx_a = fmaxf(mx_a, fmaxf(sc[j][0], sc[j][1]));
+    mx_b = fmaxf(mx_b, fmaxf(sc[j][2], sc[j][3]));
+  }
+  mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+  mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+  mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+  mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+  const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+  const float ca = m_a == -INFINITY ? 0.0f : ex2(m_a - mn_a);
+  const float cb = m_b == -INFINITY ? 0.0f : ex2(m_b - mn_b);
+  m_a = mn_a;
+  m_b = mn_b;
+  float sa = 0.0f, sb = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    sc[j][0] = ex2(sc[j][0] - mn_a);
+    sc[j][1] = ex2(sc[j][1] - mn_a);
+    sc[j][2] = ex2(sc[j][2] - mn_b);
+    sc[j][3] = ex2(sc[j][3] - mn_b);
+    sa += sc[j][0] + sc[j][1];
+    sb += sc[j][2] + sc[j][3];
+  }
+  l_a = fmaf(l_a, ca, sa);
+  l_b = fmaf(l_b, cb, sb);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    o[j][0] *= ca;
+    o[j][1] *= ca;
+    o[j][2] *= cb;
+    o[j][3] *= cb;
+  }
+}
+
+// P of k-step kk (16 tokens) as the A operand of m16n8k16: high parts and
+// remainders, straight from the S accumulators
+__device__ __forceinline__ void p_operand(const float (&sc)[8][4], int kk, uint32_t (&ph)[4], uint32_t (&pl)[4]) {
+  split_half2(sc[2 * kk][0], sc[2 * kk][1], ph[0], pl[0]);
+  split_half2(sc[2 * kk][2], sc[2 * kk][3], ph[1], pl[1]);
+  split_half2(sc[2 * kk + 1][0], sc[2 * kk + 1][1], ph[2], pl[2]);
+  split_half2(sc[2 * kk + 1][2], sc[2 * kk + 1][3], ph[3], pl[3]);
+}
+
+// out = O / l for the warp's rows g and g + 8 (queries past B are not written)
+__device__ __forceinline__ void store_rows(const float (&o)[16][4], float l_a, float l_b, const BatchParams& p,
+                                           int q0, int g, int t, int h) {
+  l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
+  l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
+  l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
+  l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
+  const float ia = l_a > 0.0f ? 1.0f / l_a : 0.0f, ib = l_b > 0.0f ? 1.0f / l_b : 0.0f;
+  const int ra = q0 + g, rb = q0 + g + 8;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int c = 8 * j + 2 * t;
+    if (ra < p.B)
+      *reinterpret_cast<float2*>(p.out + ((size_t)ra * p.H + h) * 128 + c) = make_float2(o[j][0] * ia, o[j][1] * ia);
+    if (rb < p.B)
+      *reinterpret_cast<float2*>(p.out + ((size_t)rb * p.H + h) * 128 + c) = make_float2(o[j][2] * ib, o[j][3] * ib);
+  }
+}
+
+template <int KVF>
 __global__ void __launch_bounds__(32 * kWarps, 2)
     fa_batch_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                     BatchParams p) {
+  using F = RawFmt<KVF>;
+  constexpr int kBlk = F::kBlk, kRawRow = F::kRawRow, kRawTile = F::kRawTile;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~(uintptr_t)127);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + F::kOffBar);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int h = blockIdx.y;
   const int q0 = blockIdx.x * kQTile + warp * 16;  // this warp's first query
   const int ntiles = (p.S + kTTile - 1) / kTTile;
   const int xoff = (h & 1) * 8;                    // the head's first byte inside a raw row
-  const int bx = 17 * h - (h & 1);                 // box start in 8-byte units (16-byte aligned)
-  const uint32_t vh_s = smem_u32(smem + kOffVh), vl_s = smem_u32(smem + kOffVl);
-  float* dks = reinterpret_cast<float*>(smem + kOffDk);
+  const int bx = F::kUnits * h - (h & 1);          // box start in 8-byte units (16-byte aligned)
+  const uint32_t vh_s = smem_u32(smem + F::kOffVh), vl_s = smem_u32(smem + F::kOffVl);
+  float* dks = reinterpret_cast<float*>(smem + F::kOffDk);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
     fence_mbar_init();
   }
   __syncthreads();
+
   auto issue = [&](int i) {
     const int s = i % kStages;
     mbar_arrive_expect_tx(&full[s], 2 * kRawTile);
     tma_load_2d(smem + s * kRawTile, &kmap, bx, i * kTTile, &full[s]);
-    tma_load_2d(smem + kOffRawV + s * kRawTile, &vmap, bx, i * kTTile, &full[s]);
+    tma_load_2d(smem + F::kOffRawV + s * kRawTile, &vmap, bx, i * kTTile, &full[s]);
   };
   if (threadIdx.x == 0)
     for (int i = 0; i < min(kStages, ntiles); ++i) issue(i);
@@ -228,38 +367,51 @@ __global__ void __launch_bounds__(32 * kWarps, 2)
   for (int i = 0; i < ntiles; ++i) {
     const int s = i % kStages;
     mbar_wait_or_poison(&full[s], (i / kStages) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-    // ---- dequantise: thread = (token, pair of 32-dim blocks) ----
+    // ---- dequantise V and gather the K block scales: thread = (token, pair
+    // of 32-dim blocks) ----
     {
       const int tok = threadIdx.x >> 1, hb = threadIdx.x & 1;
       const uint8_t* rk = smem + s * kRawTile + tok * kRawRow + xoff;
-      const uint8_t* rv = smem + kOffRawV + s * kRawTile + tok * kRawRow + xoff;
-      uint8_t* dvh = smem + kOffVh + tok * kHPitch;
-      uint8_t* dvl = smem + kOffVl + tok * kHPitch;
+      const uint8_t* rv = smem + F::kOffRawV + s * kRawTile + tok * kRawRow + xoff;
+      uint8_t* dvh = smem + F::kOffVh + tok * kHPitch;
+      uint8_t* dvl = smem + F::kOffVl + tok * kHPitch;
 #pragma unroll
       for (int bi = 0; bi < 2; ++bi) {
         const int blk = 2 * hb + bi;
-        // V: code * d rounded once to fp16 (mul.rn) and its remainder (fma.rn
-        // of the exact product minus the high part): the bits of rounding the
-        // exact fp32 product, in fp16 arithmetic; K: its block scales only
-        dks[blk * kTTile + tok] = __half2float(*reinterpret_cast<const __half*>(rk + 34 * blk));
-        const __half sdv = *reinterpret_cast<const __half*>(rv + 34 * blk);
+        dks[blk * kTTile + tok] = __half2float(*reinterpret_cast<const __half*>(rk + kBlk * blk));
+        const __half sdv = *reinterpret_cast<const __half*>(rv + kBlk * blk);
         const __half2 dv2 = __halves2half2(sdv, sdv);
+        if constexpr (KVF == KQ_KV_Q8_0) {
 #pragma unroll
-        for (int pr = 0; pr < 4; ++pr) {  // 8 codes
-          const int co = 34 * blk + 2 + 8 * pr;
-          const uint32_t v0 = lds_u32_a2(rv + co), v1 = lds_u32_a2(rv + co + 4);
-          __half2 e[4];
-          codes_f16(v0, e[0], e[1]);
-          codes_f16(v1, e[2], e[3]);
-          __half2 g2[4];
+          for (int pr = 0; pr < 4; ++pr) {  // codes 8 pr .. 8 pr + 7
+            const int co = kBlk * blk + 2 + 8 * pr;
+            __half2 e0[2], e1[2];
+            codes_f16(lds_u32_a2(rv + co), e0[0], e0[1]);
+            codes_f16(lds_u32_a2(rv + co + 4), e1[0], e1[1]);
+            uint2 h0, l0, h1, l1;
+            scale_split4(e0, dv2, h0, l0);
+            scale_split4(e1, dv2, h1, l1);
+            const int d = (32 * blk + 8 * pr) * 2;
+            *reinterpret_cast<uint4*>(dvh + d) = make_uint4(h0.x, h0.y, h1.x, h1.y);
+            *reinterpret_cast<uint4*>(dvl + d) = make_uint4(l0.x, l0.y, l1.x, l1.y);
+          }
+        } else {
+          // q4_0: byte e of the 16 holds element e (low nibble) and e + 16
 #pragma unroll
-          for (int x = 0; x < 4; ++x) g2[x] = __hmul2(e[x], dv2);
-          const uint4 vv = make_uint4(h2u(g2[0]), h2u(g2[1]), h2u(g2[2]), h2u(g2[3]));
-          const uint4 vl = make_uint4(h2u(__hfma2(e[0], dv2, __hneg2(g2[0]))), h2u(__hfma2(e[1], dv2, __hneg2(g2[1]))),
-                                      h2u(__hfma2(e[2], dv2, __hneg2(g2[2]))), h2u(__hfma2(e[3], dv2, __hneg2(g2[3]))));
-          const int d = (32 * blk + 8 * pr) * 2;
-          *reinterpret_cast<uint4*>(dvh + d) = vv;
-          *reinterpret_cast<uint4*>(dvl + d) = vl;
+          for (int w = 0; w < 4; ++w) {
+            const uint32_t x = lds_u32_a2(rv + kBlk * blk + 2 + 4 * w);
+            __half2 e0[2], e1[2];
+            nibbles_f16(x & 0x0F0F0F0Fu, e0[0], e0[1]);
+            nibbles_f16((x >> 4) & 0x0F0F0F0Fu, e1[0], e1[1]);
+            uint2 h0, l0, h1, l1;
+            scale_split4(e0, dv2, h0, l0);
+            scale_split4(e1, dv2, h1, l1);
+            const int d0 = (32 * blk + 4 * w) * 2, d1 = d0 + 32;
+            *reinterpret_cast<uint2*>(dvh + d0) = h0;
+            *reinterpret_cast<uint2*>(dvl + d0) = l0;
+            *reinterpret_cast<uint2*>(dvh + d1) = h1;
+            *reinterpret_cast<uint2*>(dvl + d1) = l1;
+          }
         }
       }
     }
@@ -277,7 +429,15 @@ __global__ void __launch_bounds__(32 * kWarps, 2)
         const uint8_t* krow = kraw + (8 * j + g) * kRawRow;  // B column = token 8 j + g
 #pragma unroll
         for (int b = 0; b < 4; ++b) {
-          const uint32_t b0 = lds_u32_a2(krow + 34 * b), b1 = lds_u32_a2(krow + 34 * b + 16);
+          uint32_t b0, b1;
+          if constexpr (KVF == KQ_KV_Q8_0) {
+            b0 = lds_u32_a2(krow + kBlk * b);
+            b1 = lds_u32_a2(krow + kBlk * b + 16);
+          } else {  // dims 4t .. 4t + 3 are the low nibbles of bytes 4t .., dims 16 + 4t .. their high ones
+            const uint32_t x = lds_u32_a2(krow + kBlk * b);
+            b0 = nibbles_s8(x & 0x0F0F0F0Fu);
+            b1 = nibbles_s8((x >> 4) & 0x0F0F0F0Fu);
+          }
           int d1[4], d2[4];
           mma_s8(d1, qc[0][b], b0, b1);
           mma_s8(d2, qc[1][b], b0, b1);
@@ -297,58 +457,12 @@ __global__ void __launch_bounds__(32 * kWarps, 2)
     fence_proxy_async_smem();
     __syncthreads();
     if (threadIdx.x == 0 && i + kStages < ntiles) issue(i + kStages);
-    // tokens past the cache end (the last tile) weigh nothing
-    const int tbase = i * kTTile + 2 * t;
-    if (i * kTTile + kTTile > p.S) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (tbase + 8 * j >= p.S) sc[j][0] = sc[j][2] = -INFINITY;
-        if (tbase + 8 * j + 1 >= p.S) sc[j][1] = sc[j][3] = -INFINITY;
-      }
-    }
-    // ---- online softmax, rows g (a) and g + 8 (b) ----
-    float mx_a = -INFINITY, mx_b = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      mx_a = fmaxf(mx_a, fmaxf(sc[j][0], sc[j][1]));
-      mx_b = fmaxf(mx_b, fmaxf(sc[j][2], sc[j][3]));
-    }
-    mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
-    mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
-    mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
-    mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
-    const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
-    const float ca = m_a == -INFINITY ? 0.0f : ex2(m_a - mn_a);
-    const float cb = m_b == -INFINITY ? 0.0f : ex2(m_b - mn_b);
-    m_a = mn_a;
-    m_b = mn_b;
-    float sa = 0.0f, sb = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      sc[j][0] = ex2(sc[j][0] - mn_a);
-      sc[j][1] = ex2(sc[j][1] - mn_a);
-      sc[j][2] = ex2(sc[j][2] - mn_b);
-      sc[j][3] = ex2(sc[j][3] - mn_b);
-      sa += sc[j][0] + sc[j][1];
-      sb += sc[j][2] + sc[j][3];
-    }
-    l_a = fmaf(l_a, ca, sa);
-    l_b = fmaf(l_b, cb, sb);
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      o[j][0] *= ca;
-      o[j][1] *= ca;
-      o[j][2] *= cb;
-      o[j][3] *= cb;
-    }
-    // ---- O += P_hi V_hi + P_lo V_hi + P_hi V_lo: k-steps of 16 tokens, P from the S accumulators ----
+    softmax_tile(sc, i * kTTile, p.S, t, m_a, m_b, l_a, l_b, o);
+    // ---- O += P_hi V_hi + P_lo V_hi + P_hi V_lo: k-steps of 16 tokens ----
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
       uint32_t ph[4], pl[4];
-      split_half2(sc[2 * kk][0], sc[2 * kk][1], ph[0], pl[0]);
-      split_half2(sc[2 * kk][2], sc[2 * kk][3], ph[1], pl[1]);
-      split_half2(sc[2 * kk + 1][0], sc[2 * kk + 1][1], ph[2], pl[2]);
-      split_half2(sc[2 * kk + 1][2], sc[2 * kk + 1][3], ph[3], pl[3]);
+      p_operand(sc, kk, ph, pl);
 #pragma unroll
       for (int np = 0; np < 8; ++np) {
         uint32_t vb[4], vr[4];
@@ -365,58 +479,181 @@ __global__ void __launch_bounds__(32 * kWarps, 2)
     }
     __syncthreads();  // the V tiles and K scales are rewritten by the next tile
   }
-
-  // ---- out = O / l ----
-  l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
-  l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
-  l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
-  l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
-  const float ia = l_a > 0.0f ? 1.0f / l_a : 0.0f, ib = l_b > 0.0f ? 1.0f / l_b : 0.0f;
-  const int ra = q0 + g, rb = q0 + g + 8;
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const int c = 8 * j + 2 * t;
-    if (ra < p.B)
-      *reinterpret_cast<float2*>(p.out + ((size_t)ra * p.H + h) * 128 + c) = make_float2(o[j][0] * ia, o[j][1] * ia);
-    if (rb < p.B)
-      *reinterpret_cast<float2*>(p.out + ((size_t)rb * p.H + h) * 128 + c) = make_float2(o[j][2] * ib, o[j][3] * ib);
-  }
+  store_rows(o, l_a, l_b, p, q0, g, t, h);
 }
 
-bool encode_raw_map(CUtensorMap* map, const void* base, uint64_t rows, int heads) {
-  // [rows][heads * 136 bytes] as 8-byte elements; boxes of 64 rows x 18
-  // elements (one head's 136 bytes plus 8 before or after, so every box
+__global__ void __launch_bounds__(32 * kWarps, 2)
+    fa_batch_f16_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                        BatchParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kF16OffBar);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int h = blockIdx.y;
+  const int q0 = blockIdx.x * kQTile + warp * 16;  // this warp's first query
+  const int ntiles = (p.S + kTTile - 1) / kTTile;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  auto issue = [&](int i) {
+    const int s = i % kStages;
+    uint8_t* st = smem + s * kF16Stage;
+    mbar_arrive_expect_tx(&full[s], kF16Stage);
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      tma_load_2d(st + hf * kF16Half, &kmap, 128 * h + 64 * hf, i * kTTile, &full[s]);
+      tma_load_2d(st + kF16Tile + hf * kF16Half, &vmap, 128 * h + 64 * hf, i * kTTile, &full[s]);
+    }
+  };
+  if (threadIdx.x == 0)
+    for (int i = 0; i < min(kStages, ntiles); ++i) issue(i);
+
+  // ---- the warp's 16 queries * scale * log2(e): fp16 high parts (rows 0-15)
+  // and remainders (rows 16-31); lane = 4 dims of each row ----
+  uint8_t* qsm = smem + kF16OffQ + warp * kF16QWarp;
+#pragma unroll 4
+  for (int r = 0; r < 16; ++r) {
+    const int row = q0 + r;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (row < p.B) x = *reinterpret_cast<const float4*>(p.q + ((size_t)row * p.H + h) * 128 + 4 * lane);
+    uint32_t h0, l0, h1, l1;
+    split_half2(x.x * p.qscale, x.y * p.qscale, h0, l0);
+    split_half2(x.z * p.qscale, x.w * p.qscale, h1, l1);
+    *reinterpret_cast<uint2*>(qsm + r * kHPitch + 8 * lane) = make_uint2(h0, h1);
+    *reinterpret_cast<uint2*>(qsm + (16 + r) * kHPitch + 8 * lane) = make_uint2(l0, l1);
+  }
+  __syncwarp();
+
+  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.0f, l_b = 0.0f;  // rows g and g + 8
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+  bool dead = false;
+  // ldmatrix row addresses: matrix mi = lane / 8, row r8 = lane % 8. In the
+  // swizzled K / V halves, 16-byte chunk c of token row r sits at chunk
+  // c ^ (r % 8), and r % 8 = r8 for every row a lane addresses.
+  const int mi = lane >> 3, r8 = lane & 7;
+  const uint32_t q_s = smem_u32(qsm) + (uint32_t)(((mi & 1) * 8 + r8) * kHPitch + (mi >> 1) * 16);
+
+  for (int i = 0; i < ntiles; ++i) {
+    const int s = i % kStages;
+    mbar_wait_or_poison(&full[s], (i / kStages) & 1, p.err, DEV_TIMEOUT_FULL, dead);
+    const uint32_t k_s = smem_u32(smem + s * kF16Stage), v_s = k_s + kF16Tile;
+
+    // ---- S = Q_hi K + Q_lo K: k-steps of 16 dims; B = K rows (tokens) ----
+    float sc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      uint32_t qh[4], ql[4];
+      ldsm_x4(qh, q_s + 32 * ks);
+      ldsm_x4(ql, q_s + 16 * kHPitch + 32 * ks);
+      const uint32_t kc = (uint32_t)(((((2 * ks) & 7) + (mi & 1)) ^ r8) << 4);
+      const uint32_t kbase = k_s + (uint32_t)((ks >> 2) * kF16Half) + kc;
+#pragma unroll
+      for (int jp = 0; jp < 4; ++jp) {  // tokens 16 jp .. + 15
+        uint32_t kb[4];
+        ldsm_x4(kb, kbase + (uint32_t)((16 * jp + (mi >> 1) * 8 + r8) * 128));
+        mma_f16(sc[2 * jp], qh[0], qh[1], qh[2], qh[3], kb[0], kb[1]);
+        mma_f16(sc[2 * jp], ql[0], ql[1], ql[2], ql[3], kb[0], kb[1]);
+        mma_f16(sc[2 * jp + 1], qh[0], qh[1], qh[2], qh[3], kb[2], kb[3]);
+        mma_f16(sc[2 * jp + 1], ql[0], ql[1], ql[2], ql[3], kb[2], kb[3]);
+      }
+    }
+    softmax_tile(sc, i * kTTile, p.S, t, m_a, m_b, l_a, l_b, o);
+    // ---- O += P_hi V + P_lo V: k-steps of 16 tokens, V by ldmatrix.trans ----
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t ph[4], pl[4];
+      p_operand(sc, kk, ph, pl);
+      const uint32_t vrow = v_s + (uint32_t)((16 * kk + (mi & 1) * 8 + r8) * 128);
+#pragma unroll
+      for (int np = 0; np < 8; ++np) {  // dims 16 np .. + 15
+        const uint32_t vc = (uint32_t)(((((2 * np) & 7) + (mi >> 1)) ^ r8) << 4);
+        uint32_t vb[4];
+        ldsm_x4_trans(vb, vrow + (uint32_t)((np >> 2) * kF16Half) + vc);
+        mma_f16(o[2 * np], ph[0], ph[1], ph[2], ph[3], vb[0], vb[1]);
+        mma_f16(o[2 * np + 1], ph[0], ph[1], ph[2], ph[3], vb[2], vb[3]);
+        mma_f16(o[2 * np], pl[0], pl[1], pl[2], pl[3], vb[0], vb[1]);
+        mma_f16(o[2 * np + 1], pl[0], pl[1], pl[2], pl[3], vb[2], vb[3]);
+      }
+    }
+    // the stage is no longer read: refill it once every warp is past PV
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (threadIdx.x == 0 && i + kStages < ntiles) issue(i + kStages);
+  }
+  store_rows(o, l_a, l_b, p, q0, g, t, h);
+}
+
+bool encode_raw_map(CUtensorMap* map, const void* base, uint64_t rows, int heads, int units) {
+  // [rows][heads * units 8-byte elements]; boxes of 64 rows x (units + 1)
+  // elements (one head's row plus 8 bytes before or after, so every box
   // starts on a 16-byte boundary; past the last row the fill is zero)
   auto fn = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
   if (!fn) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)heads * 17, rows};
-  cuuint64_t strides[1] = {(cuuint64_t)heads * 136};
-  cuuint32_t box[2] = {kRawRow / 8, kTTile};
+  cuuint64_t dims[2] = {(cuuint64_t)heads * units, rows};
+  cuuint64_t strides[1] = {(cuuint64_t)heads * units * 8};
+  cuuint32_t box[2] = {(cuuint32_t)units + 1, kTTile};
   cuuint32_t estr[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool encode_f16_map(CUtensorMap* map, const void* base, uint64_t rows, int heads) {
+  // [rows][heads * 128] fp16; boxes of 64 rows x 64 elements (128 bytes)
+  // with the 128-byte swizzle (past the last row the fill is zero)
+  auto fn = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)heads * 128, rows};
+  cuuint64_t strides[1] = {(cuuint64_t)heads * 256};
+  cuuint32_t box[2] = {64, kTTile};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int KVF>
+kq_status_t launch_raw(const CUtensorMap& km, const CUtensorMap& vm, const BatchParams& p, dim3 grid, cudaStream_t s) {
+  kq_status_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(fa_batch_kernel<KVF>), RawFmt<KVF>::kSmem,
+                                       "fa_batch smem attribute");
+  if (st) return st;
+  fa_batch_kernel<KVF><<<grid, 32 * kWarps, RawFmt<KVF>::kSmem, s>>>(km, vm, p);
+  return check_launch("fa_batch");
+}
+
 }  // namespace
 
-bool fa_batch_supported(const void* q, const void* k, const void* v, const void* out, int B, int S, int H, int D) {
+bool fa_batch_supported(int kv_format, const void* q, const void* k, const void* v, const void* out, int B, int S,
+                        int H, int D) {
   auto al = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
-  // an even head count keeps every head's 16-byte aligned box inside the rows;
-  // enough (query tile, head) CTAs to fill the GPU without splitting the cache
-  return D == 128 && H >= 2 && H % 2 == 0 && S >= 1 && al(q) && al(k) && al(v) && al(out) &&
+  // block-quantised caches: an even head count keeps every head's 16-byte
+  // aligned box inside the rows; enough (query tile, head) CTAs to fill the
+  // GPU without splitting the cache
+  const bool heads = kv_format == KQ_KV_F16 ? H >= 1
+                                            : (kv_format == KQ_KV_Q8_0 || kv_format == KQ_KV_Q4_0) && H >= 2 &&
+                                                  H % 2 == 0;
+  return heads && D == 128 && S >= 1 && al(q) && al(k) && al(v) && al(out) &&
          (long long)((B + kQTile - 1) / kQTile) * H >= sm_count() && (B + kQTile - 1) / kQTile <= 65535 &&
          H <= 65535;
 }
 
-kq_status_t launch_fa_batch_mha(const float* q, const void* k, const void* v, float* out, int B, int S, int H,
-                                cudaStream_t s) {
+kq_status_t launch_fa_batch_mha(int kv_format, const float* q, const void* k, const void* v, float* out, int B,
+                                int S, int H, cudaStream_t s) {
   CUtensorMap km, vm;
-  if (!encode_raw_map(&km, k, (uint64_t)S, H) || !encode_raw_map(&vm, v, (uint64_t)S, H))
-    return fail(KQ_ERR_CUDA, "fa_batch: KV tensor map rejected");
-  kq_status_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(fa_batch_kernel), kSmem,
-                                       "fa_batch smem attribute");
-  if (st) return st;
+  const bool ok = kv_format == KQ_KV_F16
+                      ? encode_f16_map(&km, k, (uint64_t)S, H) && encode_f16_map(&vm, v, (uint64_t)S, H)
+                      : encode_raw_map(&km, k, (uint64_t)S, H, kv_format == KQ_KV_Q8_0 ? 17 : 9) &&
+                            encode_raw_map(&vm, v, (uint64_t)S, H, kv_format == KQ_KV_Q8_0 ? 17 : 9);
+  if (!ok) return fail(KQ_ERR_CUDA, "fa_batch: KV tensor map rejected");
   BatchParams p;
   p.q = q;
   p.out = out;
@@ -426,8 +663,18 @@ kq_status_t launch_fa_batch_mha(const float* q, const void* k, const void* v, fl
   p.S = S;
   p.qscale = (float)(1.0 / std::sqrt(128.0) * 1.4426950408889634);
   dim3 grid((unsigned)((B + kQTile - 1) / kQTile), (unsigned)H);
-  fa_batch_kernel<<<grid, 32 * kWarps, kSmem, s>>>(km, vm, p);
-  return check_launch("fa_batch");
+  switch (kv_format) {
+    case KQ_KV_Q8_0: return launch_raw<KQ_KV_Q8_0>(km, vm, p, grid, s);
+    case KQ_KV_Q4_0: return launch_raw<KQ_KV_Q4_0>(km, vm, p, grid, s);
+    case KQ_KV_F16: {
+      kq_status_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(fa_batch_f16_kernel), kF16Smem,
+                                           "fa_batch smem attribute");
+      if (st) return st;
+      fa_batch_f16_kernel<<<grid, 32 * kWarps, kF16Smem, s>>>(km, vm, p);
+      return check_launch("fa_batch(f16)");
+    }
+    default: return fail(KQ_ERR_INVALID, "fa_batch: unknown KV format %d", kv_format);
+  }
 }
 
 }  // namespace kq

@@ -181,12 +181,14 @@ kq_status_t launch_fa_small_mha(const float* q, const void* k, const void* v, fl
                                 cudaStream_t s);
 kq_status_t launch_fa_small_ragged(const void* q, const void* k, const void* v, const int32_t* cu, int B, int Hq,
                                    int Hkv, int max_seqlen, int total_rows, float scale, void* out, cudaStream_t s);
-// fa_batch.cu: the harness form with many queries per head (q8_0, D = 128,
-// an even head count, ceil(B / 64) * H >= SMs): fp16 tensor-core flash
-// attention over the dequantised cache, 64 queries per CTA
-bool fa_batch_supported(const void* q, const void* k, const void* v, const void* out, int B, int S, int H, int D);
-kq_status_t launch_fa_batch_mha(const float* q, const void* k, const void* v, float* out, int B, int S, int H,
-                                cudaStream_t s);
+// fa_batch.cu: the harness form with many queries per head (q8_0, q4_0 or
+// fp16 caches, D = 128, an even head count for the block formats,
+// ceil(B / 64) * H >= SMs, 16-byte aligned q, k, v and out): tensor-core
+// flash attention, 64 queries per CTA
+bool fa_batch_supported(int kv_format, const void* q, const void* k, const void* v, const void* out, int B, int S,
+                        int H, int D);
+kq_status_t launch_fa_batch_mha(int kv_format, const float* q, const void* k, const void* v, float* out, int B,
+                                int S, int H, cudaStream_t s);
 kq_status_t launch_fa_ragged(const void* q, const void* k, const void* v, const int32_t* cu, int B, int Hq, int Hkv,
                              int D, int max_seqlen, int total_rows, float scale, void* out, cudaStream_t s);
 

@@ -345,6 +345,30 @@ def test_batch_mha(cuda, B, S, H):
     assert kq.device_error() == 0
 
 
+@pytest.mark.parametrize("fmt", ["q4_0", "f16"])
+@pytest.mark.parametrize("B,S,H", [(512, 64, 32), (300, 65, 32), (512, 1, 32), (1024, 100, 24), (512, 777, 28),
+                                   (320, 2048, 32), (1920, 129, 5)])
+def test_batch_mha_kv_formats(cuda, fmt, B, S, H):
+    """Harness batches over q4_0 and fp16 caches run the batch kernel too
+    (fa_batch.cu): q4_0 through the exact int8 QK on the nibble codes and the
+    split V, fp16 with the split query over the cache read in place. Partial
+    query tiles, lengths around the 64-token tile, a one-token cache, and for
+    fp16 an odd head count (H = 5; the block formats need an even one)."""
+    import kq
+    if fmt == "q4_0" and H % 2:
+        pytest.skip("block-quantised caches take the batch kernel with an even head count only")
+    rng = np.random.default_rng(B + S + H + len(fmt))
+    D = 128
+    q = rng.standard_normal((B, H, D)).astype(np.float32)
+    k = _cache(fmt, rng.standard_normal((S, H, D)).astype(np.float32), D)
+    v = _cache(fmt, rng.standard_normal((S, H, D)).astype(np.float32), D)
+    got = kq.flash_attn(_t(q, cuda), _t(k, cuda), _t(v, cuda), B, S, H, D, fmt).cpu().numpy()
+    ref = Q.flash_decode_mha(q, k, v, S, H, D, fmt)
+    ok, msg = Q.check_close(got, ref)
+    assert ok, msg
+    assert kq.device_error() == 0
+
+
 @pytest.mark.parametrize("lens,Hq,Hkv", [([8192], 32, 8), ([64] * 32 + [4096] * 8, 32, 8)])
 def test_decode_after_producer(cuda, lens, Hq, Hkv):
     """The decode kernels are programmatic dependents of whatever precedes
