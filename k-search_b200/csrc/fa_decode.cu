@@ -622,10 +622,11 @@ bool encode_kv_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t h
                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Decode kernel family for q8_0 caches in the TMA-able shapes, read once per
-// process from KQ_FA_PATH: the tensor-pipe streaming kernel (fa_stream.cu) by
-// default; "tma" = the TMA CUDA-core kernel; "generic" = the split-KV kernel
-// every other shape uses.
+// Decode kernel family, read once per process from KQ_FA_PATH: by default
+// the tensor-pipe kernels (fa_stream.cu, fa_small.cu, fa_batch.cu) where
+// their shapes allow; "tma" = the TMA CUDA-core kernel for q8_0 caches in the
+// TMA-able shapes; "generic" = the split-KV kernel every other shape uses,
+// for every shape and cache format.
 enum class FaPath { kStream, kTma, kGeneric };
 FaPath fa_path() {
   static const FaPath p = [] {
