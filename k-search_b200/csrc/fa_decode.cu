@@ -737,15 +737,19 @@ kq_status_t launch_fa_mha(int kvf, const float* q, const void* k, const void* v,
     // the small-batch kernel also takes what neither other kernel does (head
     // counts not in groups of 8): the generic kernel is ~3x slower there
     if ((small_batch(tiles, std::min(B, 4)) || (!batch && !stream)) &&
-        fa_small_supported(q, k, v, out, D, H, std::min(B, 4)))
-      return launch_fa_small_mha(q, k, v, out, B, S, H, s);
+        fa_small_supported(KQ_KV_Q8_0, q, k, v, out, D, H, std::min(B, 4)))
+      return launch_fa_small_mha(KQ_KV_Q8_0, q, k, v, out, B, S, H, s);
     if (batch) return launch_fa_batch_mha(KQ_KV_Q8_0, q, k, v, out, B, S, H, s);
     if (stream) return launch_fa_stream_mha(q, k, v, out, B, S, H, s);
   }
-  // q4_0 / fp16 caches: the tensor-core batch kernel when its CTAs fill the GPU
-  if (kvf != KQ_KV_Q8_0 && fa_path() == FaPath::kStream && S > 0 &&
-      fa_batch_supported(kvf, q, k, v, out, B, S, H, D))
-    return launch_fa_batch_mha(kvf, q, k, v, out, B, S, H, s);
+  // q4_0 / fp16 caches: the tensor-core batch kernel when its CTAs fill the
+  // GPU, else the small-batch kernel (each K / V tile read once for up to 4
+  // queries; the generic kernel reads it once per query)
+  if (kvf != KQ_KV_Q8_0 && fa_path() == FaPath::kStream && S > 0) {
+    if (fa_batch_supported(kvf, q, k, v, out, B, S, H, D)) return launch_fa_batch_mha(kvf, q, k, v, out, B, S, H, s);
+    if (fa_small_supported(kvf, q, k, v, out, D, H, std::min(B, 4)))
+      return launch_fa_small_mha(kvf, q, k, v, out, B, S, H, s);
+  }
   const bool fast = kvf == KQ_KV_Q8_0 && fast_ok(k, v, D, H, 1) && S > 0 &&
                     (long long)((B + kG - 1) / kG) * (H / kHpc) <= 65535;
   int chunk = 0;
@@ -790,7 +794,7 @@ kq_status_t launch_fa_ragged(const void* q, const void* k, const void* v, const 
   if (fa_path() == FaPath::kStream) {
     const long long tiles = (long long)B * std::max(1, Hkv / 8) * ((std::max(max_seqlen, 1) + 15) / 16);
     const bool stream = fa_stream_supported(q, k, v, out, D, Hkv, g, B);
-    if ((small_batch(tiles, g) || !stream) && fa_small_supported(q, k, v, out, D, Hkv, g))
+    if ((small_batch(tiles, g) || !stream) && fa_small_supported(KQ_KV_Q8_0, q, k, v, out, D, Hkv, g))
       return launch_fa_small_ragged(q, k, v, cu, B, Hq, Hkv, max_seqlen, total_rows, scale, out, s);
     if (stream) return launch_fa_stream_ragged(q, k, v, cu, B, Hq, Hkv, total_rows, scale, out, s);
   }

@@ -46,15 +46,27 @@ constexpr int kTok = 16;                  // tokens per tile
 constexpr int kWarps = 4;                 // warps per CTA (independent tasks)
 constexpr int kStages = 2;                // TMA ring depth per warp
 constexpr int kQ = 4;                     // queries per unit (at most)
-constexpr int kRow = 144;                 // smem row: 136 bytes of the head (+8 before or after)
-constexpr int kTile = kTok * kRow;        // 2304 bytes per K (or V) tile
-// per warp: K and V rings, query codes [4 queries][2 levels][128], barriers
-constexpr int kOffV = kStages * kTile;
-constexpr int kOffQ = 2 * kStages * kTile;
-constexpr int kOffBar = kOffQ + kQ * 2 * 128;
-constexpr int kWarpSmem = (kOffBar + kStages * 8 + 127) / 128 * 128;
-constexpr int kSmem = kWarps * kWarpSmem + 128;  // + base alignment slack
-static_assert(kTile % 128 == 0 && kWarpSmem % 128 == 0, "TMA destinations stay 128-byte aligned");
+
+// Per-warp shared memory by cache format: K and V rings, the queries (int8
+// codes [4 queries][2 levels][128] for the block formats, fp32 [4][128] for
+// fp16), barriers. Block formats: a smem row is the head's 136- (q8_0) or
+// 72-byte (q4_0) row plus 8 bytes before or after it. fp16: a row is the
+// head's 256 bytes as two 128-byte halves, each half tile (16 rows) stored
+// with the 128-byte swizzle (1024-byte aligned).
+template <int KVF>
+struct SmallFmt {
+  static constexpr int kBlk = KVF == KQ_KV_Q8_0 ? 34 : 18;     // block formats: bytes per 32 dims
+  static constexpr int kUnits = 4 * kBlk / 8;                   // the head's row in 8-byte units (17, 9)
+  static constexpr int kRow = KVF == KQ_KV_F16 ? 256 : 8 * (kUnits + 1);
+  static constexpr int kTile = kTok * kRow;                     // 2304, 1280, 4096 bytes
+  static constexpr int kOffV = kStages * kTile;
+  static constexpr int kOffQ = 2 * kStages * kTile;
+  static constexpr int kOffBar = kOffQ + (KVF == KQ_KV_F16 ? kQ * 128 * 4 : kQ * 2 * 128);
+  static constexpr int kAlign = KVF == KQ_KV_F16 ? 1024 : 128;
+  static constexpr int kWarpSmem = (kOffBar + kStages * 8 + kAlign - 1) / kAlign * kAlign;
+  static constexpr int kSmem = kWarps * kWarpSmem + kAlign;    // + base alignment slack
+  static_assert(kTile % kAlign == 0 && kWarpSmem % kAlign == 0, "TMA destinations stay aligned");
+};
 
 struct SmallParams {
   const void* q;          // ragged: fp16 [B, Hq, 128]; MHA: fp32 [B, H, 128]
@@ -106,6 +118,12 @@ __device__ __forceinline__ float4 load_q4(const __half* q, size_t i) {
   return make_float4(a.x, a.y, b.x, b.y);
 }
 
+// Four nibbles (one per byte) -> four int8 codes q - 8 (no borrow between
+// bytes: every byte is at least 0x80 before the subtraction)
+__device__ __forceinline__ uint32_t nibbles_s8(uint32_t x) {
+  return ((x | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
+}
+
 __device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
   return (uint32_t)(a & 0xFF) | ((uint32_t)(b & 0xFF) << 8) | ((uint32_t)(c & 0xFF) << 16) | ((uint32_t)d << 24);
 }
@@ -133,16 +151,20 @@ __device__ __forceinline__ size_t query_index(const SmallParams& p, int grp, int
   return (size_t)(grp * kQ + j) * p.H + hk;
 }
 
-template <typename QT, bool RAGGED, int NQ>
+template <typename QT, bool RAGGED, int NQ, int KVF>
 __global__ void __launch_bounds__(32 * kWarps)
     fa_small_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                     SmallParams p) {
+  using F = SmallFmt<KVF>;
+  constexpr int kRow = F::kRow, kTile = F::kTile, kBlk = F::kBlk;
   extern __shared__ uint8_t smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint8_t* ws = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~(uintptr_t)127) +
-                warp * kWarpSmem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(ws + kOffBar);
-  int8_t* qc = reinterpret_cast<int8_t*>(ws + kOffQ);  // [query][level][128]
+  uint8_t* cta = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + F::kAlign - 1) &
+                                            ~(uintptr_t)(F::kAlign - 1));
+  uint8_t* ws = cta + warp * F::kWarpSmem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ws + F::kOffBar);
+  int8_t* qc = reinterpret_cast<int8_t*>(ws + F::kOffQ);   // block formats: [query][level][128]
+  float* qf = reinterpret_cast<float*>(ws + F::kOffQ);     // fp16: [query][128]
   // launched as a programmatic dependent: no global read before the
   // preceding kernel (the previous call's merge, or the queries' producer) ends
   pdl_wait();
@@ -156,8 +178,8 @@ __global__ void __launch_bounds__(32 * kWarps)
   unit_of<RAGGED>(p, u, grp, hk, row0, len, nq);
   const int t0 = c * p.chunk, t1 = min(len, t0 + p.chunk);
   const int ntiles = t1 > t0 ? (t1 - t0 + kTok - 1) / kTok : 0;
-  const int xoff = (hk & 1) * 8;         // the head's first byte inside the smem row
-  const int bx = 17 * hk - (hk & 1);     // box start in 8-byte units (16-byte aligned)
+  const int xoff = KVF == KQ_KV_F16 ? 0 : (hk & 1) * 8;  // block formats: the head's first byte in a row
+  const int bx = F::kUnits * hk - (hk & 1);              // block formats: box start in 8-byte units
 
   if (lane == 0) {
     for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
@@ -166,14 +188,24 @@ __global__ void __launch_bounds__(32 * kWarps)
   __syncwarp();
   auto issue = [&](int i) {
     const int s = i % kStages;
+    const int y = row0 + t0 + i * kTok;
     mbar_arrive_expect_tx(&full[s], 2 * kTile);
-    tma_load_2d(ws + s * kTile, &kmap, bx, row0 + t0 + i * kTok, &full[s]);
-    tma_load_2d(ws + kOffV + s * kTile, &vmap, bx, row0 + t0 + i * kTok, &full[s]);
+    if constexpr (KVF == KQ_KV_F16) {
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        tma_load_2d(ws + s * kTile + hf * (kTile / 2), &kmap, 128 * hk + 64 * hf, y, &full[s]);
+        tma_load_2d(ws + F::kOffV + s * kTile + hf * (kTile / 2), &vmap, 128 * hk + 64 * hf, y, &full[s]);
+      }
+    } else {
+      tma_load_2d(ws + s * kTile, &kmap, bx, y, &full[s]);
+      tma_load_2d(ws + F::kOffV + s * kTile, &vmap, bx, y, &full[s]);
+    }
   };
   if (lane == 0)
     for (int i = 0; i < min(kStages, ntiles); ++i) issue(i);
 
-  // ---- queries as two int8 levels (lane = dims 4 lane .. 4 lane + 3) ----
+  // ---- queries (lane = dims 4 lane .. 4 lane + 3): fp32 for fp16 caches,
+  // else two int8 levels ----
   float s2[NQ];  // level-2 scale of each query: score = s2 * sum_b d_k (127 dot1 + dot2)
 #pragma unroll
   for (int j = 0; j < NQ; ++j) {
@@ -183,19 +215,24 @@ __global__ void __launch_bounds__(32 * kWarps)
       const float4 t = load_q4(qp, 4 * lane);
       v[0] = t.x * p.qscale; v[1] = t.y * p.qscale; v[2] = t.z * p.qscale; v[3] = t.w * p.qscale;
     }
-    const float a = warp_max(fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3]))));
-    const float s1 = a > 0.0f ? a / 127.0f : 1.0f;
-    const float inv1 = a > 0.0f ? 127.0f / a : 0.0f;
-    const float inv2 = 127.0f * inv1;
-    int c1[4], c2[4];
+    if constexpr (KVF == KQ_KV_F16) {
+      reinterpret_cast<float4*>(qf + j * 128)[lane] = make_float4(v[0], v[1], v[2], v[3]);
+      s2[j] = 1.0f;
+    } else {
+      const float a = warp_max(fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3]))));
+      const float s1 = a > 0.0f ? a / 127.0f : 1.0f;
+      const float inv1 = a > 0.0f ? 127.0f / a : 0.0f;
+      const float inv2 = 127.0f * inv1;
+      int c1[4], c2[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      c1[i] = max(-127, min(127, __float2int_rn(v[i] * inv1)));
-      c2[i] = max(-127, min(127, __float2int_rn(fmaf(-s1, (float)c1[i], v[i]) * inv2)));
+      for (int i = 0; i < 4; ++i) {
+        c1[i] = max(-127, min(127, __float2int_rn(v[i] * inv1)));
+        c2[i] = max(-127, min(127, __float2int_rn(fmaf(-s1, (float)c1[i], v[i]) * inv2)));
+      }
+      reinterpret_cast<uint32_t*>(qc + (j * 2) * 128)[lane] = pack_s8x4(c1[0], c1[1], c1[2], c1[3]);
+      reinterpret_cast<uint32_t*>(qc + (j * 2 + 1) * 128)[lane] = pack_s8x4(c2[0], c2[1], c2[2], c2[3]);
+      s2[j] = s1 * (1.0f / 127.0f);
     }
-    reinterpret_cast<uint32_t*>(qc + (j * 2) * 128)[lane] = pack_s8x4(c1[0], c1[1], c1[2], c1[3]);
-    reinterpret_cast<uint32_t*>(qc + (j * 2 + 1) * 128)[lane] = pack_s8x4(c2[0], c2[1], c2[2], c2[3]);
-    s2[j] = s1 * (1.0f / 127.0f);
   }
   __syncwarp();
 
@@ -206,9 +243,16 @@ __global__ void __launch_bounds__(32 * kWarps)
     l_run[j] = 0.0f;
     acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
   }
-  const int tq = lane & 15, half = lane >> 4;  // QK: token, block pair {2 half, 2 half + 1}
+  const int tq = lane & 15, half = lane >> 4;  // QK: token, block pair {2 half, 2 half + 1} (dims 64 half ..)
   const int vb = lane >> 3;                     // PV: block of this lane's 4 dims
-  const int voff = xoff + vb * 34 + 2 + 4 * (lane & 7);
+  // PV: this lane's 4 codes. q8_0: bytes 4 (lane % 8) .. of block vb; q4_0:
+  // element e = 4 (lane % 8) of the block is the low nibble of byte e for
+  // e < 16, else the high nibble of byte e - 16; fp16: bytes 8 lane .. of
+  // the row, in half lane / 16 at swizzled chunk ((lane % 16) / 2) ^ (row % 8)
+  const int voff = KVF == KQ_KV_Q8_0   ? xoff + vb * kBlk + 2 + 4 * (lane & 7)
+                   : KVF == KQ_KV_Q4_0 ? xoff + vb * kBlk + 2 + 4 * (lane & 3)
+                                       : (lane >> 4) * (kTile / 2) + 8 * (lane & 1);
+  const int vshift = (lane & 4) ? 4 : 0;        // q4_0: high nibbles for elements 16-31
   bool dead = false;
 
   for (int i = 0; i < ntiles; ++i) {
@@ -216,46 +260,77 @@ __global__ void __launch_bounds__(32 * kWarps)
     const int nvalid = min(kTok, t1 - (t0 + i * kTok));
     mbar_wait_or_poison(&full[s], (i / kStages) & 1, p.err, DEV_TIMEOUT_FULL, dead);
     const uint8_t* kt = ws + s * kTile;
-    const uint8_t* vt = ws + kOffV + s * kTile;
+    const uint8_t* vt = ws + F::kOffV + s * kTile;
 
     // ---- QK: token tq, blocks 2 half and 2 half + 1 ----
     float sc[NQ];
     {
-      const uint8_t* row = kt + tq * kRow + xoff;
-      int d1[NQ], d2[NQ];
       float part[NQ];
 #pragma unroll
       for (int j = 0; j < NQ; ++j) part[j] = 0.0f;
+      if constexpr (KVF == KQ_KV_F16) {
+        // dims 64 half .. + 63: the row's half `half`, 16-byte chunk c at c ^ (tq % 8)
+        const uint8_t* row = kt + half * (kTile / 2) + tq * 128;
 #pragma unroll
-      for (int bi = 0; bi < 2; ++bi) {
-        const int blk = 2 * half + bi;
-        const uint8_t* b = row + 34 * blk;
-        const float dk = lds_half(b);
-        uint32_t kw[8];
+        for (int cc = 0; cc < 8; ++cc) {
+          const uint4 kw = *reinterpret_cast<const uint4*>(row + ((cc ^ (tq & 7)) << 4));
+          const float2 k0 = __half22float2(*reinterpret_cast<const __half2*>(&kw.x));
+          const float2 k1 = __half22float2(*reinterpret_cast<const __half2*>(&kw.y));
+          const float2 k2 = __half22float2(*reinterpret_cast<const __half2*>(&kw.z));
+          const float2 k3 = __half22float2(*reinterpret_cast<const __half2*>(&kw.w));
 #pragma unroll
-        for (int w = 0; w < 8; ++w) kw[w] = lds_u32_a2(b + 2 + 4 * w);
+          for (int j = 0; j < NQ; ++j) {
+            const float4* qv = reinterpret_cast<const float4*>(qf + j * 128 + 64 * half + 8 * cc);
+            const float4 a = qv[0], b = qv[1];
+            float x = part[j];
+            x = fmaf(a.x, k0.x, x); x = fmaf(a.y, k0.y, x); x = fmaf(a.z, k1.x, x); x = fmaf(a.w, k1.y, x);
+            x = fmaf(b.x, k2.x, x); x = fmaf(b.y, k2.y, x); x = fmaf(b.z, k3.x, x); x = fmaf(b.w, k3.y, x);
+            part[j] = x;
+          }
+        }
+      } else {
+        const uint8_t* row = kt + tq * kRow + xoff;
+        int d1[NQ], d2[NQ];
 #pragma unroll
-        for (int j = 0; j < NQ; ++j) {
-          const uint4* q1 = reinterpret_cast<const uint4*>(qc + (j * 2) * 128 + 32 * blk);
-          const uint4* q2 = reinterpret_cast<const uint4*>(qc + (j * 2 + 1) * 128 + 32 * blk);
-          const uint4 a0 = q1[0], a1 = q1[1], b0 = q2[0], b1 = q2[1];
-          d1[j] = __dp4a((int)kw[0], (int)a0.x, 0);
-          d1[j] = __dp4a((int)kw[1], (int)a0.y, d1[j]);
-          d1[j] = __dp4a((int)kw[2], (int)a0.z, d1[j]);
-          d1[j] = __dp4a((int)kw[3], (int)a0.w, d1[j]);
-          d1[j] = __dp4a((int)kw[4], (int)a1.x, d1[j]);
-          d1[j] = __dp4a((int)kw[5], (int)a1.y, d1[j]);
-          d1[j] = __dp4a((int)kw[6], (int)a1.z, d1[j]);
-          d1[j] = __dp4a((int)kw[7], (int)a1.w, d1[j]);
-          d2[j] = __dp4a((int)kw[0], (int)b0.x, 0);
-          d2[j] = __dp4a((int)kw[1], (int)b0.y, d2[j]);
-          d2[j] = __dp4a((int)kw[2], (int)b0.z, d2[j]);
-          d2[j] = __dp4a((int)kw[3], (int)b0.w, d2[j]);
-          d2[j] = __dp4a((int)kw[4], (int)b1.x, d2[j]);
-          d2[j] = __dp4a((int)kw[5], (int)b1.y, d2[j]);
-          d2[j] = __dp4a((int)kw[6], (int)b1.z, d2[j]);
-          d2[j] = __dp4a((int)kw[7], (int)b1.w, d2[j]);
-          part[j] = fmaf(dk, (float)(127 * d1[j] + d2[j]), part[j]);
+        for (int bi = 0; bi < 2; ++bi) {
+          const int blk = 2 * half + bi;
+          const uint8_t* b = row + kBlk * blk;
+          const float dk = lds_half(b);
+          uint32_t kw[8];  // codes of dims 4 w .. 4 w + 3 of the block
+          if constexpr (KVF == KQ_KV_Q8_0) {
+#pragma unroll
+            for (int w = 0; w < 8; ++w) kw[w] = lds_u32_a2(b + 2 + 4 * w);
+          } else {
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+              const uint32_t x = lds_u32_a2(b + 2 + 4 * w);
+              kw[w] = nibbles_s8(x & 0x0F0F0F0Fu);
+              kw[4 + w] = nibbles_s8((x >> 4) & 0x0F0F0F0Fu);
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < NQ; ++j) {
+            const uint4* q1 = reinterpret_cast<const uint4*>(qc + (j * 2) * 128 + 32 * blk);
+            const uint4* q2 = reinterpret_cast<const uint4*>(qc + (j * 2 + 1) * 128 + 32 * blk);
+            const uint4 a0 = q1[0], a1 = q1[1], b0 = q2[0], b1 = q2[1];
+            d1[j] = __dp4a((int)kw[0], (int)a0.x, 0);
+            d1[j] = __dp4a((int)kw[1], (int)a0.y, d1[j]);
+            d1[j] = __dp4a((int)kw[2], (int)a0.z, d1[j]);
+            d1[j] = __dp4a((int)kw[3], (int)a0.w, d1[j]);
+            d1[j] = __dp4a((int)kw[4], (int)a1.x, d1[j]);
+            d1[j] = __dp4a((int)kw[5], (int)a1.y, d1[j]);
+            d1[j] = __dp4a((int)kw[6], (int)a1.z, d1[j]);
+            d1[j] = __dp4a((int)kw[7], (int)a1.w, d1[j]);
+            d2[j] = __dp4a((int)kw[0], (int)b0.x, 0);
+            d2[j] = __dp4a((int)kw[1], (int)b0.y, d2[j]);
+            d2[j] = __dp4a((int)kw[2], (int)b0.z, d2[j]);
+            d2[j] = __dp4a((int)kw[3], (int)b0.w, d2[j]);
+            d2[j] = __dp4a((int)kw[4], (int)b1.x, d2[j]);
+            d2[j] = __dp4a((int)kw[5], (int)b1.y, d2[j]);
+            d2[j] = __dp4a((int)kw[6], (int)b1.z, d2[j]);
+            d2[j] = __dp4a((int)kw[7], (int)b1.w, d2[j]);
+            part[j] = fmaf(dk, (float)(127 * d1[j] + d2[j]), part[j]);
+          }
         }
       }
 #pragma unroll
@@ -290,11 +365,26 @@ __global__ void __launch_bounds__(32 * kWarps)
     // ---- PV: lane = dims 4 lane .. 4 lane + 3 (block vb) ----
 #pragma unroll 4
     for (int t = 0; t < kTok; ++t) {
-      const uint8_t* row = vt + t * kRow;
-      const float dv = t < nvalid ? lds_half(row + xoff + 34 * vb) : 0.0f;  // masked tokens weigh nothing
-      const uint32_t w = lds_u32_a2(row + voff);
-      const float v0 = (float)(int8_t)(w & 0xFF), v1 = (float)(int8_t)((w >> 8) & 0xFF);
-      const float v2 = (float)(int8_t)((w >> 16) & 0xFF), v3 = (float)(int8_t)(w >> 24);
+      float dv, v0, v1, v2, v3;
+      if constexpr (KVF == KQ_KV_F16) {
+        const uint2 w = *reinterpret_cast<const uint2*>(vt + voff + t * 128 + ((((lane & 15) >> 1) ^ (t & 7)) << 4));
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
+        dv = t < nvalid ? 1.0f : 0.0f;  // masked tokens weigh nothing
+        v0 = a.x; v1 = a.y; v2 = b.x; v3 = b.y;
+      } else {
+        const uint8_t* row = vt + t * kRow;
+        dv = t < nvalid ? lds_half(row + xoff + kBlk * vb) : 0.0f;  // masked tokens weigh nothing
+        const uint32_t w = lds_u32_a2(row + voff);
+        if constexpr (KVF == KQ_KV_Q8_0) {
+          v0 = (float)(int8_t)(w & 0xFF); v1 = (float)(int8_t)((w >> 8) & 0xFF);
+          v2 = (float)(int8_t)((w >> 16) & 0xFF); v3 = (float)(int8_t)(w >> 24);
+        } else {
+          const uint32_t x = (w >> vshift) & 0x0F0F0F0Fu;
+          v0 = (float)((int)(x & 0xF) - 8); v1 = (float)((int)((x >> 8) & 0xF) - 8);
+          v2 = (float)((int)((x >> 16) & 0xF) - 8); v3 = (float)((int)(x >> 24) - 8);
+        }
+      }
 #pragma unroll
       for (int j = 0; j < NQ; ++j) {
         const float wt = __shfl_sync(0xffffffffu, pj[j], t) * dv;
@@ -323,7 +413,6 @@ __global__ void __launch_bounds__(32 * kWarps)
   }
   __syncthreads();
   if (warp != 0) return;
-  const uint8_t* cta = reinterpret_cast<const uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~(uintptr_t)127);
   const size_t base = ((size_t)u * (p.nchunk / kWarps) + c / kWarps) * kQ;
 #pragma unroll
   for (int j = 0; j < NQ; ++j) {
@@ -331,7 +420,7 @@ __global__ void __launch_bounds__(32 * kWarps)
     float mw[kWarps], M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) {
-      mw[w] = reinterpret_cast<const float*>(cta + w * kWarpSmem)[j * 132];
+      mw[w] = reinterpret_cast<const float*>(cta + w * F::kWarpSmem)[j * 132];
       M = fmaxf(M, mw[w]);
     }
     float L = 0.0f;
@@ -339,7 +428,7 @@ __global__ void __launch_bounds__(32 * kWarps)
     if (M != -INFINITY) {
 #pragma unroll
       for (int w = 0; w < kWarps; ++w) {
-        const float* st = reinterpret_cast<const float*>(cta + w * kWarpSmem) + j * 132;
+        const float* st = reinterpret_cast<const float*>(cta + w * F::kWarpSmem) + j * 132;
         const float wg = mw[w] == -INFINITY ? 0.0f : ex2(mw[w] - M);
         L = fmaf(st[1], wg, L);
         const float4 x = *reinterpret_cast<const float4*>(st + 4 + 4 * lane);
@@ -430,16 +519,28 @@ __global__ void __launch_bounds__(128) fa_small_combine_kernel(SmallParams p, in
   }
 }
 
-bool encode_head_map(CUtensorMap* map, const void* base, uint64_t rows, int heads) {
-  // [rows][heads * 136 bytes] as 8-byte elements; boxes of 16 rows x 18
-  // elements (one head's 136 bytes plus 8 before or after it, so every box
-  // starts on a 16-byte boundary; past the last row the fill is zero)
+bool encode_head_map(CUtensorMap* map, const void* base, uint64_t rows, int heads, int kv_format) {
   auto fn = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
   if (!fn) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)heads * 17, rows};
-  cuuint64_t strides[1] = {(cuuint64_t)heads * 136};
-  cuuint32_t box[2] = {kRow / 8, kTok};
   cuuint32_t estr[2] = {1, 1};
+  if (kv_format == KQ_KV_F16) {
+    // [rows][heads * 128] fp16; boxes of 16 rows x 64 elements (one half of
+    // a head's row) with the 128-byte swizzle; past the last row the fill is zero
+    cuuint64_t dims[2] = {(cuuint64_t)heads * 128, rows};
+    cuuint64_t strides[1] = {(cuuint64_t)heads * 256};
+    cuuint32_t box[2] = {64, kTok};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  }
+  // [rows][heads * units 8-byte elements] (units = 17 for q8_0's 136-byte
+  // head rows, 9 for q4_0's 72); boxes of 16 rows x (units + 1) elements
+  // (one head's row plus 8 bytes before or after it, so every box starts on
+  // a 16-byte boundary; past the last row the fill is zero)
+  const int units = kv_format == KQ_KV_Q8_0 ? 17 : 9;
+  cuuint64_t dims[2] = {(cuuint64_t)heads * units, rows};
+  cuuint64_t strides[1] = {(cuuint64_t)heads * units * 8};
+  cuuint32_t box[2] = {(cuuint32_t)units + 1, kTok};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
@@ -460,13 +561,14 @@ void choose_chunks(int nunits, int max_len, int* nchunk, int* chunk) {
   *nchunk = std::max(kWarps, (used + kWarps - 1) / kWarps * kWarps);
 }
 
-template <typename QT, typename OT, bool RAGGED, int NQ>
+template <typename QT, typename OT, bool RAGGED, int NQ, int KVF>
 kq_status_t launch(SmallParams p, const void* k, const void* v, uint64_t rows, int heads, long long Q,
                    cudaStream_t s) {
   CUtensorMap km, vm;
-  if (!encode_head_map(&km, k, rows, heads) || !encode_head_map(&vm, v, rows, heads))
+  if (!encode_head_map(&km, k, rows, heads, KVF) || !encode_head_map(&vm, v, rows, heads, KVF))
     return fail(KQ_ERR_CUDA, "fa_small: KV tensor map rejected");
-  auto kern = fa_small_kernel<QT, RAGGED, NQ>;
+  auto kern = fa_small_kernel<QT, RAGGED, NQ, KVF>;
+  constexpr int kSmem = SmallFmt<KVF>::kSmem;
   kq_status_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), kSmem, "fa_small smem attribute");
   if (st) return st;
   const long long tasks = (long long)p.nunits * p.nchunk;
@@ -501,12 +603,12 @@ kq_status_t launch(SmallParams p, const void* k, const void* v, uint64_t rows, i
   return check_launch("fa_small_combine");
 }
 
-template <typename QT, typename OT, bool RAGGED>
+template <typename QT, typename OT, bool RAGGED, int KVF>
 kq_status_t launch_nq(int nq, SmallParams p, const void* k, const void* v, uint64_t rows, int heads, long long Q,
                       cudaStream_t s) {
-  if (nq <= 1) return launch<QT, OT, RAGGED, 1>(p, k, v, rows, heads, Q, s);
-  if (nq <= 2) return launch<QT, OT, RAGGED, 2>(p, k, v, rows, heads, Q, s);
-  return launch<QT, OT, RAGGED, 4>(p, k, v, rows, heads, Q, s);
+  if (nq <= 1) return launch<QT, OT, RAGGED, 1, KVF>(p, k, v, rows, heads, Q, s);
+  if (nq <= 2) return launch<QT, OT, RAGGED, 2, KVF>(p, k, v, rows, heads, Q, s);
+  return launch<QT, OT, RAGGED, 4, KVF>(p, k, v, rows, heads, Q, s);
 }
 
 SmallParams carve(void* ws, int nunits, int nchunk) {
@@ -527,16 +629,19 @@ size_t scratch_bytes(int nunits, int nchunk) {
 
 }  // namespace
 
-bool fa_small_supported(const void* q, const void* k, const void* v, const void* out, int D, int Hkv,
-                        int queries_per_unit) {
+bool fa_small_supported(int kv_format, const void* q, const void* k, const void* v, const void* out, int D,
+                        int Hkv, int queries_per_unit) {
   auto al = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
-  // an even head count keeps every head's 16-byte aligned box inside the rows
-  return D == 128 && Hkv >= 2 && Hkv % 2 == 0 && queries_per_unit >= 1 && queries_per_unit <= kQ && al(q) &&
-         al(k) && al(v) && al(out);
+  // block formats: an even head count keeps every head's 16-byte aligned box inside the rows
+  const bool heads = kv_format == KQ_KV_F16 ? Hkv >= 1
+                                            : (kv_format == KQ_KV_Q8_0 || kv_format == KQ_KV_Q4_0) && Hkv >= 2 &&
+                                                  Hkv % 2 == 0;
+  return heads && D == 128 && queries_per_unit >= 1 && queries_per_unit <= kQ && al(q) && al(k) && al(v) &&
+         al(out);
 }
 
-kq_status_t launch_fa_small_mha(const float* q, const void* k, const void* v, float* out, int B, int S, int H,
-                                cudaStream_t s) {
+kq_status_t launch_fa_small_mha(int kv_format, const float* q, const void* k, const void* v, float* out, int B,
+                                int S, int H, cudaStream_t s) {
   const int ngrp = (B + kQ - 1) / kQ;
   const int nunits = ngrp * H;
   int nchunk = 1, chunk = kTok;
@@ -554,7 +659,14 @@ kq_status_t launch_fa_small_mha(const float* q, const void* k, const void* v, fl
   p.Hkv = H;
   p.S = S;
   p.qscale = (float)(1.0 / std::sqrt(128.0) * 1.4426950408889634);
-  return launch_nq<float, float, false>(std::min(B, kQ), p, k, v, (uint64_t)std::max(S, 1), H, (long long)B * H, s);
+  const int nq = std::min(B, kQ);
+  const uint64_t rows = (uint64_t)std::max(S, 1);
+  switch (kv_format) {
+    case KQ_KV_Q8_0: return launch_nq<float, float, false, KQ_KV_Q8_0>(nq, p, k, v, rows, H, (long long)B * H, s);
+    case KQ_KV_Q4_0: return launch_nq<float, float, false, KQ_KV_Q4_0>(nq, p, k, v, rows, H, (long long)B * H, s);
+    case KQ_KV_F16: return launch_nq<float, float, false, KQ_KV_F16>(nq, p, k, v, rows, H, (long long)B * H, s);
+    default: return fail(KQ_ERR_INVALID, "fa_small: unknown KV format %d", kv_format);
+  }
 }
 
 kq_status_t launch_fa_small_ragged(const void* q, const void* k, const void* v, const int32_t* cu, int B, int Hq,
@@ -575,8 +687,8 @@ kq_status_t launch_fa_small_ragged(const void* q, const void* k, const void* v, 
   p.Hkv = Hkv;
   p.S = max_seqlen;
   p.qscale = (float)((double)scale * 1.4426950408889634);
-  return launch_nq<__half, __half, true>(Hq / Hkv, p, k, v, (uint64_t)std::max(total_rows, 1), Hkv,
-                                         (long long)B * Hq, s);
+  return launch_nq<__half, __half, true, KQ_KV_Q8_0>(Hq / Hkv, p, k, v, (uint64_t)std::max(total_rows, 1), Hkv,
+                                                     (long long)B * Hq, s);
 }
 
 }  // namespace kq

@@ -172,13 +172,14 @@ kq_status_t launch_fa_stream_ragged(const void* q, const void* k, const void* v,
                                     int Hkv, int total_rows, float scale, void* out, cudaStream_t s);
 kq_status_t launch_fa_stream_mha(const float* q, const void* k, const void* v, float* out, int B, int S, int H,
                                  cudaStream_t s);
-// fa_small.cu: the small-batch decode (q8_0 caches, D = 128, an even number
-// of KV heads, <= 4 queries per KV head, 16-byte aligned q, k, v and out):
-// every warp streams one KV head's token chunk by itself
-bool fa_small_supported(const void* q, const void* k, const void* v, const void* out, int D, int Hkv,
-                        int queries_per_unit);
-kq_status_t launch_fa_small_mha(const float* q, const void* k, const void* v, float* out, int B, int S, int H,
-                                cudaStream_t s);
+// fa_small.cu: the small-batch decode (D = 128, <= 4 queries per KV head,
+// 16-byte aligned q, k, v and out; q8_0 or q4_0 caches with an even number
+// of KV heads, or fp16 caches; the ragged form q8_0 only): every warp streams
+// one KV head's token chunk by itself
+bool fa_small_supported(int kv_format, const void* q, const void* k, const void* v, const void* out, int D,
+                        int Hkv, int queries_per_unit);
+kq_status_t launch_fa_small_mha(int kv_format, const float* q, const void* k, const void* v, float* out, int B,
+                                int S, int H, cudaStream_t s);
 kq_status_t launch_fa_small_ragged(const void* q, const void* k, const void* v, const int32_t* cu, int B, int Hq,
                                    int Hkv, int max_seqlen, int total_rows, float scale, void* out, cudaStream_t s);
 // fa_batch.cu: the harness form with many queries per head (q8_0, q4_0 or

@@ -369,6 +369,29 @@ def test_batch_mha_kv_formats(cuda, fmt, B, S, H):
     assert kq.device_error() == 0
 
 
+@pytest.mark.parametrize("fmt", ["q4_0", "f16"])
+@pytest.mark.parametrize("B,S,H", [(1, 8192, 32), (8, 4096, 28), (3, 17, 32), (5, 1, 2), (2, 2049, 3), (4, 300, 7),
+                                   (64, 1000, 8)])
+def test_small_batch_kv_formats(cuda, fmt, B, S, H):
+    """Harness batches too small for the batch kernel over q4_0 and fp16
+    caches run the small-batch kernel (fa_small.cu): q4_0 nibbles as int8
+    codes for the dp4a QK and decoded in PV, fp16 rows through 128-byte
+    swizzled boxes with fp32 QK. One to four queries per group (and several
+    groups), partial tiles, a one-token cache, odd head counts for fp16."""
+    import kq
+    if fmt == "q4_0" and H % 2:
+        pytest.skip("block-quantised caches take the small-batch kernel with an even head count only")
+    rng = np.random.default_rng(B * 7 + S + H + len(fmt))
+    D = 128
+    q = rng.standard_normal((B, H, D)).astype(np.float32)
+    k = _cache(fmt, rng.standard_normal((S, H, D)).astype(np.float32), D)
+    v = _cache(fmt, rng.standard_normal((S, H, D)).astype(np.float32), D)
+    got = kq.flash_attn(_t(q, cuda), _t(k, cuda), _t(v, cuda), B, S, H, D, fmt).cpu().numpy()
+    ok, msg = Q.check_close(got, Q.flash_decode_mha(q, k, v, S, H, D, fmt))
+    assert ok, msg
+    assert kq.device_error() == 0
+
+
 @pytest.mark.parametrize("lens,Hq,Hkv", [([8192], 32, 8), ([64] * 32 + [4096] * 8, 32, 8)])
 def test_decode_after_producer(cuda, lens, Hq, Hkv):
     """The decode kernels are programmatic dependents of whatever precedes
