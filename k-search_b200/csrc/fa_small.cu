@@ -1,12 +1,14 @@
-// Flash-attention decode for small batches over a q8_0 KV cache (D = 128):
-// at most 4 queries per KV head and too few tiles for the balanced stream
-// kernel (fa_stream.cu) to fill the GPU (a single sequence, or a harness
-// batch of 1-8 queries). Semantics as the harness flash_attention operator
+// Flash-attention decode for small batches over a q8_0, q4_0 or fp16 KV
+// cache (D = 128): at most 4 queries per KV head and too few tiles for the
+// balanced stream kernel (fa_stream.cu) to fill the GPU (a single sequence,
+// or a harness batch of 1-8 queries); for q4_0 and fp16 caches every harness
+// batch the tensor-core batch kernel (fa_batch.cu) does not take. Semantics
+// as the harness flash_attention operator
 // (kernelevalplus-main/llm_kernel_test/op_test_handler.py:543-563):
 // out = softmax(q . K^T * scale) . V per (query, head), K and V stored as
-// q8_0 blocks along head_dim (op_test_handler.py:489-508), x = q * d. In the
-// ragged form sequence b owns cache rows cu[b] .. cu[b+1]-1 and query head h
-// reads KV head h / (Hq / Hkv).
+// q8_0 or q4_0 blocks along head_dim or as fp16 (op_test_handler.py:489-534).
+// In the ragged form (q8_0) sequence b owns cache rows cu[b] .. cu[b+1]-1
+// and query head h reads KV head h / (Hq / Hkv).
 //
 // Why a separate kernel: the stream kernel's CTA is 8 warps over a tile of
 // 16 tokens x 8 KV heads, so one sequence gives ~14 tiles per SM, processed
@@ -25,6 +27,11 @@
 //   softmax  online, per query, in log2 units (scale * log2 e folded into q).
 //   PV  lanes = 4 dims: for each token, its V codes times p * d_v accumulate
 //       in fp32 (no conversion to a second operand format).
+// q4_0: the box row is the head's 72 bytes plus 8; QK turns the nibbles into
+// the int8 codes q - 8 for the same dp4a dots, PV decodes them. fp16: the
+// row is the head's 256 bytes as two 128-byte-swizzled boxes (rows of a
+// half tile in distinct banks); QK is an fp32 dot of the fp32 query with
+// the fp16 row, PV takes the fp16 values with weight p.
 // Each warp writes its chunk's (m, l, acc) per query; a merge kernel combines
 // the chunks of each query.
 #include <cuda.h>
