@@ -18,22 +18,23 @@
 //    s2 = s1 / 127, so 127 dot1 + dot2 is the exact block dot at scale s2),
 //    and the fp32 epilogue applies each (token, block) K scale, as the decode
 //    kernels do;
-//  * the CTA dequantises each V tile once into fp16 in shared memory, as a
-//    high part and its fp16 remainder (hi + lo carries ~22 bits of code * d);
-//  * PV = P_hi V_hi + P_lo V_hi + P_hi V_lo (mma.m16n8k16 f16).
+//  * the CTA turns each V tile's codes into fp16 once (exact: |code| <= 127)
+//    and keeps the V block scales apart; per 32-dim block b,
+//    PV_b = P'_hi C + P'_lo C (mma.m16n8k16 f16) with P' = p * d_v(token, b)
+//    split into an fp16 high part and remainder.
 // fp16 caches (fa_batch_f16_kernel): K and V are exact in fp16, so the TMA
 // boxes (two 64-dim halves, 128-byte swizzled) are read by ldmatrix in place;
 // the query is an fp16 high part plus its remainder in shared memory, and
 // QK = Q_hi K + Q_lo K, PV = P_hi V + P_lo V.
-// Both: online softmax per query row in registers (exp2); P = p as fp16 plus
-// its fp16 remainder, taken straight from the S accumulators as the A operand
-// of the PV products.
+// Both: online softmax per query row in registers (exp2); P (or P') as fp16
+// plus its fp16 remainder, taken straight from the S accumulators as the A
+// operand of the PV products.
 // Precision, from an fp64 emulation of each arithmetic against the oracle
 // (worst |error| / per-element bar): fp16 Q, K, P and V each rounded once
 // misses the bar on a few elements; with fp16 remainders on three of the four
 // operands 0.71-0.78 (still 1 miss in 2.1 M elements on the GPU), on all four
 // 0.003 (three f16 products per GEMM); the int8 QK with P and V split
-// 0.15-0.20. The fp16-cache form has every operand exact or split.
+// 0.15-0.20. Both forms here have every operand exact or split.
 #include <cuda.h>
 
 #include <algorithm>
@@ -57,7 +58,7 @@ constexpr int kHPitch = 272;             // fp16 tile row: 256 bytes + 16 (ldmat
 constexpr int kHTile = kTTile * kHPitch;            // 17408 bytes
 
 // Shared-memory plan of the block-quantised kernels: the raw K and V rings,
-// the dequantised V (high parts, remainders) and the K block scales.
+// the V codes of the current tile as fp16 and the K and V block scales.
 template <int KVF>
 struct RawFmt {
   static constexpr int kBlk = KVF == KQ_KV_Q8_0 ? 34 : 18;  // bytes per 32-dim block
@@ -65,12 +66,12 @@ struct RawFmt {
   static constexpr int kRawRow = 8 * (kUnits + 1);           // box row: 144, 80 bytes
   static constexpr int kRawTile = kTTile * kRawRow;
   static constexpr int kOffRawV = kStages * kRawTile;
-  static constexpr int kOffVh = 2 * kStages * kRawTile;
-  static constexpr int kOffVl = kOffVh + kHTile;
-  static constexpr int kOffDk = kOffVl + kHTile;             // K block scales, fp32 [4 blocks][64 tokens]
-  static constexpr int kOffBar = kOffDk + 4 * kTTile * 4;
+  static constexpr int kOffVc = 2 * kStages * kRawTile;      // V codes as fp16 (exact) [64 tokens][kHPitch]
+  static constexpr int kOffDk = kOffVc + kHTile;             // K block scales, fp32 [4 blocks][64 tokens]
+  static constexpr int kOffDv = kOffDk + 4 * kTTile * 4;     // V block scales, fp32 [4 blocks][64 tokens]
+  static constexpr int kOffBar = kOffDv + 4 * kTTile * 4;
   static constexpr int kSmem = kOffBar + kStages * 8 + 128;  // + base alignment slack
-  static_assert(kRawTile % 128 == 0 && kOffVh % 128 == 0 && kHTile % 128 == 0, "aligned tiles");
+  static_assert(kRawTile % 128 == 0 && kOffVc % 128 == 0 && kHTile % 128 == 0, "aligned tiles");
 };
 
 // Shared-memory plan of the fp16-cache kernel: per stage K then V, each two
@@ -180,14 +181,6 @@ __device__ __forceinline__ uint32_t nibbles_s8(uint32_t x) {
 }
 __device__ __forceinline__ uint32_t h2u(__half2 x) { return *reinterpret_cast<const uint32_t*>(&x); }
 
-// The high part of code * d rounded once to fp16 (mul.rn) and its remainder
-// (fma.rn of the exact product minus the high part), four elements.
-__device__ __forceinline__ void scale_split4(const __half2 (&e)[2], __half2 d2, uint2& hi, uint2& lo) {
-  const __half2 g0 = __hmul2(e[0], d2), g1 = __hmul2(e[1], d2);
-  hi = make_uint2(h2u(g0), h2u(g1));
-  lo = make_uint2(h2u(__hfma2(e[0], d2, __hneg2(g0))), h2u(__hfma2(e[1], d2, __hneg2(g1))));
-}
-
 // Online softmax over one 64-token tile for rows g (a) and g + 8 (b) of the
 // warp's 16 queries: masks tokens at or past S (tile starting at token tok0),
 // turns the scores into p = exp2(s - m), updates the running maxima and sums
@@ -282,8 +275,9 @@ __global__ void __launch_bounds__(32 * kWarps, 2)
   const int ntiles = (p.S + kTTile - 1) / kTTile;
   const int xoff = (h & 1) * 8;                    // the head's first byte inside a raw row
   const int bx = F::kUnits * h - (h & 1);          // box start in 8-byte units (16-byte aligned)
-  const uint32_t vh_s = smem_u32(smem + F::kOffVh), vl_s = smem_u32(smem + F::kOffVl);
+  const uint32_t vc_s = smem_u32(smem + F::kOffVc);
   float* dks = reinterpret_cast<float*>(smem + F::kOffDk);
+  float* dvs = reinterpret_cast<float*>(smem + F::kOffDv);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
@@ -367,55 +361,43 @@ __global__ void __launch_bounds__(32 * kWarps, 2)
   for (int i = 0; i < ntiles; ++i) {
     const int s = i % kStages;
     mbar_wait_or_poison(&full[s], (i / kStages) & 1, p.err, DEV_TIMEOUT_FULL, dead);
-    // ---- dequantise V and gather the K block scales: thread = (token, pair
-    // of 32-dim blocks) ----
-    {
-      const int tok = threadIdx.x >> 1, hb = threadIdx.x & 1;
-      const uint8_t* rk = smem + s * kRawTile + tok * kRawRow + xoff;
-      const uint8_t* rv = smem + F::kOffRawV + s * kRawTile + tok * kRawRow + xoff;
-      uint8_t* dvh = smem + F::kOffVh + tok * kHPitch;
-      uint8_t* dvl = smem + F::kOffVl + tok * kHPitch;
+    // ---- V codes to fp16 (exact) and the K and V block scales: two (token,
+    // block) items per thread; a quarter-warp holds 8 consecutive tokens of
+    // one block, so its 16-byte stores fall in distinct banks ----
 #pragma unroll
-      for (int bi = 0; bi < 2; ++bi) {
-        const int blk = 2 * hb + bi;
-        dks[blk * kTTile + tok] = __half2float(*reinterpret_cast<const __half*>(rk + kBlk * blk));
-        const __half sdv = *reinterpret_cast<const __half*>(rv + kBlk * blk);
-        const __half2 dv2 = __halves2half2(sdv, sdv);
-        if constexpr (KVF == KQ_KV_Q8_0) {
+    for (int r = 0; r < 2; ++r) {
+      const int item = threadIdx.x + 128 * r;
+      const int tok = (item & 7) + 8 * (item >> 5), blk = (item >> 3) & 3;
+      const uint8_t* rk = smem + s * kRawTile + tok * kRawRow + xoff + kBlk * blk;
+      const uint8_t* rv = smem + F::kOffRawV + s * kRawTile + tok * kRawRow + xoff + kBlk * blk;
+      uint8_t* dvc = smem + F::kOffVc + tok * kHPitch + 64 * blk;
+      dks[blk * kTTile + tok] = __half2float(*reinterpret_cast<const __half*>(rk));
+      dvs[blk * kTTile + tok] = __half2float(*reinterpret_cast<const __half*>(rv));
+      if constexpr (KVF == KQ_KV_Q8_0) {
 #pragma unroll
-          for (int pr = 0; pr < 4; ++pr) {  // codes 8 pr .. 8 pr + 7
-            const int co = kBlk * blk + 2 + 8 * pr;
-            __half2 e0[2], e1[2];
-            codes_f16(lds_u32_a2(rv + co), e0[0], e0[1]);
-            codes_f16(lds_u32_a2(rv + co + 4), e1[0], e1[1]);
-            uint2 h0, l0, h1, l1;
-            scale_split4(e0, dv2, h0, l0);
-            scale_split4(e1, dv2, h1, l1);
-            const int d = (32 * blk + 8 * pr) * 2;
-            *reinterpret_cast<uint4*>(dvh + d) = make_uint4(h0.x, h0.y, h1.x, h1.y);
-            *reinterpret_cast<uint4*>(dvl + d) = make_uint4(l0.x, l0.y, l1.x, l1.y);
-          }
-        } else {
-          // q4_0: byte e of the 16 holds element e (low nibble) and e + 16
+        for (int pr = 0; pr < 4; ++pr) {  // codes 8 pr .. 8 pr + 7
+          __half2 e[4];
+          codes_f16(lds_u32_a2(rv + 2 + 8 * pr), e[0], e[1]);
+          codes_f16(lds_u32_a2(rv + 6 + 8 * pr), e[2], e[3]);
+          *reinterpret_cast<uint4*>(dvc + 16 * pr) = make_uint4(h2u(e[0]), h2u(e[1]), h2u(e[2]), h2u(e[3]));
+        }
+      } else {
+        // q4_0: byte e of the 16 holds element e (low nibble) and e + 16
 #pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            const uint32_t x = lds_u32_a2(rv + kBlk * blk + 2 + 4 * w);
-            __half2 e0[2], e1[2];
-            nibbles_f16(x & 0x0F0F0F0Fu, e0[0], e0[1]);
-            nibbles_f16((x >> 4) & 0x0F0F0F0Fu, e1[0], e1[1]);
-            uint2 h0, l0, h1, l1;
-            scale_split4(e0, dv2, h0, l0);
-            scale_split4(e1, dv2, h1, l1);
-            const int d0 = (32 * blk + 4 * w) * 2, d1 = d0 + 32;
-            *reinterpret_cast<uint2*>(dvh + d0) = h0;
-            *reinterpret_cast<uint2*>(dvl + d0) = l0;
-            *reinterpret_cast<uint2*>(dvh + d1) = h1;
-            *reinterpret_cast<uint2*>(dvl + d1) = l1;
-          }
+        for (int wp = 0; wp < 2; ++wp) {  // bytes 8 wp .. 8 wp + 7
+          const uint32_t x0 = lds_u32_a2(rv + 2 + 8 * wp), x1 = lds_u32_a2(rv + 6 + 8 * wp);
+          __half2 lo[4], hi[4];
+          nibbles_f16(x0 & 0x0F0F0F0Fu, lo[0], lo[1]);
+          nibbles_f16(x1 & 0x0F0F0F0Fu, lo[2], lo[3]);
+          nibbles_f16((x0 >> 4) & 0x0F0F0F0Fu, hi[0], hi[1]);
+          nibbles_f16((x1 >> 4) & 0x0F0F0F0Fu, hi[2], hi[3]);
+          *reinterpret_cast<uint4*>(dvc + 16 * wp) = make_uint4(h2u(lo[0]), h2u(lo[1]), h2u(lo[2]), h2u(lo[3]));
+          *reinterpret_cast<uint4*>(dvc + 32 + 16 * wp) =
+              make_uint4(h2u(hi[0]), h2u(hi[1]), h2u(hi[2]), h2u(hi[3]));
         }
       }
     }
-    __syncthreads();  // V tiles and K scales complete
+    __syncthreads();  // V codes and block scales complete
 
     // ---- S: 16 queries x 64 tokens per warp; per 32-dim block two s8 MMAs
     // (query levels) on the raw K codes, then the block's K scale ----
@@ -458,26 +440,33 @@ __global__ void __launch_bounds__(32 * kWarps, 2)
     __syncthreads();
     if (threadIdx.x == 0 && i + kStages < ntiles) issue(i + kStages);
     softmax_tile(sc, i * kTTile, p.S, t, m_a, m_b, l_a, l_b, o);
-    // ---- O += P_hi V_hi + P_lo V_hi + P_hi V_lo: k-steps of 16 tokens ----
+    // ---- O += P'_hi C + P'_lo C per 32-dim block b: C = the exact V codes,
+    // P' = p * d_v(token, b) split into fp16 high part and remainder; k-steps
+    // of 16 tokens (this thread's A columns: tokens 16 kk + 2 t, + 1, + 8, + 9) ----
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
-      uint32_t ph[4], pl[4];
-      p_operand(sc, kk, ph, pl);
+      const int t0 = 16 * kk + 2 * t;
 #pragma unroll
-      for (int np = 0; np < 8; ++np) {
-        uint32_t vb[4], vr[4];
-        const uint32_t off = v_off + (uint32_t)(16 * kk * kHPitch + 32 * np);
-        ldsm_x4_trans(vb, vh_s + off);
-        ldsm_x4_trans(vr, vl_s + off);
-        mma_f16(o[2 * np], ph[0], ph[1], ph[2], ph[3], vb[0], vb[1]);
-        mma_f16(o[2 * np + 1], ph[0], ph[1], ph[2], ph[3], vb[2], vb[3]);
-        mma_f16(o[2 * np], pl[0], pl[1], pl[2], pl[3], vb[0], vb[1]);
-        mma_f16(o[2 * np + 1], pl[0], pl[1], pl[2], pl[3], vb[2], vb[3]);
-        mma_f16(o[2 * np], ph[0], ph[1], ph[2], ph[3], vr[0], vr[1]);
-        mma_f16(o[2 * np + 1], ph[0], ph[1], ph[2], ph[3], vr[2], vr[3]);
+      for (int b = 0; b < 4; ++b) {
+        const float2 d01 = *reinterpret_cast<const float2*>(dvs + b * kTTile + t0);
+        const float2 d89 = *reinterpret_cast<const float2*>(dvs + b * kTTile + t0 + 8);
+        uint32_t ph[4], pl[4];
+        split_half2(sc[2 * kk][0] * d01.x, sc[2 * kk][1] * d01.y, ph[0], pl[0]);
+        split_half2(sc[2 * kk][2] * d01.x, sc[2 * kk][3] * d01.y, ph[1], pl[1]);
+        split_half2(sc[2 * kk + 1][0] * d89.x, sc[2 * kk + 1][1] * d89.y, ph[2], pl[2]);
+        split_half2(sc[2 * kk + 1][2] * d89.x, sc[2 * kk + 1][3] * d89.y, ph[3], pl[3]);
+#pragma unroll
+        for (int np = 2 * b; np < 2 * b + 2; ++np) {  // dims 16 np .. + 15
+          uint32_t vb[4];
+          ldsm_x4_trans(vb, vc_s + v_off + (uint32_t)(16 * kk * kHPitch + 32 * np));
+          mma_f16(o[2 * np], ph[0], ph[1], ph[2], ph[3], vb[0], vb[1]);
+          mma_f16(o[2 * np + 1], ph[0], ph[1], ph[2], ph[3], vb[2], vb[3]);
+          mma_f16(o[2 * np], pl[0], pl[1], pl[2], pl[3], vb[0], vb[1]);
+          mma_f16(o[2 * np + 1], pl[0], pl[1], pl[2], pl[3], vb[2], vb[3]);
+        }
       }
     }
-    __syncthreads();  // the V tiles and K scales are rewritten by the next tile
+    __syncthreads();  // the V codes and block scales are rewritten by the next tile
   }
   store_rows(o, l_a, l_b, p, q0, g, t, h);
 }
