@@ -92,6 +92,13 @@ struct BatchParams {
   int* err;
   int B, H, S;
   float qscale;     // softmax scale * log2(e)
+  // token chunks (grid z): chunk c takes tiles [c ct, (c + 1) ct); with
+  // nc > 1 each writes its unnormalised partial state, [B * H][nc] maxima and
+  // sums and [B * H][nc][128] accumulators, and a combine kernel merges them
+  int nc, ct;
+  float* pm;
+  float* pl;
+  float* pacc;
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -240,23 +247,68 @@ __device__ __forceinline__ void p_operand(const float (&sc)[8][4], int kk, uint3
   split_half2(sc[2 * kk + 1][2], sc[2 * kk + 1][3], ph[3], pl[3]);
 }
 
-// out = O / l for the warp's rows g and g + 8 (queries past B are not written)
-__device__ __forceinline__ void store_rows(const float (&o)[16][4], float l_a, float l_b, const BatchParams& p,
-                                           int q0, int g, int t, int h) {
+// The warp's rows g and g + 8 (queries past B are not written): out = O / l
+// with one token chunk, else chunk c's partial state (m, l, O).
+__device__ __forceinline__ void store_rows(const float (&o)[16][4], float m_a, float m_b, float l_a, float l_b,
+                                           const BatchParams& p, int q0, int g, int t, int h, int c) {
   l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
   l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
   l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
   l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
-  const float ia = l_a > 0.0f ? 1.0f / l_a : 0.0f, ib = l_b > 0.0f ? 1.0f / l_b : 0.0f;
   const int ra = q0 + g, rb = q0 + g + 8;
+  if (p.nc > 1) {
+    const size_t pa = ((size_t)ra * p.H + h) * p.nc + c, pb = ((size_t)rb * p.H + h) * p.nc + c;
+    if (t == 0 && ra < p.B) {
+      p.pm[pa] = m_a;
+      p.pl[pa] = l_a;
+    }
+    if (t == 0 && rb < p.B) {
+      p.pm[pb] = m_b;
+      p.pl[pb] = l_b;
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int d = 8 * j + 2 * t;
+      if (ra < p.B) *reinterpret_cast<float2*>(p.pacc + pa * 128 + d) = make_float2(o[j][0], o[j][1]);
+      if (rb < p.B) *reinterpret_cast<float2*>(p.pacc + pb * 128 + d) = make_float2(o[j][2], o[j][3]);
+    }
+    return;
+  }
+  const float ia = l_a > 0.0f ? 1.0f / l_a : 0.0f, ib = l_b > 0.0f ? 1.0f / l_b : 0.0f;
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    const int c = 8 * j + 2 * t;
+    const int d = 8 * j + 2 * t;
     if (ra < p.B)
-      *reinterpret_cast<float2*>(p.out + ((size_t)ra * p.H + h) * 128 + c) = make_float2(o[j][0] * ia, o[j][1] * ia);
+      *reinterpret_cast<float2*>(p.out + ((size_t)ra * p.H + h) * 128 + d) = make_float2(o[j][0] * ia, o[j][1] * ia);
     if (rb < p.B)
-      *reinterpret_cast<float2*>(p.out + ((size_t)rb * p.H + h) * 128 + c) = make_float2(o[j][2] * ib, o[j][3] * ib);
+      *reinterpret_cast<float2*>(p.out + ((size_t)rb * p.H + h) * 128 + d) = make_float2(o[j][2] * ib, o[j][3] * ib);
   }
+}
+
+// One warp per (query, head) row: out = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c
+// over the row's token chunks. Lane = 4 dims.
+__global__ void __launch_bounds__(128) fa_batch_combine_kernel(BatchParams p, int rows) {
+  const int r = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const size_t base = (size_t)r * p.nc;
+  float M = -INFINITY;
+  for (int c = 0; c < p.nc; ++c) M = fmaxf(M, p.pm[base + c]);
+  float L = 0.0f;
+  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (M != -INFINITY) {
+    for (int c = 0; c < p.nc; ++c) {
+      const float mc = p.pm[base + c];
+      const float w = mc == -INFINITY ? 0.0f : ex2(mc - M);
+      L = fmaf(p.pl[base + c], w, L);
+      const float4 x = reinterpret_cast<const float4*>(p.pacc + (base + c) * 128)[lane];
+      a.x = fmaf(x.x, w, a.x);
+      a.y = fmaf(x.y, w, a.y);
+      a.z = fmaf(x.z, w, a.z);
+      a.w = fmaf(x.w, w, a.w);
+    }
+  }
+  const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+  reinterpret_cast<float4*>(p.out + (size_t)r * 128)[lane] = make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
 }
 
 template <int KVF>
@@ -272,7 +324,9 @@ __global__ void __launch_bounds__(32 * kWarps, 2)
   const int g = lane >> 2, t = lane & 3;
   const int h = blockIdx.y;
   const int q0 = blockIdx.x * kQTile + warp * 16;  // this warp's first query
-  const int ntiles = (p.S + kTTile - 1) / kTTile;
+  const int c = blockIdx.z;  // token chunk
+  const int tile0 = c * p.ct;
+  const int ntiles = max(0, min((p.S + kTTile - 1) / kTTile, tile0 + p.ct) - tile0);
   const int xoff = (h & 1) * 8;                    // the head's first byte inside a raw row
   const int bx = F::kUnits * h - (h & 1);          // box start in 8-byte units (16-byte aligned)
   const uint32_t vc_s = smem_u32(smem + F::kOffVc);
@@ -288,8 +342,8 @@ __global__ void __launch_bounds__(32 * kWarps, 2)
   auto issue = [&](int i) {
     const int s = i % kStages;
     mbar_arrive_expect_tx(&full[s], 2 * kRawTile);
-    tma_load_2d(smem + s * kRawTile, &kmap, bx, i * kTTile, &full[s]);
-    tma_load_2d(smem + F::kOffRawV + s * kRawTile, &vmap, bx, i * kTTile, &full[s]);
+    tma_load_2d(smem + s * kRawTile, &kmap, bx, (tile0 + i) * kTTile, &full[s]);
+    tma_load_2d(smem + F::kOffRawV + s * kRawTile, &vmap, bx, (tile0 + i) * kTTile, &full[s]);
   };
   if (threadIdx.x == 0)
     for (int i = 0; i < min(kStages, ntiles); ++i) issue(i);
@@ -439,7 +493,7 @@ __global__ void __launch_bounds__(32 * kWarps, 2)
     fence_proxy_async_smem();
     __syncthreads();
     if (threadIdx.x == 0 && i + kStages < ntiles) issue(i + kStages);
-    softmax_tile(sc, i * kTTile, p.S, t, m_a, m_b, l_a, l_b, o);
+    softmax_tile(sc, (tile0 + i) * kTTile, p.S, t, m_a, m_b, l_a, l_b, o);
     // ---- O += P'_hi C + P'_lo C per 32-dim block b: C = the exact V codes,
     // P' = p * d_v(token, b) split into fp16 high part and remainder; k-steps
     // of 16 tokens (this thread's A columns: tokens 16 kk + 2 t, + 1, + 8, + 9) ----
@@ -468,7 +522,7 @@ __global__ void __launch_bounds__(32 * kWarps, 2)
     }
     __syncthreads();  // the V codes and block scales are rewritten by the next tile
   }
-  store_rows(o, l_a, l_b, p, q0, g, t, h);
+  store_rows(o, m_a, m_b, l_a, l_b, p, q0, g, t, h, c);
 }
 
 __global__ void __launch_bounds__(32 * kWarps, 2)
@@ -481,7 +535,9 @@ __global__ void __launch_bounds__(32 * kWarps, 2)
   const int g = lane >> 2, t = lane & 3;
   const int h = blockIdx.y;
   const int q0 = blockIdx.x * kQTile + warp * 16;  // this warp's first query
-  const int ntiles = (p.S + kTTile - 1) / kTTile;
+  const int c = blockIdx.z;  // token chunk
+  const int tile0 = c * p.ct;
+  const int ntiles = max(0, min((p.S + kTTile - 1) / kTTile, tile0 + p.ct) - tile0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
@@ -495,8 +551,8 @@ __global__ void __launch_bounds__(32 * kWarps, 2)
     mbar_arrive_expect_tx(&full[s], kF16Stage);
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
-      tma_load_2d(st + hf * kF16Half, &kmap, 128 * h + 64 * hf, i * kTTile, &full[s]);
-      tma_load_2d(st + kF16Tile + hf * kF16Half, &vmap, 128 * h + 64 * hf, i * kTTile, &full[s]);
+      tma_load_2d(st + hf * kF16Half, &kmap, 128 * h + 64 * hf, (tile0 + i) * kTTile, &full[s]);
+      tma_load_2d(st + kF16Tile + hf * kF16Half, &vmap, 128 * h + 64 * hf, (tile0 + i) * kTTile, &full[s]);
     }
   };
   if (threadIdx.x == 0)
@@ -555,7 +611,7 @@ __global__ void __launch_bounds__(32 * kWarps, 2)
         mma_f16(sc[2 * jp + 1], ql[0], ql[1], ql[2], ql[3], kb[2], kb[3]);
       }
     }
-    softmax_tile(sc, i * kTTile, p.S, t, m_a, m_b, l_a, l_b, o);
+    softmax_tile(sc, (tile0 + i) * kTTile, p.S, t, m_a, m_b, l_a, l_b, o);
     // ---- O += P_hi V + P_lo V: k-steps of 16 tokens, V by ldmatrix.trans ----
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
@@ -578,7 +634,7 @@ __global__ void __launch_bounds__(32 * kWarps, 2)
     __syncthreads();
     if (threadIdx.x == 0 && i + kStages < ntiles) issue(i + kStages);
   }
-  store_rows(o, l_a, l_b, p, q0, g, t, h);
+  store_rows(o, m_a, m_b, l_a, l_b, p, q0, g, t, h, c);
 }
 
 bool encode_raw_map(CUtensorMap* map, const void* base, uint64_t rows, int heads, int units) {
@@ -619,6 +675,36 @@ kq_status_t launch_raw(const CUtensorMap& km, const CUtensorMap& vm, const Batch
   return check_launch("fa_batch");
 }
 
+// Token chunks per (query tile, head): the block scheduler fills the GPU's
+// 2 CTAs per SM from a grid of ctas * nc CTAs. Modelled time: waves x (tiles
+// per chunk + 2), the 2 being a CTA's set-up, pipeline fill and partial
+// write in tile times (fitted to CUDA-event timings at B = 512, H = 32,
+// S = 4096 and 8192 with 1 and 8 chunks: 1.4-2.4 across the three cache
+// formats). The cheapest count of at most 16, with chunks of at least 4
+// tiles; one chunk unless a split is cheaper. B = 512: H = 32, S = 8192
+// takes 8 chunks (365 -> 356 us fp16, 603 -> 589 q8_0, 560 -> 527 q4_0);
+// S = 4096 stays whole (8 chunks were 4-10% slower); H = 28, whose 224
+// CTAs leave a quarter of the slots idle, splits (S = 8192 with 9 chunks:
+// fp16 366 -> 325 us, q4_0 569 -> 467).
+int choose_token_chunks(long long ctas, int ntiles) {
+  const long long slots = 2LL * sm_count();
+  auto cost = [&](int nc) {
+    const int ct = (ntiles + nc - 1) / nc;
+    const long long u = ctas * ((ntiles + ct - 1) / ct), waves = (u + slots - 1) / slots;
+    return (double)waves * (ct + 2.0);
+  };
+  int best = 1;
+  double bc = cost(1);
+  for (int nc = 2; nc <= 16 && ntiles / nc >= 4; ++nc) {
+    const double c = cost(nc);
+    if (c < bc) {
+      best = nc;
+      bc = c;
+    }
+  }
+  return best;
+}
+
 }  // namespace
 
 bool fa_batch_supported(int kv_format, const void* q, const void* k, const void* v, const void* out, int B, int S,
@@ -651,19 +737,38 @@ kq_status_t launch_fa_batch_mha(int kv_format, const float* q, const void* k, co
   p.H = H;
   p.S = S;
   p.qscale = (float)(1.0 / std::sqrt(128.0) * 1.4426950408889634);
-  dim3 grid((unsigned)((B + kQTile - 1) / kQTile), (unsigned)H);
+  const int qtiles = (B + kQTile - 1) / kQTile;
+  const int ntiles = (S + kTTile - 1) / kTTile;
+  const int nc0 = choose_token_chunks((long long)qtiles * H, ntiles);
+  p.ct = (ntiles + nc0 - 1) / nc0;
+  p.nc = (ntiles + p.ct - 1) / p.ct;  // no empty chunk
+  p.pm = p.pl = p.pacc = nullptr;
+  const long long rows = (long long)B * H;
+  if (p.nc > 1) {
+    float* ws = static_cast<float*>(workspace(WS_FA, (size_t)rows * p.nc * (2 + 128) * sizeof(float)));
+    if (!ws) return KQ_ERR_NOMEM;
+    p.pm = ws;
+    p.pl = ws + rows * p.nc;
+    p.pacc = ws + 2 * rows * p.nc;
+  }
+  dim3 grid((unsigned)qtiles, (unsigned)H, (unsigned)p.nc);
+  kq_status_t st = KQ_OK;
   switch (kv_format) {
-    case KQ_KV_Q8_0: return launch_raw<KQ_KV_Q8_0>(km, vm, p, grid, s);
-    case KQ_KV_Q4_0: return launch_raw<KQ_KV_Q4_0>(km, vm, p, grid, s);
+    case KQ_KV_Q8_0: st = launch_raw<KQ_KV_Q8_0>(km, vm, p, grid, s); break;
+    case KQ_KV_Q4_0: st = launch_raw<KQ_KV_Q4_0>(km, vm, p, grid, s); break;
     case KQ_KV_F16: {
-      kq_status_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(fa_batch_f16_kernel), kF16Smem,
-                                           "fa_batch smem attribute");
+      st = ensure_dynamic_smem(reinterpret_cast<const void*>(fa_batch_f16_kernel), kF16Smem,
+                               "fa_batch smem attribute");
       if (st) return st;
       fa_batch_f16_kernel<<<grid, 32 * kWarps, kF16Smem, s>>>(km, vm, p);
-      return check_launch("fa_batch(f16)");
+      st = check_launch("fa_batch(f16)");
+      break;
     }
     default: return fail(KQ_ERR_INVALID, "fa_batch: unknown KV format %d", kv_format);
   }
+  if (st || p.nc == 1) return st;
+  fa_batch_combine_kernel<<<(unsigned)((rows + 3) / 4), 128, 0, s>>>(p, (int)rows);
+  return check_launch("fa_batch_combine");
 }
 
 }  // namespace kq

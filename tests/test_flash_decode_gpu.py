@@ -325,13 +325,14 @@ def test_small_batch_ragged(cuda, lens, Hq, Hkv):
 
 
 @pytest.mark.parametrize("B,S,H", [(512, 64, 32), (300, 65, 32), (512, 1, 32), (1024, 100, 24), (512, 777, 28),
-                                   (320, 2048, 32)])
+                                   (320, 2048, 32), (512, 3000, 28)])
 def test_batch_mha(cuda, B, S, H):
     """Harness batches whose (64-query tile, head) CTAs fill the GPU run the
-    fp16 tensor-core flash attention (fa_batch.cu): K and P carry an fp16
-    remainder, Q and V are rounded once. Partial query tiles (B = 300, 320),
-    lengths at and around the 64-token tile, a one-token cache, and odd
-    multiples of the head pair (H = 24, 28)."""
+    tensor-core flash attention (fa_batch.cu). Partial query tiles (B = 300,
+    320), lengths at and around the 64-token tile, a one-token cache, odd
+    multiples of the head pair (H = 24, 28), and caches split into token
+    chunks merged by the combine kernel (S = 2048 at B = 320: 3 chunks;
+    S = 3000 at H = 28: 5 chunks, the last ending on a partial tile)."""
     import kq
     rng = np.random.default_rng(B + S + H)
     D = 128
@@ -347,7 +348,7 @@ def test_batch_mha(cuda, B, S, H):
 
 @pytest.mark.parametrize("fmt", ["q4_0", "f16"])
 @pytest.mark.parametrize("B,S,H", [(512, 64, 32), (300, 65, 32), (512, 1, 32), (1024, 100, 24), (512, 777, 28),
-                                   (320, 2048, 32), (1920, 129, 5)])
+                                   (320, 2048, 32), (1920, 129, 5), (512, 3000, 28)])
 def test_batch_mha_kv_formats(cuda, fmt, B, S, H):
     """Harness batches over q4_0 and fp16 caches run the batch kernel too
     (fa_batch.cu): q4_0 through the exact int8 QK on the nibble codes and the
