@@ -6,7 +6,10 @@
 // rather than a stream of the cache.
 //
 // CTA = 4 warps over 64 queries of one head (16 per warp); it walks the
-// cache in 64-token tiles brought by a two-stage TMA ring.
+// cache (or one token chunk of it) in 64-token tiles brought by a two-stage
+// TMA ring. When (query tile, head) CTAs alone would leave the last wave
+// short, each is split into token chunks that write their partial softmax
+// state (m, l, O), and fa_batch_combine_kernel merges them per row.
 //
 // Block-quantised caches (fa_batch_kernel<KVF>, q8_0 and q4_0):
 //  * the boxes hold the raw rows of the head (64 rows x 144 bytes for q8_0,
